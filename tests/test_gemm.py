@@ -1,0 +1,141 @@
+"""tcgen05 GEMM kernels vs a PyTorch fp32 reference of the same op."""
+import pytest
+import torch
+
+from vllm_xtu_moe_b200.ops import gemm as G
+from vllm_xtu_moe_b200.ops.quant import dequant_fp8_block, quant_fp8_block
+
+
+def _close(out, ref, tol=2e-2):
+    if ref.numel() == 0:
+        return
+    out = out.float()
+    ref = ref.float()
+    err = (out - ref).abs().max().item()
+    scale = ref.abs().max().item() + 1e-6
+    assert err / scale < tol, f"max err {err} vs scale {scale}"
+
+
+def test_interleave_gate_up_roundtrip():
+    w = torch.randn(3, 512, 64)
+    wi = G.interleave_gate_up(w)
+    # block 0 of the result is gate rows 0..127, block 1 is up rows 0..127
+    assert torch.equal(wi[:, :128], w[:, :128])
+    assert torch.equal(wi[:, 128:256], w[:, 256:384])
+    assert torch.equal(wi[:, 256:384], w[:, 128:256])
+
+
+def test_grouped_torch_path_swiglu_matches_unfused():
+    torch.manual_seed(0)
+    E, K, I = 3, 64, 256
+    w13 = torch.randn(E, 2 * I, K, dtype=torch.bfloat16) * 0.1
+    a = torch.randn(10, K, dtype=torch.bfloat16)
+    seg = torch.tensor([0, 4, 4, 10], dtype=torch.int32)
+    out = G.grouped_gemm(a, G.interleave_gate_up(w13), seg, epilogue=G.EPI_SWIGLU, act_limit=7.0)
+    for e in range(E):
+        s0, s1 = seg[e].item(), seg[e + 1].item()
+        y = a[s0:s1].float() @ w13[e].float().t()
+        ref = G.silu_and_mul_clamped(y[:, :I], y[:, I:], 7.0)
+        _close(out[s0:s1], ref)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (300, 384, 1032), (1, 4096, 4096), (1000, 128, 512),
+                                   (4096, 4096, 4096)])
+def test_gemm_bf16(M, N, K):
+    torch.manual_seed(0)
+    a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    b = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) / K ** 0.5
+    out = G.gemm_bf16(a, b)
+    out32 = G.gemm_bf16(a, b, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    G.N.check_status()
+    ref = a.float() @ b.float().t()
+    _close(out, ref)
+    _close(out32, ref, 1e-3)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M,N,K", [(200, 512, 1024), (7, 2816, 4096)])
+def test_gemm_fp8_weights(M, N, K):
+    torch.manual_seed(1)
+    a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(N, K, device="cuda") / K ** 0.5
+    q, s = quant_fp8_block(w)
+    out = G.gemm_fp8w(a, q, s, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    G.N.check_status()
+    wd = dequant_fp8_block(q, s).to(torch.bfloat16).float()
+    ref = a.float() @ wd.t()
+    _close(out, ref, 1e-3)
+
+
+def _segments(counts):
+    seg = [0]
+    for c in counts:
+        seg.append(seg[-1] + c)
+    return torch.tensor(seg, dtype=torch.int32)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("fp8", [False, True])
+@pytest.mark.parametrize("counts", [[5, 0, 130, 257, 1], [0, 0, 3, 0]])
+def test_grouped_gemm(fp8, counts):
+    torch.manual_seed(2)
+    E = len(counts)
+    K, Nn = 512, 768
+    seg = _segments(counts).cuda()
+    M = int(seg[-1])
+    a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(E, Nn, K, device="cuda") / K ** 0.5
+    if fp8:
+        q, s = quant_fp8_block(w)
+        out = G.grouped_gemm(a, q, seg, w_scale=s, epilogue=G.EPI_F32)
+        wd = dequant_fp8_block(q, s).to(torch.bfloat16)
+    else:
+        wd = w.to(torch.bfloat16)
+        out = G.grouped_gemm(a, wd, seg, epilogue=G.EPI_F32)
+    torch.cuda.synchronize()
+    G.N.check_status()
+    ref = G._grouped_gemm_torch(a.cpu(), wd.cpu(), seg.cpu(), None, G.EPI_F32,
+                                torch.zeros(M, Nn), None, None, 0, 1, 0)
+    _close(out.cpu(), ref, 1e-3)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("fp8", [False, True])
+def test_grouped_swiglu_and_scatter(fp8):
+    torch.manual_seed(3)
+    counts = [70, 0, 129, 3]
+    E, K, I = 4, 256, 256
+    seg = _segments(counts).cuda()
+    M = int(seg[-1])
+    a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    w13 = torch.randn(E, 2 * I, K, device="cuda") / K ** 0.5
+    w2 = torch.randn(E, K, I, device="cuda") / I ** 0.5
+    scale = torch.rand(M, device="cuda")
+    dest = torch.randperm(M, device="cuda").int()
+    if fp8:
+        q13, s13 = quant_fp8_block(w13)
+        q2, s2 = quant_fp8_block(w2)
+        h = G.grouped_gemm(a, G.interleave_gate_up(q13.view(torch.uint8)).view(torch.float8_e4m3fn), seg,
+                           w_scale=G.interleave_gate_up_scale(s13), epilogue=G.EPI_SWIGLU, act_limit=10.0)
+        out = G.grouped_gemm(h, q2, seg, w_scale=s2, row_scale=scale, row_dest=dest, epilogue=G.EPI_F32)
+        w13d = dequant_fp8_block(q13, s13).to(torch.bfloat16)
+        w2d = dequant_fp8_block(q2, s2).to(torch.bfloat16)
+    else:
+        w13d, w2d = w13.to(torch.bfloat16), w2.to(torch.bfloat16)
+        h = G.grouped_gemm(a, G.interleave_gate_up(w13d), seg, epilogue=G.EPI_SWIGLU, act_limit=10.0)
+        out = G.grouped_gemm(h, w2d, seg, row_scale=scale, row_dest=dest, epilogue=G.EPI_F32)
+    torch.cuda.synchronize()
+    G.N.check_status()
+    segc = seg.cpu().tolist()
+    ref = torch.zeros(M, K)
+    for e in range(E):
+        s0, s1 = segc[e], segc[e + 1]
+        y = a[s0:s1].float().cpu() @ w13d[e].float().cpu().t()
+        hh = G.silu_and_mul_clamped(y[:, :I], y[:, I:], 10.0).to(torch.bfloat16).float()
+        _close(h[s0:s1].cpu(), hh) if s1 > s0 else None
+        o = h[s0:s1].float().cpu() @ w2d[e].float().cpu().t() * scale[s0:s1].cpu()[:, None]
+        ref[dest[s0:s1].long().cpu()] = o
+    _close(out.cpu(), ref, 1e-3)

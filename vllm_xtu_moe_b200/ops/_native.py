@@ -1,0 +1,121 @@
+"""ctypes binding of ``_lib/libxtu_cuda.so`` (the sm_100a kernels, C ABI).
+
+Every wrapper in :mod:`vllm_xtu_moe_b200.ops` validates shapes, dtypes and
+contiguity on the Python side, then passes raw device pointers and the current
+CUDA stream.  Kernels report faults they can detect without trapping (timeouts
+of bounded waits, bounds checks) through a per-device status word that
+:func:`check_status` reads.
+
+On a machine with a GPU the library is mandatory: a missing or stale build
+raises instead of silently falling back to PyTorch.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from pathlib import Path
+
+import torch
+
+_LIB_DIR = Path(__file__).resolve().parent.parent / "_lib"
+_CUDA_LIB = _LIB_DIR / "libxtu_cuda.so"
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+
+c_int, c_float, c_void_p = ctypes.c_int, ctypes.c_float, ctypes.c_void_p
+P = c_void_p  # device pointer / stream handle
+
+# name -> argtypes (all return int status: 0 ok, <0 error)
+_SIGS: dict[str, list] = {
+    "xtu_status_size": [],
+    "xtu_mtile_bytes": [],
+    "xtu_gemm_bf16": [P, P, P, c_int, c_int, c_int, c_int, c_int, P, P, P],
+    "xtu_gemm_fp8w": [P, P, P, P, c_int, c_int, c_int, c_int, c_int, P, P],
+    "xtu_build_mtiles": [P, c_int, P, P, c_int, P],
+    "xtu_grouped_gemm": [P, P, P, c_int, P, c_int, c_int, c_int, c_int, c_int, P, P, c_int, c_int, P, P,
+                         c_float, c_float, c_float, P, P],
+}
+
+
+class NativeLibraryMissing(RuntimeError):
+    pass
+
+
+def lib() -> ctypes.CDLL:
+    """Load (once) and return the CUDA kernel library."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not _CUDA_LIB.exists():
+                raise NativeLibraryMissing(
+                    f"{_CUDA_LIB} is not built; run `python -m vllm_xtu_moe_b200._build`")
+            L = ctypes.CDLL(str(_CUDA_LIB), mode=ctypes.RTLD_GLOBAL)
+            for name, args in _SIGS.items():
+                fn = getattr(L, name, None)
+                if fn is None:
+                    continue
+                fn.argtypes = args
+                fn.restype = c_int
+            _lib = L
+    return _lib
+
+
+def has_symbol(name: str) -> bool:
+    try:
+        return hasattr(lib(), name)
+    except NativeLibraryMissing:
+        return False
+
+
+def call(name: str, *args) -> int:
+    rc = getattr(lib(), name)(*args)
+    if rc < 0:
+        raise RuntimeError(f"{name} failed with code {rc}")
+    return rc
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def stream_ptr(device: torch.device | None = None) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+# ---------------------------------------------------------------------------
+# per-device status word
+# ---------------------------------------------------------------------------
+_status: dict[int, torch.Tensor] = {}
+
+ERROR_NAMES = {1: "mbarrier wait timed out", 2: "peer flag wait timed out",
+               3: "host flag wait timed out", 4: "bounds check failed"}
+
+
+def status_buffer(device: torch.device | int | None = None) -> torch.Tensor:
+    dev = torch.device("cuda", torch.cuda.current_device() if device is None else
+                       (device if isinstance(device, int) else (device.index or 0)))
+    t = _status.get(dev.index)
+    if t is None:
+        t = torch.zeros(4, dtype=torch.int32, device=dev)
+        _status[dev.index] = t
+    return t
+
+
+def check_status(device=None, reset: bool = True) -> None:
+    """Raise if any kernel on `device` recorded an error since the last check."""
+    st = status_buffer(device)
+    vals = st.tolist()
+    if vals[0] != 0:
+        if reset:
+            st.zero_()
+        raise RuntimeError(
+            f"xtu kernel error: {ERROR_NAMES.get(vals[0], vals[0])} (site {vals[1]}, block {vals[2]}, extra {vals[3]})")
+
+
+def native_required() -> bool:
+    """True when the CUDA path must be used (a GPU is present and not overridden)."""
+    return torch.cuda.is_available() and os.environ.get("XTU_ALLOW_TORCH_FALLBACK", "0") != "1"

@@ -1,0 +1,196 @@
+"""Tensor-core GEMMs (tcgen05, sm_100a): dense and grouped per-expert.
+
+``linear(x, w)`` computes ``x @ w.T`` for bf16 weights or for e4m3 weights with
+128x128 fp32 block scales (the HF ``weight`` + ``weight_scale_inv`` pair).  On a
+GPU the hand-written kernels in ``csrc/cuda/gemm_tc.cu`` run; on a CPU the
+PyTorch restatement below runs (it is also the numerics oracle of the tests).
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _native as N
+from .quant import dequant_fp8_block
+
+MTILE_BYTES = 16
+BM = 128
+
+
+def _on_gpu(t: torch.Tensor) -> bool:
+    return t.is_cuda
+
+
+def gemm_bf16(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None,
+              out_dtype: torch.dtype = torch.bfloat16, row_scale: torch.Tensor | None = None) -> torch.Tensor:
+    """out[M,N] = a[M,K] @ b[N,K]^T (bf16 in, fp32 accumulate)."""
+    M, K = a.shape
+    Nn = b.shape[0]
+    if not _on_gpu(a):
+        r = a.float() @ b.float().t()
+        if row_scale is not None:
+            r = r * row_scale.float()[:, None]
+        return r.to(out_dtype) if out is None else out.copy_(r)
+    assert a.dtype == torch.bfloat16 and b.dtype == torch.bfloat16 and b.shape[1] == K
+    assert a.is_contiguous() and b.is_contiguous() and K % 8 == 0
+    if out is None:
+        out = torch.empty(M, Nn, dtype=out_dtype, device=a.device)
+    assert out.stride(1) == 1
+    N.call("xtu_gemm_bf16", a.data_ptr(), b.data_ptr(), out.data_ptr(), M, Nn, K, out.stride(0),
+           int(out.dtype == torch.float32), N.ptr(row_scale), N.status_buffer(a.device).data_ptr(),
+           N.stream_ptr(a.device))
+    return out
+
+
+def gemm_fp8w(a: torch.Tensor, w8: torch.Tensor, w_scale: torch.Tensor, out: torch.Tensor | None = None,
+              out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    """out = a @ dequant(w8, w_scale)^T with e4m3 w8 [N,K] and fp32 scales [ceil(N/128), ceil(K/128)]."""
+    M, K = a.shape
+    Nn = w8.shape[0]
+    if not _on_gpu(a):
+        w = dequant_fp8_block(w8, w_scale).to(torch.bfloat16)
+        r = a.float() @ w.float().t()
+        return r.to(out_dtype) if out is None else out.copy_(r)
+    assert a.dtype == torch.bfloat16 and a.is_contiguous() and w8.is_contiguous() and K % 16 == 0
+    if out is None:
+        out = torch.empty(M, Nn, dtype=out_dtype, device=a.device)
+    N.call("xtu_gemm_fp8w", a.data_ptr(), w8.data_ptr(), w_scale.data_ptr(), out.data_ptr(), M, Nn, K,
+           out.stride(0), int(out.dtype == torch.float32), N.status_buffer(a.device).data_ptr(),
+           N.stream_ptr(a.device))
+    return out
+
+
+def linear(x: torch.Tensor, weight: torch.Tensor, scale: torch.Tensor | None = None,
+           out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    """y = x @ W^T for 2-D or batched x; W bf16 or e4m3 (+ block scales)."""
+    shp = x.shape
+    x2 = x.reshape(-1, shp[-1])
+    if x2.shape[0] == 0:
+        return x.new_empty(*shp[:-1], weight.shape[0], dtype=out_dtype)
+    if not x2.is_contiguous():
+        x2 = x2.contiguous()
+    if scale is None:
+        y = gemm_bf16(x2, weight, out_dtype=out_dtype)
+    else:
+        y = gemm_fp8w(x2, weight, scale, out_dtype=out_dtype)
+    return y.reshape(*shp[:-1], weight.shape[0])
+
+
+# ---------------------------------------------------------------------------
+# grouped (MoE) GEMM
+# ---------------------------------------------------------------------------
+def max_mtiles(num_rows: int, num_experts: int) -> int:
+    return (num_rows + BM - 1) // BM + num_experts
+
+
+def build_mtiles(seg: torch.Tensor, num_rows: int, tiles: torch.Tensor | None = None,
+                 count: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor, int]:
+    """Device list of 128-row tiles per expert segment (seg: int32 [E+1])."""
+    E = seg.numel() - 1
+    mx = max_mtiles(num_rows, E)
+    if tiles is None:
+        tiles = torch.empty(mx * 4, dtype=torch.int32, device=seg.device)
+    if count is None:
+        count = torch.empty(1, dtype=torch.int32, device=seg.device)
+    N.call("xtu_build_mtiles", seg.data_ptr(), E, tiles.data_ptr(), count.data_ptr(), mx, N.stream_ptr(seg.device))
+    return tiles, count, mx
+
+
+EPI_BF16, EPI_F32, EPI_SWIGLU = 0, 1, 2
+
+
+def grouped_gemm(a: torch.Tensor, w: torch.Tensor, seg: torch.Tensor, *, w_scale: torch.Tensor | None = None,
+                 epilogue: int = EPI_BF16, out: torch.Tensor | None = None, row_scale: torch.Tensor | None = None,
+                 row_dest: torch.Tensor | None = None, out_rows: int | None = None,
+                 act_limit: float = 0.0, act_alpha: float = 1.0, act_beta: float = 0.0,
+                 tiles: tuple[torch.Tensor, torch.Tensor, int] | None = None) -> torch.Tensor:
+    """Grouped GEMM: rows a[seg[e]:seg[e+1]] are multiplied by w[e]^T.
+
+    w is [E, N, K] bf16, or e4m3 with w_scale [E, ceil(N/128), ceil(K/128)].
+    epilogue EPI_SWIGLU expects w rows arranged in 256-row blocks of
+    (128 gate rows, 128 up rows) (see :func:`interleave_gate_up`) and writes
+    [rows, N/2] bf16.  row_scale multiplies each output row; row_dest scatters
+    row m to out[row_dest[m]] (rows with row_dest < 0 are dropped).
+    """
+    M, K = a.shape
+    E, Nn, Kw = w.shape
+    assert Kw == K
+    out_cols = Nn // 2 if epilogue == EPI_SWIGLU else Nn
+    rows = out_rows if out_rows is not None else M
+    if out is None:
+        dt = torch.float32 if epilogue == EPI_F32 else torch.bfloat16
+        out = torch.zeros(rows, out_cols, dtype=dt, device=a.device)
+    if M == 0:
+        return out
+    if not _on_gpu(a):
+        return _grouped_gemm_torch(a, w, seg, w_scale, epilogue, out, row_scale, row_dest, act_limit,
+                                   act_alpha, act_beta)
+    assert a.dtype == torch.bfloat16 and a.is_contiguous() and w.is_contiguous()
+    assert seg.dtype == torch.int32 and seg.is_cuda
+    if tiles is None:
+        tiles = build_mtiles(seg, M)
+    t, cnt, mx = tiles
+    bfmt = 1 if w_scale is not None else 0
+    if bfmt:
+        assert w.dtype in (torch.float8_e4m3fn, torch.uint8)
+    else:
+        assert w.dtype == torch.bfloat16
+    N.call("xtu_grouped_gemm", a.data_ptr(), w.data_ptr(), N.ptr(w_scale), bfmt, out.data_ptr(), out.stride(0),
+           M, Nn, K, E, t.data_ptr(), cnt.data_ptr(), mx, epilogue, N.ptr(row_scale), N.ptr(row_dest),
+           float(act_limit), float(act_alpha), float(act_beta), N.status_buffer(a.device).data_ptr(),
+           N.stream_ptr(a.device))
+    return out
+
+
+def silu_and_mul_clamped(g: torch.Tensor, u: torch.Tensor, limit: float = 0.0, alpha: float = 1.0,
+                         beta: float = 0.0) -> torch.Tensor:
+    """Clamped gated SiLU: clamp(g, max=limit) * sigmoid(alpha*g') * (clamp(u, +-limit) + beta)."""
+    g = g.float()
+    u = u.float()
+    if limit > 0:
+        g = g.clamp(max=limit)
+        u = u.clamp(-limit, limit)
+    return g * torch.sigmoid(alpha * g) * (u + beta)
+
+
+def interleave_gate_up(w13: torch.Tensor, block: int = 128) -> torch.Tensor:
+    """[.., 2I, K] (gate rows then up rows) -> rows in (gate block, up block) pairs of `block` rows."""
+    *lead, two_i, K = w13.shape
+    I = two_i // 2
+    assert I % block == 0
+    g = w13[..., :I, :].reshape(*lead, I // block, block, K)
+    u = w13[..., I:, :].reshape(*lead, I // block, block, K)
+    return torch.stack([g, u], dim=-3).reshape(*lead, two_i, K).contiguous()
+
+
+def interleave_gate_up_scale(s13: torch.Tensor) -> torch.Tensor:
+    """Matching reorder of [.., 2I/128, K/128] block scales (one scale row per 128 rows)."""
+    *lead, nb, kb = s13.shape
+    h = nb // 2
+    g = s13[..., :h, :]
+    u = s13[..., h:, :]
+    return torch.stack([g, u], dim=-2).reshape(*lead, nb, kb).contiguous()
+
+
+def _grouped_gemm_torch(a, w, seg, w_scale, epilogue, out, row_scale, row_dest, limit, alpha, beta):
+    segl = seg.tolist()
+    for e in range(w.shape[0]):
+        s0, s1 = segl[e], segl[e + 1]
+        if s1 <= s0:
+            continue
+        we = w[e]
+        if w_scale is not None:
+            we = dequant_fp8_block(we, w_scale[e]).to(torch.bfloat16)
+        y = a[s0:s1].float() @ we.float().t()
+        if epilogue == EPI_SWIGLU:
+            n = y.shape[1]
+            yb = y.reshape(y.shape[0], n // 256, 2, 128)
+            y = silu_and_mul_clamped(yb[:, :, 0], yb[:, :, 1], limit, alpha, beta).reshape(y.shape[0], n // 2)
+        if row_scale is not None:
+            y = y * row_scale[s0:s1].float()[:, None]
+        if row_dest is not None:
+            d = row_dest[s0:s1].long()
+            keep = d >= 0
+            out[d[keep]] = y[keep].to(out.dtype)
+        else:
+            out[s0:s1] = y.to(out.dtype)
+    return out

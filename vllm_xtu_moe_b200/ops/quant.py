@@ -1,0 +1,139 @@
+"""Weight formats of the expert checkpoints and their PyTorch reference codecs.
+
+Formats (the HF safetensors layouts the reference loads):
+
+* **fp8 block-128** -- ``weight`` e4m3 ``[N, K]`` and ``weight_scale_inv`` fp32
+  ``[ceil(N/128), ceil(K/128)]``; ``W[n,k] = e4m3[n,k] * scale[n//128, k//128]``
+  (reference: xiaotu_moe/csrc/moe/moe_v2_fp8.hpp:1-20, mixed_experts.py:3326-3333).
+* **MXFP4** -- e2m1 nibbles packed along K (low nibble = even k), ``[N, K/2]`` u8,
+  and e8m0 scales ``[N, K/32]`` u8 with value ``2^(b-127)``
+  (reference: vllm_xiaotu_moe/gpu_prefill.py:14-21).
+* **NVFP4** -- e2m1 nibbles as above, e4m3 scales per 16 along K ``[N, K/16]`` and
+  one fp32 ``weight_scale_2`` per tensor (reference: hybrid_model.py:477-530).
+
+These functions are the numerics oracle for the GPU and CPU kernels, and the
+random-init quantizers used by the synthetic-weight factory.
+"""
+from __future__ import annotations
+
+import torch
+
+FP8_MAX = 448.0
+E2M1_VALUES = torch.tensor([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0,
+                            -0.0, -0.5, -1.0, -1.5, -2.0, -3.0, -4.0, -6.0], dtype=torch.float32)
+
+
+# ---------------------------------------------------------------------------
+# fp8 e4m3 with 128x128 block scales
+# ---------------------------------------------------------------------------
+def _expand_blocks(s: torch.Tensor, n: int, k: int, bn: int = 128, bk: int = 128) -> torch.Tensor:
+    return s.repeat_interleave(bn, dim=-2)[..., :n, :].repeat_interleave(bk, dim=-1)[..., :k]
+
+
+def quant_fp8_block(w: torch.Tensor, block: int = 128) -> tuple[torch.Tensor, torch.Tensor]:
+    """w [..., N, K] float -> (e4m3 [..., N, K], fp32 scales [..., ceil(N/b), ceil(K/b)])."""
+    *lead, n, k = w.shape
+    nb, kb = (n + block - 1) // block, (k + block - 1) // block
+    wp = torch.zeros(*lead, nb * block, kb * block, dtype=torch.float32, device=w.device)
+    wp[..., :n, :k] = w.float()
+    blocks = wp.reshape(*lead, nb, block, kb, block)
+    amax = blocks.abs().amax(dim=(-3, -1)).clamp(min=1e-12)
+    scale = amax / FP8_MAX
+    q = (blocks / scale[..., :, None, :, None]).clamp(-FP8_MAX, FP8_MAX)
+    q = q.reshape(*lead, nb * block, kb * block)[..., :n, :k].to(torch.float8_e4m3fn)
+    return q.contiguous(), scale.contiguous()
+
+
+def dequant_fp8_block(q: torch.Tensor, scale: torch.Tensor, block: int = 128) -> torch.Tensor:
+    """e4m3 [..., N, K] (or its uint8 bit pattern) * block scales -> fp32."""
+    if q.dtype == torch.uint8:
+        q = q.view(torch.float8_e4m3fn)
+    n, k = q.shape[-2], q.shape[-1]
+    return q.float() * _expand_blocks(scale.float(), n, k, block, block)
+
+
+# ---------------------------------------------------------------------------
+# e2m1 (fp4) helpers
+# ---------------------------------------------------------------------------
+def _round_to_e2m1_codes(x: torch.Tensor) -> torch.Tensor:
+    """Round-to-nearest-even onto the e2m1 grid; returns 4-bit codes (sign in bit 3)."""
+    mag = x.abs().clamp(max=6.0)
+    grid = E2M1_VALUES[:8].to(x.device)
+    # nearest grid point; ties go to the even mantissa (codes 0,2,4,6 are even)
+    d = (mag[..., None] - grid).abs()
+    best = d.min(dim=-1, keepdim=True).values
+    cand = (d <= best + 1e-12)
+    codes = torch.arange(8, device=x.device)
+    # prefer even code among ties
+    score = cand.float() * 2.0 + (codes % 2 == 0).float()
+    code = score.argmax(dim=-1)
+    sign = (x < 0) & (code > 0)
+    return (code + sign.long() * 8).to(torch.uint8)
+
+
+def pack_nibbles(codes: torch.Tensor) -> torch.Tensor:
+    """[..., K] 4-bit codes -> [..., K/2] bytes, low nibble = even k."""
+    lo = codes[..., 0::2]
+    hi = codes[..., 1::2]
+    return (lo | (hi << 4)).to(torch.uint8).contiguous()
+
+
+def unpack_nibbles(packed: torch.Tensor) -> torch.Tensor:
+    lo = packed & 0x0F
+    hi = packed >> 4
+    return torch.stack([lo, hi], dim=-1).reshape(*packed.shape[:-1], packed.shape[-1] * 2)
+
+
+def e2m1_decode(codes: torch.Tensor) -> torch.Tensor:
+    return E2M1_VALUES.to(codes.device)[codes.long()]
+
+
+# ---------------------------------------------------------------------------
+# MXFP4: e2m1 + e8m0 per 32 along K
+# ---------------------------------------------------------------------------
+def quant_mxfp4(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """w [..., N, K] -> (packed [..., N, K/2] u8, e8m0 scales [..., N, K/32] u8)."""
+    *lead, n, k = w.shape
+    assert k % 32 == 0
+    blocks = w.float().reshape(*lead, n, k // 32, 32)
+    amax = blocks.abs().amax(dim=-1).clamp(min=2.0 ** -126)
+    # smallest power of two s with amax / s <= 6
+    e = torch.ceil(torch.log2(amax / 6.0)).clamp(-127, 127)
+    scale = torch.pow(2.0, e)
+    codes = _round_to_e2m1_codes(blocks / scale[..., None]).reshape(*lead, n, k)
+    return pack_nibbles(codes), (e + 127).to(torch.uint8).contiguous()
+
+
+def dequant_mxfp4(packed: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
+    codes = unpack_nibbles(packed)
+    vals = e2m1_decode(codes)
+    s = torch.pow(2.0, scales.float() - 127.0)
+    *lead, n, k = vals.shape
+    return (vals.reshape(*lead, n, k // 32, 32) * s[..., None]).reshape(*lead, n, k)
+
+
+# ---------------------------------------------------------------------------
+# NVFP4: e2m1 + e4m3 per 16 along K + fp32 per-tensor scale
+# ---------------------------------------------------------------------------
+def quant_nvfp4(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """w [..., N, K] -> (packed u8 [..., N, K/2], e4m3 scales [..., N, K/16], fp32 global scale [])."""
+    *lead, n, k = w.shape
+    assert k % 16 == 0
+    blocks = w.float().reshape(*lead, n, k // 16, 16)
+    amax = blocks.abs().amax(dim=-1)
+    gscale = (amax.max() / (6.0 * FP8_MAX)).clamp(min=1e-12)
+    s = (amax / 6.0 / gscale).clamp(max=FP8_MAX).to(torch.float8_e4m3fn)
+    sf = s.float() * gscale
+    sf = torch.where(sf > 0, sf, torch.ones_like(sf))
+    codes = _round_to_e2m1_codes(blocks / sf[..., None]).reshape(*lead, n, k)
+    return pack_nibbles(codes), s.contiguous(), gscale.reshape(()).float()
+
+
+def dequant_nvfp4(packed: torch.Tensor, scales: torch.Tensor, gscale: torch.Tensor | float) -> torch.Tensor:
+    codes = unpack_nibbles(packed)
+    vals = e2m1_decode(codes)
+    if scales.dtype == torch.uint8:
+        scales = scales.view(torch.float8_e4m3fn)
+    s = scales.float() * float(gscale)
+    *lead, n, k = vals.shape
+    return (vals.reshape(*lead, n, k // 16, 16) * s[..., None]).reshape(*lead, n, k)
