@@ -1,0 +1,279 @@
+"""Serving benchmark: prefill tok/s & decode tok/s for long synthetic prompts at
+concurrency C, on N GPUs of one node (one rank per GPU, data-parallel replicas).
+
+One *step* = one serving round per rank: C requests of ``--prompt-len`` uniform
+random token ids are submitted together, prefilled (chunked), then decoded for
+``--output-len`` tokens each (greedy).  Model: GLM-4.5-Air-style MoE
+(46 layers, hidden 4096, GQA 96/8 x 128, partial RoPE,
+128 experts top-8 + 1 shared, I=1408, fp8 e4m3 128x128 block-scaled weights,
+random init).  The weights (~110 GB) and the KV cache are read every step, far
+beyond the 126 MB L2, so no L2 flush is needed between steps.
+
+``value`` is the device-timed aggregate decode throughput (CUDA events on the
+launching stream around the decode window, max over ranks); prefill tok/s and
+the decode step time are reported beside it.  ``e2e`` repeats the measurement
+through the public API (``LLM.generate``) with a host clock, including the
+host->device copy of each round's prompts and the device->host reads of every
+sampled token.
+
+Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+       (N > 1: launch with torch.distributed.run, one process per GPU)
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+METRIC = "prefill tok/s & decode tok/s (15K prompt, C=1/2/4); decode step ms"
+BASELINE_DECODE = {1: 29.8, 2: 31.6, 4: 37.2}     # GLM-5.3-Flash decode tok/s, README_EN.md:78-80
+BASELINE_PREFILL = {1: 1477.0, 2: 1441.0, 4: 1394.0}
+
+REFERENCE_UNAVAILABLE = (
+    "reference plugin does not import against the installed vLLM 0.22 "
+    "(ModuleNotFoundError: vllm.models.deepseek_v4.common.mm_preprocess); its serving path needs the "
+    "patched vLLM tree from patches/, its CPU engine .so (not produced by pip install) and real checkpoints")
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--model", default="glm-4.5-air")
+    ap.add_argument("--concurrency", type=int, default=4)
+    ap.add_argument("--prompt-len", type=int, default=14500)
+    ap.add_argument("--output-len", type=int, default=256)
+    ap.add_argument("--num-spec", type=int, default=0, help="MTP draft tokens per step (0 = off)")
+    ap.add_argument("--max-batched-tokens", type=int, default=16384)
+    ap.add_argument("--layers", type=int, default=None, help="debug only: fewer layers (invalidates the number)")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self.t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.idx), "-lms", "200"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.t = threading.Thread(target=self._read, daemon=True)
+        self.t.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def reference_arm(args):
+    line = {"impl": "reference", "unavailable": REFERENCE_UNAVAILABLE}
+    rank = int(os.environ.get("RANK", "0"))
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if os.environ.get("XTU_BENCH_WATCHDOG"):
+        import faulthandler
+        faulthandler.dump_traceback_later(int(os.environ["XTU_BENCH_WATCHDOG"]), repeat=True)
+    if args.impl == "reference":
+        return reference_arm(args)
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=600))
+
+    from vllm_xtu_moe_b200.engine import LLM, SamplingParams
+    from vllm_xtu_moe_b200.engine.runner import RunnerConfig
+    from vllm_xtu_moe_b200.engine.sequence import Status
+    from vllm_xtu_moe_b200.models.config import get_preset
+    from vllm_xtu_moe_b200.ops import _native as N
+
+    cfg = get_preset(args.model)
+    C, P, O = args.concurrency, args.prompt_len, args.output_len
+    rc = RunnerConfig(block_size=64, max_seqs=max(C, 1), max_batched_tokens=args.max_batched_tokens,
+                      max_model_len=P + O + 64, use_cuda_graph=True, graph_batch_sizes=(1, 2, 4, 8, 16),
+                      num_spec=args.num_spec)
+    t0 = time.time()
+    llm = LLM(cfg, device=str(dev), seed=1234, runner_config=rc, num_layers=args.layers)
+    torch.cuda.synchronize()
+    init_s = time.time() - t0
+    gen = torch.Generator().manual_seed(rank * 7919 + 1)
+
+    def prompts():
+        return [torch.randint(0, cfg.vocab_size, (P,), generator=gen).tolist() for _ in range(C)]
+
+    stream = torch.cuda.current_stream()
+
+    def one_round():
+        """Returns (prefill_ms, decode_ms, decode_steps) device-timed."""
+        ev0, ev_p, ev1 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        for p in prompts():
+            llm.add_request(p, SamplingParams(max_tokens=O, ignore_eos=True))
+        ev0.record(stream)
+        prefill_done = False
+        dsteps = 0
+        while llm.scheduler.has_work():
+            plan = llm.scheduler.schedule()
+            if plan is None:
+                break
+            if plan.is_decode and not prefill_done:
+                ev_p.record(stream)
+                prefill_done = True
+            llm.step(plan)
+            dsteps += int(plan.is_decode)
+        if not prefill_done:
+            ev_p.record(stream)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        return ev0.elapsed_time(ev_p), ev_p.elapsed_time(ev1), dsteps
+
+    def log(msg):
+        if rank == 0:
+            print(f"[bench +{time.time() - t0:.1f}s] {msg}", file=sys.stderr, flush=True)
+
+    log(f"init {init_s:.1f}s, weights {llm.model.nbytes() / 2**30:.1f} GiB, kv blocks {rc.num_blocks}")
+    # warm-up rounds (also captures the decode CUDA graphs)
+    for i in range(args.warmup):
+        a, b, s = one_round()
+        N.check_status()
+        log(f"warmup {i}: prefill {a:.1f} ms, decode {b:.1f} ms / {s} steps")
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
+    n_launch0 = N.launches()
+    pre_ms, dec_ms, dsteps = [], [], []
+    ev_a, ev_b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev_a.record(stream)
+    for i in range(args.steps):
+        a, b, s = one_round()
+        log(f"step {i}: prefill {a:.1f} ms, decode {b:.1f} ms / {s} steps")
+        pre_ms.append(a)
+        dec_ms.append(b)
+        dsteps.append(s)
+    ev_b.record(stream)
+    torch.cuda.synchronize()
+    total_ms = ev_a.elapsed_time(ev_b)
+    launches = N.launches() - n_launch0
+    clocks = sampler.stop()
+    if world > 1:
+        dist.barrier()
+
+    # ---- e2e through the public API (host clock, includes H2D of prompts and D2H of tokens)
+    e2e = None
+    if not args.no_e2e:
+        e2e_dec, e2e_pre = [], []
+        for _ in range(max(1, args.steps)):
+            ps = prompts()
+            torch.cuda.synchronize()
+            t_a = time.perf_counter()
+            outs = llm.generate(ps, SamplingParams(max_tokens=O, ignore_eos=True))
+            t_b = time.perf_counter()
+            ttft = max(o.ttft_s for o in outs)
+            e2e_pre.append(C * P / ttft)
+            e2e_dec.append(C * (O - 1) / max(1e-9, (t_b - t_a) - ttft))
+        e2e = {"value": statistics.median(e2e_dec) * world, "unit": "tok/s",
+               "prefill_tok_s": statistics.median(e2e_pre) * world,
+               "h2d_bytes_per_step": C * P * 4 + C * O * 64,
+               "d2h_bytes_per_step": C * O * 4}
+
+    # ---- aggregate over ranks: value = sum of tokens / max time
+    mean_pre = sum(pre_ms) / len(pre_ms)
+    mean_dec = sum(dec_ms) / len(dec_ms)
+    step_ms = total_ms / args.steps
+    vals = torch.tensor([mean_pre, mean_dec, step_ms, sum(dsteps) / len(dsteps)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    mean_pre, mean_dec, step_ms, avg_dsteps = vals.tolist()
+    decode_tok_s = world * C * (O - 1) / (mean_dec / 1e3)
+    prefill_tok_s = world * C * P / (mean_pre / 1e3)
+    if rank == 0:
+        base = BASELINE_DECODE.get(C)
+        line = {
+            "metric": METRIC, "value": round(decode_tok_s, 2), "unit": "tok/s (decode, aggregate)",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 2),
+            "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": round(decode_tok_s / base, 3) if base else None,
+            "dtype": "bf16", "data": "synthetic (uniform random token ids, random-init weights)",
+            "prefill_tok_s": round(prefill_tok_s, 1),
+            "prefill_vs_baseline": round(prefill_tok_s / BASELINE_PREFILL[C], 3) if C in BASELINE_PREFILL else None,
+            "decode_step_ms": round(mean_dec / max(1.0, avg_dsteps), 3),
+            "config": {"model": cfg.name + " (GLM-4.5-Air-style, BASELINE config 4)", "global_batch": world * C,
+                       "concurrency_per_gpu": C, "seq_len": P, "output_len": O, "parallelism": f"dp{world}",
+                       "weights": f"experts {cfg.expert_fmt}, dense {cfg.dense_fmt}, block 128x128",
+                       "mtp_draft_tokens": args.num_spec, "max_batched_tokens": args.max_batched_tokens,
+                       "l2": "inputs larger than L2 (weights + KV cache read every step); no flush",
+                       "layers": args.layers or cfg.num_layers},
+            "clocks": clocks, "e2e": e2e, "gpu_launches": launches, "init_s": round(init_s, 1),
+        }
+        if args.layers:
+            line["invalid"] = "debug run with fewer layers"
+        print(json.dumps(line), flush=True)
+    llm.shutdown()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+    main()

@@ -1,0 +1,617 @@
+// Memory-bound hot ops around the tensor-core GEMMs (sm_100a):
+//   * RMSNorm with fused residual add (W15)
+//   * RoPE (full / partial, NeoX or interleaved) + optional per-head q/k RMSNorm,
+//     fused with the paged KV-cache write (W16)
+//   * router: softmax / sigmoid scoring, correction bias, group-limited top-k,
+//     renormalisation and scaling, one warp per token (W8; replaces vLLM's
+//     fused_topk_bias used at vllm_xiaotu_moe/hybrid_model.py:1877-1890)
+//   * MoE routing permute: histogram -> prefix sum -> scatter + row gather (W3;
+//     replaces the torch argsort/scatter/cumsum of gpu_prefill.py:800-883),
+//     with an id filter that sends pairs of other tiers (CPU / remote) nowhere (W7)
+//   * MoE combine: deterministic per-token sum of the top-k slot rows (+ shared
+//     expert, + optional extra partial), no global atomics (W2)
+//   * greedy argmax and embedding gather
+// All kernels vectorise to 16-byte accesses where the row length allows.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+#include <cfloat>
+#include "ptx.cuh"
+
+namespace xtu {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+template <int NT>
+__device__ __forceinline__ float block_sum(float v, float* sh) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) sh[w] = v;
+  __syncthreads();
+  if (w == 0) {
+    float t = l < NT / 32 ? sh[l] : 0.f;
+    t = warp_sum(t);
+    if (l == 0) sh[0] = t;
+  }
+  __syncthreads();
+  const float r = sh[0];
+  __syncthreads();
+  return r;
+}
+
+// ---------------------------------------------------------------------------
+// RMSNorm:  r = x (+ residual);  residual_out = r;  y = r * rsqrt(mean(r^2) + eps) * (w [+ 1])
+// ---------------------------------------------------------------------------
+template <int NT>
+__global__ void __launch_bounds__(NT) rmsnorm_kernel(const __nv_bfloat16* __restrict__ x,
+                                                     const __nv_bfloat16* __restrict__ residual,
+                                                     __nv_bfloat16* __restrict__ residual_out,
+                                                     const __nv_bfloat16* __restrict__ w,
+                                                     __nv_bfloat16* __restrict__ y, int H, float eps, int add_one,
+                                                     int x_stride, int y_stride) {
+  extern __shared__ float row[];  // H floats
+  __shared__ float sh[32];
+  const int t = blockIdx.x;
+  const __nv_bfloat16* xr = x + (size_t)t * x_stride;
+  float ss = 0.f;
+  for (int i = threadIdx.x * 8; i < H; i += NT * 8) {
+    const uint4 xv = *reinterpret_cast<const uint4*>(xr + i);
+    const uint32_t xs[4] = {xv.x, xv.y, xv.z, xv.w};
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) { v[2 * j] = bf16_lo(xs[j]); v[2 * j + 1] = bf16_hi(xs[j]); }
+    if (residual) {
+      const uint4 rv = *reinterpret_cast<const uint4*>(residual + (size_t)t * H + i);
+      const uint32_t rs[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) { v[2 * j] += bf16_lo(rs[j]); v[2 * j + 1] += bf16_hi(rs[j]); }
+      uint4 o;
+      o.x = pack_bf16x2(v[0], v[1]); o.y = pack_bf16x2(v[2], v[3]);
+      o.z = pack_bf16x2(v[4], v[5]); o.w = pack_bf16x2(v[6], v[7]);
+      *reinterpret_cast<uint4*>(residual_out + (size_t)t * H + i) = o;
+      // normalise the bf16-rounded sum, as an unfused add-then-norm would
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t pj = j == 0 ? o.x : j == 1 ? o.y : j == 2 ? o.z : o.w;
+        v[2 * j] = bf16_lo(pj); v[2 * j + 1] = bf16_hi(pj);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) { row[i + j] = v[j]; ss += v[j] * v[j]; }
+  }
+  const float tot = block_sum<NT>(ss, sh);
+  const float inv = rsqrtf(tot / (float)H + eps);
+  __nv_bfloat16* yr = y + (size_t)t * y_stride;
+  for (int i = threadIdx.x * 8; i < H; i += NT * 8) {
+    const uint4 wv = *reinterpret_cast<const uint4*>(w + i);
+    const uint32_t ws[4] = {wv.x, wv.y, wv.z, wv.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float w0 = bf16_lo(ws[j]), w1 = bf16_hi(ws[j]);
+      if (add_one) { w0 += 1.f; w1 += 1.f; }
+      o[j] = pack_bf16x2(row[i + 2 * j] * inv * w0, row[i + 2 * j + 1] * inv * w1);
+    }
+    *reinterpret_cast<uint4*>(yr + i) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// RoPE + optional per-head RMSNorm on q/k + paged KV-cache write.
+// q [T, Hq, D] (row stride q_stride), k [T, Hk, D], v [T, Hk, Dv] (strides given)
+// cos_sin [max_pos, rot] fp32: first rot/2 = cos, next rot/2 = sin.
+// Cache layout: [num_blocks, Hk, block_size, D] bf16; slot = block*block_size + offset.
+// One warp per (token, head); heads [0,Hq) are q, [Hq, Hq+Hk) are k (+v copy).
+// ---------------------------------------------------------------------------
+__global__ void rope_kv_kernel(__nv_bfloat16* __restrict__ q, __nv_bfloat16* __restrict__ k,
+                               const __nv_bfloat16* __restrict__ v, const int* __restrict__ positions,
+                               const float* __restrict__ cos_sin, int T, int Hq, int Hk, int D, int Dv, int rot,
+                               int neox, int q_stride, int k_stride, int v_stride,
+                               const __nv_bfloat16* __restrict__ q_norm_w, const __nv_bfloat16* __restrict__ k_norm_w,
+                               float norm_eps, int norm_add_one, const int* __restrict__ slot_mapping,
+                               __nv_bfloat16* __restrict__ k_cache, __nv_bfloat16* __restrict__ v_cache,
+                               int block_size) {
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int H = Hq + Hk;
+  if (gw >= T * H) return;
+  const int t = gw / H;
+  const int h = gw - t * H;
+  const bool is_q = h < Hq;
+  __nv_bfloat16* ptr = is_q ? q + (size_t)t * q_stride + (size_t)h * D : k + (size_t)t * k_stride + (size_t)(h - Hq) * D;
+  const __nv_bfloat16* nw = is_q ? q_norm_w : k_norm_w;
+  // load the head (D <= 512): each lane holds D/32 values
+  float vals[16];
+  const int per = D / 32;
+  for (int j = 0; j < per; ++j) vals[j] = __bfloat162float(ptr[lane + 32 * j]);
+  if (nw) {
+    float ss = 0.f;
+    for (int j = 0; j < per; ++j) ss += vals[j] * vals[j];
+    ss = warp_sum(ss);
+    const float inv = rsqrtf(ss / (float)D + norm_eps);
+    for (int j = 0; j < per; ++j) {
+      float wv = __bfloat162float(nw[lane + 32 * j]);
+      if (norm_add_one) wv += 1.f;
+      // round like an unfused bf16 norm output
+      vals[j] = __bfloat162float(__float2bfloat16(vals[j] * inv * wv));
+    }
+  }
+  // write back normalised values, then rotate in place through global memory
+  for (int j = 0; j < per; ++j) ptr[lane + 32 * j] = __float2bfloat16(vals[j]);
+  __syncwarp();
+  const int pos = positions[t];
+  const float* cs = cos_sin + (size_t)pos * rot;
+  const int half = rot / 2;
+  // each lane rotates pairs i in [lane, half) step 32
+  for (int i = lane; i < half; i += 32) {
+    int i0, i1;
+    if (neox) { i0 = i; i1 = i + half; } else { i0 = 2 * i; i1 = 2 * i + 1; }
+    const float x0 = __bfloat162float(ptr[i0]);
+    const float x1 = __bfloat162float(ptr[i1]);
+    const float c = cs[i], s = cs[half + i];
+    ptr[i0] = __float2bfloat16(x0 * c - x1 * s);
+    ptr[i1] = __float2bfloat16(x1 * c + x0 * s);
+  }
+  __syncwarp();
+  if (!is_q && k_cache) {
+    const int slot = slot_mapping[t];
+    if (slot >= 0) {
+      const int hk = h - Hq;
+      const int blk = slot / block_size, off = slot - blk * block_size;
+      __nv_bfloat16* kc = k_cache + (((size_t)blk * Hk + hk) * block_size + off) * D;
+      for (int j = lane; j < D; j += 32) kc[j] = ptr[j];
+      const __nv_bfloat16* vr = v + (size_t)t * v_stride + (size_t)hk * Dv;
+      __nv_bfloat16* vc = v_cache + (((size_t)blk * Hk + hk) * block_size + off) * Dv;
+      for (int j = lane; j < Dv; j += 32) vc[j] = vr[j];
+    }
+  }
+}
+
+// plain paged KV write (no rope), e.g. for layers without positional rotation
+__global__ void kv_write_kernel(const __nv_bfloat16* __restrict__ k, const __nv_bfloat16* __restrict__ v, int T,
+                                int Hk, int D, int Dv, int k_stride, int v_stride, const int* __restrict__ slot_mapping,
+                                __nv_bfloat16* __restrict__ k_cache, __nv_bfloat16* __restrict__ v_cache,
+                                int block_size) {
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (gw >= T * Hk) return;
+  const int t = gw / Hk, h = gw - t * Hk;
+  const int slot = slot_mapping[t];
+  if (slot < 0) return;
+  const int blk = slot / block_size, off = slot - blk * block_size;
+  __nv_bfloat16* kc = k_cache + (((size_t)blk * Hk + h) * block_size + off) * D;
+  __nv_bfloat16* vc = v_cache + (((size_t)blk * Hk + h) * block_size + off) * Dv;
+  for (int j = lane; j < D; j += 32) kc[j] = k[(size_t)t * k_stride + (size_t)h * D + j];
+  for (int j = lane; j < Dv; j += 32) vc[j] = v[(size_t)t * v_stride + (size_t)h * Dv + j];
+}
+
+// ---------------------------------------------------------------------------
+// router top-k, one warp per token, E <= 1024 (32 scores per lane)
+// scoring: 0 softmax, 1 sigmoid, 2 sqrt(softplus)
+// selection uses score + bias; weights use the unbiased score.
+// n_group > 1: group score = sum of the top-2 biased scores of the group;
+// keep the best topk_group groups (DeepSeek-V3 "noaux_tc").
+// ---------------------------------------------------------------------------
+__global__ void router_topk_kernel(const float* __restrict__ logits, const float* __restrict__ bias, int T, int E,
+                                   int K, int scoring, int n_group, int topk_group, int renorm, float scale,
+                                   int* __restrict__ out_ids, float* __restrict__ out_w, int logits_stride) {
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (gw >= T) return;
+  const float* lg = logits + (size_t)gw * logits_stride;
+  constexpr int MAXP = 32;
+  float sc[MAXP], sel[MAXP];
+  const int per = (E + 31) / 32;
+  float mx = -FLT_MAX;
+  for (int j = 0; j < per; ++j) {
+    const int e = lane + 32 * j;
+    sc[j] = e < E ? lg[e] : -FLT_MAX;
+    mx = fmaxf(mx, sc[j]);
+  }
+  if (scoring == 0) {
+    mx = warp_max(mx);
+    float s = 0.f;
+    for (int j = 0; j < per; ++j) {
+      const int e = lane + 32 * j;
+      sc[j] = e < E ? __expf(sc[j] - mx) : 0.f;
+      s += sc[j];
+    }
+    s = warp_sum(s);
+    const float inv = 1.f / s;
+    for (int j = 0; j < per; ++j) sc[j] *= inv;
+  } else if (scoring == 1) {
+    for (int j = 0; j < per; ++j) sc[j] = 1.f / (1.f + __expf(-sc[j]));
+  } else {
+    for (int j = 0; j < per; ++j) {
+      const float x = sc[j];
+      const float sp = x > 20.f ? x : log1pf(__expf(x));
+      sc[j] = sqrtf(sp);
+    }
+  }
+  for (int j = 0; j < per; ++j) {
+    const int e = lane + 32 * j;
+    sel[j] = e < E ? sc[j] + (bias ? bias[e] : 0.f) : -FLT_MAX;
+  }
+  if (n_group > 1 && topk_group < n_group) {
+    // group g covers experts [g*gs, (g+1)*gs); experts of lane l, slot j: e = l + 32 j
+    const int gs = E / n_group;
+    __shared__ float gscore_sh[8][64];
+    float* gscore = gscore_sh[(threadIdx.x >> 5) & 7];
+    for (int g = 0; g < n_group; ++g) {
+      // top-2 within group g
+      float b1 = -FLT_MAX, b2 = -FLT_MAX;
+      for (int j = 0; j < per; ++j) {
+        const int e = lane + 32 * j;
+        if (e < E && e / gs == g) {
+          const float v = sel[j];
+          if (v > b1) { b2 = b1; b1 = v; } else if (v > b2) b2 = v;
+        }
+      }
+      // warp reduce top-2
+      for (int o = 16; o > 0; o >>= 1) {
+        const float o1 = __shfl_xor_sync(0xffffffffu, b1, o);
+        const float o2 = __shfl_xor_sync(0xffffffffu, b2, o);
+        float n1 = fmaxf(b1, o1);
+        float n2 = fmaxf(fminf(b1, o1), fmaxf(b2, o2));
+        b1 = n1; b2 = n2;
+      }
+      if (lane == 0) gscore[g] = b1 + b2;
+    }
+    __syncwarp();
+    // pick topk_group groups
+    unsigned long long keep = 0ull;
+    for (int r = 0; r < topk_group; ++r) {
+      int best = -1; float bv = -FLT_MAX;
+      for (int g = 0; g < n_group; ++g)
+        if (!((keep >> g) & 1ull) && gscore[g] > bv) { bv = gscore[g]; best = g; }
+      if (best >= 0) keep |= 1ull << best;
+    }
+    for (int j = 0; j < per; ++j) {
+      const int e = lane + 32 * j;
+      if (e < E && !((keep >> (e / gs)) & 1ull)) sel[j] = -FLT_MAX;
+    }
+  }
+  float wsum = 0.f;
+  float myw = 0.f;
+  int myid = -1;
+  for (int r = 0; r < K; ++r) {
+    float bv = -FLT_MAX; int bi = 0x7fffffff;
+    for (int j = 0; j < per; ++j) {
+      const int e = lane + 32 * j;
+      if (sel[j] > bv || (sel[j] == bv && e < bi)) { bv = sel[j]; bi = e; }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    // owner lane knocks the winner out and reports its unbiased score
+    float w = 0.f;
+    if ((bi & 31) == lane) {
+      const int j = bi >> 5;
+      for (int jj = 0; jj < per; ++jj) if (jj == j) { w = sc[jj]; sel[jj] = -FLT_MAX; }
+    }
+    w = __shfl_sync(0xffffffffu, w, bi & 31);
+    wsum += w;
+    if (lane == r) { myw = w; myid = bi; }
+  }
+  if (lane < K) {
+    float w = myw;
+    if (renorm) w = w / (wsum > 0.f ? wsum : 1.f);
+    out_ids[(size_t)gw * K + lane] = myid;
+    out_w[(size_t)gw * K + lane] = w * scale;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// MoE permute.  Pairs p = t*K + k with id in [lo, hi) are local; id - lo is the
+// local expert.  Everything else (other EP ranks, CPU tier, masked) is skipped.
+// ---------------------------------------------------------------------------
+__global__ void moe_count_kernel(const int* __restrict__ ids, int n, int lo, int hi, int* __restrict__ counts) {
+  extern __shared__ int hist[];
+  const int E = hi - lo;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) hist[e] = 0;
+  __syncthreads();
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const int id = ids[i];
+    if (id >= lo && id < hi) atomicAdd(&hist[id - lo], 1);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x)
+    if (hist[e]) atomicAdd(&counts[e], hist[e]);
+}
+
+// single block: seg[0..E] = exclusive scan of counts; cursor = seg; counts zeroed for reuse
+__global__ void moe_scan_kernel(int* __restrict__ counts, int E, int* __restrict__ seg, int* __restrict__ cursor) {
+  __shared__ int sh[1024];
+  const int tid = threadIdx.x;
+  const int per = (E + blockDim.x - 1) / blockDim.x;
+  int local = 0;
+  for (int j = 0; j < per; ++j) {
+    const int e = tid * per + j;
+    if (e < E) local += counts[e];
+  }
+  sh[tid] = local;
+  __syncthreads();
+  for (int off = 1; off < blockDim.x; off <<= 1) {
+    const int v = tid >= off ? sh[tid - off] : 0;
+    __syncthreads();
+    sh[tid] += v;
+    __syncthreads();
+  }
+  int run = sh[tid] - local;
+  for (int j = 0; j < per; ++j) {
+    const int e = tid * per + j;
+    if (e < E) {
+      seg[e] = run;
+      cursor[e] = run;
+      run += counts[e];
+      counts[e] = 0;
+    }
+  }
+  if (tid == blockDim.x - 1) seg[E] = sh[tid];
+}
+
+// one warp per pair: claim a row, record its source token / slot / weight, copy the row
+__global__ void moe_scatter_gather_kernel(const int* __restrict__ ids, const float* __restrict__ weights, int n,
+                                          int K, int lo, int hi, int* __restrict__ cursor,
+                                          int* __restrict__ perm_slot, float* __restrict__ perm_w,
+                                          const __nv_bfloat16* __restrict__ x, int H, int x_stride,
+                                          __nv_bfloat16* __restrict__ xp) {
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (gw >= n) return;
+  const int id = ids[gw];
+  if (id < lo || id >= hi) return;
+  int p = 0;
+  if (lane == 0) p = atomicAdd(&cursor[id - lo], 1);
+  p = __shfl_sync(0xffffffffu, p, 0);
+  if (lane == 0) {
+    perm_slot[p] = gw;
+    perm_w[p] = weights ? weights[gw] : 1.f;
+  }
+  if (xp) {
+    const int t = gw / K;
+    const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)t * x_stride);
+    uint4* dst = reinterpret_cast<uint4*>(xp + (size_t)p * H);
+    for (int i = lane; i < H / 8; i += 32) dst[i] = src[i];
+  }
+}
+
+// out[t] = sum_k slot[t*K+k] (local pairs only) + shared[t] + extra[t]
+__global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ slots, const int* __restrict__ ids, int T,
+                                   int K, int H, int lo, int hi, const __nv_bfloat16* __restrict__ shared,
+                                   const float* __restrict__ extra, __nv_bfloat16* __restrict__ out,
+                                   float* __restrict__ out_f32) {
+  const int t = blockIdx.x;
+  for (int i = threadIdx.x * 8; i < H; i += blockDim.x * 8) {
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int k = 0; k < K; ++k) {
+      const int id = ids[(size_t)t * K + k];
+      if (id < lo || id >= hi) continue;
+      const uint4 v = *reinterpret_cast<const uint4*>(slots + ((size_t)t * K + k) * H + i);
+      const uint32_t vs[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) { acc[2 * j] += bf16_lo(vs[j]); acc[2 * j + 1] += bf16_hi(vs[j]); }
+    }
+    if (shared) {
+      const uint4 v = *reinterpret_cast<const uint4*>(shared + (size_t)t * H + i);
+      const uint32_t vs[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) { acc[2 * j] += bf16_lo(vs[j]); acc[2 * j + 1] += bf16_hi(vs[j]); }
+    }
+    if (extra) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] += extra[(size_t)t * H + i + j];
+    }
+    if (out_f32) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) out_f32[(size_t)t * H + i + j] = acc[j];
+    } else {
+      uint4 o;
+      o.x = pack_bf16x2(acc[0], acc[1]); o.y = pack_bf16x2(acc[2], acc[3]);
+      o.z = pack_bf16x2(acc[4], acc[5]); o.w = pack_bf16x2(acc[6], acc[7]);
+      *reinterpret_cast<uint4*>(out + (size_t)t * H + i) = o;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// greedy argmax over rows (fp32 or bf16 logits); ties -> lowest index
+// ---------------------------------------------------------------------------
+template <typename T>
+__device__ __forceinline__ float ld_f(const T* p, size_t i);
+template <>
+__device__ __forceinline__ float ld_f<float>(const float* p, size_t i) { return p[i]; }
+template <>
+__device__ __forceinline__ float ld_f<__nv_bfloat16>(const __nv_bfloat16* p, size_t i) { return __bfloat162float(p[i]); }
+
+template <typename T>
+__global__ void argmax_kernel(const T* __restrict__ logits, int V, int stride, int* __restrict__ out,
+                              float* __restrict__ out_val) {
+  const T* row = logits + (size_t)blockIdx.x * stride;
+  float bv = -FLT_MAX;
+  int bi = 0x7fffffff;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    const float v = ld_f<T>(row, i);
+    if (v > bv) { bv = v; bi = i; }
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+  }
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) { sv[w] = bv; si[w] = bi; }
+  __syncthreads();
+  if (w == 0) {
+    const int nw = blockDim.x >> 5;
+    bv = l < nw ? sv[l] : -FLT_MAX;
+    bi = l < nw ? si[l] : 0x7fffffff;
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    if (l == 0) {
+      out[blockIdx.x] = bi;
+      if (out_val) out_val[blockIdx.x] = bv;
+    }
+  }
+}
+
+__global__ void embed_kernel(const int* __restrict__ ids, const __nv_bfloat16* __restrict__ table, int T, int H,
+                             int vocab, __nv_bfloat16* __restrict__ out) {
+  const int t = blockIdx.x;
+  int id = ids[t];
+  if (id < 0 || id >= vocab) id = 0;
+  const uint4* src = reinterpret_cast<const uint4*>(table + (size_t)id * H);
+  uint4* dst = reinterpret_cast<uint4*>(out + (size_t)t * H);
+  for (int i = threadIdx.x; i < H / 8; i += blockDim.x) dst[i] = src[i];
+}
+
+// SiLU(gate) * up for [T, 2I] rows (gate first), optional clamp; bf16 out [T, I]
+__global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ x, int T, int I, float limit, float alpha,
+                                float beta, __nv_bfloat16* __restrict__ out) {
+  const size_t n = (size_t)T * I;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    const size_t t = i / I, j = i - t * I;
+    float g = __bfloat162float(x[t * 2 * I + j]);
+    float u = __bfloat162float(x[t * 2 * I + I + j]);
+    if (limit > 0.f) { g = fminf(g, limit); u = fminf(fmaxf(u, -limit), limit); }
+    out[i] = __float2bfloat16((g / (1.f + __expf(-alpha * g))) * (u + beta));
+  }
+}
+
+}  // namespace xtu
+
+using namespace xtu;
+
+// returns `launched` (kernels enqueued) on success, a negative CUDA error otherwise
+static inline int rc_last(int launched = 1) {
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? launched : -(int)e;
+}
+
+extern "C" {
+
+int xtu_rmsnorm(const void* x, const void* residual, void* residual_out, const void* w, void* y, int T, int H,
+                float eps, int add_one, int x_stride, int y_stride, cudaStream_t s) {
+  if (T <= 0) return 0;
+  if (H % 8 != 0) return -2;
+  const size_t sm = (size_t)H * sizeof(float);
+  if (sm > 48 * 1024) {
+    cudaFuncSetAttribute(rmsnorm_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+  }
+  rmsnorm_kernel<256><<<T, 256, sm, s>>>((const __nv_bfloat16*)x, (const __nv_bfloat16*)residual,
+                                         (__nv_bfloat16*)residual_out, (const __nv_bfloat16*)w, (__nv_bfloat16*)y, H,
+                                         eps, add_one, x_stride, y_stride);
+  return rc_last();
+}
+
+int xtu_rope_kv(void* q, void* k, const void* v, const int* positions, const float* cos_sin, int T, int Hq, int Hk,
+                int D, int Dv, int rot, int neox, int q_stride, int k_stride, int v_stride, const void* q_norm_w,
+                const void* k_norm_w, float norm_eps, int norm_add_one, const int* slot_mapping, void* k_cache,
+                void* v_cache, int block_size, cudaStream_t s) {
+  if (T <= 0) return 0;
+  if (D % 32 != 0 || D > 512 || rot > D) return -2;
+  const int warps = T * (Hq + Hk);
+  const int threads = 256;
+  const int blocks = (warps * 32 + threads - 1) / threads;
+  rope_kv_kernel<<<blocks, threads, 0, s>>>((__nv_bfloat16*)q, (__nv_bfloat16*)k, (const __nv_bfloat16*)v, positions,
+                                            cos_sin, T, Hq, Hk, D, Dv, rot, neox, q_stride, k_stride, v_stride,
+                                            (const __nv_bfloat16*)q_norm_w, (const __nv_bfloat16*)k_norm_w, norm_eps,
+                                            norm_add_one, slot_mapping, (__nv_bfloat16*)k_cache,
+                                            (__nv_bfloat16*)v_cache, block_size);
+  return rc_last();
+}
+
+int xtu_kv_write(const void* k, const void* v, int T, int Hk, int D, int Dv, int k_stride, int v_stride,
+                 const int* slot_mapping, void* k_cache, void* v_cache, int block_size, cudaStream_t s) {
+  if (T <= 0) return 0;
+  const int warps = T * Hk;
+  kv_write_kernel<<<(warps * 32 + 255) / 256, 256, 0, s>>>((const __nv_bfloat16*)k, (const __nv_bfloat16*)v, T, Hk, D,
+                                                           Dv, k_stride, v_stride, slot_mapping,
+                                                           (__nv_bfloat16*)k_cache, (__nv_bfloat16*)v_cache,
+                                                           block_size);
+  return rc_last();
+}
+
+int xtu_router_topk(const float* logits, const float* bias, int T, int E, int K, int scoring, int n_group,
+                    int topk_group, int renorm, float scale, int* out_ids, float* out_w, int logits_stride,
+                    cudaStream_t s) {
+  if (T <= 0) return 0;
+  if (E > 1024 || K > 32 || n_group > 64) return -2;
+  router_topk_kernel<<<(T * 32 + 255) / 256, 256, 0, s>>>(logits, bias, T, E, K, scoring, n_group, topk_group, renorm,
+                                                          scale, out_ids, out_w, logits_stride);
+  return rc_last();
+}
+
+// counts must be zero on entry (the scan leaves it zeroed for the next call)
+int xtu_moe_permute(const int* ids, const float* weights, int T, int K, int lo, int hi, int* counts, int* seg,
+                    int* cursor, int* perm_slot, float* perm_w, const void* x, int H, int x_stride, void* xp,
+                    cudaStream_t s) {
+  const int n = T * K;
+  const int E = hi - lo;
+  if (E <= 0 || E > 65536) return -2;
+  if (n > 0) {
+    const int blocks = (n + 1023) / 1024 < 132 ? (n + 1023) / 1024 : 132;
+    moe_count_kernel<<<blocks, 1024, E * sizeof(int), s>>>(ids, n, lo, hi, counts);
+  }
+  moe_scan_kernel<<<1, 1024, 0, s>>>(counts, E, seg, cursor);
+  if (n > 0) {
+    if (xp && H % 8 != 0) return -3;
+    moe_scatter_gather_kernel<<<(n * 32 + 255) / 256, 256, 0, s>>>(ids, weights, n, K, lo, hi, cursor, perm_slot,
+                                                                   perm_w, (const __nv_bfloat16*)x, H, x_stride,
+                                                                   (__nv_bfloat16*)xp);
+  }
+  return rc_last(n > 0 ? 3 : 1);
+}
+
+int xtu_moe_combine(const void* slots, const int* ids, int T, int K, int H, int lo, int hi, const void* shared,
+                    const float* extra, void* out, float* out_f32, cudaStream_t s) {
+  if (T <= 0) return 0;
+  if (H % 8 != 0) return -2;
+  const int threads = H / 8 < 256 ? ((H / 8 + 31) / 32) * 32 : 256;
+  moe_combine_kernel<<<T, threads, 0, s>>>((const __nv_bfloat16*)slots, ids, T, K, H, lo, hi,
+                                           (const __nv_bfloat16*)shared, extra, (__nv_bfloat16*)out, out_f32);
+  return rc_last();
+}
+
+int xtu_argmax(const void* logits, int is_bf16, int T, int V, int stride, int* out, float* out_val, cudaStream_t s) {
+  if (T <= 0) return 0;
+  if (is_bf16)
+    argmax_kernel<__nv_bfloat16><<<T, 1024, 0, s>>>((const __nv_bfloat16*)logits, V, stride, out, out_val);
+  else
+    argmax_kernel<float><<<T, 1024, 0, s>>>((const float*)logits, V, stride, out, out_val);
+  return rc_last();
+}
+
+int xtu_embed(const int* ids, const void* table, int T, int H, int vocab, void* out, cudaStream_t s) {
+  if (T <= 0) return 0;
+  if (H % 8 != 0) return -2;
+  embed_kernel<<<T, 256, 0, s>>>(ids, (const __nv_bfloat16*)table, T, H, vocab, (__nv_bfloat16*)out);
+  return rc_last();
+}
+
+int xtu_silu_mul(const void* x, int T, int I, float limit, float alpha, float beta, void* out, cudaStream_t s) {
+  if (T <= 0) return 0;
+  const size_t n = (size_t)T * I;
+  int blocks = (int)((n + 255) / 256);
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  silu_mul_kernel<<<blocks, 256, 0, s>>>((const __nv_bfloat16*)x, T, I, limit, alpha, beta, (__nv_bfloat16*)out);
+  return rc_last();
+}
+
+}  // extern "C"

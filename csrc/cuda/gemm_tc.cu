@@ -467,7 +467,7 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmP
   if (grid < 1) grid = 1;
   kern<<<grid, C::NUM_WARPS * 32, C::SMEM_BYTES, stream>>>(ta, tb, p);
   cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? 0 : -(int)e;
+  return e == cudaSuccess ? 1 : -(int)e;
 }
 
 template <int BN, int BFMT>
@@ -493,7 +493,7 @@ int xtu_gemm_bf16(const void* A, const void* B, void* D, int M, int N, int K, in
   CUtensorMap ta, tb;
   int rc = make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, K, BM, BK, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  const int bn = N >= 256 ? 256 : 128;
+  const int bn = (N >= 256 && ((M + BM - 1) / BM) * ((N + 255) / 256) >= num_sms()) ? 256 : 128;
   rc = make_tmap_2d(&tb, B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, K, bn, BK, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   GemmParams p{};
@@ -516,7 +516,7 @@ int xtu_gemm_fp8w(const void* A, const void* B8, const float* b_scale, void* D, 
   CUtensorMap ta, tb;
   int rc = make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, K, BM, BK, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  const int bn = N >= 256 ? 256 : 128;
+  const int bn = (N >= 256 && ((M + BM - 1) / BM) * ((N + 255) / 256) >= num_sms()) ? 256 : 128;
   rc = make_tmap_2d(&tb, B8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, K, bn, BK, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc) return rc;
   GemmParams p{};
@@ -538,7 +538,7 @@ int xtu_build_mtiles(const int* seg, int E, void* tiles, int* count, int max_til
   while (threads < E && threads < 1024) threads <<= 1;
   build_mtiles_kernel<<<1, threads, 0, stream>>>(seg, E, reinterpret_cast<MTile*>(tiles), count, max_tiles);
   cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? 0 : -(int)e;
+  return e == cudaSuccess ? 1 : -(int)e;
 }
 
 int xtu_mtile_bytes() { return (int)sizeof(MTile); }

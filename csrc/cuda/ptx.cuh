@@ -94,18 +94,27 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Default limit for waits whose producer lives in the same CTA.  A correct kernel
 // never gets near it; it exists so that a bug shows up as a status word.
-constexpr uint64_t kIntraCtaWaitNs = 4000000000ull;  // 4 s
+constexpr uint64_t kIntraCtaWaitNs = 500000000ull;  // 0.5 s
 
 // Bounded parity wait.  Returns false (and records the failure) on timeout.
+// Once any CTA has recorded an error in `st`, every other bounded wait gives up at
+// its next check, so a fault costs one timeout in total rather than one per CTA.
+__device__ __forceinline__ bool status_failed(const XtuStatus* st) {
+  return st != nullptr && *reinterpret_cast<const volatile uint32_t*>(&st->code) != 0u;
+}
+
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, XtuStatus* st, uint32_t where,
                                           uint64_t limit_ns = kIntraCtaWaitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
-  while (true) {
+  for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (globaltimer_ns() - t0 > limit_ns) {
-      report_error(st, XTU_ERR_MBAR_TIMEOUT, where, parity);
-      return false;
+    if ((it & 63u) == 0u) {
+      if (status_failed(st)) return false;
+      if (globaltimer_ns() - t0 > limit_ns) {
+        report_error(st, XTU_ERR_MBAR_TIMEOUT, where, parity);
+        return false;
+      }
     }
   }
 }

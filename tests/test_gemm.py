@@ -139,3 +139,51 @@ def test_grouped_swiglu_and_scatter(fp8):
         o = h[s0:s1].float().cpu() @ w2d[e].float().cpu().t() * scale[s0:s1].cpu()[:, None]
         ref[dest[s0:s1].long().cpu()] = o
     _close(out.cpu(), ref, 1e-3)
+
+
+@pytest.mark.gpu
+def test_gemm_fp8_many_tiles_per_cta():
+    """Persistent CTAs looping over many tiles (the prefill shapes)."""
+    torch.manual_seed(5)
+    M, N, K = 4096, 4096, 2048
+    a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(N, K, device="cuda") / K ** 0.5
+    q, s = quant_fp8_block(w)
+    out = G.gemm_fp8w(a, q, s)
+    torch.cuda.synchronize()
+    G.N.check_status()
+    ref = a.float() @ dequant_fp8_block(q, s).to(torch.bfloat16).float().t()
+    _close(out, ref)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("fp8", [False, True])
+def test_grouped_gemm_prefill_scale(fp8):
+    """~16K routed rows over 128 experts with the fused SwiGLU epilogue (GLM-Air shapes, smaller K)."""
+    torch.manual_seed(6)
+    E, K, I = 128, 1024, 1408 // 11 * 2  # I = 256 keeps the reference cheap
+    g = torch.Generator().manual_seed(0)
+    counts = torch.multinomial(torch.ones(E), 16000, replacement=True, generator=g).bincount(minlength=E).tolist()
+    seg = _segments(counts).cuda()
+    M = int(seg[-1])
+    a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    w13 = torch.randn(E, 2 * I, K, device="cuda") / K ** 0.5
+    if fp8:
+        q, s = quant_fp8_block(w13)
+        h = G.grouped_gemm(a, G.interleave_gate_up(q.view(torch.uint8)).view(torch.float8_e4m3fn), seg,
+                           w_scale=G.interleave_gate_up_scale(s), epilogue=G.EPI_SWIGLU)
+        wd = dequant_fp8_block(q, s).to(torch.bfloat16).float()
+    else:
+        wb = w13.to(torch.bfloat16)
+        h = G.grouped_gemm(a, G.interleave_gate_up(wb), seg, epilogue=G.EPI_SWIGLU)
+        wd = wb.float()
+    torch.cuda.synchronize()
+    G.N.check_status()
+    segc = seg.tolist()
+    for e in range(0, E, 17):
+        s0, s1 = segc[e], segc[e + 1]
+        if s1 == s0:
+            continue
+        y = a[s0:s1].float() @ wd[e].t()
+        ref = G.silu_and_mul_clamped(y[:, :I], y[:, I:])
+        _close(h[s0:s1], ref)

@@ -1,0 +1,255 @@
+"""sm_100a hot-op kernels vs PyTorch fp32 restatements of the same ops."""
+import math
+
+import pytest
+import torch
+
+from vllm_xtu_moe_b200.ops import basic as B
+from vllm_xtu_moe_b200.ops import moe as M
+from vllm_xtu_moe_b200.ops import _native as N
+from vllm_xtu_moe_b200.ops.attention import AttnMetadata, paged_attention, paged_attention_ref, num_split_workspace
+from vllm_xtu_moe_b200.ops.router import router_topk, router_topk_ref, zipf_bias
+from vllm_xtu_moe_b200.ops.quant import quant_fp8_block
+
+
+def rel_err(a, b):
+    a, b = a.float(), b.float()
+    return ((a - b).abs().max() / (b.abs().max() + 1e-6)).item()
+
+
+# ---------------------------------------------------------------- CPU-only checks
+def test_router_ref_group_limited():
+    torch.manual_seed(0)
+    logits = torch.randn(5, 64)
+    bias = torch.randn(64) * 0.1
+    ids, w = router_topk_ref(logits, 8, "sigmoid", bias, n_group=8, topk_group=4, renorm=True, scale=2.5)
+    assert ids.shape == (5, 8)
+    assert torch.allclose(w.sum(-1), torch.full((5,), 2.5), atol=1e-5)
+    # every chosen expert lies in one of at most 4 groups
+    for t in range(5):
+        assert len(set((ids[t] // 8).tolist())) <= 4
+
+
+def test_zipf_bias_is_seeded_and_skewed():
+    a, b = zipf_bias(256, 1.1, seed=3), zipf_bias(256, 1.1, seed=3)
+    assert torch.equal(a, b)
+    assert a.max() - a.min() > 3.0
+
+
+def test_rope_cache_shapes_yarn():
+    cs = B.rope_cache(64, 128, 10000.0, scaling={"type": "yarn", "factor": 40, "original_max_position_embeddings": 4096,
+                                                  "beta_fast": 32, "beta_slow": 1, "mscale": 1.0,
+                                                  "mscale_all_dim": 1.0})
+    assert cs.shape == (128, 64) and torch.isfinite(cs).all()
+
+
+# ---------------------------------------------------------------- GPU kernels
+@pytest.mark.gpu
+@pytest.mark.parametrize("H", [256, 4096, 7168])
+def test_rmsnorm(H):
+    torch.manual_seed(0)
+    x = torch.randn(37, H, device="cuda", dtype=torch.bfloat16)
+    r = torch.randn(37, H, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(H, device="cuda", dtype=torch.bfloat16)
+    y, ro = B.rmsnorm(x, w, 1e-6, residual=r)
+    yr, rr = B.rmsnorm_ref(x.cpu(), w.cpu(), 1e-6, residual=r.cpu())
+    assert torch.equal(ro.cpu(), rr)
+    assert rel_err(y.cpu(), yr) < 1e-2
+    y2 = B.rmsnorm(x, w, 1e-6, add_one=True)
+    assert rel_err(y2.cpu(), B.rmsnorm_ref(x.cpu(), w.cpu(), 1e-6, add_one=True)[0]) < 1e-2
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("D,rot,neox,qknorm", [(128, 64, True, False), (64, 64, True, False), (256, 64, True, True),
+                                               (64, 64, False, False)])
+def test_rope_and_cache(D, rot, neox, qknorm):
+    torch.manual_seed(1)
+    T, Hq, Hk, bs = 19, 8, 2, 64
+    qkv = torch.randn(T, (Hq + 2 * Hk) * D, device="cuda", dtype=torch.bfloat16)
+    q = qkv[:, :Hq * D].view(T, Hq, D)
+    k = qkv[:, Hq * D:(Hq + Hk) * D].view(T, Hk, D)
+    v = qkv[:, (Hq + Hk) * D:].view(T, Hk, D)
+    pos = torch.randint(0, 1000, (T,), device="cuda", dtype=torch.int32)
+    cs = B.rope_cache(rot, 1024, 10000.0, "cuda")
+    kc = torch.zeros(4, Hk, bs, D, device="cuda", dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    slots = torch.randperm(4 * bs, device="cuda")[:T].int()
+    qn = torch.randn(D, device="cuda", dtype=torch.bfloat16) if qknorm else None
+    kn = torch.randn(D, device="cuda", dtype=torch.bfloat16) if qknorm else None
+    q_ref, k_ref, v_ref = q.clone().cpu(), k.clone().cpu(), v.clone().cpu()
+    kc_ref, vc_ref = kc.clone().cpu(), vc.clone().cpu()
+    B.rope_and_cache(q, k, v, pos, cs, rot, neox, slot_mapping=slots, k_cache=kc, v_cache=vc, q_norm_w=qn,
+                     k_norm_w=kn)
+    B.rope_and_cache(q_ref, k_ref, v_ref, pos.cpu(), cs.cpu(), rot, neox, slot_mapping=slots.cpu(), k_cache=kc_ref,
+                     v_cache=vc_ref, q_norm_w=qn.cpu() if qn is not None else None,
+                     k_norm_w=kn.cpu() if kn is not None else None)
+    assert rel_err(q.cpu(), q_ref) < 2e-2
+    assert rel_err(k.cpu(), k_ref) < 2e-2
+    assert rel_err(kc.cpu(), kc_ref) < 2e-2
+    assert torch.equal(vc.cpu(), vc_ref)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("E,K,scoring,ng,tg", [(8, 2, "softmax", 1, 1), (128, 8, "sigmoid", 1, 1),
+                                               (256, 8, "sigmoid", 8, 4), (512, 10, "softmax", 1, 1)])
+def test_router(E, K, scoring, ng, tg):
+    torch.manual_seed(2)
+    logits = torch.randn(300, E, device="cuda") + zipf_bias(E).cuda()
+    bias = torch.randn(E, device="cuda") * 0.05 if scoring == "sigmoid" else None
+    ids, w = router_topk(logits, K, scoring, bias, ng, tg, True, 2.5)
+    ids_r, w_r = router_topk_ref(logits.cpu(), K, scoring, bias.cpu() if bias is not None else None, ng, tg, True, 2.5)
+    # same expert sets and weights (order within the set may differ)
+    s1, o1 = ids.cpu().sort(-1)
+    s2, o2 = ids_r.sort(-1)
+    assert torch.equal(s1, s2)
+    assert torch.allclose(w.cpu().gather(1, o1), w_r.gather(1, o2), atol=1e-4)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("fmt", ["bf16", "fp8"])
+@pytest.mark.parametrize("T,E,K,H,I", [(1, 8, 2, 256, 512), (200, 16, 4, 512, 256), (33, 64, 8, 1024, 384)])
+def test_fused_moe(fmt, T, E, K, H, I):
+    torch.manual_seed(3)
+    x = torch.randn(T, H, device="cuda", dtype=torch.bfloat16)
+    w13 = torch.randn(E, 2 * I, H, device="cuda") / H ** 0.5
+    w2 = torch.randn(E, H, I, device="cuda") / I ** 0.5
+    if fmt == "fp8":
+        q13, s13 = quant_fp8_block(w13)
+        q2, s2 = quant_fp8_block(w2)
+        ex = M.prepare_experts("fp8", q13, q2, s13, s2)
+    else:
+        ex = M.prepare_experts("bf16", w13.to(torch.bfloat16), w2.to(torch.bfloat16))
+    logits = torch.randn(T, E, device="cuda")
+    ids, w = router_topk(logits, K, "softmax")
+    shared = torch.randn(T, H, device="cuda", dtype=torch.bfloat16)
+    y = M.fused_moe(x, ids, w, ex, shared=shared, act_limit=7.0)
+    torch.cuda.synchronize()
+    N.check_status()
+    ref = M.moe_ref(x, ids, w, ex, act_limit=7.0) + shared.float()
+    assert rel_err(y, ref) < 2e-2
+    # tier split: experts [E/2, E) elsewhere -> only [0, E/2) pairs computed here
+    half = M.prepare_experts(ex.fmt, *(_slice_raw(ex, fmt, 0, E // 2)))
+    y2 = M.fused_moe(x, ids, w, half, lo=0)
+    ref2 = M.moe_ref(x, ids, w, half, lo=0, hi=E // 2)
+    assert rel_err(y2, ref2) < 2e-2
+
+
+def _slice_raw(ex, fmt, a, b):
+    # rebuild checkpoint layout (gate, up) from the interleaved kernel layout
+    if ex.interleaved:
+        I = ex.inter
+        w = ex.w13[a:b].view(torch.uint8) if fmt == "fp8" else ex.w13[a:b]
+        blk = w.reshape(b - a, I // 128, 2, 128, -1)
+        w13 = torch.cat([blk[:, :, 0].reshape(b - a, I, -1), blk[:, :, 1].reshape(b - a, I, -1)], dim=1)
+        if fmt == "fp8":
+            w13 = w13.view(torch.float8_e4m3fn)
+            s = ex.s13[a:b]
+            nb = s.shape[1]
+            sb = s.reshape(b - a, nb // 2, 2, -1)
+            s13 = torch.cat([sb[:, :, 0], sb[:, :, 1]], dim=1)
+            return w13.contiguous(), ex.w2[a:b].contiguous(), s13.contiguous(), ex.s2[a:b].contiguous()
+        return (w13.contiguous(), ex.w2[a:b].contiguous())
+    if fmt == "fp8":
+        return ex.w13[a:b], ex.w2[a:b], ex.s13[a:b], ex.s2[a:b]
+    return ex.w13[a:b], ex.w2[a:b]
+
+
+@pytest.mark.gpu
+def test_argmax_embed():
+    torch.manual_seed(4)
+    lg = torch.randn(7, 151552, device="cuda")
+    assert torch.equal(B.argmax(lg).cpu(), lg.argmax(-1).int().cpu())
+    tab = torch.randn(1000, 256, device="cuda", dtype=torch.bfloat16)
+    ids = torch.randint(0, 1000, (9,), device="cuda", dtype=torch.int32)
+    assert torch.equal(B.embed(ids, tab), tab[ids.long()])
+
+
+def _make_paged(seqs, Hkv, D, Dv, bs=64, device="cuda"):
+    """seqs: list of (q_len, kv_len). Returns caches, metadata, q."""
+    nblk = sum((kl + bs - 1) // bs for _, kl in seqs) + 2
+    kc = torch.randn(nblk, Hkv, bs, D, device=device, dtype=torch.bfloat16)
+    vc = torch.randn(nblk, Hkv, bs, Dv, device=device, dtype=torch.bfloat16)
+    perm = torch.randperm(nblk).tolist()
+    tables, q_start, kv_len = [], [0], []
+    for ql, kl in seqs:
+        nb = (kl + bs - 1) // bs
+        tables.append([perm.pop() for _ in range(nb)])
+        q_start.append(q_start[-1] + ql)
+        kv_len.append(kl)
+    mb = max(len(t) for t in tables)
+    bt = torch.zeros(len(seqs), mb, dtype=torch.int32)
+    for i, t in enumerate(tables):
+        bt[i, :len(t)] = torch.tensor(t)
+    T = q_start[-1]
+    meta = AttnMetadata(num_seqs=len(seqs), q_start=torch.tensor(q_start, dtype=torch.int32, device=device),
+                        kv_len=torch.tensor(kv_len, dtype=torch.int32, device=device), block_table=bt.to(device),
+                        slot_mapping=torch.zeros(T, dtype=torch.int32, device=device),
+                        positions=torch.zeros(T, dtype=torch.int32, device=device),
+                        max_q_len=max(q for q, _ in seqs), max_kv_len=max(kv_len), is_decode=False,
+                        q_start_host=q_start, kv_len_host=kv_len)
+    return kc, vc, meta, T
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("Hq,Hkv,D", [(96, 8, 128), (4, 2, 64), (16, 2, 256), (8, 8, 128), (12, 1, 128)])
+@pytest.mark.parametrize("mode", ["prefill", "decode", "decode_split", "spec"])
+def test_paged_attention(Hq, Hkv, D, mode):
+    torch.manual_seed(5)
+    if mode == "prefill":
+        seqs = [(300, 300), (77, 590), (1, 1), (130, 130)]
+    elif mode == "spec":
+        seqs = [(5, 700), (5, 129), (5, 64)]
+    else:
+        seqs = [(1, 1000), (1, 63), (1, 4097)]
+    kc, vc, meta, T = _make_paged(seqs, Hkv, D, D)
+    if mode == "decode_split":
+        meta.num_splits = 8
+    q = torch.randn(T, Hq, D, device="cuda", dtype=torch.bfloat16)
+    scale = 1.0 / math.sqrt(D)
+    o = paged_attention(q, kc, vc, meta, scale)
+    torch.cuda.synchronize()
+    N.check_status()
+    ref = paged_attention_ref(q.float(), kc.float(), vc.float(), meta, scale)
+    err = (o.float() - ref.float()).abs().max().item()
+    assert err < 3e-2, err
+
+
+@pytest.mark.gpu
+def test_paged_attention_long_prefill():
+    """4K-token prompts, GQA group 12 (GLM-Air heads), two chunks of one sequence."""
+    torch.manual_seed(7)
+    seqs = [(4000, 4000), (1500, 6000)]
+    kc, vc, meta, T = _make_paged(seqs, 8, 128, 128)
+    q = torch.randn(T, 96, 128, device="cuda", dtype=torch.bfloat16)
+    o = paged_attention(q, kc, vc, meta, 1 / math.sqrt(128))
+    torch.cuda.synchronize()
+    N.check_status()
+    ref = paged_attention_ref(q, kc, vc, meta, 1 / math.sqrt(128))   # torch on the GPU, fp32 math
+    assert (o.float() - ref.float()).abs().max().item() < 3e-2
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("mode", ["prefill", "decode"])
+def test_paged_attention_running_max_rescale(mode):
+    """Scores that grow along the keys for some heads and shrink for others, so that
+    within one warp some rows must rescale O and others must not."""
+    torch.manual_seed(8)
+    Hq, Hkv, D = 96, 8, 128
+    seqs = [(700, 700), (300, 1000)] if mode == "prefill" else [(1, 3000), (4, 900)]
+    kc, vc, meta, T = _make_paged(seqs, Hkv, D, D)
+    # k[t] = 0.02 * pos(t) * ones + noise  ->  q.k grows (or shrinks) linearly with the key position
+    bs = kc.shape[2]
+    pos = torch.arange(bs, device="cuda").float()
+    for blk_row, (ql, kl) in zip(meta.block_table.tolist(), seqs):
+        for j, b in enumerate(blk_row[:(kl + bs - 1) // bs]):
+            ramp = (j * bs + pos)[None, :, None] * 0.02
+            kc[b] = (ramp + 0.1 * torch.randn(Hkv, bs, D, device="cuda")).to(torch.bfloat16)
+    sign = torch.where(torch.arange(Hq, device="cuda") % 3 == 0, -1.0, 1.0)
+    q = (sign[None, :, None] * torch.ones(T, Hq, D, device="cuda") + 0.1 * torch.randn(T, Hq, D, device="cuda"))
+    q = q.to(torch.bfloat16)
+    scale = 1 / math.sqrt(D)
+    o = paged_attention(q, kc, vc, meta, scale)
+    torch.cuda.synchronize()
+    N.check_status()
+    ref = paged_attention_ref(q, kc, vc, meta, scale)
+    assert (o.float() - ref.float()).abs().max().item() < 3e-2

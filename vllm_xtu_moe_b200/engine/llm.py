@@ -1,0 +1,141 @@
+"""Public offline-serving API.
+
+    llm = LLM("glm-4.5-air", device="cuda:0")            # preset name, ModelConfig, or HF dir
+    outs = llm.generate([[1, 2, 3], [4, 5]], SamplingParams(max_tokens=32))
+
+``generate`` runs the continuous-batching loop (scheduler -> runner) until every
+request finishes and returns the generated token ids with timing (TTFT, decode
+window) per request.  Inputs are host token lists; each step copies its
+metadata host->device and reads the sampled ids device->host.
+"""
+from __future__ import annotations
+
+import os
+import sys
+import time
+from dataclasses import dataclass
+
+import torch
+
+from ..config import EngineConfig, get_engine_config
+from ..models.config import ModelConfig, get_preset
+from ..models.model import MoETransformer, build_model
+from .block_manager import BlockManager
+from .runner import ModelRunner, RunnerConfig
+from .scheduler import Scheduler
+from .sequence import Request, SamplingParams, Status
+
+
+_DEBUG_STEPS = os.environ.get("XTU_DEBUG_STEPS", "0") == "1"
+
+
+@dataclass
+class RequestOutput:
+    rid: int
+    prompt_len: int
+    token_ids: list[int]
+    ttft_s: float
+    e2e_s: float
+    accepted: int = 0
+    proposed: int = 0
+
+
+class LLM:
+    def __init__(self, model: str | ModelConfig | MoETransformer, *, device: str = "cuda", seed: int = 0,
+                 runner_config: RunnerConfig | None = None, engine_config: EngineConfig | None = None,
+                 tiering=None, num_layers: int | None = None):
+        self.econf = engine_config or get_engine_config()
+        if isinstance(model, MoETransformer):
+            self.model = model
+        else:
+            cfg = get_preset(model) if isinstance(model, str) else model
+            sink = tiering.expert_sink if tiering is not None else None
+            self.model = build_model(cfg, device=device, seed=seed, expert_sink=sink, num_layers=num_layers)
+        if tiering is not None:
+            tiering.attach(self.model)
+        self.tiering = tiering
+        rc = runner_config or RunnerConfig()
+        self.runner = ModelRunner(self.model, rc)
+        self.blocks = BlockManager(rc.num_blocks, rc.block_size, rc.max_seqs)
+        self.scheduler = Scheduler(self.blocks, rc.max_batched_tokens, rc.max_seqs, rc.num_spec)
+        self.spec = None
+        if rc.num_spec > 0 and self.model.mtp:
+            from .spec_decode import SpecDecoder
+            self.spec = SpecDecoder(self.runner, rc.num_spec)
+        self.stats = dict(prefill_tokens=0, decode_tokens=0, prefill_time=0.0, decode_time=0.0, steps=0)
+
+    # ------------------------------------------------------------------
+    def add_request(self, prompt: list[int], params: SamplingParams) -> Request:
+        r = Request(list(prompt), params)
+        r.t_submit = time.perf_counter()
+        self.scheduler.add(r)
+        return r
+
+    def step(self, plan=None) -> list[Request]:
+        """Run one engine step (scheduling it unless a plan is given); returns finished requests."""
+        if plan is None:
+            plan = self.scheduler.schedule()
+        if plan is None:
+            return []
+        t0 = time.perf_counter()
+        if plan.is_decode and self.spec is not None:
+            done = self.spec.decode_step(plan, self.scheduler)
+            self.stats["decode_time"] += time.perf_counter() - t0
+            self.stats["steps"] += 1
+            return done
+        tok, extra = self.runner.execute(plan)
+        toks = tok.tolist() if tok is not None else []
+        now = time.perf_counter()
+        if _DEBUG_STEPS:
+            print(f"[xtu-step] {'decode' if plan.is_decode else 'prefill'} seqs={len(plan.chunks)} "
+                  f"tokens={plan.num_tokens} {1e3 * (now - t0):.1f} ms", file=sys.stderr, flush=True)
+        done = []
+        if plan.is_decode:
+            for ch, t in zip(plan.chunks, toks):
+                r = ch.req
+                r.num_computed = r.total_len
+                r.output.append(int(t))
+                self.stats["decode_tokens"] += 1
+                if r.finished():
+                    r.t_done = now
+                    self.scheduler.finish(r)
+                    done.append(r)
+            self.stats["decode_time"] += now - t0
+        else:
+            it = iter(toks)
+            for ch in plan.chunks:
+                r = ch.req
+                r.num_computed += ch.length
+                self.stats["prefill_tokens"] += ch.length
+                if r.num_computed == len(r.prompt):
+                    r.output.append(int(next(it)))
+                    r.t_first = now
+                    r.status = Status.DECODE
+                    if self.spec is not None:
+                        self.spec.after_prefill(r, extra)
+                    if r.finished():
+                        r.t_done = now
+                        self.scheduler.finish(r)
+                        done.append(r)
+            if self.spec is not None:
+                self.spec.prefill_mtp(plan, extra)
+            self.stats["prefill_time"] += now - t0
+        self.stats["steps"] += 1
+        return done
+
+    def generate(self, prompts: list[list[int]], params: SamplingParams | list[SamplingParams] | None = None):
+        params = params or SamplingParams()
+        ps = params if isinstance(params, list) else [params] * len(prompts)
+        reqs = [self.add_request(p, sp) for p, sp in zip(prompts, ps)]
+        while self.scheduler.has_work():
+            self.step()
+        out = []
+        for r in reqs:
+            out.append(RequestOutput(r.rid, len(r.prompt), list(r.output), r.t_first - r.t_submit,
+                                     r.t_done - r.t_submit, r.accepted, r.proposed))
+        return out
+
+    def shutdown(self):
+        self.runner.release_graphs()
+        if self.tiering is not None:
+            self.tiering.shutdown()

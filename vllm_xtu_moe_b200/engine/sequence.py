@@ -1,0 +1,66 @@
+"""Requests and sampling parameters."""
+from __future__ import annotations
+
+import enum
+import itertools
+from dataclasses import dataclass, field
+
+
+@dataclass
+class SamplingParams:
+    max_tokens: int = 16
+    temperature: float = 0.0      # 0 = greedy
+    top_p: float = 1.0
+    ignore_eos: bool = True
+    eos_token_id: int | None = None
+    seed: int | None = None
+
+
+class Status(enum.Enum):
+    WAITING = 0
+    PREFILL = 1
+    DECODE = 2
+    FINISHED = 3
+
+
+_ids = itertools.count()
+
+
+@dataclass
+class Request:
+    prompt: list[int]
+    params: SamplingParams
+    rid: int = field(default_factory=lambda: next(_ids))
+    output: list[int] = field(default_factory=list)
+    status: Status = Status.WAITING
+    num_computed: int = 0          # tokens whose KV is in the cache
+    blocks: list[int] = field(default_factory=list)
+    slot: int = -1                 # recurrent-state slot
+    # timing (seconds, host clock) for TTFT / TPOT accounting
+    t_submit: float = 0.0
+    t_first: float = 0.0
+    t_done: float = 0.0
+    # speculative decoding
+    draft: list[int] = field(default_factory=list)
+    accepted: int = 0
+    proposed: int = 0
+
+    @property
+    def all_tokens(self) -> list[int]:
+        return self.prompt + self.output
+
+    @property
+    def total_len(self) -> int:
+        return len(self.prompt) + len(self.output)
+
+    @property
+    def prefill_remaining(self) -> int:
+        return len(self.prompt) - self.num_computed
+
+    def finished(self) -> bool:
+        p = self.params
+        if len(self.output) >= p.max_tokens:
+            return True
+        if not p.ignore_eos and p.eos_token_id is not None and self.output and self.output[-1] == p.eos_token_id:
+            return True
+        return False

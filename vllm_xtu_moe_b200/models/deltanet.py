@@ -1,0 +1,150 @@
+"""Gated DeltaNet linear attention (Qwen3-Next "linear_attention" layers).
+
+Per value head h, with L2-normalised q, k (q additionally scaled by 1/sqrt(dk)),
+decay g_t = -exp(A_log) * softplus(a_t + dt_bias) and write strength
+beta_t = sigmoid(b_t), the state S [dk, dv] evolves as
+
+    S <- exp(g_t) * S
+    S <- S + k_t (beta_t (v_t - S^T k_t))^T
+    o_t = S^T q_t
+
+followed by a gated RMSNorm (rmsnorm(o) * w * silu(z)) and the output
+projection.  A causal depthwise conv (kernel 4, SiLU) runs over the
+concatenated q/k/v channels first.  Recurrent state and conv state are kept
+per request slot between steps (``DeltaNetState``).
+
+The per-token recurrence in ``_delta_rule_ref`` is the numerics oracle; on a
+GPU the chunked/recurrent kernels of ``csrc/cuda/deltanet.cu`` run.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn.functional as F
+
+from ..ops import _native as N
+from ..ops.attention import AttnMetadata
+from .config import ModelConfig
+from .layers import Linear
+
+
+class DeltaNetState:
+    """Recurrent state [slots, nv, dk, dv] fp32 and conv state [slots, channels, kernel-1]."""
+
+    def __init__(self, cfg: ModelConfig, max_slots: int, device):
+        nv, dk, dv = cfg.linear_num_value_heads, cfg.linear_key_head_dim, cfg.linear_value_head_dim
+        ch = 2 * cfg.linear_num_key_heads * dk + nv * dv
+        self.ssm = torch.zeros(max_slots, nv, dk, dv, dtype=torch.float32, device=device)
+        self.conv = torch.zeros(max_slots, ch, cfg.linear_conv_kernel - 1, dtype=torch.bfloat16, device=device)
+
+    def nbytes(self) -> int:
+        return self.ssm.numel() * 4 + self.conv.numel() * 2
+
+
+def _delta_rule_ref(q, k, v, g, beta, state):
+    """q,k [T, H, dk], v [T, H, dv], g,beta [T, H]; state [H, dk, dv] (updated in place)."""
+    T = q.shape[0]
+    out = torch.empty(T, v.shape[1], v.shape[2], dtype=torch.float32, device=q.device)
+    S = state
+    for t in range(T):
+        S.mul_(torch.exp(g[t])[:, None, None])
+        kv_mem = torch.einsum("hkv,hk->hv", S, k[t])
+        delta = (v[t] - kv_mem) * beta[t][:, None]
+        S.add_(torch.einsum("hk,hv->hkv", k[t], delta))
+        out[t] = torch.einsum("hkv,hk->hv", S, q[t])
+    return out
+
+
+class GatedDeltaNet:
+    def __init__(self, cfg: ModelConfig, in_qkvz: Linear, in_ba: Linear, conv_w: torch.Tensor, A_log: torch.Tensor,
+                 dt_bias: torch.Tensor, norm_w: torch.Tensor, out: Linear):
+        self.cfg = cfg
+        self.in_qkvz, self.in_ba, self.conv_w = in_qkvz, in_ba, conv_w   # conv_w [channels, kernel]
+        self.A_log, self.dt_bias, self.norm_w, self.out = A_log, dt_bias, norm_w, out
+        self.nk, self.nv = cfg.linear_num_key_heads, cfg.linear_num_value_heads
+        self.dk, self.dv = cfg.linear_key_head_dim, cfg.linear_value_head_dim
+        self.state: DeltaNetState | None = None
+
+    def _split(self, qkvz, ba):
+        T = qkvz.shape[0]
+        nk, nv, dk, dv = self.nk, self.nv, self.dk, self.dv
+        r = nv // nk
+        x = qkvz.view(T, nk, 2 * dk + 2 * r * dv)
+        q = x[:, :, :dk].reshape(T, nk * dk)
+        k = x[:, :, dk:2 * dk].reshape(T, nk * dk)
+        v = x[:, :, 2 * dk:2 * dk + r * dv].reshape(T, nv * dv)
+        z = x[:, :, 2 * dk + r * dv:].reshape(T, nv, dv)
+        bav = ba.view(T, nk, 2 * r)
+        b = bav[:, :, :r].reshape(T, nv)
+        a = bav[:, :, r:].reshape(T, nv)
+        return q, k, v, z, b, a
+
+    def __call__(self, x: torch.Tensor, meta: AttnMetadata, kv, rope) -> torch.Tensor:
+        state: DeltaNetState = kv
+        T = x.shape[0]
+        qkvz = self.in_qkvz(x)
+        ba = self.in_ba(x)
+        q, k, v, z, b, a = self._split(qkvz, ba)
+        mixed = torch.cat([q, k, v], dim=-1)            # [T, channels]
+        beta = torch.sigmoid(b.float())
+        g = -torch.exp(self.A_log.float()) * F.softplus(a.float() + self.dt_bias.float())
+        o = self._core(mixed, g, beta, meta, state)     # [T, nv, dv] fp32
+        o = self._gated_norm(o, z)
+        return self.out(o.reshape(T, self.nv * self.dv))
+
+    def _gated_norm(self, o, z):
+        of = o.float()
+        y = of * torch.rsqrt(of.pow(2).mean(-1, keepdim=True) + self.cfg.norm_eps)
+        y = y * self.norm_w.float() * F.silu(z.float())
+        return y.to(torch.bfloat16)
+
+    def _core(self, mixed, g, beta, meta, state):
+        if mixed.is_cuda and N.has_symbol("xtu_deltanet_fwd"):
+            from ..ops.deltanet import deltanet_fwd
+            return deltanet_fwd(mixed, self.conv_w, g, beta, meta, state, self.nk, self.nv, self.dk, self.dv)
+        if mixed.is_cuda and N.native_required():
+            raise N.NativeLibraryMissing("xtu_deltanet_fwd missing from the CUDA library")
+        return deltanet_ref(mixed, self.conv_w, g, beta, meta, state, self.nk, self.nv, self.dk, self.dv)
+
+    def tensors(self):
+        return (self.in_qkvz.tensors() + self.in_ba.tensors() + self.out.tensors() +
+                [self.conv_w, self.A_log, self.dt_bias, self.norm_w])
+
+
+def deltanet_ref(mixed, conv_w, g, beta, meta, state: DeltaNetState, nk, nv, dk, dv):
+    """Causal conv (with carried state) + gated delta rule per sequence (fp32)."""
+    T, ch = mixed.shape
+    kw = conv_w.shape[1]
+    qs = meta.q_start_host if meta.q_start_host is not None else meta.q_start.tolist()
+    slots = meta.seq_slots.tolist()
+    fresh = meta.seq_fresh.tolist() if meta.seq_fresh is not None else [0] * meta.num_seqs
+    out = torch.empty(T, nv, dv, dtype=torch.float32, device=mixed.device)
+    r = nv // nk
+    for bi in range(meta.num_seqs):
+        s0, s1 = qs[bi], qs[bi + 1]
+        if s1 == s0:
+            continue
+        slot = slots[bi]
+        if fresh[bi]:
+            state.conv[slot].zero_()
+            state.ssm[slot].zero_()
+        xs = mixed[s0:s1].float()                                  # [L, ch]
+        hist = state.conv[slot].float().t()                        # [kw-1, ch]
+        full = torch.cat([hist, xs], dim=0)                        # [kw-1+L, ch]
+        L = s1 - s0
+        w = conv_w.float()                                          # [ch, kw]
+        conv = torch.zeros(L, ch, device=mixed.device)
+        for j in range(kw):
+            conv += full[j:j + L] * w[:, j]
+        conv = F.silu(conv)
+        state.conv[slot].copy_(full[-(kw - 1):].t().to(state.conv.dtype))
+        q = conv[:, : nk * dk].view(L, nk, dk)
+        k = conv[:, nk * dk: 2 * nk * dk].view(L, nk, dk)
+        v = conv[:, 2 * nk * dk:].view(L, nv, dv)
+        q = F.normalize(q, dim=-1) / math.sqrt(dk)
+        k = F.normalize(k, dim=-1)
+        q = q.repeat_interleave(r, dim=1)
+        k = k.repeat_interleave(r, dim=1)
+        out[s0:s1] = _delta_rule_ref(q, k, v, g[s0:s1], beta[s0:s1], state.ssm[slot])
+    return out

@@ -36,6 +36,18 @@ _SIGS: dict[str, list] = {
     "xtu_build_mtiles": [P, c_int, P, P, c_int, P],
     "xtu_grouped_gemm": [P, P, P, c_int, P, c_int, c_int, c_int, c_int, c_int, P, P, c_int, c_int, P, P,
                          c_float, c_float, c_float, P, P],
+    "xtu_rmsnorm": [P, P, P, P, P, c_int, c_int, c_float, c_int, c_int, c_int, P],
+    "xtu_rope_kv": [P, P, P, P, P, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, P, P,
+                    c_float, c_int, P, P, P, c_int, P],
+    "xtu_kv_write": [P, P, c_int, c_int, c_int, c_int, c_int, c_int, P, P, P, c_int, P],
+    "xtu_router_topk": [P, P, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_float, P, P, c_int, P],
+    "xtu_moe_permute": [P, P, c_int, c_int, c_int, c_int, P, P, P, P, P, P, c_int, c_int, P, P],
+    "xtu_moe_combine": [P, P, c_int, c_int, c_int, c_int, c_int, P, P, P, P, P],
+    "xtu_argmax": [P, c_int, c_int, c_int, c_int, P, P, P],
+    "xtu_embed": [P, P, c_int, c_int, c_int, P, P],
+    "xtu_silu_mul": [P, c_int, c_int, c_float, c_float, c_float, P, P],
+    "xtu_paged_attention": [P, c_int, P, P, c_int, P, c_int, P, P, P, c_int, c_int, c_int, c_int, c_int, c_int,
+                            c_int, c_int, c_int, c_int, c_int, c_float, c_int, P, P, P],
 }
 
 
@@ -71,11 +83,48 @@ def has_symbol(name: str) -> bool:
         return False
 
 
+# kernels of this library enqueued by this process (entry points return their count)
+LAUNCHES = {"total": 0}
+
+
+_SYNC_CALLS = os.environ.get("XTU_SYNC_CALLS", "0") == "1"
+
+
 def call(name: str, *args) -> int:
+    if _SYNC_CALLS:
+        return _call_synced(name, *args)
     rc = getattr(lib(), name)(*args)
     if rc < 0:
         raise RuntimeError(f"{name} failed with code {rc}")
+    LAUNCHES["total"] += rc
     return rc
+
+
+def _call_synced(name: str, *args) -> int:
+    """Debug mode (XTU_SYNC_CALLS=1): synchronise after every entry point, log its
+    duration and raise at the first kernel that recorded an error."""
+    import sys
+    import time
+    torch.cuda.synchronize()
+    t = time.perf_counter()
+    print(f"[xtu-call] {name} ...", file=sys.stderr, flush=True)
+    rc = getattr(lib(), name)(*args)
+    if rc < 0:
+        raise RuntimeError(f"{name} failed with code {rc}")
+    torch.cuda.synchronize()
+    print(f"[xtu-call] {name} {1e3 * (time.perf_counter() - t):.2f} ms", file=sys.stderr, flush=True)
+    check_status()
+    LAUNCHES["total"] += rc
+    return rc
+
+
+def launches() -> int:
+    return LAUNCHES["total"]
+
+
+def add_launches(n: int) -> None:
+    """Account kernels replayed from a CUDA graph (captured launches are counted once at capture)."""
+    LAUNCHES["total"] += n
 
 
 def ptr(t: torch.Tensor | None) -> int | None:

@@ -1,0 +1,127 @@
+"""Paged attention (GQA / MHA / MLA) for prefill (varlen, causal) and decode.
+
+KV-cache layout per layer: ``k_cache [num_blocks, Hkv, block_size, D]`` and
+``v_cache [num_blocks, Hkv, block_size, Dv]`` bf16 (MLA: one latent "head" of
+kv_lora + rope dims, ``v_cache`` None).  A step's sequences are described by
+:class:`AttnMetadata`: query rows of sequence b are ``q[q_start[b]:q_start[b+1]]``
+at absolute positions ``kv_len[b] - q_len_b + i``, attending causally to keys
+``[0, pos]`` found through ``block_table[b]``.
+
+On a GPU, ``paged_attention`` runs the tcgen05 flash-attention kernel in
+``csrc/cuda/attention_tc.cu`` (query rows of a GQA group packed into one
+128-row MMA tile, split-KV for decode); ``paged_attention_ref`` is the
+PyTorch restatement used on CPU and as the test oracle.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from . import _native as N
+
+
+@dataclass
+class AttnMetadata:
+    num_seqs: int
+    q_start: torch.Tensor        # int32 [B+1] (device)
+    kv_len: torch.Tensor         # int32 [B]
+    block_table: torch.Tensor    # int32 [B, max_blocks]
+    slot_mapping: torch.Tensor   # int32 [T]
+    positions: torch.Tensor      # int32 [T]
+    max_q_len: int
+    max_kv_len: int
+    is_decode: bool
+    # host copies (for CPU reference paths / planning); optional
+    q_start_host: list | None = None
+    kv_len_host: list | None = None
+    seq_slots: torch.Tensor | None = None   # int32 [B] request slot (recurrent-state index)
+    seq_fresh: torch.Tensor | None = None   # int32 [B] 1 if the sequence starts at position 0 this step
+    num_splits: int = 1
+
+    @property
+    def num_tokens(self) -> int:
+        return self.slot_mapping.shape[0]
+
+
+def _gather_kv(cache: torch.Tensor, block_table_row: torch.Tensor, n: int) -> torch.Tensor:
+    """[num_blocks, H, bs, D] -> [n, H, D] for the first n tokens of one sequence."""
+    bs = cache.shape[2]
+    nb = (n + bs - 1) // bs
+    blocks = cache[block_table_row[:nb].long()]            # [nb, H, bs, D]
+    return blocks.permute(0, 2, 1, 3).reshape(nb * bs, cache.shape[1], cache.shape[3])[:n]
+
+
+def paged_attention_ref(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor | None, meta: AttnMetadata,
+                        scale: float, v_dim: int | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """q [T, Hq, Dqk] -> o [T, Hq, Dv] (fp32 math)."""
+    T, Hq, D = q.shape
+    qs = meta.q_start_host if meta.q_start_host is not None else meta.q_start.tolist()
+    kl = meta.kv_len_host if meta.kv_len_host is not None else meta.kv_len.tolist()
+    Dv = v_dim if v_dim is not None else (v_cache.shape[3] if v_cache is not None else D)
+    o = out if out is not None else torch.zeros(T, Hq, Dv, dtype=q.dtype, device=q.device)
+    for b in range(meta.num_seqs):
+        s0, s1 = qs[b], qs[b + 1]
+        ql = s1 - s0
+        if ql == 0:
+            continue
+        n = kl[b]
+        k = _gather_kv(k_cache, meta.block_table[b], n).float()          # [n, Hk, D]
+        v = _gather_kv(v_cache, meta.block_table[b], n).float() if v_cache is not None else k[..., :Dv]
+        Hk = k.shape[1]
+        G = Hq // Hk
+        qq = q[s0:s1].float()                                              # [ql, Hq, D]
+        kk = k.repeat_interleave(G, dim=1)
+        vv = v.repeat_interleave(G, dim=1)
+        s = torch.einsum("qhd,khd->hqk", qq, kk) * scale
+        pos = torch.arange(n - ql, n, device=q.device)
+        mask = torch.arange(n, device=q.device)[None, :] > pos[:, None]
+        s = s.masked_fill(mask[None], float("-inf"))
+        p = torch.softmax(s, dim=-1)
+        o[s0:s1] = torch.einsum("hqk,khd->qhd", p, vv).to(o.dtype)
+    return o
+
+
+def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor | None, meta: AttnMetadata,
+                    scale: float | None = None, v_dim: int | None = None, out: torch.Tensor | None = None,
+                    workspace: torch.Tensor | None = None) -> torch.Tensor:
+    T, Hq, D = q.shape
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    if not q.is_cuda or not N.has_symbol("xtu_paged_attention"):
+        if q.is_cuda and N.native_required():
+            raise N.NativeLibraryMissing("xtu_paged_attention missing from the CUDA library")
+        return paged_attention_ref(q, k_cache, v_cache, meta, scale, v_dim, out)
+    Hk = k_cache.shape[1]
+    Dv = v_dim if v_dim is not None else (v_cache.shape[3] if v_cache is not None else D)
+    o = out if out is not None else torch.empty(T, Hq, Dv, dtype=q.dtype, device=q.device)
+    assert q.stride(2) == 1 and q.stride(1) == D and o.is_contiguous()
+    splits = meta.num_splits
+    ws = workspace
+    need = num_split_workspace(T, Hq, Dv, splits) if splits > 1 else 0
+    if need and (ws is None or ws.numel() < need):
+        ws = torch.empty(need, dtype=torch.float32, device=q.device)
+    vc = v_cache if v_cache is not None else k_cache
+    N.call("xtu_paged_attention", q.data_ptr(), q.stride(0), k_cache.data_ptr(), vc.data_ptr(),
+           int(v_cache is None), o.data_ptr(), o.stride(0), meta.q_start.data_ptr(), meta.kv_len.data_ptr(),
+           meta.block_table.data_ptr(), meta.block_table.stride(0), meta.num_seqs, meta.max_q_len,
+           meta.max_kv_len, T, Hq, Hk, D, Dv, k_cache.shape[2], k_cache.shape[0], float(scale), splits,
+           N.ptr(ws) if splits > 1 else None, N.status_buffer(q.device).data_ptr(), N.stream_ptr(q.device))
+    return o
+
+
+def num_split_workspace(T: int, Hq: int, Dv: int, splits: int) -> int:
+    """fp32 elements of split-KV partials: O [splits, T, Hq, Dv] + (m, l) [splits, T, Hq, 2]."""
+    return splits * T * Hq * (Dv + 2)
+
+
+def choose_splits(num_seqs: int, num_kv_heads: int, max_kv_len: int, rows_per_tile_tiles: int = 1,
+                  num_sms: int = 148) -> int:
+    """Split-KV factor for decode so that (seqs x kv heads x splits) covers the SMs."""
+    ctas = max(1, num_seqs * num_kv_heads * rows_per_tile_tiles)
+    if ctas >= num_sms:
+        return 1
+    per_split_min = 256  # keys
+    max_split = max(1, max_kv_len // per_split_min)
+    return int(max(1, min(max_split, (num_sms + ctas - 1) // ctas, 64)))

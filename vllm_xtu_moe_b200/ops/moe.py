@@ -1,0 +1,196 @@
+"""GPU MoE layer: route -> permute -> grouped gate/up GEMM (+SwiGLU) -> grouped
+down GEMM (x top-k weight, scattered to the pair's slot) -> per-token combine.
+
+Replaces the reference's streamed-layer kernels (vllm_xiaotu_moe/gpu_prefill.py:
+2566 ``gpu_moe_layer``; gpu_prefill_fp8.py:458 ``gpu_moe_layer_fp8``) with one
+graph-capturable pipeline whose buffers are sized once (``MoEWorkspace``).
+
+Tier split: only pairs whose expert id falls in ``[lo, hi)`` are computed here;
+others (experts of another EP rank, or of the CPU tier) are skipped by the
+permute and contribute through ``extra`` in the combine.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import torch
+
+from . import _native as N
+from . import gemm as G
+from .quant import dequant_fp8_block, dequant_mxfp4, dequant_nvfp4
+
+
+@dataclass
+class ExpertWeights:
+    """Routed-expert weights of one layer in GPU-kernel layout.
+
+    fmt: "bf16" or "fp8" (e4m3 + 128x128 fp32 block scales).
+    w13: [E, 2I, H]; when ``interleaved``, rows are arranged in 256-row blocks of
+    (128 gate rows, 128 up rows) so the gate/up GEMM can fuse SwiGLU.
+    w2:  [E, H, I].
+    """
+    fmt: str
+    w13: torch.Tensor
+    w2: torch.Tensor
+    s13: torch.Tensor | None = None
+    s2: torch.Tensor | None = None
+    interleaved: bool = False
+    gs13: torch.Tensor | None = None  # nvfp4 per-expert global scales
+    gs2: torch.Tensor | None = None
+
+    @property
+    def num_experts(self) -> int:
+        return self.w13.shape[0]
+
+    @property
+    def hidden(self) -> int:
+        return self.w13.shape[2] if self.fmt in ("bf16", "fp8") else self.w13.shape[2] * 2
+
+    @property
+    def inter(self) -> int:
+        return self.w13.shape[1] // 2
+
+    def nbytes(self) -> int:
+        return sum(t.numel() * t.element_size() for t in (self.w13, self.w2, self.s13, self.s2) if t is not None)
+
+    def dequant(self, e: int) -> tuple[torch.Tensor, torch.Tensor]:
+        """Dense fp32 (w13 [2I,H] in gate-then-up order, w2 [H,I]) of expert e."""
+        if self.fmt == "bf16":
+            w13, w2 = self.w13[e].float(), self.w2[e].float()
+            s13 = None
+        elif self.fmt == "fp8":
+            w13 = dequant_fp8_block(self.w13[e], self.s13[e])
+            w2 = dequant_fp8_block(self.w2[e], self.s2[e])
+        elif self.fmt == "mxfp4":
+            w13 = dequant_mxfp4(self.w13[e], self.s13[e])
+            w2 = dequant_mxfp4(self.w2[e], self.s2[e])
+        elif self.fmt == "nvfp4":
+            w13 = dequant_nvfp4(self.w13[e], self.s13[e], self.gs13[e])
+            w2 = dequant_nvfp4(self.w2[e], self.s2[e], self.gs2[e])
+        else:
+            raise ValueError(self.fmt)
+        if self.interleaved:
+            I = w13.shape[0] // 2
+            b = w13.reshape(I // 128, 2, 128, -1)
+            w13 = torch.cat([b[:, 0].reshape(I, -1), b[:, 1].reshape(I, -1)], dim=0)
+        return w13, w2
+
+
+@dataclass
+class MoEWorkspace:
+    """Static buffers for one MoE layer call of up to ``max_tokens`` tokens."""
+    max_tokens: int
+    top_k: int
+    num_experts: int
+    hidden: int
+    inter: int
+    device: torch.device
+    bufs: dict = field(default_factory=dict)
+
+    def __post_init__(self):
+        n = self.max_tokens * self.top_k
+        E, H, I, d = self.num_experts, self.hidden, self.inter, self.device
+        self.counts = torch.zeros(E, dtype=torch.int32, device=d)
+        self.seg = torch.zeros(E + 1, dtype=torch.int32, device=d)
+        self.cursor = torch.zeros(E, dtype=torch.int32, device=d)
+        self.perm_slot = torch.zeros(n, dtype=torch.int32, device=d)
+        self.perm_w = torch.zeros(n, dtype=torch.float32, device=d)
+        self.xp = torch.empty(n, H, dtype=torch.bfloat16, device=d)
+        self.h = torch.empty(n, I, dtype=torch.bfloat16, device=d)
+        self.h13 = None  # unfused gate/up output, allocated on demand
+        self.slots = torch.empty(n, H, dtype=torch.bfloat16, device=d)
+        self.mx = G.max_mtiles(n, E)
+        self.tiles = torch.empty(self.mx * 4, dtype=torch.int32, device=d)
+        self.ntiles = torch.zeros(1, dtype=torch.int32, device=d)
+
+    def nbytes(self) -> int:
+        return sum(t.numel() * t.element_size() for t in vars(self).values() if isinstance(t, torch.Tensor))
+
+
+def moe_ref(x, ids, weights, experts: ExpertWeights, lo=0, hi=None, act_limit=0.0, act_alpha=1.0, act_beta=0.0):
+    """fp32 reference: sum_k w_k * down(SwiGLU(gate_up(x))) over local pairs (bf16 intermediates)."""
+    T, H = x.shape
+    hi = experts.num_experts + lo if hi is None else hi
+    out = torch.zeros(T, H, dtype=torch.float32, device=x.device)
+    for e in torch.unique(ids).tolist():
+        if e < lo or e >= hi:
+            continue
+        w13, w2 = experts.dequant(e - lo)
+        w13 = w13.to(torch.bfloat16).float()
+        w2 = w2.to(torch.bfloat16).float()
+        I = w13.shape[0] // 2
+        tok, kk = (ids == e).nonzero(as_tuple=True)
+        y = x[tok].float() @ w13.t()
+        h = G.silu_and_mul_clamped(y[:, :I], y[:, I:], act_limit, act_alpha, act_beta).to(torch.bfloat16).float()
+        o = (h @ w2.t()) * weights[tok, kk].float()[:, None]
+        out.index_add_(0, tok, o.to(torch.bfloat16).float())
+    return out
+
+
+def fused_moe(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, experts: ExpertWeights,
+              ws: MoEWorkspace | None = None, *, lo: int = 0, shared: torch.Tensor | None = None,
+              extra: torch.Tensor | None = None, act_limit: float = 0.0, act_alpha: float = 1.0,
+              act_beta: float = 0.0, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Routed-expert MoE over the local experts [lo, lo+E).
+
+    x [T, H] bf16, ids/weights [T, K]; shared [T, H] (shared-expert output) and
+    extra [T, H] fp32 (e.g. the CPU tier's partial) are added in the combine.
+    """
+    T, H = x.shape
+    K = ids.shape[1]
+    E = experts.num_experts
+    if not x.is_cuda:
+        o = moe_ref(x, ids, weights, experts, lo, lo + E, act_limit, act_alpha, act_beta)
+        if shared is not None:
+            o = o + shared.float()
+        if extra is not None:
+            o = o + extra.float()
+        return o.to(x.dtype) if out is None else out.copy_(o)
+    if experts.fmt not in ("bf16", "fp8"):
+        raise NotImplementedError(f"GPU grouped GEMM for {experts.fmt}")
+    if ws is None or ws.max_tokens < T:
+        ws = MoEWorkspace(T, K, E, H, experts.inter, x.device)
+    assert x.is_contiguous() and ids.is_contiguous() and weights.is_contiguous()
+    s = N.stream_ptr(x.device)
+    n = T * K
+    N.call("xtu_moe_permute", ids.data_ptr(), weights.data_ptr(), T, K, lo, lo + E, ws.counts.data_ptr(),
+           ws.seg.data_ptr(), ws.cursor.data_ptr(), ws.perm_slot.data_ptr(), ws.perm_w.data_ptr(), x.data_ptr(), H,
+           x.stride(0), ws.xp.data_ptr(), s)
+    tiles = G.build_mtiles(ws.seg, n, ws.tiles, ws.ntiles)
+    xp = ws.xp[:n]
+    ws_scale13 = experts.s13 if experts.fmt == "fp8" else None
+    ws_scale2 = experts.s2 if experts.fmt == "fp8" else None
+    I = experts.inter
+    if experts.interleaved:
+        G.grouped_gemm(xp, experts.w13, ws.seg, w_scale=ws_scale13, epilogue=G.EPI_SWIGLU, out=ws.h[:n],
+                       act_limit=act_limit, act_alpha=act_alpha, act_beta=act_beta, tiles=tiles)
+    else:
+        if ws.h13 is None or ws.h13.shape[0] < n:
+            ws.h13 = torch.empty(ws.max_tokens * K, 2 * I, dtype=torch.bfloat16, device=x.device)
+        G.grouped_gemm(xp, experts.w13, ws.seg, w_scale=ws_scale13, epilogue=G.EPI_BF16, out=ws.h13[:n],
+                       tiles=tiles)
+        N.call("xtu_silu_mul", ws.h13.data_ptr(), n, I, float(act_limit), float(act_alpha), float(act_beta),
+               ws.h.data_ptr(), s)
+    G.grouped_gemm(ws.h[:n], experts.w2, ws.seg, w_scale=ws_scale2, epilogue=G.EPI_BF16, out=ws.slots[:n],
+                   row_scale=ws.perm_w, row_dest=ws.perm_slot, tiles=tiles)
+    y = out if out is not None else torch.empty(T, H, dtype=torch.bfloat16, device=x.device)
+    N.call("xtu_moe_combine", ws.slots.data_ptr(), ids.data_ptr(), T, K, H, lo, lo + E, N.ptr(shared),
+           N.ptr(extra), y.data_ptr(), None, s)
+    return y
+
+
+def prepare_experts(fmt: str, w13: torch.Tensor, w2: torch.Tensor, s13=None, s2=None, gs13=None,
+                    gs2=None) -> ExpertWeights:
+    """Checkpoint layout (w13 [E, 2I, H] gate-then-up) -> kernel layout.
+
+    Interleaves gate/up rows in 128-row blocks when I % 128 == 0 (fused SwiGLU).
+    """
+    I = w13.shape[1] // 2
+    inter = I % 128 == 0 and fmt in ("bf16", "fp8")
+    if inter:
+        if fmt == "fp8":
+            w13 = G.interleave_gate_up(w13.view(torch.uint8)).view(torch.float8_e4m3fn)
+            s13 = G.interleave_gate_up_scale(s13)
+        else:
+            w13 = G.interleave_gate_up(w13)
+    return ExpertWeights(fmt, w13.contiguous(), w2.contiguous(), s13, s2, inter, gs13, gs2)
