@@ -49,6 +49,7 @@ struct AttnParams {
   const int* block_table;  // [B, bt_stride]
   int bt_stride;
   int Hq, Hkv, G, rows_per_tile;  // rows_per_tile = (128 / G) * G
+  int rf;                  // row replication factor (1, 2, 4): replicas split each tile's keys
   float scale_log2;        // softmax scale * log2(e)
   int splits;
   float* ws_o;             // [splits, T, Hq, DV] (splits > 1)
@@ -57,14 +58,18 @@ struct AttnParams {
   XtuStatus* status;
 };
 
-template <int D, int DV, int BN>
+// STAGES: K/V ring depth.  BTS: block-table entries staged in shared memory (0 = read
+// the table from global memory on the fly); decode configurations prefetch the CTA's
+// whole block list so the producer never waits on a dependent global load.
+template <int D, int DV, int BN, int STAGES_ = 2, int BTS = 0>
 struct AttnCfg {
-  static constexpr int STAGES = 2;
+  static constexpr int STAGES = STAGES_;
   static constexpr int Q_BYTES = 128 * D * 2;
   static constexpr int K_BYTES = BN * D * 2;
   static constexpr int V_BYTES = BN * DV * 2;
   static constexpr int P_BYTES = 128 * BN * 2;
-  static constexpr int SMEM = Q_BYTES + STAGES * (K_BYTES + V_BYTES) + 2 * P_BYTES + 1024 + 256;
+  static constexpr int BT_BYTES = BTS * 4;
+  static constexpr int SMEM = Q_BYTES + STAGES * (K_BYTES + V_BYTES) + 2 * P_BYTES + BT_BYTES + 1024 + 256;
   static constexpr int S_COL0 = 0;          // two S buffers: [0, BN), [BN, 2BN)
   static constexpr int O_COL0 = 2 * BN;     // O: [2BN, 2BN + DV)
   static constexpr int TMEM_COLS = (2 * BN + DV) <= 256 ? 256 : 512;
@@ -80,11 +85,11 @@ __device__ __forceinline__ void st_sw128(uint8_t* tile, int rows, int row, int c
   *reinterpret_cast<uint4*>(base + ((piece ^ (row & 7)) << 4)) = v;
 }
 
-template <int D, int DV, int BN>
+template <int D, int DV, int BN, int STAGES_, int BTS>
 __global__ void __launch_bounds__(192, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
                     AttnParams p) {
-  using C = AttnCfg<D, DV, BN>;
+  using C = AttnCfg<D, DV, BN, STAGES_, BTS>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
@@ -92,14 +97,15 @@ __global__ void __launch_bounds__(192, 1)
   uint8_t* sK = sQ + C::Q_BYTES;                       // [STAGES][K_BYTES]
   uint8_t* sV = sK + C::STAGES * C::K_BYTES;           // [STAGES][V_BYTES]
   uint8_t* sP = sV + C::STAGES * C::V_BYTES;           // [2][P_BYTES]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * C::P_BYTES);
-  uint64_t* kv_full = bars;                 // [STAGES]
-  uint64_t* kv_empty = bars + 2;            // [STAGES]
-  uint64_t* q_ready = bars + 4;
-  uint64_t* s_full = bars + 5;              // [2]
-  uint64_t* p_full = bars + 7;              // [2]
-  uint64_t* o_done = bars + 9;              // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  int* sBT = reinterpret_cast<int*>(sP + 2 * C::P_BYTES);      // [BTS]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * C::P_BYTES + C::BT_BYTES);
+  uint64_t* kv_full = bars;                          // [STAGES]
+  uint64_t* kv_empty = bars + C::STAGES;             // [STAGES]
+  uint64_t* q_ready = bars + 2 * C::STAGES;
+  uint64_t* s_full = q_ready + 1;                    // [2]
+  uint64_t* p_full = s_full + 2;                     // [2]
+  uint64_t* o_done = p_full + 2;                     // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = blockIdx.z;
@@ -129,6 +135,16 @@ __global__ void __launch_bounds__(192, 1)
     fence_barrier_init();
   }
   if (warp == 1) tmem_alloc(tmem_slot, C::TMEM_COLS);
+  const int n_blocks_seq = (kv_len + KV_BLOCK - 1) / KV_BLOCK;
+  const int lb0 = t_begin * (BN / KV_BLOCK);
+  const int n_lb = n_tiles * (BN / KV_BLOCK);
+  if (BTS > 0 && warp == 0) {
+    const int* bt = p.block_table + (size_t)b * p.bt_stride;
+    for (int i = lane; i < n_lb && i < BTS; i += 32) {
+      const int lb = lb0 + i;
+      sBT[i] = bt[lb < n_blocks_seq ? lb : 0];
+    }
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -138,7 +154,6 @@ __global__ void __launch_bounds__(192, 1)
     // ------------------------------------------------------------ producer
     if (elect_one() && n_tiles > 0) {
       const int* bt = p.block_table + (size_t)b * p.bt_stride;
-      const int n_blocks_seq = (kv_len + KV_BLOCK - 1) / KV_BLOCK;
       for (int jj = 0; jj < n_tiles; ++jj) {
         const int stage = jj % C::STAGES;
         const uint32_t ph = (jj / C::STAGES) & 1;
@@ -148,8 +163,14 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
         for (int sb = 0; sb < BN / KV_BLOCK; ++sb) {
           int lb = j * (BN / KV_BLOCK) + sb;
-          if (lb >= n_blocks_seq) lb = 0;              // past the end: any valid block, masked later
-          const int row = (bt[lb] * p.Hkv + kvh) * KV_BLOCK;
+          int blk;
+          if (BTS > 0 && lb - lb0 < BTS) {
+            blk = sBT[lb - lb0];                       // staged (entries past the end hold block 0)
+          } else {
+            if (lb >= n_blocks_seq) lb = 0;            // past the end: any valid block, masked later
+            blk = bt[lb];
+          }
+          const int row = (blk * p.Hkv + kvh) * KV_BLOCK;
 #pragma unroll
           for (int c = 0; c < D / 64; ++c)
             tma_load_2d(sK + stage * C::K_BYTES + c * (BN * 128) + sb * (KV_BLOCK * 128), &tmap_k, &kv_full[stage],
@@ -208,10 +229,20 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else {
     // ------------------------------------------------------------ softmax / epilogue (warps 2..5)
+    // Row layout.  r = TMEM lane / MMA row.  With few valid query rows (decode), each
+    // logical row is replicated into RF lane quarters and replica `part` only scores
+    // keys [part*KP, (part+1)*KP) of every tile, so RF warps share one row's keys; the
+    // replicas' (max, sum, O) are merged in the epilogue.
     const int qd = warp & 3;
     const int r = qd * 32 + lane;
-    const int pi = r / p.G, g = r - (r / p.G) * p.G;
-    const bool row_valid = (r < p.rows_per_tile) && (pi < n_pos);
+    const int RF = p.rf;
+    const int LR = 128 / RF;                 // logical rows
+    const int KP = BN / RF;                  // keys per replica per tile
+    const int lr = r % LR;
+    const int part = r / LR;
+    const int rows_valid_all = min(p.rows_per_tile, n_pos * p.G);
+    const int pi = lr / p.G, g = lr - (lr / p.G) * p.G;
+    const bool row_valid = lr < rows_valid_all;
     const int tok = q0 + i0 + pi;
     const int head = kvh * p.G + g;
     const int qpos = ctx0 + i0 + pi;
@@ -224,32 +255,49 @@ __global__ void __launch_bounds__(192, 1)
         if (row_valid) v = *reinterpret_cast<const uint4*>(src + c8);
         st_sw128(sQ, 128, r, c8, v);
       }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(q_ready);
     }
     float m = -FLT_MAX;   // running max (log2 domain); -FLT_MAX = none yet
     float l = 0.f;
     const uint32_t lane_base = tmem + ((uint32_t)(qd * 32) << 16);
+    // A warp whose 32 rows are all padding skips the softmax and only keeps the barrier
+    // phases in step.  Rows whose P is written only in part (replicas) or never
+    // (padding) start from zeroed P buffers.
+    const bool warp_active = ((qd * 32) % LR) < rows_valid_all;
+    if (RF > 1 || !warp_active) {
+#pragma unroll 1
+      for (int c8 = 0; c8 < BN; c8 += 8) {
+        st_sw128(sP, 128, r, c8, make_uint4(0, 0, 0, 0));
+        st_sw128(sP + C::P_BYTES, 128, r, c8, make_uint4(0, 0, 0, 0));
+      }
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(q_ready);
     bool ok = true;
     for (int jj = 0; jj < n_tiles && ok; ++jj) {
       const int j = t_begin + jj;
       if (!mbar_wait(&s_full[jj & 1], (jj >> 1) & 1, p.status, 120)) { ok = false; break; }
+      if (!warp_active) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[jj & 1]);
+        continue;
+      }
       tc_fence_after();
       const uint32_t s_addr = lane_base + C::S_COL0 + (jj & 1) * BN;
       const int key0 = j * BN;
-      // pass 1: masked row max
+      const int c_lo = part * KP, c_hi = c_lo + KP;
+      // pass 1: masked row max over this replica's keys
       float mx = -FLT_MAX;
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        uint32_t v[32];
-        tmem_ld32(s_addr + c, v);
+      for (int c = c_lo; c < c_hi; c += 16) {
+        uint32_t v[16];
+        tmem_ld16(s_addr + c, v);
         tmem_wait_ld();
 #pragma unroll
-        for (int t = 0; t < 32; ++t) {
+        for (int t = 0; t < 16; ++t) {
           const int key = key0 + c + t;
-          const float s = __uint_as_float(v[t]) * p.scale_log2;
-          if (row_valid && key <= qpos) mx = fmaxf(mx, s);
+          const float sv = __uint_as_float(v[t]) * p.scale_log2;
+          if (row_valid && key <= qpos) mx = fmaxf(mx, sv);
         }
       }
       // Raise the running max only when it grows by more than 2^8.  tcgen05.ld/st are
@@ -286,13 +334,13 @@ __global__ void __launch_bounds__(192, 1)
       uint8_t* pbuf = sP + (jj & 1) * C::P_BYTES;
       float rs = 0.f;
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        uint32_t v[32];
-        tmem_ld32(s_addr + c, v);
+      for (int c = c_lo; c < c_hi; c += 16) {
+        uint32_t v[16];
+        tmem_ld16(s_addr + c, v);
         tmem_wait_ld();
-        uint32_t pk[16];
+        uint32_t pk[8];
 #pragma unroll
-        for (int t = 0; t < 32; t += 2) {
+        for (int t = 0; t < 16; t += 2) {
           const int key = key0 + c + t;
           float e0 = 0.f, e1 = 0.f;
           if (row_valid && m_use != -FLT_MAX) {
@@ -302,9 +350,8 @@ __global__ void __launch_bounds__(192, 1)
           rs += e0 + e1;
           pk[t >> 1] = pack_bf16x2(e0, e1);
         }
-#pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4)
-          st_sw128(pbuf, 128, r, c + q4 * 8, make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]));
+        st_sw128(pbuf, 128, r, c, make_uint4(pk[0], pk[1], pk[2], pk[3]));
+        st_sw128(pbuf, 128, r, c + 8, make_uint4(pk[4], pk[5], pk[6], pk[7]));
       }
       l += rs;
       fence_proxy_async_smem();
@@ -313,48 +360,91 @@ __global__ void __launch_bounds__(192, 1)
       if (lane == 0) mbar_arrive(&p_full[jj & 1]);
     }
     // ---- epilogue
-    if (ok && n_tiles > 0) {
-      const int last = n_tiles - 1;
-      if (mbar_wait(&o_done[last & 1], (last >> 1) & 1, p.status, 123)) {
-        tc_fence_after();
-        if (p.splits == 1) {
-          const float inv = l > 0.f ? 1.f / l : 0.f;
-          __nv_bfloat16* dst = p.o + (size_t)tok * p.o_stride + (size_t)head * DV;
+    const int last = n_tiles - 1;
+    bool have_o = false;
+    if (n_tiles > 0 && warp_active && ok) {
+      have_o = mbar_wait(&o_done[last & 1], (last >> 1) & 1, p.status, 123);
+      tc_fence_after();
+    }
+    if (RF == 1) {
+      if (have_o) {
+        const float inv = l > 0.f ? 1.f / l : 0.f;
 #pragma unroll 1
-          for (int c = 0; c < DV; c += 32) {
-            uint32_t v[32];
-            tmem_ld32(lane_base + C::O_COL0 + c, v);
-            tmem_wait_ld();
-            if (row_valid) {
-              uint32_t pk[16];
+        for (int c = 0; c < DV; c += 32) {
+          uint32_t v[32];
+          tmem_ld32(lane_base + C::O_COL0 + c, v);
+          tmem_wait_ld();
+          if (!row_valid) continue;
+          if (p.splits == 1) {
+            __nv_bfloat16* dst = p.o + (size_t)tok * p.o_stride + (size_t)head * DV;
+            uint32_t pk[16];
 #pragma unroll
-              for (int t = 0; t < 16; ++t)
-                pk[t] = pack_bf16x2(__uint_as_float(v[2 * t]) * inv, __uint_as_float(v[2 * t + 1]) * inv);
-              uint4* d4 = reinterpret_cast<uint4*>(dst + c);
+            for (int t = 0; t < 16; ++t)
+              pk[t] = pack_bf16x2(__uint_as_float(v[2 * t]) * inv, __uint_as_float(v[2 * t + 1]) * inv);
+            uint4* d4 = reinterpret_cast<uint4*>(dst + c);
 #pragma unroll
-              for (int t = 0; t < 4; ++t) d4[t] = make_uint4(pk[4 * t], pk[4 * t + 1], pk[4 * t + 2], pk[4 * t + 3]);
-            }
+            for (int t = 0; t < 4; ++t) d4[t] = make_uint4(pk[4 * t], pk[4 * t + 1], pk[4 * t + 2], pk[4 * t + 3]);
+          } else {
+            float4* d4 = reinterpret_cast<float4*>(p.ws_o + (((size_t)split * p.T + tok) * p.Hq + head) * DV + c);
+#pragma unroll
+            for (int t = 0; t < 8; ++t)
+              d4[t] = make_float4(__uint_as_float(v[4 * t]) * inv, __uint_as_float(v[4 * t + 1]) * inv,
+                                  __uint_as_float(v[4 * t + 2]) * inv, __uint_as_float(v[4 * t + 3]) * inv);
+          }
+        }
+        if (p.splits > 1 && row_valid)
+          p.ws_lse[((size_t)split * p.T + tok) * p.Hq + head] = l > 0.f ? m + log2f(l) : -FLT_MAX;
+      } else if (n_tiles == 0 && p.splits > 1 && row_valid) {
+        float* dst = p.ws_o + (((size_t)split * p.T + tok) * p.Hq + head) * DV;
+        for (int c = 0; c < DV; ++c) dst[c] = 0.f;
+        p.ws_lse[((size_t)split * p.T + tok) * p.Hq + head] = -FLT_MAX;
+      }
+    } else if (n_tiles > 0) {
+      // merge the RF replicas of each logical row through shared memory (the K/V ring
+      // is idle now): ml[r] = (m, l); oacc[lr] += exp2(m - M) * O_r / L
+      float* ml = reinterpret_cast<float*>(sK);                 // [128][2]
+      float* oacc = ml + 256;                                   // [LR][DV]
+      for (int i = r; i < LR * DV; i += 128) oacc[i] = 0.f;
+      ml[2 * r] = (have_o && row_valid) ? m : -FLT_MAX;
+      ml[2 * r + 1] = (have_o && row_valid) ? l : 0.f;
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      float M = -FLT_MAX, L = 0.f;
+      for (int q = 0; q < RF; ++q) M = fmaxf(M, ml[2 * (lr + q * LR)]);
+      for (int q = 0; q < RF; ++q) {
+        const float mq = ml[2 * (lr + q * LR)];
+        if (mq != -FLT_MAX) L += ex2(mq - M) * ml[2 * (lr + q * LR) + 1];
+      }
+      const float f = (have_o && row_valid && m != -FLT_MAX && L > 0.f) ? ex2(m - M) / L : 0.f;
+      if (warp_active) {
+#pragma unroll 1
+        for (int c = 0; c < DV; c += 32) {
+          uint32_t v[32];
+          tmem_ld32(lane_base + C::O_COL0 + c, v);
+          tmem_wait_ld();
+          if (f != 0.f) {
+#pragma unroll
+            for (int t = 0; t < 32; ++t) atomicAdd(&oacc[lr * DV + c + t], __uint_as_float(v[t]) * f);
+          }
+        }
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (part == 0 && row_valid && ok) {
+        const float* src = oacc + lr * DV;
+        if (p.splits == 1) {
+          __nv_bfloat16* dst = p.o + (size_t)tok * p.o_stride + (size_t)head * DV;
+          for (int c = 0; c < DV; c += 8) {
+            uint4 o;
+            o.x = pack_bf16x2(src[c], src[c + 1]); o.y = pack_bf16x2(src[c + 2], src[c + 3]);
+            o.z = pack_bf16x2(src[c + 4], src[c + 5]); o.w = pack_bf16x2(src[c + 6], src[c + 7]);
+            *reinterpret_cast<uint4*>(dst + c) = o;
           }
         } else {
           float* dst = p.ws_o + (((size_t)split * p.T + tok) * p.Hq + head) * DV;
-          const float inv = l > 0.f ? 1.f / l : 0.f;
-#pragma unroll 1
-          for (int c = 0; c < DV; c += 32) {
-            uint32_t v[32];
-            tmem_ld32(lane_base + C::O_COL0 + c, v);
-            tmem_wait_ld();
-            if (row_valid) {
-              float4* d4 = reinterpret_cast<float4*>(dst + c);
-#pragma unroll
-              for (int t = 0; t < 8; ++t)
-                d4[t] = make_float4(__uint_as_float(v[4 * t]) * inv, __uint_as_float(v[4 * t + 1]) * inv,
-                                    __uint_as_float(v[4 * t + 2]) * inv, __uint_as_float(v[4 * t + 3]) * inv);
-            }
-          }
-          if (row_valid) p.ws_lse[((size_t)split * p.T + tok) * p.Hq + head] = l > 0.f ? m + log2f(l) : -FLT_MAX;
+          for (int c = 0; c < DV; ++c) dst[c] = src[c];
+          p.ws_lse[((size_t)split * p.T + tok) * p.Hq + head] = L > 0.f ? M + log2f(L) : -FLT_MAX;
         }
       }
-    } else if (n_tiles == 0 && p.splits > 1 && row_valid) {
+    } else if (p.splits > 1 && row_valid && part == 0) {
       float* dst = p.ws_o + (((size_t)split * p.T + tok) * p.Hq + head) * DV;
       for (int c = 0; c < DV; ++c) dst[c] = 0.f;
       p.ws_lse[((size_t)split * p.T + tok) * p.Hq + head] = -FLT_MAX;
@@ -427,11 +517,11 @@ static int attn_tmap(CUtensorMap* map, const void* base, uint64_t rows, uint64_t
   return r == CUDA_SUCCESS ? 0 : -1000 - (int)r;
 }
 
-template <int D, int DV, int BN>
+template <int D, int DV, int BN, int STAGES = 2, int BTS = 0>
 static int launch_attn(const CUtensorMap& tk, const CUtensorMap& tv, const AttnParams& p, int grid_x, int B,
                        cudaStream_t s) {
-  using C = AttnCfg<D, DV, BN>;
-  auto k = attn_fwd_kernel<D, DV, BN>;
+  using C = AttnCfg<D, DV, BN, STAGES, BTS>;
+  auto k = attn_fwd_kernel<D, DV, BN, STAGES, BTS>;
   static bool init = false;
   if (!init) {
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
@@ -480,7 +570,15 @@ int xtu_paged_attention(const void* q, int q_stride, const void* k_cache, const 
   const int pos_per_tile = p.rows_per_tile / G;
   const int grid_x = (max_q_len + pos_per_tile - 1) / pos_per_tile;
   int r;
-  if (D == 128 && DV == 128) r = launch_attn<128, 128, 128>(tk, tv, p, grid_x, B, s);
+  // decode-shaped steps (all of a sequence's query rows fit one 128-row tile): 64-key
+  // tiles, a 4-deep K/V ring and a staged block table keep more bytes in flight per SM
+  const bool decode_shape = grid_x == 1;
+  const int rows_used = max_q_len * G;
+  // replica merge buffers live in the K ring: only the decode configurations (D <= 128) use it
+  p.rf = (!decode_shape || D > 128) ? 1 : rows_used <= 32 ? 4 : rows_used <= 64 ? 2 : 1;
+  if (decode_shape && D == 128 && DV == 128) r = launch_attn<128, 128, 128, 2, 256>(tk, tv, p, grid_x, B, s);
+  else if (decode_shape && D == 64 && DV == 64) r = launch_attn<64, 64, 64, 6, 1024>(tk, tv, p, grid_x, B, s);
+  else if (D == 128 && DV == 128) r = launch_attn<128, 128, 128>(tk, tv, p, grid_x, B, s);
   else if (D == 64 && DV == 64) r = launch_attn<64, 64, 128>(tk, tv, p, grid_x, B, s);
   else if (D == 256 && DV == 256) r = launch_attn<256, 256, 64>(tk, tv, p, grid_x, B, s);
   else if (D == 192 && DV == 128) r = launch_attn<192, 128, 64>(tk, tv, p, grid_x, B, s);

@@ -393,7 +393,10 @@ __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ slots, cons
                                    const float* __restrict__ extra, __nv_bfloat16* __restrict__ out,
                                    float* __restrict__ out_f32) {
   const int t = blockIdx.x;
-  for (int i = threadIdx.x * 8; i < H; i += blockDim.x * 8) {
+  // grid.y splits the hidden dimension so that decode-sized T still fills the GPU
+  const int span = (H / 8 + gridDim.y - 1) / gridDim.y * 8;
+  const int h0 = blockIdx.y * span, h1 = min(H, h0 + span);
+  for (int i = h0 + threadIdx.x * 8; i < h1; i += blockDim.x * 8) {
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     for (int k = 0; k < K; ++k) {
       const int id = ids[(size_t)t * K + k];
@@ -435,13 +438,18 @@ __device__ __forceinline__ float ld_f<float>(const float* p, size_t i) { return 
 template <>
 __device__ __forceinline__ float ld_f<__nv_bfloat16>(const __nv_bfloat16* p, size_t i) { return __bfloat162float(p[i]); }
 
+// grid (parts, rows): block (p, r) reduces its slice of row r to (value, index) in part_v/part_i
+// (or straight to out when parts == 1); argmax_final_kernel folds the parts.
 template <typename T>
 __global__ void argmax_kernel(const T* __restrict__ logits, int V, int stride, int* __restrict__ out,
-                              float* __restrict__ out_val) {
-  const T* row = logits + (size_t)blockIdx.x * stride;
+                              float* __restrict__ out_val, float* __restrict__ part_v, int* __restrict__ part_i) {
+  const T* row = logits + (size_t)blockIdx.y * stride;
+  const int parts = gridDim.x;
+  const int per = (V + parts - 1) / parts;
+  const int lo = blockIdx.x * per, hi = min(V, lo + per);
   float bv = -FLT_MAX;
   int bi = 0x7fffffff;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+  for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) {
     const float v = ld_f<T>(row, i);
     if (v > bv) { bv = v; bi = i; }
   }
@@ -465,9 +473,35 @@ __global__ void argmax_kernel(const T* __restrict__ logits, int V, int stride, i
       if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
     }
     if (l == 0) {
-      out[blockIdx.x] = bi;
-      if (out_val) out_val[blockIdx.x] = bv;
+      if (parts == 1) {
+        out[blockIdx.y] = bi;
+        if (out_val) out_val[blockIdx.y] = bv;
+      } else {
+        part_v[blockIdx.y * parts + blockIdx.x] = bv;
+        part_i[blockIdx.y * parts + blockIdx.x] = bi;
+      }
     }
+  }
+}
+
+__global__ void argmax_final_kernel(const float* __restrict__ part_v, const int* __restrict__ part_i, int parts,
+                                    int* __restrict__ out, float* __restrict__ out_val) {
+  const int r = blockIdx.x, l = threadIdx.x;
+  float bv = -FLT_MAX;
+  int bi = 0x7fffffff;
+  for (int i = l; i < parts; i += 32) {
+    const float v = part_v[r * parts + i];
+    const int id = part_i[r * parts + i];
+    if (v > bv || (v == bv && id < bi)) { bv = v; bi = id; }
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+  }
+  if (l == 0) {
+    out[r] = bi;
+    if (out_val) out_val[r] = bv;
   }
 }
 
@@ -583,19 +617,30 @@ int xtu_moe_combine(const void* slots, const int* ids, int T, int K, int H, int 
                     const float* extra, void* out, float* out_f32, cudaStream_t s) {
   if (T <= 0) return 0;
   if (H % 8 != 0) return -2;
-  const int threads = H / 8 < 256 ? ((H / 8 + 31) / 32) * 32 : 256;
-  moe_combine_kernel<<<T, threads, 0, s>>>((const __nv_bfloat16*)slots, ids, T, K, H, lo, hi,
+  const int threads = H / 8 < 128 ? ((H / 8 + 31) / 32) * 32 : 128;
+  int ysplit = (H / 8 + threads - 1) / threads;          // one 8-wide vector per thread
+  if (T * ysplit > 2048) ysplit = (2048 + T - 1) / T;
+  if (ysplit < 1) ysplit = 1;
+  moe_combine_kernel<<<dim3(T, ysplit), threads, 0, s>>>((const __nv_bfloat16*)slots, ids, T, K, H, lo, hi,
                                            (const __nv_bfloat16*)shared, extra, (__nv_bfloat16*)out, out_f32);
   return rc_last();
 }
 
-int xtu_argmax(const void* logits, int is_bf16, int T, int V, int stride, int* out, float* out_val, cudaStream_t s) {
+// ws: scratch of >= T * 64 * 8 bytes when V is large (nullable: single block per row)
+int xtu_argmax(const void* logits, int is_bf16, int T, int V, int stride, int* out, float* out_val, void* ws,
+               cudaStream_t s) {
   if (T <= 0) return 0;
+  int parts = ws ? (V + 8191) / 8192 : 1;
+  if (parts > 64) parts = 64;
+  float* pv = reinterpret_cast<float*>(ws);
+  int* pi = ws ? reinterpret_cast<int*>(pv + (size_t)T * 64) : nullptr;
+  const dim3 grid(parts, T);
   if (is_bf16)
-    argmax_kernel<__nv_bfloat16><<<T, 1024, 0, s>>>((const __nv_bfloat16*)logits, V, stride, out, out_val);
+    argmax_kernel<__nv_bfloat16><<<grid, 512, 0, s>>>((const __nv_bfloat16*)logits, V, stride, out, out_val, pv, pi);
   else
-    argmax_kernel<float><<<T, 1024, 0, s>>>((const float*)logits, V, stride, out, out_val);
-  return rc_last();
+    argmax_kernel<float><<<grid, 512, 0, s>>>((const float*)logits, V, stride, out, out_val, pv, pi);
+  if (parts > 1) argmax_final_kernel<<<T, 32, 0, s>>>(pv, pi, parts, out, out_val);
+  return rc_last(parts > 1 ? 2 : 1);
 }
 
 int xtu_embed(const int* ids, const void* table, int T, int H, int vocab, void* out, cudaStream_t s) {

@@ -107,7 +107,8 @@ def test_router(E, K, scoring, ng, tg):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("fmt", ["bf16", "fp8"])
-@pytest.mark.parametrize("T,E,K,H,I", [(1, 8, 2, 256, 512), (200, 16, 4, 512, 256), (33, 64, 8, 1024, 384)])
+@pytest.mark.parametrize("T,E,K,H,I", [(1, 8, 2, 256, 512), (200, 16, 4, 512, 256), (33, 64, 8, 1024, 384),
+                                       (4, 128, 8, 4096, 1408), (16, 128, 8, 1024, 256), (5, 16, 8, 512, 384)])
 def test_fused_moe(fmt, T, E, K, H, I):
     torch.manual_seed(3)
     x = torch.randn(T, H, device="cuda", dtype=torch.bfloat16)
@@ -253,3 +254,29 @@ def test_paged_attention_running_max_rescale(mode):
     N.check_status()
     ref = paged_attention_ref(q, kc, vc, meta, scale)
     assert (o.float() - ref.float()).abs().max().item() < 3e-2
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("T", [1, 4, 16, 40])
+def test_dense_mlp_paths(T):
+    """Shared-expert / dense MLP: GEMV path (T <= 16) and tensor-core path vs fp32 reference."""
+    from vllm_xtu_moe_b200.models.layers import DenseMLP, Linear
+    from vllm_xtu_moe_b200.ops import gemm as G
+    torch.manual_seed(10)
+    H, I = 1024, 1408
+    w13 = torch.randn(2 * I, H, device="cuda") / H ** 0.5
+    w2 = torch.randn(H, I, device="cuda") / I ** 0.5
+    q13, s13 = quant_fp8_block(w13)
+    q2, s2 = quant_fp8_block(w2)
+    mlp = DenseMLP(Linear(G.interleave_gate_up(q13.view(torch.uint8)).view(torch.float8_e4m3fn),
+                          G.interleave_gate_up_scale(s13)), Linear(q2, s2), True)
+    x = torch.randn(T, H, device="cuda", dtype=torch.bfloat16)
+    y = mlp(x)
+    torch.cuda.synchronize()
+    from vllm_xtu_moe_b200.ops.quant import dequant_fp8_block
+    w13d = dequant_fp8_block(q13, s13).to(torch.bfloat16).float()
+    w2d = dequant_fp8_block(q2, s2).to(torch.bfloat16).float()
+    g = x.float() @ w13d.t()
+    h = G.silu_and_mul_clamped(g[:, :I], g[:, I:]).to(torch.bfloat16).float()
+    ref = h @ w2d.t()
+    assert rel_err(y, ref) < 2e-2

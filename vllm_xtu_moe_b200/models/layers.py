@@ -33,10 +33,7 @@ class Linear:
     def __call__(self, x: torch.Tensor, out_dtype=torch.bfloat16) -> torch.Tensor:
         if not x.is_cuda and x.dtype == torch.float32:
             out_dtype = torch.float32   # CPU fp32-activation mode (exact-reference runs)
-        y = G.linear(x, self.weight, self.scale, out_dtype=out_dtype)
-        if self.bias is not None:
-            y.add_(self.bias)
-        return y
+        return G.linear(x, self.weight, self.scale, out_dtype=out_dtype, bias=self.bias)
 
     def dense_weight(self) -> torch.Tensor:
         if self.scale is None:
@@ -112,6 +109,9 @@ class DenseMLP:
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         T = x.shape[0]
+        if x.is_cuda and self.interleaved and T <= G.GEMV_MAX_M:
+            return M.dense_swiglu_gemv(x.contiguous(), self.gate_up.weight, self.gate_up.scale, self.down.weight,
+                                       self.down.scale, self.limit, self._seg)
         if x.is_cuda and self.interleaved:
             seg = self._seg.get((x.device, T))
             if seg is None:

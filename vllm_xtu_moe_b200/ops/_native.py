@@ -43,9 +43,11 @@ _SIGS: dict[str, list] = {
     "xtu_router_topk": [P, P, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_float, P, P, c_int, P],
     "xtu_moe_permute": [P, P, c_int, c_int, c_int, c_int, P, P, P, P, P, P, c_int, c_int, P, P],
     "xtu_moe_combine": [P, P, c_int, c_int, c_int, c_int, c_int, P, P, P, P, P],
-    "xtu_argmax": [P, c_int, c_int, c_int, c_int, P, P, P],
+    "xtu_argmax": [P, c_int, c_int, c_int, c_int, P, P, P, P],
     "xtu_embed": [P, P, c_int, c_int, c_int, P, P],
     "xtu_silu_mul": [P, c_int, c_int, c_float, c_float, c_float, P, P],
+    "xtu_gemv": [P, P, c_int, c_int, c_int, P, c_int, c_int, P, P, c_int, c_int, P],
+    "xtu_moe_gemv": [P, P, P, P, c_int, c_int, c_int, c_int, P, P, P, P, P, P, c_int, c_float, c_float, c_float, P],
     "xtu_paged_attention": [P, c_int, P, P, c_int, P, c_int, P, P, P, c_int, c_int, c_int, c_int, c_int, c_int,
                             c_int, c_int, c_int, c_int, c_int, c_float, c_int, P, P, P],
 }

@@ -118,10 +118,11 @@ def num_split_workspace(T: int, Hq: int, Dv: int, splits: int) -> int:
 
 def choose_splits(num_seqs: int, num_kv_heads: int, max_kv_len: int, rows_per_tile_tiles: int = 1,
                   num_sms: int = 148) -> int:
-    """Split-KV factor for decode so that (seqs x kv heads x splits) covers the SMs."""
+    """Split-KV factor for decode: the largest split count whose CTAs (seqs x kv heads x
+    splits, one CTA per SM) still fit in one wave, so no SM runs a lone second-wave CTA."""
     ctas = max(1, num_seqs * num_kv_heads * rows_per_tile_tiles)
     if ctas >= num_sms:
         return 1
-    per_split_min = 256  # keys
+    per_split_min = 512  # keys
     max_split = max(1, max_kv_len // per_split_min)
-    return int(max(1, min(max_split, (num_sms + ctas - 1) // ctas, 64)))
+    return int(max(1, min(max_split, num_sms // ctas, 64)))

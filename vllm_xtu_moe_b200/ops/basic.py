@@ -183,8 +183,9 @@ def argmax(logits: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tenso
     T, V = logits.shape
     assert logits.stride(1) == 1
     y = out if out is not None else torch.empty(T, dtype=torch.int32, device=logits.device)
+    ws = torch.empty(T * 64 * 2, dtype=torch.float32, device=logits.device) if V > 8192 else None
     N.call("xtu_argmax", logits.data_ptr(), int(logits.dtype == torch.bfloat16), T, V, logits.stride(0),
-           y.data_ptr(), None, N.stream_ptr(logits.device))
+           y.data_ptr(), None, N.ptr(ws), N.stream_ptr(logits.device))
     return y
 
 

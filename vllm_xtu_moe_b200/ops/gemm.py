@@ -59,19 +59,42 @@ def gemm_fp8w(a: torch.Tensor, w8: torch.Tensor, w_scale: torch.Tensor, out: tor
     return out
 
 
+GEMV_MAX_M = 16
+
+
+def gemv(x: torch.Tensor, weight: torch.Tensor, scale: torch.Tensor | None = None, bias: torch.Tensor | None = None,
+         out_dtype: torch.dtype = torch.bfloat16, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Decode-size y[M<=16, N] = x W^T (+ bias) streaming W (bf16 or e4m3 + block scales)."""
+    M, K = x.shape
+    Nn = weight.shape[0]
+    y = out if out is not None else torch.empty(M, Nn, dtype=out_dtype, device=x.device)
+    N.call("xtu_gemv", weight.data_ptr(), N.ptr(scale), int(scale is not None), Nn, K, x.data_ptr(), x.stride(0), M,
+           N.ptr(bias), y.data_ptr(), y.stride(0), int(y.dtype == torch.float32), N.stream_ptr(x.device))
+    return y
+
+
 def linear(x: torch.Tensor, weight: torch.Tensor, scale: torch.Tensor | None = None,
-           out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
-    """y = x @ W^T for 2-D or batched x; W bf16 or e4m3 (+ block scales)."""
+           out_dtype: torch.dtype = torch.bfloat16, bias: torch.Tensor | None = None) -> torch.Tensor:
+    """y = x @ W^T (+ bias) for 2-D or batched x; W bf16 or e4m3 (+ block scales).
+
+    GPU dispatch: <= 16 rows -> weight-streaming GEMV (bias fused); more rows ->
+    tcgen05 GEMM."""
     shp = x.shape
     x2 = x.reshape(-1, shp[-1])
     if x2.shape[0] == 0:
         return x.new_empty(*shp[:-1], weight.shape[0], dtype=out_dtype)
     if not x2.is_contiguous():
         x2 = x2.contiguous()
+    K = x2.shape[1]
+    if x2.is_cuda and x2.shape[0] <= GEMV_MAX_M and K % 16 == 0 and x2.dtype == torch.bfloat16:
+        y = gemv(x2, weight, scale, bias, out_dtype)
+        return y.reshape(*shp[:-1], weight.shape[0])
     if scale is None:
         y = gemm_bf16(x2, weight, out_dtype=out_dtype)
     else:
         y = gemm_fp8w(x2, weight, scale, out_dtype=out_dtype)
+    if bias is not None:
+        y.add_(bias)
     return y.reshape(*shp[:-1], weight.shape[0])
 
 

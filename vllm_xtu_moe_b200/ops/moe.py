@@ -156,11 +156,22 @@ def fused_moe(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, experts
     N.call("xtu_moe_permute", ids.data_ptr(), weights.data_ptr(), T, K, lo, lo + E, ws.counts.data_ptr(),
            ws.seg.data_ptr(), ws.cursor.data_ptr(), ws.perm_slot.data_ptr(), ws.perm_w.data_ptr(), x.data_ptr(), H,
            x.stride(0), ws.xp.data_ptr(), s)
+    I = experts.inter
+    if T <= G.GEMV_MAX_M and experts.interleaved:
+        # decode: weight-streaming grouped GEMV (gate/up + SwiGLU, down + weight + scatter)
+        N.call("xtu_moe_gemv", experts.w13.data_ptr(), N.ptr(experts.s13 if experts.fmt == "fp8" else None),
+               experts.w2.data_ptr(), N.ptr(experts.s2 if experts.fmt == "fp8" else None),
+               int(experts.fmt == "fp8"), E, H, I, ws.xp.data_ptr(), ws.seg.data_ptr(), ws.perm_slot.data_ptr(),
+               ws.perm_w.data_ptr(), ws.h.data_ptr(), ws.slots.data_ptr(), T, float(act_limit), float(act_alpha),
+               float(act_beta), s)
+        y = out if out is not None else torch.empty(T, H, dtype=torch.bfloat16, device=x.device)
+        N.call("xtu_moe_combine", ws.slots.data_ptr(), ids.data_ptr(), T, K, H, lo, lo + E, N.ptr(shared),
+               N.ptr(extra), y.data_ptr(), None, s)
+        return y
     tiles = G.build_mtiles(ws.seg, n, ws.tiles, ws.ntiles)
     xp = ws.xp[:n]
     ws_scale13 = experts.s13 if experts.fmt == "fp8" else None
     ws_scale2 = experts.s2 if experts.fmt == "fp8" else None
-    I = experts.inter
     if experts.interleaved:
         G.grouped_gemm(xp, experts.w13, ws.seg, w_scale=ws_scale13, epilogue=G.EPI_SWIGLU, out=ws.h[:n],
                        act_limit=act_limit, act_alpha=act_alpha, act_beta=act_beta, tiles=tiles)
@@ -176,6 +187,27 @@ def fused_moe(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, experts
     y = out if out is not None else torch.empty(T, H, dtype=torch.bfloat16, device=x.device)
     N.call("xtu_moe_combine", ws.slots.data_ptr(), ids.data_ptr(), T, K, H, lo, lo + E, N.ptr(shared),
            N.ptr(extra), y.data_ptr(), None, s)
+    return y
+
+
+def dense_swiglu_gemv(x: torch.Tensor, w13: torch.Tensor, s13, w2: torch.Tensor, s2, limit: float,
+                      cache: dict) -> torch.Tensor:
+    """Decode-size SwiGLU MLP (gate/up interleaved in 128-row blocks) as a one-expert grouped GEMV."""
+    T, H = x.shape
+    I = w13.shape[0] // 2
+    key = ("gemv", x.device, T, I)
+    st = cache.get(key)
+    if st is None:
+        d = x.device
+        st = dict(seg=torch.tensor([0, T], dtype=torch.int32, device=d),
+                  slot=torch.arange(T, dtype=torch.int32, device=d),
+                  w=torch.ones(T, dtype=torch.float32, device=d),
+                  h=torch.empty(T, I, dtype=torch.bfloat16, device=d))
+        cache[key] = st
+    y = torch.empty(T, w2.shape[0], dtype=torch.bfloat16, device=x.device)
+    N.call("xtu_moe_gemv", w13.data_ptr(), N.ptr(s13), w2.data_ptr(), N.ptr(s2), int(s13 is not None), 1, H, I,
+           x.data_ptr(), st["seg"].data_ptr(), st["slot"].data_ptr(), st["w"].data_ptr(), st["h"].data_ptr(),
+           y.data_ptr(), T, float(limit), 1.0, 0.0, N.stream_ptr(x.device))
     return y
 
 
