@@ -1,0 +1,139 @@
+// AVX-512 (F/BW/VL + BF16/VNNI/VBMI) micro-kernels of the CPU expert engine.
+// Compiled with those ISA flags; the engine calls them only after checking CPUID.
+#include <immintrin.h>
+
+#include <cmath>
+#include <cstring>
+
+#include "moe_kernels.hpp"
+
+namespace xtu_cpu {
+
+namespace {
+
+const float kE2M1[16] = {0.f, 0.5f, 1.f, 1.5f, 2.f, 3.f, 4.f, 6.f, -0.f, -0.5f, -1.f, -1.5f, -2.f, -3.f, -4.f, -6.f};
+
+inline __m512 nibbles16(const uint8_t* p) {
+  // 8 bytes -> 16 nibble indices in k order (low nibble = even k)
+  uint64_t v8;
+  std::memcpy(&v8, p, 8);
+  const __m512i bytes = _mm512_cvtepu8_epi32(_mm_cvtsi64_si128((long long)v8));
+  const __m512i idx = _mm512_set_epi32(7, 7, 6, 6, 5, 5, 4, 4, 3, 3, 2, 2, 1, 1, 0, 0);
+  const __m512i sh = _mm512_set_epi32(4, 0, 4, 0, 4, 0, 4, 0, 4, 0, 4, 0, 4, 0, 4, 0);
+  const __m512i nib = _mm512_and_si512(_mm512_srlv_epi32(_mm512_permutexvar_epi32(idx, bytes), sh),
+                                       _mm512_set1_epi32(0xF));
+  return _mm512_permutexvar_ps(nib, _mm512_loadu_ps(kE2M1));
+}
+
+// 16 weights of row r starting at k (k % 16 == 0), decoded to fp32
+inline __m512 decode16(const DotArgs& a, const RowRef& r, int k) {
+  switch (a.fmt) {
+    case FMT_BF16: {
+      const __m256i v = _mm256_loadu_si256(reinterpret_cast<const __m256i*>(r.w + 2 * (size_t)k));
+      return _mm512_castsi512_ps(_mm512_slli_epi32(_mm512_cvtepu16_epi32(v), 16));
+    }
+    case FMT_FP8: {
+      // e4m3 bits -> fp32 bits (sign | magnitude << 20) is the value * 2^-120 exactly,
+      // subnormals included; the 2^120 is folded into the block scale
+      const __m512i b = _mm512_cvtepu8_epi32(_mm_loadu_si128(reinterpret_cast<const __m128i*>(r.w + k)));
+      const __m512i sign = _mm512_slli_epi32(_mm512_and_si512(b, _mm512_set1_epi32(0x80)), 24);
+      const __m512i mag = _mm512_slli_epi32(_mm512_and_si512(b, _mm512_set1_epi32(0x7F)), 20);
+      const float sc = reinterpret_cast<const float*>(r.s)[k >> 7] * 0x1p120f;
+      return _mm512_mul_ps(_mm512_castsi512_ps(_mm512_or_si512(sign, mag)), _mm512_set1_ps(sc));
+    }
+    case FMT_MXFP4: {
+      const float sc = std::ldexp(1.f, (int)r.s[k >> 5] - 127);
+      return _mm512_mul_ps(nibbles16(r.w + (k >> 1)), _mm512_set1_ps(sc));
+    }
+    default: {  // FMT_NVFP4
+      const float sc = e4m3_to_f32(r.s[k >> 4]) * a.gscale;
+      return _mm512_mul_ps(nibbles16(r.w + (k >> 1)), _mm512_set1_ps(sc));
+    }
+  }
+}
+
+template <int R, int T>
+void dot_rt(const DotArgs& a, const RowRef* rows, const float* X, int ldx, float* acc) {
+  __m512 c[R][T];
+#pragma GCC unroll 4
+  for (int r = 0; r < R; ++r)
+#pragma GCC unroll 6
+    for (int t = 0; t < T; ++t) c[r][t] = _mm512_setzero_ps();
+  for (int k = 0; k < a.K; k += 16) {
+    __m512 w[R];
+#pragma GCC unroll 4
+    for (int r = 0; r < R; ++r) w[r] = decode16(a, rows[r], k);
+#pragma GCC unroll 6
+    for (int t = 0; t < T; ++t) {
+      const __m512 xv = _mm512_loadu_ps(X + (size_t)t * ldx + k);
+#pragma GCC unroll 4
+      for (int r = 0; r < R; ++r) c[r][t] = _mm512_fmadd_ps(w[r], xv, c[r][t]);
+    }
+  }
+  for (int r = 0; r < R; ++r)
+    for (int t = 0; t < T; ++t) acc[r * T + t] = _mm512_reduce_add_ps(c[r][t]);
+}
+
+template <int R>
+void dot_r(const DotArgs& a, const RowRef* rows, const float* X, int ldx, int T, float* acc) {
+  switch (T) {
+    case 1: dot_rt<R, 1>(a, rows, X, ldx, acc); break;
+    case 2: dot_rt<R, 2>(a, rows, X, ldx, acc); break;
+    case 3: dot_rt<R, 3>(a, rows, X, ldx, acc); break;
+    case 4: dot_rt<R, 4>(a, rows, X, ldx, acc); break;
+    case 5: dot_rt<R, 5>(a, rows, X, ldx, acc); break;
+    default: dot_rt<R, 6>(a, rows, X, ldx, acc); break;
+  }
+}
+
+// ---- W4A8 ----
+const int8_t kW4[16] = {0, 1, 2, 3, 4, 6, 8, 12, 0, -1, -2, -3, -4, -6, -8, -12};   // 2 * e2m1
+
+inline __m512i w4_64(const uint8_t* p) {
+  // 32 bytes of nibbles -> 64 s8 values (2*fp4) in k order
+  const __m512i v16 = _mm512_cvtepu8_epi16(_mm256_loadu_si256(reinterpret_cast<const __m256i*>(p)));
+  const __m512i lo = _mm512_and_si512(v16, _mm512_set1_epi16(0x0F));
+  const __m512i hi = _mm512_slli_epi16(_mm512_and_si512(_mm512_srli_epi16(v16, 4), _mm512_set1_epi16(0x0F)), 8);
+  const __m512i idx = _mm512_or_si512(lo, hi);
+  const __m128i t = _mm_loadu_si128(reinterpret_cast<const __m128i*>(kW4));
+  return _mm512_shuffle_epi8(_mm512_broadcast_i32x4(t), idx);
+}
+
+}  // namespace
+
+void dot_rows_avx512(const DotArgs& a, const RowRef* rows, int R, const float* X, int ldx, int T, float* acc) {
+  switch (R) {
+    case 1: dot_r<1>(a, rows, X, ldx, T, acc); break;
+    case 2: dot_r<2>(a, rows, X, ldx, T, acc); break;
+    case 3: dot_r<3>(a, rows, X, ldx, T, acc); break;
+    default: dot_r<4>(a, rows, X, ldx, T, acc); break;
+  }
+}
+
+void dot_rows_w4a8_avx512(const RowRef* rows, int R, int K, const int8_t* xq, const int8_t* xe, int ldq, int T,
+                          float* acc) {
+  const __m512i ones = _mm512_set1_epi8(1);
+  const __m512i bias = _mm512_set1_epi8((char)0x80);
+  for (int r = 0; r < R; ++r) {
+    __m512 c[6];
+    for (int t = 0; t < T; ++t) c[t] = _mm512_setzero_ps();
+    for (int k = 0; k < K; k += 64) {
+      const __m512i w4 = w4_64(rows[r].w + (k >> 1));
+      const __m512i sw = _mm512_dpbusd_epi32(_mm512_setzero_si512(), ones, w4);   // sum of w4 per lane
+      const int b0 = rows[r].s[k >> 5], b1 = rows[r].s[(k >> 5) + 1];
+      for (int t = 0; t < T; ++t) {
+        const int8_t* q = xq + (size_t)t * ldq + k;
+        const __m512i au8 = _mm512_xor_si512(_mm512_loadu_si512(q), bias);
+        const __m512i d = _mm512_dpbusd_epi32(_mm512_setzero_si512(), au8, w4);
+        const __m512i sg = _mm512_sub_epi32(d, _mm512_slli_epi32(sw, 7));      // exact sum a8 * w4 per lane
+        const int e0 = xe[(size_t)t * (ldq / 32) + (k >> 5)], e1 = xe[(size_t)t * (ldq / 32) + (k >> 5) + 1];
+        const __m512 s = _mm512_mask_mov_ps(_mm512_set1_ps(std::ldexp(1.f, e0 + b0 - 128)), (__mmask16)0xFF00,
+                                            _mm512_set1_ps(std::ldexp(1.f, e1 + b1 - 128)));
+        c[t] = _mm512_fmadd_ps(_mm512_cvtepi32_ps(sg), s, c[t]);
+      }
+    }
+    for (int t = 0; t < T; ++t) acc[r * T + t] = _mm512_reduce_add_ps(c[t]);
+  }
+}
+
+}  // namespace xtu_cpu

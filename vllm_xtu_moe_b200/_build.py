@@ -50,6 +50,9 @@ def _compile(cmd: list[str]) -> tuple[list[str], int, str]:
     return cmd, p.returncode, p.stdout + p.stderr
 
 
+AVX512_FLAGS = ["-mavx512f", "-mavx512bw", "-mavx512vl", "-mavx512bf16", "-mavx512vnni", "-mavx512vbmi", "-mfma"]
+
+
 def _build_lib(name: str, sources: list[Path], compiler: str, flags: list[str], link_flags: list[str],
                include: list[Path], jobs: int, verbose: bool) -> Path:
     OBJDIR.mkdir(parents=True, exist_ok=True)
@@ -60,7 +63,8 @@ def _build_lib(name: str, sources: list[Path], compiler: str, flags: list[str], 
         obj = OBJDIR / (src.parent.name + "_" + src.stem + ".o")
         objs.append(obj)
         if not obj.exists() or obj.stat().st_mtime < max(src.stat().st_mtime, hdr_time):
-            cmd = [compiler, *flags, *[f"-I{d}" for d in include], "-c", str(src), "-o", str(obj)]
+            extra = AVX512_FLAGS if "avx512" in src.name else []   # ISA kernels: picked at run time
+            cmd = [compiler, *flags, *extra, *[f"-I{d}" for d in include], "-c", str(src), "-o", str(obj)]
             todo.append(cmd)
     if todo:
         with cf.ThreadPoolExecutor(max_workers=jobs) as ex:
