@@ -120,3 +120,30 @@ void xtu_cpu_bridge_destroy(void* bridge) {
 }
 
 }  // extern "C"
+
+extern "C" {
+
+// Page-lock host memory (e.g. the engine's weight shards) for full-speed DMA.
+int xtu_host_register(void* p, long long bytes) {
+  if (!p || bytes <= 0) return 0;
+  cudaError_t e = cudaHostRegister(p, (size_t)bytes, cudaHostRegisterPortable);
+  return e == cudaSuccess ? 0 : -(int)e;
+}
+
+int xtu_host_unregister(void* p) {
+  if (!p) return 0;
+  return cudaHostUnregister(p) == cudaSuccess ? 0 : -1;
+}
+
+}  // extern "C"
+
+extern "C" {
+
+// one host->device copy on `s` (used by the prefill ring and the pool swap-in)
+int xtu_memcpy_h2d_async(void* dst, const void* src, long long bytes, cudaStream_t s) {
+  if (bytes <= 0) return 0;
+  cudaError_t e = cudaMemcpyAsync(dst, src, (size_t)bytes, cudaMemcpyHostToDevice, s);
+  return e == cudaSuccess ? 0 : -(int)e;
+}
+
+}  // extern "C"

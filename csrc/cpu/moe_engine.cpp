@@ -171,12 +171,15 @@ class Engine {
     const int H = c.H, I = c.I, E = c.E;
     const size_t rb13 = row_bytes(c.fmt, H), sb13 = scale_bytes(c.fmt, H);
     const size_t rb2 = row_bytes(c.fmt, I), sb2 = scale_bytes(c.fmt, I);
-    // split columns / rows over nodes in 16-aligned (128 for fp8 block scales: scales are
-    // kept per row here, so any 16-aligned split works)
+    // Split over nodes: gate/up columns in whole 128-column blocks, down rows 16-aligned.
+    // Each node's gate/up rows are stored in the GPU kernels' interleaved order -- per
+    // 128-column block, 128 gate rows then the matching 128 up rows -- so a node's slice of
+    // an expert is one contiguous range that the prefill ring can DMA as is.
+    const int nb = I / 128;
     for (int n = 0; n < nn; ++n) {
       NodeShard& s = shards_[n];
-      s.j0 = (int)((long)I * n / nn) & ~15;
-      s.j1 = n + 1 == nn ? I : (int)((long)I * (n + 1) / nn) & ~15;
+      s.j0 = (int)((long)nb * n / nn) * 128;
+      s.j1 = (int)((long)nb * (n + 1) / nn) * 128;
       s.h0 = (int)((long)H * n / nn) & ~15;
       s.h1 = n + 1 == nn ? H : (int)((long)H * (n + 1) / nn) & ~15;
       const int jn = s.j1 - s.j0, hn = s.h1 - s.h0;
@@ -197,7 +200,7 @@ class Engine {
       for (int half = 0; half < 2; ++half)
         for (int j = 0; j < jn; ++j) {
           const int src_row = half * I + s.j0 + j;      // checkpoint: gate rows then up rows
-          const size_t dst = ((size_t)e * 2 + half) * jn + j;
+          const size_t dst = w13_row(e, jn, j, half);
           std::memcpy(s.w13 + dst * rb13, w13 + ((size_t)e * 2 * I + src_row) * rb13, rb13);
           copy_scales(s.s13 + dst * sb13, s13, e, 2 * I, H, src_row);
         }
@@ -219,6 +222,14 @@ class Engine {
       free_on_node(s.s2, s.s2_bytes);
     }
   }
+
+  // row index inside a node shard: [e][j/128][half][j%128]
+  static size_t w13_row(int e, int jn, int j, int half) {
+    return ((size_t)e * (jn / 128) + j / 128) * 256 + half * 128 + (j % 128);
+  }
+
+  const NodeShard& shard(int n) const { return shards_[n]; }
+  int fmt() const { return cfg_.fmt; }
 
   // scales of checkpoint row `row` (of a [E][rows][K] matrix) -> this engine's per-row layout
   void copy_scales(uint8_t* dst, const uint8_t* src, int e, int rows, int K, int row) const {
@@ -312,7 +323,7 @@ class Engine {
           const int nj = std::min(2, jt1 - j);
           RowRef rows[4];
           for (int u = 0; u < nj; ++u) {
-            const size_t g = ((size_t)e * 2 + 0) * jn + j + u, up = ((size_t)e * 2 + 1) * jn + j + u;
+            const size_t g = w13_row(e, jn, j + u, 0), up = w13_row(e, jn, j + u, 1);
             rows[2 * u] = {s.w13 + g * rb, s.s13 + g * sb};
             rows[2 * u + 1] = {s.w13 + up * rb, s.s13 + up * sb};
           }
@@ -390,7 +401,7 @@ extern "C" {
 void* xtu_cpu_engine_create(int fmt, int E, int H, int I, const void* w13, const void* s13, const void* w2,
                             const void* s2, const float* gs13, const float* gs2, int threads, float limit,
                             float alpha, float beta, int int8_mode, int int8_min_tokens, int deadline_ms) {
-  if (H % 16 || I % 16) return nullptr;
+  if (H % 16 || I % 128) return nullptr;
   EngineCfg c{fmt, E, H, I, threads, limit, alpha, beta, int8_mode, int8_min_tokens, deadline_ms};
   try {
     return new Engine(c, (const uint8_t*)w13, (const uint8_t*)s13, (const uint8_t*)w2, (const uint8_t*)s2, gs13, gs2);
@@ -419,6 +430,19 @@ int xtu_cpu_engine_info(void* eng, long long* info) {
 }
 
 void xtu_cpu_engine_destroy(void* eng) { delete static_cast<Engine*>(eng); }
+
+// Shard n of the engine (for DMA): ptrs = {w13, s13, w2, s2}; ranges = {j0, j1, h0, h1};
+// bytes = {w13, s13, w2, s2}.  w13 rows: [E][(j1-j0)/128][2][128][row]; w2 rows: [E][h1-h0][row].
+int xtu_cpu_engine_shard(void* eng, int n, void** ptrs, int* ranges, long long* bytes) {
+  Engine* e = static_cast<Engine*>(eng);
+  if (!e || n < 0 || n >= e->nodes()) return -1;
+  const NodeShard& s = e->shard(n);
+  ptrs[0] = s.w13; ptrs[1] = s.s13; ptrs[2] = s.w2; ptrs[3] = s.s2;
+  ranges[0] = s.j0; ranges[1] = s.j1; ranges[2] = s.h0; ranges[3] = s.h1;
+  bytes[0] = (long long)s.w13_bytes; bytes[1] = (long long)s.s13_bytes;
+  bytes[2] = (long long)s.w2_bytes; bytes[3] = (long long)s.s2_bytes;
+  return 0;
+}
 
 // exact decoders exposed for conformance tests
 float xtu_cpu_e4m3_to_f32(int b) { return e4m3_to_f32((uint8_t)b); }

@@ -429,6 +429,29 @@ __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ slots, cons
 }
 
 // ---------------------------------------------------------------------------
+// Tier split of routed pairs (W7; replaces the reference's PIN mask kernel,
+// vllm_xiaotu_moe/pin_mask_triton.py:52-72).  slotmap[e - lo] >= 0: expert e is in the
+// GPU pool at that slot; -1: it is served by the CPU tier.  Writes the pool-slot id (or
+// -1) and the CPU expert id (or -1) of every pair, and counts routed hits per expert for
+// the swap policy (device side, graph-capturable).
+// ---------------------------------------------------------------------------
+__global__ void route_split_kernel(const int* __restrict__ ids, int n, int lo, int E, const int* __restrict__ slotmap,
+                                   int* __restrict__ gpu_ids, int* __restrict__ cpu_ids, int* __restrict__ hits) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const int id = ids[i];
+    const int e = id - lo;
+    int g = -1, c = -1;
+    if (e >= 0 && e < E) {
+      const int slot = slotmap[e];
+      if (slot >= 0) g = slot; else c = id;
+      if (hits) atomicAdd(&hits[e], 1);
+    }
+    gpu_ids[i] = g;
+    cpu_ids[i] = c;
+  }
+}
+
+// ---------------------------------------------------------------------------
 // greedy argmax over rows (fp32 or bf16 logits); ties -> lowest index
 // ---------------------------------------------------------------------------
 template <typename T>
@@ -641,6 +664,15 @@ int xtu_argmax(const void* logits, int is_bf16, int T, int V, int stride, int* o
     argmax_kernel<float><<<grid, 512, 0, s>>>((const float*)logits, V, stride, out, out_val, pv, pi);
   if (parts > 1) argmax_final_kernel<<<T, 32, 0, s>>>(pv, pi, parts, out, out_val);
   return rc_last(parts > 1 ? 2 : 1);
+}
+
+int xtu_route_split(const int* ids, int n, int lo, int E, const int* slotmap, int* gpu_ids, int* cpu_ids, int* hits,
+                    cudaStream_t s) {
+  if (n <= 0) return 0;
+  int blocks = (n + 255) / 256;
+  if (blocks > 1024) blocks = 1024;
+  route_split_kernel<<<blocks, 256, 0, s>>>(ids, n, lo, E, slotmap, gpu_ids, cpu_ids, hits);
+  return rc_last();
 }
 
 int xtu_embed(const int* ids, const void* table, int T, int H, int vocab, void* out, cudaStream_t s) {

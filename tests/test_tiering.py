@@ -1,0 +1,282 @@
+"""Expert tiering: swap policy, XTUP tables, planner (CPU); route split, CPU bridge,
+hot-expert pool, prefill ring and the tiered executor against the all-GPU MoE (GPU)."""
+import inspect
+import struct
+
+import pytest
+import torch
+
+from vllm_xtu_moe_b200.models.config import get_preset, scaled_down
+from vllm_xtu_moe_b200.ops import moe as M
+from vllm_xtu_moe_b200.ops.quant import quant_fp8_block
+from vllm_xtu_moe_b200.tiering import planner as PL
+from vllm_xtu_moe_b200.tiering.policy import load_pin_table, plan_swap, save_pin_table, table_from_counts
+
+
+# ----------------------------------------------------------------------------- policy
+def test_plan_swap_evicts_coldest_and_loads_hottest():
+    res = [0, 1, 2, 3]
+    counts = {0: 10, 1: 0, 2: 5, 3: 7, 8: 50, 9: 3}
+    ev, ld = plan_swap(res, counts, 4, maxswap=2)
+    # exact: victims (1:0) then (2:5); candidates 8:50, 9:3 -> 8 replaces 1; 9 (3) is not > 5*1.25
+    assert ev == [1] and ld == [8]
+
+
+def test_plan_swap_hysteresis_and_rate_limit():
+    res = [0, 1, 2, 3, 4, 5, 6, 7]
+    counts = {e: 10 for e in res} | {20: 12, 21: 12, 22: 30, 23: 40, 24: 50}
+    ev, ld = plan_swap(res, counts, 8, hyst=0.25)     # default rate limit: nslots // 4 = 2
+    assert len(ev) == 2 and ld == [24, 23]
+    ev, ld = plan_swap(res, counts, 8, hyst=0.25, maxswap=5)
+    assert ld == [24, 23, 22] and 20 not in ld and 21 not in ld   # 12 is within 25% of 10
+    assert not set(ev) & set(ld)
+
+
+def test_plan_swap_tie_order_and_empty_pool():
+    res = [5, 6, 7, 8]
+    counts = {9: 100}
+    ev, _ = plan_swap(res, counts, 4, maxswap=1)
+    assert ev == [5]                      # oldest resident among ties
+    ev, _ = plan_swap(res, counts, 4, maxswap=1, preserve_oldest=True)
+    assert ev == [8]                      # newest among ties in prefill windows
+    assert plan_swap([], counts, 0) == ([], [])
+    assert plan_swap(res, {}, 4) == ([], [])
+
+
+def test_xtup_round_trip_and_bytes(tmp_path):
+    table = {0: [3, 1, 2], 2: [7]}
+    p = tmp_path / "t.xtup"
+    save_pin_table(p, table, 16)
+    raw = p.read_bytes()
+    assert raw[:4] == b"XTUP"
+    assert struct.unpack_from("<4sIIII", raw) == (b"XTUP", 1, 3, 16, 4)
+    assert struct.unpack_from("<HH", raw, 20) == (0, 3)
+    assert load_pin_table(p) == table
+    p.write_bytes(b"NOPE" + raw[4:])
+    with pytest.raises(ValueError):
+        load_pin_table(p)
+
+
+def test_table_from_counts():
+    t = table_from_counts({0: [0, 5, 3, 0], 1: [1, 1, 0, 9]}, 2)
+    assert t == {0: [1, 2], 1: [3, 0]}
+
+
+def test_pool_flips_table_last_and_never_frees():
+    """The slot map is updated only after the copies have completed, and slots are never reallocated."""
+    from vllm_xtu_moe_b200.tiering import pool
+    src = inspect.getsource(pool.LayerPool.maybe_adapt)
+    assert src.index("self.side.synchronize()") < src.index("self.slotmap[e] = s")
+    assert src.index("self.slotmap[v] = -1") < src.index("self._load(e, s)")
+    assert "torch.empty" not in src and "del " not in src
+
+
+# ----------------------------------------------------------------------------- planner
+def test_planner_priorities():
+    air = get_preset("glm-4.5-air")
+    p = PL.plan(air, 178.0)
+    moe = [i for i in range(air.num_layers) if air.is_moe_layer(i)]
+    assert p.resident_layers == moe and p.free >= 0 and p.staging > 0
+    ds = get_preset("deepseek-v3")
+    p = PL.plan(ds, 178.0, max_model_len=32768)
+    moe = [i for i in range(ds.num_layers) if ds.is_moe_layer(i)]
+    assert 0 < len(p.resident_layers) < len(moe)
+    mid = moe[len(moe) // 2]
+    assert mid in p.resident_layers
+    used = p.non_expert + p.kv + p.staging + p.drafter + len(p.resident_layers) * ds.num_experts * PL.expert_bytes(ds)
+    used += p.pool_per_layer * len(p.pool_layers) * PL.expert_bytes(ds)
+    assert used + p.free + 4 * PL.GiB == p.gpu_bytes
+    env = p.to_env(48, 2)
+    assert env["XIAOTU_GPF_STAGE_TILE_E"] == "48" and "XIAOTU_MOE_GPU_RESIDENT_LAYERS" in env
+    small = PL.plan(ds, 20.0)
+    assert small.notes and not small.resident_layers
+
+
+def test_layer_ranges():
+    assert PL._ranges([1, 2, 3, 7, 9, 10]) == "1-3,7,9-10"
+    from vllm_xtu_moe_b200.config import parse_layer_list
+    assert parse_layer_list("1-3,7,9-10") == {1, 2, 3, 7, 9, 10}
+
+
+# ----------------------------------------------------------------------------- CPU model through the CPU tier
+def _mini(fmt="fp8"):
+    return scaled_down(get_preset("glm-4.5-air"), layers=2, hidden=512, experts=16).replace(
+        num_heads=8, num_kv_heads=2, moe_intermediate=256, shared_intermediate=256, dense_intermediate=512,
+        expert_fmt=fmt, dense_fmt="bf16", num_mtp_layers=0)
+
+
+def test_cpu_tier_model_matches_resident():
+    from vllm_xtu_moe_b200.models.model import build_model
+    from vllm_xtu_moe_b200.tiering.executor import TieredExperts
+    cfg = _mini()
+    ref = build_model(cfg, device="cpu", seed=2)
+    tier = TieredExperts(cfg, device="cpu", resident_layers=set())
+    m = build_model(cfg, device="cpu", seed=2, expert_sink=tier.expert_sink)
+    tier.attach(m)
+    blk_r, blk_t = ref.layers[1].mlp, m.layers[1].mlp
+    assert blk_t.experts is None and blk_t.executor is not None
+    x = (torch.randn(9, cfg.hidden_size) * 0.5).to(torch.bfloat16)
+    a, b = blk_r(x).float(), blk_t(x).float()
+    assert (a - b).abs().max().item() <= 2e-2 * a.abs().max().item() + 1e-3
+    tier.shutdown()
+
+
+# ----------------------------------------------------------------------------- GPU
+def _raw_gpu(fmt, E, H, I, seed):
+    g = torch.Generator().manual_seed(seed)
+    w13 = torch.randn(E, 2 * I, H, generator=g) / H ** 0.5
+    w2 = torch.randn(E, H, I, generator=g) / I ** 0.5
+    if fmt == "bf16":
+        return dict(fmt=fmt, w13=w13.to(torch.bfloat16), w2=w2.to(torch.bfloat16))
+    q13, s13 = quant_fp8_block(w13)
+    q2, s2 = quant_fp8_block(w2)
+    return dict(fmt=fmt, w13=q13, w2=q2, s13=s13, s2=s2)
+
+
+def _routes(T, E, K, seed, skew=False):
+    g = torch.Generator().manual_seed(seed)
+    if skew:
+        p = torch.tensor([1.0 / (1 + e) ** 1.2 for e in range(E)])
+        ids = torch.stack([torch.multinomial(p, K, generator=g) for _ in range(T)])
+    else:
+        ids = torch.stack([torch.randperm(E, generator=g)[:K] for _ in range(T)])
+    w = torch.rand(T, K, generator=g)
+    return ids.int(), (w / w.sum(1, keepdim=True)).float()
+
+
+@pytest.mark.gpu
+def test_route_split_matches_torch():
+    E, T, K = 64, 37, 8
+    ids, _ = _routes(T, E, K, 1)
+    slotmap = torch.full((E,), -1, dtype=torch.int32)
+    for s, e in enumerate([3, 9, 11, 40, 63]):
+        slotmap[e] = s
+    d = "cuda"
+    gi, ci = torch.empty(T, K, dtype=torch.int32, device=d), torch.empty(T, K, dtype=torch.int32, device=d)
+    hits = torch.zeros(E, dtype=torch.int32, device=d)
+    M.route_split(ids.to(d), slotmap.to(d), 0, gi, ci, hits)
+    M.route_split(ids.to(d), slotmap.to(d), 0, gi, ci, hits)
+    s = slotmap[ids.long()]
+    assert torch.equal(gi.cpu(), torch.where(s >= 0, s, -1))
+    assert torch.equal(ci.cpu(), torch.where(s >= 0, -1, ids))
+    assert torch.equal(hits.cpu(), 2 * torch.bincount(ids.flatten().long(), minlength=E).int())
+
+
+def _executor_case(fmt, pool_experts, T, skew=False, ring=True, min_tokens=64, window=0):
+    from vllm_xtu_moe_b200.config import EngineConfig
+    from vllm_xtu_moe_b200.tiering.executor import TieredExperts
+    E, H, I, K = 32, 512, 256, 4
+    cfg = _mini(fmt).replace(num_experts=E, top_k=K, hidden_size=H, moe_intermediate=I)
+    raw = _raw_gpu(fmt, E, H, I, 5)
+    ec = EngineConfig(stage_tile_e=12, stage_nslots=2, pin_window=window)
+    tier = TieredExperts(cfg, device="cuda", engine_config=ec, resident_layers=set(), pool_experts=pool_experts,
+                         ring=ring, gpu_prefill_min_tokens=min_tokens, max_tokens=1024)
+    assert tier.expert_sink(1, raw) is None
+    res = M.prepare_experts(fmt, raw["w13"].cuda(), raw["w2"].cuda(), raw["s13"].cuda() if "s13" in raw else None,
+                            raw["s2"].cuda() if "s2" in raw else None)
+
+    class Blk:
+        experts = None
+        executor = None
+
+    Blk.cfg = cfg
+    blk = Blk()
+
+    class Mdl:
+        layers = [type("L", (), {"mlp": blk})()]
+        mtp = []
+
+    tier.attach(Mdl)
+    ids, w = _routes(T, E, K, 7, skew)
+    x = (torch.randn(T, H, generator=torch.Generator().manual_seed(3)) * 0.5).to(torch.bfloat16).cuda()
+    sh = (torch.randn(T, H) * 0.1).to(torch.bfloat16).cuda()
+    ids, w = ids.cuda(), w.cuda()
+    ref = M.fused_moe(x, ids, w, res, shared=sh).float()
+    return tier, blk, x, ids, w, sh, ref
+
+
+def _close(a, b, tol=2e-2):
+    err = (a.float() - b.float()).abs().max().item()
+    return err <= tol * b.float().abs().max().item() + 1e-3, err
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("fmt", ["bf16", "fp8"])
+@pytest.mark.parametrize("T", [1, 5, 40])
+def test_hybrid_pool_plus_cpu_matches_gpu(fmt, T):
+    tier, blk, x, ids, w, sh, ref = _executor_case(fmt, {1: [0, 3, 5, 7, 11, 20, 31]}, T, ring=False)
+    y = blk.executor(blk, x, ids, w, sh)
+    torch.cuda.synchronize()
+    ok, err = _close(y, ref)
+    assert ok, err
+    assert tier.stats()["hybrid"] == 1
+    hits = blk.executor.pool.hits.cpu()
+    assert hits.sum().item() == ids.numel()
+    tier.shutdown()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("fmt", ["bf16", "fp8"])
+def test_cpu_only_bridge_matches_gpu(fmt):
+    tier, blk, x, ids, w, sh, ref = _executor_case(fmt, {}, 6, ring=False)
+    y = blk.executor(blk, x, ids, w, sh)
+    torch.cuda.synchronize()
+    ok, err = _close(y, ref)
+    assert ok, err
+    assert tier.stats()["cpu"] == 1 and blk.executor.bridge.stats()["runs"] == 1
+    tier.shutdown()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("fmt", ["bf16", "fp8"])
+def test_prefill_ring_matches_gpu(fmt):
+    tier, blk, x, ids, w, sh, ref = _executor_case(fmt, {}, 300, ring=True, min_tokens=64)
+    y = blk.executor(blk, x, ids, w, sh)
+    torch.cuda.synchronize()
+    ok, err = _close(y, ref)
+    assert ok, err
+    assert tier.stats()["ring"] == 1
+    assert tier.ring.copied_bytes == 32 * tier.executors[0].host.expert_bytes()
+    tier.shutdown()
+
+
+@pytest.mark.gpu
+def test_pool_adapts_to_hot_experts_and_stays_exact():
+    tier, blk, x, ids, w, sh, ref = _executor_case("fp8", {1: [20, 21, 22, 23]}, 16, skew=True, ring=False,
+                                                   window=2)
+    pool = blk.executor.pool
+    for step in range(6):
+        y = blk.executor(blk, x, ids, w, sh)
+        tier.step_done()
+        torch.cuda.synchronize()
+        ok, err = _close(y, ref)
+        assert ok, (step, err)
+    assert pool.swaps_in > 0
+    sm = pool.slotmap.cpu()
+    for s, e in enumerate(pool.expert_of):
+        assert sm[e].item() == s
+    assert (sm >= 0).sum().item() == 4
+    assert 0 in pool.expert_of            # the hottest expert of the skewed routing moved in
+    tier.shutdown()
+
+
+@pytest.mark.gpu
+def test_hybrid_path_graph_replay_matches_eager():
+    tier, blk, x, ids, w, sh, ref = _executor_case("fp8", {1: [0, 1, 2, 3, 4, 5]}, 4, ring=False)
+    eager = blk.executor(blk, x, ids, w, sh).clone()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        blk.executor(blk, x, ids, w, sh)
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        out = blk.executor(blk, x, ids, w, sh)
+    for _ in range(3):
+        out.zero_()
+        g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, eager)
+    assert blk.executor.bridge.stats()["runs"] >= 5
+    del g
+    tier.shutdown()

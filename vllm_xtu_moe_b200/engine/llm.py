@@ -82,6 +82,8 @@ class LLM:
             done = self.spec.decode_step(plan, self.scheduler)
             self.stats["decode_time"] += time.perf_counter() - t0
             self.stats["steps"] += 1
+            if self.tiering is not None:
+                self.tiering.step_done()
             return done
         tok, extra = self.runner.execute(plan)
         toks = tok.tolist() if tok is not None else []
@@ -121,6 +123,8 @@ class LLM:
                 self.spec.prefill_mtp(plan, extra)
             self.stats["prefill_time"] += now - t0
         self.stats["steps"] += 1
+        if self.tiering is not None:
+            self.tiering.step_done()
         return done
 
     def generate(self, prompts: list[list[int]], params: SamplingParams | list[SamplingParams] | None = None):

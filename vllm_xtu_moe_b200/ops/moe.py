@@ -127,6 +127,56 @@ def moe_ref(x, ids, weights, experts: ExpertWeights, lo=0, hi=None, act_limit=0.
     return out
 
 
+def moe_experts_partial(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, experts: ExpertWeights,
+                        ws: MoEWorkspace, *, lo: int = 0, act_limit: float = 0.0, act_alpha: float = 1.0,
+                        act_beta: float = 0.0) -> None:
+    """Expert GEMMs for the pairs whose id is in [lo, lo + E): each such pair's weighted
+    output row lands in ws.slots[pair].  Other pairs are untouched (other tiles / tiers)."""
+    T, H = x.shape
+    K = ids.shape[1]
+    E = experts.num_experts
+    s = N.stream_ptr(x.device)
+    n = T * K
+    N.call("xtu_moe_permute", ids.data_ptr(), weights.data_ptr(), T, K, lo, lo + E, ws.counts.data_ptr(),
+           ws.seg.data_ptr(), ws.cursor.data_ptr(), ws.perm_slot.data_ptr(), ws.perm_w.data_ptr(), x.data_ptr(), H,
+           x.stride(0), ws.xp.data_ptr(), s)
+    I = experts.inter
+    fp8 = experts.fmt == "fp8"
+    if T <= G.GEMV_MAX_M and experts.interleaved:
+        # decode: weight-streaming grouped GEMV (gate/up + SwiGLU, down + weight + scatter)
+        N.call("xtu_moe_gemv", experts.w13.data_ptr(), N.ptr(experts.s13 if fp8 else None),
+               experts.w2.data_ptr(), N.ptr(experts.s2 if fp8 else None), int(fp8), E, H, I, ws.xp.data_ptr(),
+               ws.seg.data_ptr(), ws.perm_slot.data_ptr(), ws.perm_w.data_ptr(), ws.h.data_ptr(),
+               ws.slots.data_ptr(), T, float(act_limit), float(act_alpha), float(act_beta), s)
+        return
+    tiles = G.build_mtiles(ws.seg, n, ws.tiles, ws.ntiles)
+    xp = ws.xp[:n]
+    sc13 = experts.s13 if fp8 else None
+    sc2 = experts.s2 if fp8 else None
+    if experts.interleaved:
+        G.grouped_gemm(xp, experts.w13, ws.seg, w_scale=sc13, epilogue=G.EPI_SWIGLU, out=ws.h[:n],
+                       act_limit=act_limit, act_alpha=act_alpha, act_beta=act_beta, tiles=tiles)
+    else:
+        if ws.h13 is None or ws.h13.shape[0] < n:
+            ws.h13 = torch.empty(ws.max_tokens * K, 2 * I, dtype=torch.bfloat16, device=x.device)
+        G.grouped_gemm(xp, experts.w13, ws.seg, w_scale=sc13, epilogue=G.EPI_BF16, out=ws.h13[:n], tiles=tiles)
+        N.call("xtu_silu_mul", ws.h13.data_ptr(), n, I, float(act_limit), float(act_alpha), float(act_beta),
+               ws.h.data_ptr(), s)
+    G.grouped_gemm(ws.h[:n], experts.w2, ws.seg, w_scale=sc2, epilogue=G.EPI_BF16, out=ws.slots[:n],
+                   row_scale=ws.perm_w, row_dest=ws.perm_slot, tiles=tiles)
+
+
+def moe_combine(ws: MoEWorkspace, ids: torch.Tensor, lo: int, hi: int, *, shared: torch.Tensor | None = None,
+                extra: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """out[t] = sum of the slot rows of t's pairs with id in [lo, hi) (+ shared + extra fp32)."""
+    T, K = ids.shape
+    H = ws.hidden
+    y = out if out is not None else torch.empty(T, H, dtype=torch.bfloat16, device=ids.device)
+    N.call("xtu_moe_combine", ws.slots.data_ptr(), ids.data_ptr(), T, K, H, lo, hi, N.ptr(shared), N.ptr(extra),
+           y.data_ptr(), None, N.stream_ptr(ids.device))
+    return y
+
+
 def fused_moe(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, experts: ExpertWeights,
               ws: MoEWorkspace | None = None, *, lo: int = 0, shared: torch.Tensor | None = None,
               extra: torch.Tensor | None = None, act_limit: float = 0.0, act_alpha: float = 1.0,
@@ -151,43 +201,17 @@ def fused_moe(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, experts
     if ws is None or ws.max_tokens < T:
         ws = MoEWorkspace(T, K, E, H, experts.inter, x.device)
     assert x.is_contiguous() and ids.is_contiguous() and weights.is_contiguous()
-    s = N.stream_ptr(x.device)
-    n = T * K
-    N.call("xtu_moe_permute", ids.data_ptr(), weights.data_ptr(), T, K, lo, lo + E, ws.counts.data_ptr(),
-           ws.seg.data_ptr(), ws.cursor.data_ptr(), ws.perm_slot.data_ptr(), ws.perm_w.data_ptr(), x.data_ptr(), H,
-           x.stride(0), ws.xp.data_ptr(), s)
-    I = experts.inter
-    if T <= G.GEMV_MAX_M and experts.interleaved:
-        # decode: weight-streaming grouped GEMV (gate/up + SwiGLU, down + weight + scatter)
-        N.call("xtu_moe_gemv", experts.w13.data_ptr(), N.ptr(experts.s13 if experts.fmt == "fp8" else None),
-               experts.w2.data_ptr(), N.ptr(experts.s2 if experts.fmt == "fp8" else None),
-               int(experts.fmt == "fp8"), E, H, I, ws.xp.data_ptr(), ws.seg.data_ptr(), ws.perm_slot.data_ptr(),
-               ws.perm_w.data_ptr(), ws.h.data_ptr(), ws.slots.data_ptr(), T, float(act_limit), float(act_alpha),
-               float(act_beta), s)
-        y = out if out is not None else torch.empty(T, H, dtype=torch.bfloat16, device=x.device)
-        N.call("xtu_moe_combine", ws.slots.data_ptr(), ids.data_ptr(), T, K, H, lo, lo + E, N.ptr(shared),
-               N.ptr(extra), y.data_ptr(), None, s)
-        return y
-    tiles = G.build_mtiles(ws.seg, n, ws.tiles, ws.ntiles)
-    xp = ws.xp[:n]
-    ws_scale13 = experts.s13 if experts.fmt == "fp8" else None
-    ws_scale2 = experts.s2 if experts.fmt == "fp8" else None
-    if experts.interleaved:
-        G.grouped_gemm(xp, experts.w13, ws.seg, w_scale=ws_scale13, epilogue=G.EPI_SWIGLU, out=ws.h[:n],
-                       act_limit=act_limit, act_alpha=act_alpha, act_beta=act_beta, tiles=tiles)
-    else:
-        if ws.h13 is None or ws.h13.shape[0] < n:
-            ws.h13 = torch.empty(ws.max_tokens * K, 2 * I, dtype=torch.bfloat16, device=x.device)
-        G.grouped_gemm(xp, experts.w13, ws.seg, w_scale=ws_scale13, epilogue=G.EPI_BF16, out=ws.h13[:n],
-                       tiles=tiles)
-        N.call("xtu_silu_mul", ws.h13.data_ptr(), n, I, float(act_limit), float(act_alpha), float(act_beta),
-               ws.h.data_ptr(), s)
-    G.grouped_gemm(ws.h[:n], experts.w2, ws.seg, w_scale=ws_scale2, epilogue=G.EPI_BF16, out=ws.slots[:n],
-                   row_scale=ws.perm_w, row_dest=ws.perm_slot, tiles=tiles)
-    y = out if out is not None else torch.empty(T, H, dtype=torch.bfloat16, device=x.device)
-    N.call("xtu_moe_combine", ws.slots.data_ptr(), ids.data_ptr(), T, K, H, lo, lo + E, N.ptr(shared),
-           N.ptr(extra), y.data_ptr(), None, s)
-    return y
+    moe_experts_partial(x, ids, weights, experts, ws, lo=lo, act_limit=act_limit, act_alpha=act_alpha,
+                        act_beta=act_beta)
+    return moe_combine(ws, ids, lo, lo + E, shared=shared, extra=extra, out=out)
+
+
+def route_split(ids: torch.Tensor, slotmap: torch.Tensor, lo: int, gpu_ids: torch.Tensor, cpu_ids: torch.Tensor,
+                hits: torch.Tensor | None = None) -> None:
+    """Pairs -> pool slot id (or -1) and CPU expert id (or -1); counts hits per expert."""
+    n = ids.numel()
+    N.call("xtu_route_split", ids.data_ptr(), n, lo, slotmap.numel(), slotmap.data_ptr(), gpu_ids.data_ptr(),
+           cpu_ids.data_ptr(), N.ptr(hits), N.stream_ptr(ids.device))
 
 
 def dense_swiglu_gemv(x: torch.Tensor, w13: torch.Tensor, s13, w2: torch.Tensor, s2, limit: float,

@@ -1,0 +1,75 @@
+"""Streamed prefill ring: sub-layer expert tiles copied host -> GPU on a copy stream,
+double (or N-) buffered, overlapped with the expert GEMMs of the previous tile.
+
+For a long prefill chunk of a layer whose experts live on the host tier, every
+expert is needed, so they are streamed through ``nslots`` GPU slots of ``tile_e``
+experts each (``XIAOTU_GPF_STAGE_TILE_E``, default 48; ``XIAOTU_GPF_STAGE_NSLOTS``,
+>= 2).  Per tile: the copy stream waits for the slot's ``free`` event, DMAs the
+tile's experts from the page-locked host copy and records ``ready``; the compute
+stream waits ``ready``, runs permute + grouped GEMMs for the pairs of those experts,
+and records ``free``.  One combine at the end sums every pair's slot row.  Slots
+are allocated once (``staging_bytes`` is the single source of truth for the VRAM
+they take), like the reference's tile ring (vllm_xiaotu_moe/gpu_prefill.py:2911-3095).
+"""
+from __future__ import annotations
+
+import torch
+
+from ..ops import moe as M
+from .host import HostExperts, _row_bytes
+
+
+def staging_bytes(fmt: str, H: int, I: int, tile_e: int, nslots: int) -> int:
+    per = 2 * I * _row_bytes(fmt, H) + H * _row_bytes(fmt, I)
+    if fmt == "fp8":
+        per += 4 * ((2 * I + 127) // 128) * ((H + 127) // 128) + 4 * ((H + 127) // 128) * ((I + 127) // 128)
+    return per * tile_e * nslots
+
+
+class ExpertRing:
+    def __init__(self, fmt: str, H: int, I: int, tile_e: int, nslots: int, device):
+        assert nslots >= 2, "the ring needs at least two slots to overlap copy and compute"
+        self.fmt, self.H, self.I, self.tile_e, self.nslots = fmt, H, I, tile_e, nslots
+        dt = {"bf16": torch.bfloat16, "fp8": torch.float8_e4m3fn}[fmt]
+        self.slots = []
+        for _ in range(nslots):
+            w13 = torch.empty(tile_e, 2 * I, H, dtype=dt, device=device)
+            w2 = torch.empty(tile_e, H, I, dtype=dt, device=device)
+            s13 = s2 = None
+            if fmt == "fp8":
+                s13 = torch.empty(tile_e, (2 * I + 127) // 128, (H + 127) // 128, dtype=torch.float32, device=device)
+                s2 = torch.empty(tile_e, (H + 127) // 128, (I + 127) // 128, dtype=torch.float32, device=device)
+            self.slots.append(M.ExpertWeights(fmt, w13, w2, s13, s2, interleaved=True))
+        self.ready = [torch.cuda.Event() for _ in range(nslots)]
+        self.free = [torch.cuda.Event() for _ in range(nslots)]
+        self.copy_stream = torch.cuda.Stream(device=device)
+        self.bytes = staging_bytes(fmt, H, I, tile_e, nslots)
+        self.copied_bytes = 0
+
+    def run_layer(self, host: HostExperts, x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor,
+                  ws: M.MoEWorkspace, *, shared=None, act_limit=0.0, out=None) -> torch.Tensor:
+        """All routed experts of one layer through the ring; returns the combined output."""
+        E = host.E
+        main = torch.cuda.current_stream()
+        ntiles = (E + self.tile_e - 1) // self.tile_e
+        for s in range(self.nslots):
+            self.free[s].record(main)
+        for t in range(ntiles):
+            s = t % self.nslots
+            e0, e1 = t * self.tile_e, min(E, (t + 1) * self.tile_e)
+            slot = self.slots[s]
+            self.copy_stream.wait_event(self.free[s])
+            for e in range(e0, e1):
+                host.copy_expert(e, slot.w13[e - e0], slot.w2[e - e0],
+                                 slot.s13[e - e0] if slot.s13 is not None else None,
+                                 slot.s2[e - e0] if slot.s2 is not None else None, self.copy_stream)
+            self.copied_bytes += (e1 - e0) * host.expert_bytes()
+            self.ready[s].record(self.copy_stream)
+            main.wait_event(self.ready[s])
+            view = slot if e1 - e0 == self.tile_e else M.ExpertWeights(
+                slot.fmt, slot.w13[: e1 - e0], slot.w2[: e1 - e0],
+                slot.s13[: e1 - e0] if slot.s13 is not None else None,
+                slot.s2[: e1 - e0] if slot.s2 is not None else None, True)
+            M.moe_experts_partial(x, ids, weights, view, ws, lo=e0, act_limit=act_limit)
+            self.free[s].record(main)
+        return M.moe_combine(ws, ids, 0, E, shared=shared, out=out)
