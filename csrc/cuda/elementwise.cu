@@ -17,6 +17,8 @@
 #include <cstdint>
 #include <cfloat>
 #include "ptx.cuh"
+#include "xtu_argmax_static.h"
+#include <mutex>
 
 namespace xtu {
 
@@ -692,3 +694,67 @@ int xtu_silu_mul(const void* x, int T, int I, float limit, float alpha, float be
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Argmax without allocation (declared in xtu_argmax_static.h).
+//
+// Who needs it: callers that must not allocate device memory while they run.  A
+// serving process sizes its KV cache to take the HBM that is left after start-up,
+// so a later cudaMalloc can fail for lack of memory, and cudaMalloc / cudaFree
+// synchronise the device, which would stall the streams of a decode loop that
+// is in flight.  Such callers (a C or C++ decode loop without PyTorch's caching
+// allocator, for instance) cannot hand xtu_argmax its workspace.
+//
+// How: the per-row partial results live in one file-scope device array of fixed
+// size.  The first call on a device, with that device current, looks up the
+// array's address there with cudaGetSymbolAddress and keeps it; later calls on that
+// device reuse it.  Make that first call before any stream capture begins.
+// Nothing in the array needs to start at zero: every slot that the second kernel
+// reads is written by the first kernel of the same call.  All calls on one device
+// share the array, so two calls whose kernels can overlap (different streams, or
+// different host threads without ordering between them) race on it and may return
+// wrong indices: order such calls on one stream.
+// ---------------------------------------------------------------------------
+namespace {
+constexpr int kArgmaxStaticParts = 64;  // same split limit as xtu_argmax
+constexpr size_t kArgmaxStaticBytes = (size_t)XTU_ARGMAX_STATIC_MAX_ROWS * kArgmaxStaticParts *
+                                      (sizeof(float) + sizeof(int));
+constexpr int kArgmaxStaticMaxDevices = 64;
+std::mutex g_argmax_static_mu;
+void* g_argmax_static_ptr[kArgmaxStaticMaxDevices] = {};
+}  // namespace
+
+static __device__ __align__(256) unsigned char g_argmax_scratch[kArgmaxStaticBytes];
+
+extern "C" int xtu_argmax_static(const void* logits, int is_bf16, int T, int V, int stride, int* out,
+                                 float* out_val, cudaStream_t s) {
+  if (T == 0) return 0;
+  if (T < 0 || V < 1 || stride < V) return XTU_ARGMAX_STATIC_ERR_BAD_SIZE;
+  if (T > XTU_ARGMAX_STATIC_MAX_ROWS) return XTU_ARGMAX_STATIC_ERR_TOO_MANY_ROWS;
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return -(int)e;
+  if (dev < 0 || dev >= kArgmaxStaticMaxDevices) return XTU_ARGMAX_STATIC_ERR_DEVICE;
+  void* ws;
+  {
+    std::lock_guard<std::mutex> g(g_argmax_static_mu);
+    ws = g_argmax_static_ptr[dev];
+    if (!ws) {
+      e = cudaGetSymbolAddress(&ws, g_argmax_scratch);
+      if (e != cudaSuccess) return -(int)e;
+      g_argmax_static_ptr[dev] = ws;
+    }
+  }
+  int parts = (V + 8191) / 8192;
+  if (parts > kArgmaxStaticParts) parts = kArgmaxStaticParts;
+  float* pv = reinterpret_cast<float*>(ws);
+  int* pi = reinterpret_cast<int*>(pv + (size_t)T * kArgmaxStaticParts);
+  const dim3 grid(parts, T);
+  if (is_bf16)
+    argmax_kernel<__nv_bfloat16><<<grid, 512, 0, s>>>((const __nv_bfloat16*)logits, V, stride, out, out_val, pv, pi);
+  else
+    argmax_kernel<float><<<grid, 512, 0, s>>>((const float*)logits, V, stride, out, out_val, pv, pi);
+  if (parts > 1) argmax_final_kernel<<<T, 32, 0, s>>>(pv, pi, parts, out, out_val);
+  return rc_last(parts > 1 ? 2 : 1);
+}
+
