@@ -127,12 +127,15 @@ extern "C" {
 int xtu_host_register(void* p, long long bytes) {
   if (!p || bytes <= 0) return 0;
   cudaError_t e = cudaHostRegister(p, (size_t)bytes, cudaHostRegisterPortable);
+  if (e != cudaSuccess) cudaGetLastError();  // not sticky: keep it from surfacing at an unrelated later call
   return e == cudaSuccess ? 0 : -(int)e;
 }
 
 int xtu_host_unregister(void* p) {
   if (!p) return 0;
-  return cudaHostUnregister(p) == cudaSuccess ? 0 : -1;
+  if (cudaHostUnregister(p) == cudaSuccess) return 0;
+  cudaGetLastError();
+  return -1;
 }
 
 }  // extern "C"

@@ -1,0 +1,103 @@
+"""MTP speculative decoding: greedy verification and end-to-end equivalence with
+plain greedy decoding (the drafts may only change speed, never the tokens)."""
+import pytest
+import torch
+
+from vllm_xtu_moe_b200.engine import LLM, SamplingParams
+from vllm_xtu_moe_b200.engine.runner import RunnerConfig
+from vllm_xtu_moe_b200.engine.spec_decode import SpecDecoder, verify_greedy
+from vllm_xtu_moe_b200.models.config import get_preset, scaled_down
+from vllm_xtu_moe_b200.models.model import build_model
+
+
+def _cfg():
+    return scaled_down(get_preset("glm-4.5-air"), layers=2, hidden=256, experts=16).replace(
+        num_heads=4, num_kv_heads=2, head_dim=64, rotary_dim=32, moe_intermediate=256, shared_intermediate=256,
+        dense_intermediate=512, num_mtp_layers=1)
+
+
+def _run(model, k, prompts, n, device="cpu", oracle=None):
+    rc = RunnerConfig(block_size=64, max_seqs=4, max_model_len=512, max_batched_tokens=128, use_cuda_graph=False,
+                      num_spec=k)
+    llm = LLM(model, device=device, runner_config=rc)
+    if oracle is not None:
+        def chain(reqs, first, hid, _self=llm.spec):
+            out = []
+            for r in reqs:
+                ref = oracle[tuple(r.prompt)]
+                t = r.total_len - len(r.prompt)
+                out.append(ref[t:t + k] + [0] * max(0, k - len(ref[t:t + k])))
+            return out
+        llm.spec._chain = chain
+    outs = llm.generate(prompts, SamplingParams(max_tokens=n))
+    steps = llm.stats["steps"]
+    llm.shutdown()
+    return outs, steps
+
+
+def test_verify_greedy_rules():
+    # seq 0: [last, d1, d2, d3] with targets accepting d1, d2 only; seq 1: no drafts
+    ids = torch.tensor([5, 7, 8, 9, 4], dtype=torch.int32)
+    tgt = torch.tensor([7, 8, 1, 3, 6], dtype=torch.int32)
+    q = torch.tensor([0, 4, 5], dtype=torch.int32)
+    acc, row = verify_greedy(tgt, ids, q, 2, 3)
+    assert acc.tolist() == [2, 0] and row.tolist() == [2, 4]
+
+
+@pytest.mark.parametrize("k", [1, 3])
+def test_spec_decode_matches_greedy_cpu(k):
+    m = build_model(_cfg(), device="cpu", seed=1)
+    m.act_dtype = torch.float32
+    prompts = [list(range(3, 40)), list(range(50, 61))]
+    base, steps0 = _run(m, 0, prompts, 12)
+    spec, _ = _run(m, k, prompts, 12)
+    assert [o.token_ids for o in spec] == [o.token_ids for o in base]
+    assert all(o.proposed > 0 for o in spec)
+
+
+def test_oracle_drafts_are_all_accepted():
+    m = build_model(_cfg(), device="cpu", seed=1)
+    m.act_dtype = torch.float32
+    prompts = [list(range(3, 40)), list(range(50, 61))]
+    base, steps0 = _run(m, 0, prompts, 13)
+    oracle = {tuple(p): o.token_ids for p, o in zip(prompts, base)}
+    spec, steps = _run(m, 3, prompts, 13, oracle=oracle)
+    assert [o.token_ids for o in spec] == [o.token_ids for o in base]
+    assert all(o.accepted >= 9 for o in spec)
+    assert steps < steps0
+
+
+def test_spec_decoder_rejects_linear_attention_models():
+    cfg = scaled_down(get_preset("qwen3-next-80b-a3b"), layers=4, hidden=256, experts=16).replace(
+        num_heads=4, num_kv_heads=2, head_dim=64, moe_intermediate=256, shared_intermediate=256,
+        linear_num_key_heads=2, linear_num_value_heads=4, linear_key_head_dim=32, linear_value_head_dim=32,
+        rotary_dim=32, num_mtp_layers=1)
+    m = build_model(cfg, device="cpu", seed=0)
+    with pytest.raises(NotImplementedError):
+        LLM(m, device="cpu", runner_config=RunnerConfig(block_size=16, max_seqs=2, max_model_len=128,
+                                                        max_batched_tokens=64, use_cuda_graph=False, num_spec=2))
+
+
+@pytest.mark.gpu
+def test_verify_kernel_matches_host():
+    g = torch.Generator().manual_seed(0)
+    lens = [1, 4, 4, 2, 3]
+    q = torch.tensor([0] + list(torch.tensor(lens).cumsum(0)), dtype=torch.int32)
+    n = int(q[-1])
+    tgt = torch.randint(0, 3, (n,), generator=g, dtype=torch.int32)
+    ids = torch.randint(0, 3, (n,), generator=g, dtype=torch.int32)
+    a0, r0 = verify_greedy(tgt, ids, q, len(lens), 3)
+    a1, r1 = verify_greedy(tgt.cuda(), ids.cuda(), q.cuda(), len(lens), 3)
+    assert a0.tolist() == a1.cpu().tolist() and r0.tolist() == r1.cpu().tolist()
+
+
+@pytest.mark.gpu
+def test_oracle_drafts_gpu():
+    m = build_model(_cfg(), device="cuda", seed=1)
+    prompts = [list(range(3, 40)), list(range(50, 61))]
+    base, steps0 = _run(m, 0, prompts, 13, device="cuda")
+    oracle = {tuple(p): o.token_ids for p, o in zip(prompts, base)}
+    spec, steps = _run(m, 3, prompts, 13, device="cuda", oracle=oracle)
+    same = sum(a == b for o, p in zip(spec, base) for a, b in zip(o.token_ids, p.token_ids))
+    assert same >= 0.9 * sum(len(o.token_ids) for o in base)
+    assert steps < steps0

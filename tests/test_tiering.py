@@ -118,10 +118,19 @@ def test_cpu_tier_model_matches_resident():
     x = (torch.randn(9, cfg.hidden_size) * 0.5).to(torch.bfloat16)
     a, b = blk_r(x).float(), blk_t(x).float()
     assert (a - b).abs().max().item() <= 2e-2 * a.abs().max().item() + 1e-3
-    tier.shutdown()
 
 
 # ----------------------------------------------------------------------------- GPU
+_live = []
+
+
+@pytest.fixture(autouse=True)
+def _shutdown_tiers():
+    yield
+    while _live:
+        _live.pop().shutdown()
+
+
 def _raw_gpu(fmt, E, H, I, seed):
     g = torch.Generator().manual_seed(seed)
     w13 = torch.randn(E, 2 * I, H, generator=g) / H ** 0.5
@@ -171,6 +180,7 @@ def _executor_case(fmt, pool_experts, T, skew=False, ring=True, min_tokens=64, w
     ec = EngineConfig(stage_tile_e=12, stage_nslots=2, pin_window=window)
     tier = TieredExperts(cfg, device="cuda", engine_config=ec, resident_layers=set(), pool_experts=pool_experts,
                          ring=ring, gpu_prefill_min_tokens=min_tokens, max_tokens=1024)
+    _live.append(tier)
     assert tier.expert_sink(1, raw) is None
     res = M.prepare_experts(fmt, raw["w13"].cuda(), raw["w2"].cuda(), raw["s13"].cuda() if "s13" in raw else None,
                             raw["s2"].cuda() if "s2" in raw else None)
@@ -212,7 +222,6 @@ def test_hybrid_pool_plus_cpu_matches_gpu(fmt, T):
     assert tier.stats()["hybrid"] == 1
     hits = blk.executor.pool.hits.cpu()
     assert hits.sum().item() == ids.numel()
-    tier.shutdown()
 
 
 @pytest.mark.gpu
@@ -224,7 +233,6 @@ def test_cpu_only_bridge_matches_gpu(fmt):
     ok, err = _close(y, ref)
     assert ok, err
     assert tier.stats()["cpu"] == 1 and blk.executor.bridge.stats()["runs"] == 1
-    tier.shutdown()
 
 
 @pytest.mark.gpu
@@ -237,7 +245,6 @@ def test_prefill_ring_matches_gpu(fmt):
     assert ok, err
     assert tier.stats()["ring"] == 1
     assert tier.ring.copied_bytes == 32 * tier.executors[0].host.expert_bytes()
-    tier.shutdown()
 
 
 @pytest.mark.gpu
@@ -257,7 +264,6 @@ def test_pool_adapts_to_hot_experts_and_stays_exact():
         assert sm[e].item() == s
     assert (sm >= 0).sum().item() == 4
     assert 0 in pool.expert_of            # the hottest expert of the skewed routing moved in
-    tier.shutdown()
 
 
 @pytest.mark.gpu
@@ -279,4 +285,3 @@ def test_hybrid_path_graph_replay_matches_eager():
     assert torch.equal(out, eager)
     assert blk.executor.bridge.stats()["runs"] >= 5
     del g
-    tier.shutdown()

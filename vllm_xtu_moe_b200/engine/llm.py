@@ -61,7 +61,7 @@ class LLM:
         self.spec = None
         if rc.num_spec > 0 and self.model.mtp:
             from .spec_decode import SpecDecoder
-            self.spec = SpecDecoder(self.runner, rc.num_spec)
+            self.spec = SpecDecoder(self.runner, rc.num_spec, self.blocks)
         self.stats = dict(prefill_tokens=0, decode_tokens=0, prefill_time=0.0, decode_time=0.0, steps=0)
 
     # ------------------------------------------------------------------

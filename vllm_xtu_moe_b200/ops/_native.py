@@ -46,6 +46,7 @@ _SIGS: dict[str, list] = {
     "xtu_argmax": [P, c_int, c_int, c_int, c_int, P, P, P, P],
     "xtu_embed": [P, P, c_int, c_int, c_int, P, P],
     "xtu_route_split": [P, c_int, c_int, c_int, P, P, P, P, P],
+    "xtu_spec_verify": [P, P, P, c_int, c_int, P, P, P],
     "xtu_silu_mul": [P, c_int, c_int, c_float, c_float, c_float, P, P],
     "xtu_gemv": [P, P, c_int, c_int, c_int, P, c_int, c_int, P, P, c_int, c_int, P],
     "xtu_moe_gemv": [P, P, P, P, c_int, c_int, c_int, c_int, P, P, P, P, P, P, c_int, c_float, c_float, c_float, P],

@@ -83,6 +83,9 @@ def paged_attention_ref(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.T
     return o
 
 
+KV_BLOCK = 64   # tokens per KV-cache block read by the GPU kernel
+
+
 def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor | None, meta: AttnMetadata,
                     scale: float | None = None, v_dim: int | None = None, out: torch.Tensor | None = None,
                     workspace: torch.Tensor | None = None) -> torch.Tensor:
@@ -94,6 +97,9 @@ def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
             raise N.NativeLibraryMissing("xtu_paged_attention missing from the CUDA library")
         return paged_attention_ref(q, k_cache, v_cache, meta, scale, v_dim, out)
     Hk = k_cache.shape[1]
+    if k_cache.shape[2] != KV_BLOCK:
+        raise ValueError(f"the GPU paged-attention kernel reads KV blocks of {KV_BLOCK} tokens, "
+                         f"not {k_cache.shape[2]} (set RunnerConfig.block_size={KV_BLOCK})")
     Dv = v_dim if v_dim is not None else (v_cache.shape[3] if v_cache is not None else D)
     o = out if out is not None else torch.empty(T, Hq, Dv, dtype=q.dtype, device=q.device)
     assert q.stride(2) == 1 and q.stride(1) == D and o.is_contiguous()

@@ -135,6 +135,8 @@ def moe_experts_partial(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tenso
     T, H = x.shape
     K = ids.shape[1]
     E = experts.num_experts
+    if ws.num_experts < E or ws.max_tokens < T:
+        raise ValueError(f"workspace for {ws.num_experts} experts x {ws.max_tokens} tokens; call needs {E} x {T}")
     s = N.stream_ptr(x.device)
     n = T * K
     N.call("xtu_moe_permute", ids.data_ptr(), weights.data_ptr(), T, K, lo, lo + E, ws.counts.data_ptr(),
@@ -149,7 +151,8 @@ def moe_experts_partial(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tenso
                ws.seg.data_ptr(), ws.perm_slot.data_ptr(), ws.perm_w.data_ptr(), ws.h.data_ptr(),
                ws.slots.data_ptr(), T, float(act_limit), float(act_alpha), float(act_beta), s)
         return
-    tiles = G.build_mtiles(ws.seg, n, ws.tiles, ws.ntiles)
+    # the segment table of this call has E + 1 entries (the workspace may serve more experts)
+    tiles = G.build_mtiles(ws.seg[: E + 1], n, ws.tiles, ws.ntiles)
     xp = ws.xp[:n]
     sc13 = experts.s13 if fp8 else None
     sc2 = experts.s2 if fp8 else None

@@ -106,7 +106,15 @@ class HostExperts:
         return 2 * self.I * _row_bytes(self.fmt, self.H) + self.H * _row_bytes(self.fmt, self.I)
 
     def close(self):
-        L = lib()
-        for p in self.registered:
-            L.xtu_host_unregister(p)
-        self.registered = []
+        """Unregister the engine's shards (must happen before the engine frees them)."""
+        if self.registered:
+            L = lib()
+            for p in self.registered:
+                L.xtu_host_unregister(p)
+            self.registered = []
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
