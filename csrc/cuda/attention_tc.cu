@@ -285,21 +285,30 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_after();
       const uint32_t s_addr = lane_base + C::S_COL0 + (jj & 1) * BN;
       const int key0 = j * BN;
-      const int c_lo = part * KP, c_hi = c_lo + KP;
-      // pass 1: masked row max over this replica's keys
-      float mx = -FLT_MAX;
-#pragma unroll 1
-      for (int c = c_lo; c < c_hi; c += 16) {
-        uint32_t v[16];
-        tmem_ld16(s_addr + c, v);
-        tmem_wait_ld();
+      const int c_lo = part * KP;
+      // this replica's S columns -> registers, one TMEM round trip per tile.  KP is a
+      // multiple of 16 (BN >= 64, RF <= 4), so 16-column chunks never pass the range.
+      uint32_t sv[BN];
 #pragma unroll
-        for (int t = 0; t < 16; ++t) {
-          const int key = key0 + c + t;
-          const float sv = __uint_as_float(v[t]) * p.scale_log2;
-          if (row_valid && key <= qpos) mx = fmaxf(mx, sv);
+      for (int ch = 0; ch < BN / 16; ++ch)
+        if (ch * 16 < KP) tmem_ld16p(s_addr + c_lo + ch * 16, sv + ch * 16);
+      tmem_wait_ld();
+      // keys t <= lim of the range are visible to this row (causal limit; kv_len follows from it)
+      const int lim = row_valid ? qpos - (key0 + c_lo) : -1;
+      const bool all_vis = __all_sync(0xffffffffu, lim >= KP - 1);
+      float mx4[4] = {-FLT_MAX, -FLT_MAX, -FLT_MAX, -FLT_MAX};
+#pragma unroll
+      for (int ch = 0; ch < BN / 16; ++ch) {
+        if (ch * 16 < KP) {
+#pragma unroll
+          for (int t = 0; t < 16; ++t) {
+            const int i = ch * 16 + t;
+            if (all_vis || i <= lim) mx4[t & 3] = fmaxf(mx4[t & 3], __uint_as_float(sv[i]));
+          }
         }
       }
+      float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+      if (mx != -FLT_MAX) mx *= p.scale_log2;   // scale > 0: max commutes with it
       // Raise the running max only when it grows by more than 2^8.  tcgen05.ld/st are
       // warp-collective (.sync.aligned), so the O rescale is decided per warp: if any
       // row of the warp needs it, the whole warp rescales (alpha = 1 for the others).
@@ -332,27 +341,31 @@ __global__ void __launch_bounds__(192, 1)
         if (!mbar_wait(&o_done[jj & 1], ((jj - 2) >> 1) & 1, p.status, 122)) { ok = false; break; }
       }
       uint8_t* pbuf = sP + (jj & 1) * C::P_BYTES;
-      float rs = 0.f;
-#pragma unroll 1
-      for (int c = c_lo; c < c_hi; c += 16) {
-        uint32_t v[16];
-        tmem_ld16(s_addr + c, v);
-        tmem_wait_ld();
-        uint32_t pk[8];
+      const float neg_m = -m_use;
+      const bool live = row_valid && m_use != -FLT_MAX;
+      float rs4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int t = 0; t < 16; t += 2) {
-          const int key = key0 + c + t;
-          float e0 = 0.f, e1 = 0.f;
-          if (row_valid && m_use != -FLT_MAX) {
-            if (key <= qpos) e0 = ex2(__uint_as_float(v[t]) * p.scale_log2 - m_use);
-            if (key + 1 <= qpos) e1 = ex2(__uint_as_float(v[t + 1]) * p.scale_log2 - m_use);
+      for (int ch = 0; ch < BN / 16; ++ch) {
+        if (ch * 16 < KP) {
+          uint32_t pk[8];
+#pragma unroll
+          for (int t = 0; t < 16; t += 2) {
+            const int i = ch * 16 + t;
+            float e0 = ex2(fmaf(__uint_as_float(sv[i]), p.scale_log2, neg_m));
+            float e1 = ex2(fmaf(__uint_as_float(sv[i + 1]), p.scale_log2, neg_m));
+            if (!all_vis) {
+              e0 = (live && i <= lim) ? e0 : 0.f;
+              e1 = (live && i + 1 <= lim) ? e1 : 0.f;
+            }
+            rs4[(t >> 1) & 3] += e0 + e1;
+            pk[t >> 1] = pack_bf16x2(e0, e1);
           }
-          rs += e0 + e1;
-          pk[t >> 1] = pack_bf16x2(e0, e1);
+          const int c = c_lo + ch * 16;
+          st_sw128(pbuf, 128, r, c, make_uint4(pk[0], pk[1], pk[2], pk[3]));
+          st_sw128(pbuf, 128, r, c + 8, make_uint4(pk[4], pk[5], pk[6], pk[7]));
         }
-        st_sw128(pbuf, 128, r, c, make_uint4(pk[0], pk[1], pk[2], pk[3]));
-        st_sw128(pbuf, 128, r, c + 8, make_uint4(pk[4], pk[5], pk[6], pk[7]));
       }
+      const float rs = (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
       l += rs;
       fence_proxy_async_smem();
       tc_fence_before();
@@ -576,6 +589,9 @@ int xtu_paged_attention(const void* q, int q_stride, const void* k_cache, const 
   const int rows_used = max_q_len * G;
   // replica merge buffers live in the K ring: only the decode configurations (D <= 128) use it
   p.rf = (!decode_shape || D > 128) ? 1 : rows_used <= 32 ? 4 : rows_used <= 64 ? 2 : 1;
+  // every replica scores a multiple of 16 keys per tile (the softmax reads S in 16-column chunks)
+  const int bn = (decode_shape && D == 64) ? 64 : 128;
+  while (p.rf > 1 && (bn / p.rf) % 16 != 0) p.rf >>= 1;
   if (decode_shape && D == 128 && DV == 128) r = launch_attn<128, 128, 128, 2, 256>(tk, tv, p, grid_x, B, s);
   else if (decode_shape && D == 64 && DV == 64) r = launch_attn<64, 64, 64, 6, 1024>(tk, tv, p, grid_x, B, s);
   else if (D == 128 && DV == 128) r = launch_attn<128, 128, 128>(tk, tv, p, grid_x, B, s);

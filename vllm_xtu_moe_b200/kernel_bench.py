@@ -1,0 +1,214 @@
+"""Per-kernel microbenchmarks on the shapes of the serving configs, timed with CUDA
+events (warm-up, L2 flushed between iterations) and reported against the measured
+peaks of the GPU (copy bandwidth, dense bf16 GEMM rate).
+
+    python -m vllm_xtu_moe_b200.kernel_bench --op moe_prefill_fp8 [--tokens 8192]
+    python -m vllm_xtu_moe_b200.kernel_bench --op all
+
+Each op prints one JSON line: the shape, device time per call, the algorithmic
+bytes and FLOPs of one call, and the achieved fractions of the measured peaks.
+These are also the small cases that kernel profiles are captured on.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+from pathlib import Path
+
+import torch
+
+from .ops import attention as A
+from .ops import basic as B
+from .ops import gemm as G
+from .ops import moe as M
+from .ops.attention import AttnMetadata
+from .ops.quant import quant_fp8_block
+from .ops.router import router_topk, zipf_bias
+
+_PEAKS = Path(__file__).resolve().parent.parent / "MEASURED_PEAKS.json"
+
+
+def peaks() -> dict:
+    if _PEAKS.exists():
+        p = json.loads(_PEAKS.read_text())
+        return {"hbm_gbs": p["hbm_gbs"], "bf16_tflops": p["bf16_tflops"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def time_fn(fn, iters: int = 10, warmup: int = 3, flush: bool = True) -> float:
+    """Median device milliseconds per call; a 256 MB write between calls evicts L2."""
+    scratch = torch.empty(256 << 20, dtype=torch.uint8, device="cuda") if flush else None
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(iters):
+        if scratch is not None:
+            scratch.fill_(1)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        b.synchronize()
+        ts.append(a.elapsed_time(b))
+    torch.cuda.synchronize()
+    ts.sort()
+    return ts[len(ts) // 2]
+
+
+def _report(op: str, shape: dict, ms: float, nbytes: float, flops: float) -> dict:
+    pk = peaks()
+    tbs = nbytes / (ms * 1e-3) / 1e12
+    tfl = flops / (ms * 1e-3) / 1e12
+    return {"op": op, "shape": shape, "ms": round(ms, 4), "bytes": int(nbytes), "flops": int(flops),
+            "tb_s": round(tbs, 3), "tflop_s": round(tfl, 1),
+            "frac_hbm": round(tbs * 1e3 / pk["hbm_gbs"], 3), "frac_bf16": round(tfl / pk["bf16_tflops"], 3),
+            "peaks": pk["source"]}
+
+
+def _experts(E, H, I, fmt, seed=0):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    w13 = torch.randn(E, 2 * I, H, device="cuda", generator=g) * 0.02
+    w2 = torch.randn(E, H, I, device="cuda", generator=g) * 0.02
+    if fmt == "fp8":
+        q13, s13 = quant_fp8_block(w13)
+        q2, s2 = quant_fp8_block(w2)
+        del w13, w2
+        ex = M.prepare_experts("fp8", q13, q2, s13, s2)
+    else:
+        ex = M.prepare_experts("bf16", w13.to(torch.bfloat16), w2.to(torch.bfloat16))
+        del w13, w2
+    torch.cuda.empty_cache()
+    return ex
+
+
+def _routes(T, E, K, seed=0):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    logits = torch.randn(T, E, device="cuda", generator=g) + zipf_bias(E, 1.1, seed).cuda()
+    return router_topk(logits, K, "softmax")
+
+
+def bench_moe(T: int, fmt: str, E=128, H=4096, I=1408, K=8, iters=10) -> dict:
+    ex = _experts(E, H, I, fmt)
+    ids, w = _routes(T, E, K)
+    x = (torch.randn(T, H, device="cuda") * 0.5).to(torch.bfloat16)
+    ws = M.MoEWorkspace(T, K, E, H, I, x.device)
+    out = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+    fn = lambda: M.fused_moe(x, ids, w, ex, ws, out=out)
+    ms = time_fn(fn, iters)
+    active = torch.unique(ids).numel()
+    wb = (1 if fmt == "fp8" else 2) * 3 * H * I * active
+    nbytes = wb + T * H * 2 * 2 + T * K * H * 2 * 3
+    flops = 2 * T * K * 3 * H * I
+    return _report(f"moe_{'decode' if T <= G.GEMV_MAX_M else 'prefill'}_{fmt}",
+                   dict(T=T, E=E, H=H, I=I, K=K, active_experts=active), ms, nbytes, flops)
+
+
+def bench_gemv(N: int, Kd: int, M_: int, fmt: str, iters=20) -> dict:
+    w = torch.randn(N, Kd, device="cuda") * 0.02
+    if fmt == "fp8":
+        w, s = quant_fp8_block(w)
+    else:
+        w, s = w.to(torch.bfloat16), None
+    x = torch.randn(M_, Kd, device="cuda").to(torch.bfloat16)
+    fn = lambda: G.linear(x, w, s)
+    ms = time_fn(fn, iters)
+    nbytes = w.numel() * w.element_size() + M_ * (Kd + N) * 2
+    return _report(f"gemv_{fmt}", dict(N=N, K=Kd, M=M_), ms, nbytes, 2 * M_ * N * Kd)
+
+
+def bench_gemm(Mr: int, N: int, Kd: int, fmt: str, iters=10) -> dict:
+    w = torch.randn(N, Kd, device="cuda") * 0.02
+    if fmt == "fp8":
+        w, s = quant_fp8_block(w)
+    else:
+        w, s = w.to(torch.bfloat16), None
+    x = torch.randn(Mr, Kd, device="cuda").to(torch.bfloat16)
+    fn = lambda: G.linear(x, w, s)
+    ms = time_fn(fn, iters)
+    nbytes = w.numel() * w.element_size() + Mr * (Kd + N) * 2
+    return _report(f"gemm_{fmt}", dict(M=Mr, N=N, K=Kd), ms, nbytes, 2 * Mr * N * Kd)
+
+
+def _cache(Bn, kv, Hkv, D, bs=64):
+    nb_per = (kv + bs - 1) // bs
+    nb = Bn * nb_per
+    kc = (torch.randn(nb, Hkv, bs, D, device="cuda") * 0.5).to(torch.bfloat16)
+    vc = (torch.randn(nb, Hkv, bs, D, device="cuda") * 0.5).to(torch.bfloat16)
+    bt = torch.arange(nb, dtype=torch.int32, device="cuda").view(Bn, nb_per)
+    return kc, vc, bt
+
+
+def bench_attn_decode(Bn=4, kv=15000, Hq=96, Hkv=8, D=128, iters=20) -> dict:
+    kc, vc, bt = _cache(Bn, kv, Hkv, D)
+    q = (torch.randn(Bn, Hq, D, device="cuda") * 0.5).to(torch.bfloat16)
+    d = "cuda"
+    meta = AttnMetadata(num_seqs=Bn, q_start=torch.arange(Bn + 1, dtype=torch.int32, device=d),
+                        kv_len=torch.full((Bn,), kv, dtype=torch.int32, device=d), block_table=bt,
+                        slot_mapping=torch.zeros(Bn, dtype=torch.int32, device=d),
+                        positions=torch.full((Bn,), kv - 1, dtype=torch.int32, device=d), max_q_len=1,
+                        max_kv_len=kv, is_decode=True)
+    meta.num_splits = A.choose_splits(Bn, Hkv, kv)
+    ws = torch.empty(A.num_split_workspace(Bn, Hq, D, meta.num_splits), dtype=torch.float32, device=d)
+    out = torch.empty(Bn, Hq, D, dtype=torch.bfloat16, device=d)
+    fn = lambda: A.paged_attention(q, kc, vc, meta, out=out, workspace=ws)
+    ms = time_fn(fn, iters)
+    nbytes = 2 * Bn * kv * Hkv * D * 2
+    flops = 4 * Bn * kv * Hq * D
+    return _report("attention_decode", dict(B=Bn, kv=kv, Hq=Hq, Hkv=Hkv, D=D, splits=meta.num_splits), ms,
+                   nbytes, flops)
+
+
+def bench_attn_prefill(T=8192, Hq=96, Hkv=8, D=128, iters=5) -> dict:
+    kc, vc, bt = _cache(1, T, Hkv, D)
+    q = (torch.randn(T, Hq, D, device="cuda") * 0.5).to(torch.bfloat16)
+    d = "cuda"
+    meta = AttnMetadata(num_seqs=1, q_start=torch.tensor([0, T], dtype=torch.int32, device=d),
+                        kv_len=torch.tensor([T], dtype=torch.int32, device=d), block_table=bt,
+                        slot_mapping=torch.zeros(T, dtype=torch.int32, device=d),
+                        positions=torch.arange(T, dtype=torch.int32, device=d), max_q_len=T, max_kv_len=T,
+                        is_decode=False)
+    out = torch.empty(T, Hq, D, dtype=torch.bfloat16, device=d)
+    fn = lambda: A.paged_attention(q, kc, vc, meta, out=out)
+    ms = time_fn(fn, iters)
+    flops = 4 * Hq * D * T * (T + 1) / 2
+    nbytes = 2 * T * Hkv * D * 2 + 2 * T * Hq * D * 2
+    return _report("attention_prefill_causal", dict(T=T, Hq=Hq, Hkv=Hkv, D=D), ms, nbytes, flops)
+
+
+def bench_rmsnorm(T=16384, H=4096, iters=20) -> dict:
+    x = torch.randn(T, H, device="cuda").to(torch.bfloat16)
+    r = torch.randn(T, H, device="cuda").to(torch.bfloat16)
+    w = torch.ones(H, device="cuda").to(torch.bfloat16)
+    fn = lambda: B.rmsnorm(x, w, 1e-6, residual=r)
+    ms = time_fn(fn, iters)
+    return _report("rmsnorm_residual", dict(T=T, H=H), ms, 4 * T * H * 2, 0)
+
+
+OPS = {
+    "moe_prefill_fp8": lambda a: bench_moe(a.tokens, "fp8"),
+    "moe_prefill_bf16": lambda a: bench_moe(a.tokens, "bf16"),
+    "moe_decode_fp8": lambda a: bench_moe(4, "fp8"),
+    "gemv_fp8": lambda a: bench_gemv(14336, 4096, 4, "fp8"),
+    "gemm_fp8": lambda a: bench_gemm(a.tokens, 14336, 4096, "fp8"),
+    "gemm_bf16": lambda a: bench_gemm(a.tokens, 14336, 4096, "bf16"),
+    "attention_decode": lambda a: bench_attn_decode(),
+    "attention_prefill": lambda a: bench_attn_prefill(min(a.tokens, 16384)),
+    "rmsnorm": lambda a: bench_rmsnorm(),
+}
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--op", default="all", choices=["all"] + list(OPS))
+    ap.add_argument("--tokens", type=int, default=8192)
+    a = ap.parse_args(argv)
+    torch.manual_seed(0)
+    for name in (OPS if a.op == "all" else [a.op]):
+        print(json.dumps(OPS[name](a)), flush=True)
+        torch.cuda.empty_cache()
+
+
+if __name__ == "__main__":
+    main()
