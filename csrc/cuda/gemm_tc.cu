@@ -55,6 +55,8 @@ struct GemmParams {
   int ldd;                // elements
   const float* row_scale; // multiply row m by row_scale[m] (nullable)
   const int* row_dest;    // write row m to D row row_dest[m] (nullable; <0 = drop)
+  void* const* peer_D;    // (nullable) per-rank output bases: row_dest = rank * peer_rows + row,
+  int peer_rows;          //   stored over NVLink into that rank's buffer (expert-parallel combine)
   float act_limit, act_alpha, act_beta;  // clamped SwiGLU
   // fp8 B
   const float* b_scale;   // [E, ceil(N/128), ceil(K/128)]
@@ -229,11 +231,17 @@ __global__ void __launch_bounds__(Cfg<BN, BFMT>::NUM_WARPS * 32, 1)
         if (p.row_dest) drow = p.row_dest[row];
       }
       const bool write = row_ok && drow >= 0;
+      void* dbase = p.D;
+      if (p.peer_D != nullptr && write) {
+        const int pr = drow / p.peer_rows;
+        drow -= pr * p.peer_rows;
+        dbase = p.peer_D[pr];
+      }
       if (EPI == EPI_SWIGLU) {
         // B rows of this tile: [0, BN/2) gate, [BN/2, BN) up, for output cols
         // [nb*BN/2, nb*BN/2 + BN/2)
         const int out_cols = p.N / 2;
-        __nv_bfloat16* D = reinterpret_cast<__nv_bfloat16*>(p.D);
+        __nv_bfloat16* D = reinterpret_cast<__nv_bfloat16*>(dbase);
 #pragma unroll 1
         for (int c = 0; c < BN / 2; c += 32) {
           uint32_t g[32], u[32];
@@ -274,7 +282,7 @@ __global__ void __launch_bounds__(Cfg<BN, BFMT>::NUM_WARPS * 32, 1)
           const int col0 = nb * BN + c;
           if (write && col0 < p.N) {
             if (EPI == EPI_F32) {
-              float* dst = reinterpret_cast<float*>(p.D) + (size_t)drow * p.ldd + col0;
+              float* dst = reinterpret_cast<float*>(dbase) + (size_t)drow * p.ldd + col0;
               if (col0 + 32 <= p.N) {
                 float4* d4 = reinterpret_cast<float4*>(dst);
 #pragma unroll
@@ -289,7 +297,7 @@ __global__ void __launch_bounds__(Cfg<BN, BFMT>::NUM_WARPS * 32, 1)
 #pragma unroll
               for (int i = 0; i < 16; ++i)
                 packed[i] = pack_bf16x2(__uint_as_float(v[2 * i]) * rs, __uint_as_float(v[2 * i + 1]) * rs);
-              __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.D) + (size_t)drow * p.ldd + col0;
+              __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(dbase) + (size_t)drow * p.ldd + col0;
               if (col0 + 32 <= p.N) {
                 uint4* d4 = reinterpret_cast<uint4*>(dst);
 #pragma unroll
@@ -550,10 +558,27 @@ int xtu_mtile_bytes() { return (int)sizeof(MTile); }
 //   epi    : 0 = bf16 out [*, N]; 1 = f32 out; 2 = clamped SwiGLU -> bf16 out [*, N/2]
 //            (B rows per 256-row block: first 128 gate, next 128 up)
 //   row_scale / row_dest: per-row multiplier and destination row (nullable)
+int xtu_grouped_gemm_ex(const void* A, const void* B, const float* b_scale, int bfmt, void* D, int ldd, int M,
+                        int N, int K, int E, const void* tiles, const int* count, int max_mtiles, int epi,
+                        const float* row_scale, const int* row_dest, float act_limit, float act_alpha,
+                        float act_beta, void* const* peer_D, int peer_rows, void* status, cudaStream_t stream);
+
 int xtu_grouped_gemm(const void* A, const void* B, const float* b_scale, int bfmt, void* D, int ldd, int M, int N,
                      int K, int E, const void* tiles, const int* count, int max_mtiles, int epi,
                      const float* row_scale, const int* row_dest, float act_limit, float act_alpha, float act_beta,
                      void* status, cudaStream_t stream) {
+  return xtu_grouped_gemm_ex(A, B, b_scale, bfmt, D, ldd, M, N, K, E, tiles, count, max_mtiles, epi, row_scale,
+                             row_dest, act_limit, act_alpha, act_beta, nullptr, 0, status, stream);
+}
+
+// As xtu_grouped_gemm; with peer_D (device array of per-rank output bases) each kept row
+// m goes to rank row_dest[m] / peer_rows, row row_dest[m] % peer_rows, by direct stores
+// to that rank's memory (the expert-parallel combine fused into the down GEMM).
+int xtu_grouped_gemm_ex(const void* A, const void* B, const float* b_scale, int bfmt, void* D, int ldd, int M,
+                        int N, int K, int E, const void* tiles, const int* count, int max_mtiles, int epi,
+                        const float* row_scale, const int* row_dest, float act_limit, float act_alpha,
+                        float act_beta, void* const* peer_D, int peer_rows, void* status, cudaStream_t stream) {
+  if (peer_D != nullptr && (row_dest == nullptr || peer_rows <= 0)) return -7;
   if (M <= 0 || N <= 0 || K <= 0 || E <= 0) return 0;
   CUtensorMap ta, tb;
   int rc = make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, K, BM, BK, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -573,6 +598,7 @@ int xtu_grouped_gemm(const void* A, const void* B, const float* b_scale, int bfm
   p.mtiles = reinterpret_cast<const MTile*>(tiles);
   p.num_mtiles = count;
   p.D = D; p.ldd = ldd; p.row_scale = row_scale; p.row_dest = row_dest;
+  p.peer_D = peer_D; p.peer_rows = peer_rows;
   p.act_limit = act_limit; p.act_alpha = act_alpha; p.act_beta = act_beta;
   p.b_scale = b_scale; p.sb_n = (N + 127) / 128; p.sb_k = (K + 127) / 128;
   p.status = reinterpret_cast<XtuStatus*>(status);

@@ -47,6 +47,16 @@ _SIGS: dict[str, list] = {
     "xtu_embed": [P, P, c_int, c_int, c_int, P, P],
     "xtu_route_split": [P, c_int, c_int, c_int, P, P, P, P, P],
     "xtu_spec_verify": [P, P, P, c_int, c_int, P, P, P],
+    "xtu_grouped_gemm_ex": [P, P, P, c_int, P, c_int, c_int, c_int, c_int, c_int, P, P, c_int, c_int, P, P,
+                            c_float, c_float, c_float, P, c_int, P, P],
+    "xtu_ipc_handle_size": [],
+    "xtu_ipc_handle": [P, P, ctypes.POINTER(ctypes.c_longlong)],
+    "xtu_ipc_open": [P, ctypes.c_longlong, ctypes.POINTER(c_void_p), ctypes.POINTER(c_void_p)],
+    "xtu_ipc_close": [P],
+    "xtu_peer_barrier": [P, P, c_int, c_int, P, ctypes.c_longlong, P],
+    "xtu_allreduce_oneshot": [P, P, ctypes.c_longlong, c_int, P, P, c_int, c_int, P, ctypes.c_longlong, P],
+    "xtu_ep_route": [P, c_int, c_int, c_int, c_int, c_int, P, P, P, P, P, P, P, ctypes.c_longlong, P],
+    "xtu_ep_dispatch": [P, P, c_int, c_int, c_int, c_int, c_int, P, c_int, c_int, P, P, P, P, P, c_int, P],
     "xtu_silu_mul": [P, c_int, c_int, c_float, c_float, c_float, P, P],
     "xtu_gemv": [P, P, c_int, c_int, c_int, P, c_int, c_int, P, P, c_int, c_int, P],
     "xtu_moe_gemv": [P, P, P, P, c_int, c_int, c_int, c_int, P, P, P, P, P, P, c_int, c_float, c_float, c_float, P],
