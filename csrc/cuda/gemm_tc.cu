@@ -326,39 +326,48 @@ __global__ void __launch_bounds__(Cfg<BN, BFMT>::NUM_WARPS * 32, 1)
       int expert, row0, row_end, nb;
       tile_of(w, expert, row0, row_end, nb);
       bool ok = true;
+      // 16-byte chunks of the raw tile are spread over consecutive lanes (chunk q -> row
+      // q / 4, k-bytes 16 * (q % 4)), so each warp-wide load reads 512 contiguous bytes
+      // without bank conflicts.  The (at most two) block scales of a stage are fetched
+      // before the stage's data arrives.
+      constexpr int CHUNKS = BN * BK / 16;            // 16-byte chunks per stage
+      constexpr int PER_THREAD = CHUNKS / 128;
+      const int nblk0 = (nb * BN) >> 7;
+      const int nblk_max = (p.N - 1) >> 7;
+      const float* sc_e = p.b_scale + (size_t)expert * p.sb_n * p.sb_k;
       for (int kb = 0; kb < nk; ++kb) {
+        const int kscale = (kb * BK) >> 7;
+        const float s_lo = __ldg(sc_e + (size_t)min(nblk0, nblk_max) * p.sb_k + kscale);
+        const float s_hi = BN > 128 ? __ldg(sc_e + (size_t)min(nblk0 + 1, nblk_max) * p.sb_k + kscale) : s_lo;
         if (!mbar_wait(&full_bar[stage], phase, p.status, 40)) { ok = false; break; }
         uint8_t* sB = smem + stage * C::STAGE_BYTES + C::A_BYTES;
         const uint8_t* raw = sB + C::B_BYTES;
-        const int kscale = (kb * BK) >> 7;
-#pragma unroll 1
-        for (int r = ct; r < BN; r += 128) {
-          const int n = nb * BN + r;
-          const int nblk = min(n, p.N - 1) >> 7;
-          const float s = p.b_scale[((size_t)expert * p.sb_n + nblk) * p.sb_k + kscale];
-          const uint4* src = reinterpret_cast<const uint4*>(raw + r * BK);
-          uint8_t* dst_row = sB + r * 128;
+        uint4 q[PER_THREAD];
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const uint4 q = src[c];
-            const uint32_t words[4] = {q.x, q.y, q.z, q.w};
-            uint32_t out[8];
+        for (int i = 0; i < PER_THREAD; ++i) q[i] = reinterpret_cast<const uint4*>(raw)[ct + 128 * i];
 #pragma unroll
-            for (int wi = 0; wi < 4; ++wi) {
-              __half2_raw h01 = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(words[wi] & 0xFFFF), __NV_E4M3);
-              __half2_raw h23 = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(words[wi] >> 16), __NV_E4M3);
-              const float2 f01 = __half22float2(*reinterpret_cast<__half2*>(&h01));
-              const float2 f23 = __half22float2(*reinterpret_cast<__half2*>(&h23));
-              out[2 * wi] = pack_bf16x2(f01.x * s, f01.y * s);
-              out[2 * wi + 1] = pack_bf16x2(f23.x * s, f23.y * s);
-            }
-            // 16 e4m3 -> 32 bytes of bf16 = 16-B chunks 2c and 2c+1 of the 128-B row,
-            // placed with the 128-byte swizzle (chunk ^ row%8)
-            const int c0 = (2 * c) ^ (r & 7);
-            const int c1 = (2 * c + 1) ^ (r & 7);
-            *reinterpret_cast<uint4*>(dst_row + c0 * 16) = make_uint4(out[0], out[1], out[2], out[3]);
-            *reinterpret_cast<uint4*>(dst_row + c1 * 16) = make_uint4(out[4], out[5], out[6], out[7]);
+        for (int i = 0; i < PER_THREAD; ++i) {
+          const int qi = ct + 128 * i;
+          const int r = qi >> 2, c = qi & 3;
+          const float sc = r < 128 ? s_lo : s_hi;
+          const uint32_t words[4] = {q[i].x, q[i].y, q[i].z, q[i].w};
+          uint32_t out[8];
+#pragma unroll
+          for (int wi = 0; wi < 4; ++wi) {
+            __half2_raw h01 = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(words[wi] & 0xFFFF), __NV_E4M3);
+            __half2_raw h23 = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(words[wi] >> 16), __NV_E4M3);
+            const float2 f01 = __half22float2(*reinterpret_cast<__half2*>(&h01));
+            const float2 f23 = __half22float2(*reinterpret_cast<__half2*>(&h23));
+            out[2 * wi] = pack_bf16x2(f01.x * sc, f01.y * sc);
+            out[2 * wi + 1] = pack_bf16x2(f23.x * sc, f23.y * sc);
           }
+          // 16 e4m3 -> 32 bytes of bf16 = 16-B chunks 2c and 2c+1 of the row's 128 bytes,
+          // placed with the 128-byte swizzle (chunk ^ row % 8)
+          uint8_t* dst_row = sB + r * 128;
+          const int c0 = (2 * c) ^ (r & 7);
+          const int c1 = (2 * c + 1) ^ (r & 7);
+          *reinterpret_cast<uint4*>(dst_row + c0 * 16) = make_uint4(out[0], out[1], out[2], out[3]);
+          *reinterpret_cast<uint4*>(dst_row + c1 * 16) = make_uint4(out[4], out[5], out[6], out[7]);
         }
         fence_proxy_async_smem();
         __syncwarp();
