@@ -1,0 +1,41 @@
+"""Serving surface: OpenAI-compatible HTTP server, vLLM plugin entry point, custom ops."""
+import torch
+
+from vllm_xtu_moe_b200.engine import LLM
+from vllm_xtu_moe_b200.engine.runner import RunnerConfig
+from vllm_xtu_moe_b200.models.config import get_preset
+
+
+def test_completions_endpoint_cpu():
+    from fastapi.testclient import TestClient
+    from vllm_xtu_moe_b200.serve import EngineThread, build_app
+    llm = LLM(get_preset("tiny-mixtral"), device="cpu",
+              runner_config=RunnerConfig(block_size=16, max_seqs=4, max_model_len=256, max_batched_tokens=64,
+                                         use_cuda_graph=False))
+    eng = EngineThread(llm)
+    try:
+        c = TestClient(build_app(eng, "tiny-mixtral"))
+        assert c.get("/health").json() == {"status": "ok"}
+        r = c.post("/v1/completions", json={"prompt": list(range(1, 20)), "max_tokens": 6}).json()
+        assert len(r["choices"][0]["token_ids"]) == 6 and r["usage"]["prompt_tokens"] == 19
+        r2 = c.post("/v1/completions", json={"prompt": "hello", "max_tokens": 3}).json()
+        assert r2["usage"]["prompt_tokens"] == 5
+        m = c.get("/metrics").text
+        assert "xtu_requests_total 2" in m
+        # greedy and deterministic: the same prompt gives the same tokens
+        r3 = c.post("/v1/completions", json={"prompt": list(range(1, 20)), "max_tokens": 6}).json()
+        assert r3["choices"][0]["token_ids"] == r["choices"][0]["token_ids"]
+    finally:
+        eng.stop()
+
+
+def test_plugin_registers_custom_ops():
+    import vllm_xtu_moe_b200 as pkg
+    cfg = pkg.register()
+    assert cfg is pkg.register()
+    x = torch.randn(3, 64).to(torch.bfloat16)
+    w = torch.ones(64).to(torch.bfloat16)
+    y = torch.ops.xtu.rmsnorm(x, w, 1e-6)
+    ref = x.float() * torch.rsqrt(x.float().pow(2).mean(-1, keepdim=True) + 1e-6)
+    assert (y.float() - ref).abs().max().item() < 2e-2
+    assert torch.ops.xtu.argmax(torch.tensor([[0.0, 3.0, 1.0]])).tolist() == [1]

@@ -49,6 +49,10 @@ class LLM:
             self.model = model
         else:
             cfg = get_preset(model) if isinstance(model, str) else model
+            if tiering is None and self.econf.experts_load_device == "cpu":
+                # hybrid mode (VLLM_EXPERTS_LOAD_DEVICE=cpu): routed experts on the host tier
+                from ..tiering.executor import TieredExperts
+                tiering = TieredExperts(cfg, device=device, engine_config=self.econf)
             sink = tiering.expert_sink if tiering is not None else None
             self.model = build_model(cfg, device=device, seed=seed, expert_sink=sink, num_layers=num_layers)
         if tiering is not None:
@@ -63,6 +67,12 @@ class LLM:
             from .spec_decode import SpecDecoder
             self.spec = SpecDecoder(self.runner, rc.num_spec, self.blocks)
         self.stats = dict(prefill_tokens=0, decode_tokens=0, prefill_time=0.0, decode_time=0.0, steps=0)
+        self.tracer = None
+        ec = self.econf
+        if ec.routing_dump or ec.layer_timing or ec.torch_profile or ec.nvtx:
+            from ..utils.trace import Tracer
+            self.tracer = Tracer(self.model, ec)
+            self.model.attach_tracer(self.tracer)
 
     # ------------------------------------------------------------------
     def add_request(self, prompt: list[int], params: SamplingParams) -> Request:
@@ -77,6 +87,15 @@ class LLM:
             plan = self.scheduler.schedule()
         if plan is None:
             return []
+        if self.tracer is not None and self.tracer.profiler is not None:
+            self.tracer.profiler.before_step()
+        try:
+            return self._step(plan)
+        finally:
+            if self.tracer is not None and self.tracer.profiler is not None:
+                self.tracer.profiler.after_step()
+
+    def _step(self, plan) -> list[Request]:
         t0 = time.perf_counter()
         if plan.is_decode and self.spec is not None:
             done = self.spec.decode_step(plan, self.scheduler)
@@ -141,5 +160,7 @@ class LLM:
 
     def shutdown(self):
         self.runner.release_graphs()
+        if self.tracer is not None:
+            self.tracer.close()
         if self.tiering is not None:
             self.tiering.shutdown()

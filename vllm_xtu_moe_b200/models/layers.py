@@ -156,6 +156,8 @@ class MoEBlock:
         self.executor = None              # set by the tier planner
         self.ws: M.MoEWorkspace | None = None
         self.last_ids: torch.Tensor | None = None
+        self.tracer = None                # utils.trace.Tracer (routing dump) when enabled
+        self.trace_idx = layer_idx
 
     def route(self, x: torch.Tensor):
         logits = G.linear(x, self.gate, out_dtype=torch.float32)
@@ -166,6 +168,8 @@ class MoEBlock:
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         ids, w = self.route(x)
         self.last_ids = ids
+        if self.tracer is not None and self.tracer.routing is not None:
+            self.tracer.routing.record(self.trace_idx, ids)
         sh = None
         if self.shared is not None:
             sh = self.shared(x)

@@ -71,6 +71,7 @@ class MoETransformer:
         self.mtp = mtp or []
         self.device = embed.device
         self.act_dtype = torch.bfloat16   # fp32 allowed on CPU (exact-reference runs)
+        self.tracer = None
         self.rope = B.rope_cache(cfg.rot_dim, min(cfg.max_position, 1 << 18), cfg.rope_theta, self.device,
                                  cfg.rope_scaling)
 
@@ -82,10 +83,25 @@ class MoETransformer:
     def forward(self, ids: torch.Tensor, meta: AttnMetadata, caches: list, return_prenorm: bool = False):
         x = self.embed(ids)
         residual = None
+        tr = self.tracer
         for layer, kv in zip(self.layers, caches):
-            x, residual = layer(x, residual, meta, kv, self.rope)
+            if tr is None:
+                x, residual = layer(x, residual, meta, kv, self.rope)
+            else:
+                with tr.layer(layer.idx):
+                    x, residual = layer(x, residual, meta, kv, self.rope)
         h, pre = self.norm(x, residual)
         return (h, pre) if return_prenorm else h
+
+    def attach_tracer(self, tracer) -> None:
+        """Enable the observability hooks of ``utils.trace`` (routing dump, NVTX, timing)."""
+        self.tracer = tracer
+        for i, l in enumerate(self.layers):
+            if isinstance(l.mlp, MoEBlock):
+                l.mlp.tracer, l.mlp.trace_idx = tracer, i
+        for j, m in enumerate(self.mtp):
+            if isinstance(m.layer.mlp, MoEBlock):
+                m.layer.mlp.tracer, m.layer.mlp.trace_idx = tracer, len(self.layers) + j
 
     def logits(self, h: torch.Tensor) -> torch.Tensor:
         return G.linear(h, self.lm_head, out_dtype=torch.float32)
