@@ -48,13 +48,23 @@ class LLM:
         if isinstance(model, MoETransformer):
             self.model = model
         else:
-            cfg = get_preset(model) if isinstance(model, str) else model
+            ckpt = isinstance(model, str) and os.path.isdir(model)
+            if ckpt:
+                from ..models.config import from_hf_config
+                cfg = from_hf_config(model)
+            else:
+                cfg = get_preset(model) if isinstance(model, str) else model
             if tiering is None and self.econf.experts_load_device == "cpu":
                 # hybrid mode (VLLM_EXPERTS_LOAD_DEVICE=cpu): routed experts on the host tier
                 from ..tiering.executor import TieredExperts
                 tiering = TieredExperts(cfg, device=device, engine_config=self.econf)
             sink = tiering.expert_sink if tiering is not None else None
-            self.model = build_model(cfg, device=device, seed=seed, expert_sink=sink, num_layers=num_layers)
+            if ckpt:      # HF checkpoint directory (config.json + *.safetensors)
+                from ..models.loader import load_model
+                self.model, src = load_model(model, device=device, expert_sink=sink, cfg=cfg)
+                src.close()
+            else:
+                self.model = build_model(cfg, device=device, seed=seed, expert_sink=sink, num_layers=num_layers)
         if tiering is not None:
             tiering.attach(self.model)
         self.tiering = tiering

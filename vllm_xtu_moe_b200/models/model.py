@@ -240,8 +240,15 @@ class WeightFactory:
         t = torch.randn(*shape, generator=g, device=self.device, dtype=torch.float32 if self.device.type == "cpu" else dtype)
         return (t * (std if std is not None else self.std)).to(dtype)
 
-    def ones(self, shape, dtype=torch.bfloat16):
+    def ones(self, shape, dtype=torch.bfloat16, name: str | None = None):
         return torch.ones(*shape, dtype=dtype, device=self.device)
+
+    def zeros(self, shape, dtype=torch.bfloat16, name: str | None = None):
+        return torch.zeros(*shape, dtype=dtype, device=self.device)
+
+    def param(self, name: str, make):
+        """A tensor with a fixed synthetic value (``make()``); checkpoint sources load it by name."""
+        return make()
 
     def linear(self, name, n, k, fmt="bf16", bias=False, std=None) -> Linear:
         std = std if std is not None else self.std
@@ -304,9 +311,9 @@ def hash_str(s: str) -> int:
     return h
 
 
-def _norm(f: WeightFactory, cfg, shape, add_one=None):
+def _norm(f: WeightFactory, cfg, shape, name: str, add_one=None):
     add = cfg.norm_add_one if add_one is None else add_one
-    w = torch.zeros(*shape, dtype=torch.bfloat16, device=f.device) if add else f.ones(shape)
+    w = f.zeros(shape, name=name) if add else f.ones(shape, name=name)
     return RMSNorm(w, cfg.norm_eps, add)
 
 
@@ -333,29 +340,29 @@ def build_layer(f: WeightFactory, cfg: ModelConfig, i: int, expert_sink=None, na
         attn = GatedDeltaNet(cfg, f.linear(name + ".qkvz", 2 * nk * dk + 2 * nv * dv, H, dfmt),
                              f.linear(name + ".ba", 2 * nv, H, "bf16"),
                              f.normal(name + ".conv", (ch, cfg.linear_conv_kernel), 0.3),
-                             torch.log(torch.linspace(1.0, 16.0, nv, device=f.device)).float(),
-                             torch.zeros(nv, device=f.device).float(),
-                             f.ones((dv,)), f.linear(name + ".out", H, nv * dv, dfmt))
+                             f.param(name + ".A_log", lambda: torch.log(torch.linspace(1.0, 16.0, nv,
+                                                                                      device=f.device)).float()),
+                             f.param(name + ".dt_bias", lambda: torch.zeros(nv, device=f.device).float()),
+                             f.ones((dv,), name=name + ".gdn_norm"), f.linear(name + ".out", H, nv * dv, dfmt))
     elif cfg.is_mla:
         nh = cfg.num_heads
         q_a = f.linear(name + ".q_a", cfg.q_lora_rank, H, dfmt) if cfg.q_lora_rank else None
-        attn = MLAAttention(cfg, q_a, f.ones((cfg.q_lora_rank,)) if q_a else None,
+        attn = MLAAttention(cfg, q_a, f.ones((cfg.q_lora_rank,), name=name + ".q_a_norm") if q_a else None,
                             f.linear(name + ".q_b", nh * (cfg.qk_nope_head_dim + cfg.qk_rope_head_dim),
                                      cfg.q_lora_rank or H, dfmt),
                             f.linear(name + ".kv_a", cfg.kv_lora_rank + cfg.qk_rope_head_dim, H, dfmt),
-                            f.ones((cfg.kv_lora_rank,)),
+                            f.ones((cfg.kv_lora_rank,), name=name + ".kv_a_norm"),
                             f.linear(name + ".kv_b", nh * (cfg.qk_nope_head_dim + cfg.v_head_dim), cfg.kv_lora_rank,
                                      dfmt),
                             f.linear(name + ".o", H, nh * cfg.v_head_dim, dfmt))
     else:
         nh, nkv, hd = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim
         qdim = nh * hd * (2 if cfg.attn_output_gate else 1)
+        qkn = (f.zeros if cfg.norm_add_one else f.ones) if cfg.qk_norm else None
         attn = GQAAttention(cfg, f.linear(name + ".qkv", qdim + 2 * nkv * hd, H, dfmt, bias=cfg.qkv_bias),
                             f.linear(name + ".o", H, nh * hd, dfmt),
-                            f.ones((hd,)) if cfg.qk_norm and not cfg.norm_add_one else
-                            (torch.zeros(hd, dtype=torch.bfloat16, device=f.device) if cfg.qk_norm else None),
-                            f.ones((hd,)) if cfg.qk_norm and not cfg.norm_add_one else
-                            (torch.zeros(hd, dtype=torch.bfloat16, device=f.device) if cfg.qk_norm else None))
+                            qkn((hd,), name=name + ".q_norm") if qkn else None,
+                            qkn((hd,), name=name + ".k_norm") if qkn else None)
     if cfg.is_moe_layer(min(i, cfg.num_layers - 1)):
         E, I = cfg.num_experts, cfg.moe_intermediate
         gate = f.normal(name + ".router", (E, H), 0.02)
@@ -376,15 +383,18 @@ def build_layer(f: WeightFactory, cfg: ModelConfig, i: int, expert_sink=None, na
         mlp = MoEBlock(cfg, i, gate, bias, experts, shared, sgate)
     else:
         mlp = _dense_mlp(f, name + ".mlp", H, cfg.dense_intermediate, dfmt, cfg.swiglu_limit)
-    return DecoderLayer(i, _norm(f, cfg, (H,)), attn, _norm(f, cfg, (H,)), mlp, kind)
+    return DecoderLayer(i, _norm(f, cfg, (H,), name + ".attn_norm"), attn, _norm(f, cfg, (H,), name + ".mlp_norm"),
+                        mlp, kind)
 
 
 def build_model(cfg: ModelConfig, device="cpu", seed: int = 0, expert_sink=None, std: float = 0.02,
-                num_layers: int | None = None) -> MoETransformer:
-    """Random-init model in kernel layout.  ``expert_sink(layer, raw)`` may take
-    the routed experts elsewhere (CPU engine / host tier) and return what the
-    MoE block should hold (None when no expert stays GPU-resident)."""
-    f = WeightFactory(seed, device, std)
+                num_layers: int | None = None, source=None) -> MoETransformer:
+    """Model in kernel layout, from seeded random init (default) or from ``source``
+    (a checkpoint source with the factory's interface, see ``models.loader``).
+    ``expert_sink(layer, raw)`` may take the routed experts elsewhere (CPU engine /
+    host tier) and return what the MoE block should hold (None when no expert stays
+    GPU-resident)."""
+    f = source if source is not None else WeightFactory(seed, device, std)
     H = cfg.hidden_size
     n = cfg.num_layers if num_layers is None else num_layers
     embed = f.normal("model.embed", (cfg.vocab_size, H), 1.0)
@@ -393,6 +403,7 @@ def build_model(cfg: ModelConfig, device="cpu", seed: int = 0, expert_sink=None,
     mtp = []
     for j in range(cfg.num_mtp_layers):
         layer = build_layer(f, cfg, cfg.num_layers - 1, expert_sink, name_prefix=f"model.mtp{j}")
-        mtp.append(MTPLayer(_norm(f, cfg, (H,)), _norm(f, cfg, (H,)), f.linear(f"mtp{j}.eh", H, 2 * H, cfg.dense_fmt),
-                            layer, _norm(f, cfg, (H,))))
-    return MoETransformer(cfg, embed, layers, _norm(f, cfg, (H,)), lm_head, mtp)
+        mtp.append(MTPLayer(_norm(f, cfg, (H,), f"model.mtp{j}.enorm"), _norm(f, cfg, (H,), f"model.mtp{j}.hnorm"),
+                            f.linear(f"mtp{j}.eh", H, 2 * H, cfg.dense_fmt), layer,
+                            _norm(f, cfg, (H,), f"model.mtp{j}.head_norm")))
+    return MoETransformer(cfg, embed, layers, _norm(f, cfg, (H,), "model.norm"), lm_head, mtp)
