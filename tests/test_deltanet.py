@@ -1,0 +1,62 @@
+"""Gated DeltaNet kernels (conv + L2 norm + gated delta rule) against the PyTorch
+per-token recurrence, across chunked prefill and decode of several sequences."""
+import math
+
+import pytest
+import torch
+
+from vllm_xtu_moe_b200.models.config import get_preset, scaled_down
+from vllm_xtu_moe_b200.models.deltanet import DeltaNetState, deltanet_ref
+from vllm_xtu_moe_b200.ops.attention import AttnMetadata
+
+
+def _meta(lens, starts, slots, device):
+    qs = [0]
+    for L in lens:
+        qs.append(qs[-1] + L)
+    d = device
+    return AttnMetadata(num_seqs=len(lens), q_start=torch.tensor(qs, dtype=torch.int32, device=d),
+                        kv_len=torch.tensor([s + L for s, L in zip(starts, lens)], dtype=torch.int32, device=d),
+                        block_table=torch.zeros(len(lens), 1, dtype=torch.int32, device=d),
+                        slot_mapping=torch.zeros(qs[-1], dtype=torch.int32, device=d),
+                        positions=torch.zeros(qs[-1], dtype=torch.int32, device=d), max_q_len=max(lens),
+                        max_kv_len=max(s + L for s, L in zip(starts, lens)), is_decode=False, q_start_host=qs,
+                        seq_slots=torch.tensor(slots, dtype=torch.int32, device=d),
+                        seq_fresh=torch.tensor([1 if s == 0 else 0 for s in starts], dtype=torch.int32, device=d))
+
+
+@pytest.mark.gpu
+def test_deltanet_kernels_match_reference():
+    from vllm_xtu_moe_b200.ops.deltanet import deltanet_fwd
+    torch.manual_seed(0)
+    cfg = scaled_down(get_preset("qwen3-next-80b-a3b"), layers=4, hidden=256, experts=8).replace(
+        linear_num_key_heads=2, linear_num_value_heads=4, linear_key_head_dim=128, linear_value_head_dim=128)
+    nk, nv, dk, dv, kw = 2, 4, 128, 128, cfg.linear_conv_kernel
+    r = nv // nk
+    W = 2 * dk + 2 * r * dv
+    ch = 2 * nk * dk + nv * dv
+    conv_w = (torch.randn(ch, kw) * 0.3).cuda()
+    st_gpu = DeltaNetState(cfg, 4, "cuda")
+    st_ref = DeltaNetState(cfg, 4, "cuda")
+    # step 1: two fresh sequences (prefill chunks); step 2: continue both + decode; step 3: decode only
+    plan = [([37, 130], [0, 0], [2, 0]), ([5, 1], [37, 130], [2, 0]), ([1, 1], [42, 131], [2, 0])]
+    for lens, starts, slots in plan:
+        T = sum(lens)
+        qkvz = (torch.randn(T, nk * W) * 0.5).to(torch.bfloat16).cuda()
+        g = -torch.rand(T, nv).cuda() * 0.5
+        beta = torch.rand(T, nv).cuda()
+        meta = _meta(lens, starts, slots, "cuda")
+        og = deltanet_fwd(qkvz, conv_w, g, beta, meta, st_gpu, nk, nv, dk, dv)
+        x = qkvz.view(T, nk, W)
+        q = x[:, :, :dk].reshape(T, nk * dk)
+        k = x[:, :, dk:2 * dk].reshape(T, nk * dk)
+        v = x[:, :, 2 * dk:2 * dk + r * dv].reshape(T, nv * dv)
+        mixed = torch.cat([q, k, v], -1)
+        orf = deltanet_ref(mixed, conv_w, g, beta, meta, st_ref, nk, nv, dk, dv)
+        torch.cuda.synchronize()
+        err = (og - orf).abs().max().item() / orf.abs().max().item()
+        assert err < 2e-3, (lens, err)
+        for s in slots:
+            es = (st_gpu.ssm[s] - st_ref.ssm[s]).abs().max().item() / st_ref.ssm[s].abs().max().item()
+            assert es < 2e-3
+            assert torch.equal(st_gpu.conv[s], st_ref.conv[s])

@@ -177,6 +177,34 @@ def bench_attn_prefill(T=8192, Hq=96, Hkv=8, D=128, iters=5) -> dict:
     return _report("attention_prefill_causal", dict(T=T, Hq=Hq, Hkv=Hkv, D=D), ms, nbytes, flops)
 
 
+def bench_deltanet(T=15000, nk=16, nv=32, dk=128, dv=128, kw=4, iters=3) -> dict:
+    """Qwen3-Next linear-attention layer core (conv + gated delta rule) over one long prompt."""
+    from .models.config import get_preset
+    from .models.deltanet import DeltaNetState
+    from .ops.deltanet import deltanet_fwd
+    cfg = get_preset("qwen3-next-80b-a3b")
+    r = nv // nk
+    W = 2 * dk + 2 * r * dv
+    d = "cuda"
+    qkvz = (torch.randn(T, nk * W, device=d) * 0.5).to(torch.bfloat16)
+    conv_w = torch.randn(2 * nk * dk + nv * dv, kw, device=d) * 0.3
+    g = -torch.rand(T, nv, device=d) * 0.5
+    beta = torch.rand(T, nv, device=d)
+    st = DeltaNetState(cfg, 1, d)
+    meta = AttnMetadata(num_seqs=1, q_start=torch.tensor([0, T], dtype=torch.int32, device=d),
+                        kv_len=torch.tensor([T], dtype=torch.int32, device=d),
+                        block_table=torch.zeros(1, 1, dtype=torch.int32, device=d),
+                        slot_mapping=torch.zeros(T, dtype=torch.int32, device=d),
+                        positions=torch.zeros(T, dtype=torch.int32, device=d), max_q_len=T, max_kv_len=T,
+                        is_decode=False, seq_slots=torch.zeros(1, dtype=torch.int32, device=d),
+                        seq_fresh=torch.ones(1, dtype=torch.int32, device=d))
+    fn = lambda: deltanet_fwd(qkvz, conv_w, g, beta, meta, st, nk, nv, dk, dv)
+    ms = time_fn(fn, iters)
+    flops = T * nv * dk * dv * 2 * 4
+    nbytes = qkvz.numel() * 2 + T * nv * dv * 4
+    return _report("deltanet_prefill", dict(T=T, nk=nk, nv=nv, dk=dk, dv=dv), ms, nbytes, flops)
+
+
 def bench_rmsnorm(T=16384, H=4096, iters=20) -> dict:
     x = torch.randn(T, H, device="cuda").to(torch.bfloat16)
     r = torch.randn(T, H, device="cuda").to(torch.bfloat16)
@@ -196,6 +224,7 @@ OPS = {
     "attention_decode": lambda a: bench_attn_decode(),
     "attention_prefill": lambda a: bench_attn_prefill(min(a.tokens, 16384)),
     "rmsnorm": lambda a: bench_rmsnorm(),
+    "deltanet_prefill": lambda a: bench_deltanet(),
 }
 
 

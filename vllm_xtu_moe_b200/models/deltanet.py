@@ -14,7 +14,7 @@ concatenated q/k/v channels first.  Recurrent state and conv state are kept
 per request slot between steps (``DeltaNetState``).
 
 The per-token recurrence in ``_delta_rule_ref`` is the numerics oracle; on a
-GPU the chunked/recurrent kernels of ``csrc/cuda/deltanet.cu`` run.
+GPU (key head dim 128) the conv / recurrence kernels of ``csrc/cuda/deltanet.cu`` run.
 """
 from __future__ import annotations
 
@@ -86,10 +86,17 @@ class GatedDeltaNet:
         qkvz = self.in_qkvz(x)
         ba = self.in_ba(x)
         q, k, v, z, b, a = self._split(qkvz, ba)
-        mixed = torch.cat([q, k, v], dim=-1)            # [T, channels]
         beta = torch.sigmoid(b.float())
         g = -torch.exp(self.A_log.float()) * F.softplus(a.float() + self.dt_bias.float())
-        o = self._core(mixed, g, beta, meta, state)     # [T, nv, dv] fp32
+        if x.is_cuda and N.has_symbol("xtu_deltanet_fwd") and self.dk == 128:
+            from ..ops.deltanet import deltanet_fwd
+            if getattr(self, "_conv_w32", None) is None or self._conv_w32.device != x.device:
+                self._conv_w32 = self.conv_w.float().contiguous()
+            o = deltanet_fwd(qkvz.contiguous(), self._conv_w32, g, beta, meta, state, self.nk, self.nv, self.dk,
+                             self.dv)
+        else:
+            mixed = torch.cat([q, k, v], dim=-1)        # [T, channels]
+            o = self._core(mixed, g, beta, meta, state)  # [T, nv, dv] fp32
         o = self._gated_norm(o, z)
         return self.out(o.reshape(T, self.nv * self.dv))
 
@@ -100,10 +107,7 @@ class GatedDeltaNet:
         return y.to(torch.bfloat16)
 
     def _core(self, mixed, g, beta, meta, state):
-        if mixed.is_cuda and N.has_symbol("xtu_deltanet_fwd"):
-            from ..ops.deltanet import deltanet_fwd
-            return deltanet_fwd(mixed, self.conv_w, g, beta, meta, state, self.nk, self.nv, self.dk, self.dv)
-        if mixed.is_cuda and N.native_required():
+        if mixed.is_cuda and N.native_required() and self.dk == 128:
             raise N.NativeLibraryMissing("xtu_deltanet_fwd missing from the CUDA library")
         return deltanet_ref(mixed, self.conv_w, g, beta, meta, state, self.nk, self.nv, self.dk, self.dv)
 

@@ -47,6 +47,8 @@ _SIGS: dict[str, list] = {
     "xtu_embed": [P, P, c_int, c_int, c_int, P, P],
     "xtu_route_split": [P, c_int, c_int, c_int, P, P, P, P, P],
     "xtu_spec_verify": [P, P, P, c_int, c_int, P, P, P],
+    "xtu_deltanet_fwd": [P, c_int, c_int, c_int, P, P, P, c_int, c_int, c_int, c_int, c_int, P, P, P, P, P,
+                         P, P, P, P, P],
     "xtu_grouped_gemm_ex": [P, P, P, c_int, P, c_int, c_int, c_int, c_int, c_int, P, P, c_int, c_int, P, P,
                             c_float, c_float, c_float, P, c_int, P, P],
     "xtu_ipc_handle_size": [],
