@@ -52,7 +52,8 @@ struct AttnParams {
   int rf;                  // row replication factor (1, 2, 4): replicas split each tile's keys
   float scale_log2;        // softmax scale * log2(e)
   int splits;
-  float* ws_o;             // [splits, T, Hq, DV] (splits > 1)
+  int dv_total, dv_halves;  // output width per head; CTAs that split it (MLA: 2 x 256 of 512)
+  float* ws_o;             // [splits, T, Hq, dv_total] (splits > 1)
   float* ws_lse;           // [splits, T, Hq]
   int T;
   XtuStatus* status;
@@ -61,20 +62,22 @@ struct AttnParams {
 // STAGES: K/V ring depth.  BTS: block-table entries staged in shared memory (0 = read
 // the table from global memory on the fly); decode configurations prefetch the CTA's
 // whole block list so the producer never waits on a dependent global load.
-template <int D, int DV, int BN, int STAGES_ = 2, int BTS = 0>
+// VK: V is the first dims of K (MLA latent cache) and is read from the K stage itself;
+// the CTA then computes DV output columns starting at its half's offset.
+template <int D, int DV, int BN, int STAGES_ = 2, int BTS = 0, int VK = 0>
 struct AttnCfg {
   static constexpr int STAGES = STAGES_;
   static constexpr int Q_BYTES = 128 * D * 2;
   static constexpr int K_BYTES = BN * D * 2;
-  static constexpr int V_BYTES = BN * DV * 2;
-  static constexpr int P_BYTES = 128 * BN * 2;
+  static constexpr int V_BYTES = VK ? 0 : BN * DV * 2;
+  static constexpr int P_BYTES = 128 * (BN < 64 ? 64 : BN) * 2;   // rows padded to one 128-B swizzle atom
   static constexpr int BT_BYTES = BTS * 4;
   static constexpr int SMEM = Q_BYTES + STAGES * (K_BYTES + V_BYTES) + 2 * P_BYTES + BT_BYTES + 1024 + 256;
   static constexpr int S_COL0 = 0;          // two S buffers: [0, BN), [BN, 2BN)
   static constexpr int O_COL0 = 2 * BN;     // O: [2BN, 2BN + DV)
   static constexpr int TMEM_COLS = (2 * BN + DV) <= 256 ? 256 : 512;
   static_assert(2 * BN + DV <= 512, "TMEM budget");
-  static_assert(D % 64 == 0 && DV % 64 == 0 && BN % 64 == 0, "tile shapes");
+  static_assert(D % 64 == 0 && DV % 64 == 0 && BN % 16 == 0 && (BN % 64 == 0 || 64 % BN == 0), "tile shapes");
 };
 
 // write 8 bf16 (16 B) at (row, col8) of a K-major SW128 operand tile [rows][64-col chunks]
@@ -85,11 +88,11 @@ __device__ __forceinline__ void st_sw128(uint8_t* tile, int rows, int row, int c
   *reinterpret_cast<uint4*>(base + ((piece ^ (row & 7)) << 4)) = v;
 }
 
-template <int D, int DV, int BN, int STAGES_, int BTS>
+template <int D, int DV, int BN, int STAGES_, int BTS, int VK>
 __global__ void __launch_bounds__(192, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
                     AttnParams p) {
-  using C = AttnCfg<D, DV, BN, STAGES_, BTS>;
+  using C = AttnCfg<D, DV, BN, STAGES_, BTS, VK>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
@@ -110,7 +113,9 @@ __global__ void __launch_bounds__(192, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = blockIdx.z;
   const int kvh = blockIdx.y % p.Hkv;
-  const int split = blockIdx.y / p.Hkv;
+  const int split = (blockIdx.y / p.Hkv) % p.splits;
+  const int dv_off = VK ? (blockIdx.y / (p.Hkv * p.splits)) * DV : 0;   // this CTA's output columns
+  const int dv_tot = p.dv_total;
   const int q0 = p.q_start[b];
   const int q_len = p.q_start[b + 1] - q0;
   const int kv_len = p.kv_len[b];
@@ -136,8 +141,8 @@ __global__ void __launch_bounds__(192, 1)
   }
   if (warp == 1) tmem_alloc(tmem_slot, C::TMEM_COLS);
   const int n_blocks_seq = (kv_len + KV_BLOCK - 1) / KV_BLOCK;
-  const int lb0 = t_begin * (BN / KV_BLOCK);
-  const int n_lb = n_tiles * (BN / KV_BLOCK);
+  const int lb0 = (t_begin * BN) / KV_BLOCK;                       // first logical block of this CTA
+  const int n_lb = n_tiles > 0 ? (t_end * BN + KV_BLOCK - 1) / KV_BLOCK - lb0 : 0;
   if (BTS > 0 && warp == 0) {
     const int* bt = p.block_table + (size_t)b * p.bt_stride;
     for (int i = lane; i < n_lb && i < BTS; i += 32) {
@@ -160,6 +165,28 @@ __global__ void __launch_bounds__(192, 1)
         if (!mbar_wait(&kv_empty[stage], ph ^ 1u, p.status, 100)) break;
         mbar_arrive_expect_tx(&kv_full[stage], C::K_BYTES + C::V_BYTES);
         const int j = t_begin + jj;
+        if (BN < KV_BLOCK) {
+          // a tile is a slice of one 64-token block (the tensor map's box is BN rows)
+          int lb = (j * BN) / KV_BLOCK;
+          const int off = (j * BN) % KV_BLOCK;
+          int blk;
+          if (BTS > 0 && lb - lb0 < BTS) {
+            blk = sBT[lb - lb0];
+          } else {
+            if (lb >= n_blocks_seq) lb = 0;
+            blk = bt[lb];
+          }
+          const int row = (blk * p.Hkv + kvh) * KV_BLOCK + off;
+#pragma unroll
+          for (int c = 0; c < D / 64; ++c)
+            tma_load_2d(sK + stage * C::K_BYTES + c * (BN * 128), &tmap_k, &kv_full[stage], c * 64, row);
+          if (!VK) {
+#pragma unroll
+            for (int c = 0; c < DV / 64; ++c)
+              tma_load_2d(sV + stage * C::V_BYTES + c * (BN * 128), &tmap_v, &kv_full[stage], c * 64, row);
+          }
+          continue;
+        }
 #pragma unroll
         for (int sb = 0; sb < BN / KV_BLOCK; ++sb) {
           int lb = j * (BN / KV_BLOCK) + sb;
@@ -175,10 +202,12 @@ __global__ void __launch_bounds__(192, 1)
           for (int c = 0; c < D / 64; ++c)
             tma_load_2d(sK + stage * C::K_BYTES + c * (BN * 128) + sb * (KV_BLOCK * 128), &tmap_k, &kv_full[stage],
                         c * 64, row);
+          if (!VK) {
 #pragma unroll
-          for (int c = 0; c < DV / 64; ++c)
-            tma_load_2d(sV + stage * C::V_BYTES + c * (BN * 128) + sb * (KV_BLOCK * 128), &tmap_v, &kv_full[stage],
-                        c * 64, row);
+            for (int c = 0; c < DV / 64; ++c)
+              tma_load_2d(sV + stage * C::V_BYTES + c * (BN * 128) + sb * (KV_BLOCK * 128), &tmap_v,
+                          &kv_full[stage], c * 64, row);
+          }
         }
       }
     }
@@ -211,7 +240,8 @@ __global__ void __launch_bounds__(192, 1)
           if (!mbar_wait(&p_full[pj & 1], (pj >> 1) & 1, p.status, 112)) { ok = false; break; }
           tc_fence_after();
           const int stage = pj % C::STAGES;
-          const uint32_t v_addr = smem_u32(sV + stage * C::V_BYTES);
+          const uint32_t v_addr = VK ? smem_u32(sK + stage * C::K_BYTES + (dv_off / 64) * (BN * 128))
+                                     : smem_u32(sV + stage * C::V_BYTES);
           const uint32_t p_addr = smem_u32(sP + (pj & 1) * C::P_BYTES);
 #pragma unroll
           for (int k = 0; k < BN / 16; ++k) {
@@ -389,7 +419,7 @@ __global__ void __launch_bounds__(192, 1)
           tmem_wait_ld();
           if (!row_valid) continue;
           if (p.splits == 1) {
-            __nv_bfloat16* dst = p.o + (size_t)tok * p.o_stride + (size_t)head * DV;
+            __nv_bfloat16* dst = p.o + (size_t)tok * p.o_stride + (size_t)head * dv_tot + dv_off;
             uint32_t pk[16];
 #pragma unroll
             for (int t = 0; t < 16; ++t)
@@ -398,7 +428,7 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
             for (int t = 0; t < 4; ++t) d4[t] = make_uint4(pk[4 * t], pk[4 * t + 1], pk[4 * t + 2], pk[4 * t + 3]);
           } else {
-            float4* d4 = reinterpret_cast<float4*>(p.ws_o + (((size_t)split * p.T + tok) * p.Hq + head) * DV + c);
+            float4* d4 = reinterpret_cast<float4*>(p.ws_o + (((size_t)split * p.T + tok) * p.Hq + head) * dv_tot + dv_off + c);
 #pragma unroll
             for (int t = 0; t < 8; ++t)
               d4[t] = make_float4(__uint_as_float(v[4 * t]) * inv, __uint_as_float(v[4 * t + 1]) * inv,
@@ -408,7 +438,7 @@ __global__ void __launch_bounds__(192, 1)
         if (p.splits > 1 && row_valid)
           p.ws_lse[((size_t)split * p.T + tok) * p.Hq + head] = l > 0.f ? m + log2f(l) : -FLT_MAX;
       } else if (n_tiles == 0 && p.splits > 1 && row_valid) {
-        float* dst = p.ws_o + (((size_t)split * p.T + tok) * p.Hq + head) * DV;
+        float* dst = p.ws_o + (((size_t)split * p.T + tok) * p.Hq + head) * dv_tot + dv_off;
         for (int c = 0; c < DV; ++c) dst[c] = 0.f;
         p.ws_lse[((size_t)split * p.T + tok) * p.Hq + head] = -FLT_MAX;
       }
@@ -444,7 +474,7 @@ __global__ void __launch_bounds__(192, 1)
       if (part == 0 && row_valid && ok) {
         const float* src = oacc + lr * DV;
         if (p.splits == 1) {
-          __nv_bfloat16* dst = p.o + (size_t)tok * p.o_stride + (size_t)head * DV;
+          __nv_bfloat16* dst = p.o + (size_t)tok * p.o_stride + (size_t)head * dv_tot + dv_off;
           for (int c = 0; c < DV; c += 8) {
             uint4 o;
             o.x = pack_bf16x2(src[c], src[c + 1]); o.y = pack_bf16x2(src[c + 2], src[c + 3]);
@@ -452,13 +482,13 @@ __global__ void __launch_bounds__(192, 1)
             *reinterpret_cast<uint4*>(dst + c) = o;
           }
         } else {
-          float* dst = p.ws_o + (((size_t)split * p.T + tok) * p.Hq + head) * DV;
+          float* dst = p.ws_o + (((size_t)split * p.T + tok) * p.Hq + head) * dv_tot + dv_off;
           for (int c = 0; c < DV; ++c) dst[c] = src[c];
           p.ws_lse[((size_t)split * p.T + tok) * p.Hq + head] = L > 0.f ? M + log2f(L) : -FLT_MAX;
         }
       }
     } else if (p.splits > 1 && row_valid && part == 0) {
-      float* dst = p.ws_o + (((size_t)split * p.T + tok) * p.Hq + head) * DV;
+      float* dst = p.ws_o + (((size_t)split * p.T + tok) * p.Hq + head) * dv_tot + dv_off;
       for (int c = 0; c < DV; ++c) dst[c] = 0.f;
       p.ws_lse[((size_t)split * p.T + tok) * p.Hq + head] = -FLT_MAX;
     }
@@ -515,14 +545,15 @@ static PFN_encodeTiled_t attn_encode_fn() {
   return fn;
 }
 
-// cache viewed as [rows = blocks*Hkv*64, dim] bf16 with row pitch `pitch` elements; box {64 cols, 64 rows}
-static int attn_tmap(CUtensorMap* map, const void* base, uint64_t rows, uint64_t dim, uint64_t pitch) {
+// cache viewed as [rows = blocks*Hkv*64, dim] bf16 with row pitch `pitch` elements; box {64 cols, box_rows}
+static int attn_tmap(CUtensorMap* map, const void* base, uint64_t rows, uint64_t dim, uint64_t pitch,
+                     uint32_t box_rows = 64) {
   PFN_encodeTiled_t enc = attn_encode_fn();
   if (!enc) return -100;
   if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (pitch * 2) % 16 != 0) return -101;
   cuuint64_t dims[2] = {dim, rows};
   cuuint64_t strides[1] = {pitch * 2};
-  cuuint32_t box[2] = {64, 64};
+  cuuint32_t box[2] = {64, box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -530,18 +561,18 @@ static int attn_tmap(CUtensorMap* map, const void* base, uint64_t rows, uint64_t
   return r == CUDA_SUCCESS ? 0 : -1000 - (int)r;
 }
 
-template <int D, int DV, int BN, int STAGES = 2, int BTS = 0>
+template <int D, int DV, int BN, int STAGES = 2, int BTS = 0, int VK = 0>
 static int launch_attn(const CUtensorMap& tk, const CUtensorMap& tv, const AttnParams& p, int grid_x, int B,
                        cudaStream_t s) {
-  using C = AttnCfg<D, DV, BN, STAGES, BTS>;
-  auto k = attn_fwd_kernel<D, DV, BN, STAGES, BTS>;
+  using C = AttnCfg<D, DV, BN, STAGES, BTS, VK>;
+  auto k = attn_fwd_kernel<D, DV, BN, STAGES, BTS, VK>;
   static bool init = false;
   if (!init) {
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (e != cudaSuccess) return -(int)e;
     init = true;
   }
-  dim3 grid(grid_x, p.Hkv * p.splits, B);
+  dim3 grid(grid_x, p.Hkv * p.splits * p.dv_halves, B);
   k<<<grid, 192, C::SMEM, s>>>(tk, tv, p);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 1 : -(int)e;
@@ -574,11 +605,17 @@ int xtu_paged_attention(const void* q, int q_stride, const void* k_cache, const 
     p.ws_o = ws;
     p.ws_lse = ws + (size_t)p.splits * T * Hq * DV;
   }
+  // MLA latent cache (576 = 512 latent + 64 rope, V = the latent): 16-key tiles read once
+  // into shared memory serve both QK^T and PV; two CTAs split the 512 output columns
+  const bool mla = v_is_k && D == 576 && DV == 512;
+  p.dv_total = DV;
+  p.dv_halves = mla ? 2 : 1;
   const uint64_t rows = (uint64_t)num_blocks * Hkv * KV_BLOCK;
   CUtensorMap tk, tv;
-  int rc = attn_tmap(&tk, k_cache, rows, D, D);
+  int rc = attn_tmap(&tk, k_cache, rows, D, D, mla ? 16 : 64);
   if (rc) return rc;
-  rc = v_is_k ? attn_tmap(&tv, k_cache, rows, DV, D) : attn_tmap(&tv, v_cache, rows, DV, DV);
+  if (mla) tv = tk;
+  else rc = v_is_k ? attn_tmap(&tv, k_cache, rows, DV, D) : attn_tmap(&tv, v_cache, rows, DV, DV);
   if (rc) return rc;
   const int pos_per_tile = p.rows_per_tile / G;
   const int grid_x = (max_q_len + pos_per_tile - 1) / pos_per_tile;
@@ -592,7 +629,8 @@ int xtu_paged_attention(const void* q, int q_stride, const void* k_cache, const 
   // every replica scores a multiple of 16 keys per tile (the softmax reads S in 16-column chunks)
   const int bn = (decode_shape && D == 64) ? 64 : 128;
   while (p.rf > 1 && (bn / p.rf) % 16 != 0) p.rf >>= 1;
-  if (decode_shape && D == 128 && DV == 128) r = launch_attn<128, 128, 128, 2, 256>(tk, tv, p, grid_x, B, s);
+  if (mla) r = launch_attn<576, 256, 16, 2, 1024, 1>(tk, tv, p, grid_x, B, s);
+  else if (decode_shape && D == 128 && DV == 128) r = launch_attn<128, 128, 128, 2, 256>(tk, tv, p, grid_x, B, s);
   else if (decode_shape && D == 64 && DV == 64) r = launch_attn<64, 64, 64, 6, 1024>(tk, tv, p, grid_x, B, s);
   else if (D == 128 && DV == 128) r = launch_attn<128, 128, 128>(tk, tv, p, grid_x, B, s);
   else if (D == 64 && DV == 64) r = launch_attn<64, 64, 128>(tk, tv, p, grid_x, B, s);

@@ -160,6 +160,28 @@ def bench_attn_decode(Bn=4, kv=15000, Hq=96, Hkv=8, D=128, iters=20) -> dict:
                    nbytes, flops)
 
 
+def bench_mla_decode(Bn=4, kv=15000, Hq=128, iters=20) -> dict:
+    """DeepSeek-V3 absorbed MLA decode over the 576-wide latent cache (V = first 512 dims)."""
+    d = "cuda"
+    nb_per = (kv + 63) // 64
+    kc = (torch.randn(Bn * nb_per, 1, 64, 576, device=d) * 0.5).to(torch.bfloat16)
+    bt = torch.arange(Bn * nb_per, dtype=torch.int32, device=d).view(Bn, nb_per)
+    q = (torch.randn(Bn, Hq, 576, device=d) * 0.5).to(torch.bfloat16)
+    meta = AttnMetadata(num_seqs=Bn, q_start=torch.arange(Bn + 1, dtype=torch.int32, device=d),
+                        kv_len=torch.full((Bn,), kv, dtype=torch.int32, device=d), block_table=bt,
+                        slot_mapping=torch.zeros(Bn, dtype=torch.int32, device=d),
+                        positions=torch.full((Bn,), kv - 1, dtype=torch.int32, device=d), max_q_len=1,
+                        max_kv_len=kv, is_decode=True)
+    meta.num_splits = A.choose_splits(Bn, 2, kv)
+    ws = torch.empty(A.num_split_workspace(Bn, Hq, 512, meta.num_splits), dtype=torch.float32, device=d)
+    out = torch.empty(Bn, Hq, 512, dtype=torch.bfloat16, device=d)
+    fn = lambda: A.paged_attention(q, kc, None, meta, 1.0 / 192 ** 0.5, v_dim=512, out=out, workspace=ws)
+    ms = time_fn(fn, iters)
+    nbytes = Bn * kv * 576 * 2
+    flops = 2 * Bn * Hq * kv * (576 + 512)
+    return _report("mla_decode", dict(B=Bn, kv=kv, Hq=Hq, splits=meta.num_splits), ms, nbytes, flops)
+
+
 def bench_attn_prefill(T=8192, Hq=96, Hkv=8, D=128, iters=5) -> dict:
     kc, vc, bt = _cache(1, T, Hkv, D)
     q = (torch.randn(T, Hq, D, device="cuda") * 0.5).to(torch.bfloat16)
@@ -222,6 +244,7 @@ OPS = {
     "gemm_fp8": lambda a: bench_gemm(a.tokens, 14336, 4096, "fp8"),
     "gemm_bf16": lambda a: bench_gemm(a.tokens, 14336, 4096, "bf16"),
     "attention_decode": lambda a: bench_attn_decode(),
+    "mla_decode": lambda a: bench_mla_decode(),
     "attention_prefill": lambda a: bench_attn_prefill(min(a.tokens, 16384)),
     "rmsnorm": lambda a: bench_rmsnorm(),
     "deltanet_prefill": lambda a: bench_deltanet(),

@@ -84,6 +84,43 @@ class MLAAttention:
         k_cache[blk[valid], 0, off[valid]] = entry[valid, 0].to(k_cache.dtype)
 
     def _prefill(self, q_nope, q_rope, meta, k_cache):
+        if q_nope.is_cuda and (self.dn + self.dr, self.dv) in ((192, 128), (128, 128), (64, 64), (256, 256)):
+            return self._prefill_flash(q_nope, q_rope, meta, k_cache)
+        return self._prefill_ref(q_nope, q_rope, meta, k_cache)
+
+    def _prefill_flash(self, q_nope, q_rope, meta, k_cache):
+        """Expand each sequence's latent context into per-head K [n, nh, dn+dr] and V
+        [n, nh, dv], lay them out as a paged cache of 64-token blocks, and run the causal
+        flash kernel (no [q, k] score matrix is ever materialised)."""
+        nh, dn, dr, dv, dc = self.nh, self.dn, self.dr, self.dv, self.dc
+        T = q_nope.shape[0]
+        qs = meta.q_start_host if meta.q_start_host is not None else meta.q_start.tolist()
+        kl = meta.kv_len_host if meta.kv_len_host is not None else meta.kv_len.tolist()
+        out = torch.empty(T, nh, dv, dtype=torch.bfloat16, device=q_nope.device)
+        bs = k_cache.shape[2]
+        d = q_nope.device
+        for b in range(meta.num_seqs):
+            s0, s1 = qs[b], qs[b + 1]
+            if s1 == s0:
+                continue
+            n = kl[b]
+            nb = (n + bs - 1) // bs
+            ent = k_cache[meta.block_table[b, :nb].long(), 0].reshape(nb * bs, dc + dr)
+            kvb = self.kv_b(ent[:, :dc].contiguous()).view(nb * bs, nh, dn + dv)
+            k = torch.cat([kvb[:, :, :dn], ent[:, dc:].view(nb * bs, 1, dr).expand(nb * bs, nh, dr)], dim=-1)
+            kc = k.view(nb, bs, nh, dn + dr).permute(0, 2, 1, 3).contiguous()
+            vc = kvb[:, :, dn:].reshape(nb, bs, nh, dv).permute(0, 2, 1, 3).contiguous()
+            q = torch.cat([q_nope[s0:s1], q_rope[s0:s1].to(q_nope.dtype)], dim=-1).contiguous()
+            ql = s1 - s0
+            m1 = AttnMetadata(num_seqs=1, q_start=torch.tensor([0, ql], dtype=torch.int32, device=d),
+                              kv_len=torch.tensor([n], dtype=torch.int32, device=d),
+                              block_table=torch.arange(nb, dtype=torch.int32, device=d).view(1, nb),
+                              slot_mapping=meta.slot_mapping[s0:s1], positions=meta.positions[s0:s1], max_q_len=ql,
+                              max_kv_len=n, is_decode=False, q_start_host=[0, ql], kv_len_host=[n])
+            out[s0:s1] = paged_attention(q, kc, vc, m1, self.scale)
+        return out
+
+    def _prefill_ref(self, q_nope, q_rope, meta, k_cache):
         """Expand latent -> per-head K/V for every context token, causal attention."""
         nh, dn, dr, dv, dc = self.nh, self.dn, self.dr, self.dv, self.dc
         T = q_nope.shape[0]
