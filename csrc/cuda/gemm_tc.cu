@@ -32,7 +32,10 @@ constexpr int BM = 128;        // rows per tile (one TMEM lane per row)
 constexpr int BK = 64;         // bf16 K per stage = one 128-byte swizzle row
 constexpr int UMMA_K = 16;     // K per tcgen05.mma kind::f16
 
-enum BFormat : int { B_BF16 = 0, B_FP8_BLOCK128 = 1 };
+// B formats: bf16; e4m3 + 128x128 fp32 block scales; MXFP4 (e2m1 pairs + e8m0 per 32);
+// NVFP4 (e2m1 pairs + e4m3 per 16 + fp32 per expert).  All but bf16 are widened to bf16
+// in shared memory by the converter warps before the tcgen05 kind::f16 MMAs.
+enum BFormat : int { B_BF16 = 0, B_FP8_BLOCK128 = 1, B_MXFP4 = 2, B_NVFP4 = 3 };
 enum Epilogue : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_SWIGLU = 2 };
 
 // One m-tile of the grouped problem: rows [row0, row_end) of A all belong to
@@ -61,6 +64,10 @@ struct GemmParams {
   // fp8 B
   const float* b_scale;   // [E, ceil(N/128), ceil(K/128)]
   int sb_n, sb_k;
+  // fp4 B: per-row scale bytes [E, N, K/32] (e8m0) or [E, N, K/16] (e4m3); NVFP4 global [E]
+  const uint8_t* b_sc8;
+  int sc_k;
+  const float* b_gs;
   XtuStatus* status;
 };
 
@@ -68,13 +75,16 @@ template <int BN, int BFMT>
 struct Cfg {
   static constexpr int A_BYTES = BM * BK * 2;           // 16 KB
   static constexpr int B_BYTES = BN * BK * 2;           // bf16 tile fed to the MMA
-  static constexpr int BRAW_BYTES = (BFMT == B_FP8_BLOCK128) ? BN * BK : 0;  // e4m3 staging
+  static constexpr bool CONV = BFMT != B_BF16;           // converter warps widen B to bf16
+  static constexpr bool FP4 = BFMT == B_MXFP4 || BFMT == B_NVFP4;
+  static constexpr int BRAW_BYTES = BFMT == B_FP8_BLOCK128 ? BN * BK : (FP4 ? BN * BK / 2 : 0);  // raw staging
+  static constexpr int LUT_BYTES = FP4 ? 1024 : 0;       // byte -> two bf16 (e2m1 pair)
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + BRAW_BYTES;
-  static constexpr int STAGES = (BFMT == B_FP8_BLOCK128) ? (BN == 256 ? 3 : 4) : (BN == 256 ? 4 : 6);
-  static constexpr int NUM_WARPS = (BFMT == B_FP8_BLOCK128) ? 10 : 6;
+  static constexpr int STAGES = CONV ? (BN == 256 ? 3 : 4) : (BN == 256 ? 4 : 6);
+  static constexpr int NUM_WARPS = CONV ? 10 : 6;
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
-  static constexpr uint32_t TX_BYTES = A_BYTES + (BFMT == B_FP8_BLOCK128 ? BRAW_BYTES : B_BYTES);
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/ + LUT_BYTES;
+  static constexpr uint32_t TX_BYTES = A_BYTES + (CONV ? BRAW_BYTES : B_BYTES);
 };
 
 __device__ __forceinline__ float silu_clamped(float g, float u, float limit, float alpha, float beta) {
@@ -158,7 +168,9 @@ __global__ void __launch_bounds__(Cfg<BN, BFMT>::NUM_WARPS * 32, 1)
           uint8_t* sB = sA + C::A_BYTES;
           mbar_arrive_expect_tx(&full_bar[stage], C::TX_BYTES);
           tma_load_2d(sA, &tmap_a, &full_bar[stage], kb * BK, row0);
-          if (BFMT == B_FP8_BLOCK128) {
+          if (C::FP4) {
+            tma_load_2d(sB + C::B_BYTES, &tmap_b, &full_bar[stage], kb * (BK / 2), brow);
+          } else if (BFMT == B_FP8_BLOCK128) {
             tma_load_2d(sB + C::B_BYTES, &tmap_b, &full_bar[stage], kb * BK, brow);
           } else {
             tma_load_2d(sB, &tmap_b, &full_bar[stage], kb * BK, brow);
@@ -186,7 +198,7 @@ __global__ void __launch_bounds__(Cfg<BN, BFMT>::NUM_WARPS * 32, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         for (int kb = 0; kb < nk; ++kb) {
-          uint64_t* ready = (BFMT == B_FP8_BLOCK128) ? &conv_bar[stage] : &full_bar[stage];
+          uint64_t* ready = C::CONV ? &conv_bar[stage] : &full_bar[stage];
           if (!mbar_wait(ready, phase, p.status, 21)) { ok = false; break; }
           tc_fence_after();
           const uint32_t a_addr = smem_u32(smem + stage * C::STAGE_BYTES);
@@ -316,6 +328,88 @@ __global__ void __launch_bounds__(Cfg<BN, BFMT>::NUM_WARPS * 32, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+    }
+  } else if (C::FP4) {
+    // ---------------- e2m1 -> bf16 dequantizer (warps 6..9) ----------------
+    // 16-byte raw chunks (32 e2m1 values, low nibble = even k) go to consecutive lanes;
+    // a 256-entry table maps a byte to its two bf16 values.  MXFP4 scales are powers of
+    // two, so the bf16 product is exact; NVFP4 scales (e4m3 x fp32 global) are applied
+    // in fp32.
+    const int ct = threadIdx.x - 6 * 32;  // 0..127
+    uint32_t* lut = reinterpret_cast<uint32_t*>(smem + C::STAGES * C::STAGE_BYTES + 256);
+    for (int b = ct; b < 256; b += 128) {
+      const uint16_t tab[8] = {0x0000, 0x3F00, 0x3F80, 0x3FC0, 0x4000, 0x4040, 0x4080, 0x40C0};
+      const int lo = b & 15, hi = b >> 4;
+      const uint32_t flo = (lo & 8 ? 0x8000u : 0u) | tab[lo & 7];
+      const uint32_t fhi = (hi & 8 ? 0x8000u : 0u) | tab[hi & 7];
+      lut[b] = flo | (fhi << 16);
+    }
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    int stage = 0;
+    uint32_t phase = 0;
+    constexpr int CHUNKS = BN * BK / 2 / 16;        // 16-byte chunks per stage (2 per row)
+    constexpr int PER_THREAD = CHUNKS / 128;
+    for (int w = blockIdx.x; w < total; w += gridDim.x) {
+      int expert, row0, row_end, nb;
+      tile_of(w, expert, row0, row_end, nb);
+      bool ok = true;
+      for (int kb = 0; kb < nk; ++kb) {
+        if (!mbar_wait(&full_bar[stage], phase, p.status, 41)) { ok = false; break; }
+        uint8_t* sB = smem + stage * C::STAGE_BYTES + C::A_BYTES;
+        const uint8_t* raw = sB + C::B_BYTES;
+#pragma unroll
+        for (int i = 0; i < PER_THREAD; ++i) {
+          const int qi = ct + 128 * i;
+          const int r = qi >> 1, hk = qi & 1;     // row, which 32 k of the 64
+          const int n = min(nb * BN + r, p.N - 1);
+          const uint8_t* srow = p.b_sc8 + ((size_t)expert * p.N + n) * p.sc_k;
+          const uint4 q4 = reinterpret_cast<const uint4*>(raw)[qi];
+          const uint32_t words[4] = {q4.x, q4.y, q4.z, q4.w};
+          uint32_t out[16];
+          if (BFMT == B_MXFP4) {
+            const uint32_t e = srow[kb * 2 + hk];
+            const uint32_t sb = e == 0 ? 0x0040u : (e == 255 ? 0x7FC0u : (e << 7));   // bf16 of 2^(e-127)
+            const uint32_t s2 = sb | (sb << 16);
+            const __nv_bfloat162 sc = *reinterpret_cast<const __nv_bfloat162*>(&s2);
+#pragma unroll
+            for (int wi = 0; wi < 4; ++wi) {
+#pragma unroll
+              for (int bi = 0; bi < 4; ++bi) {
+                uint32_t v = lut[(words[wi] >> (8 * bi)) & 0xFF];
+                __nv_bfloat162 x = __hmul2(*reinterpret_cast<__nv_bfloat162*>(&v), sc);
+                out[wi * 4 + bi] = *reinterpret_cast<uint32_t*>(&x);
+              }
+            }
+          } else {
+            const float gs = p.b_gs[expert];
+            const int g0 = kb * 4 + hk * 2;
+            const __nv_fp8_storage_t e0 = srow[g0], e1 = srow[g0 + 1];
+            const float s0 = __half2float(__half(__nv_cvt_fp8_to_halfraw(e0, __NV_E4M3))) * gs;
+            const float s1 = __half2float(__half(__nv_cvt_fp8_to_halfraw(e1, __NV_E4M3))) * gs;
+#pragma unroll
+            for (int wi = 0; wi < 4; ++wi) {
+              const float sc = wi < 2 ? s0 : s1;     // words 0-1: k 0..15, words 2-3: k 16..31
+#pragma unroll
+              for (int bi = 0; bi < 4; ++bi) {
+                const uint32_t v = lut[(words[wi] >> (8 * bi)) & 0xFF];
+                out[wi * 4 + bi] = pack_bf16x2(bf16_lo(v) * sc, bf16_hi(v) * sc);
+              }
+            }
+          }
+          uint8_t* dst_row = sB + r * 128;
+#pragma unroll
+          for (int pc = 0; pc < 4; ++pc) {
+            const int c = (hk * 4 + pc) ^ (r & 7);
+            *reinterpret_cast<uint4*>(dst_row + c * 16) =
+                make_uint4(out[4 * pc], out[4 * pc + 1], out[4 * pc + 2], out[4 * pc + 3]);
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&conv_bar[stage]);
+        if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
+      }
+      if (!ok) break;
     }
   } else if (BFMT == B_FP8_BLOCK128) {
     // ---------------- fp8 -> bf16 dequantizer (warps 6..9) ----------------
@@ -567,25 +661,28 @@ int xtu_mtile_bytes() { return (int)sizeof(MTile); }
 //   epi    : 0 = bf16 out [*, N]; 1 = f32 out; 2 = clamped SwiGLU -> bf16 out [*, N/2]
 //            (B rows per 256-row block: first 128 gate, next 128 up)
 //   row_scale / row_dest: per-row multiplier and destination row (nullable)
-int xtu_grouped_gemm_ex(const void* A, const void* B, const float* b_scale, int bfmt, void* D, int ldd, int M,
-                        int N, int K, int E, const void* tiles, const int* count, int max_mtiles, int epi,
-                        const float* row_scale, const int* row_dest, float act_limit, float act_alpha,
+int xtu_grouped_gemm_ex(const void* A, const void* B, const void* b_scale, const float* b_gs, int bfmt, void* D,
+                        int ldd, int M, int N, int K, int E, const void* tiles, const int* count, int max_mtiles,
+                        int epi, const float* row_scale, const int* row_dest, float act_limit, float act_alpha,
                         float act_beta, void* const* peer_D, int peer_rows, void* status, cudaStream_t stream);
 
 int xtu_grouped_gemm(const void* A, const void* B, const float* b_scale, int bfmt, void* D, int ldd, int M, int N,
                      int K, int E, const void* tiles, const int* count, int max_mtiles, int epi,
                      const float* row_scale, const int* row_dest, float act_limit, float act_alpha, float act_beta,
                      void* status, cudaStream_t stream) {
-  return xtu_grouped_gemm_ex(A, B, b_scale, bfmt, D, ldd, M, N, K, E, tiles, count, max_mtiles, epi, row_scale,
-                             row_dest, act_limit, act_alpha, act_beta, nullptr, 0, status, stream);
+  return xtu_grouped_gemm_ex(A, B, b_scale, nullptr, bfmt, D, ldd, M, N, K, E, tiles, count, max_mtiles, epi,
+                             row_scale, row_dest, act_limit, act_alpha, act_beta, nullptr, 0, status, stream);
 }
 
-// As xtu_grouped_gemm; with peer_D (device array of per-rank output bases) each kept row
-// m goes to rank row_dest[m] / peer_rows, row row_dest[m] % peer_rows, by direct stores
-// to that rank's memory (the expert-parallel combine fused into the down GEMM).
-int xtu_grouped_gemm_ex(const void* A, const void* B, const float* b_scale, int bfmt, void* D, int ldd, int M,
-                        int N, int K, int E, const void* tiles, const int* count, int max_mtiles, int epi,
-                        const float* row_scale, const int* row_dest, float act_limit, float act_alpha,
+// As xtu_grouped_gemm, plus:
+//   bfmt 2 (MXFP4): B [E, N, K/2] bytes (two e2m1, low nibble = even k), b_scale [E, N, K/32] e8m0;
+//   bfmt 3 (NVFP4): same B, b_scale [E, N, K/16] e4m3, b_gs [E] fp32 global scales;
+//   peer_D (device array of per-rank output bases): each kept row m goes to rank
+//   row_dest[m] / peer_rows, row row_dest[m] % peer_rows, by direct stores to that rank's
+//   memory (the expert-parallel combine fused into the down GEMM).
+int xtu_grouped_gemm_ex(const void* A, const void* B, const void* b_scale, const float* b_gs, int bfmt, void* D,
+                        int ldd, int M, int N, int K, int E, const void* tiles, const int* count, int max_mtiles,
+                        int epi, const float* row_scale, const int* row_dest, float act_limit, float act_alpha,
                         float act_beta, void* const* peer_D, int peer_rows, void* status, cudaStream_t stream) {
   if (peer_D != nullptr && (row_dest == nullptr || peer_rows <= 0)) return -7;
   if (M <= 0 || N <= 0 || K <= 0 || E <= 0) return 0;
@@ -594,12 +691,17 @@ int xtu_grouped_gemm_ex(const void* A, const void* B, const float* b_scale, int 
   if (rc) return rc;
   const int bn = (epi == EPI_SWIGLU || N >= 256) ? 256 : 128;
   if (epi == EPI_SWIGLU && (N % 256) != 0) return -4;
-  if (bfmt == B_FP8_BLOCK128)
+  if (bfmt == B_MXFP4 || bfmt == B_NVFP4) {
+    if (K % 64 != 0 || b_scale == nullptr || (bfmt == B_NVFP4 && b_gs == nullptr)) return -8;
+    rc = make_tmap_2d(&tb, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)E * N, K / 2, bn, BK / 2,
+                      CU_TENSOR_MAP_SWIZZLE_NONE);
+  } else if (bfmt == B_FP8_BLOCK128) {
     rc = make_tmap_2d(&tb, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)E * N, K, bn, BK,
                       CU_TENSOR_MAP_SWIZZLE_NONE);
-  else
+  } else {
     rc = make_tmap_2d(&tb, B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)E * N, K, bn, BK,
                       CU_TENSOR_MAP_SWIZZLE_128B);
+  }
   if (rc) return rc;
   GemmParams p{};
   p.M = M; p.N = N; p.K = K;
@@ -609,9 +711,18 @@ int xtu_grouped_gemm_ex(const void* A, const void* B, const float* b_scale, int 
   p.D = D; p.ldd = ldd; p.row_scale = row_scale; p.row_dest = row_dest;
   p.peer_D = peer_D; p.peer_rows = peer_rows;
   p.act_limit = act_limit; p.act_alpha = act_alpha; p.act_beta = act_beta;
-  p.b_scale = b_scale; p.sb_n = (N + 127) / 128; p.sb_k = (K + 127) / 128;
+  p.b_scale = reinterpret_cast<const float*>(b_scale); p.sb_n = (N + 127) / 128; p.sb_k = (K + 127) / 128;
+  p.b_sc8 = reinterpret_cast<const uint8_t*>(b_scale);
+  p.sc_k = bfmt == B_MXFP4 ? K / 32 : K / 16;
+  p.b_gs = b_gs;
   p.status = reinterpret_cast<XtuStatus*>(status);
   const int work = max_mtiles * p.n_blocks;
+  if (bfmt == B_MXFP4)
+    return bn == 256 ? dispatch_epi<256, B_MXFP4>(epi, ta, tb, p, work, stream)
+                     : dispatch_epi<128, B_MXFP4>(epi, ta, tb, p, work, stream);
+  if (bfmt == B_NVFP4)
+    return bn == 256 ? dispatch_epi<256, B_NVFP4>(epi, ta, tb, p, work, stream)
+                     : dispatch_epi<128, B_NVFP4>(epi, ta, tb, p, work, stream);
   if (bfmt == B_FP8_BLOCK128)
     return bn == 256 ? dispatch_epi<256, B_FP8_BLOCK128>(epi, ta, tb, p, work, stream)
                      : dispatch_epi<128, B_FP8_BLOCK128>(epi, ta, tb, p, work, stream);

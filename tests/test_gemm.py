@@ -209,3 +209,37 @@ def test_gemv_decode(fp8, M, N_, K):
     torch.cuda.synchronize()
     ref = x.float() @ wd.t() + bias.float()
     _close(y, ref, 2e-3)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("fmt", ["mxfp4", "nvfp4"])
+@pytest.mark.parametrize("T,E,H,I,K", [(37, 8, 512, 256, 2), (300, 16, 1024, 512, 4), (5, 4, 256, 128, 2)])
+def test_fused_moe_fp4_matches_reference(fmt, T, E, H, I, K):
+    """MXFP4 / NVFP4 experts through the grouped GEMM (on-chip widening) vs fp32 dequant reference."""
+    from vllm_xtu_moe_b200.ops import moe as M
+    from vllm_xtu_moe_b200.ops.quant import quant_mxfp4, quant_nvfp4
+    g = torch.Generator().manual_seed(T + E)
+    w13 = torch.randn(E, 2 * I, H, generator=g) / H ** 0.5
+    w2 = torch.randn(E, H, I, generator=g) / I ** 0.5
+    if fmt == "mxfp4":
+        p13, s13 = quant_mxfp4(w13)
+        p2, s2 = quant_mxfp4(w2)
+        gs13 = gs2 = None
+    else:
+        r13 = [quant_nvfp4(w13[e]) for e in range(E)]
+        r2 = [quant_nvfp4(w2[e]) for e in range(E)]
+        p13, s13, gs13 = (torch.stack([r[i] for r in r13]) for i in range(3))
+        p2, s2, gs2 = (torch.stack([r[i] for r in r2]) for i in range(3))
+    cpu = M.prepare_experts(fmt, p13, p2, s13, s2, gs13, gs2)
+    d = "cuda"
+    gpu = M.prepare_experts(fmt, p13.to(d), p2.to(d), s13.to(d), s2.to(d), None if gs13 is None else gs13.to(d),
+                            None if gs2 is None else gs2.to(d))
+    x = (torch.randn(T, H, generator=g) * 0.5).to(torch.bfloat16)
+    ids = torch.stack([torch.randperm(E, generator=g)[:K] for _ in range(T)]).int()
+    w = torch.rand(T, K, generator=g)
+    w = (w / w.sum(1, keepdim=True)).float()
+    ref = M.moe_ref(x, ids, w, cpu).float()
+    out = M.fused_moe(x.to(d), ids.to(d), w.to(d), gpu).float().cpu()
+    torch.cuda.synchronize()
+    err = (out - ref).abs().max().item()
+    assert err <= 2e-2 * ref.abs().max().item() + 1e-3, err

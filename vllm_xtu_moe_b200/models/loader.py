@@ -305,7 +305,10 @@ def export_hf(model, cfg: ModelConfig, path) -> None:
                 s13 = None if ex.s13 is None else ex.s13[e].cpu()
                 if ex.interleaved:
                     w13 = _deinterleave(w13)
-                    s13 = None if s13 is None else _deinterleave_scale(s13)
+                    if s13 is not None and ex.fmt in ("mxfp4", "nvfp4"):      # per-row scales
+                        s13 = _deinterleave(s13.view(torch.uint8)).view(s13.dtype)
+                    elif s13 is not None:
+                        s13 = _deinterleave_scale(s13)
                 I = w13.shape[0] // 2
                 out[f"{base}.{e}.{fam['gate']}.weight"] = w13[:I].clone()
                 out[f"{base}.{e}.{fam['up']}.weight"] = w13[I:].clone()

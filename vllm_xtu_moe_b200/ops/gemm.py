@@ -121,11 +121,15 @@ def build_mtiles(seg: torch.Tensor, num_rows: int, tiles: torch.Tensor | None = 
 EPI_BF16, EPI_F32, EPI_SWIGLU = 0, 1, 2
 
 
+FP4_FMTS = {"mxfp4": 2, "nvfp4": 3}
+
+
 def grouped_gemm(a: torch.Tensor, w: torch.Tensor, seg: torch.Tensor, *, w_scale: torch.Tensor | None = None,
                  epilogue: int = EPI_BF16, out: torch.Tensor | None = None, row_scale: torch.Tensor | None = None,
                  row_dest: torch.Tensor | None = None, out_rows: int | None = None,
                  act_limit: float = 0.0, act_alpha: float = 1.0, act_beta: float = 0.0,
-                 tiles: tuple[torch.Tensor, torch.Tensor, int] | None = None) -> torch.Tensor:
+                 tiles: tuple[torch.Tensor, torch.Tensor, int] | None = None, w_fmt: str | None = None,
+                 w_gs: torch.Tensor | None = None) -> torch.Tensor:
     """Grouped GEMM: rows a[seg[e]:seg[e+1]] are multiplied by w[e]^T.
 
     w is [E, N, K] bf16, or e4m3 with w_scale [E, ceil(N/128), ceil(K/128)].
@@ -136,6 +140,9 @@ def grouped_gemm(a: torch.Tensor, w: torch.Tensor, seg: torch.Tensor, *, w_scale
     """
     M, K = a.shape
     E, Nn, Kw = w.shape
+    if w_fmt in FP4_FMTS:
+        return _grouped_gemm_fp4(a, w, seg, w_scale, w_gs, FP4_FMTS[w_fmt], epilogue, out, row_scale, row_dest,
+                                 out_rows, act_limit, act_alpha, act_beta, tiles)
     assert Kw == K
     out_cols = Nn // 2 if epilogue == EPI_SWIGLU else Nn
     rows = out_rows if out_rows is not None else M
@@ -216,4 +223,31 @@ def _grouped_gemm_torch(a, w, seg, w_scale, epilogue, out, row_scale, row_dest, 
             out[d[keep]] = y[keep].to(out.dtype)
         else:
             out[s0:s1] = y.to(out.dtype)
+    return out
+
+
+def _grouped_gemm_fp4(a, w, seg, w_scale, w_gs, bfmt, epilogue, out, row_scale, row_dest, out_rows, act_limit,
+                      act_alpha, act_beta, tiles):
+    """MXFP4 / NVFP4 expert weights: w [E, N, K/2] bytes + per-row scales, widened on chip."""
+    M, K = a.shape
+    E, Nn, Kh = w.shape
+    assert Kh * 2 == K and w.dtype == torch.uint8 and w_scale is not None
+    out_cols = Nn // 2 if epilogue == EPI_SWIGLU else Nn
+    rows = out_rows if out_rows is not None else M
+    if out is None:
+        dt = torch.float32 if epilogue == EPI_F32 else torch.bfloat16
+        out = torch.zeros(rows, out_cols, dtype=dt, device=a.device)
+    if M == 0:
+        return out
+    assert a.is_cuda and a.dtype == torch.bfloat16 and a.is_contiguous() and w.is_contiguous()
+    if tiles is None:
+        tiles = build_mtiles(seg, M)
+    t, cnt, mx = tiles
+    gs = None
+    if bfmt == 3:
+        gs = w_gs.float().contiguous()
+    N.call("xtu_grouped_gemm_ex", a.data_ptr(), w.data_ptr(), w_scale.contiguous().data_ptr(), N.ptr(gs), bfmt,
+           out.data_ptr(), out.stride(0), M, Nn, K, E, t.data_ptr(), cnt.data_ptr(), mx, epilogue, N.ptr(row_scale),
+           N.ptr(row_dest), float(act_limit), float(act_alpha), float(act_beta), None, 0,
+           N.status_buffer(a.device).data_ptr(), N.stream_ptr(a.device))
     return out

@@ -144,6 +144,9 @@ def moe_experts_partial(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tenso
            x.stride(0), ws.xp.data_ptr(), s)
     I = experts.inter
     fp8 = experts.fmt == "fp8"
+    if experts.fmt in G.FP4_FMTS:
+        _experts_fp4(experts, ws, n, act_limit, act_alpha, act_beta)
+        return
     if T <= G.GEMV_MAX_M and experts.interleaved:
         # decode: weight-streaming grouped GEMV (gate/up + SwiGLU, down + weight + scatter)
         N.call("xtu_moe_gemv", experts.w13.data_ptr(), N.ptr(experts.s13 if fp8 else None),
@@ -167,6 +170,17 @@ def moe_experts_partial(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tenso
                ws.h.data_ptr(), s)
     G.grouped_gemm(ws.h[:n], experts.w2, ws.seg, w_scale=sc2, epilogue=G.EPI_BF16, out=ws.slots[:n],
                    row_scale=ws.perm_w, row_dest=ws.perm_slot, tiles=tiles)
+
+
+def _experts_fp4(experts: ExpertWeights, ws: MoEWorkspace, n: int, act_limit, act_alpha, act_beta) -> None:
+    """MXFP4 / NVFP4 experts (gate/up rows interleaved): grouped GEMMs with on-chip widening."""
+    tiles = G.build_mtiles(ws.seg[: experts.num_experts + 1], n, ws.tiles, ws.ntiles)
+    seg = ws.seg[: experts.num_experts + 1]
+    G.grouped_gemm(ws.xp[:n], experts.w13, seg, w_scale=experts.s13, w_fmt=experts.fmt, w_gs=experts.gs13,
+                   epilogue=G.EPI_SWIGLU, out=ws.h[:n], act_limit=act_limit, act_alpha=act_alpha,
+                   act_beta=act_beta, tiles=tiles)
+    G.grouped_gemm(ws.h[:n], experts.w2, seg, w_scale=experts.s2, w_fmt=experts.fmt, w_gs=experts.gs2,
+                   epilogue=G.EPI_BF16, out=ws.slots[:n], row_scale=ws.perm_w, row_dest=ws.perm_slot, tiles=tiles)
 
 
 def moe_combine(ws: MoEWorkspace, ids: torch.Tensor, lo: int, hi: int, *, shared: torch.Tensor | None = None,
@@ -199,8 +213,8 @@ def fused_moe(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, experts
         if extra is not None:
             o = o + extra.float()
         return o.to(x.dtype) if out is None else out.copy_(o)
-    if experts.fmt not in ("bf16", "fp8"):
-        raise NotImplementedError(f"GPU grouped GEMM for {experts.fmt}")
+    if experts.fmt in G.FP4_FMTS and not experts.interleaved:
+        raise NotImplementedError(f"GPU {experts.fmt} experts need I % 128 == 0 (gate/up interleave)")
     if ws is None or ws.max_tokens < T:
         ws = MoEWorkspace(T, K, E, H, experts.inter, x.device)
     assert x.is_contiguous() and ids.is_contiguous() and weights.is_contiguous()
@@ -245,11 +259,15 @@ def prepare_experts(fmt: str, w13: torch.Tensor, w2: torch.Tensor, s13=None, s2=
     Interleaves gate/up rows in 128-row blocks when I % 128 == 0 (fused SwiGLU).
     """
     I = w13.shape[1] // 2
-    inter = I % 128 == 0 and fmt in ("bf16", "fp8")
+    inter = I % 128 == 0
     if inter:
         if fmt == "fp8":
             w13 = G.interleave_gate_up(w13.view(torch.uint8)).view(torch.float8_e4m3fn)
             s13 = G.interleave_gate_up_scale(s13)
+        elif fmt in ("mxfp4", "nvfp4"):   # per-row scales follow their rows
+            w13 = G.interleave_gate_up(w13)
+            sdt = s13.dtype
+            s13 = G.interleave_gate_up(s13.view(torch.uint8)).view(sdt)
         else:
             w13 = G.interleave_gate_up(w13)
     return ExpertWeights(fmt, w13.contiguous(), w2.contiguous(), s13, s2, inter, gs13, gs2)

@@ -108,7 +108,7 @@ class EPMoE:
         G.grouped_gemm(self.xp.local, ex.w13, self.seg, w_scale=ex.s13 if fp8 else None, epilogue=G.EPI_SWIGLU,
                        out=self.h, act_limit=self.act_limit, tiles=tiles)
         t, cnt, mx = tiles
-        N.call("xtu_grouped_gemm_ex", self.h.data_ptr(), ex.w2.data_ptr(), N.ptr(ex.s2 if fp8 else None),
+        N.call("xtu_grouped_gemm_ex", self.h.data_ptr(), ex.w2.data_ptr(), N.ptr(ex.s2 if fp8 else None), None,
                1 if fp8 else 0, self.slots.local.data_ptr(), H, self.recv_cap, H, self.I, self.El, t.data_ptr(),
                cnt.data_ptr(), mx, G.EPI_BF16, self.rw.local.data_ptr(), self.rsrc.local.data_ptr(),
                float(self.act_limit), 1.0, 0.0, self.slots.ptr(), self.pair_cap, st, s)
