@@ -132,11 +132,22 @@ def _shutdown_tiers():
 
 
 def _raw_gpu(fmt, E, H, I, seed):
+    from vllm_xtu_moe_b200.ops.quant import quant_mxfp4, quant_nvfp4
     g = torch.Generator().manual_seed(seed)
     w13 = torch.randn(E, 2 * I, H, generator=g) / H ** 0.5
     w2 = torch.randn(E, H, I, generator=g) / I ** 0.5
     if fmt == "bf16":
         return dict(fmt=fmt, w13=w13.to(torch.bfloat16), w2=w2.to(torch.bfloat16))
+    if fmt == "mxfp4":
+        p13, s13 = quant_mxfp4(w13)
+        p2, s2 = quant_mxfp4(w2)
+        return dict(fmt=fmt, w13=p13, w2=p2, s13=s13, s2=s2)
+    if fmt == "nvfp4":
+        r13 = [quant_nvfp4(w13[e]) for e in range(E)]
+        r2 = [quant_nvfp4(w2[e]) for e in range(E)]
+        p13, s13, g13 = (torch.stack([r[i] for r in r13]) for i in range(3))
+        p2, s2, g2 = (torch.stack([r[i] for r in r2]) for i in range(3))
+        return dict(fmt=fmt, w13=p13, w2=p2, s13=s13, s2=s2, gs13=g13, gs2=g2)
     q13, s13 = quant_fp8_block(w13)
     q2, s2 = quant_fp8_block(w2)
     return dict(fmt=fmt, w13=q13, w2=q2, s13=s13, s2=s2)
@@ -182,8 +193,8 @@ def _executor_case(fmt, pool_experts, T, skew=False, ring=True, min_tokens=64, w
                          ring=ring, gpu_prefill_min_tokens=min_tokens, max_tokens=1024)
     _live.append(tier)
     assert tier.expert_sink(1, raw) is None
-    res = M.prepare_experts(fmt, raw["w13"].cuda(), raw["w2"].cuda(), raw["s13"].cuda() if "s13" in raw else None,
-                            raw["s2"].cuda() if "s2" in raw else None)
+    cu = lambda k: raw[k].cuda() if k in raw else None
+    res = M.prepare_experts(fmt, cu("w13"), cu("w2"), cu("s13"), cu("s2"), cu("gs13"), cu("gs2"))
 
     class Blk:
         experts = None
@@ -211,7 +222,7 @@ def _close(a, b, tol=2e-2):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("fmt", ["bf16", "fp8"])
+@pytest.mark.parametrize("fmt", ["bf16", "fp8", "mxfp4", "nvfp4"])
 @pytest.mark.parametrize("T", [1, 5, 40])
 def test_hybrid_pool_plus_cpu_matches_gpu(fmt, T):
     tier, blk, x, ids, w, sh, ref = _executor_case(fmt, {1: [0, 3, 5, 7, 11, 20, 31]}, T, ring=False)
@@ -236,7 +247,7 @@ def test_cpu_only_bridge_matches_gpu(fmt):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("fmt", ["bf16", "fp8"])
+@pytest.mark.parametrize("fmt", ["bf16", "fp8", "mxfp4", "nvfp4"])
 def test_prefill_ring_matches_gpu(fmt):
     tier, blk, x, ids, w, sh, ref = _executor_case(fmt, {}, 300, ring=True, min_tokens=64)
     y = blk.executor(blk, x, ids, w, sh)
@@ -245,6 +256,7 @@ def test_prefill_ring_matches_gpu(fmt):
     assert ok, err
     assert tier.stats()["ring"] == 1
     assert tier.ring.copied_bytes == 32 * tier.executors[0].host.expert_bytes()
+    assert y.shape == ref.shape
 
 
 @pytest.mark.gpu

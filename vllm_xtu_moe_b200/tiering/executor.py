@@ -30,7 +30,7 @@ from .policy import load_pin_table
 from .pool import LayerPool
 from .ring import ExpertRing
 
-GPU_FMTS = ("bf16", "fp8")
+GPU_FMTS = ("bf16", "fp8", "mxfp4", "nvfp4")
 
 
 class LayerExecutor:
@@ -147,7 +147,8 @@ class TieredExperts:
                               deadline_ms=self.ec.pool_deadline_ms)
         host = pool = None
         if self.device.type == "cuda" and fmt in GPU_FMTS:
-            scales = HostExperts.gpu_scales_from_checkpoint(fmt, _cpu(raw.get("s13")), _cpu(raw.get("s2")))
+            scales = HostExperts.gpu_scales_from_checkpoint(fmt, _cpu(raw.get("s13")), _cpu(raw.get("s2")),
+                                                            _cpu(raw.get("gs13")), _cpu(raw.get("gs2")))
             host = HostExperts(eng, scales)
             experts = self._pool_list(layer)
             if experts:

@@ -31,6 +31,46 @@ def _row_bytes(fmt: str, K: int) -> int:
     return {"bf16": 2 * K, "fp8": K}.get(fmt, K // 2)
 
 
+def _scale_shape(fmt: str, rows: int, K: int) -> tuple[tuple, torch.dtype] | None:
+    """Per-expert scale tensor shape/dtype in GPU kernel layout."""
+    if fmt == "fp8":
+        return ((rows + 127) // 128, (K + 127) // 128), torch.float32
+    if fmt == "mxfp4":
+        return (rows, K // 32), torch.uint8
+    if fmt == "nvfp4":
+        return (rows, K // 16), torch.float8_e4m3fn
+    return None
+
+
+def alloc_expert_slots(fmt: str, n: int, H: int, I: int, device):
+    """n GPU expert slots of one layer (gate/up rows interleaved) as ExpertWeights."""
+    from ..ops import moe as M
+    wdt = {"bf16": torch.bfloat16, "fp8": torch.float8_e4m3fn}.get(fmt, torch.uint8)
+    kdiv = 2 if fmt in ("mxfp4", "nvfp4") else 1
+    w13 = torch.empty(n, 2 * I, H // kdiv, dtype=wdt, device=device)
+    w2 = torch.empty(n, H, I // kdiv, dtype=wdt, device=device)
+    s13 = s2 = gs13 = gs2 = None
+    sh13, sh2 = _scale_shape(fmt, 2 * I, H), _scale_shape(fmt, H, I)
+    if sh13 is not None:
+        s13 = torch.empty(n, *sh13[0], dtype=sh13[1], device=device)
+        s2 = torch.empty(n, *sh2[0], dtype=sh2[1], device=device)
+    if fmt == "nvfp4":
+        gs13 = torch.ones(n, dtype=torch.float32, device=device)
+        gs2 = torch.ones(n, dtype=torch.float32, device=device)
+    return M.ExpertWeights(fmt, w13, w2, s13, s2, True, gs13, gs2)
+
+
+def expert_slot_bytes(fmt: str, H: int, I: int) -> int:
+    n = 2 * I * _row_bytes(fmt, H) + H * _row_bytes(fmt, I)
+    for sh in (_scale_shape(fmt, 2 * I, H), _scale_shape(fmt, H, I)):
+        if sh is not None:
+            k = 1
+            for d in sh[0]:
+                k *= d
+            n += k * torch.tensor([], dtype=sh[1]).element_size()
+    return n + (8 if fmt == "nvfp4" else 0)
+
+
 class HostExperts:
     """One layer's routed experts held by a CpuExpertEngine, DMA-able into GPU slots."""
 
@@ -61,7 +101,7 @@ class HostExperts:
                     if sh[key] and L.xtu_host_register(sh[key], sh[key + "_bytes"]) == 0:
                         self.registered.append(sh[key])
         # scales in GPU layout (pinned): fp8 [E, 2I/128, H/128] interleaved + [E, H/128, I/128]
-        self.s13 = self.s2 = None
+        self.s13 = self.s2 = self.gs13 = self.gs2 = None
         if gpu_scales:
             pin = torch.cuda.is_available()
             self.s13 = gpu_scales["s13"].contiguous()
@@ -69,12 +109,30 @@ class HostExperts:
             if pin:
                 self.s13 = self.s13.pin_memory()
                 self.s2 = self.s2.pin_memory()
+            if "gs13" in gpu_scales:
+                self.gs13, self.gs2 = gpu_scales["gs13"], gpu_scales["gs2"]
 
     @staticmethod
-    def gpu_scales_from_checkpoint(fmt: str, s13: torch.Tensor | None, s2: torch.Tensor | None) -> dict | None:
+    def gpu_scales_from_checkpoint(fmt: str, s13: torch.Tensor | None, s2: torch.Tensor | None, gs13=None,
+                                   gs2=None) -> dict | None:
         if fmt == "fp8":
             return {"s13": G.interleave_gate_up_scale(s13.float()), "s2": s2.float()}
+        if fmt in ("mxfp4", "nvfp4"):    # per-row scales follow the interleaved gate/up rows
+            dt = s13.dtype
+            out = {"s13": G.interleave_gate_up(s13.view(torch.uint8)).view(dt), "s2": s2}
+            if fmt == "nvfp4":
+                out["gs13"], out["gs2"] = gs13.float().reshape(-1), gs2.float().reshape(-1)
+            return out
         return None
+
+    def copy_slot(self, e: int, slots, i: int, stream: torch.cuda.Stream) -> None:
+        """Expert e -> slot i of an ExpertWeights of slots (weights, scales, global scales)."""
+        self.copy_expert(e, slots.w13[i], slots.w2[i], slots.s13[i] if slots.s13 is not None else None,
+                         slots.s2[i] if slots.s2 is not None else None, stream)
+        if slots.gs13 is not None and self.gs13 is not None:
+            with torch.cuda.stream(stream):
+                slots.gs13[i].fill_(float(self.gs13[e]))
+                slots.gs2[i].fill_(float(self.gs2[e]))
 
     def copy_expert(self, e: int, w13_dst: torch.Tensor, w2_dst: torch.Tensor, s13_dst: torch.Tensor | None,
                     s2_dst: torch.Tensor | None, stream: torch.cuda.Stream) -> None:
@@ -103,7 +161,7 @@ class HostExperts:
                 s2_dst.copy_(self.s2[e], non_blocking=True)
 
     def expert_bytes(self) -> int:
-        return 2 * self.I * _row_bytes(self.fmt, self.H) + self.H * _row_bytes(self.fmt, self.I)
+        return expert_slot_bytes(self.fmt, self.H, self.I)
 
     def close(self):
         """Unregister the engine's shards (must happen before the engine frees them)."""

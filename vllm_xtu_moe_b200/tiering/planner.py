@@ -115,7 +115,7 @@ def plan(cfg: ModelConfig, gpu_gib: float = 178.0, *, max_model_len: int = 16384
     kv = kv_bytes_per_token(cfg) * max_model_len * max_seqs + int(graph_pool_gib * GiB)
     eb = expert_bytes(cfg)
     layer_b = eb * cfg.num_experts
-    gfmt = cfg.expert_fmt in ("bf16", "fp8")
+    gfmt = cfg.expert_fmt in ("bf16", "fp8", "mxfp4", "nvfp4")
     te = max(1, min(tile_e, cfg.num_experts))
     stage = staging_bytes(cfg.expert_fmt, cfg.hidden_size, cfg.moe_intermediate, te, nslots) if gfmt else 0
     nd = cfg.num_mtp_layers if drafter_layers is None else drafter_layers

@@ -16,7 +16,7 @@ from __future__ import annotations
 import torch
 
 from ..ops import moe as M
-from .host import HostExperts
+from .host import HostExperts, alloc_expert_slots
 from .policy import plan_swap
 
 
@@ -27,18 +27,7 @@ class LayerPool:
         self.E = host.E
         self.nslots = len(experts)
         self.window, self.hyst, self.maxswap = window, hyst, maxswap
-        fmt = host.fmt
-        dt = {"bf16": torch.bfloat16, "fp8": torch.float8_e4m3fn}[fmt]
-        S, H, I = max(1, self.nslots), host.H, host.I
-        w13 = torch.empty(S, 2 * I, H, dtype=dt, device=device)
-        w2 = torch.empty(S, H, I, dtype=dt, device=device)
-        s13 = s2 = None
-        if fmt == "fp8":
-            s13 = torch.empty(S, (2 * I + 127) // 128, (H + 127) // 128, dtype=torch.float32, device=device)
-            s2 = torch.empty(S, (H + 127) // 128, (I + 127) // 128, dtype=torch.float32, device=device)
-        self.slots = M.ExpertWeights(fmt, w13[: self.nslots], w2[: self.nslots],
-                                     s13[: self.nslots] if s13 is not None else None,
-                                     s2[: self.nslots] if s2 is not None else None, interleaved=True)
+        self.slots = alloc_expert_slots(host.fmt, self.nslots, host.H, host.I, device)
         self.expert_of = list(experts)
         sm = torch.full((self.E,), -1, dtype=torch.int32)
         for s, e in enumerate(experts):
@@ -56,9 +45,7 @@ class LayerPool:
         return self.nslots * self.host.expert_bytes()
 
     def _load(self, e: int, s: int) -> None:
-        sl = self.slots
-        self.host.copy_expert(e, sl.w13[s], sl.w2[s], sl.s13[s] if sl.s13 is not None else None,
-                              sl.s2[s] if sl.s2 is not None else None, self.side)
+        self.host.copy_slot(e, self.slots, s, self.side)
 
     def maybe_adapt(self, preserve_oldest: bool = False) -> tuple[list[int], list[int]]:
         """Called by the host once per step (outside graph capture)."""

@@ -16,30 +16,18 @@ from __future__ import annotations
 import torch
 
 from ..ops import moe as M
-from .host import HostExperts, _row_bytes
+from .host import HostExperts, alloc_expert_slots, expert_slot_bytes
 
 
 def staging_bytes(fmt: str, H: int, I: int, tile_e: int, nslots: int) -> int:
-    per = 2 * I * _row_bytes(fmt, H) + H * _row_bytes(fmt, I)
-    if fmt == "fp8":
-        per += 4 * ((2 * I + 127) // 128) * ((H + 127) // 128) + 4 * ((H + 127) // 128) * ((I + 127) // 128)
-    return per * tile_e * nslots
+    return expert_slot_bytes(fmt, H, I) * tile_e * nslots
 
 
 class ExpertRing:
     def __init__(self, fmt: str, H: int, I: int, tile_e: int, nslots: int, device):
         assert nslots >= 2, "the ring needs at least two slots to overlap copy and compute"
         self.fmt, self.H, self.I, self.tile_e, self.nslots = fmt, H, I, tile_e, nslots
-        dt = {"bf16": torch.bfloat16, "fp8": torch.float8_e4m3fn}[fmt]
-        self.slots = []
-        for _ in range(nslots):
-            w13 = torch.empty(tile_e, 2 * I, H, dtype=dt, device=device)
-            w2 = torch.empty(tile_e, H, I, dtype=dt, device=device)
-            s13 = s2 = None
-            if fmt == "fp8":
-                s13 = torch.empty(tile_e, (2 * I + 127) // 128, (H + 127) // 128, dtype=torch.float32, device=device)
-                s2 = torch.empty(tile_e, (H + 127) // 128, (I + 127) // 128, dtype=torch.float32, device=device)
-            self.slots.append(M.ExpertWeights(fmt, w13, w2, s13, s2, interleaved=True))
+        self.slots = [alloc_expert_slots(fmt, tile_e, H, I, device) for _ in range(nslots)]
         self.ready = [torch.cuda.Event() for _ in range(nslots)]
         self.free = [torch.cuda.Event() for _ in range(nslots)]
         self.copy_stream = torch.cuda.Stream(device=device)
@@ -60,16 +48,14 @@ class ExpertRing:
             slot = self.slots[s]
             self.copy_stream.wait_event(self.free[s])
             for e in range(e0, e1):
-                host.copy_expert(e, slot.w13[e - e0], slot.w2[e - e0],
-                                 slot.s13[e - e0] if slot.s13 is not None else None,
-                                 slot.s2[e - e0] if slot.s2 is not None else None, self.copy_stream)
+                host.copy_slot(e, slot, e - e0, self.copy_stream)
             self.copied_bytes += (e1 - e0) * host.expert_bytes()
             self.ready[s].record(self.copy_stream)
             main.wait_event(self.ready[s])
-            view = slot if e1 - e0 == self.tile_e else M.ExpertWeights(
-                slot.fmt, slot.w13[: e1 - e0], slot.w2[: e1 - e0],
-                slot.s13[: e1 - e0] if slot.s13 is not None else None,
-                slot.s2[: e1 - e0] if slot.s2 is not None else None, True)
+            n = e1 - e0
+            cut = lambda t: None if t is None else t[:n]
+            view = slot if n == self.tile_e else M.ExpertWeights(
+                slot.fmt, slot.w13[:n], slot.w2[:n], cut(slot.s13), cut(slot.s2), True, cut(slot.gs13), cut(slot.gs2))
             M.moe_experts_partial(x, ids, weights, view, ws, lo=e0, act_limit=act_limit)
             self.free[s].record(main)
         return M.moe_combine(ws, ids, 0, E, shared=shared, out=out)
