@@ -74,6 +74,48 @@ __global__ void allreduce_sum_kernel(const void* const* peer_in, T* out, int64_t
   }
 }
 
+// Two-shot all-reduce: rank r sums slice r of every rank's input (reads over NVLink) and
+// stores the sum into slice r of every rank's output (writes over NVLink), so each byte
+// crosses the links twice instead of W-1 times (large tensors, e.g. prefill activations).
+template <typename T>
+__global__ void allreduce_twoshot_kernel(const void* const* peer_in, void* const* peer_out, int64_t n, int rank,
+                                         int world) {
+  const int64_t n8 = n / 8;
+  const int64_t per = (n8 + world - 1) / world;
+  const int64_t lo = per * rank, hi = min(n8, lo + per);
+  for (int64_t i = lo + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < hi; i += (int64_t)gridDim.x * blockDim.x) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int r = 0; r < world; ++r) {
+      const T* src = reinterpret_cast<const T*>(peer_in[r]) + i * 8;
+      if constexpr (sizeof(T) == 2) {
+        const uint4 v = *reinterpret_cast<const uint4*>(src);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          acc[2 * j] += bf16_lo(w[j]);
+          acc[2 * j + 1] += bf16_hi(w[j]);
+        }
+      } else {
+        const float4 a = *reinterpret_cast<const float4*>(src);
+        const float4 b = *reinterpret_cast<const float4*>(src + 4);
+        acc[0] += a.x; acc[1] += a.y; acc[2] += a.z; acc[3] += a.w;
+        acc[4] += b.x; acc[5] += b.y; acc[6] += b.z; acc[7] += b.w;
+      }
+    }
+    for (int r = 0; r < world; ++r) {
+      const int dst_rank = (rank + r) % world;     // stagger the destinations across ranks
+      T* dst = reinterpret_cast<T*>(peer_out[dst_rank]) + i * 8;
+      if constexpr (sizeof(T) == 2) {
+        *reinterpret_cast<uint4*>(dst) = make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]),
+                                                    pack_bf16x2(acc[4], acc[5]), pack_bf16x2(acc[6], acc[7]));
+      } else {
+        *reinterpret_cast<float4*>(dst) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        *reinterpret_cast<float4*>(dst + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
+      }
+    }
+  }
+}
+
 }  // namespace xtu
 
 using namespace xtu;
@@ -158,6 +200,31 @@ int xtu_allreduce_oneshot(void* const* peer_in, void* out, long long n, int dtyp
   else
     allreduce_sum_kernel<float><<<blocks, 256, 0, s>>>(reinterpret_cast<const void* const*>(peer_in), (float*)out,
                                                        n, world);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return -(int)e;
+  rc = xtu_peer_barrier(peer_flags, epoch, rank, world, status, timeout_ns, s);
+  return rc < 0 ? rc : 3;
+}
+
+// peer_in / peer_out: device arrays [world] of each rank's symmetric input / output; this
+// rank's input already written.  On return (in stream order) every rank's output holds the sum.
+int xtu_allreduce_twoshot(void* const* peer_in, void* const* peer_out, long long n, int dtype,
+                          void* const* peer_flags, int* epoch, int rank, int world, void* status, long long timeout_ns,
+                          cudaStream_t s) {
+  if (n <= 0) return 0;
+  if (n % 8) return -2;
+  int rc = xtu_peer_barrier(peer_flags, epoch, rank, world, status, timeout_ns, s);
+  if (rc < 0) return rc;
+  const int64_t slice8 = (n / 8 + world - 1) / world;
+  int blocks = (int)((slice8 + 255) / 256);
+  if (blocks > 148 * 4) blocks = 148 * 4;
+  if (blocks < 1) blocks = 1;
+  if (dtype == 0)
+    allreduce_twoshot_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(reinterpret_cast<const void* const*>(peer_in),
+                                                                   peer_out, n, rank, world);
+  else
+    allreduce_twoshot_kernel<float><<<blocks, 256, 0, s>>>(reinterpret_cast<const void* const*>(peer_in), peer_out, n,
+                                                           rank, world);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return -(int)e;
   rc = xtu_peer_barrier(peer_flags, epoch, rank, world, status, timeout_ns, s);

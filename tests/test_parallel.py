@@ -164,3 +164,83 @@ def _timeout_worker(rank, world, port):
 def test_peer_barrier_times_out_instead_of_hanging():
     _need_two_gpus()
     mp.spawn(_timeout_worker, args=(2, _port()), nprocs=2)
+
+
+# ----------------------------------------------------------------------------- tensor parallel
+def _tp_cfg(name):
+    from vllm_xtu_moe_b200.models.config import get_preset, scaled_down
+    cfg = get_preset(name)
+    return scaled_down(cfg, layers=4 if "qwen" in name else 2, hidden=256, experts=8).replace(
+        num_heads=4, num_kv_heads=2, head_dim=64 if not cfg.is_mla else cfg.head_dim, moe_intermediate=256,
+        shared_intermediate=256, dense_intermediate=512, linear_num_key_heads=2, linear_num_value_heads=4,
+        linear_key_head_dim=32, linear_value_head_dim=32, q_lora_rank=64 if cfg.is_mla else 0,
+        kv_lora_rank=64 if cfg.is_mla else 0, qk_nope_head_dim=32 if cfg.is_mla else 0,
+        v_head_dim=32 if cfg.is_mla else 0, rotary_dim=32 if cfg.rotary_dim else None, num_mtp_layers=0,
+        dense_fmt="bf16", expert_fmt="bf16")
+
+
+def _tp_logits(model, device):
+    from vllm_xtu_moe_b200.engine import LLM, SamplingParams
+    from vllm_xtu_moe_b200.engine.runner import RunnerConfig
+    llm = LLM(model, device=device, runner_config=RunnerConfig(block_size=64 if device != "cpu" else 16, max_seqs=2,
+                                                                max_model_len=256, max_batched_tokens=128,
+                                                                use_cuda_graph=False))
+    for p in ([3, 4, 5, 6, 7, 8, 9, 10, 11], list(range(20, 60))):
+        llm.add_request(p, SamplingParams(max_tokens=1))
+    plan = llm.scheduler.schedule()
+    ids, meta = llm.runner.build_meta(plan)
+    rows = torch.tensor([meta.q_start_host[i + 1] - 1 for i in range(meta.num_seqs)], device=model.device)
+    _, _, _, logits = llm.runner.forward(ids, meta, rows)
+    return logits.float().cpu()
+
+
+def _tp_cpu_worker(rank, world, port, name):
+    from vllm_xtu_moe_b200.models.model import build_model
+    from vllm_xtu_moe_b200.parallel.tp import TPReducer, build_tp_model
+    _init(rank, world, port, "gloo")
+    cfg = _tp_cfg(name)
+    ref = build_model(cfg, device="cpu", seed=4)
+    ref.act_dtype = torch.float32
+    red = TPReducer(256, cfg.hidden_size, mode="nccl")
+    m = build_tp_model(cfg, rank, world, "cpu", seed=4, reducer=red)
+    m.act_dtype = torch.float32
+    a, b = _tp_logits(ref, "cpu"), _tp_logits(m, "cpu")
+    assert red.calls == 2 * cfg.num_layers
+    err = (a - b).abs().max().item() / a.abs().max().item()
+    assert err < 1e-3, (name, err)
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("name", ["glm-4.5-air", "qwen3-next-80b-a3b", "deepseek-v3"])
+def test_tensor_parallel_matches_single_rank_cpu(name):
+    mp.spawn(_tp_cpu_worker, args=(2, _port(), name), nprocs=2)
+
+
+def _tp_gpu_worker(rank, world, port):
+    from vllm_xtu_moe_b200.models.model import build_model
+    from vllm_xtu_moe_b200.ops import _native as N
+    from vllm_xtu_moe_b200.parallel.tp import TPReducer, build_tp_model
+    _init(rank, world, port, "nccl")
+    d = torch.device("cuda", rank)
+    cfg = _tp_cfg("glm-4.5-air").replace(hidden_size=512, num_heads=8, dense_fmt="fp8", expert_fmt="fp8")
+    ref = build_model(cfg, device=d, seed=4)
+    red = TPReducer(256, cfg.hidden_size, device=d, mode="p2p")
+    m = build_tp_model(cfg, rank, world, d, seed=4, reducer=red)
+    a, b = _tp_logits(ref, str(d)), _tp_logits(m, str(d))
+    torch.cuda.synchronize(d)
+    N.check_status(d)
+    err = (a - b).abs().max().item() / a.abs().max().item()
+    assert err < 5e-2, err
+    # both ranks hold identical activations -> identical logits
+    other = [torch.empty_like(b) for _ in range(world)]
+    dist.all_gather_object(other, b)
+    assert torch.equal(other[0], other[1])
+    red.close()
+    dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+@pytest.mark.multigpu
+def test_tensor_parallel_p2p_matches_single_gpu():
+    _need_two_gpus()
+    mp.spawn(_tp_gpu_worker, args=(2, _port()), nprocs=2)

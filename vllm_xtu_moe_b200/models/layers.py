@@ -158,6 +158,7 @@ class MoEBlock:
         self.last_ids: torch.Tensor | None = None
         self.tracer = None                # utils.trace.Tracer (routing dump) when enabled
         self.trace_idx = layer_idx
+        self.expert_lo = 0                # first global expert id held here (expert parallel over TP ranks)
 
     def route(self, x: torch.Tensor):
         logits = G.linear(x, self.gate, out_dtype=torch.float32)
@@ -178,7 +179,8 @@ class MoEBlock:
                 sh = (sh.float() * g).to(x.dtype)
         if self.executor is not None:
             return self.executor(self, x, ids, w, sh)
-        return M.fused_moe(x, ids, w, self.experts, self.workspace(x), shared=sh, act_limit=self.cfg.swiglu_limit)
+        return M.fused_moe(x, ids, w, self.experts, self.workspace(x), lo=self.expert_lo, shared=sh,
+                           act_limit=self.cfg.swiglu_limit)
 
     def workspace(self, x: torch.Tensor) -> M.MoEWorkspace | None:
         if not x.is_cuda:

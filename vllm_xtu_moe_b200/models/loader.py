@@ -126,8 +126,8 @@ class CheckpointSource:
 
     zeros = ones
 
-    def param(self, name: str, make):
-        ref = make()
+    def param(self, name: str, make, n: int):
+        ref = make(n)
         return self._get(self._hf(name)[0]).to(device=self.device, dtype=ref.dtype, copy=True).view(ref.shape)
 
     def linear(self, name, n, k, fmt="bf16", bias=False, std=None) -> Linear:

@@ -25,6 +25,7 @@ from .mla import MLAAttention
 class DecoderLayer:
     def __init__(self, idx: int, attn_norm: RMSNorm, attn, mlp_norm: RMSNorm, mlp, kind: str):
         self.idx, self.attn_norm, self.attn, self.mlp_norm, self.mlp, self.kind = idx, attn_norm, attn, mlp_norm, mlp, kind
+        self.reduce = None      # tensor parallel: sums the ranks' partial outputs (parallel.tp)
 
     def __call__(self, x, residual, meta, kv, rope):
         if residual is None:
@@ -33,8 +34,13 @@ class DecoderLayer:
         else:
             h, residual = self.attn_norm(x, residual)
         h = self.attn(h, meta, kv, rope)
+        if self.reduce is not None:
+            h = self.reduce(h)
         h, residual = self.mlp_norm(h, residual)
-        return self.mlp(h), residual
+        h = self.mlp(h)
+        if self.reduce is not None:
+            h = self.reduce(h)
+        return h, residual
 
     def tensors(self):
         return self.attn_norm.tensors() + self.attn.tensors() + self.mlp_norm.tensors() + self.mlp.tensors()
@@ -246,9 +252,9 @@ class WeightFactory:
     def zeros(self, shape, dtype=torch.bfloat16, name: str | None = None):
         return torch.zeros(*shape, dtype=dtype, device=self.device)
 
-    def param(self, name: str, make):
-        """A tensor with a fixed synthetic value (``make()``); checkpoint sources load it by name."""
-        return make()
+    def param(self, name: str, make, n: int):
+        """A length-n tensor with a fixed synthetic value (``make(n)``); checkpoint sources load it by name."""
+        return make(n)
 
     def linear(self, name, n, k, fmt="bf16", bias=False, std=None) -> Linear:
         std = std if std is not None else self.std
@@ -340,9 +346,9 @@ def build_layer(f: WeightFactory, cfg: ModelConfig, i: int, expert_sink=None, na
         attn = GatedDeltaNet(cfg, f.linear(name + ".qkvz", 2 * nk * dk + 2 * nv * dv, H, dfmt),
                              f.linear(name + ".ba", 2 * nv, H, "bf16"),
                              f.normal(name + ".conv", (ch, cfg.linear_conv_kernel), 0.3),
-                             f.param(name + ".A_log", lambda: torch.log(torch.linspace(1.0, 16.0, nv,
-                                                                                      device=f.device)).float()),
-                             f.param(name + ".dt_bias", lambda: torch.zeros(nv, device=f.device).float()),
+                             f.param(name + ".A_log", lambda n: torch.log(torch.linspace(1.0, 16.0, n,
+                                                                                        device=f.device)).float(), nv),
+                             f.param(name + ".dt_bias", lambda n: torch.zeros(n, device=f.device).float(), nv),
                              f.ones((dv,), name=name + ".gdn_norm"), f.linear(name + ".out", H, nv * dv, dfmt))
     elif cfg.is_mla:
         nh = cfg.num_heads

@@ -57,6 +57,7 @@ _SIGS: dict[str, list] = {
     "xtu_ipc_close": [P],
     "xtu_peer_barrier": [P, P, c_int, c_int, P, ctypes.c_longlong, P],
     "xtu_allreduce_oneshot": [P, P, ctypes.c_longlong, c_int, P, P, c_int, c_int, P, ctypes.c_longlong, P],
+    "xtu_allreduce_twoshot": [P, P, ctypes.c_longlong, c_int, P, P, c_int, c_int, P, ctypes.c_longlong, P],
     "xtu_ep_route": [P, c_int, c_int, c_int, c_int, c_int, P, P, P, P, P, P, P, ctypes.c_longlong, P],
     "xtu_ep_dispatch": [P, P, c_int, c_int, c_int, c_int, c_int, P, c_int, c_int, P, P, P, P, P, c_int, P],
     "xtu_silu_mul": [P, c_int, c_int, c_float, c_float, c_float, P, P],

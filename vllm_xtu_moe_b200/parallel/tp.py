@@ -1,0 +1,275 @@
+"""Tensor parallelism over the GPUs of one node (attention / dense / shared expert split
+across ranks, routed experts split by expert id), the reference's TP=2 + EP layout
+(X1/X2: vLLM column/row-parallel linears, experts divided over TP ranks, partial sums
+reduced after o_proj and after the MoE block, vllm_xiaotu_moe/hybrid_model.py:943-967,
+1987, 2041).
+
+* ``TPWeightFactory`` wraps any weight source (seeded synthetic or a checkpoint) and
+  hands the model builder this rank's slices: query / key-value heads of the fused
+  qkv, o_proj input columns, gate/up rows and down columns of dense and shared MLPs,
+  DeltaNet key/value heads, MLA heads, and an expert range [r*E/T, (r+1)*E/T).  fp8
+  block-scaled tensors are sliced exactly when the cut falls on 128-row/column
+  boundaries and re-blocked otherwise.
+* ``TPReducer`` sums the ranks' partial outputs through the peer-memory heap: a
+  one-shot kernel (every rank reads every peer) for decode-sized tensors and a two-shot
+  kernel (reduce one slice, store it into every rank) for prefill-sized ones; both sum
+  in rank order, so every rank holds bit-identical activations and samples the same
+  tokens.  ``nccl`` mode uses ``torch.distributed.all_reduce`` instead (baseline).
+* ``build_tp_model`` builds the rank's model and installs the reducer in every layer.
+"""
+from __future__ import annotations
+
+import dataclasses
+
+import torch
+import torch.distributed as dist
+
+from ..models.config import ModelConfig
+from ..models.layers import Linear, MoEBlock
+from ..models.model import WeightFactory, build_model
+from ..ops import _native as N
+from ..ops.quant import dequant_fp8_block, quant_fp8_block
+from .comm import PeerGroup
+
+
+def local_config(cfg: ModelConfig, tp: int) -> ModelConfig:
+    """Per-rank sizes (heads, intermediate widths); expert count stays global (router)."""
+    def div(x, what):
+        if x % tp:
+            raise ValueError(f"{what}={x} is not divisible by tensor-parallel size {tp}")
+        return x // tp
+    kw = dict(num_heads=div(cfg.num_heads, "num_heads"))
+    if not cfg.is_mla:
+        kw["num_kv_heads"] = cfg.num_kv_heads // tp if cfg.num_kv_heads >= tp else 1
+        if cfg.num_kv_heads >= tp:
+            div(cfg.num_kv_heads, "num_kv_heads")
+        elif tp % cfg.num_kv_heads:
+            raise ValueError("tp must be a multiple of num_kv_heads when kv heads are replicated")
+    if cfg.dense_intermediate:
+        kw["dense_intermediate"] = div(cfg.dense_intermediate, "dense_intermediate")
+    if cfg.shared_intermediate:
+        kw["shared_intermediate"] = div(cfg.shared_intermediate, "shared_intermediate")
+    if cfg.linear_num_key_heads:
+        kw["linear_num_key_heads"] = div(cfg.linear_num_key_heads, "linear_num_key_heads")
+        kw["linear_num_value_heads"] = div(cfg.linear_num_value_heads, "linear_num_value_heads")
+    if cfg.num_experts:
+        div(cfg.num_experts, "num_experts")
+    return cfg.replace(**kw)
+
+
+def _runs(idx: list[int]) -> list[tuple[int, int]]:
+    out = []
+    for i in idx:
+        if out and out[-1][1] == i:
+            out[-1] = (out[-1][0], i + 1)
+        else:
+            out.append((i, i + 1))
+    return out
+
+
+def _take(lin: Linear, rows: list[int] | None, cols: list[int] | None) -> Linear:
+    w, s, b = lin.weight, lin.scale, lin.bias
+    ri = None if rows is None else torch.tensor(rows, device=w.device)
+    ci = None if cols is None else torch.tensor(cols, device=w.device)
+    if s is None:
+        if ri is not None:
+            w = w.index_select(0, ri)
+        if ci is not None:
+            w = w.index_select(1, ci)
+        return Linear(w.contiguous(), None, None if b is None else (b if ri is None else b.index_select(0, ri)))
+    aligned = all(a % 128 == 0 and (e - a) % 128 == 0 for a, e in _runs(rows or [])) and \
+        all(a % 128 == 0 and (e - a) % 128 == 0 for a, e in _runs(cols or []))
+    if aligned:
+        wq = w.view(torch.uint8)
+        if ri is not None:
+            wq = wq.index_select(0, ri)
+            s = s.index_select(0, torch.tensor(sorted({r // 128 for r in rows}), device=w.device))
+        if ci is not None:
+            wq = wq.index_select(1, ci)
+            s = s.index_select(1, torch.tensor(sorted({c // 128 for c in cols}), device=w.device))
+        w = wq.contiguous().view(torch.float8_e4m3fn)
+    else:                                  # cut inside a scale block: widen, slice, re-block
+        d = dequant_fp8_block(w, s)
+        if ri is not None:
+            d = d.index_select(0, ri)
+        if ci is not None:
+            d = d.index_select(1, ci)
+        w, s = quant_fp8_block(d.contiguous())
+    if b is not None and ri is not None:
+        b = b.index_select(0, ri)
+    return Linear(w, s.contiguous(), b)
+
+
+class TPWeightFactory:
+    """This rank's slices of the tensors of a full-size source (see module docstring)."""
+
+    def __init__(self, base, full: ModelConfig, rank: int, tp: int):
+        self.base, self.full, self.rank, self.tp = base, full, rank, tp
+        self.device = base.device
+        self.expert_lo = 0
+
+    # -------------------------------------------------------------- index helpers
+    def _heads(self, n: int) -> list[int]:
+        per = n // self.tp
+        return list(range(self.rank * per, (self.rank + 1) * per))
+
+    def _kv_heads(self) -> list[int]:
+        c = self.full
+        if c.num_kv_heads >= self.tp:
+            return self._heads(c.num_kv_heads)
+        return [self.rank * c.num_kv_heads // self.tp]
+
+    @staticmethod
+    def _expand(heads: list[int], width: int, base: int = 0) -> list[int]:
+        return [base + h * width + i for h in heads for i in range(width)]
+
+    def _rows_cols(self, name: str):
+        """-> (full_n, full_k, rows or None, cols or None) for a sliced linear, or None if replicated."""
+        c, T = self.full, self.tp
+        H = c.hidden_size
+        suf = name.rsplit(".", 1)[-1]
+        if suf == "qkv":
+            hd = c.head_dim
+            qw = hd * (2 if c.attn_output_gate else 1)
+            nq, nkv = c.num_heads * qw, c.num_kv_heads * hd
+            rows = (self._expand(self._heads(c.num_heads), qw) + self._expand(self._kv_heads(), hd, nq) +
+                    self._expand(self._kv_heads(), hd, nq + nkv))
+            return nq + 2 * nkv, H, rows, None
+        if suf == "o" and c.is_mla:
+            return H, c.num_heads * c.v_head_dim, None, self._expand(self._heads(c.num_heads), c.v_head_dim)
+        if suf == "o":
+            return H, c.num_heads * c.head_dim, None, self._expand(self._heads(c.num_heads), c.head_dim)
+        if suf == "q_b":
+            w = c.qk_nope_head_dim + c.qk_rope_head_dim
+            return c.num_heads * w, c.q_lora_rank or H, self._expand(self._heads(c.num_heads), w), None
+        if suf == "kv_b":
+            w = c.qk_nope_head_dim + c.v_head_dim
+            return c.num_heads * w, c.kv_lora_rank, self._expand(self._heads(c.num_heads), w), None
+        if suf in ("qkvz", "ba", "out") and c.linear_num_key_heads:
+            nk, nv, dk, dv = c.linear_num_key_heads, c.linear_num_value_heads, c.linear_key_head_dim, c.linear_value_head_dim
+            r = nv // nk
+            if suf == "qkvz":
+                w = 2 * dk + 2 * r * dv
+                return nk * w, H, self._expand(self._heads(nk), w), None
+            if suf == "ba":
+                return nk * 2 * r, H, self._expand(self._heads(nk), 2 * r), None
+            return H, nv * dv, None, self._expand(self._heads(nv), dv)
+        if suf == "gate_up":
+            I = c.dense_intermediate if ".mlp." in name else c.shared_intermediate * max(1, c.num_shared_experts)
+            per = I // T
+            g = list(range(self.rank * per, (self.rank + 1) * per))
+            return 2 * I, H, g + [I + i for i in g], None
+        if suf == "down":
+            I = c.dense_intermediate if ".mlp." in name else c.shared_intermediate * max(1, c.num_shared_experts)
+            per = I // T
+            return H, I, None, list(range(self.rank * per, (self.rank + 1) * per))
+        return None
+
+    # -------------------------------------------------------------- factory interface
+    def linear(self, name, n, k, fmt="bf16", bias=False, std=None) -> Linear:
+        spec = self._rows_cols(name)
+        if spec is None:
+            return self.base.linear(name, n, k, fmt, bias, std)
+        fn, fk, rows, cols = spec
+        full = self.base.linear(name, fn, fk, fmt, bias, std)
+        out = _take(full, rows, cols)
+        assert tuple(out.weight.shape) == (n, k), (name, tuple(out.weight.shape), (n, k))
+        return out
+
+    def normal(self, name, shape, std=None, dtype=torch.bfloat16):
+        c = self.full
+        if name.endswith(".conv") and c.linear_num_key_heads:
+            nk, nv, dk, dv = c.linear_num_key_heads, c.linear_num_value_heads, c.linear_key_head_dim, c.linear_value_head_dim
+            full = self.base.normal(name, (2 * nk * dk + nv * dv, shape[1]), std, dtype)
+            kh = self._heads(nk)
+            ch = self._expand(kh, dk) + self._expand(kh, dk, nk * dk) + self._expand(self._heads(nv), dv, 2 * nk * dk)
+            return full.index_select(0, torch.tensor(ch, device=full.device)).contiguous()
+        return self.base.normal(name, shape, std, dtype)
+
+    def ones(self, shape, dtype=torch.bfloat16, name=None):
+        return self.base.ones(shape, dtype, name=name)
+
+    def zeros(self, shape, dtype=torch.bfloat16, name=None):
+        return self.base.zeros(shape, dtype, name=name)
+
+    def param(self, name, make, n):
+        full_n = self.full.linear_num_value_heads if name.endswith((".A_log", ".dt_bias")) else n
+        t = self.base.param(name, make, full_n)
+        if full_n != n:
+            t = t[self.rank * n:(self.rank + 1) * n].contiguous()
+        return t
+
+    def experts(self, name, E, H, I, fmt) -> dict:
+        raw = self.base.experts(name, E, H, I, fmt)
+        El = E // self.tp
+        lo = self.rank * El
+        self.expert_lo = lo
+        return {k: (v[lo:lo + El].contiguous() if isinstance(v, torch.Tensor) else v) for k, v in raw.items()}
+
+
+class TPReducer:
+    """Sum of the ranks' partial [T, H] outputs (P2P one-shot / two-shot, or NCCL)."""
+
+    ONESHOT_BYTES = 256 << 10
+
+    def __init__(self, max_tokens: int, hidden: int, group=None, device=None, mode: str = "p2p"):
+        self.mode = mode
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.n_max = max_tokens * hidden
+        if mode == "p2p":
+            nb = self.n_max * 2
+            self.pg = PeerGroup(PeerGroup.heap_bytes_for(nb, nb), group=group, device=device)
+            self.inb = self.pg.alloc((self.n_max,), torch.bfloat16)
+            self.outb = self.pg.alloc((self.n_max,), torch.bfloat16)
+        self.calls = 0
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        self.calls += 1
+        if self.mode == "nccl":
+            y = x.contiguous()
+            dist.all_reduce(y, group=self.group)
+            return y
+        n = x.numel()
+        if n > self.n_max or n % 8:
+            raise ValueError(f"TP reduce of {n} elements (capacity {self.n_max}, multiple of 8 required)")
+        self.inb.local[:n].copy_(x.reshape(-1))
+        pg = self.pg
+        if n * 2 <= self.ONESHOT_BYTES:
+            out = torch.empty_like(x)
+            N.call("xtu_allreduce_oneshot", self.inb.ptr(), out.data_ptr(), n, 0, pg.flags.ptr(),
+                   pg.epoch.data_ptr(), pg.rank, pg.world, pg.status.data_ptr(), pg.timeout_ns,
+                   N.stream_ptr(x.device))
+            return out
+        N.call("xtu_allreduce_twoshot", self.inb.ptr(), self.outb.ptr(), n, 0, pg.flags.ptr(), pg.epoch.data_ptr(),
+               pg.rank, pg.world, pg.status.data_ptr(), pg.timeout_ns, N.stream_ptr(x.device))
+        return self.outb.local[:n].view_as(x).clone()
+
+    def close(self):
+        if self.mode == "p2p":
+            self.pg.close()
+
+
+def build_tp_model(cfg: ModelConfig, rank: int, tp: int, device, seed: int = 0, source=None,
+                   reducer: TPReducer | None = None, num_layers: int | None = None):
+    """This rank's shard of the model (random init or ``source``) with the reducer installed."""
+    base = source if source is not None else WeightFactory(seed, device)
+    f = TPWeightFactory(base, cfg, rank, tp)
+    lcfg = local_config(cfg, tp)
+    lo_by_layer = {}
+
+    def sink(layer, raw):
+        lo_by_layer.setdefault(layer, []).append(f.expert_lo)
+        from ..ops import moe as M
+        return M.prepare_experts(raw["fmt"], raw["w13"], raw["w2"], raw.get("s13"), raw.get("s2"),
+                                 raw.get("gs13"), raw.get("gs2"))
+
+    m = build_model(lcfg, device=device, seed=seed, expert_sink=sink, num_layers=num_layers, source=f)
+    El = cfg.num_experts // tp if cfg.num_experts else 0
+    for l in m.layers + [mt.layer for mt in m.mtp]:
+        l.reduce = reducer
+        if isinstance(l.mlp, MoEBlock):
+            l.mlp.expert_lo = rank * El
+    m.tp = (rank, tp)
+    return m
