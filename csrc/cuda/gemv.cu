@@ -3,30 +3,36 @@
 //   y[m, n] = sum_k x[m, k] * W[n, k]     (m < M <= 16, W bf16 or e4m3 + 128x128 fp32 scales)
 //
 // At decode the GEMMs see 1..16 rows, so the job is to stream the weights at HBM
-// bandwidth.  A SIMT dot product spends ~5-12 instructions per weight byte on
-// conversions and FMAs and ends up issue-bound; here the multiply-adds go to the
-// tensor cores through warp-level mma.sync m16n8k16 instead:
+// bandwidth.  A CTA owns one 32-row weight tile and streams it through a ring of
+// shared-memory stages filled by TMA (one elected producer thread, 128-byte swizzled
+// 16-row boxes, STAGES x 8 KB in flight per CTA, several CTAs per SM), so the bytes in
+// flight do not depend on how many loads the compute threads can keep outstanding.
+// Four consumer warps split every stage along k and do the multiply-adds on the tensor
+// cores with warp-level mma.sync m16n8k16:
 //   * A = 16 weight rows x 16 k, B = 16 k x 8 tokens, D = 16 rows x 8 tokens (fp32).
 //   * The order of k inside each MMA is permuted (a dot product does not care) so that
-//     lane t's A fragment comes from ONE contiguous 16-byte load of row (t/4) and one of
-//     row (t/4 + 8): lane t owns physical k = 16*(t%4) + [0, 16) of a 64-k chunk (fp8)
-//     and feeds MMA g in 0..3 with k = 16*(t%4) + 4g + {0,1 | 2,3}.  Its B fragment is
-//     the same k slice of token t/4, so A and B agree on the permutation.
+//     lane t's A fragment is ONE 16-byte shared-memory load of row (t/4) and one of row
+//     (t/4 + 8): lane t owns k = 16*(t%4) + [0, 16) of its warp's 64-k slice (fp8) and
+//     feeds MMA g in 0..3 with k = 16*(t%4) + 4g + {0,1 | 2,3}.  Its B fragment is the
+//     same k slice of token t/4, so A and B agree on the permutation.
 //   * fp8: e4m3 pairs -> f16 pairs with one cvt each (exact), activations -> f16 scaled
 //     by 2^-8 (keeps x * 448 inside fp16 range; the scale and 2^8 are restored in fp32
-//     with the block scale, once per 64-k chunk).  bf16 weights use the bf16 MMA with
-//     no conversion at all.
-//   * Each warp streams two 16-row tiles with the next chunk's loads issued before the
-//     current chunk's MMAs.  Warps are persistent and stride over row slices.
+//     with the block scale once per 64-k slice).  bf16 weights use the bf16 MMA as is.
+//   * Activations and block scales of the next stage are loaded while the current one
+//     is multiplied; the four warps' partial sums meet in shared memory at the end.
 // Grouped (MoE) forms take the routing permutation of moe_permute: expert e owns rows
-// seg[e]..seg[e+1] of the permuted activations.
-//   * gate/up: the two row tiles are 16 gate rows and the matching 16 up rows (W13 rows
-//     interleaved in 256-row blocks), so SwiGLU is applied in registers and the
-//     [T*K, 2I] intermediate never exists.
+// seg[e]..seg[e+1] of the permuted activations, and the grid's y index walks the list of
+// experts that have rows (moe_active_kernel), so idle experts cost no CTAs.
+//   * gate/up: the tile's two 16-row halves are 16 gate rows and the matching 16 up rows
+//     (W13 rows interleaved in 256-row blocks), so SwiGLU is applied in registers and
+//     the [T*K, 2I] intermediate never exists.
 //   * down: rows scaled by the pair's routing weight and written to the pair's slot row.
+// Dense calls with few tiles split K across CTAs; the last CTA of a tile (completion
+// counter) sums the fp32 partials.
 // Replaces the reference's SIMT small-M MXFP4 kernel (xiaotu_moe/csrc/moe4_smallm.cu,
 // sm_80 FP32 FMA, split-K atomics) and the FP8 pair-centric Triton decode kernels
 // (vllm_xiaotu_moe/decode_moe_fp8.py:23-138).
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_fp8.h>
@@ -72,147 +78,188 @@ __device__ __forceinline__ uint32_t u4w(const uint4& v, int i) {
   return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
 }
 
-constexpr int GEMV_WARPS = 8;
+constexpr int GV_CWARPS = 4;                 // consumer warps (warp 0 is the producer)
+constexpr int GV_THREADS = 32 * (1 + GV_CWARPS);
+constexpr int GV_STAGES = 6;
+constexpr int GV_ROW_BYTES = 256;            // bytes of one weight row per stage (2 x 128-B boxes)
+constexpr int GV_STAGE_BYTES = 32 * GV_ROW_BYTES;   // 32 rows
 
-// One warp: two 16-row weight tiles (base rows rb[0], rb[1]; row pitch K elements) times
-// the activation rows x_row0 .. x_row0 + mcount (mcount <= 8*NT).
-// Out: acc[tile][nt][4] = D fragments (row g4 / g4+8, tokens nt*8 + 2*tq + {0,1}).
-template <bool FP8, int NT, bool PX = false>
-__device__ __forceinline__ void warp_mma_gemv(const uint8_t* __restrict__ W, const float* __restrict__ wscale,
-                                              int sk, int N, int K, const int (&rb)[2],
-                                              const __nv_bfloat16* __restrict__ x, int x_row0, int x_stride,
-                                              int mcount, int c_begin, int c_end, float (&acc)[2][NT][4]) {
-  constexpr int CK = FP8 ? 64 : 32;          // k per chunk (a lane loads 16 bytes of each of its rows)
-  constexpr int LK = FP8 ? 16 : 8;           // k per lane per chunk
-  constexpr int EB = FP8 ? 1 : 2;
-  const int lane = threadIdx.x & 31;
-  const int g4 = lane >> 2, tq = lane & 3;
+template <int NT>
+struct GvSmem {
+  static constexpr int RED_FLOATS = GV_CWARPS * 32 * 2 * NT * 4;
+  static constexpr int BYTES = 1024 + GV_STAGES * GV_STAGE_BYTES + RED_FLOATS * 4 + 2 * GV_STAGES * 8 + 64;
+};
+
+// Stream one 32-row tile (rows row0[0]..+15 and row0[1]..+15 of the tensor map) over
+// stages [s_begin, s_end) and multiply by activations x (rows x_row0 .. x_row0 + mcount).
+// Producer: warp 0.  Consumers: warps 1..4, each with acc[tile][nt][4] for its k slices.
+// Returns false (all threads) if a wait timed out.
+template <bool FP8, int NT>
+__device__ __forceinline__ bool gv_stream_tile(const CUtensorMap* tmap, uint8_t* stages, uint64_t* full,
+                                               uint64_t* empty, uint32_t& phase_base, const int (&row0)[2],
+                                               int s_begin, int s_end, int K, const float* __restrict__ wscale,
+                                               int sk, int scale_row_blk0, int scale_row_blk1,
+                                               const __nv_bfloat16* __restrict__ x, int x_row0, int x_stride,
+                                               int mcount, float (&acc)[2][NT][4], XtuStatus* st) {
+  constexpr int CK = FP8 ? 64 : 32;          // k per warp per stage
+  constexpr int LK = FP8 ? 16 : 8;           // k per lane per stage
+  constexpr int KSTAGE = GV_ROW_BYTES / (FP8 ? 1 : 2);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nst = s_end - s_begin;
+  bool ok = true;
 #pragma unroll
   for (int t = 0; t < 2; ++t)
 #pragma unroll
     for (int n = 0; n < NT; ++n)
 #pragma unroll
       for (int i = 0; i < 4; ++i) acc[t][n][i] = 0.f;
-  // the two rows of each tile this lane loads (clamped for loads; writes are masked by the caller)
-  size_t roff[2][2];
+  if (warp == 0) {
+    if (elect_one()) {
+      int issued = 0;
+      for (int i = 0; i < nst; ++i) {
+        const uint32_t it = phase_base + i;
+        const int slot = it % GV_STAGES;
+        if (it >= GV_STAGES && !mbar_wait(&empty[slot], ((it / GV_STAGES) - 1) & 1, st, 60)) { ok = false; break; }
+        ++issued;
+        mbar_arrive_expect_tx(&full[slot], GV_STAGE_BYTES);
+        uint8_t* dst = stages + slot * GV_STAGE_BYTES;
+        const int kb = (s_begin + i) * KSTAGE;   // first k (elements) of the stage
 #pragma unroll
-  for (int t = 0; t < 2; ++t) {
-    roff[t][0] = (size_t)min(rb[t] + g4, N - 1) * K;
-    roff[t][1] = (size_t)min(rb[t] + g4 + 8, N - 1) * K;
-  }
-  if (c_begin >= c_end) return;
-  // raw activations of token (nt*8 + g4) for the lane's k slice (LK bf16 = LK/8 uint4)
-  auto load_x = [&](int k, uint4 (&xr)[NT][LK / 8]) {
+        for (int b = 0; b < 2; ++b)
 #pragma unroll
-    for (int n = 0; n < NT; ++n) {
-      const int tok = n * 8 + g4;
-      const bool ok = tok < mcount && k < K;
-      const uint4* xp = reinterpret_cast<const uint4*>(x + (size_t)(x_row0 + (ok ? tok : 0)) * x_stride + (ok ? k : 0));
-#pragma unroll
-      for (int q = 0; q < LK / 8; ++q) xr[n][q] = ok ? __ldg(xp + q) : make_uint4(0, 0, 0, 0);
-    }
-  };
-  uint4 w[2][2], wn[2][2];
-  uint4 xr[NT][LK / 8], xn[NT][LK / 8];
-  {
-    const int k = c_begin * CK + tq * LK;
-#pragma unroll
-    for (int t = 0; t < 2; ++t)
-#pragma unroll
-      for (int h = 0; h < 2; ++h)
-        w[t][h] = k < K ? __ldg(reinterpret_cast<const uint4*>(W + (roff[t][h] + k) * EB)) : make_uint4(0, 0, 0, 0);
-    load_x(k, xr);
-  }
-  for (int c = c_begin; c < c_end; ++c) {
-    const int k = c * CK + tq * LK;
-    if (c + 1 < c_end) {
-      const int kn = k + CK;
-#pragma unroll
-      for (int t = 0; t < 2; ++t)
-#pragma unroll
-        for (int h = 0; h < 2; ++h)
-          wn[t][h] = kn < K ? __ldg(reinterpret_cast<const uint4*>(W + (roff[t][h] + kn) * EB))
-                            : make_uint4(0, 0, 0, 0);
-      if (PX) load_x(kn, xn);
-    }
-    if (!PX && c != c_begin) load_x(k, xr);
-    uint32_t b[NT][LK / 2];
-#pragma unroll
-    for (int n = 0; n < NT; ++n)
-#pragma unroll
-      for (int q = 0; q < LK / 8; ++q)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) b[n][4 * q + i] = FP8 ? bf16x2_f16x2_s8(u4w(xr[n][q], i)) : u4w(xr[n][q], i);
-    float d[2][NT][4];
-#pragma unroll
-    for (int t = 0; t < 2; ++t)
-#pragma unroll
-      for (int n = 0; n < NT; ++n)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) d[t][n][i] = 0.f;
-#pragma unroll
-    for (int g = 0; g < LK / 4; ++g) {
-#pragma unroll
-      for (int t = 0; t < 2; ++t) {
-        uint32_t a0, a1, a2, a3;
-        if (FP8) {
-          const uint32_t wa = u4w(w[t][0], g), wb = u4w(w[t][1], g);
-          a0 = e4m3x2_f16x2(wa);          // row g4,   k 4g, 4g+1
-          a1 = e4m3x2_f16x2(wb);          // row g4+8
-          a2 = e4m3x2_f16x2(wa >> 16);    // row g4,   k 4g+2, 4g+3
-          a3 = e4m3x2_f16x2(wb >> 16);    // row g4+8
-        } else {
-          a0 = u4w(w[t][0], 2 * g);
-          a1 = u4w(w[t][1], 2 * g);
-          a2 = u4w(w[t][0], 2 * g + 1);
-          a3 = u4w(w[t][1], 2 * g + 1);
-        }
-#pragma unroll
-        for (int n = 0; n < NT; ++n) {
-          if (FP8) mma_f16_16816(d[t][n], a0, a1, a2, a3, b[n][2 * g], b[n][2 * g + 1]);
-          else mma_bf16_16816(d[t][n], a0, a1, a2, a3, b[n][2 * g], b[n][2 * g + 1]);
+          for (int h = 0; h < 2; ++h)
+            tma_load_2d(dst + b * 4096 + h * 2048, tmap, &full[slot], kb + b * (KSTAGE / 2), row0[h]);
+      }
+      if (!ok) {   // give the copies already issued (bounded) time to land before the CTA exits
+        for (int j = issued > GV_STAGES ? issued - GV_STAGES : 0; j < issued; ++j) {
+          const uint32_t it = phase_base + j;
+          mbar_wait(&full[it % GV_STAGES], (it / GV_STAGES) & 1, nullptr, 0, 50000000ull);
         }
       }
     }
-    // fp8: block scale of (tile rows, this chunk) and the 2^8 activation pre-scale
+    __syncwarp();
+  } else {
+    const int cw = warp - 1;
+    const int g4 = lane >> 2, tq = lane & 3;
+    const int c16 = (cw & 1) * 4 + tq;     // 16-byte chunk of the 128-byte row within box (cw >> 1)
+    auto load_x = [&](int s, uint4 (&xr)[NT][LK / 8]) {
+      const int k = s * KSTAGE + cw * CK + tq * LK;
 #pragma unroll
-    for (int t = 0; t < 2; ++t) {
-      float sc = 1.f;
-      if (FP8) sc = 256.f * __ldg(wscale + (size_t)(min(rb[t], N - 1) >> 7) * sk + ((c * CK) >> 7));
+      for (int n = 0; n < NT; ++n) {
+        const int tok = n * 8 + g4;
+        const bool okx = tok < mcount && k < K;
+        const uint4* xp =
+            reinterpret_cast<const uint4*>(x + (size_t)(x_row0 + (okx ? tok : 0)) * x_stride + (okx ? k : 0));
+#pragma unroll
+        for (int q = 0; q < LK / 8; ++q) xr[n][q] = okx ? __ldg(xp + q) : make_uint4(0, 0, 0, 0);
+      }
+    };
+    auto load_sc = [&](int s, float (&sc)[2]) {
+      const int kblk = min((s * KSTAGE + cw * CK) >> 7, sk - 1);
+      sc[0] = FP8 ? 256.f * __ldg(wscale + (size_t)scale_row_blk0 * sk + kblk) : 1.f;
+      sc[1] = FP8 ? 256.f * __ldg(wscale + (size_t)scale_row_blk1 * sk + kblk) : 1.f;
+    };
+    uint4 xr[NT][LK / 8], xn[NT][LK / 8];
+    float sc[2] = {1.f, 1.f}, scn[2] = {1.f, 1.f};
+    if (nst > 0) {
+      load_x(s_begin, xr);
+      load_sc(s_begin, sc);
+    }
+    for (int i = 0; i < nst; ++i) {
+      const uint32_t it = phase_base + i;
+      const int slot = it % GV_STAGES;
+      if (i + 1 < nst) {
+        load_x(s_begin + i + 1, xn);
+        load_sc(s_begin + i + 1, scn);
+      }
+      if (!mbar_wait(&full[slot], (it / GV_STAGES) & 1, st, 61)) { ok = false; break; }
+      const uint8_t* box = stages + slot * GV_STAGE_BYTES + (cw >> 1) * 4096;
+      uint4 w[2][2];
+#pragma unroll
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int r = t * 16 + g4 + h * 8;
+          w[t][h] = *reinterpret_cast<const uint4*>(box + r * 128 + ((c16 ^ (r & 7)) << 4));
+        }
+      // these generic-proxy reads must be ordered before the TMA (async proxy) that
+      // refills the slot once it is released
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
+      uint32_t b[NT][LK / 2];
 #pragma unroll
       for (int n = 0; n < NT; ++n)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) acc[t][n][i] = fmaf(d[t][n][i], sc, acc[t][n][i]);
-    }
+        for (int q = 0; q < LK / 8; ++q)
 #pragma unroll
-    for (int t = 0; t < 2; ++t)
+          for (int j = 0; j < 4; ++j) b[n][4 * q + j] = FP8 ? bf16x2_f16x2_s8(u4w(xr[n][q], j)) : u4w(xr[n][q], j);
+      float d[2][NT][4];
 #pragma unroll
-      for (int h = 0; h < 2; ++h) w[t][h] = wn[t][h];
-    if (PX) {
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int n = 0; n < NT; ++n)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) d[t][n][j] = 0.f;
+#pragma unroll
+      for (int g = 0; g < LK / 4; ++g) {
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          uint32_t a0, a1, a2, a3;
+          if (FP8) {
+            const uint32_t wa = u4w(w[t][0], g), wb = u4w(w[t][1], g);
+            a0 = e4m3x2_f16x2(wa);
+            a1 = e4m3x2_f16x2(wb);
+            a2 = e4m3x2_f16x2(wa >> 16);
+            a3 = e4m3x2_f16x2(wb >> 16);
+          } else {
+            a0 = u4w(w[t][0], 2 * g);
+            a1 = u4w(w[t][1], 2 * g);
+            a2 = u4w(w[t][0], 2 * g + 1);
+            a3 = u4w(w[t][1], 2 * g + 1);
+          }
+#pragma unroll
+          for (int n = 0; n < NT; ++n) {
+            if (FP8) mma_f16_16816(d[t][n], a0, a1, a2, a3, b[n][2 * g], b[n][2 * g + 1]);
+            else mma_bf16_16816(d[t][n], a0, a1, a2, a3, b[n][2 * g], b[n][2 * g + 1]);
+          }
+        }
+      }
+#pragma unroll
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int n = 0; n < NT; ++n)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) acc[t][n][j] = fmaf(d[t][n][j], sc[t], acc[t][n][j]);
+#pragma unroll
+      for (int t = 0; t < 2; ++t) sc[t] = scn[t];
 #pragma unroll
       for (int n = 0; n < NT; ++n)
 #pragma unroll
         for (int q = 0; q < LK / 8; ++q) xr[n][q] = xn[n][q];
     }
   }
+  phase_base += nst;
+  return __syncthreads_and(ok);
 }
 
-// The 8 warps of a CTA split the k chunks of one slice; this sums their D fragments
-// through shared memory.  On return warp 0 holds the totals (other warps: undefined).
+// sum the consumer warps' fragments; on return consumer warp 0 (warp 1) holds the totals
 template <int NT>
-__device__ __forceinline__ void cta_reduce(float (&acc)[2][NT][4], float* red) {
+__device__ __forceinline__ void gv_reduce(float (&acc)[2][NT][4], float* red) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   constexpr int V = 2 * NT * 4;
-  float* mine = red + ((size_t)warp * 32 + lane) * V;
+  if (warp >= 1) {
+    float* mine = red + ((size_t)(warp - 1) * 32 + lane) * V;
 #pragma unroll
-  for (int t = 0; t < 2; ++t)
+    for (int t = 0; t < 2; ++t)
 #pragma unroll
-    for (int n = 0; n < NT; ++n)
+      for (int n = 0; n < NT; ++n)
 #pragma unroll
-      for (int i = 0; i < 4; ++i) mine[(t * NT + n) * 4 + i] = acc[t][n][i];
+        for (int i = 0; i < 4; ++i) mine[(t * NT + n) * 4 + i] = acc[t][n][i];
+  }
   __syncthreads();
-  if (warp == 0) {
-    for (int w = 1; w < GEMV_WARPS; ++w) {
+  if (warp == 1) {
+    for (int w = 1; w < GV_CWARPS; ++w) {
       const float* o = red + ((size_t)w * 32 + lane) * V;
 #pragma unroll
       for (int t = 0; t < 2; ++t)
@@ -225,146 +272,216 @@ __device__ __forceinline__ void cta_reduce(float (&acc)[2][NT][4], float* red) {
   __syncthreads();
 }
 
-__device__ __forceinline__ void chunk_split(int nchunks, int& c0, int& c1) {
-  const int warp = threadIdx.x >> 5;
-  const int per = (nchunks + GEMV_WARPS - 1) / GEMV_WARPS;
-  c0 = min(nchunks, warp * per);
-  c1 = min(nchunks, c0 + per);
+template <int NT>
+__device__ __forceinline__ uint8_t* gv_setup(uint64_t*& full, uint64_t*& empty, float*& red) {
+  extern __shared__ uint8_t gv_smem_raw[];
+  const uint32_t a = smem_u32(gv_smem_raw);
+  uint8_t* base = gv_smem_raw + (((a + 1023u) & ~1023u) - a);
+  red = reinterpret_cast<float*>(base + GV_STAGES * GV_STAGE_BYTES);
+  full = reinterpret_cast<uint64_t*>(red + GvSmem<NT>::RED_FLOATS);
+  empty = full + GV_STAGES;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < GV_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], GV_CWARPS);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+  return base;
 }
 
 // ---------------------------------------------------------------------------
-// dense: y[M, N] = x[M, K] W^T (+ bias); a CTA = one 32-row slice (two 16-row tiles),
-// its warps split K
+// dense: y[M, N] = x[M, K] W^T (+ bias); grid (32-row tiles, K splits)
 // ---------------------------------------------------------------------------
 template <bool FP8, int NT>
-__global__ void __launch_bounds__(GEMV_WARPS * 32) gemv_dense_kernel(
-    const uint8_t* __restrict__ W, const float* __restrict__ wscale, int N, int K, const __nv_bfloat16* __restrict__ x,
-    int x_stride, int M, const __nv_bfloat16* __restrict__ bias, void* __restrict__ y, int y_stride, int y_f32) {
-  __shared__ float red[GEMV_WARPS * 32 * 2 * NT * 4];
+__global__ void __launch_bounds__(GV_THREADS) gemv_dense_kernel(
+    const __grid_constant__ CUtensorMap tmap, const float* __restrict__ wscale, int N, int K,
+    const __nv_bfloat16* __restrict__ x, int x_stride, int M, const __nv_bfloat16* __restrict__ bias,
+    void* __restrict__ y, int y_stride, int y_f32, float* __restrict__ ws, int* __restrict__ counters,
+    XtuStatus* st) {
+  uint64_t *full, *empty;
+  float* red;
+  uint8_t* stages = gv_setup<NT>(full, empty, red);
+  if (threadIdx.x == 0) prefetch_tmap(&tmap);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g4 = lane >> 2, tq = lane & 3;
   const int sk = (K + 127) >> 7;
-  constexpr int CK = FP8 ? 64 : 32;
-  int c0, c1;
-  chunk_split((K + CK - 1) / CK, c0, c1);
-  {
-    const int sl = blockIdx.x;
-    const int rb[2] = {sl * 32, sl * 32 + 16};
-    float acc[2][NT][4];
-    warp_mma_gemv<FP8, NT, true>(W, wscale, sk, N, K, rb, x, 0, x_stride, M, c0, c1, acc);
-    cta_reduce<NT>(acc, red);
-    if (warp != 0) return;
+  const int kstage = GV_ROW_BYTES / (FP8 ? 1 : 2);
+  const int nstages = (K + kstage - 1) / kstage;
+  const int splits = gridDim.y, split = blockIdx.y;
+  const int per = (nstages + splits - 1) / splits;
+  const int s0 = min(nstages, split * per), s1 = min(nstages, s0 + per);
+  const int r0 = blockIdx.x * 32;
+  const int rows[2] = {r0, r0 + 16};
+  uint32_t pb = 0;
+  float acc[2][NT][4];
+  if (!gv_stream_tile<FP8, NT>(&tmap, stages, full, empty, pb, rows, s0, s1, K, wscale, sk, min(r0, N - 1) >> 7,
+                               min(r0 + 16, N - 1) >> 7, x, 0, x_stride, M, acc, st))
+    return;
+  gv_reduce<NT>(acc, red);
+  if (warp != 1) return;
+  if (splits > 1) {
 #pragma unroll
     for (int t = 0; t < 2; ++t)
 #pragma unroll
       for (int n = 0; n < NT; ++n)
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const int row = rb[t] + g4 + (i >> 1) * 8;
+          const int row = rows[t] + g4 + (i >> 1) * 8;
           const int tok = n * 8 + 2 * tq + (i & 1);
-          if (row < N && tok < M) {
-            float v = acc[t][n][i];
-            if (bias) v += __bfloat162float(bias[row]);
-            if (y_f32) reinterpret_cast<float*>(y)[(size_t)tok * y_stride + row] = v;
-            else reinterpret_cast<__nv_bfloat16*>(y)[(size_t)tok * y_stride + row] = __float2bfloat16(v);
-          }
+          if (row < N && tok < M) ws[((size_t)split * 16 + tok) * N + row] = acc[t][n][i];
         }
-  }
-}
-
-// ---------------------------------------------------------------------------
-// grouped gate/up + SwiGLU: grid (ctas_per_expert, E).  W13 [E, 2I, K] in 256-row
-// blocks (128 gate, 128 up); a warp slice = 16 output columns: 16 gate + 16 up rows.
-// ---------------------------------------------------------------------------
-template <bool FP8, int NT>
-__global__ void __launch_bounds__(GEMV_WARPS * 32) moe_gemv_gate_up_kernel(
-    const uint8_t* __restrict__ W, const float* __restrict__ wscale, int I, int K,
-    const __nv_bfloat16* __restrict__ xp, const int* __restrict__ seg, __nv_bfloat16* __restrict__ h, float limit,
-    float alpha, float beta) {
-  const int e = blockIdx.y;
-  const int s0 = seg[e], cnt = seg[e + 1] - s0;
-  if (cnt <= 0) return;
-  const size_t eoff = (size_t)e * 2 * I * K * (FP8 ? 1 : 2);
-  const int sk = (K + 127) >> 7;
-  const float* esc = FP8 ? wscale + (size_t)e * ((2 * I + 127) >> 7) * sk : nullptr;
-  __shared__ float red[GEMV_WARPS * 32 * 2 * NT * 4];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int g4 = lane >> 2, tq = lane & 3;
-  constexpr int CK = FP8 ? 64 : 32;
-  int c0, c1;
-  chunk_split((K + CK - 1) / CK, c0, c1);
-  {
-    const int sl = blockIdx.x;
-    const int j0 = sl * 16;
-    const int grow = (j0 >> 7) * 256 + (j0 & 127);
-    const int rb[2] = {grow, grow + 128};
-    for (int mb = 0; mb < cnt; mb += 8 * NT) {
-      const int mc = min(8 * NT, cnt - mb);
-      float acc[2][NT][4];
-      warp_mma_gemv<FP8, NT>(W + eoff, esc, sk, 2 * I, K, rb, xp, s0 + mb, K, mc, c0, c1, acc);
-      cta_reduce<NT>(acc, red);
-      if (warp != 0) continue;
+    __threadfence();
+    __syncwarp();
+    int last = 0;
+    if (lane == 0) last = atomicAdd(&counters[blockIdx.x], 1) == splits - 1;
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (!last) return;
+    __threadfence();
+#pragma unroll
+    for (int t = 0; t < 2; ++t)
 #pragma unroll
       for (int n = 0; n < NT; ++n)
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const int j = j0 + g4 + (i >> 1) * 8;
+          const int row = rows[t] + g4 + (i >> 1) * 8;
           const int tok = n * 8 + 2 * tq + (i & 1);
-          if (tok < mc) {
-            float g = acc[0][n][i], u = acc[1][n][i];
-            if (limit > 0.f) { g = fminf(g, limit); u = fminf(fmaxf(u, -limit), limit); }
-            const float v = (g / (1.f + __expf(-alpha * g))) * (u + beta);
-            h[(size_t)(s0 + mb + tok) * I + j] = __float2bfloat16(v);
-          }
+          float v = 0.f;
+          if (row < N && tok < M)
+            for (int q = 0; q < splits; ++q) v += __ldcg(ws + ((size_t)q * 16 + tok) * N + row);
+          acc[t][n][i] = v;
         }
-    }
+    if (lane == 0) counters[blockIdx.x] = 0;
+  }
+#pragma unroll
+  for (int t = 0; t < 2; ++t)
+#pragma unroll
+    for (int n = 0; n < NT; ++n)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int row = rows[t] + g4 + (i >> 1) * 8;
+        const int tok = n * 8 + 2 * tq + (i & 1);
+        if (row < N && tok < M) {
+          float v = acc[t][n][i];
+          if (bias) v += __bfloat162float(bias[row]);
+          if (y_f32) reinterpret_cast<float*>(y)[(size_t)tok * y_stride + row] = v;
+          else reinterpret_cast<__nv_bfloat16*>(y)[(size_t)tok * y_stride + row] = __float2bfloat16(v);
+        }
+      }
+}
+
+// ---------------------------------------------------------------------------
+// grouped gate/up + SwiGLU: grid (I / 16, experts with rows).  W13 [E, 2I, K] in 256-row
+// blocks (128 gate, 128 up); a tile = 16 gate rows + the matching 16 up rows.
+// ---------------------------------------------------------------------------
+template <bool FP8, int NT>
+__global__ void __launch_bounds__(GV_THREADS) moe_gemv_gate_up_kernel(
+    const __grid_constant__ CUtensorMap tmap, const float* __restrict__ wscale, int I, int K,
+    const __nv_bfloat16* __restrict__ xp, const int* __restrict__ seg, const int* __restrict__ active,
+    __nv_bfloat16* __restrict__ h, float limit, float alpha, float beta, XtuStatus* st) {
+  if ((int)blockIdx.y >= active[0]) return;
+  const int e = active[1 + blockIdx.y];
+  const int s0 = seg[e], cnt = seg[e + 1] - s0;
+  if (cnt <= 0) return;
+  uint64_t *full, *empty;
+  float* red;
+  uint8_t* stages = gv_setup<NT>(full, empty, red);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g4 = lane >> 2, tq = lane & 3;
+  const int sk = (K + 127) >> 7;
+  const int kstage = GV_ROW_BYTES / (FP8 ? 1 : 2);
+  const int nstages = (K + kstage - 1) / kstage;
+  const int j0 = blockIdx.x * 16;
+  const int grow = (j0 >> 7) * 256 + (j0 & 127);            // gate row within the expert
+  const int rows[2] = {e * 2 * I + grow, e * 2 * I + grow + 128};
+  const float* esc = FP8 ? wscale + (size_t)e * ((2 * I + 127) >> 7) * sk : nullptr;
+  uint32_t pb = 0;
+  for (int mb = 0; mb < cnt; mb += 8 * NT) {
+    const int mc = min(8 * NT, cnt - mb);
+    float acc[2][NT][4];
+    if (!gv_stream_tile<FP8, NT>(&tmap, stages, full, empty, pb, rows, 0, nstages, K, esc, sk, grow >> 7,
+                                 (grow + 128) >> 7, xp, s0 + mb, K, mc, acc, st))
+      return;
+    gv_reduce<NT>(acc, red);
+    if (warp != 1) continue;
+#pragma unroll
+    for (int n = 0; n < NT; ++n)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int j = j0 + g4 + (i >> 1) * 8;
+        const int tok = n * 8 + 2 * tq + (i & 1);
+        if (tok < mc) {
+          float g = acc[0][n][i], u = acc[1][n][i];
+          if (limit > 0.f) { g = fminf(g, limit); u = fminf(fmaxf(u, -limit), limit); }
+          const float v = (g / (1.f + __expf(-alpha * g))) * (u + beta);
+          h[(size_t)(s0 + mb + tok) * I + j] = __float2bfloat16(v);
+        }
+      }
   }
 }
 
 // ---------------------------------------------------------------------------
-// grouped down: out[slot[row]] = w[row] * (h[row] W2[e]^T); grid (ctas_per_expert, E)
+// grouped down: out[slot[row]] = w[row] * (h[row] W2[e]^T); grid (H / 32, experts with rows)
 // ---------------------------------------------------------------------------
 template <bool FP8, int NT>
-__global__ void __launch_bounds__(GEMV_WARPS * 32) moe_gemv_down_kernel(
-    const uint8_t* __restrict__ W, const float* __restrict__ wscale, int H, int I, const __nv_bfloat16* __restrict__ hp,
-    const int* __restrict__ seg, const int* __restrict__ perm_slot, const float* __restrict__ perm_w,
-    __nv_bfloat16* __restrict__ out) {
-  const int e = blockIdx.y;
+__global__ void __launch_bounds__(GV_THREADS) moe_gemv_down_kernel(
+    const __grid_constant__ CUtensorMap tmap, const float* __restrict__ wscale, int H, int I,
+    const __nv_bfloat16* __restrict__ hp, const int* __restrict__ seg, const int* __restrict__ active,
+    const int* __restrict__ perm_slot, const float* __restrict__ perm_w, __nv_bfloat16* __restrict__ out,
+    XtuStatus* st) {
+  if ((int)blockIdx.y >= active[0]) return;
+  const int e = active[1 + blockIdx.y];
   const int s0 = seg[e], cnt = seg[e + 1] - s0;
   if (cnt <= 0) return;
-  const size_t eoff = (size_t)e * H * I * (FP8 ? 1 : 2);
-  const int sk = (I + 127) >> 7;
-  const float* esc = FP8 ? wscale + (size_t)e * ((H + 127) >> 7) * sk : nullptr;
-  __shared__ float red[GEMV_WARPS * 32 * 2 * NT * 4];
+  uint64_t *full, *empty;
+  float* red;
+  uint8_t* stages = gv_setup<NT>(full, empty, red);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g4 = lane >> 2, tq = lane & 3;
-  constexpr int CK = FP8 ? 64 : 32;
-  int c0, c1;
-  chunk_split((I + CK - 1) / CK, c0, c1);
-  {
-    const int sl = blockIdx.x;
-    const int rb[2] = {sl * 32, sl * 32 + 16};
-    for (int mb = 0; mb < cnt; mb += 8 * NT) {
-      const int mc = min(8 * NT, cnt - mb);
-      float acc[2][NT][4];
-      warp_mma_gemv<FP8, NT>(W + eoff, esc, sk, H, I, rb, hp, s0 + mb, I, mc, c0, c1, acc);
-      cta_reduce<NT>(acc, red);
-      if (warp != 0) continue;
+  const int sk = (I + 127) >> 7;
+  const int kstage = GV_ROW_BYTES / (FP8 ? 1 : 2);
+  const int nstages = (I + kstage - 1) / kstage;
+  const int r0 = blockIdx.x * 32;
+  const int rows[2] = {e * H + r0, e * H + r0 + 16};
+  const float* esc = FP8 ? wscale + (size_t)e * ((H + 127) >> 7) * sk : nullptr;
+  uint32_t pb = 0;
+  for (int mb = 0; mb < cnt; mb += 8 * NT) {
+    const int mc = min(8 * NT, cnt - mb);
+    float acc[2][NT][4];
+    if (!gv_stream_tile<FP8, NT>(&tmap, stages, full, empty, pb, rows, 0, nstages, I, esc, sk,
+                                 min(r0, H - 1) >> 7, min(r0 + 16, H - 1) >> 7, hp, s0 + mb, I, mc, acc, st))
+      return;
+    gv_reduce<NT>(acc, red);
+    if (warp != 1) continue;
 #pragma unroll
-      for (int t = 0; t < 2; ++t)
+    for (int t = 0; t < 2; ++t)
 #pragma unroll
-        for (int n = 0; n < NT; ++n)
+      for (int n = 0; n < NT; ++n)
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int row = rb[t] + g4 + (i >> 1) * 8;
-            const int tok = n * 8 + 2 * tq + (i & 1);
-            if (row < H && tok < mc) {
-              const int pr = s0 + mb + tok;
-              out[(size_t)perm_slot[pr] * H + row] = __float2bfloat16(acc[t][n][i] * perm_w[pr]);
-            }
+        for (int i = 0; i < 4; ++i) {
+          const int row = r0 + t * 16 + g4 + (i >> 1) * 8;
+          const int tok = n * 8 + 2 * tq + (i & 1);
+          if (row < H && tok < mc) {
+            const int pr = s0 + mb + tok;
+            out[(size_t)perm_slot[pr] * H + row] = __float2bfloat16(acc[t][n][i] * perm_w[pr]);
           }
-    }
+        }
   }
+}
+
+// active[0] = number of experts with rows, active[1..] = those experts in order (one warp)
+__global__ void moe_active_kernel(const int* __restrict__ seg, int E, int* __restrict__ active) {
+  const int lane = threadIdx.x;
+  int n = 0;
+  for (int e0 = 0; e0 < E; e0 += 32) {
+    const int e = e0 + lane;
+    const bool has = e < E && seg[e + 1] > seg[e];
+    const unsigned m = __ballot_sync(0xffffffffu, has);
+    if (has) active[1 + n + __popc(m & ((1u << lane) - 1u))] = e;
+    n += __popc(m);
+  }
+  if (lane == 0) active[0] = n;
 }
 
 }  // namespace xtu
@@ -382,19 +499,76 @@ static int gemv_num_sms() {
   return n;
 }
 
+typedef CUresult (*PFN_gv_encode)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// weights [rows, K] (fp8 or bf16) -> 2-D map with 128-byte x 16-row swizzled boxes
+static int gv_tmap(CUtensorMap* map, const void* W, uint64_t rows, int K, bool fp8) {
+  static PFN_gv_encode enc = nullptr;
+  if (!enc) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      enc = reinterpret_cast<PFN_gv_encode>(p);
+    if (!enc) return -100;
+  }
+  const int eb = fp8 ? 1 : 2;
+  if ((reinterpret_cast<uintptr_t>(W) & 15) != 0 || ((uint64_t)K * eb) % 16 != 0) return -101;
+  cuuint64_t dims[2] = {(cuuint64_t)K, rows};
+  cuuint64_t strides[1] = {(cuuint64_t)K * eb};
+  cuuint32_t box[2] = {(cuuint32_t)(128 / eb), 16};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, fp8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                   const_cast<void*>(W), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -1000 - (int)r;
+}
+
+template <typename Kern>
+static int gv_smem_attr(Kern k, int bytes) {
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  return e == cudaSuccess ? 0 : -(int)e;
+}
+
 extern "C" {
 
 // y[M, N] = x[M, K] W^T (+ bias). fp8: W e4m3 [N, K] + scales [ceil(N/128), ceil(K/128)]; else W bf16.
+// ws (fp32, >= 4 * 16 * N) and counters (zeroed, >= ceil(N/32) ints, left zeroed) enable
+// the split-K form used when there are too few 32-row tiles to fill the GPU (nullable).
 int xtu_gemv(const void* W, const float* wscale, int fp8, int N, int K, const void* x, int x_stride, int M,
-             const void* bias, void* y, int y_stride, int y_f32, cudaStream_t s) {
+             const void* bias, void* y, int y_stride, int y_f32, float* ws, int* counters, void* status,
+             cudaStream_t s) {
   if (M <= 0 || N <= 0) return 0;
   if (M > 16 || K % 16 != 0) return -2;
-  const int grid = (N + 31) / 32;     // one 32-row slice per CTA
-  const int nt = M > 8 ? 2 : 1;
+  CUtensorMap tm;
+  int rc = gv_tmap(&tm, W, (uint64_t)N, K, fp8 != 0);
+  if (rc) return rc;
+  const int tiles = (N + 31) / 32;
+  const int kstage = GV_ROW_BYTES / (fp8 ? 1 : 2);
+  const int nstages = (K + kstage - 1) / kstage;
+  int splits = 1;
+  if (ws != nullptr && counters != nullptr && tiles < 3 * gemv_num_sms()) {
+    splits = (3 * gemv_num_sms() + tiles - 1) / tiles;
+    if (splits > 4) splits = 4;
+    while (splits > 1 && nstages / splits < 4) --splits;     // keep a few stages per CTA
+  }
+  const dim3 grid(tiles, splits);
+  XtuStatus* st = reinterpret_cast<XtuStatus*>(status);
 #define XTU_GEMV_LAUNCH(F, NTV)                                                                              \
-  gemv_dense_kernel<F, NTV><<<grid, GEMV_WARPS * 32, 0, s>>>((const uint8_t*)W, wscale, N, K,               \
-                                                             (const __nv_bfloat16*)x, x_stride, M,         \
-                                                             (const __nv_bfloat16*)bias, y, y_stride, y_f32)
+  do {                                                                                                       \
+    static bool init = false;                                                                                \
+    if (!init) {                                                                                             \
+      rc = gv_smem_attr(gemv_dense_kernel<F, NTV>, GvSmem<NTV>::BYTES);                                      \
+      if (rc) return rc;                                                                                     \
+      init = true;                                                                                           \
+    }                                                                                                        \
+    gemv_dense_kernel<F, NTV><<<grid, GV_THREADS, GvSmem<NTV>::BYTES, s>>>(                                 \
+        tm, wscale, N, K, (const __nv_bfloat16*)x, x_stride, M, (const __nv_bfloat16*)bias, y, y_stride, y_f32, \
+        ws, counters, st);                                                                                   \
+  } while (0)
+  const int nt = M > 8 ? 2 : 1;
   if (fp8) {
     if (nt == 1) XTU_GEMV_LAUNCH(true, 1); else XTU_GEMV_LAUNCH(true, 2);
   } else {
@@ -405,30 +579,47 @@ int xtu_gemv(const void* W, const float* wscale, int fp8, int N, int K, const vo
   return e == cudaSuccess ? 1 : -(int)e;
 }
 
-// grouped decode MoE: gate/up+SwiGLU then down+weight+scatter.  mmax bounds the rows
-// of any one expert (<= tokens); at most mmax * top_k (<= 16 * mmax) experts have rows.
+// grouped decode MoE: gate/up+SwiGLU then down+weight+scatter.  mmax bounds the rows of
+// any one expert; max_active bounds the experts with rows (min(E, tokens * top_k));
+// active: scratch of E + 1 ints.
 int xtu_moe_gemv(const void* W13, const float* s13, const void* W2, const float* s2, int fp8, int E, int H, int I,
                  const void* xp, const int* seg, const int* perm_slot, const float* perm_w, void* h, void* slots,
-                 int mmax, float limit, float alpha, float beta, cudaStream_t s) {
+                 int mmax, int max_active, int* active, float limit, float alpha, float beta, void* status,
+                 cudaStream_t s) {
   if (mmax <= 0) return 0;
-  if (H % 32 != 0 || I % 128 != 0) return -2;
-  const dim3 g1(I / 16, E), g2((H + 31) / 32, E);   // one slice per CTA; experts without rows exit
-  const int nt = mmax > 8 ? 2 : 1;
+  if (H % 32 != 0 || I % 128 != 0 || active == nullptr) return -2;
+  if (max_active <= 0 || max_active > E) max_active = E;
+  CUtensorMap t13, t2;
+  int rc = gv_tmap(&t13, W13, (uint64_t)E * 2 * I, H, fp8 != 0);
+  if (rc) return rc;
+  rc = gv_tmap(&t2, W2, (uint64_t)E * H, I, fp8 != 0);
+  if (rc) return rc;
+  moe_active_kernel<<<1, 32, 0, s>>>(seg, E, active);
+  const dim3 g1(I / 16, max_active), g2((H + 31) / 32, max_active);
+  XtuStatus* st = reinterpret_cast<XtuStatus*>(status);
 #define XTU_MOE_GEMV_LAUNCH(F, NTV)                                                                          \
-  moe_gemv_gate_up_kernel<F, NTV><<<g1, GEMV_WARPS * 32, 0, s>>>((const uint8_t*)W13, s13, I, H,            \
-                                                                 (const __nv_bfloat16*)xp, seg,             \
-                                                                 (__nv_bfloat16*)h, limit, alpha, beta);    \
-  moe_gemv_down_kernel<F, NTV><<<g2, GEMV_WARPS * 32, 0, s>>>((const uint8_t*)W2, s2, H, I,                 \
-                                                              (const __nv_bfloat16*)h, seg, perm_slot,      \
-                                                              perm_w, (__nv_bfloat16*)slots)
+  do {                                                                                                       \
+    static bool init = false;                                                                                \
+    if (!init) {                                                                                             \
+      rc = gv_smem_attr(moe_gemv_gate_up_kernel<F, NTV>, GvSmem<NTV>::BYTES);                                \
+      if (!rc) rc = gv_smem_attr(moe_gemv_down_kernel<F, NTV>, GvSmem<NTV>::BYTES);                          \
+      if (rc) return rc;                                                                                     \
+      init = true;                                                                                           \
+    }                                                                                                        \
+    moe_gemv_gate_up_kernel<F, NTV><<<g1, GV_THREADS, GvSmem<NTV>::BYTES, s>>>(                             \
+        t13, s13, I, H, (const __nv_bfloat16*)xp, seg, active, (__nv_bfloat16*)h, limit, alpha, beta, st);   \
+    moe_gemv_down_kernel<F, NTV><<<g2, GV_THREADS, GvSmem<NTV>::BYTES, s>>>(                                \
+        t2, s2, H, I, (const __nv_bfloat16*)h, seg, active, perm_slot, perm_w, (__nv_bfloat16*)slots, st);   \
+  } while (0)
+  const int nt = mmax > 8 ? 2 : 1;
   if (fp8) {
-    if (nt == 1) { XTU_MOE_GEMV_LAUNCH(true, 1); } else { XTU_MOE_GEMV_LAUNCH(true, 2); }
+    if (nt == 1) XTU_MOE_GEMV_LAUNCH(true, 1); else XTU_MOE_GEMV_LAUNCH(true, 2);
   } else {
-    if (nt == 1) { XTU_MOE_GEMV_LAUNCH(false, 1); } else { XTU_MOE_GEMV_LAUNCH(false, 2); }
+    if (nt == 1) XTU_MOE_GEMV_LAUNCH(false, 1); else XTU_MOE_GEMV_LAUNCH(false, 2);
   }
 #undef XTU_MOE_GEMV_LAUNCH
   cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? 2 : -(int)e;
+  return e == cudaSuccess ? 3 : -(int)e;
 }
 
 }  // extern "C"

@@ -241,6 +241,7 @@ OPS = {
     "moe_prefill_bf16": lambda a: bench_moe(a.tokens, "bf16"),
     "moe_decode_fp8": lambda a: bench_moe(4, "fp8"),
     "gemv_fp8": lambda a: bench_gemv(14336, 4096, 4, "fp8"),
+    "gemv_fp8_oproj": lambda a: bench_gemv(4096, 12288, 4, "fp8"),
     "gemm_fp8": lambda a: bench_gemm(a.tokens, 14336, 4096, "fp8"),
     "gemm_bf16": lambda a: bench_gemm(a.tokens, 14336, 4096, "bf16"),
     "attention_decode": lambda a: bench_attn_decode(),

@@ -68,9 +68,28 @@ def gemv(x: torch.Tensor, weight: torch.Tensor, scale: torch.Tensor | None = Non
     M, K = x.shape
     Nn = weight.shape[0]
     y = out if out is not None else torch.empty(M, Nn, dtype=out_dtype, device=x.device)
+    ws, cnt = _gemv_split_ws(x.device)
     N.call("xtu_gemv", weight.data_ptr(), N.ptr(scale), int(scale is not None), Nn, K, x.data_ptr(), x.stride(0), M,
-           N.ptr(bias), y.data_ptr(), y.stride(0), int(y.dtype == torch.float32), N.stream_ptr(x.device))
+           N.ptr(bias), y.data_ptr(), y.stride(0), int(y.dtype == torch.float32), ws.data_ptr(), cnt.data_ptr(),
+           N.status_buffer(x.device).data_ptr(), N.stream_ptr(x.device))
     return y
+
+
+_GEMV_WS: dict = {}
+
+
+def _gemv_split_ws(device):
+    """Per-device split-K scratch of the decode GEMV: fp32 partials for up to 4 splits x 16
+    rows x N (N < 2 * SMs * 32, the only case that splits) and zeroed slice counters that
+    the kernel leaves zeroed.  Allocated once, so captured graphs keep valid pointers."""
+    key = device.index if device.index is not None else torch.cuda.current_device()
+    t = _GEMV_WS.get(key)
+    if t is None:
+        n_max = 2 * 160 * 32
+        t = (torch.empty(4 * 16 * n_max, dtype=torch.float32, device=device),
+             torch.zeros(n_max // 32 + 1, dtype=torch.int32, device=device))
+        _GEMV_WS[key] = t
+    return t
 
 
 def linear(x: torch.Tensor, weight: torch.Tensor, scale: torch.Tensor | None = None,

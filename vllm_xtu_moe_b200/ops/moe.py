@@ -101,6 +101,7 @@ class MoEWorkspace:
         self.slots = torch.empty(n, H, dtype=torch.bfloat16, device=d)
         self.mx = G.max_mtiles(n, E)
         self.tiles = torch.empty(self.mx * 4, dtype=torch.int32, device=d)
+        self.active = torch.zeros(E + 1, dtype=torch.int32, device=d)   # decode GEMV: experts with rows
         self.ntiles = torch.zeros(1, dtype=torch.int32, device=d)
 
     def nbytes(self) -> int:
@@ -152,7 +153,8 @@ def moe_experts_partial(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tenso
         N.call("xtu_moe_gemv", experts.w13.data_ptr(), N.ptr(experts.s13 if fp8 else None),
                experts.w2.data_ptr(), N.ptr(experts.s2 if fp8 else None), int(fp8), E, H, I, ws.xp.data_ptr(),
                ws.seg.data_ptr(), ws.perm_slot.data_ptr(), ws.perm_w.data_ptr(), ws.h.data_ptr(),
-               ws.slots.data_ptr(), T, float(act_limit), float(act_alpha), float(act_beta), s)
+               ws.slots.data_ptr(), T, min(E, T * K), ws.active.data_ptr(), float(act_limit), float(act_alpha),
+               float(act_beta), N.status_buffer(x.device).data_ptr(), s)
         return
     # the segment table of this call has E + 1 entries (the workspace may serve more experts)
     tiles = G.build_mtiles(ws.seg[: E + 1], n, ws.tiles, ws.ntiles)
@@ -243,12 +245,14 @@ def dense_swiglu_gemv(x: torch.Tensor, w13: torch.Tensor, s13, w2: torch.Tensor,
         st = dict(seg=torch.tensor([0, T], dtype=torch.int32, device=d),
                   slot=torch.arange(T, dtype=torch.int32, device=d),
                   w=torch.ones(T, dtype=torch.float32, device=d),
-                  h=torch.empty(T, I, dtype=torch.bfloat16, device=d))
+                  h=torch.empty(T, I, dtype=torch.bfloat16, device=d),
+                  active=torch.zeros(2, dtype=torch.int32, device=d))
         cache[key] = st
     y = torch.empty(T, w2.shape[0], dtype=torch.bfloat16, device=x.device)
     N.call("xtu_moe_gemv", w13.data_ptr(), N.ptr(s13), w2.data_ptr(), N.ptr(s2), int(s13 is not None), 1, H, I,
            x.data_ptr(), st["seg"].data_ptr(), st["slot"].data_ptr(), st["w"].data_ptr(), st["h"].data_ptr(),
-           y.data_ptr(), T, float(limit), 1.0, 0.0, N.stream_ptr(x.device))
+           y.data_ptr(), T, 1, st["active"].data_ptr(), float(limit), 1.0, 0.0, N.status_buffer(x.device).data_ptr(),
+           N.stream_ptr(x.device))
     return y
 
 
