@@ -80,14 +80,23 @@ __device__ __forceinline__ uint32_t u4w(const uint4& v, int i) {
 
 constexpr int GV_CWARPS = 4;                 // consumer warps (warp 0 is the producer)
 constexpr int GV_THREADS = 32 * (1 + GV_CWARPS);
-constexpr int GV_STAGES = 6;
 constexpr int GV_ROW_BYTES = 256;            // bytes of one weight row per stage (2 x 128-B boxes)
-constexpr int GV_STAGE_BYTES = 32 * GV_ROW_BYTES;   // 32 rows
+constexpr int GV_W_BYTES = 32 * GV_ROW_BYTES;   // weight part of a stage: 32 rows
+constexpr int GV_MAX_KBLK = 128;             // block scales staged per tile (K <= 16384)
 
-template <int NT>
-struct GvSmem {
+// A stage = the tile's 32 weight rows x 256 bytes, followed by the activations of the same
+// k range (bf16, 8 * NT token rows per 128-byte box), both loaded by TMA.
+template <bool FP8, int NT>
+struct GvCfg {
+  static constexpr int KSTAGE = GV_ROW_BYTES / (FP8 ? 1 : 2);   // k per stage
+  static constexpr int XROWS = 8 * NT;
+  static constexpr int XBOXES = KSTAGE / 64;                     // 64 bf16 per 128-byte box
+  static constexpr int X_BYTES = XBOXES * XROWS * 128;
+  static constexpr int STAGE_BYTES = GV_W_BYTES + X_BYTES;       // multiple of 1024
+  static constexpr int STAGES = STAGE_BYTES <= 12288 ? 5 : 4;
   static constexpr int RED_FLOATS = GV_CWARPS * 32 * 2 * NT * 4;
-  static constexpr int BYTES = 1024 + GV_STAGES * GV_STAGE_BYTES + RED_FLOATS * 4 + 2 * GV_STAGES * 8 + 64;
+  static constexpr int BYTES = 1024 + STAGES * STAGE_BYTES + RED_FLOATS * 4 + 2 * GV_MAX_KBLK * 4 +
+                               2 * STAGES * 8 + 64;
 };
 
 // Stream one 32-row tile (rows row0[0]..+15 and row0[1]..+15 of the tensor map) over
@@ -95,15 +104,18 @@ struct GvSmem {
 // Producer: warp 0.  Consumers: warps 1..4, each with acc[tile][nt][4] for its k slices.
 // Returns false (all threads) if a wait timed out.
 template <bool FP8, int NT>
-__device__ __forceinline__ bool gv_stream_tile(const CUtensorMap* tmap, uint8_t* stages, uint64_t* full,
-                                               uint64_t* empty, uint32_t& phase_base, const int (&row0)[2],
-                                               int s_begin, int s_end, int K, const float* __restrict__ wscale,
-                                               int sk, int scale_row_blk0, int scale_row_blk1,
-                                               const __nv_bfloat16* __restrict__ x, int x_row0, int x_stride,
-                                               int mcount, float (&acc)[2][NT][4], XtuStatus* st) {
+__device__ __forceinline__ bool gv_stream_tile(const CUtensorMap* tmap, const CUtensorMap* xmap, uint8_t* stages,
+                                               uint64_t* full, uint64_t* empty, float* sc_sm, uint32_t& phase_base,
+                                               const int (&row0)[2], int s_begin, int s_end, int K,
+                                               const float* __restrict__ wscale, int sk, int scale_row_blk0,
+                                               int scale_row_blk1, int x_row0, int mcount, float (&acc)[2][NT][4],
+                                               XtuStatus* st) {
+  using C = GvCfg<FP8, NT>;
   constexpr int CK = FP8 ? 64 : 32;          // k per warp per stage
   constexpr int LK = FP8 ? 16 : 8;           // k per lane per stage
-  constexpr int KSTAGE = GV_ROW_BYTES / (FP8 ? 1 : 2);
+  constexpr int KSTAGE = C::KSTAGE;
+  constexpr int GV_STAGES = C::STAGES;
+  constexpr int GV_STAGE_BYTES = C::STAGE_BYTES;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nst = s_end - s_begin;
   bool ok = true;
@@ -129,6 +141,9 @@ __device__ __forceinline__ bool gv_stream_tile(const CUtensorMap* tmap, uint8_t*
 #pragma unroll
           for (int h = 0; h < 2; ++h)
             tma_load_2d(dst + b * 4096 + h * 2048, tmap, &full[slot], kb + b * (KSTAGE / 2), row0[h]);
+#pragma unroll
+        for (int xb = 0; xb < C::XBOXES; ++xb)
+          tma_load_2d(dst + GV_W_BYTES + xb * (C::XROWS * 128), xmap, &full[slot], kb + xb * 64, x_row0);
       }
       if (!ok) {   // give the copies already issued (bounded) time to land before the CTA exits
         for (int j = issued > GV_STAGES ? issued - GV_STAGES : 0; j < issued; ++j) {
@@ -142,38 +157,28 @@ __device__ __forceinline__ bool gv_stream_tile(const CUtensorMap* tmap, uint8_t*
     const int cw = warp - 1;
     const int g4 = lane >> 2, tq = lane & 3;
     const int c16 = (cw & 1) * 4 + tq;     // 16-byte chunk of the 128-byte row within box (cw >> 1)
-    auto load_x = [&](int s, uint4 (&xr)[NT][LK / 8]) {
-      const int k = s * KSTAGE + cw * CK + tq * LK;
-#pragma unroll
-      for (int n = 0; n < NT; ++n) {
-        const int tok = n * 8 + g4;
-        const bool okx = tok < mcount && k < K;
-        const uint4* xp =
-            reinterpret_cast<const uint4*>(x + (size_t)(x_row0 + (okx ? tok : 0)) * x_stride + (okx ? k : 0));
-#pragma unroll
-        for (int q = 0; q < LK / 8; ++q) xr[n][q] = okx ? __ldg(xp + q) : make_uint4(0, 0, 0, 0);
+    // this tile's block scales (x 2^8, the activation pre-scale) for its stage range
+    const int kblk0 = (s_begin * KSTAGE) >> 7;
+    const int nkblk = min(sk, ((s_end * KSTAGE + 127) >> 7)) - kblk0;
+    if (FP8) {
+      for (int j = threadIdx.x - 32; j < nkblk && j < GV_MAX_KBLK; j += 32 * GV_CWARPS) {
+        sc_sm[j] = 256.f * __ldg(wscale + (size_t)scale_row_blk0 * sk + kblk0 + j);
+        sc_sm[GV_MAX_KBLK + j] = 256.f * __ldg(wscale + (size_t)scale_row_blk1 * sk + kblk0 + j);
       }
-    };
-    auto load_sc = [&](int s, float (&sc)[2]) {
-      const int kblk = min((s * KSTAGE + cw * CK) >> 7, sk - 1);
-      sc[0] = FP8 ? 256.f * __ldg(wscale + (size_t)scale_row_blk0 * sk + kblk) : 1.f;
-      sc[1] = FP8 ? 256.f * __ldg(wscale + (size_t)scale_row_blk1 * sk + kblk) : 1.f;
-    };
-    uint4 xr[NT][LK / 8], xn[NT][LK / 8];
-    float sc[2] = {1.f, 1.f}, scn[2] = {1.f, 1.f};
-    if (nst > 0) {
-      load_x(s_begin, xr);
-      load_sc(s_begin, sc);
+      asm volatile("bar.sync 2, %0;" ::"n"(32 * GV_CWARPS) : "memory");
     }
     for (int i = 0; i < nst; ++i) {
       const uint32_t it = phase_base + i;
       const int slot = it % GV_STAGES;
-      if (i + 1 < nst) {
-        load_x(s_begin + i + 1, xn);
-        load_sc(s_begin + i + 1, scn);
+      float sc[2] = {1.f, 1.f};
+      if (FP8) {
+        const int kb = min(((s_begin + i) * KSTAGE + cw * CK) >> 7, sk - 1) - kblk0;
+        sc[0] = sc_sm[kb];
+        sc[1] = sc_sm[GV_MAX_KBLK + kb];
       }
       if (!mbar_wait(&full[slot], (it / GV_STAGES) & 1, st, 61)) { ok = false; break; }
-      const uint8_t* box = stages + slot * GV_STAGE_BYTES + (cw >> 1) * 4096;
+      const uint8_t* sbase = stages + slot * GV_STAGE_BYTES;
+      const uint8_t* box = sbase + (cw >> 1) * 4096;
       uint4 w[2][2];
 #pragma unroll
       for (int t = 0; t < 2; ++t)
@@ -182,6 +187,19 @@ __device__ __forceinline__ bool gv_stream_tile(const CUtensorMap* tmap, uint8_t*
           const int r = t * 16 + g4 + h * 8;
           w[t][h] = *reinterpret_cast<const uint4*>(box + r * 128 + ((c16 ^ (r & 7)) << 4));
         }
+      // activations of token n*8+g4 for this lane's k slice (rows past mcount are zeroed)
+      uint4 xr[NT][LK / 8];
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+        const int tok = n * 8 + g4;
+        const uint8_t* xrow = sbase + GV_W_BYTES + (FP8 ? cw : (cw >> 1)) * (C::XROWS * 128) + tok * 128;
+#pragma unroll
+        for (int q = 0; q < LK / 8; ++q) {
+          const int ch = FP8 ? (2 * tq + q) : c16;
+          const uint4 v = *reinterpret_cast<const uint4*>(xrow + ((ch ^ (tok & 7)) << 4));
+          xr[n][q] = tok < mcount ? v : make_uint4(0, 0, 0, 0);
+        }
+      }
       // these generic-proxy reads must be ordered before the TMA (async proxy) that
       // refills the slot once it is released
       fence_proxy_async_smem();
@@ -231,12 +249,6 @@ __device__ __forceinline__ bool gv_stream_tile(const CUtensorMap* tmap, uint8_t*
         for (int n = 0; n < NT; ++n)
 #pragma unroll
           for (int j = 0; j < 4; ++j) acc[t][n][j] = fmaf(d[t][n][j], sc[t], acc[t][n][j]);
-#pragma unroll
-      for (int t = 0; t < 2; ++t) sc[t] = scn[t];
-#pragma unroll
-      for (int n = 0; n < NT; ++n)
-#pragma unroll
-        for (int q = 0; q < LK / 8; ++q) xr[n][q] = xn[n][q];
     }
   }
   phase_base += nst;
@@ -272,16 +284,18 @@ __device__ __forceinline__ void gv_reduce(float (&acc)[2][NT][4], float* red) {
   __syncthreads();
 }
 
-template <int NT>
-__device__ __forceinline__ uint8_t* gv_setup(uint64_t*& full, uint64_t*& empty, float*& red) {
+template <bool FP8, int NT>
+__device__ __forceinline__ uint8_t* gv_setup(uint64_t*& full, uint64_t*& empty, float*& red, float*& sc_sm) {
+  using C = GvCfg<FP8, NT>;
   extern __shared__ uint8_t gv_smem_raw[];
   const uint32_t a = smem_u32(gv_smem_raw);
   uint8_t* base = gv_smem_raw + (((a + 1023u) & ~1023u) - a);
-  red = reinterpret_cast<float*>(base + GV_STAGES * GV_STAGE_BYTES);
-  full = reinterpret_cast<uint64_t*>(red + GvSmem<NT>::RED_FLOATS);
-  empty = full + GV_STAGES;
+  red = reinterpret_cast<float*>(base + C::STAGES * C::STAGE_BYTES);
+  sc_sm = red + C::RED_FLOATS;
+  full = reinterpret_cast<uint64_t*>(sc_sm + 2 * GV_MAX_KBLK);
+  empty = full + C::STAGES;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < GV_STAGES; ++s) {
+    for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], GV_CWARPS);
     }
@@ -296,14 +310,17 @@ __device__ __forceinline__ uint8_t* gv_setup(uint64_t*& full, uint64_t*& empty, 
 // ---------------------------------------------------------------------------
 template <bool FP8, int NT>
 __global__ void __launch_bounds__(GV_THREADS) gemv_dense_kernel(
-    const __grid_constant__ CUtensorMap tmap, const float* __restrict__ wscale, int N, int K,
-    const __nv_bfloat16* __restrict__ x, int x_stride, int M, const __nv_bfloat16* __restrict__ bias,
+    const __grid_constant__ CUtensorMap tmap, const __grid_constant__ CUtensorMap xmap,
+    const float* __restrict__ wscale, int N, int K, int M, const __nv_bfloat16* __restrict__ bias,
     void* __restrict__ y, int y_stride, int y_f32, float* __restrict__ ws, int* __restrict__ counters,
     XtuStatus* st) {
   uint64_t *full, *empty;
-  float* red;
-  uint8_t* stages = gv_setup<NT>(full, empty, red);
-  if (threadIdx.x == 0) prefetch_tmap(&tmap);
+  float *red, *sc_sm;
+  uint8_t* stages = gv_setup<FP8, NT>(full, empty, red, sc_sm);
+  if (threadIdx.x == 0) {
+    prefetch_tmap(&tmap);
+    prefetch_tmap(&xmap);
+  }
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g4 = lane >> 2, tq = lane & 3;
   const int sk = (K + 127) >> 7;
@@ -316,8 +333,8 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_dense_kernel(
   const int rows[2] = {r0, r0 + 16};
   uint32_t pb = 0;
   float acc[2][NT][4];
-  if (!gv_stream_tile<FP8, NT>(&tmap, stages, full, empty, pb, rows, s0, s1, K, wscale, sk, min(r0, N - 1) >> 7,
-                               min(r0 + 16, N - 1) >> 7, x, 0, x_stride, M, acc, st))
+  if (!gv_stream_tile<FP8, NT>(&tmap, &xmap, stages, full, empty, sc_sm, pb, rows, s0, s1, K, wscale, sk,
+                               min(r0, N - 1) >> 7, min(r0 + 16, N - 1) >> 7, 0, M, acc, st))
     return;
   gv_reduce<NT>(acc, red);
   if (warp != 1) return;
@@ -377,16 +394,16 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_dense_kernel(
 // ---------------------------------------------------------------------------
 template <bool FP8, int NT>
 __global__ void __launch_bounds__(GV_THREADS) moe_gemv_gate_up_kernel(
-    const __grid_constant__ CUtensorMap tmap, const float* __restrict__ wscale, int I, int K,
-    const __nv_bfloat16* __restrict__ xp, const int* __restrict__ seg, const int* __restrict__ active,
+    const __grid_constant__ CUtensorMap tmap, const __grid_constant__ CUtensorMap xmap,
+    const float* __restrict__ wscale, int I, int K, const int* __restrict__ seg, const int* __restrict__ active,
     __nv_bfloat16* __restrict__ h, float limit, float alpha, float beta, XtuStatus* st) {
   if ((int)blockIdx.y >= active[0]) return;
   const int e = active[1 + blockIdx.y];
   const int s0 = seg[e], cnt = seg[e + 1] - s0;
   if (cnt <= 0) return;
   uint64_t *full, *empty;
-  float* red;
-  uint8_t* stages = gv_setup<NT>(full, empty, red);
+  float *red, *sc_sm;
+  uint8_t* stages = gv_setup<FP8, NT>(full, empty, red, sc_sm);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g4 = lane >> 2, tq = lane & 3;
   const int sk = (K + 127) >> 7;
@@ -400,8 +417,8 @@ __global__ void __launch_bounds__(GV_THREADS) moe_gemv_gate_up_kernel(
   for (int mb = 0; mb < cnt; mb += 8 * NT) {
     const int mc = min(8 * NT, cnt - mb);
     float acc[2][NT][4];
-    if (!gv_stream_tile<FP8, NT>(&tmap, stages, full, empty, pb, rows, 0, nstages, K, esc, sk, grow >> 7,
-                                 (grow + 128) >> 7, xp, s0 + mb, K, mc, acc, st))
+    if (!gv_stream_tile<FP8, NT>(&tmap, &xmap, stages, full, empty, sc_sm, pb, rows, 0, nstages, K, esc, sk,
+                                 grow >> 7, (grow + 128) >> 7, s0 + mb, mc, acc, st))
       return;
     gv_reduce<NT>(acc, red);
     if (warp != 1) continue;
@@ -426,8 +443,8 @@ __global__ void __launch_bounds__(GV_THREADS) moe_gemv_gate_up_kernel(
 // ---------------------------------------------------------------------------
 template <bool FP8, int NT>
 __global__ void __launch_bounds__(GV_THREADS) moe_gemv_down_kernel(
-    const __grid_constant__ CUtensorMap tmap, const float* __restrict__ wscale, int H, int I,
-    const __nv_bfloat16* __restrict__ hp, const int* __restrict__ seg, const int* __restrict__ active,
+    const __grid_constant__ CUtensorMap tmap, const __grid_constant__ CUtensorMap xmap,
+    const float* __restrict__ wscale, int H, int I, const int* __restrict__ seg, const int* __restrict__ active,
     const int* __restrict__ perm_slot, const float* __restrict__ perm_w, __nv_bfloat16* __restrict__ out,
     XtuStatus* st) {
   if ((int)blockIdx.y >= active[0]) return;
@@ -435,8 +452,8 @@ __global__ void __launch_bounds__(GV_THREADS) moe_gemv_down_kernel(
   const int s0 = seg[e], cnt = seg[e + 1] - s0;
   if (cnt <= 0) return;
   uint64_t *full, *empty;
-  float* red;
-  uint8_t* stages = gv_setup<NT>(full, empty, red);
+  float *red, *sc_sm;
+  uint8_t* stages = gv_setup<FP8, NT>(full, empty, red, sc_sm);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g4 = lane >> 2, tq = lane & 3;
   const int sk = (I + 127) >> 7;
@@ -449,8 +466,8 @@ __global__ void __launch_bounds__(GV_THREADS) moe_gemv_down_kernel(
   for (int mb = 0; mb < cnt; mb += 8 * NT) {
     const int mc = min(8 * NT, cnt - mb);
     float acc[2][NT][4];
-    if (!gv_stream_tile<FP8, NT>(&tmap, stages, full, empty, pb, rows, 0, nstages, I, esc, sk,
-                                 min(r0, H - 1) >> 7, min(r0 + 16, H - 1) >> 7, hp, s0 + mb, I, mc, acc, st))
+    if (!gv_stream_tile<FP8, NT>(&tmap, &xmap, stages, full, empty, sc_sm, pb, rows, 0, nstages, I, esc, sk,
+                                 min(r0, H - 1) >> 7, min(r0 + 16, H - 1) >> 7, s0 + mb, mc, acc, st))
       return;
     gv_reduce<NT>(acc, red);
     if (warp != 1) continue;
@@ -503,8 +520,9 @@ typedef CUresult (*PFN_gv_encode)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
-// weights [rows, K] (fp8 or bf16) -> 2-D map with 128-byte x 16-row swizzled boxes
-static int gv_tmap(CUtensorMap* map, const void* W, uint64_t rows, int K, bool fp8) {
+// [rows, K] (fp8 or bf16, row pitch `pitch` elements) -> 2-D map, 128-byte x box_rows swizzled boxes
+static int gv_tmap(CUtensorMap* map, const void* W, uint64_t rows, int K, bool fp8, int box_rows = 16,
+                   int pitch = 0) {
   static PFN_gv_encode enc = nullptr;
   if (!enc) {
     void* p = nullptr;
@@ -515,10 +533,11 @@ static int gv_tmap(CUtensorMap* map, const void* W, uint64_t rows, int K, bool f
     if (!enc) return -100;
   }
   const int eb = fp8 ? 1 : 2;
-  if ((reinterpret_cast<uintptr_t>(W) & 15) != 0 || ((uint64_t)K * eb) % 16 != 0) return -101;
+  if (pitch <= 0) pitch = K;
+  if ((reinterpret_cast<uintptr_t>(W) & 15) != 0 || ((uint64_t)pitch * eb) % 16 != 0) return -101;
   cuuint64_t dims[2] = {(cuuint64_t)K, rows};
-  cuuint64_t strides[1] = {(cuuint64_t)K * eb};
-  cuuint32_t box[2] = {(cuuint32_t)(128 / eb), 16};
+  cuuint64_t strides[1] = {(cuuint64_t)pitch * eb};
+  cuuint32_t box[2] = {(cuuint32_t)(128 / eb), (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(map, fp8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
                    const_cast<void*>(W), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -541,9 +560,12 @@ int xtu_gemv(const void* W, const float* wscale, int fp8, int N, int K, const vo
              const void* bias, void* y, int y_stride, int y_f32, float* ws, int* counters, void* status,
              cudaStream_t s) {
   if (M <= 0 || N <= 0) return 0;
-  if (M > 16 || K % 16 != 0) return -2;
-  CUtensorMap tm;
+  if (M > 16 || K % 16 != 0 || K > GV_MAX_KBLK * 128) return -2;
+  const int nt = M > 8 ? 2 : 1;
+  CUtensorMap tm, xm;
   int rc = gv_tmap(&tm, W, (uint64_t)N, K, fp8 != 0);
+  if (rc) return rc;
+  rc = gv_tmap(&xm, x, (uint64_t)M, K, false, 8 * nt, x_stride);
   if (rc) return rc;
   const int tiles = (N + 31) / 32;
   const int kstage = GV_ROW_BYTES / (fp8 ? 1 : 2);
@@ -560,15 +582,13 @@ int xtu_gemv(const void* W, const float* wscale, int fp8, int N, int K, const vo
   do {                                                                                                       \
     static bool init = false;                                                                                \
     if (!init) {                                                                                             \
-      rc = gv_smem_attr(gemv_dense_kernel<F, NTV>, GvSmem<NTV>::BYTES);                                      \
+      rc = gv_smem_attr(gemv_dense_kernel<F, NTV>, GvCfg<F, NTV>::BYTES);                                    \
       if (rc) return rc;                                                                                     \
       init = true;                                                                                           \
     }                                                                                                        \
-    gemv_dense_kernel<F, NTV><<<grid, GV_THREADS, GvSmem<NTV>::BYTES, s>>>(                                 \
-        tm, wscale, N, K, (const __nv_bfloat16*)x, x_stride, M, (const __nv_bfloat16*)bias, y, y_stride, y_f32, \
-        ws, counters, st);                                                                                   \
+    gemv_dense_kernel<F, NTV><<<grid, GV_THREADS, GvCfg<F, NTV>::BYTES, s>>>(                               \
+        tm, xm, wscale, N, K, M, (const __nv_bfloat16*)bias, y, y_stride, y_f32, ws, counters, st);          \
   } while (0)
-  const int nt = M > 8 ? 2 : 1;
   if (fp8) {
     if (nt == 1) XTU_GEMV_LAUNCH(true, 1); else XTU_GEMV_LAUNCH(true, 2);
   } else {
@@ -582,17 +602,23 @@ int xtu_gemv(const void* W, const float* wscale, int fp8, int N, int K, const vo
 // grouped decode MoE: gate/up+SwiGLU then down+weight+scatter.  mmax bounds the rows of
 // any one expert; max_active bounds the experts with rows (min(E, tokens * top_k));
 // active: scratch of E + 1 ints.
+// n_rows: rows of the permuted activations xp [n_rows, H] and of h [n_rows, I].
 int xtu_moe_gemv(const void* W13, const float* s13, const void* W2, const float* s2, int fp8, int E, int H, int I,
                  const void* xp, const int* seg, const int* perm_slot, const float* perm_w, void* h, void* slots,
-                 int mmax, int max_active, int* active, float limit, float alpha, float beta, void* status,
-                 cudaStream_t s) {
-  if (mmax <= 0) return 0;
-  if (H % 32 != 0 || I % 128 != 0 || active == nullptr) return -2;
+                 int mmax, int max_active, int n_rows, int* active, float limit, float alpha, float beta,
+                 void* status, cudaStream_t s) {
+  if (mmax <= 0 || n_rows <= 0) return 0;
+  if (H % 32 != 0 || I % 128 != 0 || active == nullptr || H > GV_MAX_KBLK * 128) return -2;
   if (max_active <= 0 || max_active > E) max_active = E;
-  CUtensorMap t13, t2;
+  const int nt = mmax > 8 ? 2 : 1;
+  CUtensorMap t13, t2, xm, hm;
   int rc = gv_tmap(&t13, W13, (uint64_t)E * 2 * I, H, fp8 != 0);
   if (rc) return rc;
   rc = gv_tmap(&t2, W2, (uint64_t)E * H, I, fp8 != 0);
+  if (rc) return rc;
+  rc = gv_tmap(&xm, xp, (uint64_t)n_rows, H, false, 8 * nt);
+  if (rc) return rc;
+  rc = gv_tmap(&hm, h, (uint64_t)n_rows, I, false, 8 * nt);
   if (rc) return rc;
   moe_active_kernel<<<1, 32, 0, s>>>(seg, E, active);
   const dim3 g1(I / 16, max_active), g2((H + 31) / 32, max_active);
@@ -601,17 +627,16 @@ int xtu_moe_gemv(const void* W13, const float* s13, const void* W2, const float*
   do {                                                                                                       \
     static bool init = false;                                                                                \
     if (!init) {                                                                                             \
-      rc = gv_smem_attr(moe_gemv_gate_up_kernel<F, NTV>, GvSmem<NTV>::BYTES);                                \
-      if (!rc) rc = gv_smem_attr(moe_gemv_down_kernel<F, NTV>, GvSmem<NTV>::BYTES);                          \
+      rc = gv_smem_attr(moe_gemv_gate_up_kernel<F, NTV>, GvCfg<F, NTV>::BYTES);                              \
+      if (!rc) rc = gv_smem_attr(moe_gemv_down_kernel<F, NTV>, GvCfg<F, NTV>::BYTES);                        \
       if (rc) return rc;                                                                                     \
       init = true;                                                                                           \
     }                                                                                                        \
-    moe_gemv_gate_up_kernel<F, NTV><<<g1, GV_THREADS, GvSmem<NTV>::BYTES, s>>>(                             \
-        t13, s13, I, H, (const __nv_bfloat16*)xp, seg, active, (__nv_bfloat16*)h, limit, alpha, beta, st);   \
-    moe_gemv_down_kernel<F, NTV><<<g2, GV_THREADS, GvSmem<NTV>::BYTES, s>>>(                                \
-        t2, s2, H, I, (const __nv_bfloat16*)h, seg, active, perm_slot, perm_w, (__nv_bfloat16*)slots, st);   \
+    moe_gemv_gate_up_kernel<F, NTV><<<g1, GV_THREADS, GvCfg<F, NTV>::BYTES, s>>>(                           \
+        t13, xm, s13, I, H, seg, active, (__nv_bfloat16*)h, limit, alpha, beta, st);                        \
+    moe_gemv_down_kernel<F, NTV><<<g2, GV_THREADS, GvCfg<F, NTV>::BYTES, s>>>(                              \
+        t2, hm, s2, H, I, seg, active, perm_slot, perm_w, (__nv_bfloat16*)slots, st);                        \
   } while (0)
-  const int nt = mmax > 8 ? 2 : 1;
   if (fp8) {
     if (nt == 1) XTU_MOE_GEMV_LAUNCH(true, 1); else XTU_MOE_GEMV_LAUNCH(true, 2);
   } else {

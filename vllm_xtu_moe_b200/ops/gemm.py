@@ -65,6 +65,7 @@ GEMV_MAX_M = 16
 def gemv(x: torch.Tensor, weight: torch.Tensor, scale: torch.Tensor | None = None, bias: torch.Tensor | None = None,
          out_dtype: torch.dtype = torch.bfloat16, out: torch.Tensor | None = None) -> torch.Tensor:
     """Decode-size y[M<=16, N] = x W^T (+ bias) streaming W (bf16 or e4m3 + block scales)."""
+    x = tma_rows(x)
     M, K = x.shape
     Nn = weight.shape[0]
     y = out if out is not None else torch.empty(M, Nn, dtype=out_dtype, device=x.device)
@@ -73,6 +74,14 @@ def gemv(x: torch.Tensor, weight: torch.Tensor, scale: torch.Tensor | None = Non
            N.ptr(bias), y.data_ptr(), y.stride(0), int(y.dtype == torch.float32), ws.data_ptr(), cnt.data_ptr(),
            N.status_buffer(x.device).data_ptr(), N.stream_ptr(x.device))
     return y
+
+
+def tma_rows(x: torch.Tensor) -> torch.Tensor:
+    """x itself when its rows can be read by TMA (unit inner stride, 16-byte aligned base and
+    row pitch), else a packed copy."""
+    if x.stride(-1) == 1 and x.data_ptr() % 16 == 0 and (x.stride(0) * x.element_size()) % 16 == 0:
+        return x
+    return x.clone(memory_format=torch.contiguous_format)
 
 
 _GEMV_WS: dict = {}

@@ -153,7 +153,7 @@ def moe_experts_partial(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tenso
         N.call("xtu_moe_gemv", experts.w13.data_ptr(), N.ptr(experts.s13 if fp8 else None),
                experts.w2.data_ptr(), N.ptr(experts.s2 if fp8 else None), int(fp8), E, H, I, ws.xp.data_ptr(),
                ws.seg.data_ptr(), ws.perm_slot.data_ptr(), ws.perm_w.data_ptr(), ws.h.data_ptr(),
-               ws.slots.data_ptr(), T, min(E, T * K), ws.active.data_ptr(), float(act_limit), float(act_alpha),
+               ws.slots.data_ptr(), T, min(E, T * K), n, ws.active.data_ptr(), float(act_limit), float(act_alpha),
                float(act_beta), N.status_buffer(x.device).data_ptr(), s)
         return
     # the segment table of this call has E + 1 entries (the workspace may serve more experts)
@@ -236,6 +236,7 @@ def route_split(ids: torch.Tensor, slotmap: torch.Tensor, lo: int, gpu_ids: torc
 def dense_swiglu_gemv(x: torch.Tensor, w13: torch.Tensor, s13, w2: torch.Tensor, s2, limit: float,
                       cache: dict) -> torch.Tensor:
     """Decode-size SwiGLU MLP (gate/up interleaved in 128-row blocks) as a one-expert grouped GEMV."""
+    x = G.tma_rows(x)
     T, H = x.shape
     I = w13.shape[0] // 2
     key = ("gemv", x.device, T, I)
@@ -251,7 +252,7 @@ def dense_swiglu_gemv(x: torch.Tensor, w13: torch.Tensor, s13, w2: torch.Tensor,
     y = torch.empty(T, w2.shape[0], dtype=torch.bfloat16, device=x.device)
     N.call("xtu_moe_gemv", w13.data_ptr(), N.ptr(s13), w2.data_ptr(), N.ptr(s2), int(s13 is not None), 1, H, I,
            x.data_ptr(), st["seg"].data_ptr(), st["slot"].data_ptr(), st["w"].data_ptr(), st["h"].data_ptr(),
-           y.data_ptr(), T, 1, st["active"].data_ptr(), float(limit), 1.0, 0.0, N.status_buffer(x.device).data_ptr(),
+           y.data_ptr(), T, 1, T, st["active"].data_ptr(), float(limit), 1.0, 0.0, N.status_buffer(x.device).data_ptr(),
            N.stream_ptr(x.device))
     return y
 
