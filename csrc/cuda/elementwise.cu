@@ -368,7 +368,7 @@ __global__ void moe_scatter_gather_kernel(const int* __restrict__ ids, const flo
                                           int K, int lo, int hi, int* __restrict__ cursor,
                                           int* __restrict__ perm_slot, float* __restrict__ perm_w,
                                           const __nv_bfloat16* __restrict__ x, int H, int x_stride,
-                                          __nv_bfloat16* __restrict__ xp) {
+                                          __nv_bfloat16* __restrict__ xp, int xp_f16s) {
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (gw >= n) return;
@@ -385,7 +385,10 @@ __global__ void moe_scatter_gather_kernel(const int* __restrict__ ids, const flo
     const int t = gw / K;
     const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)t * x_stride);
     uint4* dst = reinterpret_cast<uint4*>(xp + (size_t)p * H);
-    for (int i = lane; i < H / 8; i += 32) dst[i] = src[i];
+    if (xp_f16s)   // the fp8-weight decode GEMV reads f16 x 2^-8 activations
+      for (int i = lane; i < H / 8; i += 32) dst[i] = bf16x8_f16x8_s8(src[i]);
+    else
+      for (int i = lane; i < H / 8; i += 32) dst[i] = src[i];
   }
 }
 
@@ -617,10 +620,11 @@ int xtu_router_topk(const float* logits, const float* bias, int T, int E, int K,
   return rc_last();
 }
 
-// counts must be zero on entry (the scan leaves it zeroed for the next call)
+// counts must be zero on entry (the scan leaves it zeroed for the next call).
+// xp_f16s: write the gathered rows as f16 x 2^-8 instead of bf16.
 int xtu_moe_permute(const int* ids, const float* weights, int T, int K, int lo, int hi, int* counts, int* seg,
                     int* cursor, int* perm_slot, float* perm_w, const void* x, int H, int x_stride, void* xp,
-                    cudaStream_t s) {
+                    int xp_f16s, cudaStream_t s) {
   const int n = T * K;
   const int E = hi - lo;
   if (E <= 0 || E > 65536) return -2;
@@ -633,7 +637,7 @@ int xtu_moe_permute(const int* ids, const float* weights, int T, int K, int lo, 
     if (xp && H % 8 != 0) return -3;
     moe_scatter_gather_kernel<<<(n * 32 + 255) / 256, 256, 0, s>>>(ids, weights, n, K, lo, hi, cursor, perm_slot,
                                                                    perm_w, (const __nv_bfloat16*)x, H, x_stride,
-                                                                   (__nv_bfloat16*)xp);
+                                                                   (__nv_bfloat16*)xp, xp_f16s);
   }
   return rc_last(n > 0 ? 3 : 1);
 }

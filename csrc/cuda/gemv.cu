@@ -15,11 +15,15 @@
 //     (t/4 + 8): lane t owns k = 16*(t%4) + [0, 16) of its warp's 64-k slice (fp8) and
 //     feeds MMA g in 0..3 with k = 16*(t%4) + 4g + {0,1 | 2,3}.  Its B fragment is the
 //     same k slice of token t/4, so A and B agree on the permutation.
-//   * fp8: e4m3 pairs -> f16 pairs with one cvt each (exact), activations -> f16 scaled
-//     by 2^-8 (keeps x * 448 inside fp16 range; the scale and 2^8 are restored in fp32
-//     with the block scale once per 64-k slice).  bf16 weights use the bf16 MMA as is.
-//   * Activations and block scales of the next stage are loaded while the current one
-//     is multiplied; the four warps' partial sums meet in shared memory at the end.
+//   * fp8: e4m3 pairs -> f16 pairs with one cvt each (exact).  The activations arrive
+//     already as f16 scaled by 2^-8 (keeps x * 448 inside the f16 range; the scale and
+//     2^8 are restored in fp32 with the block scale once per 64-k slice): moe_permute
+//     writes the MoE rows in that form, the gate/up epilogue writes h in it, and a
+//     dense call converts its few rows once in a pre-pass, so no CTA converts x per
+//     stage.  bf16 weights use the bf16 MMA on bf16 activations as is.
+//   * Each TMA stage carries the tile's activations of the same k range beside the
+//     weights; block scales are staged in shared memory once per tile; the four warps'
+//     partial sums meet in shared memory at the end.
 // Grouped (MoE) forms take the routing permutation of moe_permute: expert e owns rows
 // seg[e]..seg[e+1] of the permuted activations, and the grid's y index walks the list of
 // experts that have rows (moe_active_kernel), so idle experts cost no CTAs.
@@ -60,18 +64,11 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint3
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// two e4m3 (low 16 bits) -> f16x2 (exact)
-__device__ __forceinline__ uint32_t e4m3x2_f16x2(uint32_t v) {
-  const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(v & 0xFFFFu), __NV_E4M3);
-  return (uint32_t)h.x | ((uint32_t)h.y << 16);
-}
-
-// bf16 pair -> f16 pair scaled by 2^-8
-__device__ __forceinline__ uint32_t bf16x2_f16x2_s8(uint32_t v) {
-  const float lo = __uint_as_float(v << 16) * 0.00390625f;
-  const float hi = __uint_as_float(v & 0xFFFF0000u) * 0.00390625f;
-  const __half2 h = __floats2half2_rn(lo, hi);
-  return *reinterpret_cast<const uint32_t*>(&h);
+// four e4m3 -> two f16x2 (exact): bytes 0,1 -> lo, bytes 2,3 -> hi
+__device__ __forceinline__ void e4m3x4_f16x4(uint32_t v, uint32_t& lo, uint32_t& hi) {
+  asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %2;\n\tcvt.rn.f16x2.e4m3x2 %0, l;\n\tcvt.rn.f16x2.e4m3x2 %1, h;\n\t}"
+      : "=r"(lo), "=r"(hi)
+      : "r"(v));
 }
 
 __device__ __forceinline__ uint32_t u4w(const uint4& v, int i) {
@@ -211,7 +208,7 @@ __device__ __forceinline__ bool gv_stream_tile(const CUtensorMap* tmap, const CU
 #pragma unroll
         for (int q = 0; q < LK / 8; ++q)
 #pragma unroll
-          for (int j = 0; j < 4; ++j) b[n][4 * q + j] = FP8 ? bf16x2_f16x2_s8(u4w(xr[n][q], j)) : u4w(xr[n][q], j);
+          for (int j = 0; j < 4; ++j) b[n][4 * q + j] = u4w(xr[n][q], j);   // f16 x 2^-8 (fp8) or bf16
       float d[2][NT][4];
 #pragma unroll
       for (int t = 0; t < 2; ++t)
@@ -225,11 +222,8 @@ __device__ __forceinline__ bool gv_stream_tile(const CUtensorMap* tmap, const CU
         for (int t = 0; t < 2; ++t) {
           uint32_t a0, a1, a2, a3;
           if (FP8) {
-            const uint32_t wa = u4w(w[t][0], g), wb = u4w(w[t][1], g);
-            a0 = e4m3x2_f16x2(wa);
-            a1 = e4m3x2_f16x2(wb);
-            a2 = e4m3x2_f16x2(wa >> 16);
-            a3 = e4m3x2_f16x2(wb >> 16);
+            e4m3x4_f16x4(u4w(w[t][0], g), a0, a2);
+            e4m3x4_f16x4(u4w(w[t][1], g), a1, a3);
           } else {
             a0 = u4w(w[t][0], 2 * g);
             a1 = u4w(w[t][1], 2 * g);
@@ -432,7 +426,10 @@ __global__ void __launch_bounds__(GV_THREADS) moe_gemv_gate_up_kernel(
           float g = acc[0][n][i], u = acc[1][n][i];
           if (limit > 0.f) { g = fminf(g, limit); u = fminf(fmaxf(u, -limit), limit); }
           const float v = (g / (1.f + __expf(-alpha * g))) * (u + beta);
-          h[(size_t)(s0 + mb + tok) * I + j] = __float2bfloat16(v);
+          if (FP8)   // the down GEMV's activation form: f16 x 2^-8
+            reinterpret_cast<__half*>(h)[(size_t)(s0 + mb + tok) * I + j] = __float2half_rn(v * 0.00390625f);
+          else
+            h[(size_t)(s0 + mb + tok) * I + j] = __float2bfloat16(v);
         }
       }
   }
@@ -501,6 +498,22 @@ __global__ void moe_active_kernel(const int* __restrict__ seg, int E, int* __res
   if (lane == 0) active[0] = n;
 }
 
+
+// Workspace of the dense GEMV: fp32 split-K partials (up to 4 splits x 16 rows x N, used
+// only while the tiles do not fill the GPU) followed by the f16 activation scratch.
+constexpr long long GV_WS_PART_FLOATS = 1 << 20;
+constexpr long long GV_WS_X_HALVES = 1 << 19;
+
+// x [M, K] (row stride `stride`) bf16 -> out [M, K] f16 x 2^-8, one 16-byte chunk per thread
+__global__ void gv_x_f16s_kernel(const __nv_bfloat16* __restrict__ x, int M, int K, int stride,
+                                 uint4* __restrict__ out) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  const int per_row = K >> 3;
+  if (i >= M * per_row) return;
+  const int r = i / per_row, c8 = i - r * per_row;
+  out[i] = bf16x8_f16x8_s8(*reinterpret_cast<const uint4*>(x + (size_t)r * stride + c8 * 8));
+}
+
 }  // namespace xtu
 
 using namespace xtu;
@@ -551,33 +564,55 @@ static int gv_smem_attr(Kern k, int bytes) {
   return e == cudaSuccess ? 0 : -(int)e;
 }
 
+static inline int gv_stages_per_tile(int K, bool fp8) {
+  const int kstage = GV_ROW_BYTES / (fp8 ? 1 : 2);
+  return (K + kstage - 1) / kstage;
+}
+
+// bf16 rows -> f16 x 2^-8 rows in the workspace's activation scratch
+static const void* gv_convert_x(const void* x, int rows, int K, int stride, float* ws, cudaStream_t s) {
+  uint4* x16 = reinterpret_cast<uint4*>(ws + GV_WS_PART_FLOATS);
+  const int chunks = rows * (K / 8);
+  gv_x_f16s_kernel<<<(chunks + 255) / 256, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(x), rows, K, stride,
+                                                        x16);
+  return x16;
+}
+
 extern "C" {
 
 // y[M, N] = x[M, K] W^T (+ bias). fp8: W e4m3 [N, K] + scales [ceil(N/128), ceil(K/128)]; else W bf16.
-// ws (fp32, >= 4 * 16 * N) and counters (zeroed, >= ceil(N/32) ints, left zeroed) enable
-// the split-K form used when there are too few 32-row tiles to fill the GPU (nullable).
+// ws: fp32, GV_WS_PART_FLOATS + GV_WS_X_HALVES / 2 (split-K partials, then the f16 activations
+// of fp8 calls); counters: >= 512 ints, zeroed on first use, left zeroed by every launch.
 int xtu_gemv(const void* W, const float* wscale, int fp8, int N, int K, const void* x, int x_stride, int M,
              const void* bias, void* y, int y_stride, int y_f32, float* ws, int* counters, void* status,
              cudaStream_t s) {
   if (M <= 0 || N <= 0) return 0;
-  if (M > 16 || K % 16 != 0 || K > GV_MAX_KBLK * 128) return -2;
+  if (M > 16 || K % 16 != 0 || ws == nullptr || counters == nullptr) return -2;
+  if (K > GV_MAX_KBLK * 128) return -3;
+  if (fp8 && (long long)M * K > GV_WS_X_HALVES) return -4;
   const int nt = M > 8 ? 2 : 1;
+  const int tiles = (N + 31) / 32;
+  const int S = gv_stages_per_tile(K, fp8 != 0);
+  int launches = 1;
+  if (fp8) {   // activations -> f16 x 2^-8 once, not once per CTA and stage
+    x = gv_convert_x(x, M, K, x_stride, ws, s);
+    x_stride = K;
+    ++launches;
+  }
   CUtensorMap tm, xm;
   int rc = gv_tmap(&tm, W, (uint64_t)N, K, fp8 != 0);
   if (rc) return rc;
   rc = gv_tmap(&xm, x, (uint64_t)M, K, false, 8 * nt, x_stride);
   if (rc) return rc;
-  const int tiles = (N + 31) / 32;
-  const int kstage = GV_ROW_BYTES / (fp8 ? 1 : 2);
-  const int nstages = (K + kstage - 1) / kstage;
+  XtuStatus* st = reinterpret_cast<XtuStatus*>(status);
   int splits = 1;
-  if (ws != nullptr && counters != nullptr && tiles < 3 * gemv_num_sms()) {
+  if (tiles < 3 * gemv_num_sms()) {   // too few tiles to fill the GPU: split K as well
     splits = (3 * gemv_num_sms() + tiles - 1) / tiles;
     if (splits > 4) splits = 4;
-    while (splits > 1 && nstages / splits < 4) --splits;     // keep a few stages per CTA
+    while (splits > 1 && S / splits < 4) --splits;     // keep a few stages per CTA
+    if ((long long)splits * 16 * N > GV_WS_PART_FLOATS) splits = 1;
   }
   const dim3 grid(tiles, splits);
-  XtuStatus* st = reinterpret_cast<XtuStatus*>(status);
 #define XTU_GEMV_LAUNCH(F, NTV)                                                                              \
   do {                                                                                                       \
     static bool init = false;                                                                                \
@@ -596,21 +631,30 @@ int xtu_gemv(const void* W, const float* wscale, int fp8, int N, int K, const vo
   }
 #undef XTU_GEMV_LAUNCH
   cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? 1 : -(int)e;
+  return e == cudaSuccess ? launches : -(int)e;
 }
 
 // grouped decode MoE: gate/up+SwiGLU then down+weight+scatter.  mmax bounds the rows of
-// any one expert; max_active bounds the experts with rows (min(E, tokens * top_k));
-// active: scratch of E + 1 ints.
-// n_rows: rows of the permuted activations xp [n_rows, H] and of h [n_rows, I].
+// any one expert (<= 16); max_active bounds the experts with rows (min(E, tokens * top_k));
+// n_rows: rows of the permuted activations xp [n_rows, H] and of h [n_rows, I];
+// active: scratch of E + 1 ints; ws as for xtu_gemv (its activation scratch only).  fp8:
+// xp_f16s says xp already holds f16 x 2^-8 rows (moe_permute's form); h is written in
+// that form too.
 int xtu_moe_gemv(const void* W13, const float* s13, const void* W2, const float* s2, int fp8, int E, int H, int I,
-                 const void* xp, const int* seg, const int* perm_slot, const float* perm_w, void* h, void* slots,
-                 int mmax, int max_active, int n_rows, int* active, float limit, float alpha, float beta,
-                 void* status, cudaStream_t s) {
+                 const void* xp, int xp_f16s, const int* seg, const int* perm_slot, const float* perm_w, void* h,
+                 void* slots, int mmax, int max_active, int n_rows, int* active, float limit, float alpha,
+                 float beta, float* ws, void* status, cudaStream_t s) {
   if (mmax <= 0 || n_rows <= 0) return 0;
-  if (H % 32 != 0 || I % 128 != 0 || active == nullptr || H > GV_MAX_KBLK * 128) return -2;
+  if (mmax > 16 || H % 32 != 0 || I % 128 != 0 || active == nullptr) return -2;
+  if (H > GV_MAX_KBLK * 128 || I > GV_MAX_KBLK * 128) return -3;
   if (max_active <= 0 || max_active > E) max_active = E;
   const int nt = mmax > 8 ? 2 : 1;
+  int launches = 3;
+  if (fp8 && !xp_f16s) {
+    if (ws == nullptr || (long long)n_rows * H > GV_WS_X_HALVES) return -4;
+    xp = gv_convert_x(xp, n_rows, H, H, ws, s);
+    ++launches;
+  }
   CUtensorMap t13, t2, xm, hm;
   int rc = gv_tmap(&t13, W13, (uint64_t)E * 2 * I, H, fp8 != 0);
   if (rc) return rc;
@@ -621,8 +665,8 @@ int xtu_moe_gemv(const void* W13, const float* s13, const void* W2, const float*
   rc = gv_tmap(&hm, h, (uint64_t)n_rows, I, false, 8 * nt);
   if (rc) return rc;
   moe_active_kernel<<<1, 32, 0, s>>>(seg, E, active);
-  const dim3 g1(I / 16, max_active), g2((H + 31) / 32, max_active);
   XtuStatus* st = reinterpret_cast<XtuStatus*>(status);
+  const dim3 g1(I / 16, max_active), g2((H + 31) / 32, max_active);
 #define XTU_MOE_GEMV_LAUNCH(F, NTV)                                                                          \
   do {                                                                                                       \
     static bool init = false;                                                                                \
@@ -644,7 +688,7 @@ int xtu_moe_gemv(const void* W13, const float* s13, const void* W2, const float*
   }
 #undef XTU_MOE_GEMV_LAUNCH
   cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? 3 : -(int)e;
+  return e == cudaSuccess ? launches : -(int)e;
 }
 
 }  // extern "C"

@@ -300,4 +300,18 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 __device__ __forceinline__ float bf16_lo(uint32_t v) { return __uint_as_float(v << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }
 
+// bf16 pair -> f16 pair scaled by 2^-8: the activation form of the fp8-weight GEMVs (the
+// scale keeps x * 448 inside the f16 range; it is undone in fp32 with the block scale)
+__device__ __forceinline__ uint32_t bf16x2_f16x2_s8(uint32_t v) {
+  const float lo = __uint_as_float(v << 16) * 0.00390625f;
+  const float hi = __uint_as_float(v & 0xFFFF0000u) * 0.00390625f;
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+__device__ __forceinline__ uint4 bf16x8_f16x8_s8(uint4 v) {
+  return make_uint4(bf16x2_f16x2_s8(v.x), bf16x2_f16x2_s8(v.y), bf16x2_f16x2_s8(v.z), bf16x2_f16x2_s8(v.w));
+}
+
 }  // namespace xtu

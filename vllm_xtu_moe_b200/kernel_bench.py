@@ -37,7 +37,9 @@ def peaks() -> dict:
 
 
 def time_fn(fn, iters: int = 10, warmup: int = 3, flush: bool = True) -> float:
-    """Median device milliseconds per call; a 256 MB write between calls evicts L2."""
+    """Median device milliseconds per call; a 256 MB write between calls evicts L2.  A
+    0.1 ms device-side spin before the start event keeps the host's launch cost of `fn`
+    out of the measured interval (the GPU is still busy when `fn` is enqueued)."""
     scratch = torch.empty(256 << 20, dtype=torch.uint8, device="cuda") if flush else None
     for _ in range(warmup):
         fn()
@@ -46,6 +48,7 @@ def time_fn(fn, iters: int = 10, warmup: int = 3, flush: bool = True) -> float:
     for _ in range(iters):
         if scratch is not None:
             scratch.fill_(1)
+        torch.cuda._sleep(200_000)
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         fn()

@@ -88,17 +88,27 @@ _GEMV_WS: dict = {}
 
 
 def _gemv_split_ws(device):
-    """Per-device split-K scratch of the decode GEMV: fp32 partials for up to 4 splits x 16
-    rows x N (N < 2 * SMs * 32, the only case that splits) and zeroed slice counters that
-    the kernel leaves zeroed.  Allocated once, so captured graphs keep valid pointers."""
+    """Per-device scratch of the decode GEMVs: 4 MB of fp32 split-K partials (dense calls
+    whose tiles do not fill the GPU) followed by 1 MB for the f16 activations of fp8-weight
+    calls, and per-tile completion counters that start zeroed and that every launch leaves
+    zeroed.  Allocated once, so captured graphs keep valid pointers; launches on one stream
+    share it."""
     key = device.index if device.index is not None else torch.cuda.current_device()
     t = _GEMV_WS.get(key)
     if t is None:
-        n_max = 2 * 160 * 32
-        t = (torch.empty(4 * 16 * n_max, dtype=torch.float32, device=device),
-             torch.zeros(n_max // 32 + 1, dtype=torch.int32, device=device))
+        t = (torch.empty((1 << 20) + (1 << 18), dtype=torch.float32, device=device),
+             torch.zeros(1024, dtype=torch.int32, device=device))
         _GEMV_WS[key] = t
     return t
+
+
+def gemv_ws_reset(device) -> None:
+    """Re-zero the GEMV tile counters (after a launch that reported an error, whose CTAs
+    may have stopped between bumping a counter and clearing it)."""
+    key = device.index if device.index is not None else torch.cuda.current_device()
+    t = _GEMV_WS.get(key)
+    if t is not None:
+        t[1].zero_()
 
 
 def linear(x: torch.Tensor, weight: torch.Tensor, scale: torch.Tensor | None = None,

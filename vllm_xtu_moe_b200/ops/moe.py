@@ -140,21 +140,24 @@ def moe_experts_partial(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tenso
         raise ValueError(f"workspace for {ws.num_experts} experts x {ws.max_tokens} tokens; call needs {E} x {T}")
     s = N.stream_ptr(x.device)
     n = T * K
+    fp8 = experts.fmt == "fp8"
+    # decode: weight-streaming grouped GEMV (gate/up + SwiGLU, down + weight + scatter); with
+    # fp8 experts it reads the gathered rows as f16 x 2^-8, which the permute writes
+    gemv_path = T <= G.GEMV_MAX_M and experts.interleaved and experts.fmt not in G.FP4_FMTS
+    f16s = int(gemv_path and fp8)
     N.call("xtu_moe_permute", ids.data_ptr(), weights.data_ptr(), T, K, lo, lo + E, ws.counts.data_ptr(),
            ws.seg.data_ptr(), ws.cursor.data_ptr(), ws.perm_slot.data_ptr(), ws.perm_w.data_ptr(), x.data_ptr(), H,
-           x.stride(0), ws.xp.data_ptr(), s)
+           x.stride(0), ws.xp.data_ptr(), f16s, s)
     I = experts.inter
-    fp8 = experts.fmt == "fp8"
     if experts.fmt in G.FP4_FMTS:
         _experts_fp4(experts, ws, n, act_limit, act_alpha, act_beta)
         return
-    if T <= G.GEMV_MAX_M and experts.interleaved:
-        # decode: weight-streaming grouped GEMV (gate/up + SwiGLU, down + weight + scatter)
+    if gemv_path:
         N.call("xtu_moe_gemv", experts.w13.data_ptr(), N.ptr(experts.s13 if fp8 else None),
-               experts.w2.data_ptr(), N.ptr(experts.s2 if fp8 else None), int(fp8), E, H, I, ws.xp.data_ptr(),
+               experts.w2.data_ptr(), N.ptr(experts.s2 if fp8 else None), int(fp8), E, H, I, ws.xp.data_ptr(), f16s,
                ws.seg.data_ptr(), ws.perm_slot.data_ptr(), ws.perm_w.data_ptr(), ws.h.data_ptr(),
                ws.slots.data_ptr(), T, min(E, T * K), n, ws.active.data_ptr(), float(act_limit), float(act_alpha),
-               float(act_beta), N.status_buffer(x.device).data_ptr(), s)
+               float(act_beta), _gv_ws(x.device), N.status_buffer(x.device).data_ptr(), s)
         return
     # the segment table of this call has E + 1 entries (the workspace may serve more experts)
     tiles = G.build_mtiles(ws.seg[: E + 1], n, ws.tiles, ws.ntiles)
@@ -233,6 +236,10 @@ def route_split(ids: torch.Tensor, slotmap: torch.Tensor, lo: int, gpu_ids: torc
            cpu_ids.data_ptr(), N.ptr(hits), N.stream_ptr(ids.device))
 
 
+def _gv_ws(device):
+    return G._gemv_split_ws(device)[0].data_ptr()
+
+
 def dense_swiglu_gemv(x: torch.Tensor, w13: torch.Tensor, s13, w2: torch.Tensor, s2, limit: float,
                       cache: dict) -> torch.Tensor:
     """Decode-size SwiGLU MLP (gate/up interleaved in 128-row blocks) as a one-expert grouped GEMV."""
@@ -251,9 +258,9 @@ def dense_swiglu_gemv(x: torch.Tensor, w13: torch.Tensor, s13, w2: torch.Tensor,
         cache[key] = st
     y = torch.empty(T, w2.shape[0], dtype=torch.bfloat16, device=x.device)
     N.call("xtu_moe_gemv", w13.data_ptr(), N.ptr(s13), w2.data_ptr(), N.ptr(s2), int(s13 is not None), 1, H, I,
-           x.data_ptr(), st["seg"].data_ptr(), st["slot"].data_ptr(), st["w"].data_ptr(), st["h"].data_ptr(),
-           y.data_ptr(), T, 1, T, st["active"].data_ptr(), float(limit), 1.0, 0.0, N.status_buffer(x.device).data_ptr(),
-           N.stream_ptr(x.device))
+           x.data_ptr(), 0, st["seg"].data_ptr(), st["slot"].data_ptr(), st["w"].data_ptr(), st["h"].data_ptr(),
+           y.data_ptr(), T, 1, T, st["active"].data_ptr(), float(limit), 1.0, 0.0, _gv_ws(x.device),
+           N.status_buffer(x.device).data_ptr(), N.stream_ptr(x.device))
     return y
 
 
