@@ -527,6 +527,14 @@ __global__ void attn_combine_kernel(const float* __restrict__ ws_o, const float*
 
 }  // namespace xtu
 
+namespace xtu {
+// warp-level GQA decode kernel (attention_decode.cu); 0 = shape not served there
+int attn_decode_gqa(const CUtensorMap& tk, const CUtensorMap& tv, const void* q, int q_stride, void* o,
+                    int o_stride, const int* q_start, const int* kv_len, const int* block_table, int bt_stride,
+                    int B, int max_q_len, int T, int Hq, int Hkv, int D, float scale, int splits, float* ws_o,
+                    float* ws_lse, void* status, cudaStream_t s);
+}  // namespace xtu
+
 using namespace xtu;
 
 typedef CUresult (*PFN_encodeTiled_t)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -619,7 +627,12 @@ int xtu_paged_attention(const void* q, int q_stride, const void* k_cache, const 
   if (rc) return rc;
   const int pos_per_tile = p.rows_per_tile / G;
   const int grid_x = (max_q_len + pos_per_tile - 1) / pos_per_tile;
-  int r;
+  int r = 0;
+  // decode-shaped GQA steps with few query rows per KV head: the warp-level decode kernel
+  if (grid_x == 1 && !v_is_k && D == DV && (D == 64 || D == 128))
+    r = attn_decode_gqa(tk, tv, q, q_stride, o, o_stride, q_start, kv_len, block_table, bt_stride, B, max_q_len, T,
+                        Hq, Hkv, D, scale, p.splits, p.ws_o, p.ws_lse, status, s);
+  if (r < 0) return r;
   // decode-shaped steps (all of a sequence's query rows fit one 128-row tile): 64-key
   // tiles, a 4-deep K/V ring and a staged block table keep more bytes in flight per SM
   const bool decode_shape = grid_x == 1;
@@ -629,7 +642,8 @@ int xtu_paged_attention(const void* q, int q_stride, const void* k_cache, const 
   // every replica scores a multiple of 16 keys per tile (the softmax reads S in 16-column chunks)
   const int bn = (decode_shape && D == 64) ? 64 : 128;
   while (p.rf > 1 && (bn / p.rf) % 16 != 0) p.rf >>= 1;
-  if (mla) r = launch_attn<576, 256, 16, 2, 1024, 1>(tk, tv, p, grid_x, B, s);
+  if (r == 1) {
+  } else if (mla) r = launch_attn<576, 256, 16, 2, 1024, 1>(tk, tv, p, grid_x, B, s);
   else if (decode_shape && D == 128 && DV == 128) r = launch_attn<128, 128, 128, 2, 256>(tk, tv, p, grid_x, B, s);
   else if (decode_shape && D == 64 && DV == 64) r = launch_attn<64, 64, 64, 6, 1024>(tk, tv, p, grid_x, B, s);
   else if (D == 128 && DV == 128) r = launch_attn<128, 128, 128>(tk, tv, p, grid_x, B, s);

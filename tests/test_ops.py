@@ -193,13 +193,15 @@ def _make_paged(seqs, Hkv, D, Dv, bs=64, device="cuda"):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("Hq,Hkv,D", [(96, 8, 128), (4, 2, 64), (16, 2, 256), (8, 8, 128), (12, 1, 128)])
-@pytest.mark.parametrize("mode", ["prefill", "decode", "decode_split", "spec"])
+@pytest.mark.parametrize("mode", ["prefill", "decode", "decode_split", "spec", "spec2"])
 def test_paged_attention(Hq, Hkv, D, mode):
     torch.manual_seed(5)
     if mode == "prefill":
         seqs = [(300, 300), (77, 590), (1, 1), (130, 130)]
     elif mode == "spec":
         seqs = [(5, 700), (5, 129), (5, 64)]
+    elif mode == "spec2":          # 2 query positions: up to 32 rows per KV head (two 16-row tiles)
+        seqs = [(2, 700), (2, 129), (2, 64), (2, 2)]
     else:
         seqs = [(1, 1000), (1, 63), (1, 4097)]
     kc, vc, meta, T = _make_paged(seqs, Hkv, D, D)
@@ -230,13 +232,14 @@ def test_paged_attention_long_prefill():
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("mode", ["prefill", "decode"])
+@pytest.mark.parametrize("mode", ["prefill", "decode", "decode1"])
 def test_paged_attention_running_max_rescale(mode):
     """Scores that grow along the keys for some heads and shrink for others, so that
     within one warp some rows must rescale O and others must not."""
     torch.manual_seed(8)
     Hq, Hkv, D = 96, 8, 128
-    seqs = [(700, 700), (300, 1000)] if mode == "prefill" else [(1, 3000), (4, 900)]
+    seqs = {"prefill": [(700, 700), (300, 1000)], "decode": [(1, 3000), (4, 900)],
+            "decode1": [(1, 3000), (1, 900), (1, 65)]}[mode]
     kc, vc, meta, T = _make_paged(seqs, Hkv, D, D)
     # k[t] = 0.02 * pos(t) * ones + noise  ->  q.k grows (or shrinks) linearly with the key position
     bs = kc.shape[2]

@@ -21,7 +21,7 @@ import torch
 from ..models.model import MoETransformer
 from ..ops import basic as B
 from ..ops import _native as N
-from ..ops.attention import AttnMetadata, choose_splits
+from ..ops.attention import AttnMetadata, choose_splits, decode_ctas_per_sm
 from .scheduler import StepPlan
 
 
@@ -116,7 +116,8 @@ class ModelRunner:
                             max_kv_len=max(kv_len), is_decode=plan.is_decode, q_start_host=q_start, kv_len_host=kv_len,
                             seq_slots=T(seq_slots), seq_fresh=T(fresh))
         if plan.is_decode and self.cuda:
-            meta.num_splits = choose_splits(Bn, max(1, self.model.cfg.num_kv_heads), meta.max_kv_len)
+            meta.num_splits = choose_splits(Bn, max(1, self.model.cfg.num_kv_heads), meta.max_kv_len,
+                                            ctas_per_sm=decode_ctas_per_sm(self.model.cfg))
         return T(ids), meta
 
     # ------------------------------------------------------------------
@@ -176,7 +177,8 @@ class ModelRunner:
 
     def _static_meta(self, b: int) -> AttnMetadata:
         s = self._static
-        splits = choose_splits(b, max(1, self.model.cfg.num_kv_heads), self.rc.max_model_len)
+        splits = choose_splits(b, max(1, self.model.cfg.num_kv_heads), self.rc.max_model_len,
+                               ctas_per_sm=decode_ctas_per_sm(self.model.cfg))
         return AttnMetadata(num_seqs=b, q_start=s["q_start"][:b + 1], kv_len=s["kv_len"][:b],
                             block_table=s["bt"][:b], slot_mapping=s["slots"][:b], positions=s["pos"][:b],
                             max_q_len=1, max_kv_len=self.rc.max_model_len, is_decode=True,

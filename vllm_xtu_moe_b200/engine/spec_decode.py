@@ -28,7 +28,7 @@ import torch
 
 from ..ops import _native as N
 from ..ops import basic as B
-from ..ops.attention import AttnMetadata, choose_splits
+from ..ops.attention import AttnMetadata, choose_splits, decode_ctas_per_sm
 
 
 def verify_greedy(target: torch.Tensor, ids: torch.Tensor, q_start: torch.Tensor, num_seqs: int, k: int):
@@ -100,7 +100,8 @@ class SpecDecoder:
                                     max_kv_len=max(kv), is_decode=True, q_start_host=list(range(n + 1)),
                                     kv_len_host=kv)
                 if self.runner.cuda:
-                    meta.num_splits = choose_splits(n, max(1, self.model.cfg.num_kv_heads), max(kv))
+                    meta.num_splits = choose_splits(n, max(1, self.model.cfg.num_kv_heads), max(kv),
+                                                    ctas_per_sm=decode_ctas_per_sm(self.model.cfg))
                 hid = self._mtp(tok, hid, meta)
                 tok = B.argmax(self.model.logits(hid))
                 drafts.append(tok)

@@ -152,7 +152,7 @@ def bench_attn_decode(Bn=4, kv=15000, Hq=96, Hkv=8, D=128, iters=20) -> dict:
                         slot_mapping=torch.zeros(Bn, dtype=torch.int32, device=d),
                         positions=torch.full((Bn,), kv - 1, dtype=torch.int32, device=d), max_q_len=1,
                         max_kv_len=kv, is_decode=True)
-    meta.num_splits = A.choose_splits(Bn, Hkv, kv)
+    meta.num_splits = A.choose_splits(Bn, Hkv, kv, ctas_per_sm=2 if D in (64, 128) else 1)
     ws = torch.empty(A.num_split_workspace(Bn, Hq, D, meta.num_splits), dtype=torch.float32, device=d)
     out = torch.empty(Bn, Hq, D, dtype=torch.bfloat16, device=d)
     fn = lambda: A.paged_attention(q, kc, vc, meta, out=out, workspace=ws)

@@ -123,12 +123,21 @@ def num_split_workspace(T: int, Hq: int, Dv: int, splits: int) -> int:
 
 
 def choose_splits(num_seqs: int, num_kv_heads: int, max_kv_len: int, rows_per_tile_tiles: int = 1,
-                  num_sms: int = 148) -> int:
+                  num_sms: int = 148, ctas_per_sm: int = 1) -> int:
     """Split-KV factor for decode: the largest split count whose CTAs (seqs x kv heads x
-    splits, one CTA per SM) still fit in one wave, so no SM runs a lone second-wave CTA."""
+    splits, `ctas_per_sm` resident per SM) still fit in one wave, so no SM runs a lone
+    second-wave CTA."""
+    slots = num_sms * ctas_per_sm
     ctas = max(1, num_seqs * num_kv_heads * rows_per_tile_tiles)
-    if ctas >= num_sms:
+    if ctas >= slots:
         return 1
     per_split_min = 512  # keys
     max_split = max(1, max_kv_len // per_split_min)
-    return int(max(1, min(max_split, num_sms // ctas, 64)))
+    return int(max(1, min(max_split, slots // ctas, 64)))
+
+
+def decode_ctas_per_sm(cfg) -> int:
+    """CTAs per SM of the decode attention kernel that serves `cfg`: the warp-level GQA
+    decode kernel (head_dim 64 or 128, 96 KB ring) runs two per SM; the tcgen05 kernel
+    (MLA, other head sizes) one."""
+    return 2 if (not cfg.is_mla and cfg.head_dim in (64, 128)) else 1
