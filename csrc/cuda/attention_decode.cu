@@ -14,8 +14,9 @@
 //                               V by ldmatrix.trans
 //              The running max only moves when it grows by more than 2^8, so O is
 //              rescaled rarely.  At the end the key subsets meet in shared memory and
-//              the CTA writes bf16 O (one split) or a normalised partial + log-sum-exp
-//              for attn_combine_kernel (split-KV).
+//              the CTA writes bf16 O (one split) or a normalised partial + log-sum-exp;
+//              with split-KV the last CTA of a (sequence, kv head) to finish (counter)
+//              merges the splits, so no separate combine kernel runs.
 // Why not tcgen05 here: its smallest tile is 64 rows, so 12 real rows would carry 5x
 // padded softmax work, and softmax (not the tensor pipe) is what limits a decode CTA;
 // the warp-level MMA shape matches the GQA group.  The split count is chosen so that
@@ -62,6 +63,7 @@ struct AdParams {
   int splits;
   float* ws_o;              // [splits, T, Hq, D] normalised partials (splits > 1)
   float* ws_lse;            // [splits, T, Hq]  m + log2(l)
+  int* counters;            // [B * Hkv] zeroed; the last split CTA merges and re-zeroes
   int T;
   XtuStatus* status;
 };
@@ -345,12 +347,75 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(const __grid_co
       pk.y = pack_bf16x2(acc[2] * inv, acc[3] * inv);
       *reinterpret_cast<uint2*>(p.o + (size_t)tok * p.o_stride + (size_t)head * D + c) = pk;
     } else {
-      *reinterpret_cast<float4*>(p.ws_o + (((size_t)sp * p.T + tok) * p.Hq + head) * D + c) =
-          make_float4(acc[0] * inv, acc[1] * inv, acc[2] * inv, acc[3] * inv);
+      __stcg(reinterpret_cast<float4*>(p.ws_o + (((size_t)sp * p.T + tok) * p.Hq + head) * D + c),
+             make_float4(acc[0] * inv, acc[1] * inv, acc[2] * inv, acc[3] * inv));
       if (c == 0)
-        p.ws_lse[((size_t)sp * p.T + tok) * p.Hq + head] = Ls > 0.f ? M + __log2f(Ls) : -FLT_MAX;
+        __stcg(p.ws_lse + ((size_t)sp * p.T + tok) * p.Hq + head, Ls > 0.f ? M + __log2f(Ls) : -FLT_MAX);
     }
   }
+  if (p.splits == 1) return;
+  // ---- split-KV: the CTA that finishes last for this (sequence, kv head) merges every
+  // split's normalised partial by its log-sum-exp (split order, so the bits do not depend
+  // on which CTA came last), writes bf16 O and re-zeroes the counter
+  __shared__ int s_last;
+  __threadfence();
+  asm volatile("bar.sync 1, %0;" ::"n"(32 * AD_CWARPS) : "memory");
+  if (tid == 0) s_last = atomicAdd(p.counters + b * p.Hkv + kh, 1) == p.splits - 1;
+  asm volatile("bar.sync 1, %0;" ::"n"(32 * AD_CWARPS) : "memory");
+  if (!s_last) return;
+  __threadfence();
+  // merge weights per (row, split) once, in shared memory (the ring is free again):
+  // w = exp2(lse - max lse) / sum, all loads of a pass issued together
+  float* wsm = reinterpret_cast<float*>(stages);            // [32 rows][64 splits]
+  for (int i = tid; i < nrows * p.splits; i += 32 * AD_CWARPS) {
+    const int r = i / p.splits, s2 = i - r * p.splits;
+    const int qi = r / p.G, hh = r - qi * p.G;
+    wsm[r * 64 + s2] = __ldcg(p.ws_lse + ((size_t)s2 * p.T + q0 + qi) * p.Hq + kh * p.G + hh);
+  }
+  asm volatile("bar.sync 1, %0;" ::"n"(32 * AD_CWARPS) : "memory");
+  if (tid < nrows) {
+    float M = -FLT_MAX;
+    for (int s2 = 0; s2 < p.splits; ++s2) M = fmaxf(M, wsm[tid * 64 + s2]);
+    float sum = 0.f;
+    for (int s2 = 0; s2 < p.splits; ++s2) {
+      const float ls = wsm[tid * 64 + s2];
+      const float w = ls == -FLT_MAX ? 0.f : ad_ex2(ls - M);
+      wsm[tid * 64 + s2] = w;
+      sum += w;
+    }
+    const float inv = sum > 0.f ? 1.f / sum : 0.f;
+    for (int s2 = 0; s2 < p.splits; ++s2) wsm[tid * 64 + s2] *= inv;
+  }
+  asm volatile("bar.sync 1, %0;" ::"n"(32 * AD_CWARPS) : "memory");
+  for (int idx = tid; idx < nrows * C4; idx += 32 * AD_CWARPS) {
+    const int r = idx / C4, c = (idx - r * C4) * 4;
+    const int qi = r / p.G, hh = r - qi * p.G;
+    const int tok = q0 + qi, head = kh * p.G + hh;
+    const float* src = p.ws_o + ((size_t)tok * p.Hq + head) * D + c;
+    const size_t sstride = (size_t)p.T * p.Hq * D;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int s0 = 0; s0 < p.splits; s0 += 8) {
+      float4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        v[u] = s0 + u < p.splits ? __ldcg(reinterpret_cast<const float4*>(src + (s0 + u) * sstride))
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const float w = s0 + u < p.splits ? wsm[r * 64 + s0 + u] : 0.f;
+        acc[0] += w * v[u].x;
+        acc[1] += w * v[u].y;
+        acc[2] += w * v[u].z;
+        acc[3] += w * v[u].w;
+      }
+    }
+    const float inv = 1.f;
+    uint2 pk;
+    pk.x = pack_bf16x2(acc[0] * inv, acc[1] * inv);
+    pk.y = pack_bf16x2(acc[2] * inv, acc[3] * inv);
+    *reinterpret_cast<uint2*>(p.o + (size_t)tok * p.o_stride + (size_t)head * D + c) = pk;
+  }
+  if (tid == 0) p.counters[b * p.Hkv + kh] = 0;
 }
 
 }  // namespace
@@ -371,16 +436,20 @@ static int ad_launch(const CUtensorMap& tk, const CUtensorMap& tv, const AdParam
 }
 
 // Decode attention for GQA caches with D == DV in {64, 128} and at most 32 query rows
-// (query positions x G) per (sequence, kv head).  Returns 1 on launch, 0 when the shape
-// is not one this kernel serves (the caller then uses the general kernel), < 0 on error.
+// (query positions x G) per (sequence, kv head).  Returns 1 on launch (the output is
+// complete: split-KV partials are merged inside), 0 when the shape is not one this
+// kernel serves (the caller then uses the general kernel), < 0 on error.
+// counters: B * Hkv zeroed ints (needed when splits > 1), left zeroed.
 // tk / tv: 2-D maps of the caches viewed as [blocks * Hkv * 64, D] with 64 x 64 boxes.
 int attn_decode_gqa(const CUtensorMap& tk, const CUtensorMap& tv, const void* q, int q_stride, void* o,
                     int o_stride, const int* q_start, const int* kv_len, const int* block_table, int bt_stride,
                     int B, int max_q_len, int T, int Hq, int Hkv, int D, float scale, int splits, float* ws_o,
-                    float* ws_lse, void* status, cudaStream_t s) {
+                    float* ws_lse, int* counters, void* status, cudaStream_t s) {
   const int G = Hq / Hkv;
   const int rows = max_q_len * G;
   if ((D != 64 && D != 128) || rows > 32 || rows <= 0) return 0;
+  if (splits > 1 && counters == nullptr) return 0;
+  if (splits > 64) return 0;
   AdParams p{};
   p.q = reinterpret_cast<const __nv_bfloat16*>(q);
   p.q_stride = q_stride;
@@ -397,6 +466,7 @@ int attn_decode_gqa(const CUtensorMap& tk, const CUtensorMap& tv, const void* q,
   p.splits = splits < 1 ? 1 : splits;
   p.ws_o = ws_o;
   p.ws_lse = ws_lse;
+  p.counters = counters;
   p.T = T;
   p.status = reinterpret_cast<XtuStatus*>(status);
   if (D == 128) return rows <= 16 ? ad_launch<128, 1>(tk, tv, p, B, s) : ad_launch<128, 2>(tk, tv, p, B, s);

@@ -532,7 +532,7 @@ namespace xtu {
 int attn_decode_gqa(const CUtensorMap& tk, const CUtensorMap& tv, const void* q, int q_stride, void* o,
                     int o_stride, const int* q_start, const int* kv_len, const int* block_table, int bt_stride,
                     int B, int max_q_len, int T, int Hq, int Hkv, int D, float scale, int splits, float* ws_o,
-                    float* ws_lse, void* status, cudaStream_t s);
+                    float* ws_lse, int* counters, void* status, cudaStream_t s);
 }  // namespace xtu
 
 using namespace xtu;
@@ -588,11 +588,14 @@ static int launch_attn(const CUtensorMap& tk, const CUtensorMap& tv, const AttnP
 
 extern "C" {
 
-// q [T, Hq, D] (token stride q_stride), caches [blocks, Hkv, 64, D|DV]; v_is_k: V = first DV dims of K (MLA)
+// q [T, Hq, D] (token stride q_stride), caches [blocks, Hkv, 64, D|DV]; v_is_k: V = first DV dims of K (MLA).
+// counters (nullable): >= B * Hkv zeroed ints that let the GQA decode kernel merge its
+// split-KV partials itself (left zeroed).
 int xtu_paged_attention(const void* q, int q_stride, const void* k_cache, const void* v_cache, int v_is_k, void* o,
                         int o_stride, const int* q_start, const int* kv_len, const int* block_table, int bt_stride,
                         int B, int max_q_len, int max_kv_len, int T, int Hq, int Hkv, int D, int DV, int block_size,
-                        int num_blocks, float scale, int splits, float* ws, void* status, cudaStream_t s) {
+                        int num_blocks, float scale, int splits, float* ws, int* counters, void* status,
+                        cudaStream_t s) {
   (void)max_kv_len;
   if (B <= 0 || T <= 0) return 0;
   if (block_size != KV_BLOCK) return -2;
@@ -631,8 +634,9 @@ int xtu_paged_attention(const void* q, int q_stride, const void* k_cache, const 
   // decode-shaped GQA steps with few query rows per KV head: the warp-level decode kernel
   if (grid_x == 1 && !v_is_k && D == DV && (D == 64 || D == 128))
     r = attn_decode_gqa(tk, tv, q, q_stride, o, o_stride, q_start, kv_len, block_table, bt_stride, B, max_q_len, T,
-                        Hq, Hkv, D, scale, p.splits, p.ws_o, p.ws_lse, status, s);
+                        Hq, Hkv, D, scale, p.splits, p.ws_o, p.ws_lse, counters, status, s);
   if (r < 0) return r;
+  if (r == 1) return 1;   // complete, split merge included
   // decode-shaped steps (all of a sequence's query rows fit one 128-row tile): 64-key
   // tiles, a 4-deep K/V ring and a staged block table keep more bytes in flight per SM
   const bool decode_shape = grid_x == 1;
@@ -642,8 +646,7 @@ int xtu_paged_attention(const void* q, int q_stride, const void* k_cache, const 
   // every replica scores a multiple of 16 keys per tile (the softmax reads S in 16-column chunks)
   const int bn = (decode_shape && D == 64) ? 64 : 128;
   while (p.rf > 1 && (bn / p.rf) % 16 != 0) p.rf >>= 1;
-  if (r == 1) {
-  } else if (mla) r = launch_attn<576, 256, 16, 2, 1024, 1>(tk, tv, p, grid_x, B, s);
+  if (mla) r = launch_attn<576, 256, 16, 2, 1024, 1>(tk, tv, p, grid_x, B, s);
   else if (decode_shape && D == 128 && DV == 128) r = launch_attn<128, 128, 128, 2, 256>(tk, tv, p, grid_x, B, s);
   else if (decode_shape && D == 64 && DV == 64) r = launch_attn<64, 64, 64, 6, 1024>(tk, tv, p, grid_x, B, s);
   else if (D == 128 && DV == 128) r = launch_attn<128, 128, 128>(tk, tv, p, grid_x, B, s);

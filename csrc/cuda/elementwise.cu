@@ -203,6 +203,7 @@ __global__ void kv_write_kernel(const __nv_bfloat16* __restrict__ k, const __nv_
 // n_group > 1: group score = sum of the top-2 biased scores of the group;
 // keep the best topk_group groups (DeepSeek-V3 "noaux_tc").
 // ---------------------------------------------------------------------------
+template <int PER>
 __global__ void router_topk_kernel(const float* __restrict__ logits, const float* __restrict__ bias, int T, int E,
                                    int K, int scoring, int n_group, int topk_group, int renorm, float scale,
                                    int* __restrict__ out_ids, float* __restrict__ out_w, int logits_stride) {
@@ -210,11 +211,10 @@ __global__ void router_topk_kernel(const float* __restrict__ logits, const float
   const int lane = threadIdx.x & 31;
   if (gw >= T) return;
   const float* lg = logits + (size_t)gw * logits_stride;
-  constexpr int MAXP = 32;
-  float sc[MAXP], sel[MAXP];
-  const int per = (E + 31) / 32;
+  float sc[PER], sel[PER];   // PER = compile-time scores per lane, so these stay in registers
   float mx = -FLT_MAX;
-  for (int j = 0; j < per; ++j) {
+  #pragma unroll
+  for (int j = 0; j < PER; ++j) {
     const int e = lane + 32 * j;
     sc[j] = e < E ? lg[e] : -FLT_MAX;
     mx = fmaxf(mx, sc[j]);
@@ -222,24 +222,29 @@ __global__ void router_topk_kernel(const float* __restrict__ logits, const float
   if (scoring == 0) {
     mx = warp_max(mx);
     float s = 0.f;
-    for (int j = 0; j < per; ++j) {
+    #pragma unroll
+  for (int j = 0; j < PER; ++j) {
       const int e = lane + 32 * j;
       sc[j] = e < E ? __expf(sc[j] - mx) : 0.f;
       s += sc[j];
     }
     s = warp_sum(s);
     const float inv = 1.f / s;
-    for (int j = 0; j < per; ++j) sc[j] *= inv;
+    #pragma unroll
+  for (int j = 0; j < PER; ++j) sc[j] *= inv;
   } else if (scoring == 1) {
-    for (int j = 0; j < per; ++j) sc[j] = 1.f / (1.f + __expf(-sc[j]));
+    #pragma unroll
+  for (int j = 0; j < PER; ++j) sc[j] = 1.f / (1.f + __expf(-sc[j]));
   } else {
-    for (int j = 0; j < per; ++j) {
+    #pragma unroll
+  for (int j = 0; j < PER; ++j) {
       const float x = sc[j];
       const float sp = x > 20.f ? x : log1pf(__expf(x));
       sc[j] = sqrtf(sp);
     }
   }
-  for (int j = 0; j < per; ++j) {
+  #pragma unroll
+  for (int j = 0; j < PER; ++j) {
     const int e = lane + 32 * j;
     sel[j] = e < E ? sc[j] + (bias ? bias[e] : 0.f) : -FLT_MAX;
   }
@@ -251,7 +256,8 @@ __global__ void router_topk_kernel(const float* __restrict__ logits, const float
     for (int g = 0; g < n_group; ++g) {
       // top-2 within group g
       float b1 = -FLT_MAX, b2 = -FLT_MAX;
-      for (int j = 0; j < per; ++j) {
+      #pragma unroll
+  for (int j = 0; j < PER; ++j) {
         const int e = lane + 32 * j;
         if (e < E && e / gs == g) {
           const float v = sel[j];
@@ -277,7 +283,8 @@ __global__ void router_topk_kernel(const float* __restrict__ logits, const float
         if (!((keep >> g) & 1ull) && gscore[g] > bv) { bv = gscore[g]; best = g; }
       if (best >= 0) keep |= 1ull << best;
     }
-    for (int j = 0; j < per; ++j) {
+    #pragma unroll
+  for (int j = 0; j < PER; ++j) {
       const int e = lane + 32 * j;
       if (e < E && !((keep >> (e / gs)) & 1ull)) sel[j] = -FLT_MAX;
     }
@@ -287,7 +294,8 @@ __global__ void router_topk_kernel(const float* __restrict__ logits, const float
   int myid = -1;
   for (int r = 0; r < K; ++r) {
     float bv = -FLT_MAX; int bi = 0x7fffffff;
-    for (int j = 0; j < per; ++j) {
+    #pragma unroll
+  for (int j = 0; j < PER; ++j) {
       const int e = lane + 32 * j;
       if (sel[j] > bv || (sel[j] == bv && e < bi)) { bv = sel[j]; bi = e; }
     }
@@ -300,7 +308,7 @@ __global__ void router_topk_kernel(const float* __restrict__ logits, const float
     float w = 0.f;
     if ((bi & 31) == lane) {
       const int j = bi >> 5;
-      for (int jj = 0; jj < per; ++jj) if (jj == j) { w = sc[jj]; sel[jj] = -FLT_MAX; }
+      for (int jj = 0; jj < PER; ++jj) if (jj == j) { w = sc[jj]; sel[jj] = -FLT_MAX; }
     }
     w = __shfl_sync(0xffffffffu, w, bi & 31);
     wsum += w;
@@ -392,6 +400,91 @@ __global__ void moe_scatter_gather_kernel(const int* __restrict__ ids, const flo
   }
 }
 
+// Decode-size permute (one CTA, E <= 1024 local experts): per-expert counts, seg, the
+// (row -> pair) permutation, the list of experts that have rows, and for the token-direct
+// gate/up GEMV the map tokrow[a * 16 + t] = row of token t's pair with active expert a
+// (-1 if none; t < 16).  Rows within an expert follow arrival order (atomics); each row's
+// result is computed independently, so the order does not change any value.
+__global__ void __launch_bounds__(512) moe_permute_decode_kernel(const int* __restrict__ ids,
+                                                                 const float* __restrict__ weights, int n, int K,
+                                                                 int lo, int hi, int* __restrict__ seg,
+                                                                 int* __restrict__ perm_slot,
+                                                                 float* __restrict__ perm_w, int* __restrict__ active,
+                                                                 int* __restrict__ tokrow) {
+  __shared__ int cnt[1024], cur[1024], apos[1024];
+  __shared__ int wc[16], wa[16], nact;
+  const int E = hi - lo, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int e = tid; e < 1024; e += 512) cnt[e] = 0;
+  __syncthreads();
+  for (int p = tid; p < n; p += 512) {
+    const int id = ids[p];
+    if (id >= lo && id < hi) atomicAdd(&cnt[id - lo], 1);
+  }
+  __syncthreads();
+  // exclusive scans of the counts and of the "has rows" flags; thread tid owns entries 2tid, 2tid+1
+  const int e0 = 2 * tid;
+  const int c0 = cnt[e0], c1 = cnt[e0 + 1];
+  const int a0 = c0 > 0, a1 = c1 > 0;
+  int sc = c0 + c1, sa = a0 + a1;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, sc, o), va = __shfl_up_sync(0xffffffffu, sa, o);
+    if (lane >= o) {
+      sc += v;
+      sa += va;
+    }
+  }
+  if (lane == 31) {
+    wc[warp] = sc;
+    wa[warp] = sa;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    int v = lane < 16 ? wc[lane] : 0, va = lane < 16 ? wa[lane] : 0;
+    const int v0 = v, va0 = va;
+#pragma unroll
+    for (int o = 1; o < 16; o <<= 1) {
+      const int t = __shfl_up_sync(0xffffffffu, v, o), ta = __shfl_up_sync(0xffffffffu, va, o);
+      if (lane >= o) {
+        v += t;
+        va += ta;
+      }
+    }
+    if (lane < 16) {
+      wc[lane] = v - v0;
+      wa[lane] = va - va0;
+    }
+    if (lane == 15) nact = va;
+  }
+  __syncthreads();
+  const int exc = sc - (c0 + c1) + wc[warp], exa = sa - (a0 + a1) + wa[warp];
+  if (e0 < E) {
+    seg[e0] = exc;
+    cur[e0] = exc;
+    apos[e0] = exa;
+    if (a0) active[1 + exa] = e0;
+  }
+  if (e0 + 1 < E) {
+    seg[e0 + 1] = exc + c0;
+    cur[e0 + 1] = exc + c0;
+    apos[e0 + 1] = exa + a0;
+    if (a1) active[1 + exa + a0] = e0 + 1;
+  }
+  if (tid == 511) seg[E] = exc + c0 + c1;
+  if (tid == 0) active[0] = nact;
+  if (tokrow)
+    for (int i = tid; i < nact * 16; i += 512) tokrow[i] = -1;
+  __syncthreads();
+  for (int p = tid; p < n; p += 512) {
+    const int id = ids[p];
+    if (id < lo || id >= hi) continue;
+    const int row = atomicAdd(&cur[id - lo], 1);
+    perm_slot[row] = p;
+    perm_w[row] = weights ? weights[p] : 1.f;
+    if (tokrow) tokrow[apos[id - lo] * 16 + p / K] = row;
+  }
+}
+
 // out[t] = sum_k slot[t*K+k] (local pairs only) + shared[t] + extra[t]
 __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ slots, const int* __restrict__ ids, int T,
                                    int K, int H, int lo, int hi, const __nv_bfloat16* __restrict__ shared,
@@ -401,11 +494,25 @@ __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ slots, cons
   // grid.y splits the hidden dimension so that decode-sized T still fills the GPU
   const int span = (H / 8 + gridDim.y - 1) / gridDim.y * 8;
   const int h0 = blockIdx.y * span, h1 = min(H, h0 + span);
+  // which of the token's pairs are local, read once per block (K <= 64), so the slot
+  // loads below do not each wait on an id load
+  __shared__ unsigned long long local_mask;
+  if (threadIdx.x < 32) {
+    unsigned long long m = 0ull;
+    for (int k = threadIdx.x; k < K && k < 64; k += 32) {
+      const int id = ids[(size_t)t * K + k];
+      if (id >= lo && id < hi) m |= 1ull << k;
+    }
+    for (int o = 16; o > 0; o >>= 1) m |= __shfl_xor_sync(0xffffffffu, m, o);
+    if (threadIdx.x == 0) local_mask = m;
+  }
+  __syncthreads();
+  const unsigned long long lm = local_mask;
   for (int i = h0 + threadIdx.x * 8; i < h1; i += blockDim.x * 8) {
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll 8
     for (int k = 0; k < K; ++k) {
-      const int id = ids[(size_t)t * K + k];
-      if (id < lo || id >= hi) continue;
+      if (!((lm >> k) & 1ull)) continue;
       const uint4 v = *reinterpret_cast<const uint4*>(slots + ((size_t)t * K + k) * H + i);
       const uint32_t vs[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
@@ -615,8 +722,17 @@ int xtu_router_topk(const float* logits, const float* bias, int T, int E, int K,
                     cudaStream_t s) {
   if (T <= 0) return 0;
   if (E > 1024 || K > 32 || n_group > 64) return -2;
-  router_topk_kernel<<<(T * 32 + 255) / 256, 256, 0, s>>>(logits, bias, T, E, K, scoring, n_group, topk_group, renorm,
-                                                          scale, out_ids, out_w, logits_stride);
+  const int per = (E + 31) / 32;
+#define XTU_TOPK(P)                                                                                          \
+  router_topk_kernel<P><<<(T * 32 + 255) / 256, 256, 0, s>>>(logits, bias, T, E, K, scoring, n_group, topk_group, \
+                                                             renorm, scale, out_ids, out_w, logits_stride)
+  if (per <= 1) XTU_TOPK(1);
+  else if (per <= 2) XTU_TOPK(2);
+  else if (per <= 4) XTU_TOPK(4);
+  else if (per <= 8) XTU_TOPK(8);
+  else if (per <= 16) XTU_TOPK(16);
+  else XTU_TOPK(32);
+#undef XTU_TOPK
   return rc_last();
 }
 
@@ -642,10 +758,20 @@ int xtu_moe_permute(const int* ids, const float* weights, int T, int K, int lo, 
   return rc_last(n > 0 ? 3 : 1);
 }
 
+// decode permute without the activation gather (see moe_permute_decode_kernel): E <= 1024,
+// tokrow (nullable) needs n / K <= 16 tokens and n_active * 16 ints.
+int xtu_moe_permute_decode(const int* ids, const float* weights, int T, int K, int lo, int hi, int* seg,
+                           int* perm_slot, float* perm_w, int* active, int* tokrow, cudaStream_t s) {
+  const int E = hi - lo;
+  if (E <= 0 || E > 1024 || (tokrow && T > 16)) return -2;
+  moe_permute_decode_kernel<<<1, 512, 0, s>>>(ids, weights, T * K, K, lo, hi, seg, perm_slot, perm_w, active, tokrow);
+  return rc_last();
+}
+
 int xtu_moe_combine(const void* slots, const int* ids, int T, int K, int H, int lo, int hi, const void* shared,
                     const float* extra, void* out, float* out_f32, cudaStream_t s) {
   if (T <= 0) return 0;
-  if (H % 8 != 0) return -2;
+  if (H % 8 != 0 || K > 64) return -2;
   const int threads = H / 8 < 128 ? ((H / 8 + 31) / 32) * 32 : 128;
   int ysplit = (H / 8 + threads - 1) / threads;          // one 8-wide vector per thread
   if (T * ysplit > 2048) ysplit = (2048 + T - 1) / T;

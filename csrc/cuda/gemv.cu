@@ -29,7 +29,10 @@
 // experts that have rows (moe_active_kernel), so idle experts cost no CTAs.
 //   * gate/up: the tile's two 16-row halves are 16 gate rows and the matching 16 up rows
 //     (W13 rows interleaved in 256-row blocks), so SwiGLU is applied in registers and
-//     the [T*K, 2I] intermediate never exists.
+//     the [T*K, 2I] intermediate never exists.  At decode (<= 16 tokens) the activations
+//     are not gathered per expert at all: every expert multiplies the step's tokens (they
+//     fit the MMA's 8 or 16 columns) and writes only its own tokens' rows of h, found
+//     through the (expert, token) -> row map of moe_permute_decode.
 //   * down: rows scaled by the pair's routing weight and written to the pair's slot row.
 // Dense calls with few tiles split K across CTAs; the last CTA of a tile (completion
 // counter) sums the fp32 partials.
@@ -90,7 +93,7 @@ struct GvCfg {
   static constexpr int XBOXES = KSTAGE / 64;                     // 64 bf16 per 128-byte box
   static constexpr int X_BYTES = XBOXES * XROWS * 128;
   static constexpr int STAGE_BYTES = GV_W_BYTES + X_BYTES;       // multiple of 1024
-  static constexpr int STAGES = STAGE_BYTES <= 12288 ? 5 : 4;
+  static constexpr int STAGES = 4;
   static constexpr int RED_FLOATS = GV_CWARPS * 32 * 2 * NT * 4;
   static constexpr int BYTES = 1024 + STAGES * STAGE_BYTES + RED_FLOATS * 4 + 2 * GV_MAX_KBLK * 4 +
                                2 * STAGES * 8 + 64;
@@ -355,14 +358,34 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_dense_kernel(
 #pragma unroll
       for (int n = 0; n < NT; ++n)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int row = rows[t] + g4 + (i >> 1) * 8;
-          const int tok = n * 8 + 2 * tq + (i & 1);
-          float v = 0.f;
-          if (row < N && tok < M)
-            for (int q = 0; q < splits; ++q) v += __ldcg(ws + ((size_t)q * 16 + tok) * N + row);
-          acc[t][n][i] = v;
-        }
+        for (int i = 0; i < 4; ++i) acc[t][n][i] = 0.f;
+    // four splits per round, all their loads issued before any add (one L2 latency per
+    // round, not per split); the adds keep split order, so the sum is reproducible
+    for (int q0 = 0; q0 < splits; q0 += 4) {
+      float pv[4][2][NT][4];
+#pragma unroll
+      for (int qq = 0; qq < 4; ++qq)
+#pragma unroll
+        for (int t = 0; t < 2; ++t)
+#pragma unroll
+          for (int n = 0; n < NT; ++n)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int row = rows[t] + g4 + (i >> 1) * 8;
+              const int tok = n * 8 + 2 * tq + (i & 1);
+              const int q = q0 + qq;
+              pv[qq][t][n][i] = (q < splits && row < N && tok < M) ? __ldcg(ws + ((size_t)q * 16 + tok) * N + row)
+                                                                   : 0.f;
+            }
+#pragma unroll
+      for (int qq = 0; qq < 4; ++qq)
+#pragma unroll
+        for (int t = 0; t < 2; ++t)
+#pragma unroll
+          for (int n = 0; n < NT; ++n)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) acc[t][n][i] += pv[qq][t][n][i];
+    }
     if (lane == 0) counters[blockIdx.x] = 0;
   }
 #pragma unroll
@@ -390,11 +413,16 @@ template <bool FP8, int NT>
 __global__ void __launch_bounds__(GV_THREADS) moe_gemv_gate_up_kernel(
     const __grid_constant__ CUtensorMap tmap, const __grid_constant__ CUtensorMap xmap,
     const float* __restrict__ wscale, int I, int K, const int* __restrict__ seg, const int* __restrict__ active,
-    __nv_bfloat16* __restrict__ h, float limit, float alpha, float beta, XtuStatus* st) {
+    const int* __restrict__ tokrow, int ntok, __nv_bfloat16* __restrict__ h, float limit, float alpha, float beta,
+    XtuStatus* st) {
   if ((int)blockIdx.y >= active[0]) return;
   const int e = active[1 + blockIdx.y];
   const int s0 = seg[e], cnt = seg[e + 1] - s0;
   if (cnt <= 0) return;
+  // token-direct form: x holds the step's ntok tokens (not gathered per expert); the
+  // expert multiplies all of them and keeps the columns of its own tokens (tokrow)
+  const int* trow = tokrow ? tokrow + blockIdx.y * 16 : nullptr;
+  const int xrow0 = trow ? 0 : s0, xcnt = trow ? ntok : cnt;
   uint64_t *full, *empty;
   float *red, *sc_sm;
   uint8_t* stages = gv_setup<FP8, NT>(full, empty, red, sc_sm);
@@ -408,11 +436,11 @@ __global__ void __launch_bounds__(GV_THREADS) moe_gemv_gate_up_kernel(
   const int rows[2] = {e * 2 * I + grow, e * 2 * I + grow + 128};
   const float* esc = FP8 ? wscale + (size_t)e * ((2 * I + 127) >> 7) * sk : nullptr;
   uint32_t pb = 0;
-  for (int mb = 0; mb < cnt; mb += 8 * NT) {
-    const int mc = min(8 * NT, cnt - mb);
+  for (int mb = 0; mb < xcnt; mb += 8 * NT) {
+    const int mc = min(8 * NT, xcnt - mb);
     float acc[2][NT][4];
     if (!gv_stream_tile<FP8, NT>(&tmap, &xmap, stages, full, empty, sc_sm, pb, rows, 0, nstages, K, esc, sk,
-                                 grow >> 7, (grow + 128) >> 7, s0 + mb, mc, acc, st))
+                                 grow >> 7, (grow + 128) >> 7, xrow0 + mb, mc, acc, st))
       return;
     gv_reduce<NT>(acc, red);
     if (warp != 1) continue;
@@ -422,14 +450,15 @@ __global__ void __launch_bounds__(GV_THREADS) moe_gemv_gate_up_kernel(
       for (int i = 0; i < 4; ++i) {
         const int j = j0 + g4 + (i >> 1) * 8;
         const int tok = n * 8 + 2 * tq + (i & 1);
-        if (tok < mc) {
+        const int hr = trow ? (tok < mc ? trow[mb + tok] : -1) : (tok < mc ? s0 + mb + tok : -1);
+        if (hr >= 0) {
           float g = acc[0][n][i], u = acc[1][n][i];
           if (limit > 0.f) { g = fminf(g, limit); u = fminf(fmaxf(u, -limit), limit); }
           const float v = (g / (1.f + __expf(-alpha * g))) * (u + beta);
           if (FP8)   // the down GEMV's activation form: f16 x 2^-8
-            reinterpret_cast<__half*>(h)[(size_t)(s0 + mb + tok) * I + j] = __float2half_rn(v * 0.00390625f);
+            reinterpret_cast<__half*>(h)[(size_t)hr * I + j] = __float2half_rn(v * 0.00390625f);
           else
-            h[(size_t)(s0 + mb + tok) * I + j] = __float2bfloat16(v);
+            h[(size_t)hr * I + j] = __float2bfloat16(v);
         }
       }
   }
@@ -569,6 +598,16 @@ static inline int gv_stages_per_tile(int K, bool fp8) {
   return (K + kstage - 1) / kstage;
 }
 
+// K splits of a dense GEMV whose tiles do not fill the resident CTA slots: as many as
+// keep every split in the first wave, at least 2 stages per split, within the workspace
+static int gv_splits(int tiles, int S, int N, int slots) {
+  if (tiles >= slots) return 1;
+  int splits = slots / tiles;
+  if (splits > 16) splits = 16;
+  while (splits > 1 && (S / splits < 2 || (long long)splits * 16 * N > GV_WS_PART_FLOATS)) --splits;
+  return splits;
+}
+
 // bf16 rows -> f16 x 2^-8 rows in the workspace's activation scratch
 static const void* gv_convert_x(const void* x, int rows, int K, int stride, float* ws, cudaStream_t s) {
   uint4* x16 = reinterpret_cast<uint4*>(ws + GV_WS_PART_FLOATS);
@@ -605,22 +644,17 @@ int xtu_gemv(const void* W, const float* wscale, int fp8, int N, int K, const vo
   rc = gv_tmap(&xm, x, (uint64_t)M, K, false, 8 * nt, x_stride);
   if (rc) return rc;
   XtuStatus* st = reinterpret_cast<XtuStatus*>(status);
-  int splits = 1;
-  if (tiles < 3 * gemv_num_sms()) {   // too few tiles to fill the GPU: split K as well
-    splits = (3 * gemv_num_sms() + tiles - 1) / tiles;
-    if (splits > 4) splits = 4;
-    while (splits > 1 && S / splits < 4) --splits;     // keep a few stages per CTA
-    if ((long long)splits * 16 * N > GV_WS_PART_FLOATS) splits = 1;
-  }
-  const dim3 grid(tiles, splits);
 #define XTU_GEMV_LAUNCH(F, NTV)                                                                              \
   do {                                                                                                       \
-    static bool init = false;                                                                                \
-    if (!init) {                                                                                             \
+    static int occ = 0;                                                                                      \
+    if (!occ) {                                                                                              \
       rc = gv_smem_attr(gemv_dense_kernel<F, NTV>, GvCfg<F, NTV>::BYTES);                                    \
       if (rc) return rc;                                                                                     \
-      init = true;                                                                                           \
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gemv_dense_kernel<F, NTV>, GV_THREADS,          \
+                                                        GvCfg<F, NTV>::BYTES) != cudaSuccess || occ < 1)      \
+        occ = 1;                                                                                             \
     }                                                                                                        \
+    const dim3 grid(tiles, gv_splits(tiles, S, N, occ * gemv_num_sms()));                                   \
     gemv_dense_kernel<F, NTV><<<grid, GV_THREADS, GvCfg<F, NTV>::BYTES, s>>>(                               \
         tm, xm, wscale, N, K, M, (const __nv_bfloat16*)bias, y, y_stride, y_f32, ws, counters, st);          \
   } while (0)
@@ -636,23 +670,31 @@ int xtu_gemv(const void* W, const float* wscale, int fp8, int N, int K, const vo
 
 // grouped decode MoE: gate/up+SwiGLU then down+weight+scatter.  mmax bounds the rows of
 // any one expert (<= 16); max_active bounds the experts with rows (min(E, tokens * top_k));
-// n_rows: rows of the permuted activations xp [n_rows, H] and of h [n_rows, I];
-// active: scratch of E + 1 ints; ws as for xtu_gemv (its activation scratch only).  fp8:
+// n_rows: rows of the permuted activations xp [n_rows, H] and of h [n_rows, I].
+// tokrow (nullable, from moe_permute_decode): xp is then the step's ntok <= 16 tokens
+// [ntok, H] with row stride x_stride, not gathered per expert;
+// active: E + 1 ints, filled here from seg unless active_ready says the caller already
+// holds the list there; ws as for xtu_gemv (its activation scratch only).  fp8:
 // xp_f16s says xp already holds f16 x 2^-8 rows (moe_permute's form); h is written in
 // that form too.
 int xtu_moe_gemv(const void* W13, const float* s13, const void* W2, const float* s2, int fp8, int E, int H, int I,
-                 const void* xp, int xp_f16s, const int* seg, const int* perm_slot, const float* perm_w, void* h,
-                 void* slots, int mmax, int max_active, int n_rows, int* active, float limit, float alpha,
-                 float beta, float* ws, void* status, cudaStream_t s) {
+                 const void* xp, int xp_f16s, int x_stride, const int* tokrow, int ntok, const int* seg,
+                 const int* perm_slot, const float* perm_w, void* h,
+                 void* slots, int mmax, int max_active, int n_rows, int* active, int active_ready, float limit,
+                 float alpha, float beta, float* ws, void* status, cudaStream_t s) {
   if (mmax <= 0 || n_rows <= 0) return 0;
   if (mmax > 16 || H % 32 != 0 || I % 128 != 0 || active == nullptr) return -2;
   if (H > GV_MAX_KBLK * 128 || I > GV_MAX_KBLK * 128) return -3;
   if (max_active <= 0 || max_active > E) max_active = E;
   const int nt = mmax > 8 ? 2 : 1;
   int launches = 3;
+  if (tokrow && (ntok <= 0 || ntok > 16 || ntok > mmax)) return -2;
+  const int x_rows = tokrow ? ntok : n_rows;
+  if (x_stride <= 0) x_stride = H;
   if (fp8 && !xp_f16s) {
-    if (ws == nullptr || (long long)n_rows * H > GV_WS_X_HALVES) return -4;
-    xp = gv_convert_x(xp, n_rows, H, H, ws, s);
+    if (ws == nullptr || (long long)x_rows * H > GV_WS_X_HALVES) return -4;
+    xp = gv_convert_x(xp, x_rows, H, x_stride, ws, s);
+    x_stride = H;
     ++launches;
   }
   CUtensorMap t13, t2, xm, hm;
@@ -660,11 +702,12 @@ int xtu_moe_gemv(const void* W13, const float* s13, const void* W2, const float*
   if (rc) return rc;
   rc = gv_tmap(&t2, W2, (uint64_t)E * H, I, fp8 != 0);
   if (rc) return rc;
-  rc = gv_tmap(&xm, xp, (uint64_t)n_rows, H, false, 8 * nt);
+  rc = gv_tmap(&xm, xp, (uint64_t)x_rows, H, false, 8 * nt, x_stride);
   if (rc) return rc;
   rc = gv_tmap(&hm, h, (uint64_t)n_rows, I, false, 8 * nt);
   if (rc) return rc;
-  moe_active_kernel<<<1, 32, 0, s>>>(seg, E, active);
+  if (!active_ready) moe_active_kernel<<<1, 32, 0, s>>>(seg, E, active);
+  else --launches;
   XtuStatus* st = reinterpret_cast<XtuStatus*>(status);
   const dim3 g1(I / 16, max_active), g2((H + 31) / 32, max_active);
 #define XTU_MOE_GEMV_LAUNCH(F, NTV)                                                                          \
@@ -677,7 +720,7 @@ int xtu_moe_gemv(const void* W13, const float* s13, const void* W2, const float*
       init = true;                                                                                           \
     }                                                                                                        \
     moe_gemv_gate_up_kernel<F, NTV><<<g1, GV_THREADS, GvCfg<F, NTV>::BYTES, s>>>(                           \
-        t13, xm, s13, I, H, seg, active, (__nv_bfloat16*)h, limit, alpha, beta, st);                        \
+        t13, xm, s13, I, H, seg, active, tokrow, ntok, (__nv_bfloat16*)h, limit, alpha, beta, st);          \
     moe_gemv_down_kernel<F, NTV><<<g2, GV_THREADS, GvCfg<F, NTV>::BYTES, s>>>(                              \
         t2, hm, s2, H, I, seg, active, perm_slot, perm_w, (__nv_bfloat16*)slots, st);                        \
   } while (0)

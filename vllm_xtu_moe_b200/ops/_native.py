@@ -62,10 +62,11 @@ _SIGS: dict[str, list] = {
     "xtu_ep_dispatch": [P, P, c_int, c_int, c_int, c_int, c_int, P, c_int, c_int, P, P, P, P, P, c_int, P],
     "xtu_silu_mul": [P, c_int, c_int, c_float, c_float, c_float, P, P],
     "xtu_gemv": [P, P, c_int, c_int, c_int, P, c_int, c_int, P, P, c_int, c_int, P, P, P, P],
-    "xtu_moe_gemv": [P, P, P, P, c_int, c_int, c_int, c_int, P, c_int, P, P, P, P, P, c_int, c_int, c_int, P,
-                     c_float, c_float, c_float, P, P, P],
+    "xtu_moe_gemv": [P, P, P, P, c_int, c_int, c_int, c_int, P, c_int, c_int, P, c_int, P, P, P, P, P, c_int, c_int,
+                     c_int, P, c_int, c_float, c_float, c_float, P, P, P],
+    "xtu_moe_permute_decode": [P, P, c_int, c_int, c_int, c_int, P, P, P, P, P, P],
     "xtu_paged_attention": [P, c_int, P, P, c_int, P, c_int, P, P, P, c_int, c_int, c_int, c_int, c_int, c_int,
-                            c_int, c_int, c_int, c_int, c_int, c_float, c_int, P, P, P],
+                            c_int, c_int, c_int, c_int, c_int, c_float, c_int, P, P, P, P],
 }
 
 
@@ -179,8 +180,9 @@ def check_status(device=None, reset: bool = True) -> None:
     if vals[0] != 0:
         if reset:
             st.zero_()
-            from . import gemm      # a stopped GEMV launch may have left tile counters set
+            from . import attention, gemm   # a stopped launch may have left counters set
             gemm.gemv_ws_reset(st.device)
+            attention.split_counters_reset(st.device)
         raise RuntimeError(
             f"xtu kernel error: {ERROR_NAMES.get(vals[0], vals[0])} (site {vals[1]}, block {vals[2]}, extra {vals[3]})")
 

@@ -84,6 +84,28 @@ def paged_attention_ref(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.T
 
 
 KV_BLOCK = 64   # tokens per KV-cache block read by the GPU kernel
+_SPLIT_COUNTERS: dict = {}
+_MAX_SPLIT_GROUPS = 1 << 16
+
+
+def _split_counters(device) -> torch.Tensor:
+    """Per-device zeroed ints, one per (sequence, kv head): the decode kernel's last
+    split CTA of a group merges the partials and re-zeroes its counter.  Allocated once
+    (captured graphs keep the pointer)."""
+    key = device.index if device.index is not None else torch.cuda.current_device()
+    t = _SPLIT_COUNTERS.get(key)
+    if t is None:
+        t = torch.zeros(_MAX_SPLIT_GROUPS, dtype=torch.int32, device=device)
+        _SPLIT_COUNTERS[key] = t
+    return t
+
+
+def split_counters_reset(device) -> None:
+    """Re-zero the split counters (after a launch that reported an error)."""
+    key = device.index if device.index is not None else torch.cuda.current_device()
+    t = _SPLIT_COUNTERS.get(key)
+    if t is not None:
+        t.zero_()
 
 
 def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor | None, meta: AttnMetadata,
@@ -109,11 +131,13 @@ def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
     if need and (ws is None or ws.numel() < need):
         ws = torch.empty(need, dtype=torch.float32, device=q.device)
     vc = v_cache if v_cache is not None else k_cache
+    cnt = _split_counters(q.device) if splits > 1 and meta.num_seqs * Hk <= _MAX_SPLIT_GROUPS else None
     N.call("xtu_paged_attention", q.data_ptr(), q.stride(0), k_cache.data_ptr(), vc.data_ptr(),
            int(v_cache is None), o.data_ptr(), o.stride(0), meta.q_start.data_ptr(), meta.kv_len.data_ptr(),
            meta.block_table.data_ptr(), meta.block_table.stride(0), meta.num_seqs, meta.max_q_len,
            meta.max_kv_len, T, Hq, Hk, D, Dv, k_cache.shape[2], k_cache.shape[0], float(scale), splits,
-           N.ptr(ws) if splits > 1 else None, N.status_buffer(q.device).data_ptr(), N.stream_ptr(q.device))
+           N.ptr(ws) if splits > 1 else None, N.ptr(cnt), N.status_buffer(q.device).data_ptr(),
+           N.stream_ptr(q.device))
     return o
 
 

@@ -102,6 +102,7 @@ class MoEWorkspace:
         self.mx = G.max_mtiles(n, E)
         self.tiles = torch.empty(self.mx * 4, dtype=torch.int32, device=d)
         self.active = torch.zeros(E + 1, dtype=torch.int32, device=d)   # decode GEMV: experts with rows
+        self.tokrow = torch.zeros(min(E, n) * 16, dtype=torch.int32, device=d)   # decode: (expert, token) -> row
         self.ntiles = torch.zeros(1, dtype=torch.int32, device=d)
 
     def nbytes(self) -> int:
@@ -144,19 +145,32 @@ def moe_experts_partial(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tenso
     # decode: weight-streaming grouped GEMV (gate/up + SwiGLU, down + weight + scatter); with
     # fp8 experts it reads the gathered rows as f16 x 2^-8, which the permute writes
     gemv_path = T <= G.GEMV_MAX_M and experts.interleaved and experts.fmt not in G.FP4_FMTS
+    I = experts.inter
+    if gemv_path and E <= 1024:
+        # one-CTA permute (no row gather): the gate/up GEMV reads the T tokens directly
+        # and keeps each expert's own columns through ws.tokrow
+        xt = G.tma_rows(x)
+        N.call("xtu_moe_permute_decode", ids.data_ptr(), weights.data_ptr(), T, K, lo, lo + E, ws.seg.data_ptr(),
+               ws.perm_slot.data_ptr(), ws.perm_w.data_ptr(), ws.active.data_ptr(), ws.tokrow.data_ptr(), s)
+        N.call("xtu_moe_gemv", experts.w13.data_ptr(), N.ptr(experts.s13 if fp8 else None),
+               experts.w2.data_ptr(), N.ptr(experts.s2 if fp8 else None), int(fp8), E, H, I, xt.data_ptr(), 0,
+               xt.stride(0), ws.tokrow.data_ptr(), T, ws.seg.data_ptr(), ws.perm_slot.data_ptr(),
+               ws.perm_w.data_ptr(), ws.h.data_ptr(), ws.slots.data_ptr(), T, min(E, T * K), n,
+               ws.active.data_ptr(), 1, float(act_limit), float(act_alpha), float(act_beta), _gv_ws(x.device),
+               N.status_buffer(x.device).data_ptr(), s)
+        return
     f16s = int(gemv_path and fp8)
     N.call("xtu_moe_permute", ids.data_ptr(), weights.data_ptr(), T, K, lo, lo + E, ws.counts.data_ptr(),
            ws.seg.data_ptr(), ws.cursor.data_ptr(), ws.perm_slot.data_ptr(), ws.perm_w.data_ptr(), x.data_ptr(), H,
            x.stride(0), ws.xp.data_ptr(), f16s, s)
-    I = experts.inter
     if experts.fmt in G.FP4_FMTS:
         _experts_fp4(experts, ws, n, act_limit, act_alpha, act_beta)
         return
     if gemv_path:
         N.call("xtu_moe_gemv", experts.w13.data_ptr(), N.ptr(experts.s13 if fp8 else None),
                experts.w2.data_ptr(), N.ptr(experts.s2 if fp8 else None), int(fp8), E, H, I, ws.xp.data_ptr(), f16s,
-               ws.seg.data_ptr(), ws.perm_slot.data_ptr(), ws.perm_w.data_ptr(), ws.h.data_ptr(),
-               ws.slots.data_ptr(), T, min(E, T * K), n, ws.active.data_ptr(), float(act_limit), float(act_alpha),
+               H, None, 0, ws.seg.data_ptr(), ws.perm_slot.data_ptr(), ws.perm_w.data_ptr(), ws.h.data_ptr(),
+               ws.slots.data_ptr(), T, min(E, T * K), n, ws.active.data_ptr(), 0, float(act_limit), float(act_alpha),
                float(act_beta), _gv_ws(x.device), N.status_buffer(x.device).data_ptr(), s)
         return
     # the segment table of this call has E + 1 entries (the workspace may serve more experts)
@@ -254,12 +268,12 @@ def dense_swiglu_gemv(x: torch.Tensor, w13: torch.Tensor, s13, w2: torch.Tensor,
                   slot=torch.arange(T, dtype=torch.int32, device=d),
                   w=torch.ones(T, dtype=torch.float32, device=d),
                   h=torch.empty(T, I, dtype=torch.bfloat16, device=d),
-                  active=torch.zeros(2, dtype=torch.int32, device=d))
+                  active=torch.tensor([1, 0], dtype=torch.int32, device=d))   # one expert, always active
         cache[key] = st
     y = torch.empty(T, w2.shape[0], dtype=torch.bfloat16, device=x.device)
     N.call("xtu_moe_gemv", w13.data_ptr(), N.ptr(s13), w2.data_ptr(), N.ptr(s2), int(s13 is not None), 1, H, I,
-           x.data_ptr(), 0, st["seg"].data_ptr(), st["slot"].data_ptr(), st["w"].data_ptr(), st["h"].data_ptr(),
-           y.data_ptr(), T, 1, T, st["active"].data_ptr(), float(limit), 1.0, 0.0, _gv_ws(x.device),
+           x.data_ptr(), 0, x.stride(0), None, 0, st["seg"].data_ptr(), st["slot"].data_ptr(), st["w"].data_ptr(), st["h"].data_ptr(),
+           y.data_ptr(), T, 1, T, st["active"].data_ptr(), 1, float(limit), 1.0, 0.0, _gv_ws(x.device),
            N.status_buffer(x.device).data_ptr(), N.stream_ptr(x.device))
     return y
 
