@@ -30,6 +30,7 @@
 #include <cstdint>
 #include <cfloat>
 #include "ptx.cuh"
+#include "launch.cuh"
 
 namespace xtu {
 namespace {
@@ -105,6 +106,8 @@ template <int D, int MT>
 __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(const __grid_constant__ CUtensorMap tk,
                                                                  const __grid_constant__ CUtensorMap tv,
                                                                  const __grid_constant__ AdParams p) {
+  griddep_wait();   // launched with PDL: nothing upstream is touched before this
+  griddep_launch_dependents();
   using C = AdCfg<D>;
   constexpr int STAGES = C::STAGES;
   constexpr int NS = AD_CWARPS / MT;   // key subsets per page
@@ -430,7 +433,7 @@ static int ad_launch(const CUtensorMap& tk, const CUtensorMap& tv, const AdParam
     if (e != cudaSuccess) return -(int)e;
     init = true;
   }
-  attn_decode_kernel<D, MT><<<dim3(p.splits, p.Hkv, B), AD_THREADS, C::BYTES, s>>>(tk, tv, p);
+  launch_pdl(attn_decode_kernel<D, MT>, dim3(p.splits, p.Hkv, B), dim3(AD_THREADS), C::BYTES, s, tk, tv, p);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 1 : -(int)e;
 }

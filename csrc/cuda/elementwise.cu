@@ -17,6 +17,7 @@
 #include <cstdint>
 #include <cfloat>
 #include "ptx.cuh"
+#include "launch.cuh"
 #include "xtu_argmax_static.h"
 #include <mutex>
 
@@ -60,6 +61,8 @@ __global__ void __launch_bounds__(NT) rmsnorm_kernel(const __nv_bfloat16* __rest
                                                      const __nv_bfloat16* __restrict__ w,
                                                      __nv_bfloat16* __restrict__ y, int H, float eps, int add_one,
                                                      int x_stride, int y_stride) {
+  griddep_wait();   // launched with PDL: nothing upstream is touched before this
+  griddep_launch_dependents();
   extern __shared__ float row[];  // H floats
   __shared__ float sh[32];
   const int t = blockIdx.x;
@@ -122,6 +125,8 @@ __global__ void rope_kv_kernel(__nv_bfloat16* __restrict__ q, __nv_bfloat16* __r
                                float norm_eps, int norm_add_one, const int* __restrict__ slot_mapping,
                                __nv_bfloat16* __restrict__ k_cache, __nv_bfloat16* __restrict__ v_cache,
                                int block_size) {
+  griddep_wait();   // launched with PDL: nothing upstream is touched before this
+  griddep_launch_dependents();
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   const int H = Hq + Hk;
@@ -207,6 +212,8 @@ template <int PER>
 __global__ void router_topk_kernel(const float* __restrict__ logits, const float* __restrict__ bias, int T, int E,
                                    int K, int scoring, int n_group, int topk_group, int renorm, float scale,
                                    int* __restrict__ out_ids, float* __restrict__ out_w, int logits_stride) {
+  griddep_wait();   // launched with PDL: nothing upstream is touched before this
+  griddep_launch_dependents();
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (gw >= T) return;
@@ -411,6 +418,8 @@ __global__ void __launch_bounds__(512) moe_permute_decode_kernel(const int* __re
                                                                  int* __restrict__ perm_slot,
                                                                  float* __restrict__ perm_w, int* __restrict__ active,
                                                                  int* __restrict__ tokrow) {
+  griddep_wait();   // launched with PDL: nothing upstream is touched before this
+  griddep_launch_dependents();
   __shared__ int cnt[1024], cur[1024], apos[1024];
   __shared__ int wc[16], wa[16], nact;
   const int E = hi - lo, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -490,6 +499,8 @@ __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ slots, cons
                                    int K, int H, int lo, int hi, const __nv_bfloat16* __restrict__ shared,
                                    const float* __restrict__ extra, __nv_bfloat16* __restrict__ out,
                                    float* __restrict__ out_f32) {
+  griddep_wait();   // launched with PDL: nothing upstream is touched before this
+  griddep_launch_dependents();
   const int t = blockIdx.x;
   // grid.y splits the hidden dimension so that decode-sized T still fills the GPU
   const int span = (H / 8 + gridDim.y - 1) / gridDim.y * 8;
@@ -683,9 +694,9 @@ int xtu_rmsnorm(const void* x, const void* residual, void* residual_out, const v
   if (sm > 48 * 1024) {
     cudaFuncSetAttribute(rmsnorm_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
   }
-  rmsnorm_kernel<256><<<T, 256, sm, s>>>((const __nv_bfloat16*)x, (const __nv_bfloat16*)residual,
-                                         (__nv_bfloat16*)residual_out, (const __nv_bfloat16*)w, (__nv_bfloat16*)y, H,
-                                         eps, add_one, x_stride, y_stride);
+  launch_pdl(rmsnorm_kernel<256>, dim3(T), dim3(256), sm, s, (const __nv_bfloat16*)x,
+             (const __nv_bfloat16*)residual, (__nv_bfloat16*)residual_out, (const __nv_bfloat16*)w,
+             (__nv_bfloat16*)y, H, eps, add_one, x_stride, y_stride);
   return rc_last();
 }
 
@@ -698,11 +709,10 @@ int xtu_rope_kv(void* q, void* k, const void* v, const int* positions, const flo
   const int warps = T * (Hq + Hk);
   const int threads = 256;
   const int blocks = (warps * 32 + threads - 1) / threads;
-  rope_kv_kernel<<<blocks, threads, 0, s>>>((__nv_bfloat16*)q, (__nv_bfloat16*)k, (const __nv_bfloat16*)v, positions,
-                                            cos_sin, T, Hq, Hk, D, Dv, rot, neox, q_stride, k_stride, v_stride,
-                                            (const __nv_bfloat16*)q_norm_w, (const __nv_bfloat16*)k_norm_w, norm_eps,
-                                            norm_add_one, slot_mapping, (__nv_bfloat16*)k_cache,
-                                            (__nv_bfloat16*)v_cache, block_size);
+  launch_pdl(rope_kv_kernel, dim3(blocks), dim3(threads), 0, s, (__nv_bfloat16*)q, (__nv_bfloat16*)k,
+             (const __nv_bfloat16*)v, positions, cos_sin, T, Hq, Hk, D, Dv, rot, neox, q_stride, k_stride, v_stride,
+             (const __nv_bfloat16*)q_norm_w, (const __nv_bfloat16*)k_norm_w, norm_eps, norm_add_one, slot_mapping,
+             (__nv_bfloat16*)k_cache, (__nv_bfloat16*)v_cache, block_size);
   return rc_last();
 }
 
@@ -724,8 +734,8 @@ int xtu_router_topk(const float* logits, const float* bias, int T, int E, int K,
   if (E > 1024 || K > 32 || n_group > 64) return -2;
   const int per = (E + 31) / 32;
 #define XTU_TOPK(P)                                                                                          \
-  router_topk_kernel<P><<<(T * 32 + 255) / 256, 256, 0, s>>>(logits, bias, T, E, K, scoring, n_group, topk_group, \
-                                                             renorm, scale, out_ids, out_w, logits_stride)
+  launch_pdl(router_topk_kernel<P>, dim3((T * 32 + 255) / 256), dim3(256), 0, s, logits, bias, T, E, K, scoring,  \
+             n_group, topk_group, renorm, scale, out_ids, out_w, logits_stride)
   if (per <= 1) XTU_TOPK(1);
   else if (per <= 2) XTU_TOPK(2);
   else if (per <= 4) XTU_TOPK(4);
@@ -764,7 +774,8 @@ int xtu_moe_permute_decode(const int* ids, const float* weights, int T, int K, i
                            int* perm_slot, float* perm_w, int* active, int* tokrow, cudaStream_t s) {
   const int E = hi - lo;
   if (E <= 0 || E > 1024 || (tokrow && T > 16)) return -2;
-  moe_permute_decode_kernel<<<1, 512, 0, s>>>(ids, weights, T * K, K, lo, hi, seg, perm_slot, perm_w, active, tokrow);
+  launch_pdl(moe_permute_decode_kernel, dim3(1), dim3(512), 0, s, ids, weights, T * K, K, lo, hi, seg, perm_slot,
+             perm_w, active, tokrow);
   return rc_last();
 }
 
@@ -776,8 +787,8 @@ int xtu_moe_combine(const void* slots, const int* ids, int T, int K, int H, int 
   int ysplit = (H / 8 + threads - 1) / threads;          // one 8-wide vector per thread
   if (T * ysplit > 2048) ysplit = (2048 + T - 1) / T;
   if (ysplit < 1) ysplit = 1;
-  moe_combine_kernel<<<dim3(T, ysplit), threads, 0, s>>>((const __nv_bfloat16*)slots, ids, T, K, H, lo, hi,
-                                           (const __nv_bfloat16*)shared, extra, (__nv_bfloat16*)out, out_f32);
+  launch_pdl(moe_combine_kernel, dim3(T, ysplit), dim3(threads), 0, s, (const __nv_bfloat16*)slots, ids, T, K, H, lo,
+             hi, (const __nv_bfloat16*)shared, extra, (__nv_bfloat16*)out, out_f32);
   return rc_last();
 }
 

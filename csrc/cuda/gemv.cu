@@ -46,6 +46,7 @@
 #include <cuda_runtime.h>
 #include <cstdint>
 #include "ptx.cuh"
+#include "launch.cuh"
 
 namespace xtu {
 
@@ -103,7 +104,7 @@ struct GvCfg {
 // stages [s_begin, s_end) and multiply by activations x (rows x_row0 .. x_row0 + mcount).
 // Producer: warp 0.  Consumers: warps 1..4, each with acc[tile][nt][4] for its k slices.
 // Returns false (all threads) if a wait timed out.
-template <bool FP8, int NT>
+template <bool FP8, int NT, int WMODE>
 __device__ __forceinline__ bool gv_stream_tile(const CUtensorMap* tmap, const CUtensorMap* xmap, uint8_t* stages,
                                                uint64_t* full, uint64_t* empty, float* sc_sm, uint32_t& phase_base,
                                                const int (&row0)[2], int s_begin, int s_end, int K,
@@ -135,15 +136,21 @@ __device__ __forceinline__ bool gv_stream_tile(const CUtensorMap* tmap, const CU
         ++issued;
         mbar_arrive_expect_tx(&full[slot], GV_STAGE_BYTES);
         uint8_t* dst = stages + slot * GV_STAGE_BYTES;
-        const int kb = (s_begin + i) * KSTAGE;   // first k (elements) of the stage
+        // one box for the stage's 32 weight rows x 256 bytes (two 128-byte column chunks;
+        // WMODE 1: two 16-row halves 128 rows apart) and one for its activations
+        const int s_abs = s_begin + i;
+        if (WMODE == 0) {
+          tma_load_3d(dst, tmap, &full[slot], 0, row0[0], 2 * s_abs);
+        } else if (WMODE == 1) {
+          tma_load_4d(dst, tmap, &full[slot], 0, row0[0], 0, 2 * s_abs);
+        } else {   // rows whose byte length is not a multiple of 128: four 2-D boxes
 #pragma unroll
-        for (int b = 0; b < 2; ++b)
+          for (int b = 0; b < 2; ++b)
 #pragma unroll
-          for (int h = 0; h < 2; ++h)
-            tma_load_2d(dst + b * 4096 + h * 2048, tmap, &full[slot], kb + b * (KSTAGE / 2), row0[h]);
-#pragma unroll
-        for (int xb = 0; xb < C::XBOXES; ++xb)
-          tma_load_2d(dst + GV_W_BYTES + xb * (C::XROWS * 128), xmap, &full[slot], kb + xb * 64, x_row0);
+            for (int h = 0; h < 2; ++h)
+              tma_load_2d(dst + b * 4096 + h * 2048, tmap, &full[slot], s_abs * KSTAGE + b * (KSTAGE / 2), row0[h]);
+        }
+        tma_load_3d(dst + GV_W_BYTES, xmap, &full[slot], 0, x_row0, s_abs * C::XBOXES);
       }
       if (!ok) {   // give the copies already issued (bounded) time to land before the CTA exits
         for (int j = issued > GV_STAGES ? issued - GV_STAGES : 0; j < issued; ++j) {
@@ -305,12 +312,14 @@ __device__ __forceinline__ uint8_t* gv_setup(uint64_t*& full, uint64_t*& empty, 
 // ---------------------------------------------------------------------------
 // dense: y[M, N] = x[M, K] W^T (+ bias); grid (32-row tiles, K splits)
 // ---------------------------------------------------------------------------
-template <bool FP8, int NT>
+template <bool FP8, int NT, int WM>
 __global__ void __launch_bounds__(GV_THREADS) gemv_dense_kernel(
     const __grid_constant__ CUtensorMap tmap, const __grid_constant__ CUtensorMap xmap,
     const float* __restrict__ wscale, int N, int K, int M, const __nv_bfloat16* __restrict__ bias,
     void* __restrict__ y, int y_stride, int y_f32, float* __restrict__ ws, int* __restrict__ counters,
     XtuStatus* st) {
+  griddep_wait();   // launched with PDL: nothing upstream is touched before this
+  griddep_launch_dependents();
   uint64_t *full, *empty;
   float *red, *sc_sm;
   uint8_t* stages = gv_setup<FP8, NT>(full, empty, red, sc_sm);
@@ -330,7 +339,7 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_dense_kernel(
   const int rows[2] = {r0, r0 + 16};
   uint32_t pb = 0;
   float acc[2][NT][4];
-  if (!gv_stream_tile<FP8, NT>(&tmap, &xmap, stages, full, empty, sc_sm, pb, rows, s0, s1, K, wscale, sk,
+  if (!gv_stream_tile<FP8, NT, WM>(&tmap, &xmap, stages, full, empty, sc_sm, pb, rows, s0, s1, K, wscale, sk,
                                min(r0, N - 1) >> 7, min(r0 + 16, N - 1) >> 7, 0, M, acc, st))
     return;
   gv_reduce<NT>(acc, red);
@@ -415,6 +424,8 @@ __global__ void __launch_bounds__(GV_THREADS) moe_gemv_gate_up_kernel(
     const float* __restrict__ wscale, int I, int K, const int* __restrict__ seg, const int* __restrict__ active,
     const int* __restrict__ tokrow, int ntok, __nv_bfloat16* __restrict__ h, float limit, float alpha, float beta,
     XtuStatus* st) {
+  griddep_wait();   // launched with PDL: nothing upstream is touched before this
+  griddep_launch_dependents();
   if ((int)blockIdx.y >= active[0]) return;
   const int e = active[1 + blockIdx.y];
   const int s0 = seg[e], cnt = seg[e + 1] - s0;
@@ -439,7 +450,7 @@ __global__ void __launch_bounds__(GV_THREADS) moe_gemv_gate_up_kernel(
   for (int mb = 0; mb < xcnt; mb += 8 * NT) {
     const int mc = min(8 * NT, xcnt - mb);
     float acc[2][NT][4];
-    if (!gv_stream_tile<FP8, NT>(&tmap, &xmap, stages, full, empty, sc_sm, pb, rows, 0, nstages, K, esc, sk,
+    if (!gv_stream_tile<FP8, NT, 1>(&tmap, &xmap, stages, full, empty, sc_sm, pb, rows, 0, nstages, K, esc, sk,
                                  grow >> 7, (grow + 128) >> 7, xrow0 + mb, mc, acc, st))
       return;
     gv_reduce<NT>(acc, red);
@@ -473,6 +484,8 @@ __global__ void __launch_bounds__(GV_THREADS) moe_gemv_down_kernel(
     const float* __restrict__ wscale, int H, int I, const int* __restrict__ seg, const int* __restrict__ active,
     const int* __restrict__ perm_slot, const float* __restrict__ perm_w, __nv_bfloat16* __restrict__ out,
     XtuStatus* st) {
+  griddep_wait();   // launched with PDL: nothing upstream is touched before this
+  griddep_launch_dependents();
   if ((int)blockIdx.y >= active[0]) return;
   const int e = active[1 + blockIdx.y];
   const int s0 = seg[e], cnt = seg[e + 1] - s0;
@@ -492,7 +505,7 @@ __global__ void __launch_bounds__(GV_THREADS) moe_gemv_down_kernel(
   for (int mb = 0; mb < cnt; mb += 8 * NT) {
     const int mc = min(8 * NT, cnt - mb);
     float acc[2][NT][4];
-    if (!gv_stream_tile<FP8, NT>(&tmap, &xmap, stages, full, empty, sc_sm, pb, rows, 0, nstages, I, esc, sk,
+    if (!gv_stream_tile<FP8, NT, 0>(&tmap, &xmap, stages, full, empty, sc_sm, pb, rows, 0, nstages, I, esc, sk,
                                  min(r0, H - 1) >> 7, min(r0 + 16, H - 1) >> 7, s0 + mb, mc, acc, st))
       return;
     gv_reduce<NT>(acc, red);
@@ -515,6 +528,8 @@ __global__ void __launch_bounds__(GV_THREADS) moe_gemv_down_kernel(
 
 // active[0] = number of experts with rows, active[1..] = those experts in order (one warp)
 __global__ void moe_active_kernel(const int* __restrict__ seg, int E, int* __restrict__ active) {
+  griddep_wait();   // launched with PDL: nothing upstream is touched before this
+  griddep_launch_dependents();
   const int lane = threadIdx.x;
   int n = 0;
   for (int e0 = 0; e0 < E; e0 += 32) {
@@ -536,6 +551,8 @@ constexpr long long GV_WS_X_HALVES = 1 << 19;
 // x [M, K] (row stride `stride`) bf16 -> out [M, K] f16 x 2^-8, one 16-byte chunk per thread
 __global__ void gv_x_f16s_kernel(const __nv_bfloat16* __restrict__ x, int M, int K, int stride,
                                  uint4* __restrict__ out) {
+  griddep_wait();   // launched with PDL: nothing upstream is touched before this
+  griddep_launch_dependents();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   const int per_row = K >> 3;
   if (i >= M * per_row) return;
@@ -562,9 +579,10 @@ typedef CUresult (*PFN_gv_encode)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
-// [rows, K] (fp8 or bf16, row pitch `pitch` elements) -> 2-D map, 128-byte x box_rows swizzled boxes
-static int gv_tmap(CUtensorMap* map, const void* W, uint64_t rows, int K, bool fp8, int box_rows = 16,
-                   int pitch = 0) {
+// Tensor maps with 128-byte swizzle whose ONE box is a whole GEMV stage operand, so a
+// stage costs two TMA instructions (weights, activations) instead of eight small boxes.
+static int gv_tmap_nd(CUtensorMap* map, const void* base, bool u8, int rank, const cuuint64_t* dims,
+                      const cuuint64_t* strides, const cuuint32_t* box) {
   static PFN_gv_encode enc = nullptr;
   if (!enc) {
     void* p = nullptr;
@@ -574,17 +592,51 @@ static int gv_tmap(CUtensorMap* map, const void* W, uint64_t rows, int K, bool f
       enc = reinterpret_cast<PFN_gv_encode>(p);
     if (!enc) return -100;
   }
-  const int eb = fp8 ? 1 : 2;
-  if (pitch <= 0) pitch = K;
-  if ((reinterpret_cast<uintptr_t>(W) & 15) != 0 || ((uint64_t)pitch * eb) % 16 != 0) return -101;
-  cuuint64_t dims[2] = {(cuuint64_t)K, rows};
-  cuuint64_t strides[1] = {(cuuint64_t)pitch * eb};
-  cuuint32_t box[2] = {(cuuint32_t)(128 / eb), (cuuint32_t)box_rows};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(map, fp8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
-                   const_cast<void*>(W), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) return -101;
+  for (int i = 0; i < rank - 1; ++i)
+    if (strides[i] % 16 != 0) return -101;
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  CUresult r = enc(map, u8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank,
+                   const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? 0 : -1000 - (int)r;
+}
+
+// weights [rows, K] viewed as (128-byte chunk element, row, chunk); one box = 32 rows x 2
+// chunks, landing as [chunk][row][128 B].  halves: (element, row, half, chunk) with the
+// second half 128 rows down (gate / up blocks of W13); box 16 rows x 2 halves x 2 chunks.
+// rows2d: rows whose length is not a multiple of 128 bytes, as 2-D [rows, K] with 16-row boxes.
+static int gv_wmap(CUtensorMap* map, const void* W, uint64_t rows, int K, bool fp8, bool halves) {
+  const uint64_t eb = fp8 ? 1 : 2, rb = (uint64_t)K * eb;
+  if (rb % 128 != 0) {
+    if (halves) return -8;
+    const cuuint64_t dims[2] = {(cuuint64_t)K, rows};
+    const cuuint64_t strides[1] = {rb};
+    const cuuint32_t box[2] = {(cuuint32_t)(128 / eb), 16};
+    return gv_tmap_nd(map, W, fp8, 2, dims, strides, box);
+  }
+  const cuuint32_t c = (cuuint32_t)(128 / eb);
+  if (!halves) {
+    const cuuint64_t dims[3] = {c, rows, rb / 128};
+    const cuuint64_t strides[2] = {rb, 128};
+    const cuuint32_t box[3] = {c, 32, 2};
+    return gv_tmap_nd(map, W, fp8, 3, dims, strides, box);
+  }
+  const cuuint64_t dims[4] = {c, rows, 2, rb / 128};
+  const cuuint64_t strides[3] = {rb, 128 * rb, 128};
+  const cuuint32_t box[4] = {c, 16, 2, 2};
+  return gv_tmap_nd(map, W, fp8, 4, dims, strides, box);
+}
+
+// activations [rows, K] bf16 / f16 (row pitch `pitch` elements) viewed as (element, row,
+// 64-element chunk); one box = xrows rows x the stage's chunks, landing as [chunk][row][128 B]
+static int gv_xmap(CUtensorMap* map, const void* x, uint64_t rows, int K, int pitch, int xrows, bool fp8) {
+  if (K % 64 != 0) return -8;
+  if (pitch <= 0) pitch = K;
+  const cuuint64_t dims[3] = {64, rows, (cuuint64_t)K / 64};
+  const cuuint64_t strides[2] = {(cuuint64_t)pitch * 2, 128};
+  const cuuint32_t box[3] = {64, (cuuint32_t)xrows, (cuuint32_t)(fp8 ? 4 : 2)};
+  return gv_tmap_nd(map, x, false, 3, dims, strides, box);
 }
 
 template <typename Kern>
@@ -612,8 +664,8 @@ static int gv_splits(int tiles, int S, int N, int slots) {
 static const void* gv_convert_x(const void* x, int rows, int K, int stride, float* ws, cudaStream_t s) {
   uint4* x16 = reinterpret_cast<uint4*>(ws + GV_WS_PART_FLOATS);
   const int chunks = rows * (K / 8);
-  gv_x_f16s_kernel<<<(chunks + 255) / 256, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(x), rows, K, stride,
-                                                        x16);
+  launch_pdl(gv_x_f16s_kernel, dim3((chunks + 255) / 256), dim3(256), 0, s, reinterpret_cast<const __nv_bfloat16*>(x),
+             rows, K, stride, x16);
   return x16;
 }
 
@@ -639,29 +691,38 @@ int xtu_gemv(const void* W, const float* wscale, int fp8, int N, int K, const vo
     ++launches;
   }
   CUtensorMap tm, xm;
-  int rc = gv_tmap(&tm, W, (uint64_t)N, K, fp8 != 0);
+  int rc = gv_wmap(&tm, W, (uint64_t)N, K, fp8 != 0, false);
   if (rc) return rc;
-  rc = gv_tmap(&xm, x, (uint64_t)M, K, false, 8 * nt, x_stride);
+  rc = gv_xmap(&xm, x, (uint64_t)M, K, x_stride, 8 * nt, fp8 != 0);
   if (rc) return rc;
   XtuStatus* st = reinterpret_cast<XtuStatus*>(status);
-#define XTU_GEMV_LAUNCH(F, NTV)                                                                              \
+#define XTU_GEMV_LAUNCH(F, NTV, WMV)                                                                         \
   do {                                                                                                       \
     static int occ = 0;                                                                                      \
     if (!occ) {                                                                                              \
-      rc = gv_smem_attr(gemv_dense_kernel<F, NTV>, GvCfg<F, NTV>::BYTES);                                    \
+      rc = gv_smem_attr(gemv_dense_kernel<F, NTV, WMV>, GvCfg<F, NTV>::BYTES);                               \
       if (rc) return rc;                                                                                     \
-      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gemv_dense_kernel<F, NTV>, GV_THREADS,          \
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gemv_dense_kernel<F, NTV, WMV>, GV_THREADS,     \
                                                         GvCfg<F, NTV>::BYTES) != cudaSuccess || occ < 1)      \
         occ = 1;                                                                                             \
     }                                                                                                        \
     const dim3 grid(tiles, gv_splits(tiles, S, N, occ * gemv_num_sms()));                                   \
-    gemv_dense_kernel<F, NTV><<<grid, GV_THREADS, GvCfg<F, NTV>::BYTES, s>>>(                               \
-        tm, xm, wscale, N, K, M, (const __nv_bfloat16*)bias, y, y_stride, y_f32, ws, counters, st);          \
+    launch_pdl(gemv_dense_kernel<F, NTV, WMV>, grid, dim3(GV_THREADS), GvCfg<F, NTV>::BYTES, s, tm, xm, wscale, N, \
+               K, M, (const __nv_bfloat16*)bias, y, y_stride, y_f32, ws, counters, st);                      \
   } while (0)
+  const bool w2d = ((long long)K * (fp8 ? 1 : 2)) % 128 != 0;
   if (fp8) {
-    if (nt == 1) XTU_GEMV_LAUNCH(true, 1); else XTU_GEMV_LAUNCH(true, 2);
+    if (w2d) {
+      if (nt == 1) XTU_GEMV_LAUNCH(true, 1, 2); else XTU_GEMV_LAUNCH(true, 2, 2);
+    } else {
+      if (nt == 1) XTU_GEMV_LAUNCH(true, 1, 0); else XTU_GEMV_LAUNCH(true, 2, 0);
+    }
   } else {
-    if (nt == 1) XTU_GEMV_LAUNCH(false, 1); else XTU_GEMV_LAUNCH(false, 2);
+    if (w2d) {
+      if (nt == 1) XTU_GEMV_LAUNCH(false, 1, 2); else XTU_GEMV_LAUNCH(false, 2, 2);
+    } else {
+      if (nt == 1) XTU_GEMV_LAUNCH(false, 1, 0); else XTU_GEMV_LAUNCH(false, 2, 0);
+    }
   }
 #undef XTU_GEMV_LAUNCH
   cudaError_t e = cudaGetLastError();
@@ -698,15 +759,15 @@ int xtu_moe_gemv(const void* W13, const float* s13, const void* W2, const float*
     ++launches;
   }
   CUtensorMap t13, t2, xm, hm;
-  int rc = gv_tmap(&t13, W13, (uint64_t)E * 2 * I, H, fp8 != 0);
+  int rc = gv_wmap(&t13, W13, (uint64_t)E * 2 * I, H, fp8 != 0, true);
   if (rc) return rc;
-  rc = gv_tmap(&t2, W2, (uint64_t)E * H, I, fp8 != 0);
+  rc = gv_wmap(&t2, W2, (uint64_t)E * H, I, fp8 != 0, false);
   if (rc) return rc;
-  rc = gv_tmap(&xm, xp, (uint64_t)x_rows, H, false, 8 * nt, x_stride);
+  rc = gv_xmap(&xm, xp, (uint64_t)x_rows, H, x_stride, 8 * nt, fp8 != 0);
   if (rc) return rc;
-  rc = gv_tmap(&hm, h, (uint64_t)n_rows, I, false, 8 * nt);
+  rc = gv_xmap(&hm, h, (uint64_t)n_rows, I, I, 8 * nt, fp8 != 0);
   if (rc) return rc;
-  if (!active_ready) moe_active_kernel<<<1, 32, 0, s>>>(seg, E, active);
+  if (!active_ready) launch_pdl(moe_active_kernel, dim3(1), dim3(32), 0, s, seg, E, active);
   else --launches;
   XtuStatus* st = reinterpret_cast<XtuStatus*>(status);
   const dim3 g1(I / 16, max_active), g2((H + 31) / 32, max_active);
@@ -719,10 +780,10 @@ int xtu_moe_gemv(const void* W13, const float* s13, const void* W2, const float*
       if (rc) return rc;                                                                                     \
       init = true;                                                                                           \
     }                                                                                                        \
-    moe_gemv_gate_up_kernel<F, NTV><<<g1, GV_THREADS, GvCfg<F, NTV>::BYTES, s>>>(                           \
-        t13, xm, s13, I, H, seg, active, tokrow, ntok, (__nv_bfloat16*)h, limit, alpha, beta, st);          \
-    moe_gemv_down_kernel<F, NTV><<<g2, GV_THREADS, GvCfg<F, NTV>::BYTES, s>>>(                              \
-        t2, hm, s2, H, I, seg, active, perm_slot, perm_w, (__nv_bfloat16*)slots, st);                        \
+    launch_pdl(moe_gemv_gate_up_kernel<F, NTV>, g1, dim3(GV_THREADS), GvCfg<F, NTV>::BYTES, s, t13, xm, s13, I, \
+               H, seg, active, tokrow, ntok, (__nv_bfloat16*)h, limit, alpha, beta, st);                     \
+    launch_pdl(moe_gemv_down_kernel<F, NTV>, g2, dim3(GV_THREADS), GvCfg<F, NTV>::BYTES, s, t2, hm, s2, H, I,    \
+               seg, active, perm_slot, perm_w, (__nv_bfloat16*)slots, st);                                   \
   } while (0)
   if (fp8) {
     if (nt == 1) XTU_MOE_GEMV_LAUNCH(true, 1); else XTU_MOE_GEMV_LAUNCH(true, 2);

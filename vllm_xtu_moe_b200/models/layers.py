@@ -109,7 +109,8 @@ class DenseMLP:
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         T = x.shape[0]
-        if x.is_cuda and self.interleaved and T <= G.GEMV_MAX_M:
+        if (x.is_cuda and self.interleaved and T <= G.GEMV_MAX_M and x.shape[1] % 128 == 0
+                and self.down.weight.shape[1] % 128 == 0):
             return M.dense_swiglu_gemv(x.contiguous(), self.gate_up.weight, self.gate_up.scale, self.down.weight,
                                        self.down.scale, self.limit, self._seg)
         if x.is_cuda and self.interleaved:

@@ -124,7 +124,7 @@ def linear(x: torch.Tensor, weight: torch.Tensor, scale: torch.Tensor | None = N
     if not x2.is_contiguous():
         x2 = x2.contiguous()
     K = x2.shape[1]
-    if x2.is_cuda and x2.shape[0] <= GEMV_MAX_M and K % 16 == 0 and x2.dtype == torch.bfloat16:
+    if x2.is_cuda and x2.shape[0] <= GEMV_MAX_M and K % 64 == 0 and x2.dtype == torch.bfloat16:
         y = gemv(x2, weight, scale, bias, out_dtype)
         return y.reshape(*shp[:-1], weight.shape[0])
     if scale is None:

@@ -142,10 +142,11 @@ def moe_experts_partial(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tenso
     s = N.stream_ptr(x.device)
     n = T * K
     fp8 = experts.fmt == "fp8"
+    I = experts.inter
     # decode: weight-streaming grouped GEMV (gate/up + SwiGLU, down + weight + scatter); with
     # fp8 experts it reads the gathered rows as f16 x 2^-8, which the permute writes
-    gemv_path = T <= G.GEMV_MAX_M and experts.interleaved and experts.fmt not in G.FP4_FMTS
-    I = experts.inter
+    gemv_path = (T <= G.GEMV_MAX_M and experts.interleaved and experts.fmt not in G.FP4_FMTS
+                 and H % 128 == 0 and I % 128 == 0)   # whole 128-byte chunks per weight row
     if gemv_path and E <= 1024:
         # one-CTA permute (no row gather): the gate/up GEMV reads the T tokens directly
         # and keeps each expert's own columns through ws.tokrow
