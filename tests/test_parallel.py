@@ -244,3 +244,63 @@ def _tp_gpu_worker(rank, world, port):
 def test_tensor_parallel_p2p_matches_single_gpu():
     _need_two_gpus()
     mp.spawn(_tp_gpu_worker, args=(2, _port()), nprocs=2)
+
+
+# ----------------------------------------------------------------------------- pipeline parallel
+def _pp_worker(rank, world, port, name, backend):
+    from vllm_xtu_moe_b200.engine import LLM, SamplingParams
+    from vllm_xtu_moe_b200.engine.runner import RunnerConfig
+    from vllm_xtu_moe_b200.models.model import build_model
+    from vllm_xtu_moe_b200.ops import _native as N
+    from vllm_xtu_moe_b200.parallel.pp import PipelineStage, stage_bounds
+    _init(rank, world, port, backend)
+    gpu = backend == "nccl"
+    dev = f"cuda:{rank}" if gpu else "cpu"
+    cfg = _tp_cfg(name).replace(num_layers=5)
+    if gpu:
+        cfg = cfg.replace(hidden_size=512, num_heads=8, dense_fmt="fp8", expert_fmt="fp8")
+    full = build_model(cfg, device=dev, seed=4)
+    if not gpu:
+        full.act_dtype = torch.float32
+    stage = PipelineStage(full, rank, world)
+    assert (stage.lo, stage.hi) == stage_bounds(5, world, rank) and len(stage.layers) == stage.hi - stage.lo
+    bs = 64 if gpu else 16
+
+    def rc():
+        return RunnerConfig(block_size=bs, max_seqs=2, max_model_len=256, max_batched_tokens=128,
+                            use_cuda_graph=False)
+    prompts = [[3, 4, 5, 6, 7, 8, 9], list(range(20, 45))]
+    sp = SamplingParams(max_tokens=4)
+    got = [r.token_ids for r in LLM(stage, device=dev, runner_config=rc()).generate(prompts, sp)]
+    ref = [r.token_ids for r in LLM(full, device=dev, runner_config=rc()).generate(prompts, sp)]
+    assert got == ref, (rank, got, ref)   # the same kernels on the same rows: identical tokens
+
+    # micro-batches: a batch through the stages with non-blocking sends, vs one local pass
+    llm = LLM(full, device=dev, runner_config=rc())
+    caches_ref = llm.runner.caches
+    st_caches = stage.allocate_caches(llm.runner.rc.num_blocks, bs, 2)
+    batches = []
+    for p in prompts:
+        llm.add_request(p, SamplingParams(max_tokens=1))
+    plan = llm.scheduler.schedule()
+    ids, meta = llm.runner.build_meta(plan)
+    batches.append((ids, meta))
+    outs = stage.forward_microbatches(batches, st_caches)
+    if stage.last:
+        ref_h = full.forward(ids, meta, caches_ref)
+        assert torch.equal(outs[0], ref_h)
+    if gpu:
+        torch.cuda.synchronize()
+        N.check_status(torch.device(dev))
+    dist.destroy_process_group()
+
+
+def test_pipeline_stages_match_single_rank_cpu():
+    mp.spawn(_pp_worker, args=(3, _port(), "glm-4.5-air", "gloo"), nprocs=3)
+
+
+@pytest.mark.gpu
+@pytest.mark.multigpu
+def test_pipeline_stages_nccl_match_single_gpu():
+    _need_two_gpus()
+    mp.spawn(_pp_worker, args=(2, _port(), "glm-4.5-air", "nccl"), nprocs=2)

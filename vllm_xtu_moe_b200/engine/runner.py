@@ -42,6 +42,9 @@ class ModelRunner:
     def __init__(self, model: MoETransformer, rc: RunnerConfig):
         self.model = model
         self.rc = rc
+        self.pipeline = bool(getattr(model, "is_pipeline_stage", False))
+        if self.pipeline and rc.num_spec > 0:
+            raise ValueError("speculative decoding with pipeline stages is not supported")
         self.device = model.device
         self.cuda = self.device.type == "cuda"
         self.max_blocks_per_seq = (rc.max_model_len + rc.block_size - 1) // rc.block_size + 1
@@ -123,6 +126,8 @@ class ModelRunner:
     # ------------------------------------------------------------------
     @torch.inference_mode()
     def forward(self, ids, meta, logit_rows: torch.Tensor | None):
+        if self.pipeline:   # pipeline stage: tokens come back from the last stage
+            return self.model.sample(ids, meta, self.caches, logit_rows), None, None, None
         h, pre = self.model.forward(ids, meta, self.caches, return_prenorm=True)
         if logit_rows is not None:
             hs = h.index_select(0, logit_rows)
@@ -136,7 +141,7 @@ class ModelRunner:
         ids, meta = self.build_meta(plan)
         if plan.is_decode:
             rows = None  # every row produces logits
-            if self.cuda and self.rc.use_cuda_graph and self.rc.num_spec == 0:
+            if self.cuda and self.rc.use_cuda_graph and self.rc.num_spec == 0 and not self.pipeline:
                 tok = self._decode_graph(ids, meta)
                 return tok, None
             tok, h, pre, _ = self.forward(ids, meta, torch.arange(ids.shape[0], device=self.device))
