@@ -423,17 +423,25 @@ __global__ void __launch_bounds__(GV_THREADS) moe_gemv_gate_up_kernel(
     const __grid_constant__ CUtensorMap tmap, const __grid_constant__ CUtensorMap xmap,
     const float* __restrict__ wscale, int I, int K, const int* __restrict__ seg, const int* __restrict__ active,
     const int* __restrict__ tokrow, int ntok, __nv_bfloat16* __restrict__ h, float limit, float alpha, float beta,
+    const __grid_constant__ CUtensorMap tmap_sh, const float* __restrict__ wscale_sh, int sh_row0, int has_sh,
     XtuStatus* st) {
   griddep_wait();   // launched with PDL: nothing upstream is touched before this
   griddep_launch_dependents();
-  if ((int)blockIdx.y >= active[0]) return;
-  const int e = active[1 + blockIdx.y];
-  const int s0 = seg[e], cnt = seg[e + 1] - s0;
+  // grid rows past the active experts: the shared expert (has_sh), as one more expert
+  // over every token, its h rows at sh_row0 + token; the rest exit
+  const int nact = active[0];
+  const bool sh = has_sh && (int)blockIdx.y == nact;
+  if (!sh && (int)blockIdx.y >= nact) return;
+  const int e = sh ? 0 : active[1 + blockIdx.y];
+  const int s0 = sh ? sh_row0 : seg[e], cnt = sh ? ntok : seg[e + 1] - s0;
   if (cnt <= 0) return;
   // token-direct form: x holds the step's ntok tokens (not gathered per expert); the
   // expert multiplies all of them and keeps the columns of its own tokens (tokrow)
-  const int* trow = tokrow ? tokrow + blockIdx.y * 16 : nullptr;
-  const int xrow0 = trow ? 0 : s0, xcnt = trow ? ntok : cnt;
+  const int* trow = (tokrow && !sh) ? tokrow + blockIdx.y * 16 : nullptr;
+  const bool direct = tokrow != nullptr;
+  const int xrow0 = direct ? 0 : s0, xcnt = direct ? ntok : cnt;
+  const CUtensorMap* wmap = sh ? &tmap_sh : &tmap;
+  wscale = sh ? wscale_sh : wscale;
   uint64_t *full, *empty;
   float *red, *sc_sm;
   uint8_t* stages = gv_setup<FP8, NT>(full, empty, red, sc_sm);
@@ -450,7 +458,7 @@ __global__ void __launch_bounds__(GV_THREADS) moe_gemv_gate_up_kernel(
   for (int mb = 0; mb < xcnt; mb += 8 * NT) {
     const int mc = min(8 * NT, xcnt - mb);
     float acc[2][NT][4];
-    if (!gv_stream_tile<FP8, NT, 1>(&tmap, &xmap, stages, full, empty, sc_sm, pb, rows, 0, nstages, K, esc, sk,
+    if (!gv_stream_tile<FP8, NT, 1>(wmap, &xmap, stages, full, empty, sc_sm, pb, rows, 0, nstages, K, esc, sk,
                                  grow >> 7, (grow + 128) >> 7, xrow0 + mb, mc, acc, st))
       return;
     gv_reduce<NT>(acc, red);
@@ -461,7 +469,7 @@ __global__ void __launch_bounds__(GV_THREADS) moe_gemv_gate_up_kernel(
       for (int i = 0; i < 4; ++i) {
         const int j = j0 + g4 + (i >> 1) * 8;
         const int tok = n * 8 + 2 * tq + (i & 1);
-        const int hr = trow ? (tok < mc ? trow[mb + tok] : -1) : (tok < mc ? s0 + mb + tok : -1);
+        const int hr = tok >= mc ? -1 : trow ? trow[mb + tok] : s0 + mb + tok;
         if (hr >= 0) {
           float g = acc[0][n][i], u = acc[1][n][i];
           if (limit > 0.f) { g = fminf(g, limit); u = fminf(fmaxf(u, -limit), limit); }
@@ -483,13 +491,20 @@ __global__ void __launch_bounds__(GV_THREADS) moe_gemv_down_kernel(
     const __grid_constant__ CUtensorMap tmap, const __grid_constant__ CUtensorMap xmap,
     const float* __restrict__ wscale, int H, int I, const int* __restrict__ seg, const int* __restrict__ active,
     const int* __restrict__ perm_slot, const float* __restrict__ perm_w, __nv_bfloat16* __restrict__ out,
-    XtuStatus* st) {
+    const __grid_constant__ CUtensorMap tmap_sh, const float* __restrict__ wscale_sh, int sh_row0, int sh_out0,
+    int ntok, int has_sh, XtuStatus* st) {
   griddep_wait();   // launched with PDL: nothing upstream is touched before this
   griddep_launch_dependents();
-  if ((int)blockIdx.y >= active[0]) return;
-  const int e = active[1 + blockIdx.y];
-  const int s0 = seg[e], cnt = seg[e + 1] - s0;
+  // the grid row after the active experts is the shared expert (has_sh): h rows
+  // sh_row0 + token, output rows sh_out0 + token with weight 1
+  const int nact = active[0];
+  const bool sh = has_sh && (int)blockIdx.y == nact;
+  if (!sh && (int)blockIdx.y >= nact) return;
+  const int e = sh ? 0 : active[1 + blockIdx.y];
+  const int s0 = sh ? sh_row0 : seg[e], cnt = sh ? ntok : seg[e + 1] - s0;
   if (cnt <= 0) return;
+  const CUtensorMap* wmap = sh ? &tmap_sh : &tmap;
+  wscale = sh ? wscale_sh : wscale;
   uint64_t *full, *empty;
   float *red, *sc_sm;
   uint8_t* stages = gv_setup<FP8, NT>(full, empty, red, sc_sm);
@@ -505,7 +520,7 @@ __global__ void __launch_bounds__(GV_THREADS) moe_gemv_down_kernel(
   for (int mb = 0; mb < cnt; mb += 8 * NT) {
     const int mc = min(8 * NT, cnt - mb);
     float acc[2][NT][4];
-    if (!gv_stream_tile<FP8, NT, 0>(&tmap, &xmap, stages, full, empty, sc_sm, pb, rows, 0, nstages, I, esc, sk,
+    if (!gv_stream_tile<FP8, NT, 0>(wmap, &xmap, stages, full, empty, sc_sm, pb, rows, 0, nstages, I, esc, sk,
                                  min(r0, H - 1) >> 7, min(r0 + 16, H - 1) >> 7, s0 + mb, mc, acc, st))
       return;
     gv_reduce<NT>(acc, red);
@@ -520,7 +535,8 @@ __global__ void __launch_bounds__(GV_THREADS) moe_gemv_down_kernel(
           const int tok = n * 8 + 2 * tq + (i & 1);
           if (row < H && tok < mc) {
             const int pr = s0 + mb + tok;
-            out[(size_t)perm_slot[pr] * H + row] = __float2bfloat16(acc[t][n][i] * perm_w[pr]);
+            if (sh) out[(size_t)(sh_out0 + mb + tok) * H + row] = __float2bfloat16(acc[t][n][i]);
+            else out[(size_t)perm_slot[pr] * H + row] = __float2bfloat16(acc[t][n][i] * perm_w[pr]);
           }
         }
   }
@@ -742,7 +758,8 @@ int xtu_moe_gemv(const void* W13, const float* s13, const void* W2, const float*
                  const void* xp, int xp_f16s, int x_stride, const int* tokrow, int ntok, const int* seg,
                  const int* perm_slot, const float* perm_w, void* h,
                  void* slots, int mmax, int max_active, int n_rows, int* active, int active_ready, float limit,
-                 float alpha, float beta, float* ws, void* status, cudaStream_t s) {
+                 float alpha, float beta, const void* W13s, const float* s13s, const void* W2s, const float* s2s,
+                 int sh_out0, float* ws, void* status, cudaStream_t s) {
   if (mmax <= 0 || n_rows <= 0) return 0;
   if (mmax > 16 || H % 32 != 0 || I % 128 != 0 || active == nullptr) return -2;
   if (H > GV_MAX_KBLK * 128 || I > GV_MAX_KBLK * 128) return -3;
@@ -765,12 +782,22 @@ int xtu_moe_gemv(const void* W13, const float* s13, const void* W2, const float*
   if (rc) return rc;
   rc = gv_xmap(&xm, xp, (uint64_t)x_rows, H, x_stride, 8 * nt, fp8 != 0);
   if (rc) return rc;
-  rc = gv_xmap(&hm, h, (uint64_t)n_rows, I, I, 8 * nt, fp8 != 0);
+  // shared expert (token-direct form only): one more grid row in both launches, its h rows
+  // after the pairs' (n_rows + token), its output rows sh_out0 + token of slots
+  const int has_sh = (W13s != nullptr && W2s != nullptr && tokrow != nullptr) ? 1 : 0;
+  CUtensorMap t13s = t13, t2s = t2;
+  if (has_sh) {
+    rc = gv_wmap(&t13s, W13s, (uint64_t)2 * I, H, fp8 != 0, true);
+    if (rc) return rc;
+    rc = gv_wmap(&t2s, W2s, (uint64_t)H, I, fp8 != 0, false);
+    if (rc) return rc;
+  }
+  rc = gv_xmap(&hm, h, (uint64_t)n_rows + (has_sh ? ntok : 0), I, I, 8 * nt, fp8 != 0);
   if (rc) return rc;
   if (!active_ready) launch_pdl(moe_active_kernel, dim3(1), dim3(32), 0, s, seg, E, active);
   else --launches;
   XtuStatus* st = reinterpret_cast<XtuStatus*>(status);
-  const dim3 g1(I / 16, max_active), g2((H + 31) / 32, max_active);
+  const dim3 g1(I / 16, max_active + has_sh), g2((H + 31) / 32, max_active + has_sh);
 #define XTU_MOE_GEMV_LAUNCH(F, NTV)                                                                          \
   do {                                                                                                       \
     static bool init = false;                                                                                \
@@ -781,9 +808,11 @@ int xtu_moe_gemv(const void* W13, const float* s13, const void* W2, const float*
       init = true;                                                                                           \
     }                                                                                                        \
     launch_pdl(moe_gemv_gate_up_kernel<F, NTV>, g1, dim3(GV_THREADS), GvCfg<F, NTV>::BYTES, s, t13, xm, s13, I, \
-               H, seg, active, tokrow, ntok, (__nv_bfloat16*)h, limit, alpha, beta, st);                     \
+               H, seg, active, tokrow, ntok, (__nv_bfloat16*)h, limit, alpha, beta, t13s, s13s, n_rows, has_sh, \
+               st);                                                                                          \
     launch_pdl(moe_gemv_down_kernel<F, NTV>, g2, dim3(GV_THREADS), GvCfg<F, NTV>::BYTES, s, t2, hm, s2, H, I,    \
-               seg, active, perm_slot, perm_w, (__nv_bfloat16*)slots, st);                                   \
+               seg, active, perm_slot, perm_w, (__nv_bfloat16*)slots, t2s, s2s, n_rows, sh_out0, ntok, has_sh,   \
+               st);                                                                                          \
   } while (0)
   if (fp8) {
     if (nt == 1) XTU_MOE_GEMV_LAUNCH(true, 1); else XTU_MOE_GEMV_LAUNCH(true, 2);

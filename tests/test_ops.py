@@ -128,6 +128,22 @@ def test_fused_moe(fmt, T, E, K, H, I):
     N.check_status()
     ref = M.moe_ref(x, ids, w, ex, act_limit=7.0) + shared.float()
     assert rel_err(y, ref) < 2e-2
+    # shared expert fused into the routed decode GEMV launches (expert 0's weights serve as
+    # the shared MLP) vs the same MLP run on its own and added in the combine
+    if T <= 16 and H % 128 == 0 and I % 128 == 0:
+        from vllm_xtu_moe_b200.models.layers import DenseMLP, Linear
+        mlp = DenseMLP(Linear(ex.w13[0], ex.s13[0] if fmt == "fp8" else None),
+                       Linear(ex.w2[0], ex.s2[0] if fmt == "fp8" else None), interleaved=True, limit=7.0)
+        assert M.shared_fusable(mlp, ex, 7.0)
+        ws = M.MoEWorkspace(T, K, E, H, I, x.device)
+        for _ in range(2):   # repeated calls reuse the workspace rows of the shared expert
+            yf = M.fused_moe(x, ids, w, ex, ws, act_limit=7.0, shared_mlp=mlp)
+            ys = M.fused_moe(x, ids, w, ex, ws, act_limit=7.0, shared=mlp(x))
+            torch.cuda.synchronize()
+            N.check_status()
+            assert rel_err(yf, ys.float()) < 1e-2
+        sh_ref = M.moe_ref(x, torch.zeros_like(ids[:, :1]), torch.ones_like(w[:, :1]), ex, act_limit=7.0)
+        assert rel_err(yf, M.moe_ref(x, ids, w, ex, act_limit=7.0) + sh_ref) < 2e-2
     # tier split: experts [E/2, E) elsewhere -> only [0, E/2) pairs computed here
     half = M.prepare_experts(ex.fmt, *(_slice_raw(ex, fmt, 0, E // 2)))
     y2 = M.fused_moe(x, ids, w, half, lo=0)

@@ -173,6 +173,12 @@ class MoEBlock:
         if self.tracer is not None and self.tracer.routing is not None:
             self.tracer.routing.record(self.trace_idx, ids)
         sh = None
+        if (self.shared is not None and self.shared_gate is None and self.executor is None and x.is_cuda
+                and x.shape[0] <= G.GEMV_MAX_M
+                and M.shared_fusable(self.shared, self.experts, self.cfg.swiglu_limit)):
+            # decode: the shared expert runs inside the routed experts' GEMV launches
+            return M.fused_moe(x, ids, w, self.experts, self.workspace(x), lo=self.expert_lo,
+                               act_limit=self.cfg.swiglu_limit, shared_mlp=self.shared)
         if self.shared is not None:
             sh = self.shared(x)
             if self.shared_gate is not None:

@@ -96,9 +96,10 @@ class MoEWorkspace:
         self.perm_slot = torch.zeros(n, dtype=torch.int32, device=d)
         self.perm_w = torch.zeros(n, dtype=torch.float32, device=d)
         self.xp = torch.empty(n, H, dtype=torch.bfloat16, device=d)
-        self.h = torch.empty(n, I, dtype=torch.bfloat16, device=d)
+        # pair rows, then one row per token for a shared expert fused into the decode GEMV
+        self.h = torch.empty(n + self.max_tokens, I, dtype=torch.bfloat16, device=d)
         self.h13 = None  # unfused gate/up output, allocated on demand
-        self.slots = torch.empty(n, H, dtype=torch.bfloat16, device=d)
+        self.slots = torch.empty(n + self.max_tokens, H, dtype=torch.bfloat16, device=d)
         self.mx = G.max_mtiles(n, E)
         self.tiles = torch.empty(self.mx * 4, dtype=torch.int32, device=d)
         self.active = torch.zeros(E + 1, dtype=torch.int32, device=d)   # decode GEMV: experts with rows
@@ -131,9 +132,13 @@ def moe_ref(x, ids, weights, experts: ExpertWeights, lo=0, hi=None, act_limit=0.
 
 def moe_experts_partial(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, experts: ExpertWeights,
                         ws: MoEWorkspace, *, lo: int = 0, act_limit: float = 0.0, act_alpha: float = 1.0,
-                        act_beta: float = 0.0) -> None:
+                        act_beta: float = 0.0, shared_mlp=None) -> torch.Tensor | None:
     """Expert GEMMs for the pairs whose id is in [lo, lo + E): each such pair's weighted
-    output row lands in ws.slots[pair].  Other pairs are untouched (other tiles / tiers)."""
+    output row lands in ws.slots[pair].  Other pairs are untouched (other tiles / tiers).
+
+    ``shared_mlp`` (a DenseMLP in the experts' layout): on the decode GEMV path it runs in
+    the same launches as one more expert over every token, and its output rows are
+    returned (ws.slots[T*K : T*K + T]); otherwise None is returned and the caller runs it."""
     T, H = x.shape
     K = ids.shape[1]
     E = experts.num_experts
@@ -157,23 +162,23 @@ def moe_experts_partial(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tenso
                experts.w2.data_ptr(), N.ptr(experts.s2 if fp8 else None), int(fp8), E, H, I, xt.data_ptr(), 0,
                xt.stride(0), ws.tokrow.data_ptr(), T, ws.seg.data_ptr(), ws.perm_slot.data_ptr(),
                ws.perm_w.data_ptr(), ws.h.data_ptr(), ws.slots.data_ptr(), T, min(E, T * K), n,
-               ws.active.data_ptr(), 1, float(act_limit), float(act_alpha), float(act_beta), _gv_ws(x.device),
-               N.status_buffer(x.device).data_ptr(), s)
-        return
+               ws.active.data_ptr(), 1, float(act_limit), float(act_alpha), float(act_beta),
+               *_shared_ptrs(shared_mlp), n, _gv_ws(x.device), N.status_buffer(x.device).data_ptr(), s)
+        return ws.slots[n:n + T] if shared_mlp is not None else None
     f16s = int(gemv_path and fp8)
     N.call("xtu_moe_permute", ids.data_ptr(), weights.data_ptr(), T, K, lo, lo + E, ws.counts.data_ptr(),
            ws.seg.data_ptr(), ws.cursor.data_ptr(), ws.perm_slot.data_ptr(), ws.perm_w.data_ptr(), x.data_ptr(), H,
            x.stride(0), ws.xp.data_ptr(), f16s, s)
     if experts.fmt in G.FP4_FMTS:
         _experts_fp4(experts, ws, n, act_limit, act_alpha, act_beta)
-        return
+        return None
     if gemv_path:
         N.call("xtu_moe_gemv", experts.w13.data_ptr(), N.ptr(experts.s13 if fp8 else None),
                experts.w2.data_ptr(), N.ptr(experts.s2 if fp8 else None), int(fp8), E, H, I, ws.xp.data_ptr(), f16s,
                H, None, 0, ws.seg.data_ptr(), ws.perm_slot.data_ptr(), ws.perm_w.data_ptr(), ws.h.data_ptr(),
                ws.slots.data_ptr(), T, min(E, T * K), n, ws.active.data_ptr(), 0, float(act_limit), float(act_alpha),
-               float(act_beta), _gv_ws(x.device), N.status_buffer(x.device).data_ptr(), s)
-        return
+               float(act_beta), None, None, None, None, 0, _gv_ws(x.device), N.status_buffer(x.device).data_ptr(), s)
+        return None
     # the segment table of this call has E + 1 entries (the workspace may serve more experts)
     tiles = G.build_mtiles(ws.seg[: E + 1], n, ws.tiles, ws.ntiles)
     xp = ws.xp[:n]
@@ -190,6 +195,7 @@ def moe_experts_partial(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tenso
                ws.h.data_ptr(), s)
     G.grouped_gemm(ws.h[:n], experts.w2, ws.seg, w_scale=sc2, epilogue=G.EPI_BF16, out=ws.slots[:n],
                    row_scale=ws.perm_w, row_dest=ws.perm_slot, tiles=tiles)
+    return None
 
 
 def _experts_fp4(experts: ExpertWeights, ws: MoEWorkspace, n: int, act_limit, act_alpha, act_beta) -> None:
@@ -217,7 +223,7 @@ def moe_combine(ws: MoEWorkspace, ids: torch.Tensor, lo: int, hi: int, *, shared
 def fused_moe(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, experts: ExpertWeights,
               ws: MoEWorkspace | None = None, *, lo: int = 0, shared: torch.Tensor | None = None,
               extra: torch.Tensor | None = None, act_limit: float = 0.0, act_alpha: float = 1.0,
-              act_beta: float = 0.0, out: torch.Tensor | None = None) -> torch.Tensor:
+              act_beta: float = 0.0, out: torch.Tensor | None = None, shared_mlp=None) -> torch.Tensor:
     """Routed-expert MoE over the local experts [lo, lo+E).
 
     x [T, H] bf16, ids/weights [T, K]; shared [T, H] (shared-expert output) and
@@ -238,8 +244,12 @@ def fused_moe(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, experts
     if ws is None or ws.max_tokens < T:
         ws = MoEWorkspace(T, K, E, H, experts.inter, x.device)
     assert x.is_contiguous() and ids.is_contiguous() and weights.is_contiguous()
-    moe_experts_partial(x, ids, weights, experts, ws, lo=lo, act_limit=act_limit, act_alpha=act_alpha,
-                        act_beta=act_beta)
+    fused_sh = moe_experts_partial(x, ids, weights, experts, ws, lo=lo, act_limit=act_limit, act_alpha=act_alpha,
+                                   act_beta=act_beta, shared_mlp=shared_mlp)
+    if shared_mlp is not None and fused_sh is None:   # not the decode GEMV path: run it on its own
+        fused_sh = shared_mlp(x)
+    if fused_sh is not None:
+        shared = fused_sh if shared is None else shared + fused_sh
     return moe_combine(ws, ids, lo, lo + E, shared=shared, extra=extra, out=out)
 
 
@@ -249,6 +259,28 @@ def route_split(ids: torch.Tensor, slotmap: torch.Tensor, lo: int, gpu_ids: torc
     n = ids.numel()
     N.call("xtu_route_split", ids.data_ptr(), n, lo, slotmap.numel(), slotmap.data_ptr(), gpu_ids.data_ptr(),
            cpu_ids.data_ptr(), N.ptr(hits), N.stream_ptr(ids.device))
+
+
+def shared_fusable(shared_mlp, experts: ExpertWeights, act_limit: float = 0.0, act_alpha: float = 1.0,
+                   act_beta: float = 0.0) -> bool:
+    """Whether a DenseMLP shared expert can ride in the routed decode GEMV launches: same
+    weight format, width and activation as the experts, gate/up interleaved in 128-row blocks."""
+    if act_alpha != 1.0 or act_beta != 0.0 or getattr(shared_mlp, "limit", None) != act_limit:
+        return False
+    if shared_mlp is None or experts is None or not getattr(shared_mlp, "interleaved", False):
+        return False
+    fp8 = experts.fmt == "fp8"
+    if experts.fmt not in ("fp8", "bf16") or (shared_mlp.gate_up.scale is not None) != fp8:
+        return False
+    return (shared_mlp.gate_up.weight.dtype == experts.w13.dtype and shared_mlp.down.weight.shape[1] == experts.inter
+            and shared_mlp.gate_up.weight.shape[0] == 2 * experts.inter)
+
+
+def _shared_ptrs(shared_mlp):
+    if shared_mlp is None:
+        return None, None, None, None
+    return (shared_mlp.gate_up.weight.data_ptr(), N.ptr(shared_mlp.gate_up.scale), shared_mlp.down.weight.data_ptr(),
+            N.ptr(shared_mlp.down.scale))
 
 
 def _gv_ws(device):
@@ -274,7 +306,8 @@ def dense_swiglu_gemv(x: torch.Tensor, w13: torch.Tensor, s13, w2: torch.Tensor,
     y = torch.empty(T, w2.shape[0], dtype=torch.bfloat16, device=x.device)
     N.call("xtu_moe_gemv", w13.data_ptr(), N.ptr(s13), w2.data_ptr(), N.ptr(s2), int(s13 is not None), 1, H, I,
            x.data_ptr(), 0, x.stride(0), None, 0, st["seg"].data_ptr(), st["slot"].data_ptr(), st["w"].data_ptr(), st["h"].data_ptr(),
-           y.data_ptr(), T, 1, T, st["active"].data_ptr(), 1, float(limit), 1.0, 0.0, _gv_ws(x.device),
+           y.data_ptr(), T, 1, T, st["active"].data_ptr(), 1, float(limit), 1.0, 0.0, None, None, None, None, 0,
+           _gv_ws(x.device),
            N.status_buffer(x.device).data_ptr(), N.stream_ptr(x.device))
     return y
 
