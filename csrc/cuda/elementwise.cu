@@ -208,16 +208,14 @@ __global__ void kv_write_kernel(const __nv_bfloat16* __restrict__ k, const __nv_
 // n_group > 1: group score = sum of the top-2 biased scores of the group;
 // keep the best topk_group groups (DeepSeek-V3 "noaux_tc").
 // ---------------------------------------------------------------------------
+// One warp: token gw's scores -> its K expert ids / weights (out_ids / out_w rows gw).
+// gscore: 64 floats of shared memory private to the warp (group scores).
 template <int PER>
-__global__ void router_topk_kernel(const float* __restrict__ logits, const float* __restrict__ bias, int T, int E,
-                                   int K, int scoring, int n_group, int topk_group, int renorm, float scale,
-                                   int* __restrict__ out_ids, float* __restrict__ out_w, int logits_stride) {
-  griddep_wait();   // launched with PDL: nothing upstream is touched before this
-  griddep_launch_dependents();
-  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+__device__ __forceinline__ void router_topk_warp(const float* __restrict__ lg, const float* __restrict__ bias,
+                                                 int gw, int E, int K, int scoring, int n_group, int topk_group,
+                                                 int renorm, float scale, int* __restrict__ out_ids,
+                                                 float* __restrict__ out_w, float* gscore) {
   const int lane = threadIdx.x & 31;
-  if (gw >= T) return;
-  const float* lg = logits + (size_t)gw * logits_stride;
   float sc[PER], sel[PER];   // PER = compile-time scores per lane, so these stay in registers
   float mx = -FLT_MAX;
   #pragma unroll
@@ -258,8 +256,6 @@ __global__ void router_topk_kernel(const float* __restrict__ logits, const float
   if (n_group > 1 && topk_group < n_group) {
     // group g covers experts [g*gs, (g+1)*gs); experts of lane l, slot j: e = l + 32 j
     const int gs = E / n_group;
-    __shared__ float gscore_sh[8][64];
-    float* gscore = gscore_sh[(threadIdx.x >> 5) & 7];
     for (int g = 0; g < n_group; ++g) {
       // top-2 within group g
       float b1 = -FLT_MAX, b2 = -FLT_MAX;
@@ -327,6 +323,19 @@ __global__ void router_topk_kernel(const float* __restrict__ logits, const float
     out_ids[(size_t)gw * K + lane] = myid;
     out_w[(size_t)gw * K + lane] = w * scale;
   }
+}
+
+template <int PER>
+__global__ void router_topk_kernel(const float* __restrict__ logits, const float* __restrict__ bias, int T, int E,
+                                   int K, int scoring, int n_group, int topk_group, int renorm, float scale,
+                                   int* __restrict__ out_ids, float* __restrict__ out_w, int logits_stride) {
+  griddep_wait();   // launched with PDL: nothing upstream is touched before this
+  griddep_launch_dependents();
+  __shared__ float gscore_sh[8][64];
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (gw >= T) return;
+  router_topk_warp<PER>(logits + (size_t)gw * logits_stride, bias, gw, E, K, scoring, n_group, topk_group, renorm,
+                        scale, out_ids, out_w, gscore_sh[(threadIdx.x >> 5) & 7]);
 }
 
 // ---------------------------------------------------------------------------
@@ -412,14 +421,11 @@ __global__ void moe_scatter_gather_kernel(const int* __restrict__ ids, const flo
 // gate/up GEMV the map tokrow[a * 16 + t] = row of token t's pair with active expert a
 // (-1 if none; t < 16).  Rows within an expert follow arrival order (atomics); each row's
 // result is computed independently, so the order does not change any value.
-__global__ void __launch_bounds__(512) moe_permute_decode_kernel(const int* __restrict__ ids,
-                                                                 const float* __restrict__ weights, int n, int K,
-                                                                 int lo, int hi, int* __restrict__ seg,
-                                                                 int* __restrict__ perm_slot,
-                                                                 float* __restrict__ perm_w, int* __restrict__ active,
-                                                                 int* __restrict__ tokrow) {
-  griddep_wait();   // launched with PDL: nothing upstream is touched before this
-  griddep_launch_dependents();
+// the body, for a block of exactly 512 threads (also the tail of the fused decode router)
+__device__ __forceinline__ void permute_decode_block(const int* __restrict__ ids, const float* __restrict__ weights,
+                                                     int n, int K, int lo, int hi, int* __restrict__ seg,
+                                                     int* __restrict__ perm_slot, float* __restrict__ perm_w,
+                                                     int* __restrict__ active, int* __restrict__ tokrow) {
   __shared__ int cnt[1024], cur[1024], apos[1024];
   __shared__ int wc[16], wa[16], nact;
   const int E = hi - lo, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -492,6 +498,83 @@ __global__ void __launch_bounds__(512) moe_permute_decode_kernel(const int* __re
     perm_w[row] = weights ? weights[p] : 1.f;
     if (tokrow) tokrow[apos[id - lo] * 16 + p / K] = row;
   }
+}
+
+__global__ void __launch_bounds__(512) moe_permute_decode_kernel(const int* __restrict__ ids,
+                                                                 const float* __restrict__ weights, int n, int K,
+                                                                 int lo, int hi, int* __restrict__ seg,
+                                                                 int* __restrict__ perm_slot,
+                                                                 float* __restrict__ perm_w, int* __restrict__ active,
+                                                                 int* __restrict__ tokrow) {
+  griddep_wait();   // launched with PDL: nothing upstream is touched before this
+  griddep_launch_dependents();
+  permute_decode_block(ids, weights, n, K, lo, hi, seg, perm_slot, perm_w, active, tokrow);
+}
+
+// Decode router in one launch (T <= 16 tokens, E <= 1024 experts): every CTA computes the
+// fp32 logits of some experts for all tokens (one warp per expert row, bf16 gate weights
+// [E, H]), the CTA that finishes last (counter, re-zeroed) then runs the top-k of every
+// token and the decode permute.
+template <int PER>
+__global__ void __launch_bounds__(512) moe_route_decode_kernel(
+    const __nv_bfloat16* __restrict__ x, int x_stride, int T, const __nv_bfloat16* __restrict__ gate, int E, int H,
+    const float* __restrict__ bias, int K, int scoring, int n_group, int topk_group, int renorm, float scale,
+    float* __restrict__ logits, int* __restrict__ counter, int* __restrict__ out_ids, float* __restrict__ out_w,
+    int lo, int hi, int* __restrict__ seg, int* __restrict__ perm_slot, float* __restrict__ perm_w,
+    int* __restrict__ active, int* __restrict__ tokrow) {
+  griddep_wait();   // launched with PDL: nothing upstream is touched before this
+  griddep_launch_dependents();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  // four experts per CTA, four warps per expert row (a quarter of H each), so that many
+  // SMs stream the gate weights and every warp has few dependent loads
+  __shared__ float part[16][16];
+  const int gw = blockIdx.x * 4 + (warp >> 2), q = warp & 3;
+  float acc[16];
+#pragma unroll
+  for (int t = 0; t < 16; ++t) acc[t] = 0.f;
+  if (gw < E) {
+    const int kq = ((H / 8 + 3) / 4) * 8;           // this quarter's [k0, k1)
+    const int k0 = q * kq, k1 = min(H, k0 + kq);
+    const __nv_bfloat16* g = gate + (size_t)gw * H;
+#pragma unroll 4
+    for (int k = k0 + lane * 8; k < k1; k += 256) {
+      const uint4 gv = *reinterpret_cast<const uint4*>(g + k);
+      const uint32_t gs[4] = {gv.x, gv.y, gv.z, gv.w};
+#pragma unroll
+      for (int t = 0; t < 16; ++t) {
+        if (t >= T) break;
+        const uint4 xv = __ldg(reinterpret_cast<const uint4*>(x + (size_t)t * x_stride + k));
+        const uint32_t xs[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[t] += bf16_lo(gs[j]) * bf16_lo(xs[j]) + bf16_hi(gs[j]) * bf16_hi(xs[j]);
+      }
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < 16; ++t) {
+    const float v = warp_sum(acc[t]);
+    if (lane == 0) part[warp][t] = v;
+  }
+  __syncthreads();
+  if (threadIdx.x < 64) {   // (expert of the CTA, token): the four quarters in order
+    const int ee = threadIdx.x >> 4, t = threadIdx.x & 15, e = blockIdx.x * 4 + ee;
+    if (e < E && t < T)
+      logits[(size_t)t * E + e] = ((part[4 * ee][t] + part[4 * ee + 1][t]) + part[4 * ee + 2][t]) + part[4 * ee + 3][t];
+  }
+  __shared__ int s_last;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(counter, 1) == (int)gridDim.x - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  __shared__ float gscore_sh[16][64];
+  for (int t = warp; t < T; t += 16)
+    router_topk_warp<PER>(logits + (size_t)t * E, bias, t, E, K, scoring, n_group, topk_group, renorm, scale,
+                          out_ids, out_w, gscore_sh[warp]);
+  __syncthreads();
+  permute_decode_block(out_ids, out_w, T * K, K, lo, hi, seg, perm_slot, perm_w, active, tokrow);
+  if (threadIdx.x == 0) *counter = 0;
 }
 
 // out[t] = sum_k slot[t*K+k] (local pairs only) + shared[t] + extra[t]
@@ -776,6 +859,31 @@ int xtu_moe_permute_decode(const int* ids, const float* weights, int T, int K, i
   if (E <= 0 || E > 1024 || (tokrow && T > 16)) return -2;
   launch_pdl(moe_permute_decode_kernel, dim3(1), dim3(512), 0, s, ids, weights, T * K, K, lo, hi, seg, perm_slot,
              perm_w, active, tokrow);
+  return rc_last();
+}
+
+// decode router + permute in one launch (see moe_route_decode_kernel).  x [T <= 16, H] bf16
+// (rows 16-byte aligned), gate [E, H] bf16; logits: T * E fp32 scratch; counter: one zeroed
+// int (left zeroed).  Outputs as xtu_router_topk + xtu_moe_permute_decode.
+int xtu_moe_route_decode(const void* x, int x_stride, int T, const void* gate, int E, int H, const float* bias, int K,
+                         int scoring, int n_group, int topk_group, int renorm, float scale, float* logits,
+                         int* counter, int* out_ids, float* out_w, int lo, int hi, int* seg, int* perm_slot,
+                         float* perm_w, int* active, int* tokrow, cudaStream_t s) {
+  if (T <= 0) return 0;
+  if (T > 16 || E > 1024 || K > 32 || n_group > 64 || H % 8 != 0 || hi - lo <= 0 || hi - lo > 1024) return -2;
+  const int per = (E + 31) / 32;
+  const dim3 grid((E + 3) / 4);
+#define XTU_ROUTE(P)                                                                                         \
+  launch_pdl(moe_route_decode_kernel<P>, grid, dim3(512), 0, s, (const __nv_bfloat16*)x, x_stride, T,        \
+             (const __nv_bfloat16*)gate, E, H, bias, K, scoring, n_group, topk_group, renorm, scale, logits,   \
+             counter, out_ids, out_w, lo, hi, seg, perm_slot, perm_w, active, tokrow)
+  if (per <= 1) XTU_ROUTE(1);
+  else if (per <= 2) XTU_ROUTE(2);
+  else if (per <= 4) XTU_ROUTE(4);
+  else if (per <= 8) XTU_ROUTE(8);
+  else if (per <= 16) XTU_ROUTE(16);
+  else XTU_ROUTE(32);
+#undef XTU_ROUTE
   return rc_last();
 }
 

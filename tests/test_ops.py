@@ -299,3 +299,43 @@ def test_dense_mlp_paths(T):
     h = G.silu_and_mul_clamped(g[:, :I], g[:, I:]).to(torch.bfloat16).float()
     ref = h @ w2d.t()
     assert rel_err(y, ref) < 2e-2
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("T", [1, 4, 16])
+@pytest.mark.parametrize("E,K,scoring,ng,tg", [(128, 8, "sigmoid", 1, 1), (256, 8, "sigmoid", 8, 4),
+                                               (64, 4, "softmax", 1, 1)])
+def test_route_decode_matches_separate_router(T, E, K, scoring, ng, tg):
+    """Router + permute in one launch vs logits GEMV -> router_topk -> permute."""
+    from vllm_xtu_moe_b200.ops import gemm as G
+    torch.manual_seed(11)
+    H, I = 1024, 256
+    x = torch.randn(T, H, device="cuda", dtype=torch.bfloat16)
+    gate = (torch.randn(E, H, device="cuda") * 0.2).to(torch.bfloat16)   # well-separated scores
+    bias = torch.randn(E, device="cuda") * 0.05 if scoring == "sigmoid" else None
+    ex = M.prepare_experts("bf16", torch.zeros(E, 2 * I, H, device="cuda", dtype=torch.bfloat16),
+                           torch.zeros(E, H, I, device="cuda", dtype=torch.bfloat16))
+    assert M.decode_route_ok(x, gate, ex, K, ng)
+    ws = M.MoEWorkspace(16, K, E, H, I, x.device)
+    for lo, n_local in [(0, E), (E // 4, E // 2)]:
+        for _ in range(2):   # the launch counter must be left zeroed
+            ids, w = M.route_decode(x, gate, bias, K, scoring, ng, tg, True, 2.5, ws, lo, n_local)
+            torch.cuda.synchronize()
+            N.check_status()
+            logits = G.linear(x, gate, out_dtype=torch.float32)
+            ids_r, w_r = router_topk(logits, K, scoring, bias, ng, tg, True, 2.5)
+            s1, o1 = ids.sort(-1)
+            s2, o2 = ids_r.sort(-1)
+            assert torch.equal(s1, s2)
+            assert torch.allclose(w.gather(1, o1), w_r.gather(1, o2), atol=1e-4)
+            # the permutation: each local pair lands in its expert's segment, once
+            seg = ws.seg[: n_local + 1].cpu()
+            cnt = torch.bincount((ids.flatten() - lo).clamp(0, n_local)[(ids.flatten() >= lo) &
+                                 (ids.flatten() < lo + n_local)].long().cpu(), minlength=n_local)
+            assert torch.equal(seg[1:] - seg[:-1], cnt.int())
+            rows = ws.perm_slot[: int(seg[-1])].cpu()
+            assert sorted(rows.tolist()) == [p for p in range(T * K)
+                                             if lo <= int(ids.flatten()[p]) < lo + n_local]
+            act = ws.active.cpu()
+            assert act[0].item() == int((cnt > 0).sum()) and torch.equal(act[1:1 + act[0]],
+                                                                          torch.nonzero(cnt).flatten().int())

@@ -168,7 +168,17 @@ class MoEBlock:
                            c.routed_scale)
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
-        ids, w = self.route(x)
+        c = self.cfg
+        permuted = False
+        if self.executor is None and M.decode_route_ok(x, self.gate, self.experts, c.top_k, c.n_group):
+            # decode: router and permute in one launch, straight into the MoE workspace
+            bias = self.gate_bias.float() if self.gate_bias is not None else None
+            ids, w = M.route_decode(x, self.gate, bias, c.top_k, c.scoring, c.n_group, c.topk_group,
+                                    c.norm_topk_prob, c.routed_scale, self.workspace(x), self.expert_lo,
+                                    self.experts.num_experts)
+            permuted = True
+        else:
+            ids, w = self.route(x)
         self.last_ids = ids
         if self.tracer is not None and self.tracer.routing is not None:
             self.tracer.routing.record(self.trace_idx, ids)
@@ -178,7 +188,7 @@ class MoEBlock:
                 and M.shared_fusable(self.shared, self.experts, self.cfg.swiglu_limit)):
             # decode: the shared expert runs inside the routed experts' GEMV launches
             return M.fused_moe(x, ids, w, self.experts, self.workspace(x), lo=self.expert_lo,
-                               act_limit=self.cfg.swiglu_limit, shared_mlp=self.shared)
+                               act_limit=self.cfg.swiglu_limit, shared_mlp=self.shared, permuted=permuted)
         if self.shared is not None:
             sh = self.shared(x)
             if self.shared_gate is not None:
@@ -187,7 +197,7 @@ class MoEBlock:
         if self.executor is not None:
             return self.executor(self, x, ids, w, sh)
         return M.fused_moe(x, ids, w, self.experts, self.workspace(x), lo=self.expert_lo, shared=sh,
-                           act_limit=self.cfg.swiglu_limit)
+                           act_limit=self.cfg.swiglu_limit, permuted=permuted)
 
     def workspace(self, x: torch.Tensor) -> M.MoEWorkspace | None:
         if not x.is_cuda:

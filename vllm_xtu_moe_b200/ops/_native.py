@@ -65,6 +65,8 @@ _SIGS: dict[str, list] = {
     "xtu_moe_gemv": [P, P, P, P, c_int, c_int, c_int, c_int, P, c_int, c_int, P, c_int, P, P, P, P, P, c_int, c_int,
                      c_int, P, c_int, c_float, c_float, c_float, P, P, P, P, c_int, P, P, P],
     "xtu_moe_permute_decode": [P, P, c_int, c_int, c_int, c_int, P, P, P, P, P, P],
+    "xtu_moe_route_decode": [P, c_int, c_int, P, c_int, c_int, P, c_int, c_int, c_int, c_int, c_int, c_float, P, P,
+                             P, P, c_int, c_int, P, P, P, P, P, P],
     "xtu_paged_attention": [P, c_int, P, P, c_int, P, c_int, P, P, P, c_int, c_int, c_int, c_int, c_int, c_int,
                             c_int, c_int, c_int, c_int, c_int, c_float, c_int, P, P, P, P],
 }

@@ -104,6 +104,8 @@ class MoEWorkspace:
         self.tiles = torch.empty(self.mx * 4, dtype=torch.int32, device=d)
         self.active = torch.zeros(E + 1, dtype=torch.int32, device=d)   # decode GEMV: experts with rows
         self.tokrow = torch.zeros(min(E, n) * 16, dtype=torch.int32, device=d)   # decode: (expert, token) -> row
+        self.route_logits = None                                                 # fused decode router scratch
+        self.route_counter = torch.zeros(1, dtype=torch.int32, device=d)
         self.ntiles = torch.zeros(1, dtype=torch.int32, device=d)
 
     def nbytes(self) -> int:
@@ -132,13 +134,14 @@ def moe_ref(x, ids, weights, experts: ExpertWeights, lo=0, hi=None, act_limit=0.
 
 def moe_experts_partial(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, experts: ExpertWeights,
                         ws: MoEWorkspace, *, lo: int = 0, act_limit: float = 0.0, act_alpha: float = 1.0,
-                        act_beta: float = 0.0, shared_mlp=None) -> torch.Tensor | None:
+                        act_beta: float = 0.0, shared_mlp=None, permuted: bool = False) -> torch.Tensor | None:
     """Expert GEMMs for the pairs whose id is in [lo, lo + E): each such pair's weighted
     output row lands in ws.slots[pair].  Other pairs are untouched (other tiles / tiers).
 
     ``shared_mlp`` (a DenseMLP in the experts' layout): on the decode GEMV path it runs in
     the same launches as one more expert over every token, and its output rows are
-    returned (ws.slots[T*K : T*K + T]); otherwise None is returned and the caller runs it."""
+    returned (ws.slots[T*K : T*K + T]); otherwise None is returned and the caller runs it.
+    ``permuted``: :func:`route_decode` has already filled the decode permutation."""
     T, H = x.shape
     K = ids.shape[1]
     E = experts.num_experts
@@ -156,8 +159,9 @@ def moe_experts_partial(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tenso
         # one-CTA permute (no row gather): the gate/up GEMV reads the T tokens directly
         # and keeps each expert's own columns through ws.tokrow
         xt = G.tma_rows(x)
-        N.call("xtu_moe_permute_decode", ids.data_ptr(), weights.data_ptr(), T, K, lo, lo + E, ws.seg.data_ptr(),
-               ws.perm_slot.data_ptr(), ws.perm_w.data_ptr(), ws.active.data_ptr(), ws.tokrow.data_ptr(), s)
+        if not permuted:
+            N.call("xtu_moe_permute_decode", ids.data_ptr(), weights.data_ptr(), T, K, lo, lo + E, ws.seg.data_ptr(),
+                   ws.perm_slot.data_ptr(), ws.perm_w.data_ptr(), ws.active.data_ptr(), ws.tokrow.data_ptr(), s)
         N.call("xtu_moe_gemv", experts.w13.data_ptr(), N.ptr(experts.s13 if fp8 else None),
                experts.w2.data_ptr(), N.ptr(experts.s2 if fp8 else None), int(fp8), E, H, I, xt.data_ptr(), 0,
                xt.stride(0), ws.tokrow.data_ptr(), T, ws.seg.data_ptr(), ws.perm_slot.data_ptr(),
@@ -165,6 +169,8 @@ def moe_experts_partial(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tenso
                ws.active.data_ptr(), 1, float(act_limit), float(act_alpha), float(act_beta),
                *_shared_ptrs(shared_mlp), n, _gv_ws(x.device), N.status_buffer(x.device).data_ptr(), s)
         return ws.slots[n:n + T] if shared_mlp is not None else None
+    if permuted:
+        raise ValueError("a decode-permuted workspace needs the decode GEMV path")
     f16s = int(gemv_path and fp8)
     N.call("xtu_moe_permute", ids.data_ptr(), weights.data_ptr(), T, K, lo, lo + E, ws.counts.data_ptr(),
            ws.seg.data_ptr(), ws.cursor.data_ptr(), ws.perm_slot.data_ptr(), ws.perm_w.data_ptr(), x.data_ptr(), H,
@@ -223,7 +229,8 @@ def moe_combine(ws: MoEWorkspace, ids: torch.Tensor, lo: int, hi: int, *, shared
 def fused_moe(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, experts: ExpertWeights,
               ws: MoEWorkspace | None = None, *, lo: int = 0, shared: torch.Tensor | None = None,
               extra: torch.Tensor | None = None, act_limit: float = 0.0, act_alpha: float = 1.0,
-              act_beta: float = 0.0, out: torch.Tensor | None = None, shared_mlp=None) -> torch.Tensor:
+              act_beta: float = 0.0, out: torch.Tensor | None = None, shared_mlp=None,
+              permuted: bool = False) -> torch.Tensor:
     """Routed-expert MoE over the local experts [lo, lo+E).
 
     x [T, H] bf16, ids/weights [T, K]; shared [T, H] (shared-expert output) and
@@ -245,7 +252,7 @@ def fused_moe(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, experts
         ws = MoEWorkspace(T, K, E, H, experts.inter, x.device)
     assert x.is_contiguous() and ids.is_contiguous() and weights.is_contiguous()
     fused_sh = moe_experts_partial(x, ids, weights, experts, ws, lo=lo, act_limit=act_limit, act_alpha=act_alpha,
-                                   act_beta=act_beta, shared_mlp=shared_mlp)
+                                   act_beta=act_beta, shared_mlp=shared_mlp, permuted=permuted)
     if shared_mlp is not None and fused_sh is None:   # not the decode GEMV path: run it on its own
         fused_sh = shared_mlp(x)
     if fused_sh is not None:
@@ -259,6 +266,39 @@ def route_split(ids: torch.Tensor, slotmap: torch.Tensor, lo: int, gpu_ids: torc
     n = ids.numel()
     N.call("xtu_route_split", ids.data_ptr(), n, lo, slotmap.numel(), slotmap.data_ptr(), gpu_ids.data_ptr(),
            cpu_ids.data_ptr(), N.ptr(hits), N.stream_ptr(ids.device))
+
+
+def decode_route_ok(x: torch.Tensor, gate: torch.Tensor, experts: ExpertWeights | None, top_k: int,
+                    n_group: int) -> bool:
+    """Whether :func:`route_decode` (router + permute in one launch) serves this step."""
+    if experts is None or not x.is_cuda or x.shape[0] > G.GEMV_MAX_M or x.dtype != torch.bfloat16:
+        return False
+    H = x.shape[1]
+    return (gate.dtype == torch.bfloat16 and gate.is_contiguous() and gate.shape[0] <= 1024 and H % 128 == 0
+            and experts.num_experts <= 1024 and experts.interleaved and experts.fmt in ("fp8", "bf16")
+            and experts.inter % 128 == 0 and top_k <= 32 and n_group <= 64)
+
+
+def route_decode(x: torch.Tensor, gate: torch.Tensor, bias: torch.Tensor | None, top_k: int, scoring: str,
+                 n_group: int, topk_group: int, renorm: bool, scale: float, ws: MoEWorkspace, lo: int,
+                 num_local: int):
+    """Decode router and permute in one launch: logits = x gate^T (fp32), scoring + bias +
+    grouped top-k + renorm + scale per token, then the decode permutation of the pairs whose
+    expert is in [lo, lo + num_local) into ``ws``.  Returns (ids int32 [T, K], weights fp32)."""
+    from .router import SCORING
+    T, H = x.shape
+    E = gate.shape[0]
+    xt = G.tma_rows(x)
+    if ws.route_logits is None or ws.route_logits.numel() < 16 * E:
+        ws.route_logits = torch.empty(16 * E, dtype=torch.float32, device=x.device)
+    ids = torch.empty(T, top_k, dtype=torch.int32, device=x.device)
+    w = torch.empty(T, top_k, dtype=torch.float32, device=x.device)
+    N.call("xtu_moe_route_decode", xt.data_ptr(), xt.stride(0), T, gate.data_ptr(), E, H, N.ptr(bias), top_k,
+           SCORING[scoring], n_group, topk_group, int(renorm), float(scale), ws.route_logits.data_ptr(),
+           ws.route_counter.data_ptr(), ids.data_ptr(), w.data_ptr(), lo, lo + num_local, ws.seg.data_ptr(),
+           ws.perm_slot.data_ptr(), ws.perm_w.data_ptr(), ws.active.data_ptr(), ws.tokrow.data_ptr(),
+           N.stream_ptr(x.device))
+    return ids, w
 
 
 def shared_fusable(shared_mlp, experts: ExpertWeights, act_limit: float = 0.0, act_alpha: float = 1.0,
