@@ -18,6 +18,7 @@
 #include <cfloat>
 #include "ptx.cuh"
 #include "launch.cuh"
+#include "../comm/peer.cuh"
 #include "xtu_argmax_static.h"
 #include <mutex>
 
@@ -107,6 +108,93 @@ __global__ void __launch_bounds__(NT) rmsnorm_kernel(const __nv_bfloat16* __rest
       o[j] = pack_bf16x2(row[i + 2 * j] * inv * w0, row[i + 2 * j + 1] * inv * w1);
     }
     *reinterpret_cast<uint4*>(yr + i) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+// Tensor-parallel sum + residual add + RMSNorm (the consumer of xtu_gemv_tp): waits
+// (bounded) until every rank's partial rows have landed in this rank's receive buffer,
+// sums them in rank order in fp32, rounds to bf16 (the all-reduce result), then adds
+// the residual and normalises exactly as rmsnorm_kernel.  One CTA per token; the CTA
+// that finishes last publishes the epoch for the next producer.
+template <int NT>
+__global__ void __launch_bounds__(NT) tp_sum_rmsnorm_kernel(
+    const __nv_bfloat16* __restrict__ recv, long long slot, int world, int H, const int* flags, const int* ep_p,
+    int* ep_c, int* done, const __nv_bfloat16* __restrict__ residual, __nv_bfloat16* __restrict__ residual_out,
+    const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ y, float eps, int add_one, XtuStatus* st,
+    long long timeout_ns) {
+  griddep_wait();   // launched with PDL: nothing upstream is touched before this
+  griddep_launch_dependents();
+  extern __shared__ float row[];  // H floats
+  __shared__ float sh[32];
+  const int t = blockIdx.x;
+  const int e = *ep_p, par = e & 1;
+  bool ok = true;
+  if ((int)threadIdx.x < world) {
+    const uint64_t t0 = globaltimer_ns();
+    uint32_t spins = 0;
+    while (ld_acquire_sys(flags + threadIdx.x) < e) {
+      if ((++spins & 63u) == 0u) {
+        if (globaltimer_ns() - t0 > (uint64_t)timeout_ns) {
+          report_error(st, XTU_ERR_PEER_TIMEOUT, 210, threadIdx.x);
+          ok = false;
+          break;
+        }
+        if (status_failed(st)) { ok = false; break; }
+      }
+    }
+  }
+  if (!__syncthreads_and(ok)) return;
+  float ss = 0.f;
+  for (int i = threadIdx.x * 8; i < H; i += NT * 8) {
+    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int p = 0; p < world; ++p) {
+      const uint4 pv = __ldcg(reinterpret_cast<const uint4*>(recv + (size_t)(par * world + p) * slot +
+                                                             (size_t)t * H + i));
+      const uint32_t ps[4] = {pv.x, pv.y, pv.z, pv.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) { v[2 * j] += bf16_lo(ps[j]); v[2 * j + 1] += bf16_hi(ps[j]); }
+    }
+    uint4 xs4;   // the all-reduce result in bf16, as the unfused path would hold it
+    xs4.x = pack_bf16x2(v[0], v[1]); xs4.y = pack_bf16x2(v[2], v[3]);
+    xs4.z = pack_bf16x2(v[4], v[5]); xs4.w = pack_bf16x2(v[6], v[7]);
+    const uint32_t xs[4] = {xs4.x, xs4.y, xs4.z, xs4.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) { v[2 * j] = bf16_lo(xs[j]); v[2 * j + 1] = bf16_hi(xs[j]); }
+    const uint4 rv = *reinterpret_cast<const uint4*>(residual + (size_t)t * H + i);
+    const uint32_t rs[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) { v[2 * j] += bf16_lo(rs[j]); v[2 * j + 1] += bf16_hi(rs[j]); }
+    uint4 o;
+    o.x = pack_bf16x2(v[0], v[1]); o.y = pack_bf16x2(v[2], v[3]);
+    o.z = pack_bf16x2(v[4], v[5]); o.w = pack_bf16x2(v[6], v[7]);
+    *reinterpret_cast<uint4*>(residual_out + (size_t)t * H + i) = o;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t pj = j == 0 ? o.x : j == 1 ? o.y : j == 2 ? o.z : o.w;
+      v[2 * j] = bf16_lo(pj); v[2 * j + 1] = bf16_hi(pj);
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) { row[i + j] = v[j]; ss += v[j] * v[j]; }
+  }
+  const float tot = block_sum<NT>(ss, sh);
+  const float inv = rsqrtf(tot / (float)H + eps);
+  __nv_bfloat16* yr = y + (size_t)t * H;
+  for (int i = threadIdx.x * 8; i < H; i += NT * 8) {
+    const uint4 wv = *reinterpret_cast<const uint4*>(w + i);
+    const uint32_t ws[4] = {wv.x, wv.y, wv.z, wv.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float w0 = bf16_lo(ws[j]), w1 = bf16_hi(ws[j]);
+      if (add_one) { w0 += 1.f; w1 += 1.f; }
+      o[j] = pack_bf16x2(row[i + 2 * j] * inv * w0, row[i + 2 * j + 1] * inv * w1);
+    }
+    *reinterpret_cast<uint4*>(yr + i) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && atomicAdd(done, 1) == (int)gridDim.x - 1) {
+    *done = 0;
+    *ep_c = e;
   }
 }
 
@@ -780,6 +868,23 @@ int xtu_rmsnorm(const void* x, const void* residual, void* residual_out, const v
   launch_pdl(rmsnorm_kernel<256>, dim3(T), dim3(256), sm, s, (const __nv_bfloat16*)x,
              (const __nv_bfloat16*)residual, (__nv_bfloat16*)residual_out, (const __nv_bfloat16*)w,
              (__nv_bfloat16*)y, H, eps, add_one, x_stride, y_stride);
+  return rc_last();
+}
+
+// consumer of xtu_gemv_tp; recv: this rank's receive buffer (2 * world slots of `slot`
+// elements); flags: this rank's flag array; ep_p / ep_c / done as xtu_gemv_tp's.
+int xtu_tp_sum_rmsnorm(const void* recv, long long slot, int world, int T, int H, const int* flags, const int* ep_p,
+                       int* ep_c, int* done, const void* residual, void* residual_out, const void* w, void* y,
+                       float eps, int add_one, void* status, long long timeout_ns, cudaStream_t s) {
+  if (T <= 0) return 0;
+  if (H % 8 != 0 || world > 256 || (long long)T * H > slot) return -2;
+  const size_t sm = (size_t)H * sizeof(float);
+  if (sm > 48 * 1024) cudaFuncSetAttribute(tp_sum_rmsnorm_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)sm);
+  launch_pdl(tp_sum_rmsnorm_kernel<256>, dim3(T), dim3(256), sm, s, (const __nv_bfloat16*)recv, slot, world, H, flags,
+             ep_p, ep_c, done, (const __nv_bfloat16*)residual, (__nv_bfloat16*)residual_out,
+             (const __nv_bfloat16*)w, (__nv_bfloat16*)y, eps, add_one, reinterpret_cast<XtuStatus*>(status),
+             timeout_ns);
   return rc_last();
 }
 

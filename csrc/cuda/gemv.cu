@@ -47,6 +47,7 @@
 #include <cstdint>
 #include "ptx.cuh"
 #include "launch.cuh"
+#include "../comm/peer.cuh"
 
 namespace xtu {
 
@@ -312,12 +313,27 @@ __device__ __forceinline__ uint8_t* gv_setup(uint64_t*& full, uint64_t*& empty, 
 // ---------------------------------------------------------------------------
 // dense: y[M, N] = x[M, K] W^T (+ bias); grid (32-row tiles, K splits)
 // ---------------------------------------------------------------------------
-template <bool FP8, int NT, int WM>
+// Tensor-parallel epilogue: instead of y, every rank's partial rows go straight into all
+// ranks' receive buffers (slot [parity][rank]) by peer stores, and the tile that finishes
+// last raises this rank's flag on every peer.  The rows are summed by the next kernel
+// (xtu_tp_sum_rmsnorm).  Epochs: e = *ep_c + 1 (advanced by that consumer), published in
+// *ep_p for it; two receive parities so use u + 1 never overwrites what use u still reads.
+struct GvPeer {
+  __nv_bfloat16* const* dst;   // [world] receive buffers (symmetric), 2 * world slots each
+  long long slot;              // elements per slot (>= M * N)
+  int rank, world;
+  int* done;                   // finished-tile counter (zeroed, left zeroed)
+  int* const* flags;           // [world] peers' flag arrays
+  const int* ep_c;             // epoch the consumer finished
+  int* ep_p;                   // epoch this producer published
+};
+
+template <bool FP8, int NT, int WM, bool PEER = false>
 __global__ void __launch_bounds__(GV_THREADS) gemv_dense_kernel(
     const __grid_constant__ CUtensorMap tmap, const __grid_constant__ CUtensorMap xmap,
     const float* __restrict__ wscale, int N, int K, int M, const __nv_bfloat16* __restrict__ bias,
     void* __restrict__ y, int y_stride, int y_f32, float* __restrict__ ws, int* __restrict__ counters,
-    XtuStatus* st) {
+    XtuStatus* st, GvPeer pr = GvPeer{}) {
   griddep_wait();   // launched with PDL: nothing upstream is touched before this
   griddep_launch_dependents();
   uint64_t *full, *empty;
@@ -408,10 +424,29 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_dense_kernel(
         if (row < N && tok < M) {
           float v = acc[t][n][i];
           if (bias) v += __bfloat162float(bias[row]);
-          if (y_f32) reinterpret_cast<float*>(y)[(size_t)tok * y_stride + row] = v;
-          else reinterpret_cast<__nv_bfloat16*>(y)[(size_t)tok * y_stride + row] = __float2bfloat16(v);
+          if (PEER) {
+            const __nv_bfloat16 bv = __float2bfloat16(v);
+            const int par = (*pr.ep_c + 1) & 1;
+            const size_t off = (size_t)(par * pr.world + pr.rank) * pr.slot + (size_t)tok * N + row;
+            for (int p = 0; p < pr.world; ++p) pr.dst[p][off] = bv;
+          } else if (y_f32) {
+            reinterpret_cast<float*>(y)[(size_t)tok * y_stride + row] = v;
+          } else {
+            reinterpret_cast<__nv_bfloat16*>(y)[(size_t)tok * y_stride + row] = __float2bfloat16(v);
+          }
         }
       }
+  if (PEER) {   // this tile's rows are out: the last tile raises the flag on every peer
+    __threadfence_system();
+    __syncwarp();
+    if (lane == 0 && atomicAdd(pr.done, 1) == (int)gridDim.x - 1) {
+      *pr.done = 0;
+      const int e = *pr.ep_c + 1;
+      fence_acq_rel_sys();
+      for (int p = 0; p < pr.world; ++p) st_release_sys(pr.flags[p] + pr.rank, e);
+      *pr.ep_p = e;
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -724,7 +759,7 @@ int xtu_gemv(const void* W, const float* wscale, int fp8, int N, int K, const vo
     }                                                                                                        \
     const dim3 grid(tiles, gv_splits(tiles, S, N, occ * gemv_num_sms()));                                   \
     launch_pdl(gemv_dense_kernel<F, NTV, WMV>, grid, dim3(GV_THREADS), GvCfg<F, NTV>::BYTES, s, tm, xm, wscale, N, \
-               K, M, (const __nv_bfloat16*)bias, y, y_stride, y_f32, ws, counters, st);                      \
+               K, M, (const __nv_bfloat16*)bias, y, y_stride, y_f32, ws, counters, st, GvPeer{});            \
   } while (0)
   const bool w2d = ((long long)K * (fp8 ? 1 : 2)) % 128 != 0;
   if (fp8) {
@@ -741,6 +776,66 @@ int xtu_gemv(const void* W, const float* wscale, int fp8, int N, int K, const vo
     }
   }
 #undef XTU_GEMV_LAUNCH
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? launches : -(int)e;
+}
+
+// Tensor-parallel decode GEMV: this rank's partial y[M, N] = x W^T (W row-parallel slice)
+// goes to every rank's receive buffer by peer stores and is summed there by
+// xtu_tp_sum_rmsnorm; see GvPeer.  bf16 output, no bias; other arguments as xtu_gemv.
+int xtu_gemv_tp(const void* W, const float* wscale, int fp8, int N, int K, const void* x, int x_stride, int M,
+                float* ws, int* counters, void* const* dst, long long slot, int rank, int world, int* done,
+                void* const* flags, const int* ep_c, int* ep_p, void* status, cudaStream_t s) {
+  if (M <= 0 || N <= 0) return 0;
+  if (M > 16 || K % 64 != 0 || ws == nullptr || counters == nullptr || (long long)M * N > slot) return -2;
+  if (K > GV_MAX_KBLK * 128) return -3;
+  if (fp8 && (long long)M * K > GV_WS_X_HALVES) return -4;
+  const int nt = M > 8 ? 2 : 1;
+  const int tiles = (N + 31) / 32;
+  const int S = gv_stages_per_tile(K, fp8 != 0);
+  int launches = 1;
+  if (fp8) {
+    x = gv_convert_x(x, M, K, x_stride, ws, s);
+    x_stride = K;
+    ++launches;
+  }
+  CUtensorMap tm, xm;
+  int rc = gv_wmap(&tm, W, (uint64_t)N, K, fp8 != 0, false);
+  if (rc) return rc;
+  rc = gv_xmap(&xm, x, (uint64_t)M, K, x_stride, 8 * nt, fp8 != 0);
+  if (rc) return rc;
+  XtuStatus* st = reinterpret_cast<XtuStatus*>(status);
+  GvPeer pr;
+  pr.dst = reinterpret_cast<__nv_bfloat16* const*>(dst);
+  pr.slot = slot;
+  pr.rank = rank;
+  pr.world = world;
+  pr.done = done;
+  pr.flags = reinterpret_cast<int* const*>(flags);
+  pr.ep_c = ep_c;
+  pr.ep_p = ep_p;
+  const bool w2d = ((long long)K * (fp8 ? 1 : 2)) % 128 != 0;
+  if (w2d) return -8;
+#define XTU_GEMV_TP_LAUNCH(F, NTV)                                                                           \
+  do {                                                                                                       \
+    static int occ = 0;                                                                                      \
+    if (!occ) {                                                                                              \
+      rc = gv_smem_attr(gemv_dense_kernel<F, NTV, 0, true>, GvCfg<F, NTV>::BYTES);                           \
+      if (rc) return rc;                                                                                     \
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gemv_dense_kernel<F, NTV, 0, true>, GV_THREADS, \
+                                                        GvCfg<F, NTV>::BYTES) != cudaSuccess || occ < 1)      \
+        occ = 1;                                                                                             \
+    }                                                                                                        \
+    const dim3 grid(tiles, gv_splits(tiles, S, N, occ * gemv_num_sms()));                                   \
+    launch_pdl(gemv_dense_kernel<F, NTV, 0, true>, grid, dim3(GV_THREADS), GvCfg<F, NTV>::BYTES, s, tm, xm,    \
+               wscale, N, K, M, (const __nv_bfloat16*)nullptr, (void*)nullptr, 0, 0, ws, counters, st, pr);  \
+  } while (0)
+  if (fp8) {
+    if (nt == 1) XTU_GEMV_TP_LAUNCH(true, 1); else XTU_GEMV_TP_LAUNCH(true, 2);
+  } else {
+    if (nt == 1) XTU_GEMV_TP_LAUNCH(false, 1); else XTU_GEMV_TP_LAUNCH(false, 2);
+  }
+#undef XTU_GEMV_TP_LAUNCH
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? launches : -(int)e;
 }

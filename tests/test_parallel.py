@@ -216,7 +216,9 @@ def test_tensor_parallel_matches_single_rank_cpu(name):
     mp.spawn(_tp_cpu_worker, args=(2, _port(), name), nprocs=2)
 
 
-def _tp_gpu_worker(rank, world, port):
+def _tp_gpu_worker(rank, world, port, mode="p2p"):
+    from vllm_xtu_moe_b200.engine import LLM, SamplingParams
+    from vllm_xtu_moe_b200.engine.runner import RunnerConfig
     from vllm_xtu_moe_b200.models.model import build_model
     from vllm_xtu_moe_b200.ops import _native as N
     from vllm_xtu_moe_b200.parallel.tp import TPReducer, build_tp_model
@@ -224,13 +226,28 @@ def _tp_gpu_worker(rank, world, port):
     d = torch.device("cuda", rank)
     cfg = _tp_cfg("glm-4.5-air").replace(hidden_size=512, num_heads=8, dense_fmt="fp8", expert_fmt="fp8")
     ref = build_model(cfg, device=d, seed=4)
-    red = TPReducer(256, cfg.hidden_size, device=d, mode="p2p")
+    red = TPReducer(256, cfg.hidden_size, device=d, mode=mode)
     m = build_tp_model(cfg, rank, world, d, seed=4, reducer=red)
     a, b = _tp_logits(ref, str(d)), _tp_logits(m, str(d))
     torch.cuda.synchronize(d)
     N.check_status(d)
     err = (a - b).abs().max().item() / a.abs().max().item()
     assert err < 5e-2, err
+    if mode == "fused":
+        # decode steps (<= 16 tokens) take the GEMV -> peer-scatter -> sum-in-norm path; greedy
+        # generation through the engine, eager and CUDA-graph decode, matches the one-GPU model
+        for graph in (False, True):
+            rc = dict(block_size=64, max_seqs=2, max_model_len=256, max_batched_tokens=128, use_cuda_graph=graph)
+            n0 = red.fused_calls
+            prompts = [[3, 4, 5, 6, 7, 8, 9], list(range(20, 60))]
+            sp = SamplingParams(max_tokens=6)
+            got = [r.token_ids for r in LLM(m, device=str(d), runner_config=RunnerConfig(**rc)).generate(prompts, sp)]
+            want = [r.token_ids for r in LLM(ref, device=str(d), runner_config=RunnerConfig(**rc)).generate(prompts, sp)]
+            torch.cuda.synchronize(d)
+            N.check_status(d)
+            assert red.fused_calls > n0
+            same = sum(x == y for g, w in zip(got, want) for x, y in zip(g, w))
+            assert same >= 0.8 * sum(len(w) for w in want), (got, want)
     # both ranks hold identical activations -> identical logits
     other = [torch.empty_like(b) for _ in range(world)]
     dist.all_gather_object(other, b)
@@ -241,9 +258,10 @@ def _tp_gpu_worker(rank, world, port):
 
 @pytest.mark.gpu
 @pytest.mark.multigpu
-def test_tensor_parallel_p2p_matches_single_gpu():
+@pytest.mark.parametrize("mode", ["p2p", "fused"])
+def test_tensor_parallel_p2p_matches_single_gpu(mode):
     _need_two_gpus()
-    mp.spawn(_tp_gpu_worker, args=(2, _port()), nprocs=2)
+    mp.spawn(_tp_gpu_worker, args=(2, _port(), mode), nprocs=2)
 
 
 # ----------------------------------------------------------------------------- pipeline parallel

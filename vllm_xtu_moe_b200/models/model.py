@@ -34,9 +34,12 @@ class DecoderLayer:
         else:
             h, residual = self.attn_norm(x, residual)
         h = self.attn(h, meta, kv, rope)
-        if self.reduce is not None:
-            h = self.reduce(h)
-        h, residual = self.mlp_norm(h, residual)
+        if hasattr(h, "finish"):   # tensor parallel, fused: the partials are summed inside the norm
+            h, residual = h.finish(residual, self.mlp_norm)
+        else:
+            if self.reduce is not None:
+                h = self.reduce(h)
+            h, residual = self.mlp_norm(h, residual)
         h = self.mlp(h)
         if self.reduce is not None:
             h = self.reduce(h)

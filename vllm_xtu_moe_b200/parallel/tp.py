@@ -208,9 +208,16 @@ class TPWeightFactory:
 
 
 class TPReducer:
-    """Sum of the ranks' partial [T, H] outputs (P2P one-shot / two-shot, or NCCL)."""
+    """Sum of the ranks' partial [T, H] outputs (P2P one-shot / two-shot, or NCCL).
+
+    mode "fused" adds the decode form of the row-parallel output projection (SURVEY row
+    W10): the GEMV's epilogue stores each rank's partial rows straight into every rank's
+    receive buffer over NVLink and flags them (``xtu_gemv_tp``); the next RMSNorm sums
+    them in rank order, adds the residual and normalises (``xtu_tp_sum_rmsnorm``), so no
+    separate all-reduce or copy runs.  Larger steps use the one-shot / two-shot kernels."""
 
     ONESHOT_BYTES = 256 << 10
+    FUSED_MAX_TOKENS = 16
 
     def __init__(self, max_tokens: int, hidden: int, group=None, device=None, mode: str = "p2p"):
         self.mode = mode
@@ -218,14 +225,62 @@ class TPReducer:
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.n_max = max_tokens * hidden
-        if mode == "p2p":
+        self.hidden = hidden
+        if mode in ("p2p", "fused"):
             nb = self.n_max * 2
-            self.pg = PeerGroup(PeerGroup.heap_bytes_for(nb, nb), group=group, device=device)
+            self.slot = self.FUSED_MAX_TOKENS * hidden
+            sizes = [nb, nb] + ([2 * self.world * self.slot * 2, self.world * 4] if mode == "fused" else [])
+            self.pg = PeerGroup(PeerGroup.heap_bytes_for(*sizes), group=group, device=device)
             self.inb = self.pg.alloc((self.n_max,), torch.bfloat16)
             self.outb = self.pg.alloc((self.n_max,), torch.bfloat16)
+            if mode == "fused":
+                d = self.pg.device
+                self.recv = self.pg.alloc((2 * self.world * self.slot,), torch.bfloat16)
+                self.tpflags = self.pg.alloc((self.world,), torch.int32)
+                # ep_c, ep_p (epochs the consumer / producer last finished), done_p, done_c
+                self.ctl = torch.zeros(4, dtype=torch.int32, device=d)
+                self.pg.barrier()   # every rank's flags are zero before any use
         self.calls = 0
+        self.fused_calls = 0
+
+    # ------------------------------------------------------------------ fused decode form
+    def fusable(self, x: torch.Tensor, lin) -> bool:
+        T, K = x.shape
+        return (self.mode == "fused" and x.is_cuda and T <= self.FUSED_MAX_TOKENS and lin.bias is None
+                and lin.weight.shape[0] == self.hidden and K % 64 == 0 and x.dtype == torch.bfloat16
+                and (K * lin.weight.element_size()) % 128 == 0)
+
+    def linear_scatter(self, x: torch.Tensor, lin) -> "PendingTPSum":
+        """Row-parallel ``lin(x)`` whose partial goes to every rank's receive buffer."""
+        from ..ops import gemm as G
+        x = G.tma_rows(x)
+        T, K = x.shape
+        ws, cnt = G._gemv_split_ws(x.device)
+        c = self.ctl
+        N.call("xtu_gemv_tp", lin.weight.data_ptr(), N.ptr(lin.scale), int(lin.scale is not None), self.hidden, K,
+               x.data_ptr(), x.stride(0), T, ws.data_ptr(), cnt.data_ptr(), self.recv.ptr(), self.slot, self.pg.rank,
+               self.world, c[2:].data_ptr(), self.tpflags.ptr(), c[0:].data_ptr(), c[1:].data_ptr(),
+               N.status_buffer(x.device).data_ptr(), N.stream_ptr(x.device))
+        self.fused_calls += 1
+        return PendingTPSum(self, T)
+
+    def sum_rmsnorm(self, T: int, residual: torch.Tensor, norm) -> tuple[torch.Tensor, torch.Tensor]:
+        """(RMSNorm(sum of the ranks' partials + residual), the new residual)."""
+        H = self.hidden
+        y = torch.empty(T, H, dtype=torch.bfloat16, device=residual.device)
+        r_out = torch.empty_like(y)
+        c = self.ctl
+        N.call("xtu_tp_sum_rmsnorm", self.recv.local.data_ptr(), self.slot, self.world, T, H,
+               self.tpflags.local.data_ptr(), c[1:].data_ptr(), c[0:].data_ptr(), c[3:].data_ptr(),
+               residual.contiguous().data_ptr(), r_out.data_ptr(), norm.weight.data_ptr(), y.data_ptr(),
+               float(norm.eps), int(norm.add_one), N.status_buffer(residual.device).data_ptr(), self.pg.timeout_ns,
+               N.stream_ptr(residual.device))
+        self.calls += 1
+        return y, r_out
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        if isinstance(x, PendingTPSum):
+            raise TypeError("a pending fused TP sum is finished by sum_rmsnorm, not reduced again")
         self.calls += 1
         if self.mode == "nccl":
             y = x.contiguous()
@@ -247,8 +302,40 @@ class TPReducer:
         return self.outb.local[:n].view_as(x).clone()
 
     def close(self):
-        if self.mode == "p2p":
+        if self.mode in ("p2p", "fused"):
             self.pg.close()
+
+
+class PendingTPSum:
+    """A row-parallel projection whose ranks' partials are in flight to every rank's
+    receive buffer; ``finish`` sums them inside the following RMSNorm."""
+
+    def __init__(self, reducer: TPReducer, T: int):
+        self.reducer, self.T = reducer, T
+
+    def finish(self, residual: torch.Tensor, norm) -> tuple[torch.Tensor, torch.Tensor]:
+        return self.reducer.sum_rmsnorm(self.T, residual, norm)
+
+
+class TPRowLinear:
+    """Output projection of a TP attention block: decode-size calls take the fused
+    GEMV -> peer-scatter path (returning a PendingTPSum), others run the plain linear."""
+
+    def __init__(self, lin, reducer: TPReducer):
+        self.lin, self.reducer = lin, reducer
+        self.weight, self.scale, self.bias = lin.weight, lin.scale, lin.bias
+
+    @property
+    def out_features(self) -> int:
+        return self.lin.out_features
+
+    def __call__(self, x: torch.Tensor, out_dtype=torch.bfloat16):
+        if out_dtype == torch.bfloat16 and self.reducer.fusable(x, self.lin):
+            return self.reducer.linear_scatter(x, self.lin)
+        return self.lin(x, out_dtype)
+
+    def tensors(self):
+        return self.lin.tensors()
 
 
 def build_tp_model(cfg: ModelConfig, rank: int, tp: int, device, seed: int = 0, source=None,
@@ -269,6 +356,8 @@ def build_tp_model(cfg: ModelConfig, rank: int, tp: int, device, seed: int = 0, 
     El = cfg.num_experts // tp if cfg.num_experts else 0
     for l in m.layers + [mt.layer for mt in m.mtp]:
         l.reduce = reducer
+        if reducer is not None and reducer.mode == "fused" and hasattr(l.attn, "o"):
+            l.attn.o = TPRowLinear(l.attn.o, reducer)   # GQA / MLA output projection
         if isinstance(l.mlp, MoEBlock):
             l.mlp.expert_lo = rank * El
     m.tp = (rank, tp)
