@@ -65,6 +65,7 @@ struct AdParams {
   float* ws_o;              // [splits, T, Hq, D] normalised partials (splits > 1)
   float* ws_lse;            // [splits, T, Hq]  m + log2(l)
   int* counters;            // [B * Hkv] zeroed; the last split CTA merges and re-zeroes
+  int num_blocks;           // pages in the cache (bounds-check build)
   int T;
   XtuStatus* status;
 };
@@ -151,6 +152,8 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(const __grid_co
       const int cnt = min(32, nj - c0);
       for (int k = 0; k < cnt; ++k) {
         const int pg = __shfl_sync(0xffffffffu, page, k);
+        // a page id past the cache reads zero fill (TMA bounds); the bounds-check build reports it
+        if (lane == 0) (void)XTU_IN_BOUNDS(pg >= 0 && pg < p.num_blocks, p.status, 230, pg);
         if (lane == 0) {
           const int i = c0 + k, slot = i % STAGES;
           if (i >= STAGES && !mbar_wait(&empty[slot], ((i / STAGES) - 1) & 1, p.status, 130)) {
@@ -447,7 +450,7 @@ static int ad_launch(const CUtensorMap& tk, const CUtensorMap& tv, const AdParam
 int attn_decode_gqa(const CUtensorMap& tk, const CUtensorMap& tv, const void* q, int q_stride, void* o,
                     int o_stride, const int* q_start, const int* kv_len, const int* block_table, int bt_stride,
                     int B, int max_q_len, int T, int Hq, int Hkv, int D, float scale, int splits, float* ws_o,
-                    float* ws_lse, int* counters, void* status, cudaStream_t s) {
+                    float* ws_lse, int* counters, int num_blocks, void* status, cudaStream_t s) {
   const int G = Hq / Hkv;
   const int rows = max_q_len * G;
   if ((D != 64 && D != 128) || rows > 32 || rows <= 0) return 0;
@@ -470,6 +473,7 @@ int attn_decode_gqa(const CUtensorMap& tk, const CUtensorMap& tv, const void* q,
   p.ws_o = ws_o;
   p.ws_lse = ws_lse;
   p.counters = counters;
+  p.num_blocks = num_blocks;
   p.T = T;
   p.status = reinterpret_cast<XtuStatus*>(status);
   if (D == 128) return rows <= 16 ? ad_launch<128, 1>(tk, tv, p, B, s) : ad_launch<128, 2>(tk, tv, p, B, s);

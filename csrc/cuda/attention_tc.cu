@@ -532,7 +532,7 @@ namespace xtu {
 int attn_decode_gqa(const CUtensorMap& tk, const CUtensorMap& tv, const void* q, int q_stride, void* o,
                     int o_stride, const int* q_start, const int* kv_len, const int* block_table, int bt_stride,
                     int B, int max_q_len, int T, int Hq, int Hkv, int D, float scale, int splits, float* ws_o,
-                    float* ws_lse, int* counters, void* status, cudaStream_t s);
+                    float* ws_lse, int* counters, int num_blocks, void* status, cudaStream_t s);
 }  // namespace xtu
 
 using namespace xtu;
@@ -634,7 +634,7 @@ int xtu_paged_attention(const void* q, int q_stride, const void* k_cache, const 
   // decode-shaped GQA steps with few query rows per KV head: the warp-level decode kernel
   if (grid_x == 1 && !v_is_k && D == DV && (D == 64 || D == 128))
     r = attn_decode_gqa(tk, tv, q, q_stride, o, o_stride, q_start, kv_len, block_table, bt_stride, B, max_q_len, T,
-                        Hq, Hkv, D, scale, p.splits, p.ws_o, p.ws_lse, counters, status, s);
+                        Hq, Hkv, D, scale, p.splits, p.ws_o, p.ws_lse, counters, num_blocks, status, s);
   if (r < 0) return r;
   if (r == 1) return 1;   // complete, split merge included
   // decode-shaped steps (all of a sequence's query rows fit one 128-row tile): 64-key

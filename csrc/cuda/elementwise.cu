@@ -212,7 +212,7 @@ __global__ void rope_kv_kernel(__nv_bfloat16* __restrict__ q, __nv_bfloat16* __r
                                const __nv_bfloat16* __restrict__ q_norm_w, const __nv_bfloat16* __restrict__ k_norm_w,
                                float norm_eps, int norm_add_one, const int* __restrict__ slot_mapping,
                                __nv_bfloat16* __restrict__ k_cache, __nv_bfloat16* __restrict__ v_cache,
-                               int block_size) {
+                               int block_size, long long num_slots, XtuStatus* st) {
   griddep_wait();   // launched with PDL: nothing upstream is touched before this
   griddep_launch_dependents();
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -259,7 +259,8 @@ __global__ void rope_kv_kernel(__nv_bfloat16* __restrict__ q, __nv_bfloat16* __r
   __syncwarp();
   if (!is_q && k_cache) {
     const int slot = slot_mapping[t];
-    if (slot >= 0) {
+    // slots past the cache are skipped always, and reported by the bounds-check build
+    if (slot >= 0 && XTU_IN_BOUNDS(slot < num_slots, st, 220, slot) && slot < num_slots) {
       const int hk = h - Hq;
       const int blk = slot / block_size, off = slot - blk * block_size;
       __nv_bfloat16* kc = k_cache + (((size_t)blk * Hk + hk) * block_size + off) * D;
@@ -275,13 +276,14 @@ __global__ void rope_kv_kernel(__nv_bfloat16* __restrict__ q, __nv_bfloat16* __r
 __global__ void kv_write_kernel(const __nv_bfloat16* __restrict__ k, const __nv_bfloat16* __restrict__ v, int T,
                                 int Hk, int D, int Dv, int k_stride, int v_stride, const int* __restrict__ slot_mapping,
                                 __nv_bfloat16* __restrict__ k_cache, __nv_bfloat16* __restrict__ v_cache,
-                                int block_size) {
+                                int block_size, long long num_slots, XtuStatus* st) {
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (gw >= T * Hk) return;
   const int t = gw / Hk, h = gw - t * Hk;
   const int slot = slot_mapping[t];
   if (slot < 0) return;
+  if (!XTU_IN_BOUNDS(slot < num_slots, st, 221, slot) || slot >= num_slots) return;
   const int blk = slot / block_size, off = slot - blk * block_size;
   __nv_bfloat16* kc = k_cache + (((size_t)blk * Hk + h) * block_size + off) * D;
   __nv_bfloat16* vc = v_cache + (((size_t)blk * Hk + h) * block_size + off) * Dv;
@@ -823,9 +825,10 @@ __global__ void argmax_final_kernel(const float* __restrict__ part_v, const int*
 }
 
 __global__ void embed_kernel(const int* __restrict__ ids, const __nv_bfloat16* __restrict__ table, int T, int H,
-                             int vocab, __nv_bfloat16* __restrict__ out) {
+                             int vocab, __nv_bfloat16* __restrict__ out, XtuStatus* st) {
   const int t = blockIdx.x;
   int id = ids[t];
+  if (threadIdx.x == 0) (void)XTU_IN_BOUNDS(id >= 0 && id < vocab, st, 222, id);
   if (id < 0 || id >= vocab) id = 0;
   const uint4* src = reinterpret_cast<const uint4*>(table + (size_t)id * H);
   uint4* dst = reinterpret_cast<uint4*>(out + (size_t)t * H);
@@ -891,7 +894,7 @@ int xtu_tp_sum_rmsnorm(const void* recv, long long slot, int world, int T, int H
 int xtu_rope_kv(void* q, void* k, const void* v, const int* positions, const float* cos_sin, int T, int Hq, int Hk,
                 int D, int Dv, int rot, int neox, int q_stride, int k_stride, int v_stride, const void* q_norm_w,
                 const void* k_norm_w, float norm_eps, int norm_add_one, const int* slot_mapping, void* k_cache,
-                void* v_cache, int block_size, cudaStream_t s) {
+                void* v_cache, int block_size, long long num_slots, void* status, cudaStream_t s) {
   if (T <= 0) return 0;
   if (D % 32 != 0 || D > 512 || rot > D) return -2;
   const int warps = T * (Hq + Hk);
@@ -900,18 +903,21 @@ int xtu_rope_kv(void* q, void* k, const void* v, const int* positions, const flo
   launch_pdl(rope_kv_kernel, dim3(blocks), dim3(threads), 0, s, (__nv_bfloat16*)q, (__nv_bfloat16*)k,
              (const __nv_bfloat16*)v, positions, cos_sin, T, Hq, Hk, D, Dv, rot, neox, q_stride, k_stride, v_stride,
              (const __nv_bfloat16*)q_norm_w, (const __nv_bfloat16*)k_norm_w, norm_eps, norm_add_one, slot_mapping,
-             (__nv_bfloat16*)k_cache, (__nv_bfloat16*)v_cache, block_size);
+             (__nv_bfloat16*)k_cache, (__nv_bfloat16*)v_cache, block_size, num_slots,
+             reinterpret_cast<XtuStatus*>(status));
   return rc_last();
 }
 
 int xtu_kv_write(const void* k, const void* v, int T, int Hk, int D, int Dv, int k_stride, int v_stride,
-                 const int* slot_mapping, void* k_cache, void* v_cache, int block_size, cudaStream_t s) {
+                 const int* slot_mapping, void* k_cache, void* v_cache, int block_size, long long num_slots,
+                 void* status, cudaStream_t s) {
   if (T <= 0) return 0;
   const int warps = T * Hk;
   kv_write_kernel<<<(warps * 32 + 255) / 256, 256, 0, s>>>((const __nv_bfloat16*)k, (const __nv_bfloat16*)v, T, Hk, D,
                                                            Dv, k_stride, v_stride, slot_mapping,
                                                            (__nv_bfloat16*)k_cache, (__nv_bfloat16*)v_cache,
-                                                           block_size);
+                                                           block_size, num_slots,
+                                                           reinterpret_cast<XtuStatus*>(status));
   return rc_last();
 }
 
@@ -1031,10 +1037,12 @@ int xtu_route_split(const int* ids, int n, int lo, int E, const int* slotmap, in
   return rc_last();
 }
 
-int xtu_embed(const int* ids, const void* table, int T, int H, int vocab, void* out, cudaStream_t s) {
+int xtu_embed(const int* ids, const void* table, int T, int H, int vocab, void* out, void* status,
+              cudaStream_t s) {
   if (T <= 0) return 0;
   if (H % 8 != 0) return -2;
-  embed_kernel<<<T, 256, 0, s>>>(ids, (const __nv_bfloat16*)table, T, H, vocab, (__nv_bfloat16*)out);
+  embed_kernel<<<T, 256, 0, s>>>(ids, (const __nv_bfloat16*)table, T, H, vocab, (__nv_bfloat16*)out,
+                                 reinterpret_cast<XtuStatus*>(status));
   return rc_last();
 }
 

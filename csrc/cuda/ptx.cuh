@@ -40,6 +40,17 @@ __device__ __forceinline__ void report_error(XtuStatus* st, uint32_t code, uint3
   }
 }
 
+// Index checks of the bounds-check build (-DXTU_BOUNDS_CHECK, libxtu_cuda_checked.so):
+// a failed check records XTU_ERR_BOUNDS with the site and the index in the status word
+// and evaluates false, so the kernel skips the access instead of trapping.  In the
+// normal build it is `true` and costs nothing.
+#ifdef XTU_BOUNDS_CHECK
+#define XTU_IN_BOUNDS(cond, st, where, extra) \
+  ((cond) || (::xtu::report_error((st), ::xtu::XTU_ERR_BOUNDS, (where), (uint32_t)(extra)), false))
+#else
+#define XTU_IN_BOUNDS(cond, st, where, extra) true
+#endif
+
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

@@ -156,3 +156,35 @@ def test_shm_ep_missing_peer_times_out():
     with pytest.raises(TimeoutError):
         g.allreduce_(torch.ones(64))
     g.close()
+
+
+# ----------------------------------------------------------------------------- sanitizers
+@pytest.mark.parametrize("kind", ["thread", "address,undefined"])
+def test_engine_under_host_sanitizers(kind, tmp_path):
+    """The CPU expert engine and its NUMA work pool built with ThreadSanitizer /
+    AddressSanitizer+UBSan into a host-only driver (tests/cpp/engine_sanitize.cpp) that
+    checks its forward passes against a scalar MoE; any sanitizer report fails."""
+    import shutil
+    import subprocess
+    from pathlib import Path
+    cxx = shutil.which("g++")
+    if cxx is None:
+        pytest.skip("no g++")
+    root = Path(__file__).resolve().parents[1]
+    cpu = root / "csrc" / "cpu"
+    exe = tmp_path / "engine_sanitize"
+    isa = ["-mavx512f", "-mavx512bw", "-mavx512vl", "-mavx512bf16", "-mavx512vnni", "-mavx512vbmi", "-mfma"]
+    cmd = [cxx, "-std=c++17", "-O1", "-g", "-fno-omit-frame-pointer", f"-fsanitize={kind}", "-pthread", *isa,
+           f"-I{cpu}", str(root / "tests" / "cpp" / "engine_sanitize.cpp"), str(cpu / "moe_engine.cpp"),
+           str(cpu / "moe_kernels_avx512.cpp"), str(cpu / "numa_pool.cpp"), "-o", str(exe)]
+    b = subprocess.run(cmd, capture_output=True, text=True, timeout=600)
+    if b.returncode != 0 and "sanitizer" in b.stderr.lower() and "cannot find" in b.stderr.lower():
+        pytest.skip("sanitizer runtime not installed")
+    assert b.returncode == 0, b.stderr[-2000:]
+    env = dict(os.environ, TSAN_OPTIONS="halt_on_error=1", ASAN_OPTIONS="detect_leaks=1",
+               UBSAN_OPTIONS="halt_on_error=1:print_stacktrace=1")
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=600, env=env)
+    out = r.stdout + r.stderr
+    assert r.returncode == 0 and "engine_sanitize: ok" in out, out[-4000:]
+    assert "WARNING: ThreadSanitizer" not in out and "ERROR: AddressSanitizer" not in out, out[-4000:]
+    assert "runtime error" not in out, out[-4000:]

@@ -54,13 +54,14 @@ AVX512_FLAGS = ["-mavx512f", "-mavx512bw", "-mavx512vl", "-mavx512bf16", "-mavx5
 
 
 def _build_lib(name: str, sources: list[Path], compiler: str, flags: list[str], link_flags: list[str],
-               include: list[Path], jobs: int, verbose: bool) -> Path:
-    OBJDIR.mkdir(parents=True, exist_ok=True)
+               include: list[Path], jobs: int, verbose: bool, objdir: Path | None = None) -> Path:
+    objdir = objdir or OBJDIR
+    objdir.mkdir(parents=True, exist_ok=True)
     LIBDIR.mkdir(parents=True, exist_ok=True)
     hdr_time = _newest_header(include)
     objs, todo = [], []
     for src in sources:
-        obj = OBJDIR / (src.parent.name + "_" + src.stem + ".o")
+        obj = objdir / (src.parent.name + "_" + src.stem + ".o")
         objs.append(obj)
         if not obj.exists() or obj.stat().st_mtime < max(src.stat().st_mtime, hdr_time):
             extra = AVX512_FLAGS if "avx512" in src.name else []   # ISA kernels: picked at run time
@@ -85,10 +86,14 @@ def _build_lib(name: str, sources: list[Path], compiler: str, flags: list[str], 
     return out
 
 
-def build_cuda(jobs: int = 8, verbose: bool = False) -> Path:
+def build_cuda(jobs: int = 8, verbose: bool = False, checked: bool = False) -> Path:
+    """The kernel library; ``checked``: the bounds-check build (-DXTU_BOUNDS_CHECK), loaded
+    instead of the normal one when XTU_CHECKED=1."""
     srcs = sorted((CSRC / "cuda").glob("*.cu")) + sorted((CSRC / "comm").glob("*.cu"))
-    return _build_lib("libxtu_cuda.so", srcs, NVCC, NVCC_FLAGS, ["-Xcompiler", "-fPIC", "-lcudart"],
-                      [CSRC / "cuda", CSRC / "comm"], jobs, verbose)
+    name = "libxtu_cuda_checked.so" if checked else "libxtu_cuda.so"
+    flags = NVCC_FLAGS + (["-DXTU_BOUNDS_CHECK"] if checked else [])
+    return _build_lib(name, srcs, NVCC, flags, ["-Xcompiler", "-fPIC", "-lcudart"],
+                      [CSRC / "cuda", CSRC / "comm"], jobs, verbose, OBJDIR / "checked" if checked else OBJDIR)
 
 
 def build_cpu(jobs: int = 8, verbose: bool = False) -> Path:
@@ -101,7 +106,7 @@ def build_cpu(jobs: int = 8, verbose: bool = False) -> Path:
 
 def build_all(verbose: bool = False) -> list[Path]:
     jobs = max(1, min(16, os.cpu_count() or 1))
-    out = [build_cuda(jobs, verbose)]
+    out = [build_cuda(jobs, verbose), build_cuda(jobs, verbose, checked=True)]
     if list((CSRC / "cpu").glob("*.cpp")):
         out.append(build_cpu(jobs, verbose))
     return out

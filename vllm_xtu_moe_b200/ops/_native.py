@@ -19,7 +19,9 @@ from pathlib import Path
 import torch
 
 _LIB_DIR = Path(__file__).resolve().parent.parent / "_lib"
-_CUDA_LIB = _LIB_DIR / "libxtu_cuda.so"
+# XTU_CHECKED=1 loads the bounds-check build (device index checks that record
+# XTU_ERR_BOUNDS and skip the access; see csrc/cuda/ptx.cuh XTU_IN_BOUNDS)
+_CUDA_LIB = _LIB_DIR / ("libxtu_cuda_checked.so" if os.environ.get("XTU_CHECKED", "0") == "1" else "libxtu_cuda.so")
 
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None
@@ -38,13 +40,13 @@ _SIGS: dict[str, list] = {
                          c_float, c_float, c_float, P, P],
     "xtu_rmsnorm": [P, P, P, P, P, c_int, c_int, c_float, c_int, c_int, c_int, P],
     "xtu_rope_kv": [P, P, P, P, P, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, P, P,
-                    c_float, c_int, P, P, P, c_int, P],
-    "xtu_kv_write": [P, P, c_int, c_int, c_int, c_int, c_int, c_int, P, P, P, c_int, P],
+                    c_float, c_int, P, P, P, c_int, ctypes.c_longlong, P, P],
+    "xtu_kv_write": [P, P, c_int, c_int, c_int, c_int, c_int, c_int, P, P, P, c_int, ctypes.c_longlong, P, P],
     "xtu_router_topk": [P, P, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_float, P, P, c_int, P],
     "xtu_moe_permute": [P, P, c_int, c_int, c_int, c_int, P, P, P, P, P, P, c_int, c_int, P, c_int, P],
     "xtu_moe_combine": [P, P, c_int, c_int, c_int, c_int, c_int, P, P, P, P, P],
     "xtu_argmax": [P, c_int, c_int, c_int, c_int, P, P, P, P],
-    "xtu_embed": [P, P, c_int, c_int, c_int, P, P],
+    "xtu_embed": [P, P, c_int, c_int, c_int, P, P, P],
     "xtu_route_split": [P, c_int, c_int, c_int, P, P, P, P, P],
     "xtu_spec_verify": [P, P, P, c_int, c_int, P, P, P],
     "xtu_deltanet_fwd": [P, c_int, c_int, c_int, P, P, P, c_int, c_int, c_int, c_int, c_int, P, P, P, P, P,

@@ -139,6 +139,7 @@ def rope_and_cache(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, positions:
     N.call("xtu_rope_kv", q.data_ptr(), k.data_ptr(), v.data_ptr(), positions.data_ptr(), cos_sin.data_ptr(), T,
            Hq, Hk, D, Dv, rot, int(neox), q.stride(0), k.stride(0), v.stride(0), N.ptr(q_norm_w), N.ptr(k_norm_w),
            float(norm_eps), int(norm_add_one), N.ptr(slot_mapping), N.ptr(k_cache), N.ptr(v_cache), bs,
+           k_cache.shape[0] * bs if k_cache is not None else 0, N.status_buffer(q.device).data_ptr(),
            N.stream_ptr(q.device))
     return q, k
 
@@ -159,7 +160,8 @@ def write_kv(k, v, slot_mapping, k_cache, v_cache):
     T, Hk, D = k.shape
     Dv = v.shape[2]
     N.call("xtu_kv_write", k.data_ptr(), v.data_ptr(), T, Hk, D, Dv, k.stride(0), v.stride(0),
-           slot_mapping.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.shape[2], N.stream_ptr(k.device))
+           slot_mapping.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.shape[2],
+           k_cache.shape[0] * k_cache.shape[2], N.status_buffer(k.device).data_ptr(), N.stream_ptr(k.device))
 
 
 # ---------------------------------------------------------------------------
@@ -172,7 +174,7 @@ def embed(ids: torch.Tensor, table: torch.Tensor, out: torch.Tensor | None = Non
     H = table.shape[1]
     y = out if out is not None else torch.empty(T, H, dtype=table.dtype, device=table.device)
     N.call("xtu_embed", ids.data_ptr(), table.data_ptr(), T, H, table.shape[0], y.data_ptr(),
-           N.stream_ptr(ids.device))
+           N.status_buffer(ids.device).data_ptr(), N.stream_ptr(ids.device))
     return y
 
 
