@@ -61,7 +61,7 @@ __global__ void __launch_bounds__(NT) rmsnorm_kernel(const __nv_bfloat16* __rest
                                                      __nv_bfloat16* __restrict__ residual_out,
                                                      const __nv_bfloat16* __restrict__ w,
                                                      __nv_bfloat16* __restrict__ y, int H, float eps, int add_one,
-                                                     int x_stride, int y_stride) {
+                                                     int x_stride, int y_stride, uint4* __restrict__ y16) {
   griddep_wait();   // launched with PDL: nothing upstream is touched before this
   griddep_launch_dependents();
   extern __shared__ float row[];  // H floats
@@ -108,6 +108,8 @@ __global__ void __launch_bounds__(NT) rmsnorm_kernel(const __nv_bfloat16* __rest
       o[j] = pack_bf16x2(row[i + 2 * j] * inv * w0, row[i + 2 * j + 1] * inv * w1);
     }
     *reinterpret_cast<uint4*>(yr + i) = make_uint4(o[0], o[1], o[2], o[3]);
+    // the fp8-weight GEMVs' activation form (f16 x 2^-8) of the same bf16 values
+    if (y16) y16[((size_t)t * H + i) >> 3] = bf16x8_f16x8_s8(make_uint4(o[0], o[1], o[2], o[3]));
   }
 }
 
@@ -860,8 +862,9 @@ static inline int rc_last(int launched = 1) {
 
 extern "C" {
 
+// y16 (nullable): also write y as f16 x 2^-8 rows [T, H] (the fp8-weight GEMVs' input form)
 int xtu_rmsnorm(const void* x, const void* residual, void* residual_out, const void* w, void* y, int T, int H,
-                float eps, int add_one, int x_stride, int y_stride, cudaStream_t s) {
+                float eps, int add_one, int x_stride, int y_stride, void* y16, cudaStream_t s) {
   if (T <= 0) return 0;
   if (H % 8 != 0) return -2;
   const size_t sm = (size_t)H * sizeof(float);
@@ -870,7 +873,7 @@ int xtu_rmsnorm(const void* x, const void* residual, void* residual_out, const v
   }
   launch_pdl(rmsnorm_kernel<256>, dim3(T), dim3(256), sm, s, (const __nv_bfloat16*)x,
              (const __nv_bfloat16*)residual, (__nv_bfloat16*)residual_out, (const __nv_bfloat16*)w,
-             (__nv_bfloat16*)y, H, eps, add_one, x_stride, y_stride);
+             (__nv_bfloat16*)y, H, eps, add_one, x_stride, y_stride, reinterpret_cast<uint4*>(y16));
   return rc_last();
 }
 

@@ -723,11 +723,14 @@ static const void* gv_convert_x(const void* x, int rows, int K, int stride, floa
 extern "C" {
 
 // y[M, N] = x[M, K] W^T (+ bias). fp8: W e4m3 [N, K] + scales [ceil(N/128), ceil(K/128)]; else W bf16.
+// fp8 bit 2 (value 4): x already holds the f16 x 2^-8 rows (e.g. from xtu_rmsnorm's y16).
 // ws: fp32, GV_WS_PART_FLOATS + GV_WS_X_HALVES / 2 (split-K partials, then the f16 activations
 // of fp8 calls); counters: >= 512 ints, zeroed on first use, left zeroed by every launch.
 int xtu_gemv(const void* W, const float* wscale, int fp8, int N, int K, const void* x, int x_stride, int M,
              const void* bias, void* y, int y_stride, int y_f32, float* ws, int* counters, void* status,
              cudaStream_t s) {
+  const int x_f16s = (fp8 >> 2) & 1;
+  fp8 &= 1;
   if (M <= 0 || N <= 0) return 0;
   if (M > 16 || K % 16 != 0 || ws == nullptr || counters == nullptr) return -2;
   if (K > GV_MAX_KBLK * 128) return -3;
@@ -736,7 +739,7 @@ int xtu_gemv(const void* W, const float* wscale, int fp8, int N, int K, const vo
   const int tiles = (N + 31) / 32;
   const int S = gv_stages_per_tile(K, fp8 != 0);
   int launches = 1;
-  if (fp8) {   // activations -> f16 x 2^-8 once, not once per CTA and stage
+  if (fp8 && !x_f16s) {   // activations -> f16 x 2^-8 once, not once per CTA and stage
     x = gv_convert_x(x, M, K, x_stride, ws, s);
     x_stride = K;
     ++launches;

@@ -48,9 +48,13 @@ class Linear:
 class RMSNorm:
     def __init__(self, weight: torch.Tensor, eps: float, add_one: bool = False):
         self.weight, self.eps, self.add_one = weight, eps, add_one
+        # set when the consumers are fp8-weight decode GEMVs: decode-size calls then also
+        # write the f16 x 2^-8 copy those GEMVs read (attached as y.xtu_f16s)
+        self.emit_f16s = False
 
     def __call__(self, x, residual=None):
-        return B.rmsnorm(x, self.weight, self.eps, residual=residual, add_one=self.add_one)
+        f16s = self.emit_f16s and x.is_cuda and x.dim() == 2 and x.shape[0] <= G.GEMV_MAX_M
+        return B.rmsnorm(x, self.weight, self.eps, residual=residual, add_one=self.add_one, f16s=f16s)
 
     def tensors(self):
         return [self.weight]

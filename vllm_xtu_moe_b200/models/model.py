@@ -83,6 +83,21 @@ class MoETransformer:
         self.tracer = None
         self.rope = B.rope_cache(cfg.rot_dim, min(cfg.max_position, 1 << 18), cfg.rope_theta, self.device,
                                  cfg.rope_scaling)
+        self.wire_activation_forms()
+
+    def wire_activation_forms(self) -> None:
+        """Let each RMSNorm whose consumers are fp8-weight decode GEMVs also write their
+        f16 x 2^-8 input rows (the GEMVs then skip their conversion pre-pass)."""
+        def fp8_linear(lin) -> bool:
+            return lin is not None and getattr(lin, "scale", None) is not None
+
+        for l in list(self.layers) + [m.layer for m in self.mtp]:
+            l.attn_norm.emit_f16s = fp8_linear(getattr(l.attn, "qkv", None))
+            mlp = l.mlp
+            if isinstance(mlp, MoEBlock):
+                l.mlp_norm.emit_f16s = mlp.experts is not None and mlp.experts.fmt == "fp8"
+            else:
+                l.mlp_norm.emit_f16s = fp8_linear(getattr(mlp, "gate_up", None))
 
     # ------------------------------------------------------------------
     def embed(self, ids: torch.Tensor) -> torch.Tensor:

@@ -38,7 +38,7 @@ _SIGS: dict[str, list] = {
     "xtu_build_mtiles": [P, c_int, P, P, c_int, P],
     "xtu_grouped_gemm": [P, P, P, c_int, P, c_int, c_int, c_int, c_int, c_int, P, P, c_int, c_int, P, P,
                          c_float, c_float, c_float, P, P],
-    "xtu_rmsnorm": [P, P, P, P, P, c_int, c_int, c_float, c_int, c_int, c_int, P],
+    "xtu_rmsnorm": [P, P, P, P, P, c_int, c_int, c_float, c_int, c_int, c_int, P, P],
     "xtu_rope_kv": [P, P, P, P, P, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, P, P,
                     c_float, c_int, P, P, P, c_int, ctypes.c_longlong, P, P],
     "xtu_kv_write": [P, P, c_int, c_int, c_int, c_int, c_int, c_int, P, P, P, c_int, ctypes.c_longlong, P, P],

@@ -28,8 +28,11 @@ def rmsnorm_ref(x, w, eps, residual=None, add_one=False):
 
 
 def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-6, residual: torch.Tensor | None = None,
-            add_one: bool = False, out: torch.Tensor | None = None):
-    """y = RMSNorm(x [+ residual]) * w.  With a residual, returns (y, x + residual)."""
+            add_one: bool = False, out: torch.Tensor | None = None, f16s: bool = False):
+    """y = RMSNorm(x [+ residual]) * w.  With a residual, returns (y, x + residual).
+
+    ``f16s``: also produce y as f16 x 2^-8 (the input form of the fp8-weight decode GEMVs),
+    attached to the returned y as ``y.xtu_f16s`` so those GEMVs skip their conversion."""
     if not x.is_cuda:
         y, r = rmsnorm_ref(x, w, eps, residual, add_one)
         return (y, r) if residual is not None else y
@@ -43,9 +46,12 @@ def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-6, residual: torch
         residual = residual.reshape(-1, H)
         assert residual.is_contiguous()
         r_out = torch.empty_like(residual)
+    y16 = torch.empty(T, H, dtype=torch.float16, device=x.device) if f16s and H % 8 == 0 else None
     N.call("xtu_rmsnorm", x2.data_ptr(), N.ptr(residual), N.ptr(r_out), w.data_ptr(), y.data_ptr(), T, H,
-           float(eps), int(add_one), x2.stride(0), y.stride(0), N.stream_ptr(x.device))
+           float(eps), int(add_one), x2.stride(0), y.stride(0), N.ptr(y16), N.stream_ptr(x.device))
     y = y.reshape(x.shape)
+    if y16 is not None and y.dim() == 2 and y.stride(0) == H:
+        y.xtu_f16s = y16
     if residual is not None:
         return y, r_out.reshape(x.shape)
     return y

@@ -63,14 +63,21 @@ GEMV_MAX_M = 16
 
 
 def gemv(x: torch.Tensor, weight: torch.Tensor, scale: torch.Tensor | None = None, bias: torch.Tensor | None = None,
-         out_dtype: torch.dtype = torch.bfloat16, out: torch.Tensor | None = None) -> torch.Tensor:
-    """Decode-size y[M<=16, N] = x W^T (+ bias) streaming W (bf16 or e4m3 + block scales)."""
+         out_dtype: torch.dtype = torch.bfloat16, out: torch.Tensor | None = None,
+         x16: torch.Tensor | None = None) -> torch.Tensor:
+    """Decode-size y[M<=16, N] = x W^T (+ bias) streaming W (bf16 or e4m3 + block scales).
+    ``x16``: the same rows already as f16 x 2^-8 (fp8 weights then skip their conversion)."""
     x = tma_rows(x)
     M, K = x.shape
+    flags = int(scale is not None)
+    xp, xs = x.data_ptr(), x.stride(0)
+    if x16 is not None and scale is not None and x16.shape == (M, K) and x16.is_contiguous():
+        flags |= 4
+        xp, xs = x16.data_ptr(), K
     Nn = weight.shape[0]
     y = out if out is not None else torch.empty(M, Nn, dtype=out_dtype, device=x.device)
     ws, cnt = _gemv_split_ws(x.device)
-    N.call("xtu_gemv", weight.data_ptr(), N.ptr(scale), int(scale is not None), Nn, K, x.data_ptr(), x.stride(0), M,
+    N.call("xtu_gemv", weight.data_ptr(), N.ptr(scale), flags, Nn, K, xp, xs, M,
            N.ptr(bias), y.data_ptr(), y.stride(0), int(y.dtype == torch.float32), ws.data_ptr(), cnt.data_ptr(),
            N.status_buffer(x.device).data_ptr(), N.stream_ptr(x.device))
     return y
@@ -118,6 +125,7 @@ def linear(x: torch.Tensor, weight: torch.Tensor, scale: torch.Tensor | None = N
     GPU dispatch: <= 16 rows -> weight-streaming GEMV (bias fused); more rows ->
     tcgen05 GEMM."""
     shp = x.shape
+    x16 = getattr(x, "xtu_f16s", None)   # f16 x 2^-8 copy written by the producing RMSNorm
     x2 = x.reshape(-1, shp[-1])
     if x2.shape[0] == 0:
         return x.new_empty(*shp[:-1], weight.shape[0], dtype=out_dtype)
@@ -125,7 +133,7 @@ def linear(x: torch.Tensor, weight: torch.Tensor, scale: torch.Tensor | None = N
         x2 = x2.contiguous()
     K = x2.shape[1]
     if x2.is_cuda and x2.shape[0] <= GEMV_MAX_M and K % 64 == 0 and x2.dtype == torch.bfloat16:
-        y = gemv(x2, weight, scale, bias, out_dtype)
+        y = gemv(x2, weight, scale, bias, out_dtype, x16=x16)
         return y.reshape(*shp[:-1], weight.shape[0])
     if scale is None:
         y = gemm_bf16(x2, weight, out_dtype=out_dtype)

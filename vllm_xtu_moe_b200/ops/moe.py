@@ -159,12 +159,15 @@ def moe_experts_partial(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tenso
         # one-CTA permute (no row gather): the gate/up GEMV reads the T tokens directly
         # and keeps each expert's own columns through ws.tokrow
         xt = G.tma_rows(x)
+        x16 = getattr(x, "xtu_f16s", None)   # f16 x 2^-8 rows from the producing RMSNorm
+        use16 = fp8 and x16 is not None and x16.shape == x.shape and x16.is_contiguous()
         if not permuted:
             N.call("xtu_moe_permute_decode", ids.data_ptr(), weights.data_ptr(), T, K, lo, lo + E, ws.seg.data_ptr(),
                    ws.perm_slot.data_ptr(), ws.perm_w.data_ptr(), ws.active.data_ptr(), ws.tokrow.data_ptr(), s)
         N.call("xtu_moe_gemv", experts.w13.data_ptr(), N.ptr(experts.s13 if fp8 else None),
-               experts.w2.data_ptr(), N.ptr(experts.s2 if fp8 else None), int(fp8), E, H, I, xt.data_ptr(), 0,
-               xt.stride(0), ws.tokrow.data_ptr(), T, ws.seg.data_ptr(), ws.perm_slot.data_ptr(),
+               experts.w2.data_ptr(), N.ptr(experts.s2 if fp8 else None), int(fp8), E, H, I,
+               x16.data_ptr() if use16 else xt.data_ptr(), int(use16), H if use16 else xt.stride(0),
+               ws.tokrow.data_ptr(), T, ws.seg.data_ptr(), ws.perm_slot.data_ptr(),
                ws.perm_w.data_ptr(), ws.h.data_ptr(), ws.slots.data_ptr(), T, min(E, T * K), n,
                ws.active.data_ptr(), 1, float(act_limit), float(act_alpha), float(act_beta),
                *_shared_ptrs(shared_mlp), n, _gv_ws(x.device), N.status_buffer(x.device).data_ptr(), s)
@@ -330,7 +333,10 @@ def _gv_ws(device):
 def dense_swiglu_gemv(x: torch.Tensor, w13: torch.Tensor, s13, w2: torch.Tensor, s2, limit: float,
                       cache: dict) -> torch.Tensor:
     """Decode-size SwiGLU MLP (gate/up interleaved in 128-row blocks) as a one-expert grouped GEMV."""
+    x16 = getattr(x, "xtu_f16s", None)
     x = G.tma_rows(x)
+    if x16 is not None:
+        x.xtu_f16s = x16
     T, H = x.shape
     I = w13.shape[0] // 2
     key = ("gemv", x.device, T, I)
@@ -344,8 +350,11 @@ def dense_swiglu_gemv(x: torch.Tensor, w13: torch.Tensor, s13, w2: torch.Tensor,
                   active=torch.tensor([1, 0], dtype=torch.int32, device=d))   # one expert, always active
         cache[key] = st
     y = torch.empty(T, w2.shape[0], dtype=torch.bfloat16, device=x.device)
+    x16 = getattr(x, "xtu_f16s", None)   # f16 x 2^-8 rows from the producing RMSNorm
+    use16 = s13 is not None and x16 is not None and x16.shape == x.shape and x16.is_contiguous()
     N.call("xtu_moe_gemv", w13.data_ptr(), N.ptr(s13), w2.data_ptr(), N.ptr(s2), int(s13 is not None), 1, H, I,
-           x.data_ptr(), 0, x.stride(0), None, 0, st["seg"].data_ptr(), st["slot"].data_ptr(), st["w"].data_ptr(), st["h"].data_ptr(),
+           x16.data_ptr() if use16 else x.data_ptr(), int(use16), H if use16 else x.stride(0), None, 0,
+           st["seg"].data_ptr(), st["slot"].data_ptr(), st["w"].data_ptr(), st["h"].data_ptr(),
            y.data_ptr(), T, 1, T, st["active"].data_ptr(), 1, float(limit), 1.0, 0.0, None, None, None, None, 0,
            _gv_ws(x.device),
            N.status_buffer(x.device).data_ptr(), N.stream_ptr(x.device))
