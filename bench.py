@@ -118,6 +118,20 @@ def reference_arm(args):
         print(json.dumps(line), flush=True)
 
 
+def copy_rate(seqs: list[list[int]], n: int = 8) -> float:
+    """Benchmark health ("deg"): the share of n-grams of the generated tokens that repeat an
+    earlier n-gram of the same sequence (0 = no loops, 1 = a loop from the start)."""
+    rep = tot = 0
+    for s in seqs:
+        seen = set()
+        for i in range(len(s) - n + 1):
+            g = tuple(s[i:i + n])
+            rep += g in seen
+            seen.add(g)
+            tot += 1
+    return rep / tot if tot else 0.0
+
+
 def main():
     args = parse()
     if os.environ.get("XTU_BENCH_WATCHDOG"):
@@ -220,6 +234,7 @@ def main():
 
     # ---- e2e through the public API (host clock, includes H2D of prompts and D2H of tokens)
     e2e = None
+    deg = None
     if not args.no_e2e:
         e2e_dec, e2e_pre = [], []
         for _ in range(max(1, args.steps)):
@@ -229,6 +244,7 @@ def main():
             outs = llm.generate(ps, SamplingParams(max_tokens=O, ignore_eos=True))
             t_b = time.perf_counter()
             ttft = max(o.ttft_s for o in outs)
+            deg = copy_rate([o.token_ids for o in outs])
             e2e_pre.append(C * P / ttft)
             e2e_dec.append(C * (O - 1) / max(1e-9, (t_b - t_a) - ttft))
         e2e = {"value": statistics.median(e2e_dec) * world, "unit": "tok/s",
@@ -256,6 +272,7 @@ def main():
             "dtype": "bf16", "data": "synthetic (uniform random token ids, random-init weights)",
             "prefill_tok_s": round(prefill_tok_s, 1),
             "prefill_vs_baseline": round(prefill_tok_s / BASELINE_PREFILL[C], 3) if C in BASELINE_PREFILL else None,
+            "deg": None if deg is None else round(deg, 4),
             "decode_step_ms": round(mean_dec / max(1.0, avg_dsteps), 3),
             "config": {"model": cfg.name + " (GLM-4.5-Air-style, BASELINE config 4)", "global_batch": world * C,
                        "concurrency_per_gpu": C, "seq_len": P, "output_len": O, "parallelism": f"dp{world}",
