@@ -297,3 +297,31 @@ def test_hybrid_path_graph_replay_matches_eager():
     assert torch.equal(out, eager)
     assert blk.executor.bridge.stats()["runs"] >= 5
     del g
+
+
+def test_tiny_mixtral_on_cpu_engine_greedy_matches_eager():
+    """The tiny Mixtral workload with every expert on the C++ CPU engine (no GPU): 2
+    layers, hidden 256, 4 heads / 2 KV heads at head_dim 64, 8 experts top-2, SwiGLU
+    intermediate 512, vocab 1024, bf16 weights N(0, 0.02) seed 0; two 64-token prompts,
+    32 greedy tokens, token for token against the PyTorch eager model."""
+    from vllm_xtu_moe_b200.engine import LLM, SamplingParams
+    from vllm_xtu_moe_b200.engine.runner import RunnerConfig
+    from vllm_xtu_moe_b200.models.model import build_model
+    from vllm_xtu_moe_b200.tiering.executor import TieredExperts
+    cfg = get_preset("tiny-mixtral")
+    ref = build_model(cfg, device="cpu", seed=0, std=0.02)
+    tier = TieredExperts(cfg, device="cpu", resident_layers=set())
+    m = build_model(cfg, device="cpu", seed=0, std=0.02, expert_sink=tier.expert_sink)
+    tier.attach(m)
+    assert all(l.mlp.experts is None and l.mlp.executor is not None for l in m.layers)
+    g = torch.Generator().manual_seed(0)
+    prompts = [torch.randint(0, 1024, (64,), generator=g).tolist() for _ in range(2)]
+    sp = SamplingParams(max_tokens=32)
+
+    def rc():
+        return RunnerConfig(block_size=16, max_seqs=2, max_model_len=128, max_batched_tokens=256,
+                            use_cuda_graph=False)
+    want = [o.token_ids for o in LLM(ref, device="cpu", runner_config=rc()).generate(prompts, sp)]
+    got = [o.token_ids for o in LLM(m, device="cpu", runner_config=rc()).generate(prompts, sp)]
+    tier.shutdown()
+    assert got == want
