@@ -63,7 +63,8 @@ def main(argv=None):
         _set_mode(model, red)
         graphs = mode != "nccl"
         rc = RunnerConfig(block_size=64, max_seqs=C, max_model_len=P + a.steps + 64, max_batched_tokens=16384,
-                          use_cuda_graph=graphs, graph_batch_sizes=(1, 2, 4, 8, 16))
+                          use_cuda_graph=graphs, graph_batch_sizes=(1, 2, 4, 8, 16),
+                          num_blocks=C * ((P + a.steps + 128) // 64 + 2))
         llm = LLM(model, device=str(dev), runner_config=rc)
         for p in prompts:
             llm.add_request(p, SamplingParams(max_tokens=a.steps + 8, ignore_eos=True))
