@@ -237,6 +237,8 @@ def main():
     deg = None
     if not args.no_e2e:
         e2e_dec, e2e_pre = [], []
+        r = llm.runner
+        b_in0, b_out0, st0 = r.h2d_bytes, r.d2h_bytes, r.steps
         for _ in range(max(1, args.steps)):
             ps = prompts()
             torch.cuda.synchronize()
@@ -247,10 +249,13 @@ def main():
             deg = copy_rate([o.token_ids for o in outs])
             e2e_pre.append(C * P / ttft)
             e2e_dec.append(C * (O - 1) / max(1e-9, (t_b - t_a) - ttft))
+        n_st = max(1, r.steps - st0)
         e2e = {"value": statistics.median(e2e_dec) * world, "unit": "tok/s",
                "prefill_tok_s": statistics.median(e2e_pre) * world,
-               "h2d_bytes_per_step": C * P * 4 + C * O * 64,
-               "d2h_bytes_per_step": C * O * 4}
+               # counted from the pinned H2D copies (token ids, positions, slots, block tables)
+               # and the D2H token reads of the engine steps inside the e2e window
+               "h2d_bytes_per_step": round((r.h2d_bytes - b_in0) / n_st),
+               "d2h_bytes_per_step": round((r.d2h_bytes - b_out0) / n_st)}
 
     # ---- aggregate over ranks: value = sum of tokens / max time
     mean_pre = sum(pre_ms) / len(pre_ms)

@@ -116,6 +116,8 @@ class LLM:
             return done
         tok, extra = self.runner.execute(plan)
         toks = tok.tolist() if tok is not None else []
+        if tok is not None:
+            self.runner.d2h_bytes += tok.numel() * tok.element_size()
         now = time.perf_counter()
         if _DEBUG_STEPS:
             print(f"[xtu-step] {'decode' if plan.is_decode else 'prefill'} seqs={len(plan.chunks)} "

@@ -56,6 +56,10 @@ class ModelRunner:
         model.prepare_workspaces(max_rows)
         self.graphs: dict[int, tuple] = {}
         self._static = None
+        # bytes of the per-step host<->device copies (pinned H2D metadata and ids, D2H tokens)
+        self.h2d_bytes = 0
+        self.d2h_bytes = 0
+        self.steps = 0
 
     # ------------------------------------------------------------------
     def _auto_blocks(self) -> int:
@@ -111,8 +115,14 @@ class ModelRunner:
 
         def T(x, dt=torch.int32):
             t = torch.tensor(x, dtype=dt)
-            return t.pin_memory().to(d, non_blocking=True) if nb else t
+            if not nb:
+                return t
+            self.h2d_bytes += t.numel() * t.element_size()
+            return t.pin_memory().to(d, non_blocking=True)
 
+        if nb:
+            self.h2d_bytes += bt.numel() * bt.element_size()
+        self.steps += 1
         meta = AttnMetadata(num_seqs=Bn, q_start=T(q_start), kv_len=T(kv_len),
                             block_table=bt.pin_memory().to(d, non_blocking=True) if nb else bt,
                             slot_mapping=T(slots), positions=T(pos), max_q_len=max(q_start[i + 1] - q_start[i] for i in range(Bn)),
