@@ -22,6 +22,7 @@ from .ops import attention as A
 from .ops import basic as B
 from .ops import gemm as G
 from .ops import moe as M
+from .ops import _native as N_
 from .ops.attention import AttnMetadata
 from .ops.quant import quant_fp8_block
 from .ops.router import router_topk, zipf_bias
@@ -239,6 +240,71 @@ def bench_rmsnorm(T=16384, H=4096, iters=20) -> dict:
     return _report("rmsnorm_residual", dict(T=T, H=H), ms, 4 * T * H * 2, 0)
 
 
+def _one_rank_group():
+    """A 1-rank process group (NCCL) so the fused multi-GPU kernels run on one GPU: their
+    peer stores then land in this GPU's own receive buffers."""
+    import os
+    import socket
+    import torch.distributed as dist
+    if not dist.is_initialized():
+        sk = socket.socket()
+        sk.bind(("127.0.0.1", 0))
+        port = sk.getsockname()[1]
+        sk.close()
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("nccl", rank=0, world_size=1, device_id=torch.device("cuda", 0))
+
+
+def bench_tp_fused(M_=4, N=4096, Kd=6144, iters=20) -> dict:
+    """TP decode output projection (GLM-4.5-Air o_proj slice at TP=2): the fused GEMV whose
+    epilogue scatters the partial rows to the ranks' receive buffers, then the sum +
+    residual + RMSNorm kernel that consumes them."""
+    from .models.layers import Linear, RMSNorm
+    from .parallel.tp import TPReducer
+    _one_rank_group()
+    red = TPReducer(16, N, device=torch.device("cuda", 0), mode="fused")
+    w, s = quant_fp8_block(torch.randn(N, Kd, device="cuda") * 0.02)
+    lin = Linear(w, s)
+    norm = RMSNorm(torch.ones(N, device="cuda", dtype=torch.bfloat16), 1e-5)
+    x = torch.randn(M_, Kd, device="cuda").to(torch.bfloat16)
+    res = torch.randn(M_, N, device="cuda").to(torch.bfloat16)
+    fn = lambda: red.linear_scatter(x, lin).finish(res, norm)
+    ms = time_fn(fn, iters)
+    N_.check_status()
+    nbytes = w.numel() + M_ * (Kd + 3 * N) * 2
+    out = _report("tp_gemv_scatter_sum_rmsnorm", dict(M=M_, N=N, K=Kd, world=1), ms, nbytes, 2 * M_ * N * Kd)
+    red.close()
+    return out
+
+
+def bench_ep_fused(T=256, E=32, K=8, H=7168, I=2048, iters=10) -> dict:
+    """The expert-parallel MoE layer (dispatch -> grouped GEMM with SwiGLU -> down GEMM whose
+    epilogue stores the weighted rows to their source rank -> combine) on one rank."""
+    from .ops.router import router_topk, zipf_bias
+    from .parallel.comm import PeerGroup
+    from .parallel.ep import EPMoE
+    _one_rank_group()
+    d = torch.device("cuda", 0)
+    q13, s13 = quant_fp8_block(torch.randn(E, 2 * I, H, device=d) * 0.02)
+    q2, s2 = quant_fp8_block(torch.randn(E, H, I, device=d) * 0.02)
+    ex = M.prepare_experts("fp8", q13, q2, s13, s2)
+    del q13, q2
+    torch.cuda.empty_cache()   # keep only the layer's buffers on the device
+    pg = PeerGroup(EPMoE.heap_bytes(E, K, H, T, 1), device=d)
+    layer = EPMoE(ex, E, K, max_tokens=T, pg=pg)
+    x = torch.randn(T, H, device=d).to(torch.bfloat16)
+    ids, w = router_topk(torch.randn(T, E, device=d) + zipf_bias(E, 1.1, seed=7).to(d), K, "softmax")
+    fn = lambda: layer.forward(x, ids, w)
+    ms = time_fn(fn, iters)
+    N_.check_status()
+    active = torch.unique(ids).numel()
+    nbytes = 3 * H * I * active + T * K * H * 2 * 2
+    out = _report("ep_moe_layer_fused", dict(T=T, E=E, K=K, H=H, I=I, world=1, active_experts=active), ms, nbytes,
+                  2 * T * K * 3 * H * I)
+    pg.close()
+    return out
+
+
 OPS = {
     "moe_prefill_fp8": lambda a: bench_moe(a.tokens, "fp8"),
     "moe_prefill_bf16": lambda a: bench_moe(a.tokens, "bf16"),
@@ -251,6 +317,8 @@ OPS = {
     "mla_decode": lambda a: bench_mla_decode(),
     "attention_prefill": lambda a: bench_attn_prefill(min(a.tokens, 16384)),
     "rmsnorm": lambda a: bench_rmsnorm(),
+    "tp_fused": lambda a: bench_tp_fused(),
+    "ep_fused": lambda a: bench_ep_fused(),
     "deltanet_prefill": lambda a: bench_deltanet(),
 }
 
