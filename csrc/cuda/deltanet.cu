@@ -15,8 +15,8 @@
 //                      so a token costs three 32-term dot products and one 32-term update
 //                      per lane; c is folded back into the registers before it underflows.
 //
-// Replaces the FLA chunked kernels the reference's vLLM patches run for these layers
-// (SURVEY kernel row W19); the numerics oracle is models/deltanet.py:_delta_rule_ref.
+// Replaces the FLA chunked kernels the reference's vLLM patches run for these layers;
+// the numerics oracle is models/deltanet.py:_delta_rule_ref.
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <cstdint>

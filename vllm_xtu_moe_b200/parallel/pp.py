@@ -12,7 +12,7 @@ stay in step.
 non-blocking sends, so stage r computes micro-batch i + 1 while micro-batch i is in
 flight to stage r + 1 (the GPipe forward schedule).
 
-The reference serves with PP = 1 everywhere (SURVEY row W21 has no reference kernel);
+The reference serves with PP = 1 everywhere and has no pipeline kernel of its own;
 this is the framework's own stage runtime over the same engine contract as
 :class:`models.model.MoETransformer` (``forward`` / ``logits`` / cache allocation).
 """

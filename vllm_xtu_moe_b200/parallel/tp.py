@@ -210,8 +210,8 @@ class TPWeightFactory:
 class TPReducer:
     """Sum of the ranks' partial [T, H] outputs (P2P one-shot / two-shot, or NCCL).
 
-    mode "fused" adds the decode form of the row-parallel output projection (SURVEY row
-    W10): the GEMV's epilogue stores each rank's partial rows straight into every rank's
+    mode "fused" adds the decode form of the row-parallel output projection (the
+    GEMM -> reduce-scatter fusion at decode sizes): the GEMV's epilogue stores each rank's partial rows straight into every rank's
     receive buffer over NVLink and flags them (``xtu_gemv_tp``); the next RMSNorm sums
     them in rank order, adds the residual and normalises (``xtu_tp_sum_rmsnorm``), so no
     separate all-reduce or copy runs.  Larger steps use the one-shot / two-shot kernels."""
