@@ -22,6 +22,7 @@ enum : uint32_t {
   XTU_ERR_PEER_TIMEOUT = 2,    // a wait on another GPU's flag ran out of time
   XTU_ERR_HOST_TIMEOUT = 3,    // a wait on a host-written flag ran out of time
   XTU_ERR_BOUNDS = 4,          // a bounds check in a debug build tripped
+  XTU_ERR_PROTOCOL = 5,        // a host-bridge request posted into a busy slot, or read back unposted
 };
 
 struct XtuStatus {

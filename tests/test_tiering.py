@@ -7,6 +7,7 @@ import pytest
 import torch
 
 from vllm_xtu_moe_b200.models.config import get_preset, scaled_down
+from vllm_xtu_moe_b200.ops import _native as N
 from vllm_xtu_moe_b200.ops import moe as M
 from vllm_xtu_moe_b200.ops.quant import quant_fp8_block
 from vllm_xtu_moe_b200.tiering import planner as PL
@@ -325,3 +326,200 @@ def test_tiny_mixtral_on_cpu_engine_greedy_matches_eager():
     got = [o.token_ids for o in LLM(m, device="cpu", runner_config=rc()).generate(prompts, sp)]
     tier.shutdown()
     assert got == want
+
+
+# ----------------------------------------------------------------------------- async bridge + expert deferral
+def _defer_case(device, fmt="bf16", layers=3, T=4, pool=None, defer=True):
+    from vllm_xtu_moe_b200.config import EngineConfig
+    from vllm_xtu_moe_b200.tiering.executor import TieredExperts
+    E, H, I, K = 32, 512, 256, 4
+    cfg = _mini(fmt).replace(num_experts=E, top_k=K, hidden_size=H, moe_intermediate=I, num_layers=layers)
+    ec = EngineConfig(moe_defer=defer, moe_async=True, moe_async_timeout_ms=5000)
+    tier = TieredExperts(cfg, device=device, engine_config=ec, resident_layers=set(), pool_experts=pool or {},
+                         ring=False, max_tokens=1024)
+    _live.append(tier)
+    raws = [_raw_gpu(fmt, E, H, I, 5 + l) for l in range(layers)]
+    for l in range(layers):
+        assert tier.expert_sink(l, raws[l]) is None
+
+    def blk():
+        b = type("Blk", (), {"experts": None, "executor": None, "cfg": cfg})()
+        return b
+
+    blocks = [blk() for _ in range(layers)]
+
+    class Mdl:
+        pass
+
+    Mdl.layers = [type("L", (), {"mlp": b})() for b in blocks]
+    Mdl.mtp = []
+    tier.attach(Mdl)
+    g = torch.Generator().manual_seed(9)
+    xs = [(torch.randn(T, H, generator=g) * 0.5).to(torch.bfloat16) for _ in range(layers)]
+    shs = [(torch.randn(T, H, generator=g) * 0.1).to(torch.bfloat16) for _ in range(layers)]
+    routes = [_routes(T, E, K, 20 + l) for l in range(layers)]
+    return tier, cfg, raws, blocks, xs, shs, routes
+
+
+def _deferred_expectation(routed, shs):
+    """out_0 = sh_0; out_l = sh_l + routed_{l-1}; the last also adds its own routed part."""
+    L = len(routed)
+    exp = []
+    for l in range(L):
+        e = shs[l].float() + (routed[l - 1] if l > 0 else 0)
+        if l == L - 1:
+            e = e + routed[l]
+        exp.append(e)
+    return exp
+
+
+def test_deferral_on_host_tensors_follows_the_layer_shift():
+    """Host-tensor path of expert deferral: layer l's CPU-expert result lands in layer l+1."""
+    tier, cfg, raws, blocks, xs, shs, routes = _defer_case("cpu")
+    outs = [b.executor(b, xs[l], routes[l][0], routes[l][1], shs[l]) for l, b in enumerate(blocks)]
+    routed = [tier.executors[l].engine.forward(xs[l], routes[l][0], routes[l][1]) for l in range(len(blocks))]
+    for l, (o, e) in enumerate(zip(outs, _deferred_expectation(routed, shs))):
+        ok, err = _close(o, e)
+        assert ok, (l, err)
+    assert tier.cpu_pending is None
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("defer", [False, True])
+def test_async_bridge_layers_match_resident(defer):
+    """The asynchronous bridge (post kernel -> worker thread -> bounded wait kernel) over
+    three layers, with and without deferral, against all-GPU MoE layers."""
+    tier, cfg, raws, blocks, xs, shs, routes = _defer_case("cuda", defer=defer)
+    xs = [x.cuda() for x in xs]
+    shs = [s.cuda() for s in shs]
+    routes = [(i.cuda(), w.cuda()) for i, w in routes]
+    outs = [b.executor(b, xs[l], *routes[l], shs[l]) for l, b in enumerate(blocks)]
+    torch.cuda.synchronize()
+    N.check_status()
+    routed = []
+    for l, r in enumerate(raws):
+        res = M.prepare_experts(r["fmt"], r["w13"].cuda(), r["w2"].cuda())
+        routed.append(M.fused_moe(xs[l], *routes[l], res).float())
+    exp = (_deferred_expectation(routed, shs) if defer else [shs[l].float() + routed[l] for l in range(len(raws))])
+    for l, (o, e) in enumerate(zip(outs, exp)):
+        ok, err = _close(o, e)
+        assert ok, (l, err)
+    st = tier.stats()
+    assert st["deferred"] == (2 if defer else 0) and st["async"] == (1 if defer else 3)
+    assert tier.defer_pending is None
+    bs = tier._async_bridge.stats()
+    assert bs["runs"] == 3 and bs["req"] == 3 and bs["done"] == 3
+
+
+@pytest.mark.gpu
+def test_async_bridge_with_pool_and_graph_replay():
+    """Deferral with a hot-expert pool in every layer, captured once and replayed: the
+    request numbers live on the device, so replays equal the eager run bit for bit."""
+    pool = {l: [0, 3, 5, 7, 11] for l in range(3)}
+    tier, cfg, raws, blocks, xs, shs, routes = _defer_case("cuda", fmt="fp8", pool=pool)
+    xs = [x.cuda() for x in xs]
+    shs = [s.cuda() for s in shs]
+    routes = [(i.cuda(), w.cuda()) for i, w in routes]
+
+    def run():
+        return [b.executor(b, xs[l], *routes[l], shs[l]) for l, b in enumerate(blocks)]
+
+    eager = [o.clone() for o in run()]
+    torch.cuda.synchronize()
+    N.check_status()
+    routed = []
+    for l, r in enumerate(raws):
+        res = M.prepare_experts("fp8", r["w13"].cuda(), r["w2"].cuda(), r["s13"].cuda(), r["s2"].cuda())
+        routed.append(M.fused_moe(xs[l], *routes[l], res).float())
+    for l, (o, e) in enumerate(zip(eager, _deferred_expectation(routed, shs))):
+        ok, err = _close(o, e)
+        assert ok, (l, err)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        run()
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        outs = run()
+    for _ in range(3):
+        for o in outs:
+            o.zero_()
+        g.replay()
+    torch.cuda.synchronize()
+    N.check_status()
+    for o, e in zip(outs, eager):
+        assert torch.equal(o, e)
+    assert tier._async_bridge.stats()["done"] == 3 + 3 + 3 * 3   # eager, warm-up, three replays
+    del g
+
+
+@pytest.mark.gpu
+def test_async_bridge_wait_times_out_and_recovers():
+    """A wait whose request nobody computes (worker paused) ends after its time limit with
+    a host-timeout status, the context stays usable, and a reset brings the bridge back."""
+    tier, cfg, raws, blocks, xs, shs, routes = _defer_case("cuda", layers=1, defer=False)
+    ex = tier.executors[0]
+    br = tier.async_bridge(cfg.top_k)
+    x, (ids, w) = xs[0].cuda(), routes[0]
+    ids, w = ids.cuda(), w.cuda()
+    out = torch.zeros(x.shape[0], cfg.hidden_size, device="cuda")
+    br.pause(True)
+    br.timeout_ns = 200_000_000
+    br.post(x, ids, w, engine=ex.engine_index)
+    br.wait(out)
+    torch.cuda.synchronize()
+    with pytest.raises(RuntimeError, match="host flag wait timed out"):
+        N.check_status()
+    br.reset()
+    br.timeout_ns = 5_000_000_000
+    br.post(x, ids, w, engine=ex.engine_index)
+    br.wait(out)
+    torch.cuda.synchronize()
+    N.check_status()
+    ref = ex.engine.forward(x.cpu(), ids.cpu(), w.cpu())
+    ok, err = _close(out.cpu(), ref)
+    assert ok, err
+
+
+def _tiny_tiered_llm_tokens(ec, graphs: bool):
+    from vllm_xtu_moe_b200.engine import LLM, SamplingParams
+    from vllm_xtu_moe_b200.engine.runner import RunnerConfig
+    from vllm_xtu_moe_b200.models.model import build_model
+    from vllm_xtu_moe_b200.tiering.executor import TieredExperts
+    cfg = get_preset("tiny-mixtral")
+    tier = TieredExperts(cfg, device="cuda", engine_config=ec, resident_layers=set(), ring=False)
+    _live.append(tier)
+    m = build_model(cfg, device="cuda", seed=0, std=0.02, expert_sink=tier.expert_sink)
+    tier.attach(m)
+    g = torch.Generator().manual_seed(0)
+    prompts = [torch.randint(0, 1024, (64,), generator=g).tolist() for _ in range(2)]
+    rc = RunnerConfig(block_size=64, max_seqs=2, max_model_len=256, max_batched_tokens=256, use_cuda_graph=graphs,
+                      graph_batch_sizes=(1, 2))
+    llm = LLM(m, device="cuda", runner_config=rc)
+    toks = [o.token_ids for o in llm.generate(prompts, SamplingParams(max_tokens=24))]
+    N.check_status()
+    llm.shutdown()
+    return toks, tier.stats()
+
+
+@pytest.mark.gpu
+def test_tiny_mixtral_async_bridge_matches_host_function_bridge():
+    """Every expert on the CPU engine, decode in CUDA graphs: the asynchronous bridge gives
+    the same greedy tokens as the host-function bridge (same engine, same numerics)."""
+    from vllm_xtu_moe_b200.config import EngineConfig
+    want, st0 = _tiny_tiered_llm_tokens(EngineConfig(), True)
+    got, st1 = _tiny_tiered_llm_tokens(EngineConfig(moe_async=True), True)
+    assert got == want
+    assert st0["async"] == 0 and st1["async"] > 0 and st1["cpu"] == 0
+
+
+@pytest.mark.gpu
+def test_tiny_mixtral_deferral_graphs_match_eager():
+    """Expert deferral through the engine: decode replayed from CUDA graphs gives the same
+    tokens as eager decode with deferral, and decode steps defer every layer but the last."""
+    from vllm_xtu_moe_b200.config import EngineConfig
+    eager, st_e = _tiny_tiered_llm_tokens(EngineConfig(moe_defer=True), False)
+    graph, st_g = _tiny_tiered_llm_tokens(EngineConfig(moe_defer=True), True)
+    assert graph == eager
+    assert st_e["deferred"] > 0 and st_e["async"] > st_e["deferred"]   # 2 layers: the last never defers

@@ -93,7 +93,8 @@ def build_cuda(jobs: int = 8, verbose: bool = False, checked: bool = False) -> P
     name = "libxtu_cuda_checked.so" if checked else "libxtu_cuda.so"
     flags = NVCC_FLAGS + (["-DXTU_BOUNDS_CHECK"] if checked else [])
     return _build_lib(name, srcs, NVCC, flags, ["-Xcompiler", "-fPIC", "-lcudart"],
-                      [CSRC / "cuda", CSRC / "comm"], jobs, verbose, OBJDIR / "checked" if checked else OBJDIR)
+                      [CSRC / "cuda", CSRC / "comm", CSRC / "cpu"], jobs, verbose,
+                      OBJDIR / "checked" if checked else OBJDIR)
 
 
 def build_cpu(jobs: int = 8, verbose: bool = False) -> Path:

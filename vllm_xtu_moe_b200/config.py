@@ -87,7 +87,12 @@ class EngineConfig:
     moe_int8: str = _f("auto", "XIAOTU_MOE_INT8")
     moe_int8_min_tokens: int = _f(160, "XIAOTU_MOE_INT8_VNNI_MIN_TOKENS")
     pool_deadline_ms: int = _f(300000, "XIAOTU_MOE_POOL_DEADLINE_MS")
+    moe_async: bool = _f(False, "XIAOTU_MOE_ASYNC")
+    moe_async_timeout_ms: int = _f(20000, "XIAOTU_MOE_ASYNC_TIMEOUT_MS")
+    moe_spin_idle_us: int = _f(50, "XIAOTU_MOE_SPIN_IDLE_US")
     moe_defer: bool = _f(False, "XIAOTU_MOE_DEFER")
+    moe_defer_maxq: int = _f(16, "XIAOTU_MOE_DEFER_MAXQ")
+    moe_defer_maxlayer: int = _f(-1, "XIAOTU_MOE_DEFER_MAXLAYER")
     # expert parallel
     moe_ep: str = _f("auto", "XIAOTU_MOE_EP")
     # formats

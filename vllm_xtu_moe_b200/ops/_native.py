@@ -73,6 +73,8 @@ _SIGS: dict[str, list] = {
     "xtu_moe_permute_decode": [P, P, c_int, c_int, c_int, c_int, P, P, P, P, P, P],
     "xtu_moe_route_decode": [P, c_int, c_int, P, c_int, c_int, P, c_int, c_int, c_int, c_int, c_int, c_float, P, P,
                              P, P, c_int, c_int, P, P, P, P, P, P],
+    "xtu_bridge_post": [P, c_int, P, P, c_int, c_int, c_int, c_int, c_int, c_int, P, P, P, P, c_int, c_int, P, P, P],
+    "xtu_bridge_wait": [P, P, c_int, c_int, c_int, P, c_int, c_int, c_int, P, ctypes.c_longlong, P, P],
     "xtu_paged_attention": [P, c_int, P, P, c_int, P, c_int, P, P, P, c_int, c_int, c_int, c_int, c_int, c_int,
                             c_int, c_int, c_int, c_int, c_int, c_float, c_int, P, P, P, P],
 }
@@ -168,7 +170,8 @@ def stream_ptr(device: torch.device | None = None) -> int:
 _status: dict[int, torch.Tensor] = {}
 
 ERROR_NAMES = {1: "mbarrier wait timed out", 2: "peer flag wait timed out",
-               3: "host flag wait timed out", 4: "bounds check failed"}
+               3: "host flag wait timed out", 4: "bounds check failed",
+               5: "host bridge protocol misuse"}
 
 
 def status_buffer(device: torch.device | int | None = None) -> torch.Tensor:

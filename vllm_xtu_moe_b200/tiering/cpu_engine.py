@@ -54,6 +54,17 @@ def lib() -> ctypes.CDLL:
                 L.xtu_cpu_bridge_stats.restype = I_
                 L.xtu_cpu_bridge_stats.argtypes = [P, ctypes.POINTER(ctypes.c_longlong)]
                 L.xtu_cpu_bridge_destroy.argtypes = [P]
+                L.xtu_async_bridge_create.restype = P
+                L.xtu_async_bridge_create.argtypes = [P, I_, I_, I_, I_, I_]
+                for name in ("xtu_async_bridge_ptrs", "xtu_async_bridge_stats", "xtu_async_bridge_pause",
+                             "xtu_async_bridge_reset", "xtu_async_bridge_add_engine"):
+                    getattr(L, name).restype = I_
+                L.xtu_async_bridge_ptrs.argtypes = [P, ctypes.POINTER(P)]
+                L.xtu_async_bridge_stats.argtypes = [P, ctypes.POINTER(ctypes.c_longlong)]
+                L.xtu_async_bridge_pause.argtypes = [P, I_]
+                L.xtu_async_bridge_reset.argtypes = [P]
+                L.xtu_async_bridge_add_engine.argtypes = [P, P]
+                L.xtu_async_bridge_destroy.argtypes = [P]
                 L.xtu_shm_ep_open.restype = P
                 L.xtu_shm_ep_open.argtypes = [ctypes.c_char_p, I_, I_, I_, I_, I_]
                 L.xtu_shm_ep_allreduce.restype = I_
@@ -161,6 +172,98 @@ class CpuBridge:
         if getattr(self, "_h", None):
             lib().xtu_cpu_bridge_destroy(self._h)
             self._h = None
+
+
+class AsyncCpuBridge:
+    """CPU-expert calls through a polling worker thread instead of a host-function node.
+
+    ``post`` launches one kernel that writes the inputs into a pinned, mapped slot and
+    publishes the request; ``wait`` launches one kernel that waits (bounded) for the
+    worker's result and copies or adds it into a device fp32 buffer.  Requests are read
+    back in the order they were posted, at most ``slots`` outstanding; both kernels keep
+    their request numbers on the device, so a captured post/wait sequence replays from a
+    CUDA graph.  This is the reference's ``XIAOTU_MOE_ASYNC`` path (mapped flags polled by
+    one worker thread, xiaotu_moe/csrc/python_binding/binding.cpp:339-430) and the
+    mechanism of expert deferral (a layer's request is read back one layer later)."""
+
+    def __init__(self, engine: CpuExpertEngine, top_k: int, max_tokens: int, slots: int = 2,
+                 spin_idle_us: int = 50, timeout_ms: int = 20000, device=None):
+        self.engine, self.top_k, self.max_tokens, self.slots = engine, top_k, max_tokens, slots
+        self.timeout_ns = int(timeout_ms) * 1_000_000
+        self.H = engine.H
+        self._h = lib().xtu_async_bridge_create(engine._h, engine.H, top_k, max_tokens, slots, spin_idle_us)
+        if not self._h:
+            raise RuntimeError("mapped pinned allocation for the async CPU bridge failed")
+        ptrs = (P * 5)()
+        lib().xtu_async_bridge_ptrs(self._h, ptrs)
+        self._ctl, self._hx, self._hids, self._hw, self._hout = (ptrs[i] for i in range(5))
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.counters = torch.zeros(4, dtype=torch.int32, device=self.device)   # posted, consumed, 2 arrivals
+        self.engines = [engine]
+
+    def add_engine(self, engine: CpuExpertEngine) -> int:
+        """Let requests run on another engine (one worker serves every tiered layer)."""
+        assert engine.H == self.H
+        i = lib().xtu_async_bridge_add_engine(self._h, engine._h)
+        if i < 0:
+            raise RuntimeError("async CPU bridge: engine table full")
+        self.engines.append(engine)
+        return i
+
+    def post(self, x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, engine: int = 0, lo: int = 0,
+             hi: int | None = None, stream: torch.cuda.Stream | None = None) -> None:
+        from ..ops import _native as N
+        M = ids.shape[0]
+        hi = self.engines[engine].E if hi is None else hi
+        assert x.dtype == torch.bfloat16 and x.stride(1) == 1 and ids.is_contiguous() and weights.is_contiguous()
+        assert ids.dtype == torch.int32 and weights.dtype == torch.float32 and ids.shape[1] == self.top_k
+        s = (stream or torch.cuda.current_stream(self.device)).cuda_stream
+        N.call("xtu_bridge_post", x.data_ptr(), x.stride(0), ids.data_ptr(), weights.data_ptr(), M, self.H,
+               self.top_k, lo, hi, engine, self._ctl, self._hx, self._hids, self._hw, self.slots, self.max_tokens,
+               self.counters.data_ptr(), N.status_buffer(self.device).data_ptr(), s)
+
+    def wait(self, out: torch.Tensor, accumulate: bool = False, stream: torch.cuda.Stream | None = None) -> None:
+        from ..ops import _native as N
+        assert out.dtype == torch.float32 and out.stride(1) == 1 and out.shape[1] == self.H
+        s = (stream or torch.cuda.current_stream(self.device)).cuda_stream
+        N.call("xtu_bridge_wait", self._ctl, self._hout, self.slots, self.max_tokens, self.H, out.data_ptr(),
+               out.stride(0), out.shape[0], int(accumulate), self.counters.data_ptr(), self.timeout_ns,
+               N.status_buffer(self.device).data_ptr(), s)
+
+    def pending(self) -> int:
+        """Requests posted and not read back (synchronises the device)."""
+        c = self.counters.tolist()
+        return c[0] - c[1]
+
+    def pause(self, paused: bool = True) -> None:
+        if lib().xtu_async_bridge_pause(self._h, int(paused)) < 0:
+            raise TimeoutError("the async bridge worker did not park")
+
+    def reset(self) -> None:
+        """Drop every request on both sides (after a wait ran out of time).  Synchronises."""
+        torch.cuda.synchronize(self.device)
+        self.pause(True)
+        if lib().xtu_async_bridge_reset(self._h) < 0:
+            raise RuntimeError("async bridge reset failed")
+        self.counters.zero_()
+        torch.cuda.synchronize(self.device)
+        self.pause(False)
+
+    def stats(self) -> dict:
+        arr = (ctypes.c_longlong * 5)()
+        lib().xtu_async_bridge_stats(self._h, arr)
+        return {"runs": arr[0], "pairs": arr[1], "busy_ms": arr[2] / 1e6, "req": arr[3], "done": arr[4]}
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().xtu_async_bridge_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 class ShmEpGroup:

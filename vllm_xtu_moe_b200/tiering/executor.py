@@ -15,6 +15,16 @@ call (the reference's per-layer ``apply``, vllm_xiaotu_moe/mixed_experts.py:1919
    partial and the shared expert;
 3. otherwise: the CPU engine alone (bridge), combined with the shared expert.
 
+The CPU part of (2) and (3) goes through one of two bridges: the host-function bridge
+(D2H copies, a host-function node, H2D copy, on a side stream), or -- with
+``XIAOTU_MOE_ASYNC`` -- the asynchronous bridge, where a kernel posts the request into
+mapped host memory, one worker thread serves every tiered layer, and a second kernel
+reads the result back with a bounded wait.  Expert deferral (``XIAOTU_MOE_DEFER``, the
+reference's vllm_xiaotu_moe/mixed_experts.py:233-276) builds on the latter: in decode,
+layer L's CPU-expert result is read back in layer L + 1 and added to that layer's MoE
+output, so the CPU computes while the GPU runs layer L + 1's attention; the last main
+layer reads back both its predecessor's and its own result.
+
 Every path is graph-capturable except (1), which is host-orchestrated; decode
 graphs therefore contain route split + pool GEMV + bridge + combine.
 """
@@ -24,7 +34,7 @@ import torch
 
 from ..config import EngineConfig, get_engine_config, parse_layer_list
 from ..ops import moe as M
-from .cpu_engine import CpuBridge, CpuExpertEngine
+from .cpu_engine import AsyncCpuBridge, CpuBridge, CpuExpertEngine
 from .host import HostExperts
 from .policy import load_pin_table
 from .pool import LayerPool
@@ -39,7 +49,9 @@ class LayerExecutor:
         self.owner, self.layer = owner, layer
         self.engine, self.host, self.pool = engine, host, pool
         self.bridge: CpuBridge | None = None
-        self.calls = {"ring": 0, "hybrid": 0, "cpu": 0}
+        self.calls = {"ring": 0, "hybrid": 0, "cpu": 0, "async": 0, "deferred": 0}
+        self.is_mtp = False
+        self.engine_index = -1            # index in the shared async bridge
 
     def _bridge(self, K: int) -> CpuBridge:
         if self.bridge is None:
@@ -51,7 +63,7 @@ class LayerExecutor:
         act = block.cfg.swiglu_limit
         T, H = x.shape
         if not x.is_cuda:
-            y = self.engine.forward(x, ids, w)
+            y = self._cpu_deferred(self.engine.forward(x, ids, w), T)
             if sh is not None:
                 y = y + sh.float()
             return y.to(x.dtype)
@@ -63,6 +75,8 @@ class LayerExecutor:
             self.calls["ring"] += 1
             return o.ring.run_layer(self.host, x, ids, w, o.workspace(T, ids.shape[1], x.device), shared=sh,
                                     act_limit=act)
+        if o.use_async and T <= o.bridge_tokens:
+            return self._async(x, ids, w, sh, act)
         extra = torch.empty(T, H, dtype=torch.float32, device=x.device)
         main = torch.cuda.current_stream()
         if self.pool is not None and self.pool.nslots > 0:
@@ -80,6 +94,59 @@ class LayerExecutor:
         main.wait_stream(o.side)
         ws = o.pool_workspace(T, ids.shape[1], 1, x.device)
         return M.moe_combine(ws, ids, 0, 0, shared=sh, extra=extra)
+
+    def _cpu_deferred(self, y: torch.Tensor, T: int) -> torch.Tensor:
+        """Host-tensor form of expert deferral (the oracle of the device path): returns the
+        fp32 CPU-expert part this layer adds, given its own result `y`."""
+        o = self.owner
+        prev = o.cpu_pending
+        if prev is not None and prev.shape[0] != T:      # left by an aborted forward
+            prev = None
+        if o.defer_ok(self, T):
+            o.cpu_pending = y
+            return prev if prev is not None else torch.zeros_like(y)
+        o.cpu_pending = None
+        return y if prev is None else y + prev
+
+    def _async(self, x, ids, w, sh, act):
+        """CPU experts through the asynchronous bridge, with expert deferral when enabled.
+        Requests are read back in the order they were posted: the previous layer's (when
+        deferred) before this layer's."""
+        o = self.owner
+        T, H = x.shape
+        K = ids.shape[1]
+        br = o.async_bridge(K)
+        pool = self.pool if self.pool is not None and self.pool.nslots > 0 else None
+        if pool is not None:
+            gpu_ids, cpu_ids = torch.empty_like(ids), torch.empty_like(ids)
+            M.route_split(ids, pool.slotmap, 0, gpu_ids, cpu_ids, pool.hits)
+        else:
+            gpu_ids, cpu_ids = ids, ids
+        prev = o.defer_pending
+        if prev is not None and prev != T:               # left by an aborted forward: drop it
+            br.wait(torch.empty(prev, H, dtype=torch.float32, device=x.device))
+            prev = None
+        br.post(x, cpu_ids, w, engine=self.engine_index)
+        if pool is not None:
+            ws = o.pool_workspace(T, K, pool.nslots, x.device)
+            M.moe_experts_partial(x, gpu_ids, w, pool.slots, ws, lo=0, act_limit=act)
+            nslots = pool.nslots
+        else:
+            ws = o.pool_workspace(T, K, 1, x.device)
+            nslots = 0
+        extra = torch.empty(T, H, dtype=torch.float32, device=x.device)
+        if prev is not None:
+            br.wait(extra)                               # the previous layer's CPU part
+        if o.defer_ok(self, T):
+            self.calls["deferred"] += 1
+            o.defer_pending = T
+            if prev is None:
+                extra = None
+        else:
+            self.calls["async"] += 1
+            br.wait(extra, accumulate=prev is not None)
+            o.defer_pending = None
+        return M.moe_combine(ws, gpu_ids, 0, nslots, shared=sh, extra=extra)
 
     def _cpu(self, x, ids, w, extra, main, T):
         """CPU-engine partial of the pairs in `ids` (ids < 0 are skipped) into `extra`, on the side stream."""
@@ -125,6 +192,12 @@ class TieredExperts:
         self._ws: dict = {}
         self.side = torch.cuda.Stream(device=self.device) if self.device.type == "cuda" else None
         self.swaps = 0
+        self.defer = bool(ec.moe_defer)
+        self.use_async = bool(ec.moe_async) or self.defer   # deferral runs on the async bridge
+        self._async_bridge: AsyncCpuBridge | None = None
+        self.defer_pending: int | None = None     # T of the request posted by the previous layer, if deferred
+        self.cpu_pending: torch.Tensor | None = None   # the same on the host-tensor path
+        self._last_main: LayerExecutor | None = None
 
     # ---------------------------------------------------------------- build
     def _pool_list(self, layer: int) -> list[int]:
@@ -163,14 +236,39 @@ class TieredExperts:
 
     def attach(self, model) -> None:
         blocks = [l.mlp for l in model.layers] + [m.layer.mlp for m in getattr(model, "mtp", [])]
+        n_main = len(model.layers)
         it = iter(self._pending)
-        for b in blocks:
+        for i, b in enumerate(blocks):
             if getattr(b, "experts", "dense") is None:
                 layer, eng, host, pool = next(it)
                 ex = LayerExecutor(self, layer, eng, host, pool)
+                ex.is_mtp = i >= n_main
                 b.executor = ex
                 self.executors.append(ex)
+                if not ex.is_mtp:
+                    self._last_main = ex
         self._pending = []
+
+    def defer_ok(self, ex: LayerExecutor, T: int) -> bool:
+        """May `ex` leave its CPU result for the next layer?  Only in decode-sized steps,
+        only main-model layers up to XIAOTU_MOE_DEFER_MAXLAYER, never the last one (it
+        reads back before the final norm)."""
+        if not self.defer or T > self.ec.moe_defer_maxq or ex.is_mtp or ex is self._last_main:
+            return False
+        return self.ec.moe_defer_maxlayer < 0 or ex.layer <= self.ec.moe_defer_maxlayer
+
+    def async_bridge(self, K: int) -> AsyncCpuBridge:
+        """The one asynchronous bridge of this model: every tiered layer's engine registered,
+        one worker thread."""
+        if self._async_bridge is None:
+            first = self.executors[0]
+            br = AsyncCpuBridge(first.engine, K, self.bridge_tokens, slots=2, spin_idle_us=self.ec.moe_spin_idle_us,
+                                timeout_ms=self.ec.moe_async_timeout_ms, device=self.device)
+            first.engine_index = 0
+            for ex in self.executors[1:]:
+                ex.engine_index = br.add_engine(ex.engine)
+            self._async_bridge = br
+        return self._async_bridge
 
     # ---------------------------------------------------------------- runtime
     def workspace(self, T: int, K: int, device) -> M.MoEWorkspace:
@@ -205,7 +303,7 @@ class TieredExperts:
         return {"pools": pools, "ring": ring, "workspaces": ws}
 
     def stats(self) -> dict:
-        out = {"ring": 0, "hybrid": 0, "cpu": 0, "swaps": self.swaps}
+        out = {"ring": 0, "hybrid": 0, "cpu": 0, "async": 0, "deferred": 0, "swaps": self.swaps}
         for ex in self.executors:
             for k, v in ex.calls.items():
                 out[k] += v
@@ -214,6 +312,9 @@ class TieredExperts:
     def shutdown(self) -> None:
         if self.device.type == "cuda":
             torch.cuda.synchronize(self.device)
+        if self._async_bridge is not None:
+            self._async_bridge.close()
+            self._async_bridge = None
         for ex in self.executors:
             if ex.bridge is not None:
                 ex.bridge.close()
