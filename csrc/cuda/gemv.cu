@@ -318,6 +318,8 @@ __device__ __forceinline__ uint8_t* gv_setup(uint64_t*& full, uint64_t*& empty, 
 // last raises this rank's flag on every peer.  The rows are summed by the next kernel
 // (xtu_tp_sum_rmsnorm).  Epochs: e = *ep_c + 1 (advanced by that consumer), published in
 // *ep_p for it; two receive parities so use u + 1 never overwrites what use u still reads.
+constexpr int GV_MAX_WORLD = 8;   // ranks a fused TP GEMV scatters to (one NVSwitch node)
+
 struct GvPeer {
   __nv_bfloat16* const* dst;   // [world] receive buffers (symmetric), 2 * world slots each
   long long slot;              // elements per slot (>= M * N)
@@ -413,6 +415,15 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_dense_kernel(
     }
     if (lane == 0) counters[blockIdx.x] = 0;
   }
+  // PEER: the receive-slot base of every rank, read once (the stores below could alias
+  // the pointer table and the epoch as far as the compiler knows)
+  __nv_bfloat16* dst[GV_MAX_WORLD];
+  if (PEER) {
+    const int par = (__ldcg(pr.ep_c) + 1) & 1;
+    const size_t base = (size_t)(par * pr.world + pr.rank) * pr.slot;
+#pragma unroll
+    for (int p = 0; p < GV_MAX_WORLD; ++p) dst[p] = p < pr.world ? pr.dst[p] + base : nullptr;
+  }
 #pragma unroll
   for (int t = 0; t < 2; ++t)
 #pragma unroll
@@ -426,9 +437,10 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_dense_kernel(
           if (bias) v += __bfloat162float(bias[row]);
           if (PEER) {
             const __nv_bfloat16 bv = __float2bfloat16(v);
-            const int par = (*pr.ep_c + 1) & 1;
-            const size_t off = (size_t)(par * pr.world + pr.rank) * pr.slot + (size_t)tok * N + row;
-            for (int p = 0; p < pr.world; ++p) pr.dst[p][off] = bv;
+            const size_t off = (size_t)tok * N + row;
+#pragma unroll
+            for (int p = 0; p < GV_MAX_WORLD; ++p)
+              if (p < pr.world) dst[p][off] = bv;
           } else if (y_f32) {
             reinterpret_cast<float*>(y)[(size_t)tok * y_stride + row] = v;
           } else {
@@ -437,8 +449,10 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_dense_kernel(
         }
       }
   if (PEER) {   // this tile's rows are out: the last tile raises the flag on every peer
-    __threadfence_system();
+    // the warp barrier orders every lane's stores before lane 0; lane 0's system-scope
+    // fence (cumulative) then publishes them all before its counter increment
     __syncwarp();
+    if (lane == 0) __threadfence_system();
     if (lane == 0 && atomicAdd(pr.done, 1) == (int)gridDim.x - 1) {
       *pr.done = 0;
       const int e = *pr.ep_c + 1;
@@ -793,6 +807,7 @@ int xtu_gemv_tp(const void* W, const float* wscale, int fp8, int N, int K, const
   if (M > 16 || K % 64 != 0 || ws == nullptr || counters == nullptr || (long long)M * N > slot) return -2;
   if (K > GV_MAX_KBLK * 128) return -3;
   if (fp8 && (long long)M * K > GV_WS_X_HALVES) return -4;
+  if (world < 1 || world > GV_MAX_WORLD || rank < 0 || rank >= world) return -5;
   const int nt = M > 8 ? 2 : 1;
   const int tiles = (N + 31) / 32;
   const int S = gv_stages_per_tile(K, fp8 != 0);

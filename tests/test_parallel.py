@@ -322,3 +322,50 @@ def test_pipeline_stages_match_single_rank_cpu():
 def test_pipeline_stages_nccl_match_single_gpu():
     _need_two_gpus()
     mp.spawn(_pp_worker, args=(2, _port(), "glm-4.5-air", "nccl"), nprocs=2)
+
+
+_ONE_RANK_TP = r'''
+import torch
+from vllm_xtu_moe_b200.kernel_bench import _one_rank_group
+from vllm_xtu_moe_b200.models.layers import Linear, RMSNorm
+from vllm_xtu_moe_b200.ops import _native as N
+from vllm_xtu_moe_b200.ops.quant import quant_fp8_block
+from vllm_xtu_moe_b200.parallel.tp import TPReducer
+_one_rank_group()
+d = torch.device("cuda", 0)
+g = torch.Generator(device=d).manual_seed(3)
+H, K = 1024, 2048
+red = TPReducer(16, H, device=d, mode="fused")
+w, s = quant_fp8_block(torch.randn(H, K, device=d, generator=g) * 0.02)
+lin = Linear(w, s)
+norm = RMSNorm((torch.rand(H, device=d, generator=g) + 0.5).to(torch.bfloat16), 1e-5)
+worst = 0.0
+for it, M in enumerate((1, 4, 16, 4, 1)):          # consecutive calls flip the receive parity
+    x = torch.randn(M, K, device=d, generator=g).to(torch.bfloat16)
+    res = torch.randn(M, H, device=d, generator=g).to(torch.bfloat16)
+    y, r = red.linear_scatter(x, lin).finish(res, norm)
+    o = lin(x)
+    r_ref = (o.float() + res.float()).to(torch.bfloat16)
+    y_ref = norm(r_ref.clone())
+    y_ref = y_ref[0] if isinstance(y_ref, tuple) else y_ref
+    torch.cuda.synchronize()
+    N.check_status()
+    er = (r.float() - r_ref.float()).abs().max().item() / (r_ref.float().abs().max().item() + 1e-6)
+    ey = (y.float() - y_ref.float()).abs().max().item() / (y_ref.float().abs().max().item() + 1e-6)
+    worst = max(worst, er, ey)
+red.close()
+print("WORST", worst, "CALLS", red.fused_calls)
+'''
+
+
+@pytest.mark.gpu
+def test_tp_fused_gemv_sum_rmsnorm_on_one_rank():
+    """The fused TP decode path (GEMV whose epilogue stores to the ranks' receive slots,
+    then sum + residual + RMSNorm) on a 1-rank group, against the plain GEMV and norm;
+    successive calls alternate the receive parity."""
+    import subprocess
+    import sys
+    r = subprocess.run([sys.executable, "-c", _ONE_RANK_TP], capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
+    line = [l for l in r.stdout.splitlines() if l.startswith("WORST")][-1].split()
+    assert float(line[1]) < 2e-2 and int(line[3]) == 5, line
