@@ -427,11 +427,17 @@ def test_async_bridge_with_pool_and_graph_replay():
     eager = [o.clone() for o in run()]
     torch.cuda.synchronize()
     N.check_status()
-    routed = []
+    # pool pairs run in their own layer, only the CPU pairs are deferred; the MoE output
+    # is linear in the routing weights, so each part is the layer with the other's zeroed
+    cpu_part, pool_part = [], []
     for l, r in enumerate(raws):
         res = M.prepare_experts("fp8", r["w13"].cuda(), r["w2"].cuda(), r["s13"].cuda(), r["s2"].cuda())
-        routed.append(M.fused_moe(xs[l], *routes[l], res).float())
-    for l, (o, e) in enumerate(zip(eager, _deferred_expectation(routed, shs))):
+        ids, w = routes[l]
+        in_pool = torch.isin(ids, torch.tensor(pool[l], device=ids.device))
+        pool_part.append(M.fused_moe(xs[l], ids, torch.where(in_pool, w, 0.0), res).float())
+        cpu_part.append(M.fused_moe(xs[l], ids, torch.where(in_pool, 0.0, w), res).float())
+    exp = _deferred_expectation(cpu_part, [shs[l].float() + pool_part[l] for l in range(3)])
+    for l, (o, e) in enumerate(zip(eager, exp)):
         ok, err = _close(o, e)
         assert ok, (l, err)
     s = torch.cuda.Stream()

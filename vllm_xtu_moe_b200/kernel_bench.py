@@ -273,6 +273,9 @@ def bench_tp_fused(M_=4, N=4096, Kd=6144, iters=20) -> dict:
     N_.check_status()
     nbytes = w.numel() + M_ * (Kd + 3 * N) * 2
     out = _report("tp_gemv_scatter_sum_rmsnorm", dict(M=M_, N=N, K=Kd, world=1), ms, nbytes, 2 * M_ * N * Kd)
+    # the same work unfused on one GPU: plain GEMV, then residual add + RMSNorm
+    out["plain_gemv_ms"] = round(time_fn(lambda: lin(x), iters), 4)
+    out["plain_pair_ms"] = round(time_fn(lambda: norm(lin(x), res), iters), 4)
     red.close()
     return out
 
@@ -305,6 +308,61 @@ def bench_ep_fused(T=256, E=32, K=8, H=7168, I=2048, iters=10) -> dict:
     return out
 
 
+def bench_cpu_bridge(layers=46, T=1, E=8, H=4096, I=256, K=2, reps=20) -> dict:
+    """Round trip of the CPU-expert bridges in a CUDA graph of `layers` MoE calls, each a
+    small CPU engine call (so the bridge, not the engine, is what is timed):
+    host-function bridge (D2H copies -> host function -> H2D copy) against the
+    asynchronous bridge (post kernel -> polling worker -> bounded wait kernel)."""
+    import time
+    from .tiering.cpu_engine import AsyncCpuBridge, CpuBridge, CpuExpertEngine
+    g = torch.Generator().manual_seed(1)
+    w13 = (torch.randn(E, 2 * I, H, generator=g) / H ** 0.5).to(torch.bfloat16)
+    w2 = (torch.randn(E, H, I, generator=g) / I ** 0.5).to(torch.bfloat16)
+    eng = CpuExpertEngine("bf16", w13, w2, threads=4)
+    x = torch.randn(T, H, device="cuda").to(torch.bfloat16)
+    ids = torch.randint(0, E, (T, K), device="cuda", dtype=torch.int32)
+    wts = torch.full((T, K), 1.0 / K, device="cuda")
+    out = torch.empty(T, H, device="cuda")
+    hb = CpuBridge(eng, K, 16)
+    ab = AsyncCpuBridge(eng, K, 16)
+
+    def host_fn():
+        for _ in range(layers):
+            hb.enqueue(x, ids, wts, out, 0, E)
+
+    def async_fn():
+        for _ in range(layers):
+            ab.post(x, ids, wts)
+            ab.wait(out)
+
+    res = {}
+    for name, fn in (("host_function", host_fn), ("async", async_fn)):
+        fn()
+        torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            fn()
+        gr.replay()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            gr.replay()
+            torch.cuda.synchronize()
+            ts.append(time.perf_counter() - t0)
+        ts.sort()
+        res[name + "_us_per_layer"] = round(ts[len(ts) // 2] / layers * 1e6, 2)
+        del gr
+    N_.check_status()
+    ref = eng.forward(x.cpu(), ids.cpu(), wts.cpu())
+    res["max_err"] = float((out.cpu() - ref).abs().max())
+    res["engine_us_per_call"] = round(ab.stats()["busy_ms"] * 1e3 / max(1, ab.stats()["runs"]), 2)
+    ab.close()
+    hb.close()
+    eng.close()
+    return {"op": "cpu_bridge_round_trip", "shape": dict(layers=layers, T=T, E=E, H=H, I=I, K=K), **res}
+
+
 OPS = {
     "moe_prefill_fp8": lambda a: bench_moe(a.tokens, "fp8"),
     "moe_prefill_bf16": lambda a: bench_moe(a.tokens, "bf16"),
@@ -320,6 +378,7 @@ OPS = {
     "tp_fused": lambda a: bench_tp_fused(),
     "ep_fused": lambda a: bench_ep_fused(),
     "deltanet_prefill": lambda a: bench_deltanet(),
+    "cpu_bridge": lambda a: bench_cpu_bridge(),
 }
 
 
