@@ -67,6 +67,8 @@ struct AdParams {
   int* counters;            // [B * Hkv] zeroed; the last split CTA merges and re-zeroes
   int num_blocks;           // pages in the cache (bounds-check build)
   int T;
+  int window;               // > 0: a query at position t sees keys (t - window, t] only
+  const float* sinks;       // [Hq] learned sink logits (softmax scale applied), or null
   XtuStatus* status;
 };
 
@@ -134,8 +136,10 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(const __grid_co
   const int q0 = __ldg(p.q_start + b), ql = __ldg(p.q_start + b + 1) - q0;
   const int nrows = ql * p.G;
   const int nblk = (L + AD_KEYS - 1) / AD_KEYS;
-  const int per = (nblk + p.splits - 1) / p.splits;
-  const int j0 = min(nblk, sp * per), j1 = min(nblk, j0 + per);
+  // sliding window: no query of this sequence sees a key below L - ql - window + 1
+  const int jfirst = p.window > 0 ? max(0, L - ql - p.window + 1) / AD_KEYS : 0;
+  const int per = (nblk - jfirst + p.splits - 1) / p.splits;
+  const int j0 = min(nblk, jfirst + sp * per), j1 = min(nblk, j0 + per);
   const int nj = j1 - j0;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (warp == 0) {
@@ -186,13 +190,14 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(const __grid_co
   const int g4 = lane >> 2, tq = lane & 3;
   // this lane's two query rows (r and r + 8 of the m-tile): Q fragments and causal limit
   uint32_t qa[DK][4];
-  int lim[2];
+  int lim[2], low[2];
 #pragma unroll
   for (int h2 = 0; h2 < 2; ++h2) {
     const int r = mt * 16 + g4 + h2 * 8;
     const bool valid = r < nrows;
     const int qi = valid ? r / p.G : 0, hh = valid ? r - (r / p.G) * p.G : 0;
     lim[h2] = valid ? L - ql + qi : L - 1;
+    low[h2] = p.window > 0 ? lim[h2] - p.window + 1 : 0;
     const __nv_bfloat16* qrow = p.q + (size_t)(q0 + qi) * p.q_stride + (size_t)(kh * p.G + hh) * D;
 #pragma unroll
     for (int k = 0; k < DK; ++k) {
@@ -241,7 +246,7 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(const __grid_co
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int key = kabs + nt * 8 + 2 * tq + (e & 1);
-        const float v = key <= lim[e >> 1] ? s[nt][e] * p.scale_log2 : -INFINITY;
+        const float v = (key <= lim[e >> 1] && key >= low[e >> 1]) ? s[nt][e] * p.scale_log2 : -INFINITY;
         s[nt][e] = v;
         mx[e >> 1] = fmaxf(mx[e >> 1], v);
       }
@@ -344,9 +349,12 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(const __grid_co
       acc[2] += wgt * v.z;
       acc[3] += wgt * v.w;
     }
-    const float inv = Ls > 0.f ? 1.f / Ls : 0.f;
     const int qi = r / p.G, hh = r - qi * p.G;
     const int tok = q0 + qi, head = kh * p.G + hh;
+    // the sink joins the softmax denominator only (once: here, or in the split merge)
+    if (p.sinks != nullptr && p.splits == 1 && M != -INFINITY)
+      Ls += ad_ex2(__ldg(p.sinks + head) * 1.4426950408889634f - M);
+    const float inv = Ls > 0.f ? 1.f / Ls : 0.f;
     if (p.splits == 1) {
       uint2 pk;
       pk.x = pack_bf16x2(acc[0] * inv, acc[1] * inv);
@@ -380,9 +388,11 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(const __grid_co
   }
   asm volatile("bar.sync 1, %0;" ::"n"(32 * AD_CWARPS) : "memory");
   if (tid < nrows) {
-    float M = -FLT_MAX;
+    const int hh = tid - (tid / p.G) * p.G;
+    const float sk = p.sinks != nullptr ? __ldg(p.sinks + kh * p.G + hh) * 1.4426950408889634f : -FLT_MAX;
+    float M = sk;
     for (int s2 = 0; s2 < p.splits; ++s2) M = fmaxf(M, wsm[tid * 64 + s2]);
-    float sum = 0.f;
+    float sum = sk == -FLT_MAX ? 0.f : ad_ex2(sk - M);
     for (int s2 = 0; s2 < p.splits; ++s2) {
       const float ls = wsm[tid * 64 + s2];
       const float w = ls == -FLT_MAX ? 0.f : ad_ex2(ls - M);
@@ -450,7 +460,8 @@ static int ad_launch(const CUtensorMap& tk, const CUtensorMap& tv, const AdParam
 int attn_decode_gqa(const CUtensorMap& tk, const CUtensorMap& tv, const void* q, int q_stride, void* o,
                     int o_stride, const int* q_start, const int* kv_len, const int* block_table, int bt_stride,
                     int B, int max_q_len, int T, int Hq, int Hkv, int D, float scale, int splits, float* ws_o,
-                    float* ws_lse, int* counters, int num_blocks, void* status, cudaStream_t s) {
+                    float* ws_lse, int* counters, int num_blocks, int window, const float* sinks, void* status,
+                    cudaStream_t s) {
   const int G = Hq / Hkv;
   const int rows = max_q_len * G;
   if ((D != 64 && D != 128) || rows > 32 || rows <= 0) return 0;
@@ -475,6 +486,8 @@ int attn_decode_gqa(const CUtensorMap& tk, const CUtensorMap& tv, const void* q,
   p.counters = counters;
   p.num_blocks = num_blocks;
   p.T = T;
+  p.window = window;
+  p.sinks = sinks;
   p.status = reinterpret_cast<XtuStatus*>(status);
   if (D == 128) return rows <= 16 ? ad_launch<128, 1>(tk, tv, p, B, s) : ad_launch<128, 2>(tk, tv, p, B, s);
   return rows <= 16 ? ad_launch<64, 1>(tk, tv, p, B, s) : ad_launch<64, 2>(tk, tv, p, B, s);

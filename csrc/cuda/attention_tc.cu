@@ -56,6 +56,8 @@ struct AttnParams {
   float* ws_o;             // [splits, T, Hq, dv_total] (splits > 1)
   float* ws_lse;           // [splits, T, Hq]
   int T;
+  int window;              // > 0: a query at position t sees keys (t - window, t] only
+  const float* sinks;      // [Hq] learned sink logits (softmax scale applied), or null
   XtuStatus* status;
 };
 
@@ -126,8 +128,10 @@ __global__ void __launch_bounds__(192, 1)
   const int ctx0 = kv_len - q_len;                   // absolute position of query 0
   const int max_pos = ctx0 + i0 + n_pos - 1;
   const int n_tiles_all = (max_pos + BN) / BN;       // keys [0, max_pos]
-  const int per = (n_tiles_all + p.splits - 1) / p.splits;
-  const int t_begin = split * per;
+  // sliding window: the tile's first query sees nothing below ctx0 + i0 - window + 1
+  const int t_first = p.window > 0 ? max(0, ctx0 + i0 - p.window + 1) / BN : 0;
+  const int per = (n_tiles_all - t_first + p.splits - 1) / p.splits;
+  const int t_begin = t_first + split * per;
   const int t_end = min(n_tiles_all, t_begin + per);
   const int n_tiles = max(0, t_end - t_begin);
 
@@ -325,7 +329,9 @@ __global__ void __launch_bounds__(192, 1)
       tmem_wait_ld();
       // keys t <= lim of the range are visible to this row (causal limit; kv_len follows from it)
       const int lim = row_valid ? qpos - (key0 + c_lo) : -1;
-      const bool all_vis = __all_sync(0xffffffffu, lim >= KP - 1);
+      // sliding window: keys t >= low are visible too (low <= 0: the whole range)
+      const int low = p.window > 0 ? qpos - p.window + 1 - (key0 + c_lo) : 0;
+      const bool all_vis = __all_sync(0xffffffffu, lim >= KP - 1 && low <= 0);
       float mx4[4] = {-FLT_MAX, -FLT_MAX, -FLT_MAX, -FLT_MAX};
 #pragma unroll
       for (int ch = 0; ch < BN / 16; ++ch) {
@@ -333,7 +339,7 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
           for (int t = 0; t < 16; ++t) {
             const int i = ch * 16 + t;
-            if (all_vis || i <= lim) mx4[t & 3] = fmaxf(mx4[t & 3], __uint_as_float(sv[i]));
+            if (all_vis || (i <= lim && i >= low)) mx4[t & 3] = fmaxf(mx4[t & 3], __uint_as_float(sv[i]));
           }
         }
       }
@@ -384,8 +390,8 @@ __global__ void __launch_bounds__(192, 1)
             float e0 = ex2(fmaf(__uint_as_float(sv[i]), p.scale_log2, neg_m));
             float e1 = ex2(fmaf(__uint_as_float(sv[i + 1]), p.scale_log2, neg_m));
             if (!all_vis) {
-              e0 = (live && i <= lim) ? e0 : 0.f;
-              e1 = (live && i + 1 <= lim) ? e1 : 0.f;
+              e0 = (live && i <= lim && i >= low) ? e0 : 0.f;
+              e1 = (live && i + 1 <= lim && i + 1 >= low) ? e1 : 0.f;
             }
             rs4[(t >> 1) & 3] += e0 + e1;
             pk[t >> 1] = pack_bf16x2(e0, e1);
@@ -409,8 +415,13 @@ __global__ void __launch_bounds__(192, 1)
       have_o = mbar_wait(&o_done[last & 1], (last >> 1) & 1, p.status, 123);
       tc_fence_after();
     }
+    // the sink joins the softmax denominator once: here when there is one split, else in
+    // attn_combine_kernel
+    const float sink_l2 = (p.sinks != nullptr && p.splits == 1 && row_valid)
+                              ? __ldg(p.sinks + head) * 1.4426950408889634f : -FLT_MAX;
     if (RF == 1) {
       if (have_o) {
+        if (sink_l2 != -FLT_MAX && m != -FLT_MAX) l += ex2(sink_l2 - m);
         const float inv = l > 0.f ? 1.f / l : 0.f;
 #pragma unroll 1
         for (int c = 0; c < DV; c += 32) {
@@ -457,6 +468,7 @@ __global__ void __launch_bounds__(192, 1)
         const float mq = ml[2 * (lr + q * LR)];
         if (mq != -FLT_MAX) L += ex2(mq - M) * ml[2 * (lr + q * LR) + 1];
       }
+      if (sink_l2 != -FLT_MAX && M != -FLT_MAX) L += ex2(sink_l2 - M);
       const float f = (have_o && row_valid && m != -FLT_MAX && L > 0.f) ? ex2(m - M) / L : 0.f;
       if (warp_active) {
 #pragma unroll 1
@@ -503,14 +515,16 @@ __global__ void __launch_bounds__(192, 1)
 
 // merge split-KV partials: one warp per (token, head)
 __global__ void attn_combine_kernel(const float* __restrict__ ws_o, const float* __restrict__ ws_lse, int splits,
-                                    int T, int Hq, int DV, __nv_bfloat16* __restrict__ o, int o_stride) {
+                                    int T, int Hq, int DV, __nv_bfloat16* __restrict__ o, int o_stride,
+                                    const float* __restrict__ sinks) {
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (gw >= T * Hq) return;
   const int t = gw / Hq, h = gw - (gw / Hq) * Hq;
-  float mx = -FLT_MAX;
+  const float sk = sinks != nullptr ? sinks[h] * 1.4426950408889634f : -FLT_MAX;   // log2 units
+  float mx = sk;
   for (int s = 0; s < splits; ++s) mx = fmaxf(mx, ws_lse[((size_t)s * T + t) * Hq + h]);
-  float wsum = 0.f;
+  float wsum = (sk == -FLT_MAX) ? 0.f : exp2f(sk - mx);
   float w[64];
   for (int s = 0; s < splits && s < 64; ++s) {
     const float ls = ws_lse[((size_t)s * T + t) * Hq + h];
@@ -532,7 +546,8 @@ namespace xtu {
 int attn_decode_gqa(const CUtensorMap& tk, const CUtensorMap& tv, const void* q, int q_stride, void* o,
                     int o_stride, const int* q_start, const int* kv_len, const int* block_table, int bt_stride,
                     int B, int max_q_len, int T, int Hq, int Hkv, int D, float scale, int splits, float* ws_o,
-                    float* ws_lse, int* counters, int num_blocks, void* status, cudaStream_t s);
+                    float* ws_lse, int* counters, int num_blocks, int window, const float* sinks, void* status,
+                    cudaStream_t s);
 }  // namespace xtu
 
 using namespace xtu;
@@ -594,8 +609,8 @@ extern "C" {
 int xtu_paged_attention(const void* q, int q_stride, const void* k_cache, const void* v_cache, int v_is_k, void* o,
                         int o_stride, const int* q_start, const int* kv_len, const int* block_table, int bt_stride,
                         int B, int max_q_len, int max_kv_len, int T, int Hq, int Hkv, int D, int DV, int block_size,
-                        int num_blocks, float scale, int splits, float* ws, int* counters, void* status,
-                        cudaStream_t s) {
+                        int num_blocks, float scale, int splits, float* ws, int* counters, int window,
+                        const float* sinks, void* status, cudaStream_t s) {
   (void)max_kv_len;
   if (B <= 0 || T <= 0) return 0;
   if (block_size != KV_BLOCK) return -2;
@@ -610,6 +625,8 @@ int xtu_paged_attention(const void* q, int q_stride, const void* k_cache, const 
   p.scale_log2 = scale * 1.4426950408889634f;
   p.splits = splits < 1 ? 1 : splits;
   p.T = T;
+  p.window = window;
+  p.sinks = sinks;
   p.status = reinterpret_cast<XtuStatus*>(status);
   if (p.splits > 1) {
     if (!ws) return -5;
@@ -634,7 +651,7 @@ int xtu_paged_attention(const void* q, int q_stride, const void* k_cache, const 
   // decode-shaped GQA steps with few query rows per KV head: the warp-level decode kernel
   if (grid_x == 1 && !v_is_k && D == DV && (D == 64 || D == 128))
     r = attn_decode_gqa(tk, tv, q, q_stride, o, o_stride, q_start, kv_len, block_table, bt_stride, B, max_q_len, T,
-                        Hq, Hkv, D, scale, p.splits, p.ws_o, p.ws_lse, counters, num_blocks, status, s);
+                        Hq, Hkv, D, scale, p.splits, p.ws_o, p.ws_lse, counters, num_blocks, window, sinks, status, s);
   if (r < 0) return r;
   if (r == 1) return 1;   // complete, split merge included
   // decode-shaped steps (all of a sequence's query rows fit one 128-row tile): 64-key
@@ -658,7 +675,7 @@ int xtu_paged_attention(const void* q, int q_stride, const void* k_cache, const 
   if (p.splits > 1) {
     const int warps = T * Hq;
     attn_combine_kernel<<<(warps * 32 + 255) / 256, 256, 0, s>>>(p.ws_o, p.ws_lse, p.splits, T, Hq, DV,
-                                                                  (__nv_bfloat16*)o, o_stride);
+                                                                  (__nv_bfloat16*)o, o_stride, sinks);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return -(int)e;
     return 2;

@@ -234,6 +234,50 @@ def test_paged_attention(Hq, Hkv, D, mode):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("Hq,Hkv,D,Dv", [(64, 8, 192, 128), (16, 2, 128, 128), (8, 2, 64, 64)])
+@pytest.mark.parametrize("mode", ["prefill", "decode", "decode_split", "spec"])
+@pytest.mark.parametrize("window,sinks", [(128, True), (200, False), (0, True)])
+def test_paged_attention_window_and_sinks(Hq, Hkv, D, Dv, mode, window, sinks):
+    """Sliding-window attention with learned per-head sinks (MiMo-style SWA layers; 192/128
+    q-k/v head dims) in the prefill, decode, split-decode and multi-token decode forms."""
+    torch.manual_seed(11)
+    seqs = {"prefill": [(300, 300), (77, 590), (1, 1), (130, 700)], "decode": [(1, 1000), (1, 63), (1, 4097)],
+            "decode_split": [(1, 1000), (1, 63), (1, 4097)], "spec": [(3, 700), (3, 129), (3, 64)]}[mode]
+    kc, vc, meta, T = _make_paged(seqs, Hkv, D, Dv)
+    if mode == "decode_split":
+        meta.num_splits = 8
+    q = torch.randn(T, Hq, D, device="cuda", dtype=torch.bfloat16)
+    sk = (torch.randn(Hq, device="cuda") * 2.0).float() if sinks else None
+    scale = 1.0 / math.sqrt(D)
+    o = paged_attention(q, kc, vc, meta, scale, window=window, sinks=sk)
+    torch.cuda.synchronize()
+    N.check_status()
+    ref = paged_attention_ref(q.float(), kc.float(), vc.float(), meta, scale, window=window, sinks=sk)
+    err = (o.float() - ref.float()).abs().max().item()
+    assert err < 3e-2, err
+
+
+def test_attention_ref_window_and_sinks_semantics():
+    """The restatement itself: a window of 1 returns each query's own value row; a huge
+    sink drives the output to zero; window >= context equals full causal attention."""
+    torch.manual_seed(2)
+    kc, vc, meta, T = _make_paged([(5, 9), (3, 3)], 1, 16, 16, bs=16, device="cpu")
+    q = torch.randn(T, 2, 16)
+    own = paged_attention_ref(q, kc.float(), vc.float(), meta, 0.25, window=1)
+    for b, (ql, kl) in enumerate([(5, 9), (3, 3)]):
+        s0 = meta.q_start_host[b]
+        for i in range(ql):
+            p = kl - ql + i
+            blk = int(meta.block_table[b, p // 16])
+            assert torch.allclose(own[s0 + i, 0], vc[blk, 0, p % 16].float(), atol=1e-5)
+    zero = paged_attention_ref(q, kc.float(), vc.float(), meta, 0.25, sinks=torch.full((2,), 80.0))
+    assert zero.abs().max().item() < 1e-6
+    full = paged_attention_ref(q, kc.float(), vc.float(), meta, 0.25)
+    wide = paged_attention_ref(q, kc.float(), vc.float(), meta, 0.25, window=64)
+    assert torch.allclose(full, wide)
+
+
+@pytest.mark.gpu
 def test_paged_attention_long_prefill():
     """4K-token prompts, GQA group 12 (GLM-Air heads), two chunks of one sequence."""
     torch.manual_seed(7)

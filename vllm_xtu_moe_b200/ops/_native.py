@@ -76,7 +76,7 @@ _SIGS: dict[str, list] = {
     "xtu_bridge_post": [P, c_int, P, P, c_int, c_int, c_int, c_int, c_int, c_int, P, P, P, P, c_int, c_int, P, P, P],
     "xtu_bridge_wait": [P, P, c_int, c_int, c_int, P, c_int, c_int, c_int, P, ctypes.c_longlong, P, P],
     "xtu_paged_attention": [P, c_int, P, P, c_int, P, c_int, P, P, P, c_int, c_int, c_int, c_int, c_int, c_int,
-                            c_int, c_int, c_int, c_int, c_int, c_float, c_int, P, P, P, P],
+                            c_int, c_int, c_int, c_int, c_int, c_float, c_int, P, P, c_int, P, P, P],
 }
 
 

@@ -5,7 +5,9 @@ KV-cache layout per layer: ``k_cache [num_blocks, Hkv, block_size, D]`` and
 kv_lora + rope dims, ``v_cache`` None).  A step's sequences are described by
 :class:`AttnMetadata`: query rows of sequence b are ``q[q_start[b]:q_start[b+1]]``
 at absolute positions ``kv_len[b] - q_len_b + i``, attending causally to keys
-``[0, pos]`` found through ``block_table[b]``.
+``[0, pos]`` found through ``block_table[b]`` -- or, with a sliding ``window``, to
+``(pos - window, pos]``.  Optional per-head ``sinks`` (learned logits on the scale of the
+scaled scores) join each row's softmax denominator and take no value.
 
 On a GPU, ``paged_attention`` runs the tcgen05 flash-attention kernel in
 ``csrc/cuda/attention_tc.cu`` (query rows of a GQA group packed into one
@@ -54,7 +56,8 @@ def _gather_kv(cache: torch.Tensor, block_table_row: torch.Tensor, n: int) -> to
 
 
 def paged_attention_ref(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor | None, meta: AttnMetadata,
-                        scale: float, v_dim: int | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+                        scale: float, v_dim: int | None = None, out: torch.Tensor | None = None, window: int = 0,
+                        sinks: torch.Tensor | None = None) -> torch.Tensor:
     """q [T, Hq, Dqk] -> o [T, Hq, Dv] (fp32 math)."""
     T, Hq, D = q.shape
     qs = meta.q_start_host if meta.q_start_host is not None else meta.q_start.tolist()
@@ -76,9 +79,16 @@ def paged_attention_ref(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.T
         vv = v.repeat_interleave(G, dim=1)
         s = torch.einsum("qhd,khd->hqk", qq, kk) * scale
         pos = torch.arange(n - ql, n, device=q.device)
-        mask = torch.arange(n, device=q.device)[None, :] > pos[:, None]
+        keys = torch.arange(n, device=q.device)[None, :]
+        mask = keys > pos[:, None]
+        if window > 0:
+            mask |= keys <= pos[:, None] - window
         s = s.masked_fill(mask[None], float("-inf"))
-        p = torch.softmax(s, dim=-1)
+        if sinks is not None:   # one more logit per row that takes no value
+            sk = sinks.float().to(q.device)[:, None, None].expand(Hq, ql, 1)
+            p = torch.softmax(torch.cat([s, sk], dim=-1), dim=-1)[..., :-1]
+        else:
+            p = torch.softmax(s, dim=-1)
         o[s0:s1] = torch.einsum("hqk,khd->qhd", p, vv).to(o.dtype)
     return o
 
@@ -110,15 +120,18 @@ def split_counters_reset(device) -> None:
 
 def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor | None, meta: AttnMetadata,
                     scale: float | None = None, v_dim: int | None = None, out: torch.Tensor | None = None,
-                    workspace: torch.Tensor | None = None) -> torch.Tensor:
+                    workspace: torch.Tensor | None = None, window: int = 0,
+                    sinks: torch.Tensor | None = None) -> torch.Tensor:
     T, Hq, D = q.shape
     if scale is None:
         scale = 1.0 / math.sqrt(D)
     if not q.is_cuda or not N.has_symbol("xtu_paged_attention"):
         if q.is_cuda and N.native_required():
             raise N.NativeLibraryMissing("xtu_paged_attention missing from the CUDA library")
-        return paged_attention_ref(q, k_cache, v_cache, meta, scale, v_dim, out)
+        return paged_attention_ref(q, k_cache, v_cache, meta, scale, v_dim, out, window, sinks)
     Hk = k_cache.shape[1]
+    if sinks is not None:
+        assert sinks.dtype == torch.float32 and sinks.is_contiguous() and sinks.numel() == Hq
     if k_cache.shape[2] != KV_BLOCK:
         raise ValueError(f"the GPU paged-attention kernel reads KV blocks of {KV_BLOCK} tokens, "
                          f"not {k_cache.shape[2]} (set RunnerConfig.block_size={KV_BLOCK})")
@@ -136,7 +149,8 @@ def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
            int(v_cache is None), o.data_ptr(), o.stride(0), meta.q_start.data_ptr(), meta.kv_len.data_ptr(),
            meta.block_table.data_ptr(), meta.block_table.stride(0), meta.num_seqs, meta.max_q_len,
            meta.max_kv_len, T, Hq, Hk, D, Dv, k_cache.shape[2], k_cache.shape[0], float(scale), splits,
-           N.ptr(ws) if splits > 1 else None, N.ptr(cnt), N.status_buffer(q.device).data_ptr(),
+           N.ptr(ws) if splits > 1 else None, N.ptr(cnt), int(window),
+           N.ptr(sinks), N.status_buffer(q.device).data_ptr(),
            N.stream_ptr(q.device))
     return o
 
