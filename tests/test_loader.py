@@ -31,6 +31,10 @@ def _cfg(name):
     cfg = get_preset(name)
     if name == "tiny-mixtral":
         return cfg
+    if name == "mimo-v2-flash":
+        return scaled_down(cfg, layers=4, hidden=256, experts=8).replace(
+            num_heads=4, num_kv_heads=1, swa_num_kv_heads=2, head_dim=64, v_head_dim=32, rotary_dim=32,
+            sliding_window=8, moe_intermediate=256, dense_intermediate=512, expert_fmt="bf16", dense_fmt="bf16")
     return scaled_down(cfg, layers=4 if "qwen" in name else 2, hidden=256, experts=8).replace(
         num_heads=4, num_kv_heads=2, head_dim=64 if not cfg.is_mla else cfg.head_dim, moe_intermediate=256,
         shared_intermediate=256, dense_intermediate=512, linear_num_key_heads=2, linear_num_value_heads=4,
@@ -51,7 +55,8 @@ def _logits(model):
     return logits.float()
 
 
-@pytest.mark.parametrize("name", ["tiny-mixtral", "glm-4.5-air", "deepseek-v3", "qwen3-next-80b-a3b"])
+@pytest.mark.parametrize("name", ["tiny-mixtral", "glm-4.5-air", "deepseek-v3", "qwen3-next-80b-a3b",
+                                  "mimo-v2-flash"])
 def test_hf_checkpoint_round_trip(tmp_path, name):
     cfg = _cfg(name)
     m = build_model(cfg, device="cpu", seed=11)

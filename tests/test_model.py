@@ -15,6 +15,15 @@ def _glm_mini():
         dense_fmt="fp8", expert_fmt="fp8")
 
 
+def _mimo_mini(head_dim=192, v_dim=128, window=32):
+    """MiMo-V2 structure at test size: full, swa, swa, swa layers (the full layer with 2 KV
+    heads, the sliding-window layers with 4 and learned sinks), 192-wide q/k, 128-wide v."""
+    return scaled_down(get_preset("mimo-v2-flash"), layers=4, hidden=512, experts=16).replace(
+        num_heads=8, num_kv_heads=2, swa_num_kv_heads=4, head_dim=head_dim, v_head_dim=v_dim, rotary_dim=64,
+        sliding_window=window, moe_intermediate=256, dense_intermediate=1024, expert_fmt="bf16", dense_fmt="bf16",
+        num_mtp_layers=0)
+
+
 def _rc(graph):
     return RunnerConfig(block_size=64, max_seqs=4, max_model_len=1024, max_batched_tokens=256, use_cuda_graph=graph)
 
@@ -35,6 +44,39 @@ def test_generate_cpu_all_families():
         assert all(len(o.token_ids) == 6 for o in outs)
 
 
+def test_mimo_structure_on_cpu():
+    """MiMo-V2 layers: per-layer KV-head counts and value width in the caches, the window and
+    sinks on the sliding-window layers only, and generation through the engine."""
+    cfg = _mimo_mini(head_dim=64, v_dim=32, window=16)
+    m = build_model(cfg, device="cpu", seed=1)
+    kinds = [cfg.layer_type(i) for i in range(cfg.num_layers)]
+    assert kinds == ["full", "swa", "swa", "swa"]
+    caches = m.allocate_caches(8, 16, 2)
+    assert caches[0][0].shape == (8, 2, 16, 64) and caches[0][1].shape == (8, 2, 16, 32)
+    assert caches[1][0].shape == (8, 4, 16, 64) and caches[1][1].shape == (8, 4, 16, 32)
+    a0, a1 = m.layers[0].attn, m.layers[1].attn
+    assert a0.window == 0 and a0.sinks is None and a1.window == 16 and a1.sinks.shape == (8,)
+    assert m.kv_bytes_per_token() == (2 * 96 + 3 * 4 * 96) * 2
+    llm = LLM(m, device="cpu", runner_config=RunnerConfig(block_size=16, max_seqs=2, max_model_len=256,
+                                                          max_batched_tokens=64, use_cuda_graph=False))
+    outs = llm.generate([list(range(1, 70)), list(range(5, 40))], SamplingParams(max_tokens=5))
+    assert all(len(o.token_ids) == 5 for o in outs)
+
+
+def test_mimo_hf_config_mapping():
+    from vllm_xtu_moe_b200.models.config import from_hf_config
+    hf = {"architectures": ["MiMoV2FlashForCausalLM"], "hidden_size": 4096, "num_attention_heads": 64,
+          "num_key_value_heads": 4, "head_dim": 192, "v_head_dim": 128, "num_hidden_layers": 4,
+          "vocab_size": 1000, "hybrid_layer_pattern": [0, 1, 1, 1], "sliding_window": 128,
+          "swa_num_key_value_heads": 8, "add_swa_attention_sink_bias": True, "partial_rotary_factor": 0.334,
+          "n_routed_experts": 256, "num_experts_per_tok": 8, "moe_intermediate_size": 2048,
+          "intermediate_size": 16384, "first_k_dense_replace": 1}
+    c = from_hf_config(hf)
+    assert c.arch == "mimo_v2" and c.layer_types == ["full", "swa", "swa", "swa"]
+    assert (c.kv_heads(0), c.kv_heads(1), c.window(0), c.window(2)) == (4, 8, 0, 128)
+    assert c.has_sinks(1) and not c.has_sinks(0) and c.gqa_v_dim == 128 and c.rot_dim == 64
+
+
 def _prefill_logits(model, prompts):
     llm = LLM(model, runner_config=_rc(False))
     for p in prompts:
@@ -47,9 +89,9 @@ def _prefill_logits(model, prompts):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("which", ["tiny-mixtral", "glm-mini"])
+@pytest.mark.parametrize("which", ["tiny-mixtral", "glm-mini", "mimo-mini"])
 def test_gpu_matches_cpu_prefill(which):
-    cfg = get_preset("tiny-mixtral") if which == "tiny-mixtral" else _glm_mini()
+    cfg = {"tiny-mixtral": lambda: get_preset("tiny-mixtral"), "glm-mini": _glm_mini, "mimo-mini": _mimo_mini}[which]()
     cpu = build_model(cfg, device="cpu", seed=3)
     gpu = cpu.to("cuda")
     prompts = [list(range(3, 200)), list(range(50, 120))]
@@ -62,8 +104,9 @@ def test_gpu_matches_cpu_prefill(which):
 
 
 @pytest.mark.gpu
-def test_gpu_decode_graph_matches_eager():
-    cfg = _glm_mini()
+@pytest.mark.parametrize("which", ["glm-mini", "mimo-mini"])
+def test_gpu_decode_graph_matches_eager(which):
+    cfg = _glm_mini() if which == "glm-mini" else _mimo_mini()
     m = build_model(cfg, device="cuda", seed=4)
     prompts = [list(range(1, 150)), list(range(9, 70)), list(range(100, 400))]
     outs = {}

@@ -63,11 +63,12 @@ class ModelRunner:
 
     # ------------------------------------------------------------------
     def _auto_blocks(self) -> int:
-        per_tok = max(1, self.model.kv_bytes_per_token() + sum(
-            0 for _ in self.model.mtp))
+        per_tok = max(1, self.model.kv_bytes_per_token())
         if self.model.mtp:
             c = self.model.cfg
-            per_tok += (2 * c.num_kv_heads * c.head_dim * 2) if not c.is_mla else (c.kv_lora_rank + c.qk_rope_head_dim) * 2
+            last = c.num_layers - 1     # MTP layers: the last decoder layer's attention type
+            per_tok += len(self.model.mtp) * ((c.kv_heads(last) * (c.head_dim + c.gqa_v_dim) * 2) if not c.is_mla
+                                              else (c.kv_lora_rank + c.qk_rope_head_dim) * 2)
         need = self.rc.max_seqs * self.max_blocks_per_seq
         if not self.cuda:
             return need

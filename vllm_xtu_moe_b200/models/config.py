@@ -4,8 +4,10 @@ One dataclass describes every family the framework serves: Mixtral-style
 (GQA + softmax top-k MoE), GLM-4.5-style (GQA with partial RoPE and qkv bias,
 sigmoid router with correction bias, shared expert, leading dense layers, MTP
 layer), Qwen3-Next-style (3 gated-DeltaNet : 1 gated-GQA, 512 experts, shared
-expert with a sigmoid gate, zero-centred norms) and DeepSeek-V3-style (MLA,
-group-limited sigmoid router, shared expert, leading dense layers).
+expert with a sigmoid gate, zero-centred norms), DeepSeek-V3-style (MLA,
+group-limited sigmoid router, shared expert, leading dense layers) and MiMo-V2-style
+(hybrid global / sliding-window GQA with their own KV-head counts, 192-wide q/k and
+128-wide v heads, learned attention sinks on the sliding-window layers).
 ``from_hf_config`` maps a HF ``config.json`` onto it.
 """
 from __future__ import annotations
@@ -19,7 +21,7 @@ from pathlib import Path
 @dataclass
 class ModelConfig:
     name: str
-    arch: str                      # "mixtral" | "glm4_moe" | "qwen3_next" | "deepseek_v3"
+    arch: str                      # "mixtral" | "glm4_moe" | "qwen3_next" | "deepseek_v3" | "mimo_v2"
     vocab_size: int
     hidden_size: int
     num_layers: int
@@ -39,9 +41,13 @@ class ModelConfig:
     kv_lora_rank: int = 0
     qk_nope_head_dim: int = 0
     qk_rope_head_dim: int = 0
-    v_head_dim: int = 0
+    v_head_dim: int = 0            # MLA value width; for GQA a value width other than head_dim
+    # sliding-window attention (MiMo-V2): layers of type "swa"
+    sliding_window: int = 0
+    swa_num_kv_heads: int = 0      # KV heads of the "swa" layers (0: num_kv_heads)
+    attn_sinks: str = ""           # learned per-head sink logits on "swa" | "full" | "all" layers
     # gated DeltaNet linear attention (Qwen3-Next)
-    layer_types: list[str] | None = None   # per layer: "full" | "linear"
+    layer_types: list[str] | None = None   # per layer: "full" | "linear" | "swa"
     linear_num_key_heads: int = 0
     linear_num_value_heads: int = 0
     linear_key_head_dim: int = 0
@@ -90,6 +96,23 @@ class ModelConfig:
             return "full"
         return self.layer_types[i]
 
+    def kv_heads(self, i: int) -> int:
+        """KV heads of GQA layer i."""
+        if self.layer_type(i) == "swa" and self.swa_num_kv_heads:
+            return self.swa_num_kv_heads
+        return self.num_kv_heads
+
+    @property
+    def gqa_v_dim(self) -> int:
+        return self.v_head_dim if (self.v_head_dim and not self.is_mla) else self.head_dim
+
+    def window(self, i: int) -> int:
+        return self.sliding_window if self.layer_type(i) == "swa" else 0
+
+    def has_sinks(self, i: int) -> bool:
+        k = self.layer_type(i)
+        return self.attn_sinks == "all" or (self.attn_sinks == k and k in ("swa", "full"))
+
     def is_moe_layer(self, i: int) -> bool:
         return self.num_experts > 0 and i >= self.num_dense_layers
 
@@ -111,7 +134,8 @@ class ModelConfig:
                 tot += self.num_heads * self.v_head_dim * H
             else:
                 q = self.num_heads * self.head_dim * (2 if self.attn_output_gate else 1)
-                tot += H * (q + 2 * self.num_kv_heads * self.head_dim) + self.num_heads * self.head_dim * H
+                kv = self.kv_heads(li) * (self.head_dim + self.gqa_v_dim)
+                tot += H * (q + kv) + self.num_heads * self.gqa_v_dim * H
             if self.is_moe_layer(li):
                 ne = self.top_k if active else self.num_experts
                 tot += ne * 3 * H * self.moe_intermediate + H * self.num_experts
@@ -187,12 +211,29 @@ def deepseek_v3() -> ModelConfig:
                        num_mtp_layers=1, max_position=163840)
 
 
+def mimo_v2_flash() -> ModelConfig:
+    """MiMo-V2-style hybrid-attention MoE (the shape the reference's MiMo guide lists): 48
+    layers (1 dense + 47 MoE), hidden 4096, 9 global-attention layers (64 q / 4 kv heads) and
+    39 sliding-window layers (window 128, 64 q / 8 kv heads, learned sinks), q/k heads 192
+    wide with 64 rotary dims, v heads 128 wide; 256 experts top-8, I=2048, sigmoid router
+    with correction bias, plain SwiGLU, MXFP4 experts, 3 MTP layers."""
+    types = ["full" if (i == 0 or i % 6 == 5) else "swa" for i in range(48)]
+    return ModelConfig(name="mimo-v2-flash", arch="mimo_v2", vocab_size=152576, hidden_size=4096, num_layers=48,
+                       num_heads=64, num_kv_heads=4, head_dim=192, v_head_dim=128, rotary_dim=64,
+                       rope_theta=5e6, layer_types=types, sliding_window=128, swa_num_kv_heads=8,
+                       attn_sinks="swa", num_dense_layers=1, dense_intermediate=16384, num_experts=256, top_k=8,
+                       moe_intermediate=2048, scoring="sigmoid", router_bias=True, n_group=1, topk_group=1,
+                       norm_topk_prob=True, expert_fmt="mxfp4", dense_fmt="fp8", num_mtp_layers=3,
+                       norm_eps=1e-5, max_position=262144)
+
+
 PRESETS = {
     "tiny-mixtral": tiny_mixtral,
     "dsv3-moe-layer": deepseek_v3_moe_layer,
     "qwen3-next-80b-a3b": qwen3_next_80b,
     "glm-4.5-air": glm45_air,
     "deepseek-v3": deepseek_v3,
+    "mimo-v2-flash": mimo_v2_flash,
 }
 
 
@@ -223,7 +264,7 @@ def scaled_down(cfg: ModelConfig, layers: int = 2, hidden: int | None = None, ex
 
 
 def from_hf_config(path_or_dict) -> ModelConfig:
-    """Map a HF config.json (Mixtral / Glm4Moe / Qwen3Next / DeepseekV3) onto ModelConfig."""
+    """Map a HF config.json (Mixtral / Glm4Moe / Qwen3Next / DeepseekV3 / MiMoV2) onto ModelConfig."""
     if isinstance(path_or_dict, (str, Path)):
         p = Path(path_or_dict)
         if p.is_dir():
@@ -280,6 +321,29 @@ def from_hf_config(path_or_dict) -> ModelConfig:
                            num_shared_experts=1, shared_intermediate=hf["shared_expert_intermediate_size"],
                            shared_expert_gate=True, scoring="softmax", norm_topk_prob=hf.get("norm_topk_prob", True),
                            expert_fmt=fmt, norm_add_one=True, **base)
+    if archs.startswith("MiMoV2"):
+        # keys read: hybrid_layer_pattern (per layer, 1 = sliding window), sliding_window,
+        # swa_num_key_value_heads, v_head_dim, partial_rotary_factor,
+        # add_swa_attention_sink_bias / add_full_attention_sink_bias, n_routed_experts,
+        # moe_intermediate_size, first_k_dense_replace, num_nextn_predict_layers
+        n = base["num_layers"]
+        pat = hf.get("hybrid_layer_pattern") or [0] * n
+        types = ["swa" if int(pat[i]) == 1 else "full" for i in range(n)]
+        sw, fl = hf.get("add_swa_attention_sink_bias", False), hf.get("add_full_attention_sink_bias", False)
+        sinks = "all" if (sw and fl) else "swa" if sw else "full" if fl else ""
+        return ModelConfig(name="mimo_v2", arch="mimo_v2", layer_types=types,
+                           rotary_dim=int(base["head_dim"] * hf.get("partial_rotary_factor", 1.0)),
+                           v_head_dim=hf.get("v_head_dim", base["head_dim"]),
+                           sliding_window=hf.get("sliding_window", 0) or 0,
+                           swa_num_kv_heads=hf.get("swa_num_key_value_heads", base["num_kv_heads"]),
+                           attn_sinks=sinks, num_dense_layers=hf.get("first_k_dense_replace", 1),
+                           dense_intermediate=hf["intermediate_size"], num_experts=hf["n_routed_experts"],
+                           top_k=hf["num_experts_per_tok"], moe_intermediate=hf["moe_intermediate_size"],
+                           scoring=hf.get("scoring_func", "sigmoid"), router_bias=True,
+                           n_group=hf.get("n_group", 1), topk_group=hf.get("topk_group", 1),
+                           routed_scale=hf.get("routed_scaling_factor", 1.0) or 1.0,
+                           norm_topk_prob=hf.get("norm_topk_prob", True), expert_fmt=fmt, dense_fmt=fmt,
+                           num_mtp_layers=hf.get("num_nextn_predict_layers", 0), **base)
     if archs.startswith("DeepseekV3"):
         base["head_dim"] = hf["qk_nope_head_dim"] + hf["qk_rope_head_dim"]
         return ModelConfig(name="deepseek_v3", arch="deepseek_v3", rope_neox=False, q_lora_rank=hf["q_lora_rank"],

@@ -62,20 +62,26 @@ class RMSNorm:
 
 class GQAAttention:
     """Grouped-query attention with partial RoPE, optional qkv bias, per-head q/k
-    norm and a sigmoid output gate (Qwen3-Next), over the paged KV cache."""
+    norm and a sigmoid output gate (Qwen3-Next), over the paged KV cache; optionally a
+    sliding window, learned per-head sink logits and a value width other than the
+    q/k width (MiMo-V2)."""
 
     def __init__(self, cfg: ModelConfig, qkv: Linear, o: Linear, q_norm: torch.Tensor | None = None,
-                 k_norm: torch.Tensor | None = None):
+                 k_norm: torch.Tensor | None = None, num_kv_heads: int | None = None, window: int = 0,
+                 sinks: torch.Tensor | None = None):
         self.cfg = cfg
         self.qkv = qkv
         self.o = o
         self.q_norm, self.k_norm = q_norm, k_norm
-        self.nh, self.nkv, self.hd = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim
+        self.nh, self.hd, self.vd = cfg.num_heads, cfg.head_dim, cfg.gqa_v_dim
+        self.nkv = num_kv_heads if num_kv_heads is not None else cfg.num_kv_heads
+        self.window = window
+        self.sinks = sinks.float().contiguous() if sinks is not None else None
         self.scale = 1.0 / math.sqrt(self.hd)
 
     def __call__(self, x: torch.Tensor, meta: AttnMetadata, kv: tuple, rope: torch.Tensor) -> torch.Tensor:
         T = x.shape[0]
-        nh, nkv, hd = self.nh, self.nkv, self.hd
+        nh, nkv, hd, vd = self.nh, self.nkv, self.hd, self.vd
         y = self.qkv(x)
         gate = None
         if self.cfg.attn_output_gate:
@@ -84,23 +90,23 @@ class GQAAttention:
             q = qg[:, :, :hd].contiguous()
             gate = qg[:, :, hd:]
             k = y[:, 2 * nh * hd: 2 * nh * hd + nkv * hd].view(T, nkv, hd)
-            v = y[:, 2 * nh * hd + nkv * hd:].view(T, nkv, hd)
+            v = y[:, 2 * nh * hd + nkv * hd:].view(T, nkv, vd)
         else:
             q = y[:, : nh * hd].view(T, nh, hd)
             k = y[:, nh * hd: (nh + nkv) * hd].view(T, nkv, hd)
-            v = y[:, (nh + nkv) * hd:].view(T, nkv, hd)
+            v = y[:, (nh + nkv) * hd:].view(T, nkv, vd)
         k_cache, v_cache = kv
         B.rope_and_cache(q, k, v, meta.positions, rope, self.cfg.rot_dim, self.cfg.rope_neox,
                          slot_mapping=meta.slot_mapping, k_cache=k_cache, v_cache=v_cache, q_norm_w=self.q_norm,
                          k_norm_w=self.k_norm, norm_eps=self.cfg.norm_eps, norm_add_one=self.cfg.norm_add_one)
-        o = paged_attention(q, k_cache, v_cache, meta, self.scale)
+        o = paged_attention(q, k_cache, v_cache, meta, self.scale, window=self.window, sinks=self.sinks)
         if gate is not None:
             o = (o.float() * torch.sigmoid(gate.float())).to(o.dtype)
-        return self.o(o.reshape(T, nh * hd))
+        return self.o(o.reshape(T, nh * vd))
 
     def tensors(self):
         ts = self.qkv.tensors() + self.o.tensors()
-        return ts + [t for t in (self.q_norm, self.k_norm) if t is not None]
+        return ts + [t for t in (self.q_norm, self.k_norm, self.sinks) if t is not None]
 
 
 class DenseMLP:

@@ -84,7 +84,7 @@ class CheckpointSource:
             "head_norm": [f"{pre}.shared_head.norm.weight"],
             "qkv": [f"{pre}.{sa}.q_proj", f"{pre}.{sa}.k_proj", f"{pre}.{sa}.v_proj"],
             "o": [f"{pre}.{sa}.o_proj"], "q_norm": [f"{pre}.{sa}.q_norm.weight"],
-            "k_norm": [f"{pre}.{sa}.k_norm.weight"],
+            "k_norm": [f"{pre}.{sa}.k_norm.weight"], "sinks": [f"{pre}.{sa}.attention_sink_bias"],
             "q_a": [f"{pre}.{sa}.q_a_proj"], "q_a_norm": [f"{pre}.{sa}.q_a_layernorm.weight"],
             "q_b": [f"{pre}.{sa}.q_b_proj" if c.q_lora_rank else f"{pre}.{sa}.q_proj"],
             "kv_a": [f"{pre}.{sa}.kv_a_proj_with_mqa"], "kv_a_norm": [f"{pre}.{sa}.kv_a_layernorm.weight"],
@@ -264,12 +264,13 @@ def export_hf(model, cfg: ModelConfig, path) -> None:
         a = l.attn
         if isinstance(a, GQAAttention):
             qd = cfg.num_heads * cfg.head_dim * (2 if cfg.attn_output_gate else 1)
-            kd = cfg.num_kv_heads * cfg.head_dim
-            put_linear(name + ".qkv", a.qkv, [qd, kd, kd])
+            put_linear(name + ".qkv", a.qkv, [qd, a.nkv * a.hd, a.nkv * a.vd])
             put_linear(name + ".o", a.o)
             if a.q_norm is not None:
                 put(name + ".q_norm", a.q_norm)
                 put(name + ".k_norm", a.k_norm)
+            if a.sinks is not None:
+                put(name + ".sinks", a.sinks)
         elif isinstance(a, MLAAttention):
             if a.q_a is not None:
                 put_linear(name + ".q_a", a.q_a)

@@ -186,49 +186,44 @@ class MoETransformer:
         return sum(t.numel() * t.element_size() for t in self.tensors() if (t.is_cuda or not device_only))
 
     # KV cache / state allocation ---------------------------------------
-    def kv_bytes_per_token(self) -> int:
+    def kv_bytes_per_token(self, layers: range | None = None) -> int:
         c = self.cfg
         n = 0
-        for i in range(c.num_layers):
+        for i in layers if layers is not None else range(c.num_layers):
             if c.layer_type(i) == "linear":
                 continue
             if c.is_mla:
                 n += (c.kv_lora_rank + c.qk_rope_head_dim) * 2
             else:
-                n += 2 * c.num_kv_heads * c.head_dim * 2
+                n += c.kv_heads(i) * (c.head_dim + c.gqa_v_dim) * 2
         return n
 
-    def allocate_caches(self, num_blocks: int, block_size: int, max_seqs: int, device=None) -> list:
+    def _attn_cache(self, i: int, num_blocks: int, block_size: int, dtype, device):
+        """Paged KV cache of attention layer i: (K, V), or (latent, None) for MLA."""
+        c = self.cfg
+        if c.is_mla:
+            return (torch.zeros(num_blocks, 1, block_size, c.kv_lora_rank + c.qk_rope_head_dim,
+                                dtype=torch.bfloat16, device=device), None)
+        nkv = c.kv_heads(i)
+        return (torch.zeros(num_blocks, nkv, block_size, c.head_dim, dtype=dtype, device=device),
+                torch.zeros(num_blocks, nkv, block_size, c.gqa_v_dim, dtype=dtype, device=device))
+
+    def allocate_caches(self, num_blocks: int, block_size: int, max_seqs: int, device=None,
+                        layers: range | None = None) -> list:
         c = self.cfg
         device = device or self.device
         caches = []
-        for i in range(c.num_layers):
+        for i in layers if layers is not None else range(c.num_layers):
             if c.layer_type(i) == "linear":
                 caches.append(DeltaNetState(c, max_seqs, device))
-            elif c.is_mla:
-                caches.append((torch.zeros(num_blocks, 1, block_size, c.kv_lora_rank + c.qk_rope_head_dim,
-                                           dtype=torch.bfloat16, device=device), None))
             else:
-                caches.append((torch.zeros(num_blocks, c.num_kv_heads, block_size, c.head_dim, dtype=self.act_dtype,
-                                           device=device),
-                               torch.zeros(num_blocks, c.num_kv_heads, block_size, c.head_dim, dtype=self.act_dtype,
-                                           device=device)))
+                caches.append(self._attn_cache(i, num_blocks, block_size, self.act_dtype, device))
         return caches
 
     def allocate_mtp_caches(self, num_blocks: int, block_size: int, max_seqs: int, device=None) -> list:
-        c = self.cfg
         device = device or self.device
-        out = []
-        for _ in self.mtp:
-            if c.is_mla:
-                out.append((torch.zeros(num_blocks, 1, block_size, c.kv_lora_rank + c.qk_rope_head_dim,
-                                        dtype=torch.bfloat16, device=device), None))
-            else:
-                out.append((torch.zeros(num_blocks, c.num_kv_heads, block_size, c.head_dim, dtype=torch.bfloat16,
-                                        device=device),
-                            torch.zeros(num_blocks, c.num_kv_heads, block_size, c.head_dim, dtype=torch.bfloat16,
-                                        device=device)))
-        return out
+        last = self.cfg.num_layers - 1      # an MTP layer has the last decoder layer's attention type
+        return [self._attn_cache(last, num_blocks, block_size, torch.bfloat16, device) for _ in self.mtp]
 
     def prepare_workspaces(self, max_tokens: int):
         """Allocate one MoE workspace shared by every MoE layer (they run one at a time)."""
@@ -380,13 +375,17 @@ def build_layer(f: WeightFactory, cfg: ModelConfig, i: int, expert_sink=None, na
                                      dfmt),
                             f.linear(name + ".o", H, nh * cfg.v_head_dim, dfmt))
     else:
-        nh, nkv, hd = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim
+        li = min(i, cfg.num_layers - 1)
+        nh, nkv, hd, vd = cfg.num_heads, cfg.kv_heads(li), cfg.head_dim, cfg.gqa_v_dim
         qdim = nh * hd * (2 if cfg.attn_output_gate else 1)
         qkn = (f.zeros if cfg.norm_add_one else f.ones) if cfg.qk_norm else None
-        attn = GQAAttention(cfg, f.linear(name + ".qkv", qdim + 2 * nkv * hd, H, dfmt, bias=cfg.qkv_bias),
-                            f.linear(name + ".o", H, nh * hd, dfmt),
+        sinks = (f.param(name + ".sinks", lambda n: torch.linspace(-1.0, 1.0, n, device=f.device).float(), nh)
+                 if cfg.has_sinks(li) else None)
+        attn = GQAAttention(cfg, f.linear(name + ".qkv", qdim + nkv * (hd + vd), H, dfmt, bias=cfg.qkv_bias),
+                            f.linear(name + ".o", H, nh * vd, dfmt),
                             qkn((hd,), name=name + ".q_norm") if qkn else None,
-                            qkn((hd,), name=name + ".k_norm") if qkn else None)
+                            qkn((hd,), name=name + ".k_norm") if qkn else None,
+                            num_kv_heads=nkv, window=cfg.window(li), sinks=sinks)
     if cfg.is_moe_layer(min(i, cfg.num_layers - 1)):
         E, I = cfg.num_experts, cfg.moe_intermediate
         gate = f.normal(name + ".router", (E, H), 0.02)

@@ -21,7 +21,6 @@ from __future__ import annotations
 import torch
 import torch.distributed as dist
 
-from ..models.deltanet import DeltaNetState
 from ..models.model import MoETransformer
 from ..ops import basic as B
 
@@ -67,30 +66,13 @@ class PipelineStage(MoETransformer):
         return torch.stack([x, residual]).contiguous()
 
     # ------------------------------------------------------------------ engine contract
-    def kv_bytes_per_token(self) -> int:
-        c = self.cfg
-        n = 0
-        for i in range(self.lo, self.hi):
-            if c.layer_type(i) == "linear":
-                continue
-            n += (c.kv_lora_rank + c.qk_rope_head_dim) * 2 if c.is_mla else 2 * c.num_kv_heads * c.head_dim * 2
-        return n
+    def kv_bytes_per_token(self, layers: range | None = None) -> int:
+        return super().kv_bytes_per_token(range(self.lo, self.hi) if layers is None else layers)
 
-    def allocate_caches(self, num_blocks: int, block_size: int, max_seqs: int, device=None) -> list:
-        c = self.cfg
-        device = device or self.device
-        caches = []
-        for i in range(self.lo, self.hi):
-            if c.layer_type(i) == "linear":
-                caches.append(DeltaNetState(c, max_seqs, device))
-            elif c.is_mla:
-                caches.append((torch.zeros(num_blocks, 1, block_size, c.kv_lora_rank + c.qk_rope_head_dim,
-                                           dtype=torch.bfloat16, device=device), None))
-            else:
-                shape = (num_blocks, c.num_kv_heads, block_size, c.head_dim)
-                caches.append((torch.zeros(shape, dtype=self.act_dtype, device=device),
-                               torch.zeros(shape, dtype=self.act_dtype, device=device)))
-        return caches
+    def allocate_caches(self, num_blocks: int, block_size: int, max_seqs: int, device=None,
+                        layers: range | None = None) -> list:
+        return super().allocate_caches(num_blocks, block_size, max_seqs, device,
+                                       range(self.lo, self.hi) if layers is None else layers)
 
     def _run_layers(self, x, residual, meta, caches):
         for layer, kv in zip(self.layers, caches):

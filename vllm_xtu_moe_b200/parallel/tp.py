@@ -40,11 +40,15 @@ def local_config(cfg: ModelConfig, tp: int) -> ModelConfig:
         return x // tp
     kw = dict(num_heads=div(cfg.num_heads, "num_heads"))
     if not cfg.is_mla:
-        kw["num_kv_heads"] = cfg.num_kv_heads // tp if cfg.num_kv_heads >= tp else 1
-        if cfg.num_kv_heads >= tp:
-            div(cfg.num_kv_heads, "num_kv_heads")
-        elif tp % cfg.num_kv_heads:
-            raise ValueError("tp must be a multiple of num_kv_heads when kv heads are replicated")
+        for key in ("num_kv_heads", "swa_num_kv_heads"):
+            n = getattr(cfg, key)
+            if not n:
+                continue
+            kw[key] = n // tp if n >= tp else 1
+            if n >= tp:
+                div(n, key)
+            elif tp % n:
+                raise ValueError(f"tp must be a multiple of {key} when kv heads are replicated")
     if cfg.dense_intermediate:
         kw["dense_intermediate"] = div(cfg.dense_intermediate, "dense_intermediate")
     if cfg.shared_intermediate:
@@ -113,11 +117,21 @@ class TPWeightFactory:
         per = n // self.tp
         return list(range(self.rank * per, (self.rank + 1) * per))
 
-    def _kv_heads(self) -> list[int]:
+    def _kv_heads(self, n: int | None = None) -> list[int]:
+        n = self.full.num_kv_heads if n is None else n
+        if n >= self.tp:
+            return self._heads(n)
+        return [self.rank * n // self.tp]
+
+    def _layer(self, name: str) -> int:
+        """Decoder-layer index in a tensor name ("model.layers.<i>. ..."; MTP layers: the last)."""
         c = self.full
-        if c.num_kv_heads >= self.tp:
-            return self._heads(c.num_kv_heads)
-        return [self.rank * c.num_kv_heads // self.tp]
+        parts = name.split(".")
+        if "layers" in parts:
+            j = parts.index("layers") + 1
+            if j < len(parts) and parts[j].isdigit():
+                return min(int(parts[j]), c.num_layers - 1)
+        return c.num_layers - 1
 
     @staticmethod
     def _expand(heads: list[int], width: int, base: int = 0) -> list[int]:
@@ -129,16 +143,17 @@ class TPWeightFactory:
         H = c.hidden_size
         suf = name.rsplit(".", 1)[-1]
         if suf == "qkv":
-            hd = c.head_dim
+            hd, vd = c.head_dim, c.gqa_v_dim
+            kvh = c.kv_heads(self._layer(name))
             qw = hd * (2 if c.attn_output_gate else 1)
-            nq, nkv = c.num_heads * qw, c.num_kv_heads * hd
-            rows = (self._expand(self._heads(c.num_heads), qw) + self._expand(self._kv_heads(), hd, nq) +
-                    self._expand(self._kv_heads(), hd, nq + nkv))
-            return nq + 2 * nkv, H, rows, None
+            nq, nk = c.num_heads * qw, kvh * hd
+            rows = (self._expand(self._heads(c.num_heads), qw) + self._expand(self._kv_heads(kvh), hd, nq) +
+                    self._expand(self._kv_heads(kvh), vd, nq + nk))
+            return nq + nk + kvh * vd, H, rows, None
         if suf == "o" and c.is_mla:
             return H, c.num_heads * c.v_head_dim, None, self._expand(self._heads(c.num_heads), c.v_head_dim)
         if suf == "o":
-            return H, c.num_heads * c.head_dim, None, self._expand(self._heads(c.num_heads), c.head_dim)
+            return H, c.num_heads * c.gqa_v_dim, None, self._expand(self._heads(c.num_heads), c.gqa_v_dim)
         if suf == "q_b":
             w = c.qk_nope_head_dim + c.qk_rope_head_dim
             return c.num_heads * w, c.q_lora_rank or H, self._expand(self._heads(c.num_heads), w), None
@@ -193,7 +208,8 @@ class TPWeightFactory:
         return self.base.zeros(shape, dtype, name=name)
 
     def param(self, name, make, n):
-        full_n = self.full.linear_num_value_heads if name.endswith((".A_log", ".dt_bias")) else n
+        full_n = (self.full.linear_num_value_heads if name.endswith((".A_log", ".dt_bias"))
+                  else self.full.num_heads if name.endswith(".sinks") else n)
         t = self.base.param(name, make, full_n)
         if full_n != n:
             t = t[self.rank * n:(self.rank + 1) * n].contiguous()

@@ -44,10 +44,12 @@ def expert_bytes(cfg: ModelConfig, fmt: str | None = None) -> int:
 
 
 def kv_bytes_per_token(cfg: ModelConfig, kv_dtype_bytes: int = 2) -> int:
-    full = [i for i in range(cfg.num_layers) if cfg.layer_type(i) == "full"]
+    """Paged-KV bytes per token over the attention layers (sliding-window layers keep the
+    whole context in the paged cache too)."""
+    attn = [i for i in range(cfg.num_layers) if cfg.layer_type(i) in ("full", "swa")]
     if cfg.is_mla:
-        return len(full) * (cfg.kv_lora_rank + cfg.qk_rope_head_dim) * kv_dtype_bytes
-    return len(full) * 2 * cfg.num_kv_heads * cfg.head_dim * kv_dtype_bytes
+        return len(attn) * (cfg.kv_lora_rank + cfg.qk_rope_head_dim) * kv_dtype_bytes
+    return sum(cfg.kv_heads(i) * (cfg.head_dim + cfg.gqa_v_dim) for i in attn) * kv_dtype_bytes
 
 
 def non_expert_bytes(cfg: ModelConfig) -> int:
