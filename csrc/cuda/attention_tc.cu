@@ -90,7 +90,9 @@ __device__ __forceinline__ void st_sw128(uint8_t* tile, int rows, int row, int c
   *reinterpret_cast<uint4*>(base + ((piece ^ (row & 7)) << 4)) = v;
 }
 
-template <int D, int DV, int BN, int STAGES_, int BTS, int VK>
+// EXT: the sliding window and the sinks of AttnParams are honoured (EXT = 0 compiles the
+// plain causal kernel, whose softmax loop carries no extra compare).
+template <int D, int DV, int BN, int STAGES_, int BTS, int VK, int EXT>
 __global__ void __launch_bounds__(192, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
                     AttnParams p) {
@@ -129,7 +131,7 @@ __global__ void __launch_bounds__(192, 1)
   const int max_pos = ctx0 + i0 + n_pos - 1;
   const int n_tiles_all = (max_pos + BN) / BN;       // keys [0, max_pos]
   // sliding window: the tile's first query sees nothing below ctx0 + i0 - window + 1
-  const int t_first = p.window > 0 ? max(0, ctx0 + i0 - p.window + 1) / BN : 0;
+  const int t_first = (EXT && p.window > 0) ? max(0, ctx0 + i0 - p.window + 1) / BN : 0;
   const int per = (n_tiles_all - t_first + p.splits - 1) / p.splits;
   const int t_begin = t_first + split * per;
   const int t_end = min(n_tiles_all, t_begin + per);
@@ -330,8 +332,8 @@ __global__ void __launch_bounds__(192, 1)
       // keys t <= lim of the range are visible to this row (causal limit; kv_len follows from it)
       const int lim = row_valid ? qpos - (key0 + c_lo) : -1;
       // sliding window: keys t >= low are visible too (low <= 0: the whole range)
-      const int low = p.window > 0 ? qpos - p.window + 1 - (key0 + c_lo) : 0;
-      const bool all_vis = __all_sync(0xffffffffu, lim >= KP - 1 && low <= 0);
+      const int low = (EXT && p.window > 0) ? qpos - p.window + 1 - (key0 + c_lo) : 0;
+      const bool all_vis = __all_sync(0xffffffffu, lim >= KP - 1 && (!EXT || low <= 0));
       float mx4[4] = {-FLT_MAX, -FLT_MAX, -FLT_MAX, -FLT_MAX};
 #pragma unroll
       for (int ch = 0; ch < BN / 16; ++ch) {
@@ -339,7 +341,7 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
           for (int t = 0; t < 16; ++t) {
             const int i = ch * 16 + t;
-            if (all_vis || (i <= lim && i >= low)) mx4[t & 3] = fmaxf(mx4[t & 3], __uint_as_float(sv[i]));
+            if (all_vis || (i <= lim && (!EXT || i >= low))) mx4[t & 3] = fmaxf(mx4[t & 3], __uint_as_float(sv[i]));
           }
         }
       }
@@ -390,8 +392,8 @@ __global__ void __launch_bounds__(192, 1)
             float e0 = ex2(fmaf(__uint_as_float(sv[i]), p.scale_log2, neg_m));
             float e1 = ex2(fmaf(__uint_as_float(sv[i + 1]), p.scale_log2, neg_m));
             if (!all_vis) {
-              e0 = (live && i <= lim && i >= low) ? e0 : 0.f;
-              e1 = (live && i + 1 <= lim && i + 1 >= low) ? e1 : 0.f;
+              e0 = (live && i <= lim && (!EXT || i >= low)) ? e0 : 0.f;
+              e1 = (live && i + 1 <= lim && (!EXT || i + 1 >= low)) ? e1 : 0.f;
             }
             rs4[(t >> 1) & 3] += e0 + e1;
             pk[t >> 1] = pack_bf16x2(e0, e1);
@@ -417,7 +419,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     // the sink joins the softmax denominator once: here when there is one split, else in
     // attn_combine_kernel
-    const float sink_l2 = (p.sinks != nullptr && p.splits == 1 && row_valid)
+    const float sink_l2 = (EXT && p.sinks != nullptr && p.splits == 1 && row_valid)
                               ? __ldg(p.sinks + head) * 1.4426950408889634f : -FLT_MAX;
     if (RF == 1) {
       if (have_o) {
@@ -584,11 +586,11 @@ static int attn_tmap(CUtensorMap* map, const void* base, uint64_t rows, uint64_t
   return r == CUDA_SUCCESS ? 0 : -1000 - (int)r;
 }
 
-template <int D, int DV, int BN, int STAGES = 2, int BTS = 0, int VK = 0>
+template <int D, int DV, int BN, int STAGES = 2, int BTS = 0, int VK = 0, int EXT = 0>
 static int launch_attn(const CUtensorMap& tk, const CUtensorMap& tv, const AttnParams& p, int grid_x, int B,
                        cudaStream_t s) {
   using C = AttnCfg<D, DV, BN, STAGES, BTS, VK>;
-  auto k = attn_fwd_kernel<D, DV, BN, STAGES, BTS, VK>;
+  auto k = attn_fwd_kernel<D, DV, BN, STAGES, BTS, VK, EXT>;
   static bool init = false;
   if (!init) {
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
@@ -663,13 +665,28 @@ int xtu_paged_attention(const void* q, int q_stride, const void* k_cache, const 
   // every replica scores a multiple of 16 keys per tile (the softmax reads S in 16-column chunks)
   const int bn = (decode_shape && D == 64) ? 64 : 128;
   while (p.rf > 1 && (bn / p.rf) % 16 != 0) p.rf >>= 1;
+  // window / sinks: the EXT instantiations (GQA shapes only; MLA has neither)
+  const bool ext = window > 0 || sinks != nullptr;
+  if (mla && ext) return -7;
   if (mla) r = launch_attn<576, 256, 16, 2, 1024, 1>(tk, tv, p, grid_x, B, s);
-  else if (decode_shape && D == 128 && DV == 128) r = launch_attn<128, 128, 128, 2, 256>(tk, tv, p, grid_x, B, s);
-  else if (decode_shape && D == 64 && DV == 64) r = launch_attn<64, 64, 64, 6, 1024>(tk, tv, p, grid_x, B, s);
-  else if (D == 128 && DV == 128) r = launch_attn<128, 128, 128>(tk, tv, p, grid_x, B, s);
-  else if (D == 64 && DV == 64) r = launch_attn<64, 64, 128>(tk, tv, p, grid_x, B, s);
-  else if (D == 256 && DV == 256) r = launch_attn<256, 256, 64>(tk, tv, p, grid_x, B, s);
-  else if (D == 192 && DV == 128) r = launch_attn<192, 128, 64>(tk, tv, p, grid_x, B, s);
+  else if (decode_shape && D == 128 && DV == 128)
+    r = ext ? launch_attn<128, 128, 128, 2, 256, 0, 1>(tk, tv, p, grid_x, B, s)
+            : launch_attn<128, 128, 128, 2, 256>(tk, tv, p, grid_x, B, s);
+  else if (decode_shape && D == 64 && DV == 64)
+    r = ext ? launch_attn<64, 64, 64, 6, 1024, 0, 1>(tk, tv, p, grid_x, B, s)
+            : launch_attn<64, 64, 64, 6, 1024>(tk, tv, p, grid_x, B, s);
+  else if (D == 128 && DV == 128)
+    r = ext ? launch_attn<128, 128, 128, 2, 0, 0, 1>(tk, tv, p, grid_x, B, s)
+            : launch_attn<128, 128, 128>(tk, tv, p, grid_x, B, s);
+  else if (D == 64 && DV == 64)
+    r = ext ? launch_attn<64, 64, 128, 2, 0, 0, 1>(tk, tv, p, grid_x, B, s)
+            : launch_attn<64, 64, 128>(tk, tv, p, grid_x, B, s);
+  else if (D == 256 && DV == 256)
+    r = ext ? launch_attn<256, 256, 64, 2, 0, 0, 1>(tk, tv, p, grid_x, B, s)
+            : launch_attn<256, 256, 64>(tk, tv, p, grid_x, B, s);
+  else if (D == 192 && DV == 128)
+    r = ext ? launch_attn<192, 128, 64, 2, 0, 0, 1>(tk, tv, p, grid_x, B, s)
+            : launch_attn<192, 128, 64>(tk, tv, p, grid_x, B, s);
   else return -6;
   if (r < 0) return r;
   if (p.splits > 1) {
