@@ -14,6 +14,14 @@
 //                      rows each); the decay is carried as one scalar c (S = c * S_stored),
 //                      so a token costs three 32-term dot products and one 32-term update
 //                      per lane; c is folded back into the registers before it underflows.
+//                      CH = true is the channel-wise form (Kimi Delta Attention): g_t is a
+//                      vector over the key dims, S <- Diag(exp(g_t)) S before the same delta
+//                      update; exp(g_t) is taken once per (token, channel) while staging, and
+//                      each lane scales its 32 rows (one more multiply per row and token).
+//
+// The in-projection row is either interleaved per key head [q dk | k dk | v r*dv | z r*dv]
+// (Qwen3-Next's in_proj_qkvz, z feeding its output gate) or blocked [Q | K | V] with no z
+// (KDA: its q, k, v projections concatenated; the output gate has its own projection).
 //
 // Replaces the FLA chunked kernels the reference's vLLM patches run for these layers;
 // the numerics oracle is models/deltanet.py:_delta_rule_ref.
@@ -28,6 +36,7 @@ namespace xtu {
 struct GdnShape {
   int nk, nv, dk, dv, kw;
   int qkvz_stride;     // elements between tokens of the in_proj output
+  int blocked;         // 1: the row is [Q | K | V] (conv channel order), 0: per key head with z
 };
 
 __device__ __forceinline__ int seq_of(const int* __restrict__ q_start, int B, int t) {
@@ -41,6 +50,7 @@ __device__ __forceinline__ int seq_of(const int* __restrict__ q_start, int B, in
 
 // channel c of the conv input (q | k | v order) -> column of the qkvz row
 __device__ __forceinline__ int qkvz_col(const GdnShape& s, int c) {
+  if (s.blocked) return c;
   const int r = s.nv / s.nk;
   const int W = 2 * s.dk + 2 * r * s.dv;
   const int nq = s.nk * s.dk;
@@ -63,7 +73,8 @@ __global__ void gdn_conv_kernel(const __nv_bfloat16* __restrict__ qkvz, GdnShape
   const int b = seq_of(q_start, B, t);
   const int t0 = q_start[b];
   const int slot = slots[b];
-  const bool is_fresh = fresh != nullptr && fresh[b] != 0;
+  // slot < 0: a padding sequence of a captured decode graph -- no state, read as fresh
+  const bool is_fresh = slot < 0 || (fresh != nullptr && fresh[b] != 0);
   const int nq = s.nk * s.dk;
   const int ch = 2 * nq + s.nv * s.dv;
   int c0, width;
@@ -131,6 +142,7 @@ __global__ void gdn_conv_state_kernel(const __nv_bfloat16* __restrict__ qkvz, Gd
   const int L = t1 - t0;
   if (L <= 0) return;
   const int slot = slots[b];
+  if (slot < 0) return;                    // padding sequence: it owns no state
   const bool is_fresh = fresh != nullptr && fresh[b] != 0;
   const int col = qkvz_col(s, c);
   __nv_bfloat16* st = conv_state + ((size_t)slot * ch + c) * (s.kw - 1);
@@ -147,7 +159,7 @@ constexpr int GDN_COLS = 32;       // state columns per CTA
 constexpr int GDN_TB = 16;         // tokens staged in shared memory at a time
 
 // grid: (B, nv, dv / 32); block 128: lane = col8 * 4 + rq (8 columns x 4 row quarters per warp)
-template <int DK>
+template <int DK, bool CH>
 __global__ void __launch_bounds__(128) gdn_recurrent_kernel(
     const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v, const float* __restrict__ g,
     const float* __restrict__ beta, const int* __restrict__ q_start, const int* __restrict__ slots,
@@ -155,6 +167,7 @@ __global__ void __launch_bounds__(128) gdn_recurrent_kernel(
   constexpr int RPT = DK / 4;                 // state rows per thread
   __shared__ float sq[GDN_TB][DK], sk[GDN_TB][DK];
   __shared__ float sv[GDN_TB][GDN_COLS], sg[GDN_TB], sb[GDN_TB];
+  __shared__ float sa[CH ? GDN_TB : 1][CH ? DK : 1];   // CH: exp(g) per (token, key dim)
   const int b = blockIdx.x, h = blockIdx.y, cg = blockIdx.z;
   const int t0 = q_start[b], t1 = q_start[b + 1];
   if (t1 <= t0) return;
@@ -164,9 +177,11 @@ __global__ void __launch_bounds__(128) gdn_recurrent_kernel(
   const int rq = lane & 3;
   const int col = cg * GDN_COLS + cl;
   const int slot = slots[b];
-  float* S_g = ssm + (((size_t)slot * nv + h) * DK) * dv;
+  // slot < 0: a padding sequence of a captured decode graph; it starts from a zero state
+  // and writes none back
+  float* S_g = slot < 0 ? nullptr : ssm + (((size_t)slot * nv + h) * DK) * dv;
   float S[RPT];
-  const bool is_fresh = fresh != nullptr && fresh[b] != 0;
+  const bool is_fresh = slot < 0 || (fresh != nullptr && fresh[b] != 0);
 #pragma unroll
   // lane rq holds rows 4i + rq (interleaved, so the four row groups of a warp read four
   // different banks of the staged q / k vectors)
@@ -184,14 +199,25 @@ __global__ void __launch_bounds__(128) gdn_recurrent_kernel(
       const int tt = i / GDN_COLS, d = i % GDN_COLS;
       sv[tt][d] = v[((size_t)(tb + tt) * nv + h) * dv + cg * GDN_COLS + d];
     }
+    if (CH) {
+      for (int i = threadIdx.x; i < n * DK; i += 128) {
+        const int tt = i / DK, d = i % DK;
+        sa[tt][d] = __expf(g[((size_t)(tb + tt) * nv + h) * DK + d]);
+      }
+    }
     if (threadIdx.x < n) {
-      sg[threadIdx.x] = g[(size_t)(tb + threadIdx.x) * nv + h];
+      if (!CH) sg[threadIdx.x] = g[(size_t)(tb + threadIdx.x) * nv + h];
       sb[threadIdx.x] = beta[(size_t)(tb + threadIdx.x) * nv + h];
     }
     __syncthreads();
     for (int tt = 0; tt < n; ++tt) {
       const float* kt = &sk[tt][rq];
       const float* qt = &sq[tt][rq];
+      if (CH) {
+        const float* at = &sa[tt][rq];
+#pragma unroll
+        for (int i = 0; i < RPT; ++i) S[i] *= at[4 * i];
+      }
       float a = 0.f, bq = 0.f, kq = 0.f;
 #pragma unroll
       for (int i = 0; i < RPT; ++i) {
@@ -205,7 +231,7 @@ __global__ void __launch_bounds__(128) gdn_recurrent_kernel(
         bq += __shfl_xor_sync(0xffffffffu, bq, o);
         kq += __shfl_xor_sync(0xffffffffu, kq, o);
       }
-      c *= __expf(sg[tt]);
+      if (!CH) c *= __expf(sg[tt]);
       const float delta = sb[tt] * (sv[tt][cl] - c * a);
       if (rq == 0) out[((size_t)(tb + tt) * nv + h) * dv + col] = c * bq + delta * kq;
       const float dc = delta / c;
@@ -218,6 +244,7 @@ __global__ void __launch_bounds__(128) gdn_recurrent_kernel(
       }
     }
   }
+  if (S_g == nullptr) return;
 #pragma unroll
   for (int i = 0; i < RPT; ++i) S_g[(size_t)(4 * i + rq) * dv + col] = S[i] * c;
 }
@@ -229,15 +256,18 @@ using namespace xtu;
 extern "C" {
 
 // qkvz: in_proj output [T, qkvz_stride] bf16; conv_w fp32 [ch, kw]; conv_state bf16 [slots, ch, kw-1];
-// ssm fp32 [slots, nv, dk, dv]; g, beta fp32 [T, nv]; scratch q/k fp32 [T, nk, dk], v fp32 [T, nv, dv];
-// out fp32 [T, nv, dv].  Returns kernels launched or a negative error.
+// ssm fp32 [slots, nv, dk, dv] (a sequence whose slot is < 0 is computed from a zero state and
+// leaves every state untouched); g fp32 [T, nv] (g_channels = 0) or [T, nv, dk] (channel-wise
+// decay, g_channels = 1); beta fp32 [T, nv]; blocked: qkvz rows are [Q | K | V] (else per key
+// head [q | k | v | z]); scratch q/k fp32 [T, nk, dk], v fp32 [T, nv, dv]; out fp32 [T, nv, dv].
+// Returns kernels launched or a negative error.
 int xtu_deltanet_fwd(const void* qkvz, int qkvz_stride, int T, int B, const int* q_start, const int* slots,
                      const int* fresh, int nk, int nv, int dk, int dv, int kw, const float* conv_w, void* conv_state,
                      float* ssm, const float* g, const float* beta, float* qs, float* ks, float* vs, float* out,
-                     cudaStream_t stream) {
+                     int blocked, int g_channels, cudaStream_t stream) {
   if (T <= 0 || B <= 0) return 0;
   if (dk != 128 || dv % GDN_COLS != 0 || dv > 256 || kw < 2 || kw > 9 || nv % nk != 0) return -2;
-  GdnShape s{nk, nv, dk, dv, kw, qkvz_stride};
+  GdnShape s{nk, nv, dk, dv, kw, qkvz_stride, blocked ? 1 : 0};
   const int ch = 2 * nk * dk + nv * dv;
   gdn_conv_kernel<<<dim3(T, 2 * nk + nv), 32, 0, stream>>>((const __nv_bfloat16*)qkvz, s, conv_w,
                                                           (const __nv_bfloat16*)conv_state, q_start, slots, fresh, B,
@@ -245,8 +275,12 @@ int xtu_deltanet_fwd(const void* qkvz, int qkvz_stride, int T, int B, const int*
   gdn_conv_state_kernel<<<dim3(B, (ch + 255) / 256), 256, 0, stream>>>((const __nv_bfloat16*)qkvz, s,
                                                                         (__nv_bfloat16*)conv_state, q_start, slots,
                                                                         fresh);
-  gdn_recurrent_kernel<128><<<dim3(B, nv, dv / GDN_COLS), 128, 0, stream>>>(qs, ks, vs, g, beta, q_start, slots,
-                                                                            fresh, ssm, out, nk, nv, dv);
+  if (g_channels)
+    gdn_recurrent_kernel<128, true><<<dim3(B, nv, dv / GDN_COLS), 128, 0, stream>>>(qs, ks, vs, g, beta, q_start,
+                                                                                  slots, fresh, ssm, out, nk, nv, dv);
+  else
+    gdn_recurrent_kernel<128, false><<<dim3(B, nv, dv / GDN_COLS), 128, 0, stream>>>(qs, ks, vs, g, beta, q_start,
+                                                                                   slots, fresh, ssm, out, nk, nv, dv);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 3 : -(int)e;
 }

@@ -60,3 +60,49 @@ def test_deltanet_kernels_match_reference():
             es = (st_gpu.ssm[s] - st_ref.ssm[s]).abs().max().item() / st_ref.ssm[s].abs().max().item()
             assert es < 2e-3
             assert torch.equal(st_gpu.conv[s], st_ref.conv[s])
+
+
+@pytest.mark.gpu
+def test_kda_kernels_match_reference():
+    """Kimi Delta Attention form of the kernels: blocked [Q | K | V] in-projection rows and a
+    decay per key dim, against the per-token recurrence, over prefill chunks and decode."""
+    from vllm_xtu_moe_b200.ops.deltanet import deltanet_fwd
+    torch.manual_seed(1)
+    cfg = scaled_down(get_preset("kimi-linear-48b-a3b"), layers=4, hidden=256, experts=8).replace(
+        linear_num_key_heads=2, linear_num_value_heads=2, linear_key_head_dim=128, linear_value_head_dim=128)
+    nk, nv, dk, dv, kw = 2, 2, 128, 128, cfg.linear_conv_kernel
+    ch = 2 * nk * dk + nv * dv
+    conv_w = (torch.randn(ch, kw) * 0.3).cuda()
+    st_gpu = DeltaNetState(cfg, 4, "cuda")
+    st_ref = DeltaNetState(cfg, 4, "cuda")
+    plan = [([37, 130], [0, 0], [1, 3]), ([5, 1], [37, 130], [1, 3]), ([1, 1], [42, 131], [1, 3])]
+    for lens, starts, slots in plan:
+        T = sum(lens)
+        qkv = (torch.randn(T, ch) * 0.5).to(torch.bfloat16).cuda()
+        g = -torch.rand(T, nv, dk).cuda() * 0.5
+        beta = torch.rand(T, nv).cuda()
+        meta = _meta(lens, starts, slots, "cuda")
+        og = deltanet_fwd(qkv, conv_w, g, beta, meta, st_gpu, nk, nv, dk, dv, blocked=True)
+        orf = deltanet_ref(qkv, conv_w, g, beta, meta, st_ref, nk, nv, dk, dv)
+        torch.cuda.synchronize()
+        err = (og - orf).abs().max().item() / orf.abs().max().item()
+        assert err < 2e-3, (lens, err)
+        for s in slots:
+            es = (st_gpu.ssm[s] - st_ref.ssm[s]).abs().max().item() / st_ref.ssm[s].abs().max().item()
+            assert es < 2e-3
+            assert torch.equal(st_gpu.conv[s], st_ref.conv[s])
+
+
+def test_channel_decay_reduces_to_scalar_decay():
+    """A per-key-dim decay that is the same on every key dim is the scalar gated delta rule."""
+    from vllm_xtu_moe_b200.models.deltanet import _delta_rule_ref
+    torch.manual_seed(3)
+    T, H, dk, dv = 9, 3, 8, 5
+    q, k = torch.randn(T, H, dk), torch.nn.functional.normalize(torch.randn(T, H, dk), dim=-1)
+    v, beta = torch.randn(T, H, dv), torch.rand(T, H)
+    g = -torch.rand(T, H)
+    s1, s2 = torch.randn(H, dk, dv), None
+    s2 = s1.clone()
+    a = _delta_rule_ref(q, k, v, g, beta, s1)
+    b = _delta_rule_ref(q, k, v, g[:, :, None].expand(T, H, dk).contiguous(), beta, s2)
+    assert torch.allclose(a, b, atol=1e-5) and torch.allclose(s1, s2, atol=1e-5)

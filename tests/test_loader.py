@@ -31,6 +31,11 @@ def _cfg(name):
     cfg = get_preset(name)
     if name == "tiny-mixtral":
         return cfg
+    if name == "kimi-linear-48b-a3b":
+        return scaled_down(cfg, layers=4, hidden=256, experts=8).replace(
+            num_heads=4, linear_num_key_heads=2, linear_num_value_heads=2, linear_key_head_dim=32,
+            linear_value_head_dim=32, kv_lora_rank=64, qk_nope_head_dim=32, qk_rope_head_dim=16, v_head_dim=32,
+            head_dim=48, moe_intermediate=128, shared_intermediate=128, dense_intermediate=256)
     if name == "mimo-v2-flash":
         return scaled_down(cfg, layers=4, hidden=256, experts=8).replace(
             num_heads=4, num_kv_heads=1, swa_num_kv_heads=2, head_dim=64, v_head_dim=32, rotary_dim=32,
@@ -56,7 +61,7 @@ def _logits(model):
 
 
 @pytest.mark.parametrize("name", ["tiny-mixtral", "glm-4.5-air", "deepseek-v3", "qwen3-next-80b-a3b",
-                                  "mimo-v2-flash"])
+                                  "mimo-v2-flash", "kimi-linear-48b-a3b"])
 def test_hf_checkpoint_round_trip(tmp_path, name):
     cfg = _cfg(name)
     m = build_model(cfg, device="cpu", seed=11)

@@ -24,6 +24,32 @@ def _mimo_mini(head_dim=192, v_dim=128, window=32):
         num_mtp_layers=0)
 
 
+def _kimi_mini():
+    """Kimi-Linear structure at test size: 3 KDA layers (2 heads x 128, so the GPU kernels run)
+    and one MLA layer without rotary embedding."""
+    return scaled_down(get_preset("kimi-linear-48b-a3b"), layers=4, hidden=512, experts=16).replace(
+        num_heads=8, linear_num_key_heads=2, linear_num_value_heads=2, linear_key_head_dim=128,
+        linear_value_head_dim=128, kv_lora_rank=512, qk_nope_head_dim=128, qk_rope_head_dim=64, v_head_dim=128,
+        head_dim=192, moe_intermediate=256, shared_intermediate=256, dense_intermediate=1024)
+
+
+def _qwen_mini():
+    """Qwen3-Next structure at test size: 3 gated-DeltaNet layers (128-wide heads, so the GPU
+    kernels run) and one gated GQA layer."""
+    return scaled_down(get_preset("qwen3-next-80b-a3b"), layers=4, hidden=512, experts=16).replace(
+        num_heads=4, num_kv_heads=2, head_dim=128, rotary_dim=32, linear_num_key_heads=2, linear_num_value_heads=4,
+        linear_key_head_dim=128, linear_value_head_dim=128, moe_intermediate=256, shared_intermediate=256,
+        expert_fmt="bf16")
+
+
+def _dsv3_mini():
+    """DeepSeek-V3 structure at test size (MLA with kv_lora 512 + rope 64, so the latent
+    decode kernel runs)."""
+    return scaled_down(get_preset("deepseek-v3"), layers=2, hidden=512, experts=16).replace(
+        num_heads=8, q_lora_rank=256, moe_intermediate=256, shared_intermediate=256, dense_intermediate=1024,
+        expert_fmt="bf16", dense_fmt="bf16", num_mtp_layers=0)
+
+
 def _rc(graph, max_model_len=1024):
     return RunnerConfig(block_size=64, max_seqs=4, max_model_len=max_model_len, max_batched_tokens=256,
                         use_cuda_graph=graph)
@@ -64,6 +90,31 @@ def test_mimo_structure_on_cpu():
     assert all(len(o.token_ids) == 5 for o in outs)
 
 
+def test_kimi_linear_on_cpu_and_config_mapping():
+    from vllm_xtu_moe_b200.models.config import from_hf_config
+    from vllm_xtu_moe_b200.models.deltanet import KimiDeltaAttention
+    cfg = _kimi_mini().replace(hidden_size=256, linear_key_head_dim=32, linear_value_head_dim=32, kv_lora_rank=64,
+                               qk_nope_head_dim=32, qk_rope_head_dim=16, v_head_dim=32, head_dim=48)
+    m = build_model(cfg, device="cpu", seed=2)
+    assert [type(l.attn).__name__ for l in m.layers] == ["KimiDeltaAttention"] * 3 + ["MLAAttention"]
+    assert isinstance(m.layers[0].attn, KimiDeltaAttention)
+    llm = LLM(m, device="cpu", runner_config=RunnerConfig(block_size=16, max_seqs=2, max_model_len=256,
+                                                          max_batched_tokens=64, use_cuda_graph=False))
+    outs = llm.generate([list(range(1, 70)), list(range(5, 40))], SamplingParams(max_tokens=5))
+    assert all(len(o.token_ids) == 5 for o in outs)
+    hf = {"architectures": ["KimiLinearForCausalLM"], "hidden_size": 2304, "num_attention_heads": 32,
+          "num_hidden_layers": 8, "vocab_size": 1000, "kv_lora_rank": 512, "q_lora_rank": None,
+          "qk_nope_head_dim": 128, "qk_rope_head_dim": 64, "v_head_dim": 128, "mla_use_nope": True,
+          "linear_attn_config": {"full_attn_layers": [4, 8], "kda_layers": [1, 2, 3, 5, 6, 7], "num_heads": 32,
+                                 "head_dim": 128, "short_conv_kernel_size": 4},
+          "num_experts": 256, "num_experts_per_token": 8, "num_shared_experts": 1, "moe_intermediate_size": 1024,
+          "intermediate_size": 9216, "first_k_dense_replace": 1, "routed_scaling_factor": 2.446}
+    c = from_hf_config(hf)
+    assert c.arch == "kimi_linear" and c.linear_kind == "kda" and not c.mla_rope and c.is_mla
+    assert c.layer_types == ["linear"] * 3 + ["full"] + ["linear"] * 3 + ["full"]
+    assert (c.linear_num_key_heads, c.linear_key_head_dim, c.q_lora_rank) == (32, 128, 0)
+
+
 def test_mimo_hf_config_mapping():
     from vllm_xtu_moe_b200.models.config import from_hf_config
     hf = {"architectures": ["MiMoV2FlashForCausalLM"], "hidden_size": 4096, "num_attention_heads": 64,
@@ -90,9 +141,10 @@ def _prefill_logits(model, prompts):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("which", ["tiny-mixtral", "glm-mini", "mimo-mini"])
+@pytest.mark.parametrize("which", ["tiny-mixtral", "glm-mini", "mimo-mini", "kimi-mini", "qwen-mini"])
 def test_gpu_matches_cpu_prefill(which):
-    cfg = {"tiny-mixtral": lambda: get_preset("tiny-mixtral"), "glm-mini": _glm_mini, "mimo-mini": _mimo_mini}[which]()
+    cfg = {"tiny-mixtral": lambda: get_preset("tiny-mixtral"), "glm-mini": _glm_mini, "mimo-mini": _mimo_mini,
+           "kimi-mini": _kimi_mini, "qwen-mini": _qwen_mini}[which]()
     cpu = build_model(cfg, device="cpu", seed=3)
     gpu = cpu.to("cuda")
     prompts = [list(range(3, 200)), list(range(50, 120))]
@@ -105,9 +157,14 @@ def test_gpu_matches_cpu_prefill(which):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("which", ["glm-mini", "mimo-mini"])
+@pytest.mark.parametrize("which", ["glm-mini", "mimo-mini", "kimi-mini", "qwen-mini", "dsv3-mini"])
 def test_gpu_decode_graph_matches_eager(which):
-    cfg = _glm_mini() if which == "glm-mini" else _mimo_mini()
+    """Decode replayed from CUDA graphs equals eager decode token for token; for the
+    linear-attention families this also checks that capturing a graph (whose warm-up passes
+    execute) leaves the sequences' recurrent state alone, and that padding rows of a graph
+    batch own no state."""
+    cfg = {"glm-mini": _glm_mini, "mimo-mini": _mimo_mini, "kimi-mini": _kimi_mini, "qwen-mini": _qwen_mini,
+           "dsv3-mini": _dsv3_mini}[which]()
     m = build_model(cfg, device="cuda", seed=4)
     prompts = [list(range(1, 150)), list(range(9, 70)), list(range(100, 400))]
     outs = {}

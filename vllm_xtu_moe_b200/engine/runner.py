@@ -13,6 +13,8 @@
 """
 from __future__ import annotations
 
+import dataclasses
+
 import math
 from dataclasses import dataclass
 
@@ -206,9 +208,13 @@ class ModelRunner:
         s = self._static
         meta = self._static_meta(b)
         rows = s["rows"][:b]
-        # warm up (allocations happen outside the capture)
+        # warm up (allocations happen outside the capture).  The warm-up passes execute, so
+        # they run with no recurrent-state slots (-1): the step's real sequences must not have
+        # their linear-attention state advanced by a pass that is not the step itself (their
+        # KV-cache writes repeat what the replay writes, so those are harmless)
+        warm = dataclasses.replace(meta, seq_slots=torch.full((b,), -1, dtype=torch.int32, device=self.device))
         for _ in range(2):
-            tok, *_ = self.forward(s["ids"][:b], meta, rows)
+            tok, *_ = self.forward(s["ids"][:b], warm, rows)
         torch.cuda.synchronize(self.device)
         g = torch.cuda.CUDAGraph()
         n0 = N.launches()

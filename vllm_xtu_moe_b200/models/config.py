@@ -5,9 +5,10 @@ One dataclass describes every family the framework serves: Mixtral-style
 sigmoid router with correction bias, shared expert, leading dense layers, MTP
 layer), Qwen3-Next-style (3 gated-DeltaNet : 1 gated-GQA, 512 experts, shared
 expert with a sigmoid gate, zero-centred norms), DeepSeek-V3-style (MLA,
-group-limited sigmoid router, shared expert, leading dense layers) and MiMo-V2-style
+group-limited sigmoid router, shared expert, leading dense layers), MiMo-V2-style
 (hybrid global / sliding-window GQA with their own KV-head counts, 192-wide q/k and
-128-wide v heads, learned attention sinks on the sliding-window layers).
+128-wide v heads, learned attention sinks on the sliding-window layers) and
+Kimi-Linear-style (3 Kimi Delta Attention : 1 MLA without RoPE).
 ``from_hf_config`` maps a HF ``config.json`` onto it.
 """
 from __future__ import annotations
@@ -21,7 +22,7 @@ from pathlib import Path
 @dataclass
 class ModelConfig:
     name: str
-    arch: str                      # "mixtral" | "glm4_moe" | "qwen3_next" | "deepseek_v3" | "mimo_v2"
+    arch: str                      # "mixtral" | "glm4_moe" | "qwen3_next" | "deepseek_v3" | "mimo_v2" | "kimi_linear"
     vocab_size: int
     hidden_size: int
     num_layers: int
@@ -53,6 +54,8 @@ class ModelConfig:
     linear_key_head_dim: int = 0
     linear_value_head_dim: int = 0
     linear_conv_kernel: int = 4
+    linear_kind: str = "gdn"       # "gdn" (Qwen3-Next gated DeltaNet) | "kda" (Kimi Delta Attention)
+    mla_rope: bool = True          # False: MLA without rotary embedding (Kimi-Linear's NoPE MLA)
     # MLP / MoE
     num_dense_layers: int = 0      # leading dense-MLP layers
     dense_intermediate: int = 0
@@ -122,7 +125,13 @@ class ModelConfig:
         tot = self.vocab_size * H * (1 if self.tie_embeddings else 2)
         for i in range(self.num_layers + self.num_mtp_layers):
             li = min(i, self.num_layers - 1)
-            if self.layer_type(li) == "linear":
+            if self.layer_type(li) == "linear" and self.linear_kind == "kda":
+                kd = self.linear_num_key_heads * self.linear_key_head_dim
+                vd = self.linear_num_value_heads * self.linear_value_head_dim
+                dk = self.linear_key_head_dim
+                tot += H * (2 * kd + vd + self.linear_num_value_heads) + vd * H
+                tot += 2 * H * dk + dk * (self.linear_num_value_heads * dk + vd)
+            elif self.layer_type(li) == "linear":
                 kd = self.linear_num_key_heads * self.linear_key_head_dim
                 vd = self.linear_num_value_heads * self.linear_value_head_dim
                 tot += H * (2 * kd + 2 * vd + 2 * self.linear_num_value_heads) + vd * H
@@ -227,6 +236,24 @@ def mimo_v2_flash() -> ModelConfig:
                        norm_eps=1e-5, max_position=262144)
 
 
+def kimi_linear_48b() -> ModelConfig:
+    """Kimi-Linear-style 48B-A3B hybrid: 27 layers, hidden 2304; Kimi Delta Attention layers
+    (32 heads x 128, short conv 4, decay per key dim) with an MLA layer (32 heads, kv_lora 512,
+    nope 128 + rope 64 dims used without rotary, v 128) at every fourth layer and the last;
+    256 experts top-8 + 1 shared, I=1024, first layer dense (I=9216), sigmoid router with
+    correction bias, bf16 weights."""
+    types = ["full" if (i % 4 == 3 or i == 26) else "linear" for i in range(27)]
+    return ModelConfig(name="kimi-linear-48b-a3b", arch="kimi_linear", vocab_size=163840, hidden_size=2304,
+                       num_layers=27, num_heads=32, num_kv_heads=32, head_dim=192, q_lora_rank=0, kv_lora_rank=512,
+                       qk_nope_head_dim=128, qk_rope_head_dim=64, v_head_dim=128, mla_rope=False, rope_neox=False,
+                       layer_types=types, linear_kind="kda", linear_num_key_heads=32, linear_num_value_heads=32,
+                       linear_key_head_dim=128, linear_value_head_dim=128, linear_conv_kernel=4,
+                       num_dense_layers=1, dense_intermediate=9216, num_experts=256, top_k=8, moe_intermediate=1024,
+                       num_shared_experts=1, shared_intermediate=1024, scoring="sigmoid", router_bias=True,
+                       n_group=1, topk_group=1, routed_scale=2.446, norm_topk_prob=True, expert_fmt="bf16",
+                       dense_fmt="bf16", norm_eps=1e-5, max_position=1048576)
+
+
 PRESETS = {
     "tiny-mixtral": tiny_mixtral,
     "dsv3-moe-layer": deepseek_v3_moe_layer,
@@ -234,6 +261,7 @@ PRESETS = {
     "glm-4.5-air": glm45_air,
     "deepseek-v3": deepseek_v3,
     "mimo-v2-flash": mimo_v2_flash,
+    "kimi-linear-48b-a3b": kimi_linear_48b,
 }
 
 
@@ -264,7 +292,7 @@ def scaled_down(cfg: ModelConfig, layers: int = 2, hidden: int | None = None, ex
 
 
 def from_hf_config(path_or_dict) -> ModelConfig:
-    """Map a HF config.json (Mixtral / Glm4Moe / Qwen3Next / DeepseekV3 / MiMoV2) onto ModelConfig."""
+    """Map a HF config.json (Mixtral / Glm4Moe / Qwen3Next / DeepseekV3 / MiMoV2 / KimiLinear) onto ModelConfig."""
     if isinstance(path_or_dict, (str, Path)):
         p = Path(path_or_dict)
         if p.is_dir():
@@ -344,6 +372,34 @@ def from_hf_config(path_or_dict) -> ModelConfig:
                            routed_scale=hf.get("routed_scaling_factor", 1.0) or 1.0,
                            norm_topk_prob=hf.get("norm_topk_prob", True), expert_fmt=fmt, dense_fmt=fmt,
                            num_mtp_layers=hf.get("num_nextn_predict_layers", 0), **base)
+    if archs.startswith("KimiLinear"):
+        # keys read: linear_attn_config {full_attn_layers (1-based), num_heads, head_dim,
+        # short_conv_kernel_size}, mla_use_nope, q_lora_rank, kv_lora_rank, qk_nope_head_dim,
+        # qk_rope_head_dim, v_head_dim, num_experts, num_experts_per_token,
+        # num_shared_experts, moe_intermediate_size, first_k_dense_replace, routed_scaling_factor
+        n = base["num_layers"]
+        la = hf.get("linear_attn_config") or {}
+        full = {int(i) - 1 for i in la.get("full_attn_layers", [])}
+        types = ["full" if i in full else "linear" for i in range(n)]
+        nh_l, hd_l = la.get("num_heads", nh), la.get("head_dim", 128)
+        base["head_dim"] = hf["qk_nope_head_dim"] + hf["qk_rope_head_dim"]
+        return ModelConfig(name="kimi_linear", arch="kimi_linear", rope_neox=False,
+                           q_lora_rank=hf.get("q_lora_rank") or 0, kv_lora_rank=hf["kv_lora_rank"],
+                           qk_nope_head_dim=hf["qk_nope_head_dim"], qk_rope_head_dim=hf["qk_rope_head_dim"],
+                           v_head_dim=hf["v_head_dim"], mla_rope=not hf.get("mla_use_nope", False),
+                           layer_types=types, linear_kind="kda", linear_num_key_heads=nh_l,
+                           linear_num_value_heads=nh_l, linear_key_head_dim=hd_l, linear_value_head_dim=hd_l,
+                           linear_conv_kernel=la.get("short_conv_kernel_size", 4),
+                           num_dense_layers=hf.get("first_k_dense_replace", 1),
+                           dense_intermediate=hf["intermediate_size"],
+                           num_experts=hf.get("num_experts", hf.get("n_routed_experts", 0)),
+                           top_k=hf.get("num_experts_per_token", hf.get("num_experts_per_tok", 8)),
+                           moe_intermediate=hf["moe_intermediate_size"],
+                           num_shared_experts=hf.get("num_shared_experts", 1),
+                           shared_intermediate=hf["moe_intermediate_size"], scoring="sigmoid", router_bias=True,
+                           n_group=hf.get("num_expert_group", 1) or 1, topk_group=hf.get("topk_group", 1) or 1,
+                           routed_scale=hf.get("routed_scaling_factor", 1.0) or 1.0,
+                           norm_topk_prob=hf.get("moe_renormalize", True), expert_fmt=fmt, dense_fmt=fmt, **base)
     if archs.startswith("DeepseekV3"):
         base["head_dim"] = hf["qk_nope_head_dim"] + hf["qk_rope_head_dim"]
         return ModelConfig(name="deepseek_v3", arch="deepseek_v3", rope_neox=False, q_lora_rank=hf["q_lora_rank"],

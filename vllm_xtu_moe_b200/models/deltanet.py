@@ -13,6 +13,12 @@ projection.  A causal depthwise conv (kernel 4, SiLU) runs over the
 concatenated q/k/v channels first.  Recurrent state and conv state are kept
 per request slot between steps (``DeltaNetState``).
 
+Kimi Delta Attention (KDA, ``KimiDeltaAttention``) is the same recurrence with a decay per
+key dimension: g_t [nv, dk] = -exp(A_log) * softplus(f_b(f_a(x)) + dt_bias), applied as
+S <- Diag(exp(g_t)) S; its q, k, v come from separate projections (concatenated here),
+beta from its own projection, and the output gate is sigmoid(g_b(g_a(x))) in place of
+silu(z).
+
 The per-token recurrence in ``_delta_rule_ref`` is the numerics oracle; on a
 GPU (key head dim 128) the conv / recurrence kernels of ``csrc/cuda/deltanet.cu`` run.
 """
@@ -43,12 +49,13 @@ class DeltaNetState:
 
 
 def _delta_rule_ref(q, k, v, g, beta, state):
-    """q,k [T, H, dk], v [T, H, dv], g,beta [T, H]; state [H, dk, dv] (updated in place)."""
+    """q,k [T, H, dk], v [T, H, dv], g [T, H] (or [T, H, dk]: a decay per key dim), beta [T, H];
+    state [H, dk, dv] (updated in place)."""
     T = q.shape[0]
     out = torch.empty(T, v.shape[1], v.shape[2], dtype=torch.float32, device=q.device)
     S = state
     for t in range(T):
-        S.mul_(torch.exp(g[t])[:, None, None])
+        S.mul_(torch.exp(g[t])[:, :, None] if g.dim() == 3 else torch.exp(g[t])[:, None, None])
         kv_mem = torch.einsum("hkv,hk->hv", S, k[t])
         delta = (v[t] - kv_mem) * beta[t][:, None]
         S.add_(torch.einsum("hk,hv->hkv", k[t], delta))
@@ -116,6 +123,58 @@ class GatedDeltaNet:
                 [self.conv_w, self.A_log, self.dt_bias, self.norm_w])
 
 
+class KimiDeltaAttention:
+    """Kimi Delta Attention layer: conv + L2-normalised q/k, the delta rule with a decay per
+    key dimension, RMSNorm of the output times sigmoid(output gate), output projection.
+    Weights: in_qkv rows [Q | K | V] (q_proj, k_proj, v_proj), in_b [nv, H], the low-rank
+    decay f_a [dk, H] / f_b [nv*dk, dk] with dt_bias [nv*dk] and A_log [nv], the low-rank
+    gate g_a [dk, H] / g_b [nv*dv, dk], conv [channels, kernel], norm weight [dv]."""
+
+    def __init__(self, cfg: ModelConfig, in_qkv: Linear, in_b: Linear, f_a: Linear, f_b: Linear, g_a: Linear,
+                 g_b: Linear, conv_w: torch.Tensor, A_log: torch.Tensor, dt_bias: torch.Tensor,
+                 norm_w: torch.Tensor, out: Linear):
+        self.cfg = cfg
+        self.in_qkv, self.in_b, self.f_a, self.f_b, self.g_a, self.g_b = in_qkv, in_b, f_a, f_b, g_a, g_b
+        self.conv_w, self.A_log, self.dt_bias, self.norm_w, self.out = conv_w, A_log, dt_bias, norm_w, out
+        self.nk, self.nv = cfg.linear_num_key_heads, cfg.linear_num_value_heads
+        self.dk, self.dv = cfg.linear_key_head_dim, cfg.linear_value_head_dim
+
+    def decay(self, x: torch.Tensor) -> torch.Tensor:
+        """g [T, nv, dk] fp32."""
+        T = x.shape[0]
+        raw = self.f_b(self.f_a(x)).float().view(T, self.nv, self.dk)
+        return -torch.exp(self.A_log.float()).view(1, self.nv, 1) * F.softplus(
+            raw + self.dt_bias.float().view(1, self.nv, self.dk))
+
+    def __call__(self, x: torch.Tensor, meta: AttnMetadata, kv, rope) -> torch.Tensor:
+        state: DeltaNetState = kv
+        T = x.shape[0]
+        qkv = self.in_qkv(x)
+        beta = torch.sigmoid(self.in_b(x).float())
+        g = self.decay(x)
+        gate = self.g_b(self.g_a(x)).view(T, self.nv, self.dv)
+        if x.is_cuda and N.has_symbol("xtu_deltanet_fwd") and self.dk == 128:
+            from ..ops.deltanet import deltanet_fwd
+            if getattr(self, "_conv_w32", None) is None or self._conv_w32.device != x.device:
+                self._conv_w32 = self.conv_w.float().contiguous()
+            o = deltanet_fwd(qkv.contiguous(), self._conv_w32, g.contiguous(), beta, meta, state, self.nk, self.nv,
+                             self.dk, self.dv, blocked=True)
+        else:
+            if x.is_cuda and N.native_required() and self.dk == 128:
+                raise N.NativeLibraryMissing("xtu_deltanet_fwd missing from the CUDA library")
+            o = deltanet_ref(qkv, self.conv_w, g, beta, meta, state, self.nk, self.nv, self.dk, self.dv)
+        of = o.float()
+        y = of * torch.rsqrt(of.pow(2).mean(-1, keepdim=True) + self.cfg.norm_eps)
+        y = (y * self.norm_w.float() * torch.sigmoid(gate.float())).to(torch.bfloat16)
+        return self.out(y.reshape(T, self.nv * self.dv))
+
+    def tensors(self):
+        ts = []
+        for lin in (self.in_qkv, self.in_b, self.f_a, self.f_b, self.g_a, self.g_b, self.out):
+            ts += lin.tensors()
+        return ts + [self.conv_w, self.A_log, self.dt_bias, self.norm_w]
+
+
 def deltanet_ref(mixed, conv_w, g, beta, meta, state: DeltaNetState, nk, nv, dk, dv):
     """Causal conv (with carried state) + gated delta rule per sequence (fp32)."""
     T, ch = mixed.shape
@@ -130,11 +189,15 @@ def deltanet_ref(mixed, conv_w, g, beta, meta, state: DeltaNetState, nk, nv, dk,
         if s1 == s0:
             continue
         slot = slots[bi]
+        if slot < 0:      # padding sequence of a captured decode graph: zero state, nothing kept
+            conv_st, ssm_st = torch.zeros_like(state.conv[0]), torch.zeros_like(state.ssm[0])
+        else:
+            conv_st, ssm_st = state.conv[slot], state.ssm[slot]
         if fresh[bi]:
-            state.conv[slot].zero_()
-            state.ssm[slot].zero_()
+            conv_st.zero_()
+            ssm_st.zero_()
         xs = mixed[s0:s1].float()                                  # [L, ch]
-        hist = state.conv[slot].float().t()                        # [kw-1, ch]
+        hist = conv_st.float().t()                                 # [kw-1, ch]
         full = torch.cat([hist, xs], dim=0)                        # [kw-1+L, ch]
         L = s1 - s0
         w = conv_w.float()                                          # [ch, kw]
@@ -142,7 +205,7 @@ def deltanet_ref(mixed, conv_w, g, beta, meta, state: DeltaNetState, nk, nv, dk,
         for j in range(kw):
             conv += full[j:j + L] * w[:, j]
         conv = F.silu(conv)
-        state.conv[slot].copy_(full[-(kw - 1):].t().to(state.conv.dtype))
+        conv_st.copy_(full[-(kw - 1):].t().to(state.conv.dtype))
         q = conv[:, : nk * dk].view(L, nk, dk)
         k = conv[:, nk * dk: 2 * nk * dk].view(L, nk, dk)
         v = conv[:, 2 * nk * dk:].view(L, nv, dv)
@@ -150,5 +213,5 @@ def deltanet_ref(mixed, conv_w, g, beta, meta, state: DeltaNetState, nk, nv, dk,
         k = F.normalize(k, dim=-1)
         q = q.repeat_interleave(r, dim=1)
         k = k.repeat_interleave(r, dim=1)
-        out[s0:s1] = _delta_rule_ref(q, k, v, g[s0:s1], beta[s0:s1], state.ssm[slot])
+        out[s0:s1] = _delta_rule_ref(q, k, v, g[s0:s1], beta[s0:s1], ssm_st)
     return out

@@ -97,6 +97,17 @@ class CheckpointSource:
             "router_bias": [f"{pre}.{f['router']}.e_score_correction_bias"],
             "mlp.gate_up": [f"{pre}.mlp.gate_proj", f"{pre}.mlp.up_proj"], "mlp.down": [f"{pre}.mlp.down_proj"],
         }
+        if c.linear_kind == "kda":
+            # Kimi Delta Attention: separate q/k/v projections and convs, low-rank decay and gate
+            table.update({
+                "kda_qkv": [f"{pre}.{sa}.q_proj", f"{pre}.{sa}.k_proj", f"{pre}.{sa}.v_proj"],
+                "kda_b": [f"{pre}.{sa}.b_proj"], "kda_f_a": [f"{pre}.{sa}.f_a_proj"],
+                "kda_f_b": [f"{pre}.{sa}.f_b_proj"], "kda_g_a": [f"{pre}.{sa}.g_a_proj"],
+                "kda_g_b": [f"{pre}.{sa}.g_b_proj"],
+                "conv": [f"{pre}.{sa}.q_conv1d.weight", f"{pre}.{sa}.k_conv1d.weight",
+                         f"{pre}.{sa}.v_conv1d.weight"],
+                "A_log": [f"{pre}.{sa}.A_log"], "dt_bias": [f"{pre}.{sa}.dt_bias"],
+                "gdn_norm": [f"{pre}.{sa}.o_norm.weight"], "out": [f"{pre}.{sa}.o_proj"]})
         if f.get("shared"):
             table["shared.gate_up"] = [f"{pre}.{f['shared']}.gate_proj", f"{pre}.{f['shared']}.up_proj"]
             table["shared.down"] = [f"{pre}.{f['shared']}.down_proj"]
@@ -114,7 +125,9 @@ class CheckpointSource:
 
     # ------------------------------------------------------------------ factory interface
     def normal(self, name, shape, std=None, dtype=torch.bfloat16):
-        t = self._get(self._hf(name)[0])
+        parts = self._hf(name)
+        ts = [self._get(p_) for p_ in parts]
+        t = torch.cat(ts, 0) if len(ts) > 1 else ts[0]       # KDA: q / k / v convs, channel order
         if name.endswith(".conv") and t.dim() == 3:          # conv1d weight [ch, 1, k]
             t = t[:, 0, :]
         if tuple(t.shape) != tuple(shape):
@@ -128,7 +141,8 @@ class CheckpointSource:
 
     def param(self, name: str, make, n: int):
         ref = make(n)
-        return self._get(self._hf(name)[0]).to(device=self.device, dtype=ref.dtype, copy=True).view(ref.shape)
+        t = self._get(self._hf(name)[0])       # any shape with n elements (KDA keeps A_log [1, 1, nv, 1])
+        return t.to(device=self.device, dtype=ref.dtype, copy=True).reshape(ref.shape)
 
     def linear(self, name, n, k, fmt="bf16", bias=False, std=None) -> Linear:
         parts = self._hf(name)
@@ -228,7 +242,7 @@ def export_hf(model, cfg: ModelConfig, path) -> None:
     from ..utils.safetensors import save_file
     from .layers import DenseMLP, GQAAttention, MoEBlock
     from .mla import MLAAttention
-    from .deltanet import GatedDeltaNet
+    from .deltanet import GatedDeltaNet, KimiDeltaAttention
     src = CheckpointSource.__new__(CheckpointSource)
     src.cfg, src.fam = cfg, _family_names(cfg)
     out: dict[str, torch.Tensor] = {}
@@ -280,6 +294,18 @@ def export_hf(model, cfg: ModelConfig, path) -> None:
             put(name + ".kv_a_norm", a.kv_a_norm)
             put_linear(name + ".kv_b", a.kv_b)
             put_linear(name + ".o", a.o)
+        elif isinstance(a, KimiDeltaAttention):
+            kd, vd = a.nk * a.dk, a.nv * a.dv
+            put_linear(name + ".kda_qkv", a.in_qkv, [kd, kd, vd])
+            for suf, lin in (("kda_b", a.in_b), ("kda_f_a", a.f_a), ("kda_f_b", a.f_b), ("kda_g_a", a.g_a),
+                             ("kda_g_b", a.g_b), ("out", a.out)):
+                put_linear(name + "." + suf, lin)
+            cw = a.conv_w.detach().cpu().unsqueeze(1)
+            for p_, (r0, n_) in zip(src._hf(name + ".conv"), ((0, kd), (kd, kd), (2 * kd, vd))):
+                out[p_] = cw[r0:r0 + n_].clone()
+            put(name + ".A_log", a.A_log)
+            put(name + ".dt_bias", a.dt_bias)
+            put(name + ".gdn_norm", a.norm_w)
         elif isinstance(a, GatedDeltaNet):
             put_linear(name + ".qkvz", a.in_qkvz)
             put_linear(name + ".ba", a.in_ba)

@@ -57,7 +57,9 @@ class MLAAttention:
         latent = B.rmsnorm(ckv[:, :dc], self.kv_a_norm, self.cfg.norm_eps)
         k_rope = ckv[:, dc:].contiguous().view(T, 1, dr)
         q_rope = q[:, :, dn:].contiguous()
-        if x.is_cuda:
+        if not self.cfg.mla_rope:
+            pass                         # NoPE MLA: the rope dims take part in the scores unrotated
+        elif x.is_cuda:
             B.rope_and_cache(q_rope, k_rope, k_rope, meta.positions, rope, dr, self.cfg.rope_neox)
         else:
             q_rope = B.apply_rope_ref(q_rope, meta.positions, rope, dr, self.cfg.rope_neox)
@@ -77,11 +79,7 @@ class MLAAttention:
         return self.o(o.reshape(T, nh * dv))
 
     def _write_latent(self, entry, meta, k_cache):
-        bs = k_cache.shape[2]
-        sm = meta.slot_mapping.long()
-        valid = sm >= 0
-        blk, off = sm // bs, sm % bs
-        k_cache[blk[valid], 0, off[valid]] = entry[valid, 0].to(k_cache.dtype)
+        B.write_cache_rows(entry.to(k_cache.dtype).contiguous(), meta.slot_mapping, k_cache)
 
     def _prefill(self, q_nope, q_rope, meta, k_cache):
         if q_nope.is_cuda and (self.dn + self.dr, self.dv) in ((192, 128), (128, 128), (64, 64), (256, 256)):

@@ -17,7 +17,7 @@ from ..ops import gemm as G
 from ..ops import moe as M
 from ..ops.attention import AttnMetadata
 from .config import ModelConfig
-from .deltanet import DeltaNetState, GatedDeltaNet
+from .deltanet import DeltaNetState, GatedDeltaNet, KimiDeltaAttention
 from .layers import DenseMLP, GQAAttention, Linear, MoEBlock, RMSNorm
 from .mla import MLAAttention
 
@@ -353,7 +353,18 @@ def build_layer(f: WeightFactory, cfg: ModelConfig, i: int, expert_sink=None, na
     name = f"{name_prefix}.{i}"
     kind = cfg.layer_type(min(i, cfg.num_layers - 1))
     dfmt = cfg.dense_fmt
-    if kind == "linear":
+    if kind == "linear" and cfg.linear_kind == "kda":
+        nk, nv, dk, dv = cfg.linear_num_key_heads, cfg.linear_num_value_heads, cfg.linear_key_head_dim, cfg.linear_value_head_dim
+        ch = 2 * nk * dk + nv * dv
+        attn = KimiDeltaAttention(
+            cfg, f.linear(name + ".kda_qkv", ch, H, dfmt), f.linear(name + ".kda_b", nv, H, "bf16"),
+            f.linear(name + ".kda_f_a", dk, H, "bf16"), f.linear(name + ".kda_f_b", nv * dk, dk, "bf16"),
+            f.linear(name + ".kda_g_a", dk, H, "bf16"), f.linear(name + ".kda_g_b", nv * dv, dk, "bf16"),
+            f.normal(name + ".conv", (ch, cfg.linear_conv_kernel), 0.3),
+            f.param(name + ".A_log", lambda n: torch.log(torch.linspace(1.0, 16.0, n, device=f.device)).float(), nv),
+            f.param(name + ".dt_bias", lambda n: torch.zeros(n, device=f.device).float(), nv * dk),
+            f.ones((dv,), name=name + ".gdn_norm"), f.linear(name + ".out", H, nv * dv, dfmt))
+    elif kind == "linear":
         nk, nv, dk, dv = cfg.linear_num_key_heads, cfg.linear_num_value_heads, cfg.linear_key_head_dim, cfg.linear_value_head_dim
         ch = 2 * nk * dk + nv * dv
         attn = GatedDeltaNet(cfg, f.linear(name + ".qkvz", 2 * nk * dk + 2 * nv * dv, H, dfmt),

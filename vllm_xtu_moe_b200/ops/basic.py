@@ -170,6 +170,23 @@ def write_kv(k, v, slot_mapping, k_cache, v_cache):
            k_cache.shape[0] * k_cache.shape[2], N.status_buffer(k.device).data_ptr(), N.stream_ptr(k.device))
 
 
+def write_cache_rows(x, slot_mapping, cache):
+    """cache[slot // bs, :, slot % bs] = x[t] for every token t with slot >= 0 (x [T, H, D]
+    bf16, cache [blocks, H, bs, D]): one kernel, no host synchronisation, so it can be
+    captured in a CUDA graph (the MLA latent cache, which has no separate V cache)."""
+    if not x.is_cuda:
+        bs = cache.shape[2]
+        sm = slot_mapping.long()
+        valid = sm >= 0
+        cache[(sm // bs)[valid], :, (sm % bs)[valid]] = x[valid].to(cache.dtype)
+        return
+    T, H, D = x.shape
+    assert x.stride(2) == 1 and x.stride(1) == D and x.dtype == cache.dtype == torch.bfloat16
+    N.call("xtu_kv_write", x.data_ptr(), x.data_ptr(), T, H, D, 0, x.stride(0), x.stride(0),
+           slot_mapping.data_ptr(), cache.data_ptr(), cache.data_ptr(), cache.shape[2],
+           cache.shape[0] * cache.shape[2], N.status_buffer(x.device).data_ptr(), N.stream_ptr(x.device))
+
+
 # ---------------------------------------------------------------------------
 # embedding / argmax / silu
 # ---------------------------------------------------------------------------

@@ -38,6 +38,8 @@ def local_config(cfg: ModelConfig, tp: int) -> ModelConfig:
         if x % tp:
             raise ValueError(f"{what}={x} is not divisible by tensor-parallel size {tp}")
         return x // tp
+    if cfg.linear_kind == "kda" and tp > 1 and cfg.layer_types and "linear" in cfg.layer_types:
+        raise ValueError("tensor parallelism is not built for Kimi Delta Attention layers")
     kw = dict(num_heads=div(cfg.num_heads, "num_heads"))
     if not cfg.is_mla:
         for key in ("num_kv_heads", "swa_num_kv_heads"):
