@@ -25,6 +25,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
+#include <cstdlib>
 #include <cstdint>
 #include <cfloat>
 #include "ptx.cuh"
@@ -66,7 +67,7 @@ struct AttnParams {
 // whole block list so the producer never waits on a dependent global load.
 // VK: V is the first dims of K (MLA latent cache) and is read from the K stage itself;
 // the CTA then computes DV output columns starting at its half's offset.
-template <int D, int DV, int BN, int STAGES_ = 2, int BTS = 0, int VK = 0>
+template <int D, int DV, int BN, int STAGES_ = 2, int BTS = 0, int VK = 0, int CS = 1>
 struct AttnCfg {
   static constexpr int STAGES = STAGES_;
   static constexpr int Q_BYTES = 128 * D * 2;
@@ -78,7 +79,11 @@ struct AttnCfg {
   static constexpr int S_COL0 = 0;          // two S buffers: [0, BN), [BN, 2BN)
   static constexpr int O_COL0 = 2 * BN;     // O: [2BN, 2BN + DV)
   static constexpr int TMEM_COLS = (2 * BN + DV) <= 256 ? 256 : 512;
+  static constexpr int XC = 2 * BN + DV;    // CS > 1: 4 exchange columns [XC, XC + 4)
+  static constexpr int THREADS = 64 + 128 * CS;
   static_assert(2 * BN + DV <= 512, "TMEM budget");
+  static_assert(CS == 1 || XC + 4 <= TMEM_COLS, "exchange columns");
+  static_assert(CS == 1 || ((BN / CS) % 16 == 0 && (DV / CS) % 32 == 0 && VK == 0), "column split");
   static_assert(D % 64 == 0 && DV % 64 == 0 && BN % 16 == 0 && (BN % 64 == 0 || 64 % BN == 0), "tile shapes");
 };
 
@@ -92,11 +97,16 @@ __device__ __forceinline__ void st_sw128(uint8_t* tile, int rows, int row, int c
 
 // EXT: the sliding window and the sinks of AttnParams are honoured (EXT = 0 compiles the
 // plain causal kernel, whose softmax loop carries no extra compare).
-template <int D, int DV, int BN, int STAGES_, int BTS, int VK, int EXT>
-__global__ void __launch_bounds__(192, 1)
+// CS: softmax warps per TMEM lane quarter.  CS = 2 gives each row two threads in two warps
+// (8 softmax warps, two per scheduler), each scoring half of every tile's keys; per tile
+// they swap their partial row max through four spare TMEM columns (an mbarrier round,
+// bounded like every wait here), so both keep the same running max, and they swap their
+// partial sums once at the end.  Each half rescales and writes half of O's columns.
+template <int D, int DV, int BN, int STAGES_, int BTS, int VK, int EXT, int CS>
+__global__ void __launch_bounds__(64 + 128 * CS, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
                     AttnParams p) {
-  using C = AttnCfg<D, DV, BN, STAGES_, BTS, VK>;
+  using C = AttnCfg<D, DV, BN, STAGES_, BTS, VK, CS>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
@@ -112,7 +122,8 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* s_full = q_ready + 1;                    // [2]
   uint64_t* p_full = s_full + 2;                     // [2]
   uint64_t* o_done = p_full + 2;                     // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 2);
+  uint64_t* xb = o_done + 2;                         // [2] CS > 1: partial-max exchange rounds
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xb + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = blockIdx.z;
@@ -142,7 +153,12 @@ __global__ void __launch_bounds__(192, 1)
     prefetch_tmap(&tmap_v);
     for (int s = 0; s < C::STAGES; ++s) { mbar_init(&kv_full[s], 1); mbar_init(&kv_empty[s], 1); }
     mbar_init(q_ready, 4);
-    for (int i = 0; i < 2; ++i) { mbar_init(&s_full[i], 1); mbar_init(&p_full[i], 4); mbar_init(&o_done[i], 1); }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 4 * CS);
+      mbar_init(&o_done[i], 1);
+      mbar_init(&xb[i], 4 * CS);
+    }
     fence_barrier_init();
   }
   if (warp == 1) tmem_alloc(tmem_slot, C::TMEM_COLS);
@@ -271,9 +287,11 @@ __global__ void __launch_bounds__(192, 1)
     // replicas' (max, sum, O) are merged in the epilogue.
     const int qd = warp & 3;
     const int r = qd * 32 + lane;
-    const int RF = p.rf;
+    const int half = CS > 1 ? (warp - 2) >> 2 : 0;   // CS > 1: which half of each tile's keys
+    const int RF = CS > 1 ? 1 : p.rf;
     const int LR = 128 / RF;                 // logical rows
-    const int KP = BN / RF;                  // keys per replica per tile
+    constexpr int KPC = BN / CS;
+    const int KP = CS > 1 ? KPC : BN / RF;   // keys per replica (or per half) per tile
     const int lr = r % LR;
     const int part = r / LR;
     const int rows_valid_all = min(p.rows_per_tile, n_pos * p.G);
@@ -282,8 +300,8 @@ __global__ void __launch_bounds__(192, 1)
     const int tok = q0 + i0 + pi;
     const int head = kvh * p.G + g;
     const int qpos = ctx0 + i0 + pi;
-    // load this row of Q into swizzled smem
-    {
+    // load this row of Q into swizzled smem (the first half's warps)
+    if (half == 0) {
       const __nv_bfloat16* src = p.q + (size_t)tok * p.q_stride + (size_t)head * D;
 #pragma unroll 4
       for (int c8 = 0; c8 < D; c8 += 8) {
@@ -301,19 +319,38 @@ __global__ void __launch_bounds__(192, 1)
     const bool warp_active = ((qd * 32) % LR) < rows_valid_all;
     if (RF > 1 || !warp_active) {
 #pragma unroll 1
-      for (int c8 = 0; c8 < BN; c8 += 8) {
+      for (int c8 = half * KPC; c8 < (half + 1) * KPC; c8 += 8) {
         st_sw128(sP, 128, r, c8, make_uint4(0, 0, 0, 0));
         st_sw128(sP + C::P_BYTES, 128, r, c8, make_uint4(0, 0, 0, 0));
       }
     }
     fence_proxy_async_smem();
     __syncwarp();
-    if (lane == 0) mbar_arrive(q_ready);
+    if (lane == 0 && half == 0) mbar_arrive(q_ready);
     bool ok = true;
+    // CS > 1: swap one float with the other half's thread of this row (exchange round `rd`;
+    // the two TMEM column pairs alternate so a column is rewritten only after both read it)
+    auto xchg = [&](int rd, float mine) -> float {
+      const uint32_t col = C::XC + 2 * (rd & 1);
+      tmem_st1(lane_base + col + half, __float_as_uint(mine));
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&xb[rd & 1]);
+      if (!__all_sync(0xffffffffu, mbar_wait(&xb[rd & 1], (rd >> 1) & 1, p.status, 124))) {
+        ok = false;
+        return mine;
+      }
+      tc_fence_after();
+      const uint32_t v = tmem_ld1(lane_base + col + (half ^ 1));
+      tmem_wait_ld();
+      return __uint_as_float(v);
+    };
     for (int jj = 0; jj < n_tiles && ok; ++jj) {
       const int j = t_begin + jj;
       if (!mbar_wait(&s_full[jj & 1], (jj >> 1) & 1, p.status, 120)) { ok = false; break; }
       if (!warp_active) {
+        if (CS > 1) (void)xchg(jj, -FLT_MAX);   // keep the exchange rounds in step
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[jj & 1]);
         continue;
@@ -321,12 +358,12 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_after();
       const uint32_t s_addr = lane_base + C::S_COL0 + (jj & 1) * BN;
       const int key0 = j * BN;
-      const int c_lo = part * KP;
-      // this replica's S columns -> registers, one TMEM round trip per tile.  KP is a
-      // multiple of 16 (BN >= 64, RF <= 4), so 16-column chunks never pass the range.
-      uint32_t sv[BN];
+      const int c_lo = CS > 1 ? half * KPC : part * KP;
+      // this replica's (half's) S columns -> registers, one TMEM round trip per tile.  KP is
+      // a multiple of 16 (BN >= 64, RF <= 4), so 16-column chunks never pass the range.
+      uint32_t sv[KPC];
 #pragma unroll
-      for (int ch = 0; ch < BN / 16; ++ch)
+      for (int ch = 0; ch < KPC / 16; ++ch)
         if (ch * 16 < KP) tmem_ld16p(s_addr + c_lo + ch * 16, sv + ch * 16);
       tmem_wait_ld();
       // keys t <= lim of the range are visible to this row (causal limit; kv_len follows from it)
@@ -336,7 +373,7 @@ __global__ void __launch_bounds__(192, 1)
       const bool all_vis = __all_sync(0xffffffffu, lim >= KP - 1 && (!EXT || low <= 0));
       float mx4[4] = {-FLT_MAX, -FLT_MAX, -FLT_MAX, -FLT_MAX};
 #pragma unroll
-      for (int ch = 0; ch < BN / 16; ++ch) {
+      for (int ch = 0; ch < KPC / 16; ++ch) {
         if (ch * 16 < KP) {
 #pragma unroll
           for (int t = 0; t < 16; ++t) {
@@ -347,6 +384,10 @@ __global__ void __launch_bounds__(192, 1)
       }
       float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
       if (mx != -FLT_MAX) mx *= p.scale_log2;   // scale > 0: max commutes with it
+      if (CS > 1) {
+        mx = fmaxf(mx, xchg(jj, mx));            // the row's max over both halves
+        if (!ok) break;
+      }
       // Raise the running max only when it grows by more than 2^8.  tcgen05.ld/st are
       // warp-collective (.sync.aligned), so the O rescale is decided per warp: if any
       // row of the warp needs it, the whole warp rescales (alpha = 1 for the others).
@@ -362,7 +403,7 @@ __global__ void __launch_bounds__(192, 1)
         const float alpha = lane_rescale ? ex2(m - m_new) : 1.f;
         l *= alpha;
 #pragma unroll 1
-        for (int c = 0; c < DV; c += 16) {
+        for (int c = half * (DV / CS); c < (half + 1) * (DV / CS); c += 16) {
           uint32_t o16[16];
           tmem_ld16(lane_base + C::O_COL0 + c, o16);
           tmem_wait_ld();
@@ -383,7 +424,7 @@ __global__ void __launch_bounds__(192, 1)
       const bool live = row_valid && m_use != -FLT_MAX;
       float rs4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int ch = 0; ch < BN / 16; ++ch) {
+      for (int ch = 0; ch < KPC / 16; ++ch) {
         if (ch * 16 < KP) {
           uint32_t pk[8];
 #pragma unroll
@@ -417,6 +458,8 @@ __global__ void __launch_bounds__(192, 1)
       have_o = mbar_wait(&o_done[last & 1], (last >> 1) & 1, p.status, 123);
       tc_fence_after();
     }
+    if (CS > 1 && n_tiles > 0 && ok) l += xchg(n_tiles, l);   // the row's sum over both halves
+    if (CS > 1 && !ok) have_o = false;
     // the sink joins the softmax denominator once: here when there is one split, else in
     // attn_combine_kernel
     const float sink_l2 = (EXT && p.sinks != nullptr && p.splits == 1 && row_valid)
@@ -426,7 +469,7 @@ __global__ void __launch_bounds__(192, 1)
         if (sink_l2 != -FLT_MAX && m != -FLT_MAX) l += ex2(sink_l2 - m);
         const float inv = l > 0.f ? 1.f / l : 0.f;
 #pragma unroll 1
-        for (int c = 0; c < DV; c += 32) {
+        for (int c = half * (DV / CS); c < (half + 1) * (DV / CS); c += 32) {
           uint32_t v[32];
           tmem_ld32(lane_base + C::O_COL0 + c, v);
           tmem_wait_ld();
@@ -448,9 +491,9 @@ __global__ void __launch_bounds__(192, 1)
                                   __uint_as_float(v[4 * t + 2]) * inv, __uint_as_float(v[4 * t + 3]) * inv);
           }
         }
-        if (p.splits > 1 && row_valid)
+        if (p.splits > 1 && row_valid && half == 0)
           p.ws_lse[((size_t)split * p.T + tok) * p.Hq + head] = l > 0.f ? m + log2f(l) : -FLT_MAX;
-      } else if (n_tiles == 0 && p.splits > 1 && row_valid) {
+      } else if (n_tiles == 0 && p.splits > 1 && row_valid && half == 0) {
         float* dst = p.ws_o + (((size_t)split * p.T + tok) * p.Hq + head) * dv_tot + dv_off;
         for (int c = 0; c < DV; ++c) dst[c] = 0.f;
         p.ws_lse[((size_t)split * p.T + tok) * p.Hq + head] = -FLT_MAX;
@@ -586,11 +629,11 @@ static int attn_tmap(CUtensorMap* map, const void* base, uint64_t rows, uint64_t
   return r == CUDA_SUCCESS ? 0 : -1000 - (int)r;
 }
 
-template <int D, int DV, int BN, int STAGES = 2, int BTS = 0, int VK = 0, int EXT = 0>
+template <int D, int DV, int BN, int STAGES = 2, int BTS = 0, int VK = 0, int EXT = 0, int CS = 1>
 static int launch_attn(const CUtensorMap& tk, const CUtensorMap& tv, const AttnParams& p, int grid_x, int B,
                        cudaStream_t s) {
-  using C = AttnCfg<D, DV, BN, STAGES, BTS, VK>;
-  auto k = attn_fwd_kernel<D, DV, BN, STAGES, BTS, VK, EXT>;
+  using C = AttnCfg<D, DV, BN, STAGES, BTS, VK, CS>;
+  auto k = attn_fwd_kernel<D, DV, BN, STAGES, BTS, VK, EXT, CS>;
   static bool init = false;
   if (!init) {
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
@@ -598,9 +641,20 @@ static int launch_attn(const CUtensorMap& tk, const CUtensorMap& tv, const AttnP
     init = true;
   }
   dim3 grid(grid_x, p.Hkv * p.splits * p.dv_halves, B);
-  k<<<grid, 192, C::SMEM, s>>>(tk, tv, p);
+  k<<<grid, C::THREADS, C::SMEM, s>>>(tk, tv, p);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 1 : -(int)e;
+}
+
+// XTU_ATTN_CS=1 in the environment selects the one-thread-per-row softmax for prefill
+// tiles of 128-wide heads (the default splits each row's keys over two threads)
+static bool attn_split_softmax() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("XTU_ATTN_CS");
+    v = (e && e[0] == '1') ? 0 : 1;
+  }
+  return v == 1;
 }
 
 extern "C" {
@@ -675,6 +729,9 @@ int xtu_paged_attention(const void* q, int q_stride, const void* k_cache, const 
   else if (decode_shape && D == 64 && DV == 64)
     r = ext ? launch_attn<64, 64, 64, 6, 1024, 0, 1>(tk, tv, p, grid_x, B, s)
             : launch_attn<64, 64, 64, 6, 1024>(tk, tv, p, grid_x, B, s);
+  else if (D == 128 && DV == 128 && attn_split_softmax())   // two softmax threads per row
+    r = ext ? launch_attn<128, 128, 128, 2, 0, 0, 1, 2>(tk, tv, p, grid_x, B, s)
+            : launch_attn<128, 128, 128, 2, 0, 0, 0, 2>(tk, tv, p, grid_x, B, s);
   else if (D == 128 && DV == 128)
     r = ext ? launch_attn<128, 128, 128, 2, 0, 0, 1>(tk, tv, p, grid_x, B, s)
             : launch_attn<128, 128, 128>(tk, tv, p, grid_x, B, s);
