@@ -79,10 +79,10 @@ struct AttnCfg {
   static constexpr int S_COL0 = 0;          // two S buffers: [0, BN), [BN, 2BN)
   static constexpr int O_COL0 = 2 * BN;     // O: [2BN, 2BN + DV)
   static constexpr int TMEM_COLS = (2 * BN + DV) <= 256 ? 256 : 512;
-  static constexpr int XC = 2 * BN + DV;    // CS > 1: 4 exchange columns [XC, XC + 4)
+  static constexpr int XC = 2 * BN + DV;    // CS > 1: 2 * CS exchange columns from XC
   static constexpr int THREADS = 64 + 128 * CS;
   static_assert(2 * BN + DV <= 512, "TMEM budget");
-  static_assert(CS == 1 || XC + 4 <= TMEM_COLS, "exchange columns");
+  static_assert(CS == 1 || XC + 2 * CS <= TMEM_COLS, "exchange columns");
   static_assert(CS == 1 || ((BN / CS) % 16 == 0 && (DV / CS) % 32 == 0 && VK == 0), "column split");
   static_assert(D % 64 == 0 && DV % 64 == 0 && BN % 16 == 0 && (BN % 64 == 0 || 64 % BN == 0), "tile shapes");
 };
@@ -97,11 +97,11 @@ __device__ __forceinline__ void st_sw128(uint8_t* tile, int rows, int row, int c
 
 // EXT: the sliding window and the sinks of AttnParams are honoured (EXT = 0 compiles the
 // plain causal kernel, whose softmax loop carries no extra compare).
-// CS: softmax warps per TMEM lane quarter.  CS = 2 gives each row two threads in two warps
-// (8 softmax warps, two per scheduler), each scoring half of every tile's keys; per tile
-// they swap their partial row max through four spare TMEM columns (an mbarrier round,
-// bounded like every wait here), so both keep the same running max, and they swap their
-// partial sums once at the end.  Each half rescales and writes half of O's columns.
+// CS: softmax warps per TMEM lane quarter.  CS > 1 gives each row CS threads in CS warps
+// (4 * CS softmax warps, CS per scheduler), each scoring 1/CS of every tile's keys; per
+// tile they swap their partial row max through 2 * CS spare TMEM columns (an mbarrier
+// round, bounded like every wait here), so all keep the same running max, and they swap
+// their partial sums once at the end.  Each part rescales and writes 1/CS of O's columns.
 template <int D, int DV, int BN, int STAGES_, int BTS, int VK, int EXT, int CS>
 __global__ void __launch_bounds__(64 + 128 * CS, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
@@ -287,7 +287,7 @@ __global__ void __launch_bounds__(64 + 128 * CS, 1)
     // replicas' (max, sum, O) are merged in the epilogue.
     const int qd = warp & 3;
     const int r = qd * 32 + lane;
-    const int half = CS > 1 ? (warp - 2) >> 2 : 0;   // CS > 1: which half of each tile's keys
+    const int half = CS > 1 ? (warp - 2) >> 2 : 0;   // CS > 1: which part of each tile's keys
     const int RF = CS > 1 ? 1 : p.rf;
     const int LR = 128 / RF;                 // logical rows
     constexpr int KPC = BN / CS;
@@ -328,10 +328,11 @@ __global__ void __launch_bounds__(64 + 128 * CS, 1)
     __syncwarp();
     if (lane == 0 && half == 0) mbar_arrive(q_ready);
     bool ok = true;
-    // CS > 1: swap one float with the other half's thread of this row (exchange round `rd`;
-    // the two TMEM column pairs alternate so a column is rewritten only after both read it)
-    auto xchg = [&](int rd, float mine) -> float {
-      const uint32_t col = C::XC + 2 * (rd & 1);
+    // CS > 1: combine one float with the other parts' threads of this row, as a max or a
+    // sum (exchange round `rd`; the two column groups alternate, so a column is rewritten
+    // only after every part has read it)
+    auto xchg = [&](int rd, float mine, bool is_max) -> float {
+      const uint32_t col = C::XC + CS * (rd & 1);
       tmem_st1(lane_base + col + half, __float_as_uint(mine));
       tmem_wait_st();
       tc_fence_before();
@@ -342,15 +343,20 @@ __global__ void __launch_bounds__(64 + 128 * CS, 1)
         return mine;
       }
       tc_fence_after();
-      const uint32_t v = tmem_ld1(lane_base + col + (half ^ 1));
+      uint32_t v[CS];
+#pragma unroll
+      for (int q = 0; q < CS; ++q) v[q] = tmem_ld1(lane_base + col + q);
       tmem_wait_ld();
-      return __uint_as_float(v);
+      float acc = is_max ? -FLT_MAX : 0.f;     // every part in part order: identical in all
+#pragma unroll
+      for (int q = 0; q < CS; ++q) acc = is_max ? fmaxf(acc, __uint_as_float(v[q])) : acc + __uint_as_float(v[q]);
+      return acc;
     };
     for (int jj = 0; jj < n_tiles && ok; ++jj) {
       const int j = t_begin + jj;
       if (!mbar_wait(&s_full[jj & 1], (jj >> 1) & 1, p.status, 120)) { ok = false; break; }
       if (!warp_active) {
-        if (CS > 1) (void)xchg(jj, -FLT_MAX);   // keep the exchange rounds in step
+        if (CS > 1) (void)xchg(jj, -FLT_MAX, true);   // keep the exchange rounds in step
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[jj & 1]);
         continue;
@@ -385,7 +391,7 @@ __global__ void __launch_bounds__(64 + 128 * CS, 1)
       float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
       if (mx != -FLT_MAX) mx *= p.scale_log2;   // scale > 0: max commutes with it
       if (CS > 1) {
-        mx = fmaxf(mx, xchg(jj, mx));            // the row's max over both halves
+        mx = xchg(jj, mx, true);                   // the row's max over all parts
         if (!ok) break;
       }
       // Raise the running max only when it grows by more than 2^8.  tcgen05.ld/st are
@@ -458,7 +464,7 @@ __global__ void __launch_bounds__(64 + 128 * CS, 1)
       have_o = mbar_wait(&o_done[last & 1], (last >> 1) & 1, p.status, 123);
       tc_fence_after();
     }
-    if (CS > 1 && n_tiles > 0 && ok) l += xchg(n_tiles, l);   // the row's sum over both halves
+    if (CS > 1 && n_tiles > 0 && ok) l = xchg(n_tiles, l, false);   // the row's sum over all parts
     if (CS > 1 && !ok) have_o = false;
     // the sink joins the softmax denominator once: here when there is one split, else in
     // attn_combine_kernel
@@ -646,15 +652,16 @@ static int launch_attn(const CUtensorMap& tk, const CUtensorMap& tv, const AttnP
   return e == cudaSuccess ? 1 : -(int)e;
 }
 
-// XTU_ATTN_CS=1 in the environment selects the one-thread-per-row softmax for prefill
-// tiles of 128-wide heads (the default splits each row's keys over two threads)
-static bool attn_split_softmax() {
-  static int v = -1;
-  if (v < 0) {
+// Softmax threads per row for prefill tiles of 128-wide heads: XTU_ATTN_CS = 1, 2 or 4
+// in the environment (default 2; at 8K causal GQA tokens 1 / 2 / 4 measured 483 / 598 /
+// 569 TFLOP/s: past two parts the exchange rounds cost more than the parallelism gains)
+static int attn_softmax_parts() {
+  static int v = 0;
+  if (v == 0) {
     const char* e = getenv("XTU_ATTN_CS");
-    v = (e && e[0] == '1') ? 0 : 1;
+    v = (e && (e[0] == '1' || e[0] == '4')) ? e[0] - '0' : 2;
   }
-  return v == 1;
+  return v;
 }
 
 extern "C" {
@@ -729,7 +736,10 @@ int xtu_paged_attention(const void* q, int q_stride, const void* k_cache, const 
   else if (decode_shape && D == 64 && DV == 64)
     r = ext ? launch_attn<64, 64, 64, 6, 1024, 0, 1>(tk, tv, p, grid_x, B, s)
             : launch_attn<64, 64, 64, 6, 1024>(tk, tv, p, grid_x, B, s);
-  else if (D == 128 && DV == 128 && attn_split_softmax())   // two softmax threads per row
+  else if (D == 128 && DV == 128 && attn_softmax_parts() == 4)   // four softmax threads per row
+    r = ext ? launch_attn<128, 128, 128, 2, 0, 0, 1, 4>(tk, tv, p, grid_x, B, s)
+            : launch_attn<128, 128, 128, 2, 0, 0, 0, 4>(tk, tv, p, grid_x, B, s);
+  else if (D == 128 && DV == 128 && attn_softmax_parts() == 2)   // two softmax threads per row
     r = ext ? launch_attn<128, 128, 128, 2, 0, 0, 1, 2>(tk, tv, p, grid_x, B, s)
             : launch_attn<128, 128, 128, 2, 0, 0, 0, 2>(tk, tv, p, grid_x, B, s);
   else if (D == 128 && DV == 128)
