@@ -78,8 +78,8 @@ struct AttnCfg {
   static constexpr int SMEM = Q_BYTES + STAGES * (K_BYTES + V_BYTES) + 2 * P_BYTES + BT_BYTES + 1024 + 256;
   static constexpr int S_COL0 = 0;          // two S buffers: [0, BN), [BN, 2BN)
   static constexpr int O_COL0 = 2 * BN;     // O: [2BN, 2BN + DV)
-  static constexpr int TMEM_COLS = (2 * BN + DV) <= 256 ? 256 : 512;
   static constexpr int XC = 2 * BN + DV;    // CS > 1: 2 * CS exchange columns from XC
+  static constexpr int TMEM_COLS = (XC + (CS > 1 ? 2 * CS : 0)) <= 256 ? 256 : 512;
   static constexpr int THREADS = 64 + 128 * CS;
   static_assert(2 * BN + DV <= 512, "TMEM budget");
   static_assert(CS == 1 || XC + 2 * CS <= TMEM_COLS, "exchange columns");
@@ -745,15 +745,22 @@ int xtu_paged_attention(const void* q, int q_stride, const void* k_cache, const 
   else if (D == 128 && DV == 128)
     r = ext ? launch_attn<128, 128, 128, 2, 0, 0, 1>(tk, tv, p, grid_x, B, s)
             : launch_attn<128, 128, 128>(tk, tv, p, grid_x, B, s);
+  // the other prefill shapes: two softmax threads per row unless XTU_ATTN_CS=1
   else if (D == 64 && DV == 64)
-    r = ext ? launch_attn<64, 64, 128, 2, 0, 0, 1>(tk, tv, p, grid_x, B, s)
-            : launch_attn<64, 64, 128>(tk, tv, p, grid_x, B, s);
+    r = attn_softmax_parts() == 1 ? (ext ? launch_attn<64, 64, 128, 2, 0, 0, 1>(tk, tv, p, grid_x, B, s)
+                                         : launch_attn<64, 64, 128>(tk, tv, p, grid_x, B, s))
+                                  : (ext ? launch_attn<64, 64, 128, 2, 0, 0, 1, 2>(tk, tv, p, grid_x, B, s)
+                                         : launch_attn<64, 64, 128, 2, 0, 0, 0, 2>(tk, tv, p, grid_x, B, s));
   else if (D == 256 && DV == 256)
-    r = ext ? launch_attn<256, 256, 64, 2, 0, 0, 1>(tk, tv, p, grid_x, B, s)
-            : launch_attn<256, 256, 64>(tk, tv, p, grid_x, B, s);
+    r = attn_softmax_parts() == 1 ? (ext ? launch_attn<256, 256, 64, 2, 0, 0, 1>(tk, tv, p, grid_x, B, s)
+                                         : launch_attn<256, 256, 64>(tk, tv, p, grid_x, B, s))
+                                  : (ext ? launch_attn<256, 256, 64, 2, 0, 0, 1, 2>(tk, tv, p, grid_x, B, s)
+                                         : launch_attn<256, 256, 64, 2, 0, 0, 0, 2>(tk, tv, p, grid_x, B, s));
   else if (D == 192 && DV == 128)
-    r = ext ? launch_attn<192, 128, 64, 2, 0, 0, 1>(tk, tv, p, grid_x, B, s)
-            : launch_attn<192, 128, 64>(tk, tv, p, grid_x, B, s);
+    r = attn_softmax_parts() == 1 ? (ext ? launch_attn<192, 128, 64, 2, 0, 0, 1>(tk, tv, p, grid_x, B, s)
+                                         : launch_attn<192, 128, 64>(tk, tv, p, grid_x, B, s))
+                                  : (ext ? launch_attn<192, 128, 64, 2, 0, 0, 1, 2>(tk, tv, p, grid_x, B, s)
+                                         : launch_attn<192, 128, 64, 2, 0, 0, 0, 2>(tk, tv, p, grid_x, B, s));
   else return -6;
   if (r < 0) return r;
   if (p.splits > 1) {
