@@ -378,13 +378,20 @@ __global__ void __launch_bounds__(64 + 128 * CS, 1)
       const int low = (EXT && p.window > 0) ? qpos - p.window + 1 - (key0 + c_lo) : 0;
       const bool all_vis = __all_sync(0xffffffffu, lim >= KP - 1 && (!EXT || low <= 0));
       float mx4[4] = {-FLT_MAX, -FLT_MAX, -FLT_MAX, -FLT_MAX};
+      if (CS > 1 && all_vis) {
+        // whole range visible: two keys per three-input max (half the ALU instructions)
 #pragma unroll
-      for (int ch = 0; ch < KPC / 16; ++ch) {
-        if (ch * 16 < KP) {
+        for (int i = 0; i < KPC; i += 2)
+          mx4[(i >> 1) & 3] = fmax3(mx4[(i >> 1) & 3], __uint_as_float(sv[i]), __uint_as_float(sv[i + 1]));
+      } else {
 #pragma unroll
-          for (int t = 0; t < 16; ++t) {
-            const int i = ch * 16 + t;
-            if (all_vis || (i <= lim && (!EXT || i >= low))) mx4[t & 3] = fmaxf(mx4[t & 3], __uint_as_float(sv[i]));
+        for (int ch = 0; ch < KPC / 16; ++ch) {
+          if (ch * 16 < KP) {
+#pragma unroll
+            for (int t = 0; t < 16; ++t) {
+              const int i = ch * 16 + t;
+              if (all_vis || (i <= lim && (!EXT || i >= low))) mx4[t & 3] = fmaxf(mx4[t & 3], __uint_as_float(sv[i]));
+            }
           }
         }
       }

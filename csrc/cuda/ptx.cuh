@@ -256,6 +256,13 @@ __device__ __forceinline__ void tmem_ld16p(uint32_t taddr, uint32_t* r) {
       : "r"(taddr));
 }
 
+// max of three floats in one instruction (three-input max, sm_100)
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 // one 32-bit column of this warp's 32 TMEM lanes (value valid after tmem_wait_ld)
 __device__ __forceinline__ uint32_t tmem_ld1(uint32_t taddr) {
   uint32_t v;
