@@ -170,7 +170,12 @@ def test_peer_barrier_times_out_instead_of_hanging():
 def _tp_cfg(name):
     from vllm_xtu_moe_b200.models.config import get_preset, scaled_down
     cfg = get_preset(name)
-    return scaled_down(cfg, layers=4 if "qwen" in name else 2, hidden=256, experts=8).replace(
+    if name == "mimo-v2-flash":     # 2 full-attention KV heads, 4 sliding-window ones, window 8
+        return scaled_down(cfg, layers=4, hidden=256, experts=8).replace(
+            num_heads=4, num_kv_heads=2, swa_num_kv_heads=4, head_dim=64, v_head_dim=32, rotary_dim=32,
+            sliding_window=8, moe_intermediate=256, dense_intermediate=512, num_mtp_layers=0, dense_fmt="bf16",
+            expert_fmt="bf16")
+    return scaled_down(cfg, layers=4 if ("qwen" in name or "kimi" in name) else 2, hidden=256, experts=8).replace(
         num_heads=4, num_kv_heads=2, head_dim=64 if not cfg.is_mla else cfg.head_dim, moe_intermediate=256,
         shared_intermediate=256, dense_intermediate=512, linear_num_key_heads=2, linear_num_value_heads=4,
         linear_key_head_dim=32, linear_value_head_dim=32, q_lora_rank=64 if cfg.is_mla else 0,
@@ -211,7 +216,8 @@ def _tp_cpu_worker(rank, world, port, name):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("name", ["glm-4.5-air", "qwen3-next-80b-a3b", "deepseek-v3"])
+@pytest.mark.parametrize("name", ["glm-4.5-air", "qwen3-next-80b-a3b", "deepseek-v3", "kimi-linear-48b-a3b",
+                                  "mimo-v2-flash"])
 def test_tensor_parallel_matches_single_rank_cpu(name):
     mp.spawn(_tp_cpu_worker, args=(2, _port(), name), nprocs=2)
 

@@ -165,7 +165,7 @@ class KimiDeltaAttention:
             o = deltanet_ref(qkv, self.conv_w, g, beta, meta, state, self.nk, self.nv, self.dk, self.dv)
         of = o.float()
         y = of * torch.rsqrt(of.pow(2).mean(-1, keepdim=True) + self.cfg.norm_eps)
-        y = (y * self.norm_w.float() * torch.sigmoid(gate.float())).to(torch.bfloat16)
+        y = (y * self.norm_w.float() * torch.sigmoid(gate.float())).to(x.dtype)
         return self.out(y.reshape(T, self.nv * self.dv))
 
     def tensors(self):

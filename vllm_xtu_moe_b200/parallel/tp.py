@@ -38,8 +38,6 @@ def local_config(cfg: ModelConfig, tp: int) -> ModelConfig:
         if x % tp:
             raise ValueError(f"{what}={x} is not divisible by tensor-parallel size {tp}")
         return x // tp
-    if cfg.linear_kind == "kda" and tp > 1 and cfg.layer_types and "linear" in cfg.layer_types:
-        raise ValueError("tensor parallelism is not built for Kimi Delta Attention layers")
     kw = dict(num_heads=div(cfg.num_heads, "num_heads"))
     if not cfg.is_mla:
         for key in ("num_kv_heads", "swa_num_kv_heads"):
@@ -162,6 +160,19 @@ class TPWeightFactory:
         if suf == "kv_b":
             w = c.qk_nope_head_dim + c.v_head_dim
             return c.num_heads * w, c.kv_lora_rank, self._expand(self._heads(c.num_heads), w), None
+        if suf.startswith("kda_"):
+            nk, nv, dk, dv = c.linear_num_key_heads, c.linear_num_value_heads, c.linear_key_head_dim, c.linear_value_head_dim
+            if suf == "kda_qkv":     # blocked [Q | K | V]
+                rows = (self._expand(self._heads(nk), dk) + self._expand(self._heads(nk), dk, nk * dk) +
+                        self._expand(self._heads(nv), dv, 2 * nk * dk))
+                return 2 * nk * dk + nv * dv, H, rows, None
+            if suf == "kda_b":
+                return nv, H, self._heads(nv), None
+            if suf == "kda_f_b":
+                return nv * dk, dk, self._expand(self._heads(nv), dk), None
+            if suf == "kda_g_b":
+                return nv * dv, dk, self._expand(self._heads(nv), dv), None
+            return None              # kda_f_a, kda_g_a: the low-rank down-projections are replicated
         if suf in ("qkvz", "ba", "out") and c.linear_num_key_heads:
             nk, nv, dk, dv = c.linear_num_key_heads, c.linear_num_value_heads, c.linear_key_head_dim, c.linear_value_head_dim
             r = nv // nk
@@ -210,8 +221,13 @@ class TPWeightFactory:
         return self.base.zeros(shape, dtype, name=name)
 
     def param(self, name, make, n):
-        full_n = (self.full.linear_num_value_heads if name.endswith((".A_log", ".dt_bias"))
-                  else self.full.num_heads if name.endswith(".sinks") else n)
+        c = self.full
+        if name.endswith(".dt_bias") and c.linear_kind == "kda":
+            full_n = c.linear_num_value_heads * c.linear_key_head_dim      # one bias per (head, key dim)
+        elif name.endswith((".A_log", ".dt_bias")):
+            full_n = c.linear_num_value_heads
+        else:
+            full_n = c.num_heads if name.endswith(".sinks") else n
         t = self.base.param(name, make, full_n)
         if full_n != n:
             t = t[self.rank * n:(self.rank + 1) * n].contiguous()
