@@ -1049,6 +1049,23 @@ int xtu_embed(const int* ids, const void* table, int T, int H, int vocab, void* 
   return rc_last();
 }
 
+// The same lookup from a table in pinned host memory: the device reads the rows over the
+// host link through the table's mapped address (large tables kept off HBM, e.g. the
+// reference's per-layer-embedding offload).  Returns -3 if the table is not pinned.
+int xtu_embed_host(const int* ids, const void* host_table, int T, int H, int vocab, void* out, void* status,
+                   cudaStream_t s) {
+  if (T <= 0) return 0;
+  if (H % 8 != 0) return -2;
+  void* dtab = nullptr;
+  if (cudaHostGetDevicePointer(&dtab, const_cast<void*>(host_table), 0) != cudaSuccess || dtab == nullptr) {
+    cudaGetLastError();
+    return -3;
+  }
+  embed_kernel<<<T, 256, 0, s>>>(ids, (const __nv_bfloat16*)dtab, T, H, vocab, (__nv_bfloat16*)out,
+                                 reinterpret_cast<XtuStatus*>(status));
+  return rc_last();
+}
+
 int xtu_silu_mul(const void* x, int T, int I, float limit, float alpha, float beta, void* out, cudaStream_t s) {
   if (T <= 0) return 0;
   const size_t n = (size_t)T * I;

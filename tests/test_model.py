@@ -178,3 +178,20 @@ def test_gpu_decode_graph_matches_eager(which):
     torch.cuda.synchronize()
     N.check_status()
     assert outs[False] == outs[True]
+
+
+@pytest.mark.gpu
+def test_embedding_offloaded_to_pinned_host_memory():
+    """The token-embedding table kept in pinned host memory (read by the lookup kernel over
+    the host link) gives the same logits as the device-resident table, and frees its HBM."""
+    cfg = _glm_mini()
+    m = build_model(cfg, device="cuda", seed=6)
+    prompts = [list(range(3, 90)), list(range(40, 75))]
+    want = _prefill_logits(m, prompts)
+    freed = m.offload_embedding()
+    assert freed == cfg.vocab_size * cfg.hidden_size * 2
+    assert not m.embed_tokens.is_cuda and m.embed_tokens.is_pinned()
+    got = _prefill_logits(m, prompts)
+    torch.cuda.synchronize()
+    N.check_status()
+    assert torch.equal(got, want)

@@ -172,6 +172,17 @@ def _slice_raw(ex, fmt, a, b):
 
 
 @pytest.mark.gpu
+def test_embed_from_pinned_host_table():
+    tab = torch.randn(5000, 512).to(torch.bfloat16).pin_memory()
+    ids = torch.randint(0, 5000, (37,), dtype=torch.int32, device="cuda")
+    y = B.embed(ids, tab)
+    torch.cuda.synchronize()
+    assert y.is_cuda and torch.equal(y.cpu(), tab[ids.long().cpu()])
+    with pytest.raises(ValueError):
+        B.embed(ids, torch.randn(10, 512).to(torch.bfloat16))     # not pinned
+
+
+@pytest.mark.gpu
 def test_argmax_embed():
     torch.manual_seed(4)
     lg = torch.randn(7, 151552, device="cuda")

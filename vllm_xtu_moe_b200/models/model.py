@@ -78,7 +78,7 @@ class MoETransformer:
         self.norm = norm
         self.lm_head = lm_head
         self.mtp = mtp or []
-        self.device = embed.device
+        self.device = lm_head.device
         self.act_dtype = torch.bfloat16   # fp32 allowed on CPU (exact-reference runs)
         self.tracer = None
         self.rope = B.rope_cache(cfg.rot_dim, min(cfg.max_position, 1 << 18), cfg.rope_theta, self.device,
@@ -98,6 +98,21 @@ class MoETransformer:
                 l.mlp_norm.emit_f16s = mlp.experts is not None and mlp.experts.fmt == "fp8"
             else:
                 l.mlp_norm.emit_f16s = fp8_linear(getattr(mlp, "gate_up", None))
+
+    def offload_embedding(self) -> int:
+        """Keep the token-embedding table in pinned host memory instead of HBM (the rows a
+        step needs are read over the host link by the lookup kernel), as the reference does
+        for its large per-layer-embedding table (vllm_xiaotu_moe/ple_offload.py:176-267).
+        Returns the device bytes freed.  Not for tied embeddings (the LM head reads it)."""
+        if self.cfg.tie_embeddings or self.lm_head is self.embed_tokens:
+            raise ValueError("tied embeddings are read by the LM head; keep them on the device")
+        t = self.embed_tokens
+        if not t.is_cuda:
+            return 0
+        host = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+        host.copy_(t)
+        self.embed_tokens = host
+        return t.numel() * t.element_size()
 
     # ------------------------------------------------------------------
     def embed(self, ids: torch.Tensor) -> torch.Tensor:

@@ -47,6 +47,7 @@ _SIGS: dict[str, list] = {
     "xtu_moe_combine": [P, P, c_int, c_int, c_int, c_int, c_int, P, P, P, P, P],
     "xtu_argmax": [P, c_int, c_int, c_int, c_int, P, P, P, P],
     "xtu_embed": [P, P, c_int, c_int, c_int, P, P, P],
+    "xtu_embed_host": [P, P, c_int, c_int, c_int, P, P, P],
     "xtu_route_split": [P, c_int, c_int, c_int, P, P, P, P, P],
     "xtu_spec_verify": [P, P, P, c_int, c_int, P, P, P],
     "xtu_deltanet_fwd": [P, c_int, c_int, c_int, P, P, P, c_int, c_int, c_int, c_int, c_int, P, P, P, P, P,

@@ -191,13 +191,21 @@ def write_cache_rows(x, slot_mapping, cache):
 # embedding / argmax / silu
 # ---------------------------------------------------------------------------
 def embed(ids: torch.Tensor, table: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Rows of ``table`` for ``ids``.  With ids on a GPU the table may also be pinned host
+    memory: the kernel then reads the rows over the host link (HBM holds no copy)."""
     if not ids.is_cuda:
         return table[ids.long()]
     T = ids.numel()
     H = table.shape[1]
-    y = out if out is not None else torch.empty(T, H, dtype=table.dtype, device=table.device)
-    N.call("xtu_embed", ids.data_ptr(), table.data_ptr(), T, H, table.shape[0], y.data_ptr(),
-           N.status_buffer(ids.device).data_ptr(), N.stream_ptr(ids.device))
+    y = out if out is not None else torch.empty(T, H, dtype=table.dtype, device=ids.device)
+    if table.is_cuda:
+        N.call("xtu_embed", ids.data_ptr(), table.data_ptr(), T, H, table.shape[0], y.data_ptr(),
+               N.status_buffer(ids.device).data_ptr(), N.stream_ptr(ids.device))
+    else:
+        if not table.is_pinned() or table.dtype != torch.bfloat16 or not table.is_contiguous():
+            raise ValueError("a host-resident embedding table must be contiguous, bf16 and pinned")
+        N.call("xtu_embed_host", ids.data_ptr(), table.data_ptr(), T, H, table.shape[0], y.data_ptr(),
+               N.status_buffer(ids.device).data_ptr(), N.stream_ptr(ids.device))
     return y
 
 
