@@ -529,3 +529,54 @@ def test_tiny_mixtral_deferral_graphs_match_eager():
     graph, st_g = _tiny_tiered_llm_tokens(EngineConfig(moe_defer=True), True)
     assert graph == eager
     assert st_e["deferred"] > 0 and st_e["async"] > st_e["deferred"]   # 2 layers: the last never defers
+
+
+# ----------------------------------------------------------------------------- host-side fault injection
+def test_damaged_pin_tables_are_rejected(tmp_path):
+    """A corrupt XTUP table raises a clear error instead of pinning the wrong experts."""
+    good = tmp_path / "good.xtup"
+    save_pin_table(good, {0: [3, 1], 1: [2]}, n_experts=8)
+    assert load_pin_table(good) == {0: [3, 1], 1: [2]}
+    raw = good.read_bytes()
+    cases = {
+        "magic": b"XTUQ" + raw[4:],
+        "short header": raw[:10],
+        "truncated": raw[:-2],
+        "expert range": raw[:-4] + struct.pack("<HH", 1, 9),
+        "layer range": raw[:-4] + struct.pack("<HH", 7, 2),
+        "duplicate": raw[:-4] + struct.pack("<HH", 0, 3),
+    }
+    for name, data in cases.items():
+        p = tmp_path / f"{name.replace(' ', '_')}.xtup"
+        p.write_bytes(data)
+        with pytest.raises(ValueError):
+            load_pin_table(p)
+
+
+def test_failing_host_copy_raises(monkeypatch):
+    """A host-to-device copy that fails (the copy layer returns an error code, injected by a
+    fake) surfaces as an exception from the expert copy, never as a silently stale slot."""
+    from vllm_xtu_moe_b200.tiering import host as H
+    from vllm_xtu_moe_b200.tiering.cpu_engine import CpuExpertEngine
+    E, Hd, I = 4, 256, 128
+    g = torch.Generator().manual_seed(1)
+    eng = CpuExpertEngine("bf16", (torch.randn(E, 2 * I, Hd, generator=g) / 16).to(torch.bfloat16),
+                          (torch.randn(E, Hd, I, generator=g) / 16).to(torch.bfloat16), threads=2)
+    hx = H.HostExperts(eng, None, register=False)
+    calls = []
+
+    def fake_copy(dst, src, nbytes, stream):
+        calls.append(nbytes)
+        return -719                      # the error code of a failed cudaMemcpyAsync
+
+    monkeypatch.setattr(H, "_h2d", lambda: fake_copy)
+
+    class _Stream:
+        cuda_stream = 0
+
+    dst13 = torch.empty(2 * I, Hd, dtype=torch.bfloat16)
+    dst2 = torch.empty(Hd, I, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="cudaMemcpyAsync failed"):
+        hx.copy_expert(1, dst13, dst2, None, None, _Stream())
+    assert len(calls) == 1
+    eng.close()

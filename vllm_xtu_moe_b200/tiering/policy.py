@@ -25,16 +25,29 @@ _ENT = "<HH"
 
 
 def load_pin_table(path: str | Path) -> dict[int, list[int]]:
-    """layer -> experts, most frequent first."""
+    """layer -> experts, most frequent first.  A damaged table (wrong magic or version, a
+    header or entry count that runs past the file, a layer or expert outside the header's
+    ranges, an expert listed twice for one layer) raises ValueError naming the problem,
+    so a bad file never places the wrong experts silently."""
     buf = Path(path).read_bytes()
+    hsz, esz = struct.calcsize(_HDR), struct.calcsize(_ENT)
+    if len(buf) < hsz:
+        raise ValueError(f"XTUP table {path}: {len(buf)} bytes, shorter than its header")
     magic, ver, n_layers, n_experts, n_ent = struct.unpack_from(_HDR, buf, 0)
     if magic != b"XTUP" or ver != 1:
         raise ValueError(f"not an XTUP v1 table: {magic!r} v{ver}")
-    off = struct.calcsize(_HDR)
+    if len(buf) < hsz + esz * n_ent:
+        raise ValueError(f"XTUP table {path}: {n_ent} entries announced, {(len(buf) - hsz) // esz} present")
     out: dict[int, list[int]] = {}
     for i in range(n_ent):
-        layer, expert = struct.unpack_from(_ENT, buf, off + 4 * i)
-        out.setdefault(int(layer), []).append(int(expert))
+        layer, expert = struct.unpack_from(_ENT, buf, hsz + esz * i)
+        if layer >= n_layers or expert >= n_experts:
+            raise ValueError(f"XTUP table {path}: entry {i} (layer {layer}, expert {expert}) outside "
+                             f"{n_layers} layers x {n_experts} experts")
+        lst = out.setdefault(int(layer), [])
+        if expert in lst:
+            raise ValueError(f"XTUP table {path}: expert {expert} listed twice for layer {layer}")
+        lst.append(int(expert))
     return out
 
 
