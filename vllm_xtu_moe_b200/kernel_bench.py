@@ -231,6 +231,34 @@ def bench_deltanet(T=15000, nk=16, nv=32, dk=128, dv=128, kw=4, iters=3) -> dict
     return _report("deltanet_prefill", dict(T=T, nk=nk, nv=nv, dk=dk, dv=dv), ms, nbytes, flops)
 
 
+def bench_kda(T=15000, nh=32, dk=128, dv=128, kw=4, iters=3) -> dict:
+    """Kimi Delta Attention layer core (conv over blocked q|k|v rows + the delta rule with a
+    decay per key dim) over one long prompt, Kimi-Linear head shapes."""
+    from .models.config import get_preset
+    from .models.deltanet import DeltaNetState
+    from .ops.deltanet import deltanet_fwd
+    cfg = get_preset("kimi-linear-48b-a3b")
+    d = "cuda"
+    ch = 2 * nh * dk + nh * dv
+    qkv = (torch.randn(T, ch, device=d) * 0.5).to(torch.bfloat16)
+    conv_w = torch.randn(ch, kw, device=d) * 0.3
+    g = -torch.rand(T, nh, dk, device=d) * 0.5
+    beta = torch.rand(T, nh, device=d)
+    st = DeltaNetState(cfg, 1, d)
+    meta = AttnMetadata(num_seqs=1, q_start=torch.tensor([0, T], dtype=torch.int32, device=d),
+                        kv_len=torch.tensor([T], dtype=torch.int32, device=d),
+                        block_table=torch.zeros(1, 1, dtype=torch.int32, device=d),
+                        slot_mapping=torch.zeros(T, dtype=torch.int32, device=d),
+                        positions=torch.zeros(T, dtype=torch.int32, device=d), max_q_len=T, max_kv_len=T,
+                        is_decode=False, seq_slots=torch.zeros(1, dtype=torch.int32, device=d),
+                        seq_fresh=torch.ones(1, dtype=torch.int32, device=d))
+    fn = lambda: deltanet_fwd(qkv, conv_w, g, beta, meta, st, nh, nh, dk, dv, blocked=True)
+    ms = time_fn(fn, iters)
+    flops = T * nh * dk * dv * 2 * 5
+    nbytes = qkv.numel() * 2 + g.numel() * 4 + T * nh * dv * 4
+    return _report("kda_prefill", dict(T=T, nh=nh, dk=dk, dv=dv), ms, nbytes, flops)
+
+
 def bench_rmsnorm(T=16384, H=4096, iters=20) -> dict:
     x = torch.randn(T, H, device="cuda").to(torch.bfloat16)
     r = torch.randn(T, H, device="cuda").to(torch.bfloat16)
@@ -378,6 +406,7 @@ OPS = {
     "tp_fused": lambda a: bench_tp_fused(),
     "ep_fused": lambda a: bench_ep_fused(),
     "deltanet_prefill": lambda a: bench_deltanet(),
+    "kda_prefill": lambda a: bench_kda(),
     "cpu_bridge": lambda a: bench_cpu_bridge(),
 }
 
