@@ -195,3 +195,44 @@ def test_embedding_offloaded_to_pinned_host_memory():
     torch.cuda.synchronize()
     N.check_status()
     assert torch.equal(got, want)
+
+
+def _mimo_generate(device, bounded, graphs=False, bs=16, window=16, max_tokens=8):
+    cfg = _mimo_mini(head_dim=64 if device == "cpu" else 192, v_dim=32 if device == "cpu" else 128, window=window)
+    m = build_model(cfg, device=device, seed=3)
+    rc = RunnerConfig(block_size=bs, max_seqs=2, max_model_len=512, max_batched_tokens=64, use_cuda_graph=graphs,
+                      graph_batch_sizes=(1, 2), swa_bounded=bounded)
+    llm = LLM(m, device=device, runner_config=rc)
+    prompts = [list(range(1, 71)), list(range(9, 44))]
+    held = []
+    orig = llm.blocks.ensure
+
+    def ensure(req, upto):          # record how many window-pool blocks a request holds
+        ok = orig(req, upto)
+        held.append(len(req.swa_blocks))
+        return ok
+
+    llm.blocks.ensure = ensure
+    toks = [o.token_ids for o in llm.generate(prompts, SamplingParams(max_tokens=max_tokens))]
+    return toks, held, rc.swa_blocks, llm.blocks
+
+
+def test_bounded_sliding_window_pool_matches_full_context_cpu():
+    """Sliding-window layers keeping only their window in a pool of their own give the same
+    tokens as keeping the whole context, across chunked prefill and decode, while a request
+    never holds more than window / block_size + 2 + its chunk's blocks of that pool."""
+    want, _, nb0, _ = _mimo_generate("cpu", bounded=False)
+    got, held, nb, bm = _mimo_generate("cpu", bounded=True)
+    assert nb0 == 0 and nb > 0
+    assert got == want
+    assert max(held) <= 16 // 16 + 2 + 64 // 16
+    assert len(bm.swa_free) == nb           # everything returned at the end
+
+
+@pytest.mark.gpu
+def test_bounded_sliding_window_pool_matches_full_context_gpu():
+    want, _, _, _ = _mimo_generate("cuda", bounded=False, graphs=True, bs=64, window=32, max_tokens=10)
+    got, _, nb, _ = _mimo_generate("cuda", bounded=True, graphs=True, bs=64, window=32, max_tokens=10)
+    torch.cuda.synchronize()
+    N.check_status()
+    assert nb > 0 and got == want

@@ -70,7 +70,8 @@ class LLM:
         self.tiering = tiering
         rc = runner_config or RunnerConfig()
         self.runner = ModelRunner(self.model, rc)
-        self.blocks = BlockManager(rc.num_blocks, rc.block_size, rc.max_seqs)
+        self.blocks = BlockManager(rc.num_blocks, rc.block_size, rc.max_seqs, swa_blocks=rc.swa_blocks,
+                                   window=self.model.cfg.sliding_window)
         self.scheduler = Scheduler(self.blocks, rc.max_batched_tokens, rc.max_seqs, rc.num_spec)
         self.spec = None
         if rc.num_spec > 0 and self.model.mtp:

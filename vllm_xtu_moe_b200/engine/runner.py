@@ -24,6 +24,7 @@ from ..models.model import MoETransformer
 from ..ops import basic as B
 from ..ops import _native as N
 from ..ops.attention import AttnMetadata, choose_splits, decode_ctas_per_sm
+from .block_manager import swa_pool_blocks
 from .scheduler import StepPlan
 
 
@@ -38,6 +39,10 @@ class RunnerConfig:
     graph_batch_sizes: tuple = (1, 2, 4, 8, 16)
     kv_mem_fraction: float = 0.9   # of free memory after weights, for the KV cache
     num_spec: int = 0
+    # sliding-window layers keep only their window in a small pool of their own (models
+    # with "swa" layers, no speculative decoding); False: they share the full-context pool
+    swa_bounded: bool = True
+    swa_blocks: int = 0            # set by the runner: blocks of that pool (0 = no pool)
 
 
 class ModelRunner:
@@ -50,9 +55,17 @@ class ModelRunner:
         self.device = model.device
         self.cuda = self.device.type == "cuda"
         self.max_blocks_per_seq = (rc.max_model_len + rc.block_size - 1) // rc.block_size + 1
+        cfg = model.cfg
+        has_swa = cfg.sliding_window > 0 and cfg.layer_types is not None and "swa" in cfg.layer_types
+        rc.swa_blocks = (swa_pool_blocks(rc.max_seqs, cfg.sliding_window, rc.block_size, rc.max_batched_tokens)
+                         if has_swa and rc.swa_bounded and rc.num_spec == 0 else 0)
         if rc.num_blocks <= 0:
             rc.num_blocks = self._auto_blocks()
-        self.caches = model.allocate_caches(rc.num_blocks, rc.block_size, rc.max_seqs)
+        self.caches = model.allocate_caches(rc.num_blocks, rc.block_size, rc.max_seqs, swa_blocks=rc.swa_blocks)
+        if rc.swa_blocks:
+            for l in model.layers:
+                if getattr(l.attn, "window", 0) > 0:
+                    l.attn.bounded = True
         self.mtp_caches = model.allocate_mtp_caches(rc.num_blocks, rc.block_size, rc.max_seqs) if model.mtp else []
         max_rows = max(rc.max_batched_tokens, rc.max_seqs * (1 + rc.num_spec))
         model.prepare_workspaces(max_rows)
@@ -65,7 +78,7 @@ class ModelRunner:
 
     # ------------------------------------------------------------------
     def _auto_blocks(self) -> int:
-        per_tok = max(1, self.model.kv_bytes_per_token())
+        per_tok = max(1, self.model.kv_bytes_per_token(skip_swa=self.rc.swa_blocks > 0))
         if self.model.mtp:
             c = self.model.cfg
             last = c.num_layers - 1     # MTP layers: the last decoder layer's attention type
@@ -88,6 +101,8 @@ class ModelRunner:
         q_start = [0]
         kv_len, seq_slots, fresh = [], [], []
         tables = []
+        swa = self.rc.swa_blocks > 0
+        swa_slots, swa_tables = [], []
         for ch in plan.chunks:
             r = ch.req
             toks = r.all_tokens
@@ -102,6 +117,10 @@ class ModelRunner:
                 p = p0 + i
                 pos.append(p)
                 slots.append(r.blocks[p // bs] * bs + p % bs)
+                if swa:
+                    swa_slots.append(r.swa_blocks[p // bs] * bs + p % bs)
+            if swa:    # logical blocks below the window read a placeholder (block 0), always masked
+                swa_tables.append([r.swa_blocks.get(j, 0) for j in range(len(r.blocks))])
             q_start.append(q_start[-1] + n)
             kv_len.append(p0 + n)
             seq_slots.append(max(r.slot, 0))
@@ -131,6 +150,15 @@ class ModelRunner:
                             slot_mapping=T(slots), positions=T(pos), max_q_len=max(q_start[i + 1] - q_start[i] for i in range(Bn)),
                             max_kv_len=max(kv_len), is_decode=plan.is_decode, q_start_host=q_start, kv_len_host=kv_len,
                             seq_slots=T(seq_slots), seq_fresh=T(fresh))
+        if swa:
+            sbt = torch.zeros_like(bt)
+            for i, t in enumerate(swa_tables):
+                if t:
+                    sbt[i, :len(t)] = torch.tensor(t, dtype=torch.int32)
+            if nb:
+                self.h2d_bytes += sbt.numel() * sbt.element_size()
+            meta.swa_block_table = sbt.pin_memory().to(d, non_blocking=True) if nb else sbt
+            meta.swa_slot_mapping = T(swa_slots)
         if plan.is_decode and self.cuda:
             meta.num_splits = choose_splits(Bn, max(1, self.model.cfg.num_kv_heads), meta.max_kv_len,
                                             ctas_per_sm=decode_ctas_per_sm(self.model.cfg))
@@ -184,6 +212,8 @@ class ModelRunner:
             ids=torch.zeros(ms, dtype=torch.int32, device=d),
             pos=torch.zeros(ms, dtype=torch.int32, device=d),
             slots=torch.full((ms,), -1, dtype=torch.int32, device=d),
+            swa_slots=torch.full((ms,), -1, dtype=torch.int32, device=d),
+            swa_bt=torch.zeros(ms, self.max_blocks_per_seq, dtype=torch.int32, device=d),
             q_start=torch.arange(ms + 1, dtype=torch.int32, device=d),
             kv_len=torch.ones(ms, dtype=torch.int32, device=d),
             bt=torch.zeros(ms, self.max_blocks_per_seq, dtype=torch.int32, device=d),
@@ -200,7 +230,9 @@ class ModelRunner:
         return AttnMetadata(num_seqs=b, q_start=s["q_start"][:b + 1], kv_len=s["kv_len"][:b],
                             block_table=s["bt"][:b], slot_mapping=s["slots"][:b], positions=s["pos"][:b],
                             max_q_len=1, max_kv_len=self.rc.max_model_len, is_decode=True,
-                            seq_slots=s["seq_slots"][:b], seq_fresh=s["fresh"][:b], num_splits=splits)
+                            seq_slots=s["seq_slots"][:b], seq_fresh=s["fresh"][:b], num_splits=splits,
+                            swa_block_table=s["swa_bt"][:b] if self.rc.swa_blocks else None,
+                            swa_slot_mapping=s["swa_slots"][:b] if self.rc.swa_blocks else None)
 
     def _capture(self, b: int):
         if self._static is None:
@@ -244,6 +276,10 @@ class ModelRunner:
         s["bt"][:n, :w].copy_(meta.block_table)
         s["seq_slots"][:b].fill_(-1)
         s["seq_slots"][:n].copy_(meta.seq_slots)
+        if self.rc.swa_blocks:
+            s["swa_slots"][:b].fill_(-1)
+            s["swa_slots"][:n].copy_(meta.swa_slot_mapping)
+            s["swa_bt"][:n, :w].copy_(meta.swa_block_table)
         s["fresh"][:b].zero_()
         if b not in self.graphs:
             self._capture(b)

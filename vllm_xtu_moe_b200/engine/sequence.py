@@ -35,6 +35,7 @@ class Request:
     status: Status = Status.WAITING
     num_computed: int = 0          # tokens whose KV is in the cache
     blocks: list[int] = field(default_factory=list)
+    swa_blocks: dict = field(default_factory=dict)   # logical block -> block of the sliding-window pool
     slot: int = -1                 # recurrent-state slot
     # timing (seconds, host clock) for TTFT / TPOT accounting
     t_submit: float = 0.0

@@ -6,6 +6,8 @@ dispatch to the sm_100a kernels on a GPU and to PyTorch restatements on a CPU.
 """
 from __future__ import annotations
 
+import dataclasses
+
 import math
 
 import torch
@@ -76,6 +78,7 @@ class GQAAttention:
         self.nh, self.hd, self.vd = cfg.num_heads, cfg.head_dim, cfg.gqa_v_dim
         self.nkv = num_kv_heads if num_kv_heads is not None else cfg.num_kv_heads
         self.window = window
+        self.bounded = False        # set by the runner when this window layer has its own bounded pool
         self.sinks = sinks.float().contiguous() if sinks is not None else None
         self.scale = 1.0 / math.sqrt(self.hd)
 
@@ -96,6 +99,10 @@ class GQAAttention:
             k = y[:, nh * hd: (nh + nkv) * hd].view(T, nkv, hd)
             v = y[:, (nh + nkv) * hd:].view(T, nkv, vd)
         k_cache, v_cache = kv
+        if self.bounded:            # the sliding-window pool: its own block table and write slots
+            if meta.swa_block_table is None:
+                raise RuntimeError("a bounded sliding-window cache needs the step's window block table")
+            meta = dataclasses.replace(meta, block_table=meta.swa_block_table, slot_mapping=meta.swa_slot_mapping)
         B.rope_and_cache(q, k, v, meta.positions, rope, self.cfg.rot_dim, self.cfg.rope_neox,
                          slot_mapping=meta.slot_mapping, k_cache=k_cache, v_cache=v_cache, q_norm_w=self.q_norm,
                          k_norm_w=self.k_norm, norm_eps=self.cfg.norm_eps, norm_add_one=self.cfg.norm_add_one)

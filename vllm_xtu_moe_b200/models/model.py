@@ -201,11 +201,13 @@ class MoETransformer:
         return sum(t.numel() * t.element_size() for t in self.tensors() if (t.is_cuda or not device_only))
 
     # KV cache / state allocation ---------------------------------------
-    def kv_bytes_per_token(self, layers: range | None = None) -> int:
+    def kv_bytes_per_token(self, layers: range | None = None, skip_swa: bool = False) -> int:
+        """KV bytes per token of context (skip_swa: leave out sliding-window layers, whose
+        bounded pool does not grow with the context)."""
         c = self.cfg
         n = 0
         for i in layers if layers is not None else range(c.num_layers):
-            if c.layer_type(i) == "linear":
+            if c.layer_type(i) == "linear" or (skip_swa and c.layer_type(i) == "swa"):
                 continue
             if c.is_mla:
                 n += (c.kv_lora_rank + c.qk_rope_head_dim) * 2
@@ -224,7 +226,9 @@ class MoETransformer:
                 torch.zeros(num_blocks, nkv, block_size, c.gqa_v_dim, dtype=dtype, device=device))
 
     def allocate_caches(self, num_blocks: int, block_size: int, max_seqs: int, device=None,
-                        layers: range | None = None) -> list:
+                        layers: range | None = None, swa_blocks: int = 0) -> list:
+        """Per layer: recurrent state, or a paged KV cache of num_blocks blocks
+        (sliding-window layers: swa_blocks blocks when a bounded pool is used)."""
         c = self.cfg
         device = device or self.device
         caches = []
@@ -232,7 +236,8 @@ class MoETransformer:
             if c.layer_type(i) == "linear":
                 caches.append(DeltaNetState(c, max_seqs, device))
             else:
-                caches.append(self._attn_cache(i, num_blocks, block_size, self.act_dtype, device))
+                nb = swa_blocks if (swa_blocks > 0 and c.layer_type(i) == "swa") else num_blocks
+                caches.append(self._attn_cache(i, nb, block_size, self.act_dtype, device))
         return caches
 
     def allocate_mtp_caches(self, num_blocks: int, block_size: int, max_seqs: int, device=None) -> list:

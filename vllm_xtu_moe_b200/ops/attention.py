@@ -41,6 +41,9 @@ class AttnMetadata:
     seq_slots: torch.Tensor | None = None   # int32 [B] request slot (recurrent-state index)
     seq_fresh: torch.Tensor | None = None   # int32 [B] 1 if the sequence starts at position 0 this step
     num_splits: int = 1
+    # sliding-window layers with a bounded pool: their own block table and KV-write slots
+    swa_block_table: torch.Tensor | None = None
+    swa_slot_mapping: torch.Tensor | None = None
 
     @property
     def num_tokens(self) -> int:

@@ -66,13 +66,13 @@ class PipelineStage(MoETransformer):
         return torch.stack([x, residual]).contiguous()
 
     # ------------------------------------------------------------------ engine contract
-    def kv_bytes_per_token(self, layers: range | None = None) -> int:
-        return super().kv_bytes_per_token(range(self.lo, self.hi) if layers is None else layers)
+    def kv_bytes_per_token(self, layers: range | None = None, skip_swa: bool = False) -> int:
+        return super().kv_bytes_per_token(range(self.lo, self.hi) if layers is None else layers, skip_swa)
 
     def allocate_caches(self, num_blocks: int, block_size: int, max_seqs: int, device=None,
-                        layers: range | None = None) -> list:
+                        layers: range | None = None, swa_blocks: int = 0) -> list:
         return super().allocate_caches(num_blocks, block_size, max_seqs, device,
-                                       range(self.lo, self.hi) if layers is None else layers)
+                                       range(self.lo, self.hi) if layers is None else layers, swa_blocks)
 
     def _run_layers(self, x, residual, meta, caches):
         for layer, kv in zip(self.layers, caches):
