@@ -580,3 +580,16 @@ def test_failing_host_copy_raises(monkeypatch):
         hx.copy_expert(1, dst13, dst2, None, None, _Stream())
     assert len(calls) == 1
     eng.close()
+
+
+def test_planner_counts_window_layers_once_per_sequence():
+    """MiMo-V2's sliding-window layers hold one window per sequence, so the planned KV grows
+    with the context only through its 9 global layers."""
+    cfg = get_preset("mimo-v2-flash")
+    a = PL.kv_bytes(cfg, 16384, 4)
+    b = PL.kv_bytes(cfg, 32768, 4)
+    per_tok_full = PL.kv_bytes_per_token(cfg)
+    assert per_tok_full == 9 * 4 * (192 + 128) * 2
+    assert b - a == per_tok_full * 16384 * 4
+    p = PL.plan(cfg, max_model_len=131072, max_seqs=1)
+    assert p.kv < 20 * (1 << 30)

@@ -43,13 +43,25 @@ def expert_bytes(cfg: ModelConfig, fmt: str | None = None) -> int:
     raise ValueError(fmt)
 
 
-def kv_bytes_per_token(cfg: ModelConfig, kv_dtype_bytes: int = 2) -> int:
-    """Paged-KV bytes per token over the attention layers (sliding-window layers keep the
-    whole context in the paged cache too)."""
-    attn = [i for i in range(cfg.num_layers) if cfg.layer_type(i) in ("full", "swa")]
+def kv_bytes_per_token(cfg: ModelConfig, kv_dtype_bytes: int = 2, layer_type: str = "full") -> int:
+    """Paged-KV bytes per token over the layers of one attention type ("full": they grow
+    with the context; "swa": they hold one window per sequence)."""
+    attn = [i for i in range(cfg.num_layers) if cfg.layer_type(i) == layer_type]
     if cfg.is_mla:
         return len(attn) * (cfg.kv_lora_rank + cfg.qk_rope_head_dim) * kv_dtype_bytes
     return sum(cfg.kv_heads(i) * (cfg.head_dim + cfg.gqa_v_dim) for i in attn) * kv_dtype_bytes
+
+
+def kv_bytes(cfg: ModelConfig, max_model_len: int, max_seqs: int, max_batched_tokens: int = 16384,
+             block_size: int = 64) -> int:
+    """KV-cache bytes the runner allocates: the full-context layers for every sequence at
+    max_model_len, plus the sliding-window layers' bounded pool."""
+    from ..engine.block_manager import swa_pool_blocks
+    n = kv_bytes_per_token(cfg) * max_model_len * max_seqs
+    if cfg.sliding_window > 0:
+        blocks = swa_pool_blocks(max_seqs, cfg.sliding_window, block_size, max_batched_tokens)
+        n += kv_bytes_per_token(cfg, layer_type="swa") * blocks * block_size
+    return n
 
 
 def non_expert_bytes(cfg: ModelConfig) -> int:
@@ -114,7 +126,7 @@ def plan(cfg: ModelConfig, gpu_gib: float = 178.0, *, max_model_len: int = 16384
          reserve_gib: float = 4.0, pin_max_per_layer: int = 0, order: list[int] | None = None) -> Placement:
     gpu = int(gpu_gib * GiB)
     ne = non_expert_bytes(cfg)
-    kv = kv_bytes_per_token(cfg) * max_model_len * max_seqs + int(graph_pool_gib * GiB)
+    kv = kv_bytes(cfg, max_model_len, max_seqs) + int(graph_pool_gib * GiB)
     eb = expert_bytes(cfg)
     layer_b = eb * cfg.num_experts
     gfmt = cfg.expert_fmt in ("bf16", "fp8", "mxfp4", "nvfp4")
