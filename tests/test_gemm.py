@@ -245,3 +245,42 @@ def test_fused_moe_fp4_matches_reference(fmt, T, E, H, I, K):
     torch.cuda.synchronize()
     err = (out - ref).abs().max().item()
     assert err <= 2e-2 * ref.abs().max().item() + 1e-3, err
+
+
+def _all_codes_weight(N=256, K=128):
+    """e4m3 weight [N, K] holding every finite code: W[n, k] = code (n + k) mod 256, the two
+    NaN codes (0x7f, 0xff) replaced by 0."""
+    n = torch.arange(N)[:, None]
+    k = torch.arange(K)[None, :]
+    codes = ((n + k) % 256).to(torch.uint8)
+    codes[(codes == 0x7F) | (codes == 0xFF)] = 0
+    return codes.view(torch.float8_e4m3fn)
+
+
+@pytest.mark.gpu
+def test_fp8_decode_gemv_widens_every_code_exactly():
+    """The decode GEMV's e4m3 widening against torch.float8_e4m3fn for all finite codes:
+    one-hot activations pick single weight columns, so every output is one weight value
+    (exactly representable on the way: f16 x 2^-8 products, fp32 sums, bf16 output)."""
+    w = _all_codes_weight().cuda()
+    s = torch.ones(2, 1, device="cuda")
+    for k0 in (0, 16, 112):
+        x = torch.zeros(16, 128, device="cuda", dtype=torch.bfloat16)
+        x[torch.arange(16), k0 + torch.arange(16)] = 1.0
+        y = G.gemv(x, w, s)
+        torch.cuda.synchronize()
+        ref = w.float()[:, k0:k0 + 16].t()
+        assert torch.equal(y.float().cpu(), ref.cpu()), k0
+
+
+@pytest.mark.gpu
+def test_fp8_grouped_gemm_widens_every_code_exactly():
+    """The same for the prefill grouped GEMM's on-chip e4m3 -> bf16 widening (128 one-hot
+    rows cover every column of the 128-column block)."""
+    w = _all_codes_weight().cuda()[None]                    # [1, 256, 128]
+    s = torch.ones(1, 2, 1, device="cuda")
+    a = torch.eye(128, device="cuda", dtype=torch.bfloat16)
+    seg = torch.tensor([0, 128], dtype=torch.int32, device="cuda")
+    y = G.grouped_gemm(a, w, seg, w_scale=s)
+    torch.cuda.synchronize()
+    assert torch.equal(y.float().cpu(), w[0].float().t().cpu())
