@@ -29,6 +29,48 @@ def test_completions_endpoint_cpu():
         eng.stop()
 
 
+def test_chat_sampling_and_streaming_cpu():
+    import json
+    from fastapi.testclient import TestClient
+    from vllm_xtu_moe_b200.serve import EngineThread, build_app
+    llm = LLM(get_preset("tiny-mixtral"), device="cpu",
+              runner_config=RunnerConfig(block_size=16, max_seqs=4, max_model_len=512, max_batched_tokens=64,
+                                         use_cuda_graph=False))
+    eng = EngineThread(llm)
+    try:
+        c = TestClient(build_app(eng, "tiny-mixtral"))
+        msgs = [{"role": "user", "content": "hi"}]
+        r = c.post("/v1/chat/completions", json={"messages": msgs, "max_tokens": 5}).json()
+        ch = r["choices"][0]
+        assert ch["message"]["role"] == "assistant" and len(ch["token_ids"]) == 5
+        assert r["usage"]["completion_tokens"] == 5
+        # seeded sampling reproduces; a different seed differs
+        body = {"prompt": list(range(1, 20)), "max_tokens": 8, "temperature": 1.5}
+        s1 = c.post("/v1/completions", json={**body, "seed": 11}).json()["choices"][0]["token_ids"]
+        s2 = c.post("/v1/completions", json={**body, "seed": 11}).json()["choices"][0]["token_ids"]
+        s3 = c.post("/v1/completions", json={**body, "seed": 12}).json()["choices"][0]["token_ids"]
+        assert s1 == s2 and s1 != s3
+        assert c.post("/v1/completions", json={**body, "top_p": 0.0}).status_code == 400
+        # streaming: the events carry the same tokens as the blocking call
+        want = c.post("/v1/completions", json={"prompt": list(range(5, 25)), "max_tokens": 7}).json()
+        got, done = [], False
+        with c.stream("POST", "/v1/completions",
+                      json={"prompt": list(range(5, 25)), "max_tokens": 7, "stream": True}) as resp:
+            for line in resp.iter_lines():
+                if not line.startswith("data: "):
+                    continue
+                if line == "data: [DONE]":
+                    done = True
+                    break
+                got += json.loads(line[6:])["choices"][0]["token_ids"]
+        assert done and got == want["choices"][0]["token_ids"]
+        with c.stream("POST", "/v1/chat/completions", json={"messages": msgs, "max_tokens": 4, "stream": True}) as resp:
+            events = [l for l in resp.iter_lines() if l.startswith("data: ")]
+        assert events[-1] == "data: [DONE]" and "delta" in json.loads(events[0][6:])["choices"][0]
+    finally:
+        eng.stop()
+
+
 def test_plugin_registers_custom_ops():
     import vllm_xtu_moe_b200 as pkg
     cfg = pkg.register()

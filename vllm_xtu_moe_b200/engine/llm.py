@@ -87,6 +87,8 @@ class LLM:
 
     # ------------------------------------------------------------------
     def add_request(self, prompt: list[int], params: SamplingParams) -> Request:
+        if params.temperature > 0.0 and self.spec is not None:
+            raise ValueError("speculative decoding verifies greedy drafts; sampled requests need num_spec=0")
         r = Request(list(prompt), params)
         r.t_submit = time.perf_counter()
         self.scheduler.add(r)

@@ -24,6 +24,7 @@ from ..models.model import MoETransformer
 from ..ops import basic as B
 from ..ops import _native as N
 from ..ops.attention import AttnMetadata, choose_splits, decode_ctas_per_sm
+from . import sampling as S
 from .block_manager import swa_pool_blocks
 from .scheduler import StepPlan
 
@@ -182,18 +183,26 @@ class ModelRunner:
         ids, meta = self.build_meta(plan)
         if plan.is_decode:
             rows = None  # every row produces logits
+            reqs = [ch.req for ch in plan.chunks]
             if self.cuda and self.rc.use_cuda_graph and self.rc.num_spec == 0 and not self.pipeline:
-                tok = self._decode_graph(ids, meta)
+                tok, logits = self._decode_graph(ids, meta)
+                if logits is not None and S.needs_sampling(reqs):
+                    tok = S.sample_rows(logits, reqs, tok)
                 return tok, None
-            tok, h, pre, _ = self.forward(ids, meta, torch.arange(ids.shape[0], device=self.device))
+            tok, h, pre, logits = self.forward(ids, meta, torch.arange(ids.shape[0], device=self.device))
+            if logits is not None and S.needs_sampling(reqs):
+                tok = S.sample_rows(logits, reqs, tok)
             return tok, (h, pre, meta)
         # prefill: logits only for chunks that finish their prompt
-        rows = []
+        rows, reqs = [], []
         for i, ch in enumerate(plan.chunks):
             if ch.start + ch.length == len(ch.req.prompt):
                 rows.append(meta.q_start_host[i + 1] - 1)
+                reqs.append(ch.req)
         rt = torch.tensor(rows, dtype=torch.long, device=self.device) if rows else None
-        tok, h, pre, _ = self.forward(ids, meta, rt)
+        tok, h, pre, logits = self.forward(ids, meta, rt)
+        if logits is not None and S.needs_sampling(reqs):
+            tok = S.sample_rows(logits, reqs, tok)
         return tok, (h, pre, meta, rows)
 
     # ------------------------------------------------------------------
@@ -251,18 +260,19 @@ class ModelRunner:
         g = torch.cuda.CUDAGraph()
         n0 = N.launches()
         with torch.cuda.graph(g):
-            tok, *_ = self.forward(s["ids"][:b], meta, rows)
+            tok, _, _, logits = self.forward(s["ids"][:b], meta, rows)
             s["out"][:b].copy_(tok)
         kernels = N.launches() - n0
         N.add_launches(-kernels)      # capture enqueues nothing; replays are counted below
-        self.graphs[b] = (g, meta, kernels)
+        # `logits` is a graph output: after each replay it holds that step's logits rows
+        self.graphs[b] = (g, meta, kernels, logits)
 
     def _decode_graph(self, ids, meta):
         n = meta.num_seqs
         b = self._graph_bs(n)
         if b is None:
-            tok, *_ = self.forward(ids, meta, torch.arange(ids.shape[0], device=self.device))
-            return tok
+            tok, _, _, logits = self.forward(ids, meta, torch.arange(ids.shape[0], device=self.device))
+            return tok, logits
         if self._static is None:
             self._alloc_static()
         s = self._static
@@ -283,10 +293,10 @@ class ModelRunner:
         s["fresh"][:b].zero_()
         if b not in self.graphs:
             self._capture(b)
-        g, _, kernels = self.graphs[b]
+        g, _, kernels, logits = self.graphs[b]
         g.replay()
         N.add_launches(kernels)
-        return s["out"][:n]
+        return s["out"][:n], (logits[:n] if logits is not None else None)
 
     def release_graphs(self):
         self.graphs.clear()

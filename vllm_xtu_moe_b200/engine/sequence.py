@@ -11,6 +11,7 @@ class SamplingParams:
     max_tokens: int = 16
     temperature: float = 0.0      # 0 = greedy
     top_p: float = 1.0
+    top_k: int = 0                # 0 = no top-k filter
     ignore_eos: bool = True
     eos_token_id: int | None = None
     seed: int | None = None

@@ -2,16 +2,22 @@
 ``vllm.entrypoints.openai.api_server`` launch, scripts/serve_v41.sh:637-664).
 
     python -m vllm_xtu_moe_b200.serve --model glm-4.5-air --port 8000 [--num-spec 4]
+        [--tokenizer /path/to/hf/tokenizer]
 
-Endpoints: ``POST /v1/completions`` (prompt = token ids, or text encoded as UTF-8
-bytes when no tokenizer is configured), ``GET /v1/models``, ``GET /health`` and
-``GET /metrics`` (Prometheus: requests, generated tokens, time to first token, step
-latency).  One engine thread owns the GPU: HTTP handlers enqueue requests and wait
-on a future; the thread admits new requests between steps (continuous batching).
+Endpoints: ``POST /v1/completions`` (prompt = token ids or text) and
+``POST /v1/chat/completions`` (messages), both with greedy or sampled decoding
+(temperature, top_p, top_k, seed) and ``"stream": true`` (server-sent events, one event
+per engine step that produced tokens, then ``data: [DONE]``); ``GET /v1/models``,
+``GET /health`` and ``GET /metrics`` (Prometheus text).  Text goes through a HF tokenizer
+from a local directory when one is given, else through UTF-8 bytes (token id = byte).
+One engine thread owns the GPU: HTTP handlers enqueue requests and wait on a future (or
+a per-request queue when streaming); the thread admits new requests between steps
+(continuous batching).
 """
 
 import argparse
 import asyncio
+import json
 import queue
 import threading
 import time
@@ -22,22 +28,37 @@ from .engine.runner import RunnerConfig
 
 
 class EngineThread:
-    """Runs ``LLM.step`` in a loop on one thread; ``submit`` is thread-safe."""
+    """Runs ``LLM.step`` in a loop on one thread; ``submit`` is thread-safe.  ``on_tokens``
+    (optional) is called on the engine thread after every step that gave the request new
+    tokens, with (new token ids, finished)."""
 
     def __init__(self, llm: LLM):
         self.llm = llm
         self.inbox: queue.Queue = queue.Queue()
         self.pending: dict[int, tuple[Future, float]] = {}
+        self.streams: dict[int, list] = {}          # rid -> [callback, tokens already sent, request]
         self.metrics = {"requests": 0, "tokens": 0, "steps": 0}
         self._stop = threading.Event()
         self.error: BaseException | None = None
         self.thread = threading.Thread(target=self._loop, name="xtu-engine", daemon=True)
         self.thread.start()
 
-    def submit(self, prompt: list[int], params: SamplingParams) -> Future:
+    def submit(self, prompt: list[int], params: SamplingParams, on_tokens=None) -> Future:
         f: Future = Future()
-        self.inbox.put((prompt, params, f))
+        self.inbox.put((prompt, params, f, on_tokens))
         return f
+
+    def _push(self, r, done: bool) -> None:
+        st = self.streams.get(r.rid)
+        if st is None:
+            return
+        cb, sent, _ = st
+        new = list(r.output[sent:])
+        if new or done:
+            st[1] = len(r.output)
+            cb(new, done)
+        if done:
+            del self.streams[r.rid]
 
     def _loop(self):
         try:
@@ -45,11 +66,17 @@ class EngineThread:
                 admitted = False
                 while True:
                     try:
-                        prompt, params, f = self.inbox.get_nowait()
+                        prompt, params, f, cb = self.inbox.get_nowait()
                     except queue.Empty:
                         break
-                    r = self.llm.add_request(prompt, params)
+                    try:
+                        r = self.llm.add_request(prompt, params)
+                    except ValueError as e:       # a request this engine cannot serve
+                        f.set_exception(e)
+                        continue
                     self.pending[r.rid] = (f, time.perf_counter())
+                    if cb is not None:
+                        self.streams[r.rid] = [cb, 0, r]
                     admitted = True
                 if not self.llm.scheduler.has_work():
                     if not admitted:
@@ -57,7 +84,12 @@ class EngineThread:
                     continue
                 done = self.llm.step()
                 self.metrics["steps"] += 1
+                done_ids = {r.rid for r in done}
+                for st in list(self.streams.values()):
+                    if st[2].rid not in done_ids:
+                        self._push(st[2], False)
                 for r in done:
+                    self._push(r, True)
                     f, _ = self.pending.pop(r.rid)
                     self.metrics["requests"] += 1
                     self.metrics["tokens"] += len(r.output)
@@ -65,30 +97,74 @@ class EngineThread:
         except BaseException as e:      # surface engine failures to every waiter
             self.error = e
             for f, _ in self.pending.values():
-                f.set_exception(e)
+                if not f.done():
+                    f.set_exception(e)
+            for cb, _, _ in self.streams.values():
+                cb([], True)
 
     def stop(self):
         self._stop.set()
         self.thread.join(timeout=10)
 
 
+class TextCodec:
+    """Text <-> token ids: a HF tokenizer loaded from a local directory, or UTF-8 bytes."""
+
+    def __init__(self, tokenizer_path: str | None = None):
+        self.tok = None
+        if tokenizer_path:
+            from transformers import AutoTokenizer
+            self.tok = AutoTokenizer.from_pretrained(tokenizer_path, local_files_only=True)
+
+    def encode(self, prompt) -> list[int]:
+        if isinstance(prompt, list):
+            return [int(t) for t in prompt]
+        if self.tok is not None:
+            return list(self.tok.encode(str(prompt)))
+        return list(str(prompt).encode("utf-8"))
+
+    def decode(self, ids: list[int]) -> str:
+        if self.tok is not None:
+            return self.tok.decode(ids)
+        return bytes(i for i in ids if 0 <= i < 256).decode("utf-8", errors="replace")
+
+    def chat(self, messages: list[dict]) -> list[int]:
+        if self.tok is not None and getattr(self.tok, "chat_template", None):
+            return list(self.tok.apply_chat_template(messages, add_generation_prompt=True))
+        text = "".join(f"{m.get('role', 'user')}: {m.get('content', '')}\n" for m in messages) + "assistant: "
+        return self.encode(text)
+
+    @property
+    def eos(self) -> int | None:
+        return getattr(self.tok, "eos_token_id", None) if self.tok is not None else None
+
+
 def _encode(prompt) -> list[int]:
-    if isinstance(prompt, list):
-        return [int(t) for t in prompt]
-    return list(str(prompt).encode("utf-8"))
+    return TextCodec().encode(prompt)
 
 
-def build_app(engine: EngineThread, model_name: str):
+def build_app(engine: EngineThread, model_name: str, codec: TextCodec | None = None):
     from fastapi import FastAPI, HTTPException
-    from fastapi.responses import PlainTextResponse
+    from fastapi.responses import PlainTextResponse, StreamingResponse
     from pydantic import BaseModel
 
-    class CompletionRequest(BaseModel):
+    codec = codec or TextCodec()
+
+    class Sampling(BaseModel):
         model: str | None = None
-        prompt: list[int] | str
         max_tokens: int = 16
         temperature: float = 0.0
+        top_p: float = 1.0
+        top_k: int = 0
+        seed: int | None = None
         ignore_eos: bool = True
+        stream: bool = False
+
+    class CompletionRequest(Sampling):
+        prompt: list[int] | str
+
+    class ChatRequest(Sampling):
+        messages: list[dict]
 
     app = FastAPI(title="vllm_xtu_moe_b200")
 
@@ -113,18 +189,63 @@ def build_app(engine: EngineThread, model_name: str):
                  f"xtu_decode_seconds_total {st['decode_time']:.6f}"]
         return "\n".join(lines) + "\n"
 
+    def params_of(req: Sampling) -> SamplingParams:
+        if req.temperature < 0 or not (0 < req.top_p <= 1) or req.top_k < 0 or req.max_tokens < 1:
+            raise HTTPException(400, "invalid sampling parameters")
+        return SamplingParams(max_tokens=req.max_tokens, temperature=req.temperature, top_p=req.top_p,
+                              top_k=req.top_k, seed=req.seed, ignore_eos=req.ignore_eos, eos_token_id=codec.eos)
+
+    async def run(ids: list[int], sp: SamplingParams):
+        try:
+            return await asyncio.wrap_future(engine.submit(ids, sp))
+        except ValueError as e:
+            raise HTTPException(400, str(e))
+
+    def stream(ids: list[int], sp: SamplingParams, make_chunk):
+        loop = asyncio.get_running_loop()
+        q: asyncio.Queue = asyncio.Queue()
+        engine.submit(ids, sp, on_tokens=lambda new, done: loop.call_soon_threadsafe(q.put_nowait, (new, done)))
+
+        async def events():
+            while True:
+                new, done = await q.get()
+                if new:
+                    yield "data: " + json.dumps(make_chunk(new)) + "\n\n"
+                if done:
+                    yield "data: [DONE]\n\n"
+                    return
+        return StreamingResponse(events(), media_type="text/event-stream")
+
+    def usage(ids, out):
+        return {"prompt_tokens": len(ids), "completion_tokens": len(out), "total_tokens": len(ids) + len(out)}
+
     @app.post("/v1/completions")
     async def completions(req: CompletionRequest):
-        if req.temperature != 0.0:
-            raise HTTPException(400, "only greedy decoding (temperature 0) is served")
-        ids = _encode(req.prompt)
-        fut = engine.submit(ids, SamplingParams(max_tokens=req.max_tokens, ignore_eos=req.ignore_eos))
-        r = await asyncio.wrap_future(fut)
+        ids = codec.encode(req.prompt)
+        sp = params_of(req)
+        if req.stream:
+            return stream(ids, sp, lambda new: {"object": "text_completion", "model": model_name, "choices": [
+                {"index": 0, "token_ids": new, "text": codec.decode(new), "finish_reason": None}]})
+        r = await run(ids, sp)
         return {"id": f"cmpl-{r.rid}", "object": "text_completion", "model": model_name,
-                "choices": [{"index": 0, "token_ids": list(r.output), "finish_reason": "length"}],
-                "usage": {"prompt_tokens": len(ids), "completion_tokens": len(r.output),
-                          "total_tokens": len(ids) + len(r.output)},
+                "choices": [{"index": 0, "token_ids": list(r.output), "text": codec.decode(list(r.output)),
+                             "finish_reason": "length" if len(r.output) >= sp.max_tokens else "stop"}],
+                "usage": usage(ids, r.output),
                 "timing": {"ttft_s": r.t_first - r.t_submit, "e2e_s": r.t_done - r.t_submit}}
+
+    @app.post("/v1/chat/completions")
+    async def chat(req: ChatRequest):
+        ids = codec.chat(req.messages)
+        sp = params_of(req)
+        if req.stream:
+            return stream(ids, sp, lambda new: {"object": "chat.completion.chunk", "model": model_name, "choices": [
+                {"index": 0, "delta": {"content": codec.decode(new)}, "token_ids": new, "finish_reason": None}]})
+        r = await run(ids, sp)
+        out = list(r.output)
+        return {"id": f"chatcmpl-{r.rid}", "object": "chat.completion", "model": model_name,
+                "choices": [{"index": 0, "message": {"role": "assistant", "content": codec.decode(out)},
+                             "token_ids": out, "finish_reason": "length" if len(out) >= sp.max_tokens else "stop"}],
+                "usage": usage(ids, out)}
 
     return app
 
@@ -140,13 +261,14 @@ def main(argv=None):
     ap.add_argument("--max-batched-tokens", type=int, default=16384)
     ap.add_argument("--num-spec", type=int, default=0)
     ap.add_argument("--layers", type=int, default=None)
+    ap.add_argument("--tokenizer", default=None, help="local HF tokenizer directory (default: UTF-8 bytes)")
     a = ap.parse_args(argv)
     import uvicorn
     rc = RunnerConfig(max_seqs=a.max_seqs, max_model_len=a.max_model_len, max_batched_tokens=a.max_batched_tokens,
                       num_spec=a.num_spec)
     llm = LLM(a.model, device=a.device, runner_config=rc, num_layers=a.layers)
     eng = EngineThread(llm)
-    uvicorn.run(build_app(eng, a.model), host=a.host, port=a.port, log_level="warning")
+    uvicorn.run(build_app(eng, a.model, TextCodec(a.tokenizer)), host=a.host, port=a.port, log_level="warning")
     eng.stop()
     llm.shutdown()
 
