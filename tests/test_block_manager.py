@@ -1,0 +1,56 @@
+"""Paged KV block accounting, including the sliding-window pool's release of blocks no
+future query can see."""
+from vllm_xtu_moe_b200.engine.block_manager import BlockManager, swa_pool_blocks
+from vllm_xtu_moe_b200.engine.sequence import Request, SamplingParams
+
+
+def _req(n_prompt):
+    return Request(list(range(n_prompt)), SamplingParams(max_tokens=1000))
+
+
+def test_full_pool_allocates_and_releases():
+    bm = BlockManager(10, 16, 2)
+    r = _req(40)
+    assert bm.ensure(r, 40) and len(r.blocks) == 3 and bm.num_free == 7
+    assert not bm.can_allocate(r, 16 * 11) and bm.can_allocate(r, 16 * 10)
+    bm.release(r)
+    assert bm.num_free == 10 and r.blocks == []
+
+
+def test_window_pool_stays_bounded_over_a_long_sequence():
+    W, bs = 40, 16
+    nb = swa_pool_blocks(1, W, bs, 64)
+    bm = BlockManager(200, bs, 1, swa_blocks=nb, window=W)
+    r = _req(100)
+    # chunked prefill of 100 tokens in chunks of 64, then 300 decode steps
+    assert bm.ensure(r, 64)
+    r.num_computed = 64
+    assert bm.ensure(r, 100)
+    r.num_computed = 100
+    r.output.append(1)
+    most = 0
+    for _ in range(300):
+        assert bm.ensure(r, r.total_len + 1)
+        first_query = r.num_computed
+        lo = max(0, first_query - W + 1) // bs
+        # every block a query of this step can see is held, nothing older
+        need = set(range(lo, (r.total_len + 1 + bs - 1) // bs))
+        assert need <= set(r.swa_blocks) and min(r.swa_blocks) >= lo
+        most = max(most, len(r.swa_blocks))
+        r.num_computed = r.total_len
+        r.output.append(1)
+    assert most <= (W + bs - 1) // bs + 2
+    held = len(r.swa_blocks)
+    assert len(bm.swa_free) == nb - held
+    bm.release(r)
+    assert len(bm.swa_free) == nb and bm.num_free == 200
+
+
+def test_window_pool_refuses_without_partial_allocation():
+    bm = BlockManager(100, 16, 2, swa_blocks=3, window=16)
+    a, b = _req(40), _req(40)
+    assert bm.ensure(a, 40) and len(a.swa_blocks) == 3
+    free_before = bm.num_free
+    assert not bm.can_allocate(b, 40)
+    assert not bm.ensure(b, 40)
+    assert b.swa_blocks == {} and b.blocks == [] and bm.num_free == free_before

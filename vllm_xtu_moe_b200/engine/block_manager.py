@@ -39,11 +39,14 @@ class BlockManager:
         return sum(1 for j in range(lo, hi) if j not in req.swa_blocks)
 
     def can_allocate(self, req, upto_tokens: int) -> bool:
-        need = self.blocks_needed(upto_tokens) - len(req.blocks)
-        if self.window and self._swa_need(req, upto_tokens) > len(self.swa_free) + len(
-                [j for j in req.swa_blocks if j < self._swa_keep_from(req)]):
+        """Would ``ensure(req, upto_tokens)`` succeed?  (Changes nothing.)"""
+        if self.blocks_needed(upto_tokens) - len(req.blocks) > len(self.free):
             return False
-        return need <= len(self.free)
+        if self.window:
+            keep = self._swa_keep_from(req)
+            releasable = sum(1 for j in req.swa_blocks if j < keep)
+            return self._swa_need(req, upto_tokens) <= len(self.swa_free) + releasable
+        return True
 
     def ensure(self, req, upto_tokens: int) -> bool:
         need = self.blocks_needed(upto_tokens) - len(req.blocks)
