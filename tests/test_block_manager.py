@@ -54,3 +54,31 @@ def test_window_pool_refuses_without_partial_allocation():
     assert not bm.can_allocate(b, 40)
     assert not bm.ensure(b, 40)
     assert b.swa_blocks == {} and b.blocks == [] and bm.num_free == free_before
+
+
+def _tiny_llm(prefix, num_blocks=0):
+    from vllm_xtu_moe_b200.engine import LLM
+    from vllm_xtu_moe_b200.engine.runner import RunnerConfig
+    from vllm_xtu_moe_b200.models.config import get_preset
+    return LLM(get_preset("tiny-mixtral"), device="cpu",
+               runner_config=RunnerConfig(block_size=16, max_seqs=2, max_model_len=256, max_batched_tokens=64,
+                                          use_cuda_graph=False, prefix_caching=prefix, num_blocks=num_blocks))
+
+
+def test_prefix_caching_reuses_blocks_and_keeps_outputs():
+    """Requests that share a prompt prefix start from its cached blocks: the same tokens as
+    without caching, fewer prompt tokens computed; with a pool too small to keep them,
+    cached blocks are evicted and outputs still match."""
+    shared = list(range(3, 3 + 50))
+    prompts = [shared + [7, 8, 9], shared + [100, 101], shared[:40] + [5], list(range(200, 230))]
+    sp = SamplingParams(max_tokens=6)
+    base = _tiny_llm(False)
+    want = [base.generate([p], sp)[0].token_ids for p in prompts]
+    for nb in (0, 12):
+        llm = _tiny_llm(True, nb)
+        got = [llm.generate([p], sp)[0].token_ids for p in prompts]
+        assert got == want, nb
+        if nb == 0:
+            assert llm.blocks.prefix_hits == 48 + 32        # 3 full blocks, then 2
+            assert llm.stats["prefill_tokens"] == sum(len(p) for p in prompts) - 80
+        assert llm.blocks.num_free == llm.blocks.num_blocks   # every block back (free or cached)

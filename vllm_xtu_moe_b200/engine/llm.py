@@ -70,8 +70,12 @@ class LLM:
         self.tiering = tiering
         rc = runner_config or RunnerConfig()
         self.runner = ModelRunner(self.model, rc)
+        cfg_m = self.model.cfg
+        stateless = not (cfg_m.layer_types and "linear" in cfg_m.layer_types) and rc.swa_blocks == 0
+        if rc.prefix_caching and not stateless:
+            raise ValueError("prefix caching needs a model without linear-attention state or a sliding-window pool")
         self.blocks = BlockManager(rc.num_blocks, rc.block_size, rc.max_seqs, swa_blocks=rc.swa_blocks,
-                                   window=self.model.cfg.sliding_window)
+                                   window=cfg_m.sliding_window, prefix_caching=rc.prefix_caching)
         self.scheduler = Scheduler(self.blocks, rc.max_batched_tokens, rc.max_seqs, rc.num_spec)
         self.spec = None
         if rc.num_spec > 0 and self.model.mtp:

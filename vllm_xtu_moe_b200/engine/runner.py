@@ -44,6 +44,9 @@ class RunnerConfig:
     # with "swa" layers, no speculative decoding); False: they share the full-context pool
     swa_bounded: bool = True
     swa_blocks: int = 0            # set by the runner: blocks of that pool (0 = no pool)
+    # reuse the KV blocks of a cached prompt prefix (models without linear-attention
+    # state or a sliding-window pool, whose per-request state a shared prefix cannot carry)
+    prefix_caching: bool = False
 
 
 class ModelRunner:

@@ -61,15 +61,18 @@ class Scheduler:
                     budget -= n
         while self.waiting and budget > 0 and len(self.running) < self.max_seqs:
             r = self.waiting[0]
-            n = min(len(r.prompt), budget)
             if not self.blocks.acquire_slot(r):
                 break
-            if not self.blocks.ensure(r, n):
+            self.blocks.match_prefix(r)          # prefix caching: skip the cached blocks
+            n = min(len(r.prompt) - r.num_computed, budget)
+            if not self.blocks.ensure(r, r.num_computed + n):
+                self.blocks.release(r)           # give the shared prefix back; retry later
+                r.num_computed = 0
                 break
             self.waiting.popleft()
             r.status = Status.PREFILL
             self.running.append(r)
-            chunks.append(ScheduledChunk(r, 0, n))
+            chunks.append(ScheduledChunk(r, r.num_computed, n))
             budget -= n
         if chunks:
             return StepPlan(False, chunks)
