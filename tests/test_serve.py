@@ -51,6 +51,12 @@ def test_chat_sampling_and_streaming_cpu():
         s3 = c.post("/v1/completions", json={**body, "seed": 12}).json()["choices"][0]["token_ids"]
         assert s1 == s2 and s1 != s3
         assert c.post("/v1/completions", json={**body, "top_p": 0.0}).status_code == 400
+        # a stop token ends the completion early
+        full = c.post("/v1/completions", json={"prompt": list(range(1, 20)), "max_tokens": 8}).json()
+        toks = full["choices"][0]["token_ids"]
+        cut = c.post("/v1/completions", json={"prompt": list(range(1, 20)), "max_tokens": 8,
+                                              "stop_token_ids": [toks[2]]}).json()["choices"][0]
+        assert cut["token_ids"] == toks[:toks.index(toks[2]) + 1] and cut["finish_reason"] == "stop"
         # streaming: the events carry the same tokens as the blocking call
         want = c.post("/v1/completions", json={"prompt": list(range(5, 25)), "max_tokens": 7}).json()
         got, done = [], False

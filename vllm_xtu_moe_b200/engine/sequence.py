@@ -15,6 +15,7 @@ class SamplingParams:
     ignore_eos: bool = True
     eos_token_id: int | None = None
     seed: int | None = None
+    stop_token_ids: tuple = ()    # finish after any of these tokens (even with ignore_eos)
 
 
 class Status(enum.Enum):
@@ -64,5 +65,7 @@ class Request:
         if len(self.output) >= p.max_tokens:
             return True
         if not p.ignore_eos and p.eos_token_id is not None and self.output and self.output[-1] == p.eos_token_id:
+            return True
+        if p.stop_token_ids and self.output and self.output[-1] in p.stop_token_ids:
             return True
         return False

@@ -158,6 +158,7 @@ def build_app(engine: EngineThread, model_name: str, codec: TextCodec | None = N
         top_k: int = 0
         seed: int | None = None
         ignore_eos: bool = True
+        stop_token_ids: list[int] = []
         stream: bool = False
 
     class CompletionRequest(Sampling):
@@ -193,7 +194,8 @@ def build_app(engine: EngineThread, model_name: str, codec: TextCodec | None = N
         if req.temperature < 0 or not (0 < req.top_p <= 1) or req.top_k < 0 or req.max_tokens < 1:
             raise HTTPException(400, "invalid sampling parameters")
         return SamplingParams(max_tokens=req.max_tokens, temperature=req.temperature, top_p=req.top_p,
-                              top_k=req.top_k, seed=req.seed, ignore_eos=req.ignore_eos, eos_token_id=codec.eos)
+                              top_k=req.top_k, seed=req.seed, ignore_eos=req.ignore_eos, eos_token_id=codec.eos,
+                              stop_token_ids=tuple(req.stop_token_ids))
 
     async def run(ids: list[int], sp: SamplingParams):
         try:
@@ -262,10 +264,11 @@ def main(argv=None):
     ap.add_argument("--num-spec", type=int, default=0)
     ap.add_argument("--layers", type=int, default=None)
     ap.add_argument("--tokenizer", default=None, help="local HF tokenizer directory (default: UTF-8 bytes)")
+    ap.add_argument("--prefix-caching", action="store_true", help="reuse the KV blocks of cached prompt prefixes")
     a = ap.parse_args(argv)
     import uvicorn
     rc = RunnerConfig(max_seqs=a.max_seqs, max_model_len=a.max_model_len, max_batched_tokens=a.max_batched_tokens,
-                      num_spec=a.num_spec)
+                      num_spec=a.num_spec, prefix_caching=a.prefix_caching)
     llm = LLM(a.model, device=a.device, runner_config=rc, num_layers=a.layers)
     eng = EngineThread(llm)
     uvicorn.run(build_app(eng, a.model, TextCodec(a.tokenizer)), host=a.host, port=a.port, log_level="warning")
