@@ -51,6 +51,10 @@ def test_chat_sampling_and_streaming_cpu():
         s3 = c.post("/v1/completions", json={**body, "seed": 12}).json()["choices"][0]["token_ids"]
         assert s1 == s2 and s1 != s3
         assert c.post("/v1/completions", json={**body, "top_p": 0.0}).status_code == 400
+        # n choices: seeds seed, seed + 1 -> the first equals the single seeded call
+        multi = c.post("/v1/completions", json={**body, "seed": 11, "n": 2}).json()
+        assert [ch["index"] for ch in multi["choices"]] == [0, 1]
+        assert multi["choices"][0]["token_ids"] == s1 and multi["choices"][1]["token_ids"] == s3
         # a stop token ends the completion early
         full = c.post("/v1/completions", json={"prompt": list(range(1, 20)), "max_tokens": 8}).json()
         toks = full["choices"][0]["token_ids"]

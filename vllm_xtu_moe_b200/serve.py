@@ -17,6 +17,7 @@ a per-request queue when streaming); the thread admits new requests between step
 
 import argparse
 import asyncio
+import dataclasses
 import json
 import queue
 import threading
@@ -160,6 +161,7 @@ def build_app(engine: EngineThread, model_name: str, codec: TextCodec | None = N
         ignore_eos: bool = True
         stop_token_ids: list[int] = []
         stream: bool = False
+        n: int = 1                       # choices per request (sampled: seeds seed, seed+1, ...)
 
     class CompletionRequest(Sampling):
         prompt: list[int] | str
@@ -203,6 +205,14 @@ def build_app(engine: EngineThread, model_name: str, codec: TextCodec | None = N
         except ValueError as e:
             raise HTTPException(400, str(e))
 
+    async def run_n(ids: list[int], sp: SamplingParams, n: int):
+        """n choices: n requests (batched by the engine), seeds seed, seed + 1, ..."""
+        if n < 1 or n > 64:
+            raise HTTPException(400, "n must be in [1, 64]")
+        sps = [sp if i == 0 else dataclasses.replace(sp, seed=None if sp.seed is None else sp.seed + i)
+               for i in range(n)]
+        return await asyncio.gather(*(run(ids, p) for p in sps))
+
     def stream(ids: list[int], sp: SamplingParams, make_chunk):
         loop = asyncio.get_running_loop()
         q: asyncio.Queue = asyncio.Queue()
@@ -226,13 +236,18 @@ def build_app(engine: EngineThread, model_name: str, codec: TextCodec | None = N
         ids = codec.encode(req.prompt)
         sp = params_of(req)
         if req.stream:
+            if req.n != 1:
+                raise HTTPException(400, "streaming serves one choice (n = 1)")
             return stream(ids, sp, lambda new: {"object": "text_completion", "model": model_name, "choices": [
                 {"index": 0, "token_ids": new, "text": codec.decode(new), "finish_reason": None}]})
-        r = await run(ids, sp)
+        rs = await run_n(ids, sp, req.n)
+        r = rs[0]
         return {"id": f"cmpl-{r.rid}", "object": "text_completion", "model": model_name,
-                "choices": [{"index": 0, "token_ids": list(r.output), "text": codec.decode(list(r.output)),
-                             "finish_reason": "length" if len(r.output) >= sp.max_tokens else "stop"}],
-                "usage": usage(ids, r.output),
+                "choices": [{"index": i, "token_ids": list(x.output), "text": codec.decode(list(x.output)),
+                             "finish_reason": "length" if len(x.output) >= sp.max_tokens else "stop"}
+                            for i, x in enumerate(rs)],
+                "usage": {"prompt_tokens": len(ids), "completion_tokens": sum(len(x.output) for x in rs),
+                          "total_tokens": len(ids) + sum(len(x.output) for x in rs)},
                 "timing": {"ttft_s": r.t_first - r.t_submit, "e2e_s": r.t_done - r.t_submit}}
 
     @app.post("/v1/chat/completions")
