@@ -78,3 +78,17 @@ def test_sampling_from_decode_graph_logits():
     k1 = [o.token_ids for o in llm.generate(prompts, SamplingParams(max_tokens=8, temperature=1.0, top_k=1, seed=5))]
     assert a == b and a != greedy and k1 == greedy
     llm.shutdown()
+
+
+def test_logprobs_of_greedy_tokens():
+    """Greedy tokens come with their log-probability, which is the best of the returned
+    alternatives; sampled tokens' log-probabilities are finite and not above 0."""
+    llm = _llm()
+    out = llm.generate([list(range(1, 30))], SamplingParams(max_tokens=6, logprobs=3))[0]
+    assert len(out.logprobs) == 6
+    for tok, (lp, alt) in zip(out.token_ids, out.logprobs):
+        assert len(alt) == 3 and lp <= 0.0
+        assert abs(lp - max(alt.values())) < 1e-5 and tok in alt
+    s = llm.generate([list(range(1, 30))], SamplingParams(max_tokens=6, temperature=1.0, seed=2, logprobs=0))[0]
+    assert len(s.logprobs) == 6 and all(lp <= 0.0 and alt == {} for lp, alt in s.logprobs)
+    assert llm.generate([list(range(1, 30))], SamplingParams(max_tokens=2))[0].logprobs is None

@@ -55,6 +55,9 @@ def test_chat_sampling_and_streaming_cpu():
         multi = c.post("/v1/completions", json={**body, "seed": 11, "n": 2}).json()
         assert [ch["index"] for ch in multi["choices"]] == [0, 1]
         assert multi["choices"][0]["token_ids"] == s1 and multi["choices"][1]["token_ids"] == s3
+        lp = c.post("/v1/completions", json={"prompt": list(range(1, 20)), "max_tokens": 4,
+                                             "logprobs": 2}).json()["choices"][0]["logprobs"]
+        assert len(lp["token_logprobs"]) == 4 and all(len(t) == 2 for t in lp["top_logprobs"])
         # a stop token ends the completion early
         full = c.post("/v1/completions", json={"prompt": list(range(1, 20)), "max_tokens": 8}).json()
         toks = full["choices"][0]["token_ids"]

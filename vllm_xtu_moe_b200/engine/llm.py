@@ -38,6 +38,7 @@ class RequestOutput:
     e2e_s: float
     accepted: int = 0
     proposed: int = 0
+    logprobs: list | None = None      # per token (log-probability, top alternatives) when asked
 
 
 class LLM:
@@ -91,8 +92,9 @@ class LLM:
 
     # ------------------------------------------------------------------
     def add_request(self, prompt: list[int], params: SamplingParams) -> Request:
-        if params.temperature > 0.0 and self.spec is not None:
-            raise ValueError("speculative decoding verifies greedy drafts; sampled requests need num_spec=0")
+        if (params.temperature > 0.0 or params.logprobs is not None) and self.spec is not None:
+            raise ValueError("speculative decoding verifies greedy drafts; sampled requests and logprobs "
+                             "need num_spec=0")
         r = Request(list(prompt), params)
         r.t_submit = time.perf_counter()
         self.scheduler.add(r)
@@ -174,7 +176,8 @@ class LLM:
         out = []
         for r in reqs:
             out.append(RequestOutput(r.rid, len(r.prompt), list(r.output), r.t_first - r.t_submit,
-                                     r.t_done - r.t_submit, r.accepted, r.proposed))
+                                     r.t_done - r.t_submit, r.accepted, r.proposed,
+                                     list(r.logprobs) if r.params.logprobs is not None else None))
         return out
 
     def shutdown(self):

@@ -191,10 +191,12 @@ class ModelRunner:
                 tok, logits = self._decode_graph(ids, meta)
                 if logits is not None and S.needs_sampling(reqs):
                     tok = S.sample_rows(logits, reqs, tok)
+                self._logprobs(logits, tok, reqs)
                 return tok, None
             tok, h, pre, logits = self.forward(ids, meta, torch.arange(ids.shape[0], device=self.device))
             if logits is not None and S.needs_sampling(reqs):
                 tok = S.sample_rows(logits, reqs, tok)
+            self._logprobs(logits, tok, reqs)
             return tok, (h, pre, meta)
         # prefill: logits only for chunks that finish their prompt
         rows, reqs = [], []
@@ -206,7 +208,18 @@ class ModelRunner:
         tok, h, pre, logits = self.forward(ids, meta, rt)
         if logits is not None and S.needs_sampling(reqs):
             tok = S.sample_rows(logits, reqs, tok)
+        self._logprobs(logits, tok, reqs)
         return tok, (h, pre, meta, rows)
+
+    def _logprobs(self, logits, tok, reqs) -> None:
+        """Record each row's token log-probability (and alternatives) for requests asking."""
+        k = S.wants_logprobs(reqs) if logits is not None else -1
+        if k < 0:
+            return
+        for r, lp in zip(reqs, S.row_logprobs(logits, tok, k)):
+            if r.params.logprobs is not None:
+                n = r.params.logprobs
+                r.logprobs.append((lp[0], dict(list(lp[1].items())[:n])))
 
     # ------------------------------------------------------------------
     # CUDA-graph decode (one token per sequence)

@@ -53,3 +53,23 @@ def sample_rows(logits: torch.Tensor, reqs: list, greedy: torch.Tensor) -> torch
         p = filtered_probs(logits[i], sp.temperature, sp.top_k, sp.top_p)
         out[i] = torch.multinomial(p, 1, generator=_generator(r, logits.device)).to(out.dtype)[0]
     return out
+
+
+def wants_logprobs(reqs) -> int:
+    """Largest number of alternatives any request asks for, or -1 when none wants logprobs."""
+    ks = [r.params.logprobs for r in reqs if r.params.logprobs is not None]
+    return max(ks) if ks else -1
+
+
+def row_logprobs(logits: torch.Tensor, tokens: torch.Tensor, k: int) -> list:
+    """Per row: (log-probability of the chosen token under the model's distribution,
+    {token: log-probability} of the k most likely tokens)."""
+    lp = torch.log_softmax(logits.float(), dim=-1)
+    chosen = lp.gather(1, tokens.long().view(-1, 1)).view(-1).tolist()
+    out = []
+    if k > 0:
+        vals, idx = torch.topk(lp, k, dim=-1)
+        vals, idx = vals.tolist(), idx.tolist()
+    for i, c in enumerate(chosen):
+        out.append((c, dict(zip(idx[i], vals[i])) if k > 0 else {}))
+    return out

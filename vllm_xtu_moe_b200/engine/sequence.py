@@ -16,6 +16,7 @@ class SamplingParams:
     eos_token_id: int | None = None
     seed: int | None = None
     stop_token_ids: tuple = ()    # finish after any of these tokens (even with ignore_eos)
+    logprobs: int | None = None   # return each token's log-probability and this many top alternatives
 
 
 class Status(enum.Enum):
@@ -47,6 +48,8 @@ class Request:
     draft: list[int] = field(default_factory=list)
     accepted: int = 0
     proposed: int = 0
+    # per output token: (log-probability, {token: log-probability} of the top alternatives)
+    logprobs: list = field(default_factory=list)
 
     @property
     def all_tokens(self) -> list[int]:

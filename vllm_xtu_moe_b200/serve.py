@@ -162,6 +162,7 @@ def build_app(engine: EngineThread, model_name: str, codec: TextCodec | None = N
         stop_token_ids: list[int] = []
         stream: bool = False
         n: int = 1                       # choices per request (sampled: seeds seed, seed+1, ...)
+        logprobs: int | None = None      # per-token log-probabilities and this many alternatives
 
     class CompletionRequest(Sampling):
         prompt: list[int] | str
@@ -197,7 +198,8 @@ def build_app(engine: EngineThread, model_name: str, codec: TextCodec | None = N
             raise HTTPException(400, "invalid sampling parameters")
         return SamplingParams(max_tokens=req.max_tokens, temperature=req.temperature, top_p=req.top_p,
                               top_k=req.top_k, seed=req.seed, ignore_eos=req.ignore_eos, eos_token_id=codec.eos,
-                              stop_token_ids=tuple(req.stop_token_ids))
+                              stop_token_ids=tuple(req.stop_token_ids),
+                              logprobs=None if req.logprobs is None else max(0, min(int(req.logprobs), 20)))
 
     async def run(ids: list[int], sp: SamplingParams):
         try:
@@ -228,6 +230,12 @@ def build_app(engine: EngineThread, model_name: str, codec: TextCodec | None = N
                     return
         return StreamingResponse(events(), media_type="text/event-stream")
 
+    def logprobs_of(r):
+        if r.params.logprobs is None:
+            return None
+        return {"tokens": list(r.output), "token_logprobs": [lp for lp, _ in r.logprobs],
+                "top_logprobs": [{str(t): v for t, v in alt.items()} for _, alt in r.logprobs]}
+
     def usage(ids, out):
         return {"prompt_tokens": len(ids), "completion_tokens": len(out), "total_tokens": len(ids) + len(out)}
 
@@ -244,6 +252,7 @@ def build_app(engine: EngineThread, model_name: str, codec: TextCodec | None = N
         r = rs[0]
         return {"id": f"cmpl-{r.rid}", "object": "text_completion", "model": model_name,
                 "choices": [{"index": i, "token_ids": list(x.output), "text": codec.decode(list(x.output)),
+                             "logprobs": logprobs_of(x),
                              "finish_reason": "length" if len(x.output) >= sp.max_tokens else "stop"}
                             for i, x in enumerate(rs)],
                 "usage": {"prompt_tokens": len(ids), "completion_tokens": sum(len(x.output) for x in rs),
