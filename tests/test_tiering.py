@@ -593,3 +593,10 @@ def test_planner_counts_window_layers_once_per_sequence():
     assert b - a == per_tok_full * 16384 * 4
     p = PL.plan(cfg, max_model_len=131072, max_seqs=1)
     assert p.kv < 20 * (1 << 30)
+
+
+def test_pool_hit_share():
+    from vllm_xtu_moe_b200.tiering.policy import pool_hits
+    assert pool_hits({0: 5, 3: 2, 7: 3}, [3, 7]) == (5, 10)
+    assert pool_hits([1, 0, 4, 0], [2]) == (4, 5)
+    assert pool_hits({}, [1]) == (0, 0)

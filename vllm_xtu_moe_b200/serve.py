@@ -191,6 +191,11 @@ def build_app(engine: EngineThread, model_name: str, codec: TextCodec | None = N
                  f"xtu_decode_tokens_total {st['decode_tokens']}",
                  f"xtu_prefill_seconds_total {st['prefill_time']:.6f}",
                  f"xtu_decode_seconds_total {st['decode_time']:.6f}"]
+        tier = getattr(engine.llm, "tiering", None)
+        if tier is not None:
+            ts = tier.stats(hit_rate=False)
+            lines += [f"xtu_tier_calls_total{{path=\"{k}\"}} {v}" for k, v in ts.items() if k != "swaps"]
+            lines.append(f"xtu_pool_swaps_total {ts['swaps']}")
         return "\n".join(lines) + "\n"
 
     def params_of(req: Sampling) -> SamplingParams:

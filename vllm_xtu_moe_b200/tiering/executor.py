@@ -302,11 +302,20 @@ class TieredExperts:
         ws = sum(w.nbytes() for w in self._ws.values())
         return {"pools": pools, "ring": ring, "workspaces": ws}
 
-    def stats(self) -> dict:
+    def stats(self, hit_rate: bool = False) -> dict:
+        """Call counts per path; ``hit_rate``: also the share of routed pairs the hot-expert
+        pools served (synchronises the device)."""
         out = {"ring": 0, "hybrid": 0, "cpu": 0, "async": 0, "deferred": 0, "swaps": self.swaps}
         for ex in self.executors:
             for k, v in ex.calls.items():
                 out[k] += v
+        if hit_rate:
+            hit = tot = 0
+            for ex in self.executors:
+                if ex.pool is not None and ex.pool.nslots > 0:
+                    h, t = ex.pool.hit_counts()
+                    hit, tot = hit + h, tot + t
+            out["pool_hit_rate"] = hit / tot if tot else None
         return out
 
     def shutdown(self) -> None:

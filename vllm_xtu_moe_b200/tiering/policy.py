@@ -95,3 +95,19 @@ def plan_swap(resident: list[int], counts: dict[int, int], nslots: int, *, hyst:
     assert not (set(evict) & set(load))
     assert all(counts.get(v, 0) <= counts.get(l, 0) for v, l in zip(evict, load))
     return evict, load
+
+
+def pool_hits(counts: dict[int, int] | list[int], experts: list[int]) -> tuple[int, int]:
+    """(routed pairs that went to a pooled expert, all routed pairs) for per-expert counts
+    (the reference's PIN hit-rate windows, vllm_xiaotu_moe/mixed_experts.py:3020-3100)."""
+    if isinstance(counts, dict):
+        items = counts.items()
+    else:
+        items = enumerate(counts)
+    pooled = set(experts)
+    hit = tot = 0
+    for e, c in items:
+        tot += int(c)
+        if e in pooled:
+            hit += int(c)
+    return hit, tot

@@ -17,7 +17,7 @@ import torch
 
 from ..ops import moe as M
 from .host import HostExperts, alloc_expert_slots
-from .policy import plan_swap
+from .policy import plan_swap, pool_hits
 
 
 class LayerPool:
@@ -36,6 +36,7 @@ class LayerPool:
         self.hits = torch.zeros(self.E, dtype=torch.int32, device=device)
         self.steps = 0
         self.swaps_in = 0
+        self.hit_pairs = self.total_pairs = 0    # pairs counted at past window ends
         self.side = torch.cuda.Stream(device=device)
         for s, e in enumerate(experts):
             self._load(e, s)
@@ -47,6 +48,11 @@ class LayerPool:
     def _load(self, e: int, s: int) -> None:
         self.host.copy_slot(e, self.slots, s, self.side)
 
+    def hit_counts(self) -> tuple[int, int]:
+        """(pairs served by the pool, all routed pairs) since the pool was built (synchronises)."""
+        h, t = pool_hits(self.hits.cpu().tolist(), self.expert_of)
+        return self.hit_pairs + h, self.total_pairs + t
+
     def maybe_adapt(self, preserve_oldest: bool = False) -> tuple[list[int], list[int]]:
         """Called by the host once per step (outside graph capture)."""
         self.steps += 1
@@ -55,6 +61,9 @@ class LayerPool:
         counts_t = self.hits.cpu()
         self.hits.zero_()
         counts = {e: int(c) for e, c in enumerate(counts_t.tolist()) if c}
+        h, t = pool_hits(counts, self.expert_of)
+        self.hit_pairs += h
+        self.total_pairs += t
         evict, load = plan_swap(self.expert_of, counts, self.nslots, hyst=self.hyst, maxswap=self.maxswap,
                                 preserve_oldest=preserve_oldest)
         if not evict:
