@@ -280,7 +280,10 @@ def _pp_worker(rank, world, port, name, backend):
     _init(rank, world, port, backend)
     gpu = backend == "nccl"
     dev = f"cuda:{rank}" if gpu else "cpu"
-    cfg = _tp_cfg(name).replace(num_layers=5)
+    cfg = _tp_cfg(name)
+    if cfg.layer_types is not None:
+        cfg = cfg.replace(layer_types=(cfg.layer_types * 2)[:5])
+    cfg = cfg.replace(num_layers=5)
     if gpu:
         cfg = cfg.replace(hidden_size=512, num_heads=8, dense_fmt="fp8", expert_fmt="fp8")
     full = build_model(cfg, device=dev, seed=4)
@@ -302,7 +305,7 @@ def _pp_worker(rank, world, port, name, backend):
     # micro-batches: a batch through the stages with non-blocking sends, vs one local pass
     llm = LLM(full, device=dev, runner_config=rc())
     caches_ref = llm.runner.caches
-    st_caches = stage.allocate_caches(llm.runner.rc.num_blocks, bs, 2)
+    st_caches = stage.allocate_caches(llm.runner.rc.num_blocks, bs, 2, swa_blocks=llm.runner.rc.swa_blocks)
     batches = []
     for p in prompts:
         llm.add_request(p, SamplingParams(max_tokens=1))
@@ -319,8 +322,11 @@ def _pp_worker(rank, world, port, name, backend):
     dist.destroy_process_group()
 
 
-def test_pipeline_stages_match_single_rank_cpu():
-    mp.spawn(_pp_worker, args=(3, _port(), "glm-4.5-air", "gloo"), nprocs=3)
+@pytest.mark.parametrize("name", ["glm-4.5-air", "mimo-v2-flash"])
+def test_pipeline_stages_match_single_rank_cpu(name):
+    """Layers cut into 3 stages over gloo ranks give the single-rank tokens (MiMo: with the
+    sliding-window layers' bounded pool on every stage)."""
+    mp.spawn(_pp_worker, args=(3, _port(), name, "gloo"), nprocs=3)
 
 
 @pytest.mark.gpu
