@@ -101,3 +101,26 @@ def test_oracle_drafts_gpu():
     same = sum(a == b for o, p in zip(spec, base) for a, b in zip(o.token_ids, p.token_ids))
     assert same >= 0.9 * sum(len(o.token_ids) for o in base)
     assert steps < steps0
+
+
+def test_spec_decode_with_bounded_window_pool_cpu():
+    """MiMo-style model (sliding-window layers on their bounded pool, one MTP layer): MTP
+    speculative decoding gives the plain greedy tokens."""
+    cfg = scaled_down(get_preset("mimo-v2-flash"), layers=4, hidden=256, experts=8).replace(
+        num_heads=4, num_kv_heads=2, swa_num_kv_heads=4, head_dim=64, v_head_dim=32, rotary_dim=32,
+        sliding_window=16, moe_intermediate=128, dense_intermediate=256, num_mtp_layers=1,
+        expert_fmt="bf16", dense_fmt="bf16")
+    m = build_model(cfg, device="cpu", seed=2)
+    m.act_dtype = torch.float32
+    prompts = [list(range(3, 60)), list(range(70, 85))]
+
+    def run(k):
+        rc = RunnerConfig(block_size=16, max_seqs=2, max_model_len=256, max_batched_tokens=64,
+                          use_cuda_graph=False, num_spec=k)
+        llm = LLM(m, device="cpu", runner_config=rc)
+        assert rc.swa_blocks > 0
+        outs = [o.token_ids for o in llm.generate(prompts, SamplingParams(max_tokens=12))]
+        llm.shutdown()
+        return outs
+
+    assert run(2) == run(0)

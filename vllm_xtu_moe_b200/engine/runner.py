@@ -41,7 +41,7 @@ class RunnerConfig:
     kv_mem_fraction: float = 0.9   # of free memory after weights, for the KV cache
     num_spec: int = 0
     # sliding-window layers keep only their window in a small pool of their own (models
-    # with "swa" layers, no speculative decoding); False: they share the full-context pool
+    # with "swa" layers); False: they share the full-context pool
     swa_bounded: bool = True
     swa_blocks: int = 0            # set by the runner: blocks of that pool (0 = no pool)
     # reuse the KV blocks of a cached prompt prefix (models without linear-attention
@@ -62,7 +62,7 @@ class ModelRunner:
         cfg = model.cfg
         has_swa = cfg.sliding_window > 0 and cfg.layer_types is not None and "swa" in cfg.layer_types
         rc.swa_blocks = (swa_pool_blocks(rc.max_seqs, cfg.sliding_window, rc.block_size, rc.max_batched_tokens)
-                         if has_swa and rc.swa_bounded and rc.num_spec == 0 else 0)
+                         if has_swa and rc.swa_bounded else 0)
         if rc.num_blocks <= 0:
             rc.num_blocks = self._auto_blocks()
         self.caches = model.allocate_caches(rc.num_blocks, rc.block_size, rc.max_seqs, swa_blocks=rc.swa_blocks)
