@@ -82,3 +82,16 @@ def test_prefix_caching_reuses_blocks_and_keeps_outputs():
             assert llm.blocks.prefix_hits == 48 + 32        # 3 full blocks, then 2
             assert llm.stats["prefill_tokens"] == sum(len(p) for p in prompts) - 80
         assert llm.blocks.num_free == llm.blocks.num_blocks   # every block back (free or cached)
+
+
+def test_abort_frees_a_running_request():
+    llm = _tiny_llm(False)
+    r = llm.add_request(list(range(1, 40)), SamplingParams(max_tokens=50))
+    other = llm.add_request(list(range(5, 30)), SamplingParams(max_tokens=3))
+    for _ in range(3):
+        llm.step()
+    assert llm.abort(r.rid) and not llm.abort(r.rid)
+    while llm.scheduler.has_work():
+        llm.step()
+    assert len(other.output) == 3 and r.blocks == [] and r.slot == -1
+    assert llm.blocks.num_free == llm.blocks.num_blocks

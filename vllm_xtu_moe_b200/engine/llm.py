@@ -100,6 +100,11 @@ class LLM:
         self.scheduler.add(r)
         return r
 
+    def abort(self, rid: int) -> bool:
+        """Stop request `rid` between steps (e.g. its client went away); its blocks and
+        recurrent-state slot are freed.  Returns whether the request was still live."""
+        return self.scheduler.abort(rid) is not None
+
     def step(self, plan=None) -> list[Request]:
         """Run one engine step (scheduling it unless a plan is given); returns finished requests."""
         if plan is None:

@@ -99,6 +99,17 @@ class Scheduler:
         r.status = Status.WAITING
         self.waiting.appendleft(r)
 
+    def abort(self, rid: int) -> Request | None:
+        """Drop request `rid` (waiting or running) and free its blocks; None if unknown."""
+        for q in (self.waiting, self.running):
+            for r in list(q):
+                if r.rid == rid:
+                    q.remove(r)
+                    self.blocks.release(r)
+                    r.status = Status.FINISHED
+                    return r
+        return None
+
     def finish(self, r: Request) -> None:
         r.status = Status.FINISHED
         if r in self.running:

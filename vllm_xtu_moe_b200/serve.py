@@ -38,7 +38,8 @@ class EngineThread:
         self.inbox: queue.Queue = queue.Queue()
         self.pending: dict[int, tuple[Future, float]] = {}
         self.streams: dict[int, list] = {}          # rid -> [callback, tokens already sent, request]
-        self.metrics = {"requests": 0, "tokens": 0, "steps": 0}
+        self.metrics = {"requests": 0, "tokens": 0, "steps": 0, "aborted": 0, "ttft_s": 0.0, "e2e_s": 0.0}
+        self.aborts: queue.Queue = queue.Queue()
         self._stop = threading.Event()
         self.error: BaseException | None = None
         self.thread = threading.Thread(target=self._loop, name="xtu-engine", daemon=True)
@@ -48,6 +49,10 @@ class EngineThread:
         f: Future = Future()
         self.inbox.put((prompt, params, f, on_tokens))
         return f
+
+    def abort(self, fut: Future) -> None:
+        """Cancel the request behind `fut` at the next step boundary (thread-safe)."""
+        self.aborts.put(fut)
 
     def _push(self, r, done: bool) -> None:
         st = self.streams.get(r.rid)
@@ -79,6 +84,17 @@ class EngineThread:
                     if cb is not None:
                         self.streams[r.rid] = [cb, 0, r]
                     admitted = True
+                while True:              # cancellations (clients that went away)
+                    try:
+                        fut = self.aborts.get_nowait()
+                    except queue.Empty:
+                        break
+                    for rid, (f, _) in list(self.pending.items()):
+                        if f is fut and self.llm.abort(rid):
+                            self.pending.pop(rid)
+                            self.streams.pop(rid, None)
+                            self.metrics["aborted"] += 1
+                            f.cancel()
                 if not self.llm.scheduler.has_work():
                     if not admitted:
                         time.sleep(0.001)
@@ -94,6 +110,8 @@ class EngineThread:
                     f, _ = self.pending.pop(r.rid)
                     self.metrics["requests"] += 1
                     self.metrics["tokens"] += len(r.output)
+                    self.metrics["ttft_s"] += r.t_first - r.t_submit
+                    self.metrics["e2e_s"] += r.t_done - r.t_submit
                     f.set_result(r)
         except BaseException as e:      # surface engine failures to every waiter
             self.error = e
@@ -187,6 +205,9 @@ def build_app(engine: EngineThread, model_name: str, codec: TextCodec | None = N
         m = engine.metrics
         st = engine.llm.stats
         lines = [f"xtu_requests_total {m['requests']}", f"xtu_generated_tokens_total {m['tokens']}",
+                 f"xtu_requests_aborted_total {m['aborted']}",
+                 f"xtu_time_to_first_token_seconds_sum {m['ttft_s']:.6f}",
+                 f"xtu_request_latency_seconds_sum {m['e2e_s']:.6f}",
                  f"xtu_engine_steps_total {m['steps']}", f"xtu_prefill_tokens_total {st['prefill_tokens']}",
                  f"xtu_decode_tokens_total {st['decode_tokens']}",
                  f"xtu_prefill_seconds_total {st['prefill_time']:.6f}",
@@ -223,16 +244,22 @@ def build_app(engine: EngineThread, model_name: str, codec: TextCodec | None = N
     def stream(ids: list[int], sp: SamplingParams, make_chunk):
         loop = asyncio.get_running_loop()
         q: asyncio.Queue = asyncio.Queue()
-        engine.submit(ids, sp, on_tokens=lambda new, done: loop.call_soon_threadsafe(q.put_nowait, (new, done)))
+        fut = engine.submit(ids, sp, on_tokens=lambda new, done: loop.call_soon_threadsafe(q.put_nowait, (new, done)))
 
         async def events():
-            while True:
-                new, done = await q.get()
-                if new:
-                    yield "data: " + json.dumps(make_chunk(new)) + "\n\n"
-                if done:
-                    yield "data: [DONE]\n\n"
-                    return
+            finished = False
+            try:
+                while True:
+                    new, done = await q.get()
+                    if new:
+                        yield "data: " + json.dumps(make_chunk(new)) + "\n\n"
+                    if done:
+                        finished = True
+                        yield "data: [DONE]\n\n"
+                        return
+            finally:
+                if not finished:        # the client went away: stop generating for it
+                    engine.abort(fut)
         return StreamingResponse(events(), media_type="text/event-stream")
 
     def logprobs_of(r):
