@@ -4,7 +4,7 @@ concurrency C, on N GPUs of one node (one rank per GPU, data-parallel replicas).
 One *step* = one serving round per rank: C requests of ``--prompt-len`` uniform
 random token ids are submitted together, prefilled (chunked), then decoded for
 ``--output-len`` tokens each (greedy).  Model: GLM-4.5-Air-style MoE
-(46 layers, hidden 4096, GQA 96/8 x 128, partial RoPE,
+(benchmark config 4: 46 layers, hidden 4096, GQA 96/8 x 128, partial RoPE,
 128 experts top-8 + 1 shared, I=1408, fp8 e4m3 128x128 block-scaled weights,
 random init).  The weights (~110 GB) and the KV cache are read every step, far
 beyond the 126 MB L2, so no L2 flush is needed between steps.

@@ -161,7 +161,7 @@ class ModelConfig:
 
 
 # ---------------------------------------------------------------------------
-# presets
+# presets (the benchmarked configurations 1-5, plus the MiMo-V2 and Kimi-Linear families)
 # ---------------------------------------------------------------------------
 def tiny_mixtral() -> ModelConfig:
     """Config 1: 2 layers, hidden 256, 4 heads / 2 KV heads x 64, 8 experts top-2, I=512, vocab 1024."""
