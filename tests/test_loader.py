@@ -92,3 +92,65 @@ def test_loader_streams_experts_into_sink(tmp_path):
     assert [s[0] for s in seen] == moe_layers
     assert all(s[1] == "fp8" and s[2] == (E, 2 * I, H) and s[3] == (E, 2 * I // 128, H // 128) for s in seen)
     src.close()
+
+
+def _gptq_pack(w: torch.Tensor, group: int = 32):
+    """Test-side GPTQ packer (AutoGPTQ "gptq" format) of a weight [out, in]: returns the
+    checkpoint tensors and the exact dequantized weight they stand for."""
+    N, K = w.shape
+    G = K // group
+    wt = w.t().float()                                             # [in, out]
+    wg = wt.view(G, group, N)
+    scale = (wg.abs().amax(1) / 7.0).clamp(min=1e-4).half()       # [G, out]
+    zero = torch.full((G, N), 8, dtype=torch.int64)
+    q = (torch.round(wg / scale.float()[:, None, :]) + 8).clamp(0, 15).to(torch.int64).view(K, N)
+    qw = torch.zeros(K // 8, N, dtype=torch.int64)
+    for i in range(8):
+        qw |= q[i::8] << (4 * i)
+    qz = torch.zeros(G, N // 8, dtype=torch.int64)
+    for i in range(8):
+        qz |= (zero[:, i::8] - 1) << (4 * i)
+    deq = ((q.view(G, group, N) - zero[:, None, :]).float() * scale.float()[:, None, :]).view(K, N).t()
+    def to32(t):       # the uint32 words as the int32 tensors checkpoints store
+        return torch.tensor(((t + 2 ** 31) % 2 ** 32 - 2 ** 31).tolist(), dtype=torch.int32)
+    return {"qweight": to32(qw), "qzeros": to32(qz), "scales": scale}, deq
+
+
+def test_gptq_dequant_matches_packing():
+    from vllm_xtu_moe_b200.ops.quant import dequant_gptq
+    torch.manual_seed(0)
+    w = torch.randn(64, 128) * 0.05
+    t, deq = _gptq_pack(w)
+    got = dequant_gptq(t["qweight"], t["scales"], t["qzeros"])
+    assert torch.equal(got, deq)
+    assert (got - w).abs().max().item() < 0.02
+
+
+def test_gptq_checkpoint_loads(tmp_path):
+    """Experts and attention projections stored as GPTQ INT4: the loaded model equals one
+    loaded from the same weights dequantized to bf16."""
+    from vllm_xtu_moe_b200.utils.safetensors import SafetensorsFile, save_file
+    cfg = _cfg("tiny-mixtral")
+    m = build_model(cfg, device="cpu", seed=5)
+    export_hf(m, cfg, tmp_path / "model.safetensors")
+    f = SafetensorsFile(tmp_path / "model.safetensors")
+    tensors = {k: f.get(k).clone() for k in f.keys()}
+    f.close()
+    gptq, plain = dict(tensors), dict(tensors)
+    for k in list(tensors):
+        if k.endswith(".weight") and (".experts." in k or ".self_attn.q_proj" in k):
+            pre = k[:-len(".weight")]
+            packed, deq = _gptq_pack(tensors[k].float())
+            del gptq[k]
+            gptq.update({f"{pre}.{s}": v for s, v in packed.items()})
+            plain[k] = deq.to(torch.bfloat16)
+    (tmp_path / "g").mkdir()
+    (tmp_path / "p").mkdir()
+    save_file(gptq, tmp_path / "g" / "model.safetensors", {"format": "pt"})
+    save_file(plain, tmp_path / "p" / "model.safetensors", {"format": "pt"})
+    mg, sg = load_model(tmp_path / "g", device="cpu", cfg=cfg)
+    mp_, sp_ = load_model(tmp_path / "p", device="cpu", cfg=cfg)
+    assert sg.used == set(sg.ckpt.keys())
+    assert torch.equal(_logits(mg), _logits(mp_))
+    sg.close()
+    sp_.close()

@@ -26,7 +26,7 @@ import re
 import torch
 
 from ..ops import gemm as G
-from ..ops.quant import dequant_fp8_block, quant_fp8_block
+from ..ops.quant import dequant_fp8_block, dequant_gptq, quant_fp8_block
 from ..utils.safetensors import CheckpointDir
 from .config import ModelConfig, from_hf_config
 from .layers import Linear
@@ -144,8 +144,24 @@ class CheckpointSource:
         t = self._get(self._hf(name)[0])       # any shape with n elements (KDA keeps A_log [1, 1, nv, 1])
         return t.to(device=self.device, dtype=ref.dtype, copy=True).reshape(ref.shape)
 
+    def _gptq(self, prefix: str) -> torch.Tensor:
+        """A GPTQ-quantized projection, dequantized to fp32 [out, in]."""
+        opt = lambda k: self._get(prefix + k) if (prefix + k) in self.ckpt else None
+        return dequant_gptq(self._get(prefix + ".qweight"), self._get(prefix + ".scales"), opt(".qzeros"),
+                            opt(".g_idx"))
+
     def linear(self, name, n, k, fmt="bf16", bias=False, std=None) -> Linear:
         parts = self._hf(name)
+        if any((p + ".qweight") in self.ckpt for p in parts):   # GPTQ INT4: dequantized, then this layer's format
+            w = torch.cat([self._gptq(p) if (p + ".qweight") in self.ckpt else self._get(p + ".weight").float()
+                           for p in parts], 0)
+            b = torch.cat([self._get(p + ".bias") for p in parts], 0) if bias else None
+            if fmt == "fp8":
+                q, sc = quant_fp8_block(w)
+                return Linear(q.to(self.device), sc.to(self.device),
+                              None if b is None else b.to(device=self.device, dtype=torch.bfloat16))
+            return Linear(w.to(device=self.device, dtype=torch.bfloat16), None,
+                          None if b is None else b.to(device=self.device, dtype=torch.bfloat16))
         ws = [self._get(p + ".weight") for p in parts]
         w = torch.cat(ws, 0) if len(ws) > 1 else ws[0]
         scale = None
@@ -172,6 +188,17 @@ class CheckpointSource:
         pre, _ = self._layer_prefix(name)
         f = self.fam
         base = f"{pre}.{f['experts']}"
+        if f"{base}.0.{f['gate']}.qweight" in self.ckpt:
+            # GPTQ INT4 experts (the reference repacks them for its CPU engine): dequantized,
+            # then held as fp8-128 when the model's expert format asks for it, else bf16
+            w13 = torch.stack([torch.cat([self._gptq(f"{base}.{e}.{f['gate']}"),
+                                          self._gptq(f"{base}.{e}.{f['up']}")], 0) for e in range(E)])
+            w2 = torch.stack([self._gptq(f"{base}.{e}.{f['down']}") for e in range(E)])
+            if fmt == "fp8":
+                q13, s13 = quant_fp8_block(w13)
+                q2, s2 = quant_fp8_block(w2)
+                return {"fmt": "fp8", "w13": q13, "w2": q2, "s13": s13, "s2": s2}
+            return {"fmt": "bf16", "w13": w13.to(torch.bfloat16), "w2": w2.to(torch.bfloat16)}
         g0 = self.ckpt.get(f"{base}.0.{f['gate']}.weight")
         if g0.dtype == torch.uint8:
             fmt = "nvfp4" if f"{base}.0.{f['gate']}.weight_scale_2" in self.ckpt else "mxfp4"

@@ -137,3 +137,30 @@ def dequant_nvfp4(packed: torch.Tensor, scales: torch.Tensor, gscale: torch.Tens
     s = scales.float() * float(gscale)
     *lead, n, k = vals.shape
     return (vals.reshape(*lead, n, k // 16, 16) * s[..., None]).reshape(*lead, n, k)
+
+
+def dequant_gptq(qweight: torch.Tensor, scales: torch.Tensor, qzeros: torch.Tensor | None = None,
+                 g_idx: torch.Tensor | None = None, bits: int = 4) -> torch.Tensor:
+    """GPTQ-packed linear weight -> dense fp32 [out, in] (the HF Linear layout).
+
+    The AutoGPTQ "gptq" checkpoint format: ``qweight`` int32 [in * bits / 32, out] packs
+    32 / bits consecutive input rows per word (lowest bits first); ``scales`` [groups, out];
+    ``qzeros`` int32 [groups, out * bits / 32] packs the zero points along the output,
+    stored minus one (absent: symmetric, zero point 2^(bits-1)); ``g_idx`` [in] gives each
+    input row's group (absent: row // (in / groups)).  w[k, n] = (q[k, n] - z[g(k), n]) *
+    scales[g(k), n]."""
+    per = 32 // bits
+    mask = (1 << bits) - 1
+    qw = qweight.to(torch.int64) & 0xFFFFFFFF
+    shifts = torch.arange(per, dtype=torch.int64) * bits
+    q = ((qw[:, None, :] >> shifts[None, :, None]) & mask).reshape(qw.shape[0] * per, qw.shape[1])  # [in, out]
+    K, N = q.shape
+    G = scales.shape[0]
+    grp = g_idx.to(torch.int64) if g_idx is not None else torch.arange(K) // (K // G)
+    if qzeros is not None:
+        qz = qzeros.to(torch.int64) & 0xFFFFFFFF
+        z = ((qz[:, :, None] >> shifts[None, None, :]) & mask).reshape(G, -1)[:, :N] + 1
+    else:
+        z = torch.full((G, N), 1 << (bits - 1), dtype=torch.int64)
+    w = (q - z[grp]).float() * scales.float()[grp]
+    return w.t().contiguous()
