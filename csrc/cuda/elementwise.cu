@@ -750,7 +750,8 @@ __global__ void route_split_kernel(const int* __restrict__ ids, int n, int lo, i
 }
 
 // ---------------------------------------------------------------------------
-// greedy argmax over rows (fp32 or bf16 logits); ties -> lowest index
+// greedy argmax over rows (fp32 or bf16 logits); ties -> lowest index; NaN entries never win, and a
+// row with nothing above -FLT_MAX (all -inf / NaN) returns index 0
 // ---------------------------------------------------------------------------
 template <typename T>
 __device__ __forceinline__ float ld_f(const T* p, size_t i);
@@ -794,6 +795,9 @@ __global__ void argmax_kernel(const T* __restrict__ logits, int V, int stride, i
       if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
     }
     if (l == 0) {
+      // no element beat -FLT_MAX (the slice is all -inf or NaN): its first index stands in,
+      // so a row always yields a valid token id (NaN entries never win)
+      if (bi == 0x7fffffff && lo < hi) bi = lo;
       if (parts == 1) {
         out[blockIdx.y] = bi;
         if (out_val) out_val[blockIdx.y] = bv;

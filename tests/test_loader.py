@@ -154,3 +154,33 @@ def test_gptq_checkpoint_loads(tmp_path):
     assert torch.equal(_logits(mg), _logits(mp_))
     sg.close()
     sp_.close()
+
+
+def test_gptq_v2_zero_points_and_unsupported_formats(tmp_path):
+    """gptq_v2 stores zero points as they are (v1: minus one); 3-bit weights and unknown
+    checkpoint formats are refused instead of being dequantized wrongly."""
+    import json
+    from vllm_xtu_moe_b200.models.loader import CheckpointSource
+    from vllm_xtu_moe_b200.ops.quant import dequant_gptq
+    torch.manual_seed(1)
+    t, deq = _gptq_pack(torch.randn(64, 128) * 0.05)
+    qz = t["qzeros"].to(torch.int64) & 0xFFFFFFFF
+    v2 = torch.zeros_like(qz)
+    for i in range(8):                 # every packed zero point + 1 (no carries: v1 stores 7)
+        v2 |= (((qz >> (4 * i)) & 0xF) + 1) << (4 * i)
+    v2 = torch.tensor(((v2 + 2 ** 31) % 2 ** 32 - 2 ** 31).tolist(), dtype=torch.int32)
+    assert torch.equal(dequant_gptq(t["qweight"], t["scales"], v2, zero_offset=0), deq)
+    with pytest.raises(ValueError, match="3-bit"):
+        dequant_gptq(t["qweight"], t["scales"], t["qzeros"], bits=3)
+    for qc, ok in [({"quant_method": "gptq", "bits": 4, "checkpoint_format": "gptq_v2"}, (4, 0)),
+                   ({"quant_method": "gptq", "bits": 8}, (8, 1)),
+                   ({"quant_method": "gptq", "bits": 3}, None),
+                   ({"quant_method": "gptq", "bits": 4, "checkpoint_format": "marlin"}, None)]:
+        d = tmp_path / f"c{len(list(tmp_path.iterdir()))}"
+        d.mkdir()
+        (d / "config.json").write_text(json.dumps({"quantization_config": qc}))
+        if ok is None:
+            with pytest.raises(ValueError):
+                CheckpointSource._gptq_format(d)
+        else:
+            assert CheckpointSource._gptq_format(d) == ok

@@ -67,3 +67,24 @@ def test_argmax_static_rejects_rows_beyond_its_array():
     rc = f(logits.data_ptr(), 0, MAX_ROWS + 1, 16, 16, out.data_ptr(), None,
            torch.cuda.current_stream().cuda_stream)
     assert rc == ERR_TOO_MANY_ROWS
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("V", [4000, 151552])
+def test_argmax_static_rows_without_a_winner_return_index_zero(V):
+    """A row of all -inf (or NaN) has no element above the starting value: both entry
+    points return index 0, a valid token id, for it."""
+    f = _fn()
+    s = torch.cuda.current_stream().cuda_stream
+    logits = torch.randn(3, V, device="cuda")
+    logits[0] = float("-inf")
+    logits[2] = float("nan")
+    for call in range(2):
+        out = torch.full((3,), -1, dtype=torch.int32, device="cuda")
+        rc = f(logits.data_ptr(), 0, 3, V, V, out.data_ptr(), None, s)
+        assert rc in (1, 2), rc
+        ref_i, _ = _existing(logits, V)
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref_i), call
+        assert out[0].item() == 0 and out[2].item() == 0
+        assert out[1].item() == int(logits[1].argmax())

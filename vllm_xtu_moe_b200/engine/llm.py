@@ -91,10 +91,28 @@ class LLM:
             self.model.attach_tracer(self.tracer)
 
     # ------------------------------------------------------------------
-    def add_request(self, prompt: list[int], params: SamplingParams) -> Request:
+    def check_request(self, prompt: list[int], params: SamplingParams) -> None:
+        """Raise ValueError for a request this engine cannot serve (called by add_request;
+        the server calls it before queueing, so a bad request gets an HTTP 400 and never
+        reaches the engine thread)."""
         if (params.temperature > 0.0 or params.logprobs is not None) and self.spec is not None:
             raise ValueError("speculative decoding verifies greedy drafts; sampled requests and logprobs "
                              "need num_spec=0")
+        if not prompt:
+            raise ValueError("empty prompt")
+        if params.max_tokens < 1:
+            raise ValueError("max_tokens must be at least 1")
+        rc = self.runner.rc
+        n = len(prompt) + params.max_tokens
+        if n > rc.max_model_len:
+            raise ValueError(f"prompt ({len(prompt)} tokens) + max_tokens ({params.max_tokens}) = {n} exceeds "
+                             f"max_model_len ({rc.max_model_len})")
+        vocab = self.model.cfg.vocab_size
+        if min(prompt) < 0 or max(prompt) >= vocab:
+            raise ValueError(f"token ids must lie in [0, {vocab})")
+
+    def add_request(self, prompt: list[int], params: SamplingParams) -> Request:
+        self.check_request(prompt, params)
         r = Request(list(prompt), params)
         r.t_submit = time.perf_counter()
         self.scheduler.add(r)

@@ -58,6 +58,9 @@ class ModelRunner:
             raise ValueError("speculative decoding with pipeline stages is not supported")
         self.device = model.device
         self.cuda = self.device.type == "cuda"
+        if rc.num_spec + 1 > rc.block_size:
+            raise ValueError("num_spec + 1 must fit in one KV block (the block table keeps one block of slack "
+                             "for a step's draft rows past max_model_len)")
         self.max_blocks_per_seq = (rc.max_model_len + rc.block_size - 1) // rc.block_size + 1
         cfg = model.cfg
         has_swa = cfg.sliding_window > 0 and cfg.layer_types is not None and "swa" in cfg.layer_types

@@ -43,7 +43,16 @@ class Scheduler:
         self.running: list[Request] = []
         self.finished: list[Request] = []
 
+    def capacity_tokens(self) -> int:
+        """Most tokens (prompt + output + one step's drafts) one request may ever hold."""
+        return self.blocks.num_blocks * self.blocks.block_size
+
     def add(self, req: Request) -> None:
+        """Queue a request; one that could not fit in the whole KV pool even alone is
+        rejected here (it would otherwise wait forever for blocks)."""
+        need = len(req.prompt) + req.params.max_tokens + self.num_spec + 1
+        if self.blocks.blocks_needed(need) > self.blocks.num_blocks:
+            raise ValueError(f"request needs {need} tokens of KV cache; the pool holds {self.capacity_tokens()}")
         self.waiting.append(req)
 
     def has_work(self) -> bool:
@@ -53,13 +62,17 @@ class Scheduler:
         # 1) prefill chunks (requests already prefilling first, then new ones)
         budget = self.max_batched_tokens
         chunks: list[ScheduledChunk] = []
+        blocked = False          # a request already prefilling could not get its next chunk's blocks
         for r in self.running:
             if r.status == Status.PREFILL and budget > 0:
                 n = min(r.prefill_remaining, budget)
                 if self.blocks.ensure(r, r.num_computed + n):
                     chunks.append(ScheduledChunk(r, r.num_computed, n))
                     budget -= n
-        while self.waiting and budget > 0 and len(self.running) < self.max_seqs:
+                else:
+                    blocked = True
+        # new requests are admitted only while no admitted one is starved of blocks
+        while not blocked and self.waiting and budget > 0 and len(self.running) < self.max_seqs:
             r = self.waiting[0]
             if not self.blocks.acquire_slot(r):
                 break
@@ -79,6 +92,13 @@ class Scheduler:
         # 2) decode
         dec = [r for r in self.running if r.status == Status.DECODE]
         if not dec:
+            pre = [r for r in self.running if r.status == Status.PREFILL]
+            if blocked and len(pre) > 1:
+                # prompts in prefill hold the pool between them and none can go on: the newest
+                # goes back to the queue (its blocks freed, recomputed later); the oldest alone
+                # always fits, since add() rejects requests larger than the pool
+                self._preempt(pre[-1])
+                return self.schedule()
             return None
         out = []
         for r in dec:

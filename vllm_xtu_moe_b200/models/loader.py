@@ -51,6 +51,29 @@ class CheckpointSource:
         self.device = torch.device(device)
         self.fam = _family_names(self.cfg)
         self.used: set[str] = set()
+        self.gptq_bits, self.gptq_zero_offset = self._gptq_format(path)
+
+    @staticmethod
+    def _gptq_format(path) -> tuple[int, int]:
+        """(bits, zero-point offset) from config.json's quantization_config (GPTQ defaults:
+        4 bits, "gptq" format whose packed zero points are stored minus one)."""
+        import json
+        import os
+        qc = {}
+        cj = os.path.join(str(path), "config.json")
+        if os.path.isfile(cj):
+            with open(cj) as fh:
+                qc = json.load(fh).get("quantization_config") or {}
+        method = qc.get("quant_method", "gptq")
+        if method not in ("gptq", "fp8", "mxfp4", "modelopt", "compressed-tensors", None):
+            raise ValueError(f"quantization method {method!r} is not supported")
+        bits = int(qc.get("bits", 4)) if method == "gptq" else 4
+        fmt = qc.get("checkpoint_format", "gptq") if method == "gptq" else "gptq"
+        if fmt not in ("gptq", "gptq_v2"):
+            raise ValueError(f"GPTQ checkpoint format {fmt!r} is not supported (gptq, gptq_v2)")
+        if bits not in (2, 4, 8):
+            raise ValueError(f"GPTQ with {bits}-bit weights is not supported (2, 4 or 8)")
+        return bits, (1 if fmt == "gptq" else 0)
 
     # ------------------------------------------------------------------ name mapping
     def _layer_prefix(self, name: str) -> tuple[str, str]:
@@ -148,13 +171,22 @@ class CheckpointSource:
         """A GPTQ-quantized projection, dequantized to fp32 [out, in]."""
         opt = lambda k: self._get(prefix + k) if (prefix + k) in self.ckpt else None
         return dequant_gptq(self._get(prefix + ".qweight"), self._get(prefix + ".scales"), opt(".qzeros"),
-                            opt(".g_idx"))
+                            opt(".g_idx"), bits=self.gptq_bits, zero_offset=self.gptq_zero_offset)
+
+    def _dense_part(self, prefix: str) -> torch.Tensor:
+        """A non-GPTQ part of a fused projection, as fp32 [out, in] (fp8 parts with their scales)."""
+        w = self._get(prefix + ".weight")
+        if w.dtype == torch.float8_e4m3fn:
+            return dequant_fp8_block(w, self._get(prefix + ".weight_scale_inv").float())
+        return w.float()
 
     def linear(self, name, n, k, fmt="bf16", bias=False, std=None) -> Linear:
         parts = self._hf(name)
         if any((p + ".qweight") in self.ckpt for p in parts):   # GPTQ INT4: dequantized, then this layer's format
-            w = torch.cat([self._gptq(p) if (p + ".qweight") in self.ckpt else self._get(p + ".weight").float()
+            w = torch.cat([self._gptq(p) if (p + ".qweight") in self.ckpt else self._dense_part(p)
                            for p in parts], 0)
+            if tuple(w.shape) != (n, k):
+                raise ValueError(f"{name}: checkpoint shape {tuple(w.shape)} != {(n, k)}")
             b = torch.cat([self._get(p + ".bias") for p in parts], 0) if bias else None
             if fmt == "fp8":
                 q, sc = quant_fp8_block(w)

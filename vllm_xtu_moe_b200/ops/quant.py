@@ -140,15 +140,18 @@ def dequant_nvfp4(packed: torch.Tensor, scales: torch.Tensor, gscale: torch.Tens
 
 
 def dequant_gptq(qweight: torch.Tensor, scales: torch.Tensor, qzeros: torch.Tensor | None = None,
-                 g_idx: torch.Tensor | None = None, bits: int = 4) -> torch.Tensor:
+                 g_idx: torch.Tensor | None = None, bits: int = 4, zero_offset: int = 1) -> torch.Tensor:
     """GPTQ-packed linear weight -> dense fp32 [out, in] (the HF Linear layout).
 
     The AutoGPTQ "gptq" checkpoint format: ``qweight`` int32 [in * bits / 32, out] packs
     32 / bits consecutive input rows per word (lowest bits first); ``scales`` [groups, out];
     ``qzeros`` int32 [groups, out * bits / 32] packs the zero points along the output,
-    stored minus one (absent: symmetric, zero point 2^(bits-1)); ``g_idx`` [in] gives each
+    stored minus one (``zero_offset`` 1; the "gptq_v2" format stores them as they are:
+    ``zero_offset`` 0; absent: symmetric, zero point 2^(bits-1)); ``g_idx`` [in] gives each
     input row's group (absent: row // (in / groups)).  w[k, n] = (q[k, n] - z[g(k), n]) *
-    scales[g(k), n]."""
+    scales[g(k), n].  ``bits`` 2, 4 or 8 (widths that divide the 32-bit word)."""
+    if bits not in (2, 4, 8):
+        raise ValueError(f"GPTQ with {bits}-bit weights is not supported (2, 4 or 8)")
     per = 32 // bits
     mask = (1 << bits) - 1
     qw = qweight.to(torch.int64) & 0xFFFFFFFF
@@ -159,7 +162,7 @@ def dequant_gptq(qweight: torch.Tensor, scales: torch.Tensor, qzeros: torch.Tens
     grp = g_idx.to(torch.int64) if g_idx is not None else torch.arange(K) // (K // G)
     if qzeros is not None:
         qz = qzeros.to(torch.int64) & 0xFFFFFFFF
-        z = ((qz[:, :, None] >> shifts[None, None, :]) & mask).reshape(G, -1)[:, :N] + 1
+        z = ((qz[:, :, None] >> shifts[None, None, :]) & mask).reshape(G, -1)[:, :N] + zero_offset
     else:
         z = torch.full((G, N), 1 << (bits - 1), dtype=torch.int64)
     w = (q - z[grp]).float() * scales.float()[grp]

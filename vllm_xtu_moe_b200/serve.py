@@ -40,6 +40,7 @@ class EngineThread:
         self.streams: dict[int, list] = {}          # rid -> [callback, tokens already sent, request]
         self.metrics = {"requests": 0, "tokens": 0, "steps": 0, "aborted": 0, "ttft_s": 0.0, "e2e_s": 0.0}
         self.aborts: queue.Queue = queue.Queue()
+        self._cancelled: set = set()     # aborted futures whose request was not admitted yet
         self._stop = threading.Event()
         self.error: BaseException | None = None
         self.thread = threading.Thread(target=self._loop, name="xtu-engine", daemon=True)
@@ -75,6 +76,13 @@ class EngineThread:
                         prompt, params, f, cb = self.inbox.get_nowait()
                     except queue.Empty:
                         break
+                    if f in self._cancelled:      # its client went away before admission
+                        self._cancelled.discard(f)
+                        self.metrics["aborted"] += 1
+                        f.cancel()
+                        if cb is not None:
+                            cb([], True)
+                        continue
                     try:
                         r = self.llm.add_request(prompt, params)
                     except ValueError as e:       # a request this engine cannot serve
@@ -89,12 +97,17 @@ class EngineThread:
                         fut = self.aborts.get_nowait()
                     except queue.Empty:
                         break
+                    found = False
                     for rid, (f, _) in list(self.pending.items()):
-                        if f is fut and self.llm.abort(rid):
-                            self.pending.pop(rid)
-                            self.streams.pop(rid, None)
-                            self.metrics["aborted"] += 1
-                            f.cancel()
+                        if f is fut:
+                            found = True
+                            if self.llm.abort(rid):
+                                self.pending.pop(rid)
+                                self.streams.pop(rid, None)
+                                self.metrics["aborted"] += 1
+                                f.cancel()
+                    if not found and not fut.done():
+                        self._cancelled.add(fut)  # still in the inbox: dropped when it is drained
                 if not self.llm.scheduler.has_work():
                     if not admitted:
                         time.sleep(0.001)
@@ -228,6 +241,7 @@ def build_app(engine: EngineThread, model_name: str, codec: TextCodec | None = N
                               logprobs=None if req.logprobs is None else max(0, min(int(req.logprobs), 20)))
 
     async def run(ids: list[int], sp: SamplingParams):
+        check(ids, sp)
         try:
             return await asyncio.wrap_future(engine.submit(ids, sp))
         except ValueError as e:
@@ -241,7 +255,14 @@ def build_app(engine: EngineThread, model_name: str, codec: TextCodec | None = N
                for i in range(n)]
         return await asyncio.gather(*(run(ids, p) for p in sps))
 
+    def check(ids: list[int], sp: SamplingParams) -> None:
+        try:
+            engine.llm.check_request(ids, sp)
+        except ValueError as e:
+            raise HTTPException(400, str(e))
+
     def stream(ids: list[int], sp: SamplingParams, make_chunk):
+        check(ids, sp)
         loop = asyncio.get_running_loop()
         q: asyncio.Queue = asyncio.Queue()
         fut = engine.submit(ids, sp, on_tokens=lambda new, done: loop.call_soon_threadsafe(q.put_nowait, (new, done)))
