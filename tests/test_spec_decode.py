@@ -124,3 +124,32 @@ def test_spec_decode_with_bounded_window_pool_cpu():
         return outs
 
     assert run(2) == run(0)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("k", [1, 4])
+def test_graph_replayed_spec_step_matches_eager_gpu(k):
+    """The CUDA-graph speculative step (verify + MTP + device-side draft chain) gives the
+    tokens of the eager step and of plain greedy decoding (up to split-KV rounding)."""
+    m = build_model(_cfg(), device="cuda", seed=1)
+    prompts = [list(range(3, 40)), list(range(50, 61)), list(range(100, 170))]
+
+    def run(k_, graph):
+        rc = RunnerConfig(block_size=64, max_seqs=4, max_model_len=512, max_batched_tokens=128,
+                          use_cuda_graph=graph, num_spec=k_)
+        llm = LLM(m, device="cuda", runner_config=rc)
+        outs = llm.generate(prompts, SamplingParams(max_tokens=24))
+        gsteps = llm.spec.graph_steps if llm.spec is not None else 0
+        llm.shutdown()
+        return outs, gsteps
+
+    eager, g0 = run(k, False)
+    graph, g1 = run(k, True)
+    plain, _ = run(0, True)
+    assert g0 == 0 and g1 > 0
+    total = sum(len(o.token_ids) for o in plain)
+    assert all(len(o.token_ids) == 24 for o in graph)
+    for other in (eager, plain):
+        same = sum(a == b for x, y in zip(graph, other) for a, b in zip(x.token_ids, y.token_ids))
+        assert same >= 0.9 * total
+    assert sum(o.proposed for o in graph) > 0

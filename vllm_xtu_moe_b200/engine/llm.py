@@ -205,6 +205,8 @@ class LLM:
 
     def shutdown(self):
         self.runner.release_graphs()
+        if self.spec is not None:
+            self.spec.release_graphs()
         if self.tracer is not None:
             self.tracer.close()
         if self.tiering is not None:

@@ -21,6 +21,13 @@ layers).  Here the drafter is the model's own ``MTPLayer`` and the loop is:
 
 Linear-attention (DeltaNet) models are not drafted: their recurrent state would
 need a rollback for rejected drafts.
+
+On a GPU a decode step whose requests all carry k drafts replays one CUDA graph per batch
+bucket: the verification forward, the acceptance kernel, the MTP pass over the verified
+rows and the k - 1 chained draft passes, whose positions, KV slots and lengths a kernel
+derives on the device from the acceptance (``xtu_spec_chain_meta``).  The host copies the
+step's metadata in, replays, and reads back one int32 buffer (target tokens, accepted
+counts, next drafts).
 """
 from __future__ import annotations
 
@@ -65,6 +72,12 @@ class SpecDecoder:
             raise NotImplementedError("MTP drafting with linear-attention layers (no state rollback)")
         self.mtp = self.model.mtp[0]
         self.caches = runner.mtp_caches[0]
+        rc = runner.rc
+        self.use_graph = runner.cuda and rc.use_cuda_graph and not runner.pipeline and k >= 1
+        self.graphs: dict[int, tuple] = {}
+        self._st = None
+        self.graph_steps = 0
+        self.eager_steps = 0
 
     # ------------------------------------------------------------------ MTP passes
     def _mtp(self, tok_ids: torch.Tensor, hidden: torch.Tensor, meta: AttnMetadata) -> torch.Tensor:
@@ -136,9 +149,170 @@ class SpecDecoder:
             r.draft = d
             r.proposed += len(d)
 
+    # ------------------------------------------------------------------ graph-replayed step
+    def _graph_bucket(self, plan) -> int | None:
+        if not self.use_graph:
+            return None
+        k = self.k
+        if any(len(ch.req.draft) != k for ch in plan.chunks):
+            return None
+        n = len(plan.chunks)
+        for b in self.runner.rc.graph_batch_sizes:
+            if n <= b <= self.runner.rc.max_seqs:
+                return b
+        return None
+
+    def _alloc_static(self):
+        rn, k = self.runner, self.k
+        ms = max(b for b in rn.rc.graph_batch_sizes if b <= rn.rc.max_seqs)
+        R = ms * (k + 1)
+        d = rn.device
+        mb = rn.max_blocks_per_seq
+        self._st = dict(
+            ms=ms, ids=torch.zeros(R, dtype=torch.int32, device=d), pos=torch.zeros(R, dtype=torch.int32, device=d),
+            slots=torch.full((R,), -1, dtype=torch.int32, device=d),
+            q_start=torch.arange(0, (ms + 1) * (k + 1), k + 1, dtype=torch.int32, device=d),
+            kv_len=torch.full((ms,), k + 1, dtype=torch.int32, device=d),
+            bt=torch.zeros(ms, mb, dtype=torch.int32, device=d),
+            seq_slots=torch.full((ms,), -1, dtype=torch.int32, device=d),
+            fresh=torch.zeros(ms, dtype=torch.int32, device=d),
+            base=torch.zeros(ms, dtype=torch.int32, device=d),
+            rows=torch.arange(R, dtype=torch.long, device=d),
+            cq=torch.arange(ms + 1, dtype=torch.int32, device=d),
+            cpos=torch.zeros(max(1, k - 1), ms, dtype=torch.int32, device=d),
+            cslot=torch.full((max(1, k - 1), ms), -1, dtype=torch.int32, device=d),
+            ckv=torch.ones(max(1, k - 1), ms, dtype=torch.int32, device=d),
+            # one read-back buffer per bucket: [target rows | accepted | drafts]
+            out={})
+
+    def _graph_body(self, b: int):
+        """The step for a batch bucket of b sequences (runs eagerly to warm up, then captured)."""
+        rn, k, st, m = self.runner, self.k, self._st, self.model
+        R = b * (k + 1)
+        cfg = m.cfg
+        splits = choose_splits(b, max(1, cfg.num_kv_heads), rn.rc.max_model_len,
+                               ctas_per_sm=decode_ctas_per_sm(cfg))
+        meta = AttnMetadata(num_seqs=b, q_start=st["q_start"][:b + 1], kv_len=st["kv_len"][:b],
+                            block_table=st["bt"][:b], slot_mapping=st["slots"][:R], positions=st["pos"][:R],
+                            max_q_len=k + 1, max_kv_len=rn.rc.max_model_len, is_decode=True,
+                            seq_slots=st["seq_slots"][:b], seq_fresh=st["fresh"][:b], num_splits=splits)
+        out = st["out"][b]
+        tgt_o, acc_o, drf_o = out[:R], out[R:R + b], out[R + b:].view(b, k)
+        tgt, h, _, _ = rn.forward(st["ids"][:R], meta, st["rows"][:R])
+        last = torch.empty(b, dtype=torch.int32, device=rn.device)
+        N.call("xtu_spec_verify", tgt.data_ptr(), st["ids"].data_ptr(), meta.q_start.data_ptr(), b, k,
+               acc_o.data_ptr(), last.data_ptr(), N.stream_ptr(rn.device))
+        hid = self._mtp(tgt, h, meta).index_select(0, last.long())
+        tok = B.argmax(m.logits(hid))
+        drf_o[:, 0].copy_(tok)
+        if k > 1:
+            bt = st["bt"]
+            N.call("xtu_spec_chain_meta", st["base"].data_ptr(), acc_o.data_ptr(), bt.data_ptr(), bt.stride(0),
+                   bt.shape[1], rn.rc.block_size, b, k, st["cpos"].data_ptr(), st["cslot"].data_ptr(),
+                   st["ckv"].data_ptr(), N.stream_ptr(rn.device))
+            # cpos / cslot / ckv are [k-1, ms]: pass j's b rows start at (j-1) * b in the flat view
+            cp, cs, ck = (st[n].view(-1) for n in ("cpos", "cslot", "ckv"))
+            csplits = choose_splits(b, max(1, cfg.num_kv_heads), rn.rc.max_model_len,
+                                    ctas_per_sm=decode_ctas_per_sm(cfg))
+            for j in range(1, k):
+                o = (j - 1) * b
+                mj = AttnMetadata(num_seqs=b, q_start=st["cq"][:b + 1], kv_len=ck[o:o + b],
+                                  block_table=bt[:b], slot_mapping=cs[o:o + b], positions=cp[o:o + b], max_q_len=1,
+                                  max_kv_len=rn.rc.max_model_len, is_decode=True, num_splits=csplits)
+                hid = self._mtp(tok, hid, mj)
+                tok = B.argmax(m.logits(hid))
+                drf_o[:, j].copy_(tok)
+        tgt_o.copy_(tgt)
+
+    def _replay(self, plan, b: int):
+        """Fill the bucket's static inputs from the plan, replay its graph (capturing it on
+        first use) and return the host copy of [target rows | accepted | drafts]."""
+        rn, k = self.runner, self.k
+        if self._st is None:
+            self._alloc_static()
+        st = self._st
+        ids, meta = rn.build_meta(plan)
+        n = meta.num_seqs
+        R, Rn = b * (k + 1), n * (k + 1)
+        if b not in st["out"]:
+            st["out"][b] = torch.zeros(R + b + b * k, dtype=torch.int32, device=rn.device)
+        st["ids"][:Rn].copy_(ids)
+        st["pos"][:Rn].copy_(meta.positions)
+        st["slots"][:R].fill_(-1)
+        st["slots"][:Rn].copy_(meta.slot_mapping)
+        st["kv_len"][:b].fill_(k + 1)
+        st["kv_len"][:n].copy_(meta.kv_len)
+        w = meta.block_table.shape[1]
+        st["bt"][:n, :w].copy_(meta.block_table)
+        st["seq_slots"][:b].fill_(-1)
+        st["fresh"][:b].zero_()
+        base = torch.tensor([ch.req.total_len for ch in plan.chunks] + [0] * (b - n), dtype=torch.int32)
+        rn.h2d_bytes += base.numel() * 4
+        st["base"][:b].copy_(base.pin_memory(), non_blocking=True)
+        if b not in self.graphs:
+            for _ in range(2):           # warm-up (allocations happen outside the capture)
+                self._graph_body(b)
+            torch.cuda.synchronize(rn.device)
+            g = torch.cuda.CUDAGraph()
+            n0 = N.launches()
+            with torch.cuda.graph(g):
+                self._graph_body(b)
+            kernels = N.launches() - n0
+            N.add_launches(-kernels)
+            self.graphs[b] = (g, kernels)
+        g, kernels = self.graphs[b]
+        g.replay()
+        N.add_launches(kernels)
+        host = st["out"][b].cpu()
+        rn.d2h_bytes += host.numel() * 4
+        return meta, host
+
+    def release_graphs(self):
+        self.graphs.clear()
+
     @torch.inference_mode()
     def decode_step(self, plan, scheduler) -> list:
+        b = self._graph_bucket(plan)
+        if b is not None:
+            # the chain writes draft KV up to total_len + 2k - 1: hold those blocks first
+            if all(self.blocks.ensure(ch.req, ch.req.total_len + 2 * self.k + 1) for ch in plan.chunks):
+                return self._decode_step_graph(plan, scheduler, b)
+        return self._decode_step_eager(plan, scheduler)
+
+    def _decode_step_graph(self, plan, scheduler, b: int) -> list:
         import time
+        k = self.k
+        meta, host = self._replay(plan, b)
+        self.graph_steps += 1
+        R = b * (k + 1)
+        tgt_h = host[:R].tolist()
+        acc_h = host[R:R + b].tolist()
+        drafts = host[R + b:].view(b, k).tolist()
+        now = time.perf_counter()
+        done = []
+        for i, ch in enumerate(plan.chunks):
+            r = ch.req
+            q0 = meta.q_start_host[i]
+            a = min(acc_h[i], len(r.draft))
+            r.accepted += a
+            for t in tgt_h[q0:q0 + a + 1]:
+                if r.finished():
+                    break
+                r.output.append(int(t))
+            r.num_computed = r.total_len - 1
+            r.draft = []
+            if r.finished():
+                r.t_done = now
+                scheduler.finish(r)
+                done.append(r)
+            else:
+                r.draft = drafts[i]
+                r.proposed += k
+        return done
+
+    def _decode_step_eager(self, plan, scheduler) -> list:
+        import time
+        self.eager_steps += 1
         rn = self.runner
         ids, meta = rn.build_meta(plan)
         n_rows = ids.shape[0]
