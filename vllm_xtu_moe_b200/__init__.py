@@ -11,6 +11,9 @@ Packages:
 __version__ = "0.1.0"
 
 from .config import EngineConfig, get_engine_config  # noqa: F401
+from .utils.diagnostics import install_death_debug as _install_death_debug
+
+_install_death_debug()       # XIAOTU_DEATH_DEBUG=1: signal stack dumps + heartbeat
 
 
 def register():

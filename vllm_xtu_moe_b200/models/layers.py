@@ -177,6 +177,8 @@ class MoEBlock:
         self.tracer = None                # utils.trace.Tracer (routing dump) when enabled
         self.trace_idx = layer_idx
         self.expert_lo = 0                # first global expert id held here (expert parallel over TP ranks)
+        from ..utils.diagnostics import selfcheck_enabled
+        self.selfcheck_pending = selfcheck_enabled()   # XIAOTU_MOE_SELFCHECK: verify one real call
 
     def route(self, x: torch.Tensor):
         logits = G.linear(x, self.gate, out_dtype=torch.float32)
@@ -185,6 +187,10 @@ class MoEBlock:
                            c.routed_scale)
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        if self.selfcheck_pending and x.shape[0] <= 64:
+            y = self._checked_call(x)
+            if y is not None:
+                return y
         c = self.cfg
         permuted = False
         if self.executor is None and M.decode_route_ok(x, self.gate, self.experts, c.top_k, c.n_group):
@@ -215,6 +221,31 @@ class MoEBlock:
             return self.executor(self, x, ids, w, sh)
         return M.fused_moe(x, ids, w, self.experts, self.workspace(x), lo=self.expert_lo, shared=sh,
                            act_limit=self.cfg.swiglu_limit, permuted=permuted)
+
+    def _checked_call(self, x: torch.Tensor) -> torch.Tensor | None:
+        """XIAOTU_MOE_SELFCHECK: this call's routed experts once more on the plain path (no
+        shared expert), compared with an fp32 recomputation from the layer's own weights
+        (utils.diagnostics.moe_selfcheck); returns the layer output, or None when the call
+        does not qualify (then the normal path runs)."""
+        from ..utils import diagnostics as D
+        if x.is_cuda and torch.cuda.is_current_stream_capturing():
+            return None
+        ids, w = self.route(x)
+        if self.executor is not None:
+            routed = self.executor(self, x, ids, w, None)
+        else:
+            routed = M.fused_moe(x.contiguous(), ids.to(torch.int32).contiguous(), w.float().contiguous(),
+                                 self.experts, self.workspace(x), lo=self.expert_lo, act_limit=self.cfg.swiglu_limit)
+        if D.moe_selfcheck(self, x, ids, w, routed) is None:
+            return None
+        self.selfcheck_pending = False
+        self.last_ids = ids
+        if self.shared is None:
+            return routed
+        sh = self.shared(x)
+        if self.shared_gate is not None:
+            sh = (sh.float() * torch.sigmoid(G.linear(x, self.shared_gate, out_dtype=torch.float32))).to(x.dtype)
+        return (routed.float() + sh.float()).to(x.dtype)
 
     def workspace(self, x: torch.Tensor) -> M.MoEWorkspace | None:
         if not x.is_cuda:

@@ -35,7 +35,7 @@ import torch
 from ..config import EngineConfig, get_engine_config, parse_layer_list
 from ..ops import moe as M
 from .cpu_engine import AsyncCpuBridge, CpuBridge, CpuExpertEngine
-from .host import HostExperts
+from .host import HostExperts, alloc_expert_slots
 from .policy import load_pin_table
 from .pool import LayerPool
 from .ring import ExpertRing
@@ -94,6 +94,13 @@ class LayerExecutor:
         main.wait_stream(o.side)
         ws = o.pool_workspace(T, ids.shape[1], 1, x.device)
         return M.moe_combine(ws, ids, 0, 0, shared=sh, extra=extra)
+
+    def reference_experts(self, block):
+        """The host tier's experts as a dequantizable view (the in-service self-check's
+        oracle): expert e is copied from the engine's shards into a one-expert GPU slot."""
+        if self.host is None:
+            return None
+        return _HostExpertView(self.host, self.engine.E)
 
     def _cpu_deferred(self, y: torch.Tensor, T: int) -> torch.Tensor:
         """Host-tensor form of expert deferral (the oracle of the device path): returns the
@@ -160,6 +167,21 @@ class LayerExecutor:
             with torch.cuda.stream(o.side):
                 y = self.engine.forward(x.cpu(), ids.cpu(), w.cpu())
                 extra.copy_(y, non_blocking=False)
+
+
+class _HostExpertView:
+    """``num_experts`` + ``dequant(e)`` over a HostExperts (what ops.moe.moe_ref reads)."""
+
+    def __init__(self, host: HostExperts, num_experts: int):
+        self.host, self.num_experts = host, num_experts
+
+    def dequant(self, e: int):
+        h = self.host
+        slot = alloc_expert_slots(h.fmt, 1, h.H, h.I, torch.device("cuda", torch.cuda.current_device()))
+        st = torch.cuda.current_stream()
+        h.copy_slot(e, slot, 0, st)
+        st.synchronize()
+        return slot.dequant(0)
 
 
 class TieredExperts:
