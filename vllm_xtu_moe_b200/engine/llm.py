@@ -134,8 +134,11 @@ class LLM:
         try:
             return self._step(plan)
         finally:
-            if self.tracer is not None and self.tracer.profiler is not None:
-                self.tracer.profiler.after_step()
+            if self.tracer is not None:
+                if self.tracer.profiler is not None:
+                    self.tracer.profiler.after_step()
+                if self.tracer.routing is not None:
+                    self.tracer.routing.end_step()
 
     def _step(self, plan) -> list[Request]:
         t0 = time.perf_counter()

@@ -27,11 +27,41 @@ from ..config import get_engine_config
 
 
 class RoutingDump:
-    def __init__(self, path: str, num_layers: int, num_experts: int, device):
+    """Device routing counters plus per-window deltas: every ``window`` engine steps
+    (``XIAOTU_ROUTING_DUMP_WINDOW``, default 16) ``end_step`` keeps the counts added since
+    the last window (a device-side copy, no read-back), so the PIN tooling can evaluate a
+    table on windows it was not built from (``tiering.pin_tools``).  Past ``max_windows``
+    adjacent windows are merged pairwise, which keeps memory bounded on long runs."""
+
+    def __init__(self, path: str, num_layers: int, num_experts: int, device, window: int | None = None,
+                 max_windows: int = 4096):
         self.path = path
         self.E = num_experts
         self.counts = torch.zeros(num_layers, num_experts, dtype=torch.int64, device=device)
         self._ones = {}
+        self.window = window if window is not None else max(1, int(os.environ.get("XIAOTU_ROUTING_DUMP_WINDOW",
+                                                                                 "16")))
+        self.max_windows = max_windows
+        self._steps = 0
+        self._cut_at = 0
+        self._last = torch.zeros_like(self.counts)
+        self.windows: list[torch.Tensor] = []
+
+    def end_step(self) -> None:
+        self._steps += 1
+        if self._steps % self.window:
+            return
+        self._cut()
+
+    def _cut(self) -> None:
+        if self._steps == self._cut_at:        # nothing recorded since the last window
+            return
+        self._cut_at = self._steps
+        self.windows.append(self.counts - self._last)
+        self._last = self.counts.clone()
+        if len(self.windows) > self.max_windows:
+            w = self.windows
+            self.windows = [w[i] + w[i + 1] if i + 1 < len(w) else w[i] for i in range(0, len(w), 2)]
 
     def record(self, layer: int, ids: torch.Tensor) -> None:
         flat = ids.reshape(-1).long()
@@ -43,8 +73,14 @@ class RoutingDump:
         self.counts[layer].index_add_(0, flat.clamp_(0, self.E - 1), ones)
 
     def flush(self) -> str:
+        self._cut()
         c = self.counts.cpu().tolist()
-        data = {"experts": self.E, "counts": {str(l): row for l, row in enumerate(c) if any(row)}}
+        wins = []
+        for w in self.windows:
+            rows = w.cpu().tolist()
+            wins.append({str(l): row for l, row in enumerate(rows) if any(row)})
+        data = {"experts": self.E, "counts": {str(l): row for l, row in enumerate(c) if any(row)},
+                "window_steps": self.window, "windows": [w for w in wins if w]}
         Path(self.path).write_text(json.dumps(data))
         return self.path
 
@@ -52,6 +88,12 @@ class RoutingDump:
 def load_dump(path: str) -> tuple[int, dict[int, list[int]]]:
     d = json.loads(Path(path).read_text())
     return d["experts"], {int(k): v for k, v in d["counts"].items()}
+
+
+def load_windows(path: str) -> list[dict[int, list[int]]]:
+    """The dump's per-window count deltas (layer -> per-expert counts), oldest first."""
+    d = json.loads(Path(path).read_text())
+    return [{int(k): v for k, v in w.items()} for w in d.get("windows", [])]
 
 
 def to_xtup(dump_path: str, out_path: str, per_layer: int) -> dict:
