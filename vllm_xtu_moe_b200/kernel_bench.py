@@ -109,6 +109,78 @@ def bench_moe(T: int, fmt: str, E=128, H=4096, I=1408, K=8, iters=10) -> dict:
                    dict(T=T, E=E, H=H, I=I, K=K, active_experts=active), ms, nbytes, flops)
 
 
+_REF_ROOT = Path(__file__).resolve().parent.parent / "baseline" / "_ref"
+
+
+def load_reference_module(name: str):
+    """A module of the reference plugin, unmodified, from its install in baseline/_ref.
+
+    The plugin package's ``__init__`` (which patches a vLLM tree that is not installed
+    here) is not executed: an empty package object stands in for it, so the reference's
+    kernel modules (plain torch + Triton) import exactly as written."""
+    import importlib
+    import sys
+    import types
+    pkg = "vllm_xiaotu_moe"
+    root = _REF_ROOT / pkg
+    if not root.is_dir():
+        raise FileNotFoundError(f"{root} missing: install the reference into baseline/_ref")
+    if pkg not in sys.modules or not hasattr(sys.modules[pkg], "__path__"):
+        m = types.ModuleType(pkg)
+        m.__path__ = [str(root)]
+        sys.modules[pkg] = m
+    return importlib.import_module(f"{pkg}.{name}")
+
+
+def bench_moe_vs_reference(T: int, E=128, H=4096, I=1408, K=8, iters=10) -> dict:
+    """One fp8-128 MoE layer (GLM-4.5-Air shape) through this library's kernels and through
+    the reference's own Triton kernels on the same GPU, weights and routes: the prefill
+    entry ``gpu_moe_layer_fp8`` (vllm_xiaotu_moe/gpu_prefill_fp8.py:458) or, at decode
+    sizes, ``gpu_moe_decode_fp8`` (vllm_xiaotu_moe/decode_moe_fp8.py:103)."""
+    g = torch.Generator(device="cuda").manual_seed(0)
+    w13 = torch.randn(E, 2 * I, H, device="cuda", generator=g) * 0.02
+    w2 = torch.randn(E, H, I, device="cuda", generator=g) * 0.02
+    q13, s13 = quant_fp8_block(w13)
+    q2, s2 = quant_fp8_block(w2)
+    del w13, w2
+    ex = M.prepare_experts("fp8", q13, q2, s13, s2)
+    # the reference's K-major layout: w13t [E, H, 2I], s13t [E, H/128, 2I/128]; w2t [E, I, H]
+    w13t = q13.view(torch.uint8).transpose(1, 2).contiguous()
+    s13t = s13.transpose(1, 2).contiguous()
+    w2t = q2.view(torch.uint8).transpose(1, 2).contiguous()
+    s2t = s2.transpose(1, 2).contiguous()
+    del q13, q2
+    torch.cuda.empty_cache()
+    ids, w = _routes(T, E, K)
+    x = (torch.randn(T, H, device="cuda", generator=g) * 0.5).to(torch.bfloat16)
+    ws = M.MoEWorkspace(T, K, E, H, I, x.device)
+    out = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+    ours = lambda: M.fused_moe(x, ids, w, ex, ws, out=out)
+    decode = T <= 32
+    if decode:
+        ref_mod = load_reference_module("decode_moe_fp8")
+        ref = lambda: ref_mod.gpu_moe_decode_fp8(x, ids, w, w13t, s13t, w2t, s2t, H, I, K, device=x.device)
+        entry = "decode_moe_fp8.gpu_moe_decode_fp8"
+    else:
+        ref_mod = load_reference_module("gpu_prefill_fp8")
+        ref = lambda: ref_mod.gpu_moe_layer_fp8(x, ids, w, w13t, s13t, w2t, s2t, H, I, K, device=x.device)
+        entry = "gpu_prefill_fp8.gpu_moe_layer_fp8"
+    ours()
+    y_ref = ref().float()
+    torch.cuda.synchronize()
+    rel = float((out.float() - y_ref).norm() / y_ref.norm().clamp_min(1e-12))
+    ms_ours = time_fn(ours, iters)
+    ms_ref = time_fn(ref, iters)
+    active = torch.unique(ids).numel()
+    nbytes = 3 * H * I * active + T * H * 2 * 2 + T * K * H * 2 * 3
+    flops = 2 * T * K * 3 * H * I
+    r = _report(f"moe_{'decode' if decode else 'prefill'}_fp8_vs_reference",
+                dict(T=T, E=E, H=H, I=I, K=K, active_experts=active), ms_ours, nbytes, flops)
+    r.update({"reference_entry": entry, "reference_ms": round(ms_ref, 4),
+              "speedup_vs_reference": round(ms_ref / ms_ours, 2), "rel_err_vs_reference": round(rel, 5)})
+    return r
+
+
 def bench_gemv(N: int, Kd: int, M_: int, fmt: str, iters=20) -> dict:
     w = torch.randn(N, Kd, device="cuda") * 0.02
     if fmt == "fp8":
@@ -408,6 +480,7 @@ OPS = {
     "deltanet_prefill": lambda a: bench_deltanet(),
     "kda_prefill": lambda a: bench_kda(),
     "cpu_bridge": lambda a: bench_cpu_bridge(),
+    "moe_vs_reference": lambda a: [bench_moe_vs_reference(t) for t in a.sizes],
 }
 
 
@@ -415,10 +488,17 @@ def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--op", default="all", choices=["all"] + list(OPS))
     ap.add_argument("--tokens", type=int, default=8192)
+    ap.add_argument("--sizes", default="1,4,16,512,2048,8192",
+                    help="token counts of the moe_vs_reference sweep")
     a = ap.parse_args(argv)
+    a.sizes = [int(t) for t in a.sizes.split(",")]
     torch.manual_seed(0)
     for name in (OPS if a.op == "all" else [a.op]):
-        print(json.dumps(OPS[name](a)), flush=True)
+        if a.op == "all" and name == "moe_vs_reference" and not _REF_ROOT.is_dir():
+            continue
+        r = OPS[name](a)
+        for line in (r if isinstance(r, list) else [r]):
+            print(json.dumps(line), flush=True)
         torch.cuda.empty_cache()
 
 
