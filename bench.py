@@ -298,6 +298,20 @@ def main():
                              "mtp_accept_rate": round(acc / prop, 4) if prop else None}
             log(f"sweep C={c}: {sweep[str(c)]}")
 
+    # ---- the same C with plain decoding (no drafts), for the cost of the MTP verification
+    mtp_off = None
+    if k > 0 and not args.no_sweep:
+        llm.set_speculation(0)
+        a, b, s, _, _ = one_round(C)
+        v = torch.tensor([a, b, float(s)], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(v, op=dist.ReduceOp.MAX)
+        a, b, s = v.tolist()
+        mtp_off = {"decode_tok_s": round(C * (O - 1) / (b / 1e3), 2), "decode_step_ms": round(b / max(1.0, s), 3),
+                   "prefill_tok_s": round(C * P / (a / 1e3), 1)}
+        log(f"C={C} without drafts: {mtp_off}")
+        llm.set_speculation(k)
+
     # ---- e2e through the public API (host clock, includes H2D of prompts and D2H of tokens)
     e2e = None
     deg = None
@@ -351,6 +365,7 @@ def main():
             "mtp_accept_rate": round(acc_t / prop_t, 4) if prop_t else None,
             "tokens_per_decode_step": round(C * (O - 1) / max(1.0, avg_dsteps), 3),
             "by_concurrency": sweep,
+            "mtp_off": mtp_off,
             "config": {"model": cfg.name + " (GLM-4.5-Air-style, BASELINE config 4)", "global_batch": C,
                        "concurrency": C, "concurrency_per_gpu": C / world, "seq_len": P, "output_len": O,
                        "parallelism": (f"tp{world}+ep{world}" if world > 1 else "single GPU (tp1, ep1)"),

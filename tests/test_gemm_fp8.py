@@ -1,0 +1,147 @@
+"""Native fp8 tcgen05 GEMM (kind::f8f6f4, per-128 block-scale promotion) against a PyTorch
+fp32 restatement of the same op: activations quantized per (row, 128 columns), weights
+e4m3 with 128x128 fp32 block scales."""
+import pytest
+import torch
+
+from vllm_xtu_moe_b200.ops import gemm as G
+from vllm_xtu_moe_b200.ops import moe as M
+from vllm_xtu_moe_b200.ops.quant import dequant_fp8_block, quant_fp8_block
+
+
+def _rel(out, ref):
+    out, ref = out.float().cpu(), ref.float().cpu()
+    return ((out - ref).norm() / ref.norm().clamp_min(1e-12)).item()
+
+
+def _segments(counts):
+    seg = [0]
+    for c in counts:
+        seg.append(seg[-1] + c)
+    return torch.tensor(seg, dtype=torch.int32)
+
+
+def test_quant_rows_cpu_roundtrip():
+    torch.manual_seed(0)
+    x = (torch.randn(5, 512) * torch.logspace(-3, 2, 512)).to(torch.bfloat16)
+    x[2, :128] = 0
+    q, s = G.quant_fp8_rows(x)
+    assert q.dtype == torch.float8_e4m3fn and s.shape == (5, 4)
+    assert s[2, 0].item() == 1.0 and q[2, :128].float().abs().max().item() == 0.0
+    d = G.dequant_fp8_rows(q, s)
+    # e4m3 keeps 3 mantissa bits: every element within 1/16 of its block's max
+    blk = x.float().view(5, 4, 128).abs().amax(-1, keepdim=True)
+    assert ((d - x.float()).view(5, 4, 128).abs() <= blk / 16 + 1e-12).all()
+
+
+@pytest.mark.gpu
+def test_quant_rows_gpu_matches_cpu():
+    torch.manual_seed(1)
+    x = (torch.randn(37, 1024) * 3).to(torch.bfloat16)
+    qg, sg = G.quant_fp8_rows(x.cuda())
+    qc, sc = G.quant_fp8_rows(x)
+    torch.cuda.synchronize()
+    assert torch.equal(sg.cpu(), sc)
+    diff = (qg.cpu().view(torch.uint8) != qc.view(torch.uint8)).float().mean().item()
+    assert diff < 1e-3
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M_,N_,K", [(17, 256, 128), (300, 4096, 4096), (1000, 14336, 4096), (129, 384, 1408)])
+@pytest.mark.parametrize("bias", [False, True])
+def test_dense_fp8_native_matches_reference(M_, N_, K, bias):
+    torch.manual_seed(2)
+    x = torch.randn(M_, K, device="cuda").to(torch.bfloat16)
+    w = torch.randn(N_, K, device="cuda") / K ** 0.5
+    q, s = quant_fp8_block(w)
+    b = (torch.randn(N_, device="cuda") * 0.1).to(torch.bfloat16) if bias else None
+    xq, xs = G.quant_fp8_rows(x)
+    y = G.gemm_fp8_native(xq, xs, q, s, epilogue=G.EPI_F32, bias=b)
+    torch.cuda.synchronize()
+    G.N.check_status()
+    ref = G.dequant_fp8_rows(xq, xs) @ dequant_fp8_block(q, s).t()
+    if b is not None:
+        ref = ref + b.float()
+    assert _rel(y, ref) < 1e-4
+    # through G.linear (the model's entry point) in W8A8 mode: quantizes internally, bf16 out
+    G.FP8_MMA = True
+    try:
+        y2 = G.linear(x, q, s, bias=b)
+    finally:
+        G.FP8_MMA = False
+    torch.cuda.synchronize()
+    assert _rel(y2, ref) < 1e-2
+    assert _rel(y2, x.float() @ dequant_fp8_block(q, s).t() + (b.float() if b is not None else 0)) < 5e-2
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("counts", [[70, 0, 129, 3], [1, 1, 1, 1], [300, 5, 0, 700]])
+def test_grouped_fp8_swiglu_q8_then_down(counts):
+    torch.manual_seed(3)
+    E, H, I = len(counts), 512, 384
+    seg = _segments(counts).cuda()
+    Mr = int(seg[-1])
+    a = torch.randn(Mr, H, device="cuda").to(torch.bfloat16)
+    w13 = torch.randn(E, 2 * I, H, device="cuda") / H ** 0.5
+    w2 = torch.randn(E, H, I, device="cuda") / I ** 0.5
+    q13, s13 = quant_fp8_block(w13)
+    q2, s2 = quant_fp8_block(w2)
+    q13i = G.interleave_gate_up(q13.view(torch.uint8)).view(torch.float8_e4m3fn)
+    s13i = G.interleave_gate_up_scale(s13)
+    scale = torch.rand(Mr, device="cuda")
+    dest = torch.randperm(Mr, device="cuda").int()
+    aq, as_ = G.quant_fp8_rows(a)
+    tiles = G.build_mtiles(seg, Mr)
+    h16 = G.gemm_fp8_native(aq, as_, q13i, s13i, tiles=tiles, epilogue=G.EPI_SWIGLU, act_limit=10.0)
+    hq, hs = G.gemm_fp8_native(aq, as_, q13i, s13i, tiles=tiles, epilogue=G.EPI_SWIGLU_Q8, act_limit=10.0)
+    out = G.gemm_fp8_native(hq, hs, q2, s2, tiles=tiles, epilogue=G.EPI_F32, row_scale=scale, row_dest=dest)
+    torch.cuda.synchronize()
+    G.N.check_status()
+    ad = G.dequant_fp8_rows(aq, as_).cpu()
+    segc = seg.cpu().tolist()
+    ref_h = torch.zeros(Mr, I)
+    for e in range(E):
+        s0, s1 = segc[e], segc[e + 1]
+        if s1 == s0:
+            continue
+        y = ad[s0:s1] @ dequant_fp8_block(q13[e], s13[e]).cpu().t()
+        ref_h[s0:s1] = G.silu_and_mul_clamped(y[:, :I], y[:, I:], 10.0)
+    assert _rel(h16, ref_h) < 5e-3
+    hd = G.dequant_fp8_rows(hq, hs).cpu()
+    assert _rel(hd, ref_h) < 5e-2                      # e4m3 rounding of h
+    ref = torch.zeros(Mr, H)
+    for e in range(E):
+        s0, s1 = segc[e], segc[e + 1]
+        if s1 == s0:
+            continue
+        o = hd[s0:s1] @ dequant_fp8_block(q2[e], s2[e]).cpu().t() * scale[s0:s1].cpu()[:, None]
+        ref[dest[s0:s1].long().cpu()] = o
+    assert _rel(out, ref) < 1e-4
+
+
+@pytest.fixture
+def w8a8(monkeypatch):
+    monkeypatch.setattr(G, "FP8_MMA", True)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("T", [64, 2048])
+def test_fused_moe_fp8_native_matches_reference(T, w8a8):
+    """GLM-4.5-Air-shaped layer: the native fp8 path against the bf16-activation oracle."""
+    torch.manual_seed(4)
+    E, H, I, K = 32, 4096, 1408, 8
+    w13 = torch.randn(E, 2 * I, H, device="cuda") * 0.02
+    w2 = torch.randn(E, H, I, device="cuda") * 0.02
+    q13, s13 = quant_fp8_block(w13)
+    q2, s2 = quant_fp8_block(w2)
+    del w13, w2
+    ex = M.prepare_experts("fp8", q13, q2, s13, s2)
+    x = torch.randn(T, H, device="cuda").to(torch.bfloat16)
+    logits = torch.randn(T, E, device="cuda")
+    w, ids = torch.softmax(logits, -1).topk(K, dim=-1)
+    ids, w = ids.int().contiguous(), (w / w.sum(-1, keepdim=True)).float().contiguous()
+    y = M.fused_moe(x, ids, w, ex)
+    torch.cuda.synchronize()
+    G.N.check_status()
+    ref = M.moe_ref(x, ids, w, ex)
+    assert _rel(y, ref) < 3e-2

@@ -153,3 +153,21 @@ def test_graph_replayed_spec_step_matches_eager_gpu(k):
         same = sum(a == b for x, y in zip(graph, other) for a, b in zip(x.token_ids, y.token_ids))
         assert same >= 0.9 * total
     assert sum(o.proposed for o in graph) > 0
+
+
+def test_set_speculation_switches_between_requests_cpu():
+    m = build_model(_cfg(), device="cpu", seed=1)
+    m.act_dtype = torch.float32
+    prompts = [list(range(3, 40)), list(range(50, 61))]
+    base, _ = _run(m, 0, prompts, 10)
+    rc = RunnerConfig(block_size=64, max_seqs=4, max_model_len=512, max_batched_tokens=128, use_cuda_graph=False,
+                      num_spec=3)
+    llm = LLM(m, device="cpu", runner_config=rc)
+    for k in (0, 2, 3, 0):
+        llm.set_speculation(k)
+        outs = llm.generate(prompts, SamplingParams(max_tokens=10))
+        assert [o.token_ids for o in outs] == [o.token_ids for o in base], k
+        assert all((o.proposed > 0) == (k > 0) for o in outs)
+    with pytest.raises(ValueError):
+        llm.set_speculation(4)
+    llm.shutdown()

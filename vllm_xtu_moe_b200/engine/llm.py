@@ -79,6 +79,7 @@ class LLM:
                                    window=cfg_m.sliding_window, prefix_caching=rc.prefix_caching)
         self.scheduler = Scheduler(self.blocks, rc.max_batched_tokens, rc.max_seqs, rc.num_spec)
         self.spec = None
+        self.max_spec = rc.num_spec
         if rc.num_spec > 0 and self.model.mtp:
             from .spec_decode import SpecDecoder
             self.spec = SpecDecoder(self.runner, rc.num_spec, self.blocks)
@@ -89,6 +90,26 @@ class LLM:
             from ..utils.trace import Tracer
             self.tracer = Tracer(self.model, ec)
             self.model.attach_tracer(self.tracer)
+
+    # ------------------------------------------------------------------
+    def set_speculation(self, k: int) -> None:
+        """Change the MTP draft count between requests (0 = plain decoding), up to the
+        ``num_spec`` the runner was built with (its block reservations and workspaces are
+        sized for that); only while no request is in flight."""
+        if self.scheduler.has_work():
+            raise RuntimeError("set_speculation while requests are in flight")
+        if k < 0 or k > self.max_spec:
+            raise ValueError(f"k must lie in [0, {self.max_spec}]")
+        if k > 0 and not self.model.mtp:
+            raise ValueError("speculative decoding needs a model with an MTP layer")
+        if self.spec is not None:
+            self.spec.release_graphs()
+        self.runner.rc.num_spec = k
+        self.scheduler.num_spec = k
+        self.spec = None
+        if k > 0:
+            from .spec_decode import SpecDecoder
+            self.spec = SpecDecoder(self.runner, k, self.blocks)
 
     # ------------------------------------------------------------------
     def check_request(self, prompt: list[int], params: SamplingParams) -> None:

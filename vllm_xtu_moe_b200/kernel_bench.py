@@ -181,6 +181,34 @@ def bench_moe_vs_reference(T: int, E=128, H=4096, I=1408, K=8, iters=10) -> dict
     return r
 
 
+def bench_moe_w8a8(T: int, E=128, H=4096, I=1408, K=8, iters=10) -> dict:
+    """The fp8 MoE layer in W8A8 mode (XTU_FP8_MMA=1: activations quantized per (row, 128),
+    kind::f8f6f4 MMAs with per-128 block-scale promotion), beside the default bf16-activation
+    path on the same weights and routes; reports both and the relative difference."""
+    ex = _experts(E, H, I, "fp8")
+    ids, w = _routes(T, E, K)
+    x = (torch.randn(T, H, device="cuda") * 0.5).to(torch.bfloat16)
+    ws = M.MoEWorkspace(T, K, E, H, I, x.device)
+    out = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+    fn = lambda: M.fused_moe(x, ids, w, ex, ws, out=out)
+    ms_bf16 = time_fn(fn, iters)
+    ref = out.float().clone()
+    G.FP8_MMA = True
+    try:
+        ms = time_fn(fn, iters)
+        fn()
+        torch.cuda.synchronize()
+    finally:
+        G.FP8_MMA = False
+    rel = float((out.float() - ref).norm() / ref.norm())
+    active = torch.unique(ids).numel()
+    r = _report("moe_prefill_fp8_w8a8", dict(T=T, E=E, H=H, I=I, K=K, active_experts=active), ms,
+                3 * H * I * active + T * H * 2 * 2 + T * K * H * 2, 2 * T * K * 3 * H * I)
+    r.update({"bf16_activation_ms": round(ms_bf16, 4), "speedup_vs_bf16_activations": round(ms_bf16 / ms, 2),
+              "rel_diff_vs_bf16_activations": round(rel, 4)})
+    return r
+
+
 def bench_gemv(N: int, Kd: int, M_: int, fmt: str, iters=20) -> dict:
     w = torch.randn(N, Kd, device="cuda") * 0.02
     if fmt == "fp8":
@@ -481,6 +509,7 @@ OPS = {
     "kda_prefill": lambda a: bench_kda(),
     "cpu_bridge": lambda a: bench_cpu_bridge(),
     "moe_vs_reference": lambda a: [bench_moe_vs_reference(t) for t in a.sizes],
+    "moe_w8a8": lambda a: [bench_moe_w8a8(t) for t in a.sizes if t > G.GEMV_MAX_M],
 }
 
 

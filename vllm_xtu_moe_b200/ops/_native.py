@@ -50,6 +50,9 @@ _SIGS: dict[str, list] = {
     "xtu_embed_host": [P, P, c_int, c_int, c_int, P, P, P],
     "xtu_route_split": [P, c_int, c_int, c_int, P, P, P, P, P],
     "xtu_spec_verify": [P, P, P, c_int, c_int, P, P, P],
+    "xtu_quant_fp8_rows": [P, c_int, c_int, c_int, P, P, P],
+    "xtu_gemm_fp8_native": [P, P, P, P, P, c_int, P, c_int, c_int, c_int, c_int, c_int, P, P, c_int, c_int, P, P, P,
+                            c_float, c_float, c_float, P, c_int, P, P],
     "xtu_spec_chain_meta": [P, P, P, c_int, c_int, c_int, c_int, c_int, P, P, P, P],
     "xtu_deltanet_fwd": [P, c_int, c_int, c_int, P, P, P, c_int, c_int, c_int, c_int, c_int, P, P, P, P, P,
                          P, P, P, P, c_int, c_int, P],

@@ -137,11 +137,104 @@ def linear(x: torch.Tensor, weight: torch.Tensor, scale: torch.Tensor | None = N
         return y.reshape(*shp[:-1], weight.shape[0])
     if scale is None:
         y = gemm_bf16(x2, weight, out_dtype=out_dtype)
+    elif (x2.is_cuda and x2.dtype == torch.bfloat16 and fp8_native_ok(x2.shape[0], weight.shape[0], K)
+          and out_dtype in (torch.bfloat16, torch.float32)):
+        xq, xs = quant_fp8_rows(x2)
+        y = gemm_fp8_native(xq, xs, weight, scale, epilogue=EPI_F32 if out_dtype == torch.float32 else EPI_BF16,
+                            bias=bias if bias is not None and bias.dtype == torch.bfloat16 else None)
+        if bias is not None and bias.dtype != torch.bfloat16:
+            y.add_(bias)
+        return y.reshape(*shp[:-1], weight.shape[0])
     else:
         y = gemm_fp8w(x2, weight, scale, out_dtype=out_dtype)
     if bias is not None:
         y.add_(bias)
     return y.reshape(*shp[:-1], weight.shape[0])
+
+
+# ---------------------------------------------------------------------------
+# native fp8 (kind::f8f6f4): activations quantized per (row, 128 columns)
+# ---------------------------------------------------------------------------
+import os as _os
+
+# XTU_FP8_MMA=1 ("W8A8" mode): fp8-weight GEMMs of more than GEMV_MAX_M rows quantize their
+# activations to e4m3 per (row, 128 columns) and run on the kind::f8f6f4 tensor cores.  Off by
+# default: quantizing activations moves an MoE layer's output by ~4% (relative, measured on
+# GLM-4.5-Air shapes) from the bf16-activation result, so the default keeps bf16 activations
+# (weights widened to bf16 on chip) and the numerics of a bf16 compute path.
+FP8_MMA = _os.environ.get("XTU_FP8_MMA", "0") == "1"
+EPI_SWIGLU_Q8 = 3
+
+
+def quant_fp8_rows(x: torch.Tensor, out: torch.Tensor | None = None, scale: torch.Tensor | None = None):
+    """bf16 [M, K] -> (e4m3 [M, K], fp32 scales [M, K/128]): per (row, 128-column block)
+    scale = amax / 448, value = x / scale rounded to nearest e4m3 (saturating)."""
+    M, K = x.shape
+    assert K % 128 == 0
+    if out is None:
+        out = torch.empty(M, K, dtype=torch.float8_e4m3fn, device=x.device)
+    if scale is None:
+        scale = torch.empty(M, K // 128, dtype=torch.float32, device=x.device)
+    if not x.is_cuda:
+        xb = x.float().view(M, K // 128, 128)
+        am = xb.abs().amax(-1)
+        sc = torch.where(am > 0, am / 448.0, torch.ones_like(am))
+        inv = torch.where(am > 0, 448.0 / am, torch.zeros_like(am))
+        q = (xb * inv[..., None]).clamp(-448, 448).to(torch.float8_e4m3fn).view(M, K)
+        out.copy_(q)
+        scale.copy_(sc)
+        return out, scale
+    assert x.dtype == torch.bfloat16 and x.stride(1) == 1 and x.stride(0) % 4 == 0
+    N.call("xtu_quant_fp8_rows", x.data_ptr(), M, K, x.stride(0), out.data_ptr(), scale.data_ptr(),
+           N.stream_ptr(x.device))
+    return out, scale
+
+
+def dequant_fp8_rows(q: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
+    M, K = q.shape
+    return (q.float().view(M, K // 128, 128) * scale.float()[..., None]).view(M, K)
+
+
+def fp8_native_ok(M: int, N_out: int, K: int, swiglu: bool = False) -> bool:
+    return FP8_MMA and M > GEMV_MAX_M and K % 128 == 0 and (N_out % 256 == 0 if swiglu else N_out % 16 == 0)
+
+
+def gemm_fp8_native(aq: torch.Tensor, a_scale: torch.Tensor, w8: torch.Tensor, w_scale: torch.Tensor, *,
+                    seg: torch.Tensor | None = None, tiles=None, epilogue: int = 0,
+                    out: torch.Tensor | None = None, out_scale: torch.Tensor | None = None,
+                    row_scale: torch.Tensor | None = None, row_dest: torch.Tensor | None = None,
+                    out_rows: int | None = None, bias: torch.Tensor | None = None, act_limit: float = 0.0,
+                    act_alpha: float = 1.0, act_beta: float = 0.0, peer_out=None, peer_rows: int = 0):
+    """e4m3 activations (+ per-(row, 128) scales) x e4m3 weights (+ 128x128 block scales) on
+    the kind::f8f6f4 tensor cores.  ``w8`` [N, K] (dense) or [E, N, K] with ``seg`` (grouped);
+    epilogues as :func:`grouped_gemm`, plus EPI_SWIGLU_Q8: SwiGLU quantized to e4m3 into
+    ``out`` [*, N/2] with scales ``out_scale`` [*, N/256]."""
+    M, K = aq.shape
+    grouped = w8.dim() == 3
+    E, Nn = (w8.shape[0], w8.shape[1]) if grouped else (1, w8.shape[0])
+    assert w8.shape[-1] == K and K % 128 == 0 and aq.is_cuda and aq.is_contiguous() and w8.is_contiguous()
+    swi = epilogue in (EPI_SWIGLU, EPI_SWIGLU_Q8)
+    out_cols = Nn // 2 if swi else Nn
+    rows = out_rows if out_rows is not None else M
+    if out is None:
+        dt = {EPI_F32: torch.float32, EPI_SWIGLU_Q8: torch.float8_e4m3fn}.get(epilogue, torch.bfloat16)
+        out = torch.empty(rows, out_cols, dtype=dt, device=aq.device)
+    if epilogue == EPI_SWIGLU_Q8 and out_scale is None:
+        out_scale = torch.empty(rows, Nn // 256, dtype=torch.float32, device=aq.device)
+    if M == 0:
+        return (out, out_scale) if epilogue == EPI_SWIGLU_Q8 else out
+    t = cnt = None
+    mx = 0
+    if grouped:
+        if tiles is None:
+            tiles = build_mtiles(seg, M)
+        t, cnt, mx = tiles
+    N.call("xtu_gemm_fp8_native", aq.data_ptr(), a_scale.data_ptr(), w8.data_ptr(), w_scale.data_ptr(),
+           out.data_ptr(), out.stride(0), N.ptr(out_scale), out_scale.stride(0) if out_scale is not None else 0,
+           M, Nn, K, E, N.ptr(t), N.ptr(cnt), mx, epilogue, N.ptr(row_scale), N.ptr(row_dest), N.ptr(bias),
+           float(act_limit), float(act_alpha), float(act_beta), peer_out, int(peer_rows),
+           N.status_buffer(aq.device).data_ptr(), N.stream_ptr(aq.device))
+    return (out, out_scale) if epilogue == EPI_SWIGLU_Q8 else out
 
 
 # ---------------------------------------------------------------------------

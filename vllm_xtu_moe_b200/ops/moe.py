@@ -107,6 +107,19 @@ class MoEWorkspace:
         self.route_logits = None                                                 # fused decode router scratch
         self.route_counter = torch.zeros(1, dtype=torch.int32, device=d)
         self.ntiles = torch.zeros(1, dtype=torch.int32, device=d)
+        self.xq = self.xs = self.hq = self.hs = None                              # native fp8 path
+
+    def fp8_buffers(self):
+        """(x e4m3 [n, H], x scales [n, H/128], h e4m3 [n, I], h scales [n, I/128]) of the
+        native fp8 expert GEMMs, allocated on first use."""
+        if self.xq is None:
+            n = self.max_tokens * self.top_k
+            d = self.device
+            self.xq = torch.empty(n, self.hidden, dtype=torch.float8_e4m3fn, device=d)
+            self.xs = torch.empty(n, self.hidden // 128, dtype=torch.float32, device=d)
+            self.hq = torch.empty(n, self.inter, dtype=torch.float8_e4m3fn, device=d)
+            self.hs = torch.empty(n, self.inter // 128, dtype=torch.float32, device=d)
+        return self.xq, self.xs, self.hq, self.hs
 
     def nbytes(self) -> int:
         return sum(t.numel() * t.element_size() for t in vars(self).values() if isinstance(t, torch.Tensor))
@@ -191,6 +204,16 @@ def moe_experts_partial(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tenso
     # the segment table of this call has E + 1 entries (the workspace may serve more experts)
     tiles = G.build_mtiles(ws.seg[: E + 1], n, ws.tiles, ws.ntiles)
     xp = ws.xp[:n]
+    if fp8 and experts.interleaved and G.fp8_native_ok(n, 2 * I, H, swiglu=True) and I % 128 == 0:
+        # native fp8 tensor cores: rows quantized per 128 columns, gate/up + SwiGLU written
+        # straight back as e4m3 (+ scales), which the down GEMM reads as its A operand
+        xq, xs, hq, hs = ws.fp8_buffers()
+        G.quant_fp8_rows(xp, xq[:n], xs[:n])
+        G.gemm_fp8_native(xq[:n], xs[:n], experts.w13, experts.s13, tiles=tiles, epilogue=G.EPI_SWIGLU_Q8,
+                          out=hq[:n], out_scale=hs[:n], act_limit=act_limit, act_alpha=act_alpha, act_beta=act_beta)
+        G.gemm_fp8_native(hq[:n], hs[:n], experts.w2, experts.s2, tiles=tiles, epilogue=G.EPI_BF16,
+                          out=ws.slots, row_scale=ws.perm_w, row_dest=ws.perm_slot, out_rows=ws.slots.shape[0])
+        return None
     sc13 = experts.s13 if fp8 else None
     sc2 = experts.s2 if fp8 else None
     if experts.interleaved:
