@@ -608,6 +608,287 @@ __global__ void moe_active_kernel(const int* __restrict__ seg, int E, int* __res
 }
 
 
+// ---------------------------------------------------------------------------
+// MXFP4 / NVFP4 experts at decode (the reference's moe4_smallm.cu role, restated for
+// tensor cores).  A stage is still 32 weight rows x 256 bytes, now 512 k of packed e2m1
+// (low nibble = even k), with the activations of the same k range in bf16.  Consumer warp
+// cw owns bytes [64 cw, 64 cw + 64) of each row; lane (g4, tq) decodes its 16-byte chunk
+// (32 k = one MXFP4 scale group, two NVFP4 groups) of rows g4 and g4 + 8 through a
+// byte -> bf16-pair table in shared memory, multiplies by the row's group scale (exact in
+// bf16: a power of two, or an e4m3 value times an e2m1 value), and feeds bf16 m16n8k16
+// MMAs with k = 32 tq + 4 g + {0,1 | 2,3} for MMA g (the activations use the same order).
+// NVFP4's per-expert fp32 global scale multiplies the fp32 result.
+// ---------------------------------------------------------------------------
+template <int NT>
+struct Gv4Cfg {
+  static constexpr int KSTAGE = 512;                            // k per stage
+  static constexpr int XROWS = 8 * NT;
+  static constexpr int XBOXES = KSTAGE / 64;                    // 64 bf16 per 128-byte box
+  static constexpr int X_BYTES = XBOXES * XROWS * 128;
+  static constexpr int STAGE_BYTES = GV_W_BYTES + X_BYTES;
+  static constexpr int STAGES = 4;
+  static constexpr int RED_FLOATS = GV_CWARPS * 32 * 2 * NT * 4;
+  static constexpr int BYTES = 1024 + STAGES * STAGE_BYTES + RED_FLOATS * 4 + 256 * 4 + 2 * STAGES * 8 + 64;
+};
+
+template <int NT>
+__device__ __forceinline__ uint8_t* gv4_setup(uint64_t*& full, uint64_t*& empty, float*& red, uint32_t*& lut) {
+  using C = Gv4Cfg<NT>;
+  extern __shared__ uint8_t gv_smem_raw[];
+  const uint32_t a = smem_u32(gv_smem_raw);
+  uint8_t* base = gv_smem_raw + (((a + 1023u) & ~1023u) - a);
+  red = reinterpret_cast<float*>(base + C::STAGES * C::STAGE_BYTES);
+  lut = reinterpret_cast<uint32_t*>(red + C::RED_FLOATS);
+  full = reinterpret_cast<uint64_t*>(lut + 256);
+  empty = full + C::STAGES;
+  // byte -> (bf16 of the low nibble, bf16 of the high nibble); e2m1 magnitudes 0, .5, 1, 1.5, 2, 3, 4, 6
+  for (int b = threadIdx.x; b < 256; b += blockDim.x) {
+    const uint32_t mag[8] = {0x0000u, 0x3F00u, 0x3F80u, 0x3FC0u, 0x4000u, 0x4040u, 0x4080u, 0x40C0u};
+    const int lo = b & 15, hi = b >> 4;
+    const uint32_t vlo = ((lo & 8) ? 0x8000u : 0u) | mag[lo & 7];
+    const uint32_t vhi = ((hi & 8) ? 0x8000u : 0u) | mag[hi & 7];
+    lut[b] = vlo | (vhi << 16);
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], GV_CWARPS);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+  return base;
+}
+
+// bf16x2 of a group scale: e8m0 (MXFP4) or e4m3 (NVFP4)
+template <bool NV>
+__device__ __forceinline__ uint32_t gv4_scale2(uint8_t s) {
+  uint32_t b;
+  if (NV) {
+    const __half_raw hr = __nv_cvt_fp8_to_halfraw((__nv_fp8_storage_t)s, __NV_E4M3);
+    b = __bfloat16_as_ushort(__float2bfloat16(__half2float(__half(hr))));
+  } else {
+    b = s == 0 ? 0x0040u : (s == 255 ? 0x7FC0u : ((uint32_t)s << 7));
+  }
+  return b | (b << 16);
+}
+
+__device__ __forceinline__ uint32_t bmul2(uint32_t a, uint32_t b) {
+  __nv_bfloat162 r = __hmul2(*reinterpret_cast<__nv_bfloat162*>(&a), *reinterpret_cast<__nv_bfloat162*>(&b));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+
+// As gv_stream_tile for packed e2m1 weights; sc8: the weights' group-scale bytes, row-major
+// [rows, K / G] (G = 32 MXFP4, 16 NVFP4) indexed by the same row numbers as the tensor map.
+template <bool NV, int NT, int WMODE>
+__device__ __forceinline__ bool gv4_stream_tile(const CUtensorMap* tmap, const CUtensorMap* xmap, uint8_t* stages,
+                                                uint64_t* full, uint64_t* empty, const uint32_t* lut,
+                                                uint32_t& phase_base, const int (&row0)[2], int nst, int K,
+                                                const uint8_t* __restrict__ sc8, int x_row0, int mcount,
+                                                float (&acc)[2][NT][4], XtuStatus* st) {
+  using C = Gv4Cfg<NT>;
+  constexpr int G = NV ? 16 : 32;
+  const int ng = K / G;                       // scale groups per row
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  bool ok = true;
+#pragma unroll
+  for (int t = 0; t < 2; ++t)
+#pragma unroll
+    for (int n = 0; n < NT; ++n)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[t][n][i] = 0.f;
+  if (warp == 0) {
+    if (elect_one()) {
+      int issued = 0;
+      for (int i = 0; i < nst; ++i) {
+        const uint32_t it = phase_base + i;
+        const int slot = it % C::STAGES;
+        if (it >= C::STAGES && !mbar_wait(&empty[slot], ((it / C::STAGES) - 1) & 1, st, 62)) { ok = false; break; }
+        ++issued;
+        mbar_arrive_expect_tx(&full[slot], C::STAGE_BYTES);
+        uint8_t* dst = stages + slot * C::STAGE_BYTES;
+        if (WMODE == 0) tma_load_3d(dst, tmap, &full[slot], 0, row0[0], 2 * i);
+        else tma_load_4d(dst, tmap, &full[slot], 0, row0[0], 0, 2 * i);
+        tma_load_3d(dst + GV_W_BYTES, xmap, &full[slot], 0, x_row0, i * C::XBOXES);
+      }
+      if (!ok) {
+        for (int j = issued > C::STAGES ? issued - C::STAGES : 0; j < issued; ++j) {
+          const uint32_t it = phase_base + j;
+          mbar_wait(&full[it % C::STAGES], (it / C::STAGES) & 1, nullptr, 0, 50000000ull);
+        }
+      }
+    }
+    __syncwarp();
+  } else {
+    const int cw = warp - 1;
+    const int g4 = lane >> 2, tq = lane & 3;
+    const int c16 = (cw & 1) * 4 + tq;        // 16-byte chunk of the 128-byte row within box (cw >> 1)
+    const int xbox = cw * 2 + (tq >> 1);      // 64-element activation box of this lane's 32 k
+    for (int i = 0; i < nst; ++i) {
+      const uint32_t it = phase_base + i;
+      const int slot = it % C::STAGES;
+      // this lane's group scales for rows g4 / g4 + 8 of both 16-row halves (fetched before the wait)
+      const int k0 = i * C::KSTAGE + cw * 128 + tq * 32;
+      uint32_t s2[2][2][2];                   // [half t][row h][group of the 32 k]
+#pragma unroll
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const uint8_t* sr = sc8 + (size_t)(row0[t] + g4 + 8 * h) * ng;
+          const int gi = min(k0 / G, ng - 1);
+          s2[t][h][0] = gv4_scale2<NV>(__ldg(sr + gi));
+          s2[t][h][1] = NV ? gv4_scale2<NV>(__ldg(sr + min(gi + 1, ng - 1))) : s2[t][h][0];
+        }
+      if (!mbar_wait(&full[slot], (it / C::STAGES) & 1, st, 63)) { ok = false; break; }
+      const uint8_t* sbase = stages + slot * C::STAGE_BYTES;
+      const uint8_t* box = sbase + (cw >> 1) * 4096;
+      uint4 w[2][2];
+#pragma unroll
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int r = t * 16 + g4 + h * 8;
+          w[t][h] = *reinterpret_cast<const uint4*>(box + r * 128 + ((c16 ^ (r & 7)) << 4));
+        }
+      uint4 xr[NT][4];
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+        const int tok = n * 8 + g4;
+        const uint8_t* xrow = sbase + GV_W_BYTES + xbox * (C::XROWS * 128) + tok * 128;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint4 v = *reinterpret_cast<const uint4*>(xrow + ((((tq & 1) * 4 + q) ^ (tok & 7)) << 4));
+          xr[n][q] = tok < mcount ? v : make_uint4(0, 0, 0, 0);
+        }
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
+#pragma unroll
+      for (int g = 0; g < 8; ++g) {
+        const int grp = NV ? (g >> 2) : 0;
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          // bytes 2g, 2g+1 of each row's chunk: k = 4g .. 4g + 3
+          const uint32_t wa = u4w(w[t][0], g >> 1) >> (16 * (g & 1));
+          const uint32_t wb = u4w(w[t][1], g >> 1) >> (16 * (g & 1));
+          const uint32_t a0 = bmul2(lut[wa & 0xFF], s2[t][0][grp]);
+          const uint32_t a2 = bmul2(lut[(wa >> 8) & 0xFF], s2[t][0][grp]);
+          const uint32_t a1 = bmul2(lut[wb & 0xFF], s2[t][1][grp]);
+          const uint32_t a3 = bmul2(lut[(wb >> 8) & 0xFF], s2[t][1][grp]);
+#pragma unroll
+          for (int n = 0; n < NT; ++n)
+            mma_bf16_16816(acc[t][n], a0, a1, a2, a3, u4w(xr[n][g >> 1], 2 * (g & 1)),
+                           u4w(xr[n][g >> 1], 2 * (g & 1) + 1));
+        }
+      }
+    }
+  }
+  phase_base += nst;
+  return __syncthreads_and(ok);
+}
+
+// grouped gate/up + SwiGLU for packed-4-bit experts (token-direct form as moe_gemv_gate_up_kernel)
+template <bool NV, int NT>
+__global__ void __launch_bounds__(GV_THREADS) moe_gemv4_gate_up_kernel(
+    const __grid_constant__ CUtensorMap tmap, const __grid_constant__ CUtensorMap xmap,
+    const uint8_t* __restrict__ sc8, const float* __restrict__ gs, int I, int K, const int* __restrict__ seg,
+    const int* __restrict__ active, const int* __restrict__ tokrow, int ntok, __nv_bfloat16* __restrict__ h,
+    float limit, float alpha, float beta, XtuStatus* st) {
+  griddep_wait();
+  griddep_launch_dependents();
+  const int nact = active[0];
+  if ((int)blockIdx.y >= nact) return;
+  const int e = active[1 + blockIdx.y];
+  const int s0 = seg[e], cnt = seg[e + 1] - s0;
+  if (cnt <= 0) return;
+  const int* trow = tokrow ? tokrow + blockIdx.y * 16 : nullptr;
+  const int xrow0 = trow ? 0 : s0, xcnt = trow ? ntok : cnt;
+  uint64_t *full, *empty;
+  float* red;
+  uint32_t* lut;
+  uint8_t* stages = gv4_setup<NT>(full, empty, red, lut);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g4 = lane >> 2, tq = lane & 3;
+  const int nst = (K + Gv4Cfg<NT>::KSTAGE - 1) / Gv4Cfg<NT>::KSTAGE;
+  const int j0 = blockIdx.x * 16;
+  const int grow = (j0 >> 7) * 256 + (j0 & 127);
+  const int rows[2] = {e * 2 * I + grow, e * 2 * I + grow + 128};
+  const float g_s = NV ? gs[e] : 1.f;
+  uint32_t pb = 0;
+  for (int mb = 0; mb < xcnt; mb += 8 * NT) {
+    const int mc = min(8 * NT, xcnt - mb);
+    float acc[2][NT][4];
+    if (!gv4_stream_tile<NV, NT, 1>(&tmap, &xmap, stages, full, empty, lut, pb, rows, nst, K, sc8, xrow0 + mb, mc,
+                                    acc, st))
+      return;
+    gv_reduce<NT>(acc, red);
+    if (warp != 1) continue;
+#pragma unroll
+    for (int n = 0; n < NT; ++n)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int j = j0 + g4 + (i >> 1) * 8;
+        const int tok = n * 8 + 2 * tq + (i & 1);
+        const int hr = tok >= mc ? -1 : trow ? trow[mb + tok] : s0 + mb + tok;
+        if (hr >= 0) {
+          float g = acc[0][n][i] * g_s, u = acc[1][n][i] * g_s;
+          if (limit > 0.f) { g = fminf(g, limit); u = fminf(fmaxf(u, -limit), limit); }
+          h[(size_t)hr * I + j] = __float2bfloat16((g / (1.f + __expf(-alpha * g))) * (u + beta));
+        }
+      }
+  }
+}
+
+// grouped down for packed-4-bit experts: out[slot[row]] = w[row] * (h[row] W2[e]^T)
+template <bool NV, int NT>
+__global__ void __launch_bounds__(GV_THREADS) moe_gemv4_down_kernel(
+    const __grid_constant__ CUtensorMap tmap, const __grid_constant__ CUtensorMap xmap,
+    const uint8_t* __restrict__ sc8, const float* __restrict__ gs, int H, int I, const int* __restrict__ seg,
+    const int* __restrict__ active, const int* __restrict__ perm_slot, const float* __restrict__ perm_w,
+    __nv_bfloat16* __restrict__ out, XtuStatus* st) {
+  griddep_wait();
+  griddep_launch_dependents();
+  const int nact = active[0];
+  if ((int)blockIdx.y >= nact) return;
+  const int e = active[1 + blockIdx.y];
+  const int s0 = seg[e], cnt = seg[e + 1] - s0;
+  if (cnt <= 0) return;
+  uint64_t *full, *empty;
+  float* red;
+  uint32_t* lut;
+  uint8_t* stages = gv4_setup<NT>(full, empty, red, lut);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g4 = lane >> 2, tq = lane & 3;
+  const int nst = (I + Gv4Cfg<NT>::KSTAGE - 1) / Gv4Cfg<NT>::KSTAGE;
+  const int r0 = blockIdx.x * 32;
+  const int rows[2] = {e * H + r0, e * H + r0 + 16};
+  const float g_s = NV ? gs[e] : 1.f;
+  uint32_t pb = 0;
+  for (int mb = 0; mb < cnt; mb += 8 * NT) {
+    const int mc = min(8 * NT, cnt - mb);
+    float acc[2][NT][4];
+    if (!gv4_stream_tile<NV, NT, 0>(&tmap, &xmap, stages, full, empty, lut, pb, rows, nst, I, sc8, s0 + mb, mc, acc,
+                                    st))
+      return;
+    gv_reduce<NT>(acc, red);
+    if (warp != 1) continue;
+#pragma unroll
+    for (int t = 0; t < 2; ++t)
+#pragma unroll
+      for (int n = 0; n < NT; ++n)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int row = r0 + t * 16 + g4 + (i >> 1) * 8;
+          const int tok = n * 8 + 2 * tq + (i & 1);
+          if (row < H && tok < mc) {
+            const int pr = s0 + mb + tok;
+            out[(size_t)perm_slot[pr] * H + row] = __float2bfloat16(acc[t][n][i] * g_s * perm_w[pr]);
+          }
+        }
+  }
+}
+
 // Workspace of the dense GEMV: fp32 split-K partials (up to 4 splits x 16 rows x N, used
 // only while the tiles do not fill the GPU) followed by the f16 activation scratch.
 constexpr long long GV_WS_PART_FLOATS = 1 << 20;
@@ -933,6 +1214,75 @@ int xtu_moe_gemv(const void* W13, const float* s13, const void* W2, const float*
     if (nt == 1) XTU_MOE_GEMV_LAUNCH(false, 1); else XTU_MOE_GEMV_LAUNCH(false, 2);
   }
 #undef XTU_MOE_GEMV_LAUNCH
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? launches : -(int)e;
+}
+
+
+// packed-4-bit grouped decode MoE (MXFP4: fmt 2, scales e8m0 per 32 k; NVFP4: fmt 3, scales
+// e4m3 per 16 k and per-expert fp32 global scales gs13 / gs2).  W13 [E, 2I, H/2] bytes with
+// gate/up rows interleaved in 128-row blocks, W2 [E, H, I/2]; scales row-major per weight row.
+// xp: bf16 activations (tokrow: the step's ntok <= 16 tokens, token-direct; else permuted
+// rows); h: bf16 [n_rows, I]; slots: bf16 output rows.  Other arguments as xtu_moe_gemv.
+int xtu_moe_gemv4(const void* W13, const void* s13, const float* gs13, const void* W2, const void* s2,
+                  const float* gs2, int fmt, int E, int H, int I, const void* xp, int x_stride, const int* tokrow,
+                  int ntok, const int* seg, const int* perm_slot, const float* perm_w, void* h, void* slots, int mmax,
+                  int max_active, int n_rows, int* active, int active_ready, float limit, float alpha, float beta,
+                  void* status, cudaStream_t s) {
+  if (mmax <= 0 || n_rows <= 0) return 0;
+  if (fmt != 2 && fmt != 3) return -9;
+  if (mmax > 16 || H % 256 != 0 || I % 256 != 0 || active == nullptr || s13 == nullptr || s2 == nullptr) return -2;
+  if (fmt == 3 && (gs13 == nullptr || gs2 == nullptr)) return -8;
+  if (tokrow && (ntok <= 0 || ntok > 16 || ntok > mmax)) return -2;
+  if (max_active <= 0 || max_active > E) max_active = E;
+  const int nt = mmax > 8 ? 2 : 1;
+  const int x_rows = tokrow ? ntok : n_rows;
+  if (x_stride <= 0) x_stride = H;
+  CUtensorMap t13, t2, xm, hm;
+  int rc = gv_wmap(&t13, W13, (uint64_t)E * 2 * I, H / 2, true, true);
+  if (rc) return rc;
+  rc = gv_wmap(&t2, W2, (uint64_t)E * H, I / 2, true, false);
+  if (rc) return rc;
+  {
+    const cuuint64_t dims[3] = {64, (cuuint64_t)x_rows, (cuuint64_t)H / 64};
+    const cuuint64_t strides[2] = {(cuuint64_t)x_stride * 2, 128};
+    const cuuint32_t box[3] = {64, (cuuint32_t)(8 * nt), 8};
+    rc = gv_tmap_nd(&xm, xp, false, 3, dims, strides, box);
+    if (rc) return rc;
+    const cuuint64_t hdims[3] = {64, (cuuint64_t)n_rows, (cuuint64_t)I / 64};
+    const cuuint64_t hstrides[2] = {(cuuint64_t)I * 2, 128};
+    rc = gv_tmap_nd(&hm, h, false, 3, hdims, hstrides, box);
+    if (rc) return rc;
+  }
+  int launches = 2;
+  if (!active_ready) {
+    launch_pdl(moe_active_kernel, dim3(1), dim3(32), 0, s, seg, E, active);
+    ++launches;
+  }
+  XtuStatus* st = reinterpret_cast<XtuStatus*>(status);
+  const uint8_t* sc13 = reinterpret_cast<const uint8_t*>(s13);
+  const uint8_t* sc2 = reinterpret_cast<const uint8_t*>(s2);
+  const dim3 g1(I / 16, max_active), g2(H / 32, max_active);
+#define XTU_MOE_GEMV4_LAUNCH(NVV, NTV)                                                                        \
+  do {                                                                                                       \
+    static bool init = false;                                                                                \
+    if (!init) {                                                                                             \
+      rc = gv_smem_attr(moe_gemv4_gate_up_kernel<NVV, NTV>, Gv4Cfg<NTV>::BYTES);                              \
+      if (!rc) rc = gv_smem_attr(moe_gemv4_down_kernel<NVV, NTV>, Gv4Cfg<NTV>::BYTES);                        \
+      if (rc) return rc;                                                                                     \
+      init = true;                                                                                           \
+    }                                                                                                        \
+    launch_pdl(moe_gemv4_gate_up_kernel<NVV, NTV>, g1, dim3(GV_THREADS), Gv4Cfg<NTV>::BYTES, s, t13, xm, sc13, \
+               gs13, I, H, seg, active, tokrow, ntok, (__nv_bfloat16*)h, limit, alpha, beta, st);             \
+    launch_pdl(moe_gemv4_down_kernel<NVV, NTV>, g2, dim3(GV_THREADS), Gv4Cfg<NTV>::BYTES, s, t2, hm, sc2, gs2, \
+               H, I, seg, active, perm_slot, perm_w, (__nv_bfloat16*)slots, st);                              \
+  } while (0)
+  if (fmt == 3) {
+    if (nt == 1) XTU_MOE_GEMV4_LAUNCH(true, 1); else XTU_MOE_GEMV4_LAUNCH(true, 2);
+  } else {
+    if (nt == 1) XTU_MOE_GEMV4_LAUNCH(false, 1); else XTU_MOE_GEMV4_LAUNCH(false, 2);
+  }
+#undef XTU_MOE_GEMV4_LAUNCH
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? launches : -(int)e;
 }

@@ -215,9 +215,13 @@ def test_gemv_decode(fp8, M, N_, K):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("fmt", ["mxfp4", "nvfp4"])
-@pytest.mark.parametrize("T,E,H,I,K", [(37, 8, 512, 256, 2), (300, 16, 1024, 512, 4), (5, 4, 256, 128, 2)])
+@pytest.mark.parametrize("T,E,H,I,K", [(37, 8, 512, 256, 2), (300, 16, 1024, 512, 4), (5, 4, 256, 128, 2),
+                                       # decode sizes: the packed-4-bit grouped GEMV (xtu_moe_gemv4)
+                                       (1, 8, 512, 256, 2), (4, 32, 2048, 512, 8), (16, 16, 1024, 512, 4),
+                                       (11, 8, 512, 768, 2)])
 def test_fused_moe_fp4_matches_reference(fmt, T, E, H, I, K):
-    """MXFP4 / NVFP4 experts through the grouped GEMM (on-chip widening) vs fp32 dequant reference."""
+    """MXFP4 / NVFP4 experts through the grouped GEMM (on-chip widening) or, at decode sizes, the
+    packed-4-bit grouped GEMV, vs the fp32 dequant reference."""
     from vllm_xtu_moe_b200.ops import moe as M
     from vllm_xtu_moe_b200.ops.quant import quant_mxfp4, quant_nvfp4
     g = torch.Generator().manual_seed(T + E)

@@ -80,6 +80,20 @@ def _experts(E, H, I, fmt, seed=0):
         q2, s2 = quant_fp8_block(w2)
         del w13, w2
         ex = M.prepare_experts("fp8", q13, q2, s13, s2)
+    elif fmt == "mxfp4":
+        from .ops.quant import quant_mxfp4
+        p13, s13 = quant_mxfp4(w13)
+        p2, s2 = quant_mxfp4(w2)
+        del w13, w2
+        ex = M.prepare_experts("mxfp4", p13, p2, s13, s2)
+    elif fmt == "nvfp4":
+        from .ops.quant import quant_nvfp4
+        r13 = [quant_nvfp4(w13[e]) for e in range(E)]
+        r2 = [quant_nvfp4(w2[e]) for e in range(E)]
+        del w13, w2
+        p13, s13, gs13 = (torch.stack([r[i] for r in r13]) for i in range(3))
+        p2, s2, gs2 = (torch.stack([r[i] for r in r2]) for i in range(3))
+        ex = M.prepare_experts("nvfp4", p13, p2, s13, s2, gs13.float(), gs2.float())
     else:
         ex = M.prepare_experts("bf16", w13.to(torch.bfloat16), w2.to(torch.bfloat16))
         del w13, w2
@@ -102,7 +116,8 @@ def bench_moe(T: int, fmt: str, E=128, H=4096, I=1408, K=8, iters=10) -> dict:
     fn = lambda: M.fused_moe(x, ids, w, ex, ws, out=out)
     ms = time_fn(fn, iters)
     active = torch.unique(ids).numel()
-    wb = (1 if fmt == "fp8" else 2) * 3 * H * I * active
+    per = {"fp8": 1.0, "bf16": 2.0, "mxfp4": 0.5 + 1 / 32, "nvfp4": 0.5 + 1 / 16}[fmt]
+    wb = per * 3 * H * I * active
     nbytes = wb + T * H * 2 * 2 + T * K * H * 2 * 3
     flops = 2 * T * K * 3 * H * I
     return _report(f"moe_{'decode' if T <= G.GEMV_MAX_M else 'prefill'}_{fmt}",
@@ -509,6 +524,9 @@ OPS = {
     "kda_prefill": lambda a: bench_kda(),
     "cpu_bridge": lambda a: bench_cpu_bridge(),
     "moe_vs_reference": lambda a: [bench_moe_vs_reference(t) for t in a.sizes],
+    # Qwen3-Next-shaped packed-4-bit decode MoE (512 experts top-10, H 2048, I 512)
+    "moe_decode_mxfp4": lambda a: [bench_moe(t, "mxfp4", E=512, H=2048, I=512, K=10) for t in (1, 4, 16)],
+    "moe_decode_nvfp4": lambda a: [bench_moe(t, "nvfp4", E=512, H=2048, I=512, K=10) for t in (1, 4, 16)],
     "moe_w8a8": lambda a: [bench_moe_w8a8(t) for t in a.sizes if t > G.GEMV_MAX_M],
 }
 

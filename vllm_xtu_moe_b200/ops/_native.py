@@ -71,6 +71,8 @@ _SIGS: dict[str, list] = {
     "xtu_gemv": [P, P, c_int, c_int, c_int, P, c_int, c_int, P, P, c_int, c_int, P, P, P, P],
     "xtu_moe_gemv": [P, P, P, P, c_int, c_int, c_int, c_int, P, c_int, c_int, P, c_int, P, P, P, P, P, c_int, c_int,
                      c_int, P, c_int, c_float, c_float, c_float, P, P, P, P, c_int, P, P, P],
+    "xtu_moe_gemv4": [P, P, P, P, P, P, c_int, c_int, c_int, c_int, P, c_int, P, c_int, P, P, P, P, P, c_int, c_int,
+                      c_int, P, c_int, c_float, c_float, c_float, P, P],
     "xtu_gemv_tp": [P, P, c_int, c_int, c_int, P, c_int, c_int, P, P, P, ctypes.c_longlong, c_int, c_int, P, P, P, P,
                     P, P],
     "xtu_tp_sum_rmsnorm": [P, ctypes.c_longlong, c_int, c_int, c_int, P, P, P, P, P, P, P, P, c_float, c_int, P,

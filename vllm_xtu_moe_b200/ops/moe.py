@@ -185,6 +185,22 @@ def moe_experts_partial(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tenso
                ws.active.data_ptr(), 1, float(act_limit), float(act_alpha), float(act_beta),
                *_shared_ptrs(shared_mlp), n, _gv_ws(x.device), N.status_buffer(x.device).data_ptr(), s)
         return ws.slots[n:n + T] if shared_mlp is not None else None
+    if (T <= G.GEMV_MAX_M and experts.interleaved and experts.fmt in G.FP4_FMTS and H % 256 == 0 and I % 256 == 0
+            and E <= 1024):
+        # packed-4-bit experts at decode: the same token-direct grouped GEMV with e2m1 weights
+        # decoded on chip (xtu_moe_gemv4)
+        xt = G.tma_rows(x)
+        if not permuted:
+            N.call("xtu_moe_permute_decode", ids.data_ptr(), weights.data_ptr(), T, K, lo, lo + E, ws.seg.data_ptr(),
+                   ws.perm_slot.data_ptr(), ws.perm_w.data_ptr(), ws.active.data_ptr(), ws.tokrow.data_ptr(), s)
+        nv = experts.fmt == "nvfp4"
+        N.call("xtu_moe_gemv4", experts.w13.data_ptr(), experts.s13.data_ptr(), N.ptr(experts.gs13 if nv else None),
+               experts.w2.data_ptr(), experts.s2.data_ptr(), N.ptr(experts.gs2 if nv else None),
+               G.FP4_FMTS[experts.fmt], E, H, I, xt.data_ptr(), xt.stride(0), ws.tokrow.data_ptr(), T,
+               ws.seg.data_ptr(), ws.perm_slot.data_ptr(), ws.perm_w.data_ptr(), ws.h.data_ptr(), ws.slots.data_ptr(),
+               T, min(E, T * K), n, ws.active.data_ptr(), 1, float(act_limit), float(act_alpha), float(act_beta),
+               N.status_buffer(x.device).data_ptr(), s)
+        return None
     if permuted:
         raise ValueError("a decode-permuted workspace needs the decode GEMV path")
     f16s = int(gemv_path and fp8)
