@@ -14,6 +14,7 @@ import math
 import torch
 
 from ..ops import basic as B
+from ..ops import gemm as G
 from ..ops.attention import AttnMetadata, paged_attention
 from .config import ModelConfig
 from .layers import Linear
@@ -36,6 +37,8 @@ class MLAAttention:
         self.scale = mscale / math.sqrt(self.dn + self.dr)
         self._w_uk = None
         self._w_uv = None
+        self._w_ukT = None
+        self._dec = {}
 
     def _absorbed(self):
         """W_UK [nh, dn, dc] and W_UV [nh, dv, dc] (fp32 -> bf16) from kv_b [nh*(dn+dv), dc]."""
@@ -43,7 +46,50 @@ class MLAAttention:
             w = self.kv_b.dense_weight().view(self.nh, self.dn + self.dv, self.dc)
             self._w_uk = w[:, : self.dn].to(torch.bfloat16).contiguous()
             self._w_uv = w[:, self.dn:].to(torch.bfloat16).contiguous()
+            self._w_ukT = self._w_uk.transpose(1, 2).contiguous()      # [nh, dc, dn]: q_nope -> latent
         return self._w_uk, self._w_uv
+
+    def _decode_plan(self, T: int, device):
+        """Static per-T tensors of the absorbed decode GEMMs: head h's T rows form group h
+        (rows h*T .. h*T+T-1 of the head-major operand), and row (h, t) lands in row t*nh + h."""
+        key = (T, device)
+        p = self._dec.get(key)
+        if p is None:
+            nh = self.nh
+            seg = torch.arange(0, (nh + 1) * T, T, dtype=torch.int32, device=device)
+            hh, tt = torch.meshgrid(torch.arange(nh, device=device), torch.arange(T, device=device), indexing="ij")
+            dest = (tt * nh + hh).reshape(-1).to(torch.int32).contiguous()
+            mx = G.max_mtiles(nh * T, nh)
+            p = dict(seg=seg, dest=dest, tiles=torch.empty(mx * 4, dtype=torch.int32, device=device),
+                     cnt=torch.zeros(1, dtype=torch.int32, device=device))
+            self._dec[key] = p
+        return p
+
+    def _absorb_q(self, q_nope: torch.Tensor, q_rope: torch.Tensor) -> torch.Tensor:
+        """[T, nh, dc + dr] decode queries: q_nope W_UK per head (a grouped tcgen05 GEMM whose
+        epilogue scatters each head's rows into token order) next to the RoPE'd part."""
+        T = q_nope.shape[0]
+        nh, dc, dr = self.nh, self.dc, self.dr
+        p = self._decode_plan(T, q_nope.device)
+        a = q_nope.transpose(0, 1).reshape(nh * T, self.dn).contiguous()   # head-major rows
+        qfull = torch.empty(T, nh, dc + dr, dtype=torch.bfloat16, device=q_nope.device)
+        tiles = G.build_mtiles(p["seg"], nh * T, p["tiles"], p["cnt"])
+        G.grouped_gemm(a, self._w_ukT, p["seg"], out=qfull.view(T * nh, dc + dr)[:, :dc], row_dest=p["dest"],
+                       out_rows=T * nh, tiles=tiles)
+        qfull[:, :, dc:].copy_(q_rope)
+        return qfull
+
+    def _absorb_o(self, o_lat: torch.Tensor) -> torch.Tensor:
+        """[T, nh, dv] outputs: o_lat W_UV^T per head (grouped GEMM, rows scattered to token order)."""
+        T = o_lat.shape[0]
+        nh, dv = self.nh, self.dv
+        p = self._decode_plan(T, o_lat.device)
+        a = o_lat.transpose(0, 1).reshape(nh * T, self.dc).contiguous()
+        o = torch.empty(T, nh, dv, dtype=torch.bfloat16, device=o_lat.device)
+        tiles = G.build_mtiles(p["seg"], nh * T, p["tiles"], p["cnt"])
+        G.grouped_gemm(a, self._w_uv, p["seg"], out=o.view(T * nh, dv), row_dest=p["dest"], out_rows=T * nh,
+                       tiles=tiles)
+        return o
 
     def __call__(self, x: torch.Tensor, meta: AttnMetadata, kv: tuple, rope: torch.Tensor) -> torch.Tensor:
         T = x.shape[0]
@@ -70,10 +116,15 @@ class MLAAttention:
         q_nope = q[:, :, :dn]
         if meta.is_decode:
             w_uk, w_uv = self._absorbed()
-            qn = torch.einsum("thd,hdc->thc", q_nope.float(), w_uk.float()).to(torch.bfloat16)
-            qfull = torch.cat([qn, q_rope.to(torch.bfloat16)], dim=-1).contiguous()   # [T, nh, dc+dr]
-            o_lat = paged_attention(qfull, k_cache, None, meta, self.scale, v_dim=dc)  # [T, nh, dc]
-            o = torch.einsum("thc,hvc->thv", o_lat.float(), w_uv.float()).to(torch.bfloat16)
+            if x.is_cuda and dc % 128 == 0 and dn % 64 == 0 and dv % 16 == 0:
+                qfull = self._absorb_q(q_nope, q_rope)
+                o_lat = paged_attention(qfull, k_cache, None, meta, self.scale, v_dim=dc)  # [T, nh, dc]
+                o = self._absorb_o(o_lat)
+            else:
+                qn = torch.einsum("thd,hdc->thc", q_nope.float(), w_uk.float()).to(torch.bfloat16)
+                qfull = torch.cat([qn, q_rope.to(torch.bfloat16)], dim=-1).contiguous()   # [T, nh, dc+dr]
+                o_lat = paged_attention(qfull, k_cache, None, meta, self.scale, v_dim=dc)
+                o = torch.einsum("thc,hvc->thv", o_lat.float(), w_uv.float()).to(torch.bfloat16)
         else:
             o = self._prefill(q_nope, q_rope, meta, k_cache)
         return self.o(o.reshape(T, nh * dv))
@@ -87,36 +138,39 @@ class MLAAttention:
         return self._prefill_ref(q_nope, q_rope, meta, k_cache)
 
     def _prefill_flash(self, q_nope, q_rope, meta, k_cache):
-        """Expand each sequence's latent context into per-head K [n, nh, dn+dr] and V
-        [n, nh, dv], lay them out as a paged cache of 64-token blocks, and run the causal
-        flash kernel (no [q, k] score matrix is ever materialised)."""
+        """All sequences of the step at once: their latent context blocks are gathered into
+        one matrix, expanded by ONE kv_b GEMM into per-head K [., nh, dn+dr] and V [., nh, dv],
+        laid out as a paged cache (sequence b owns a contiguous run of 64-token blocks), and
+        ONE causal flash-attention launch covers every sequence (no [q, k] score matrix)."""
         nh, dn, dr, dv, dc = self.nh, self.dn, self.dr, self.dv, self.dc
-        T = q_nope.shape[0]
-        qs = meta.q_start_host if meta.q_start_host is not None else meta.q_start.tolist()
         kl = meta.kv_len_host if meta.kv_len_host is not None else meta.kv_len.tolist()
-        out = torch.empty(T, nh, dv, dtype=torch.bfloat16, device=q_nope.device)
         bs = k_cache.shape[2]
         d = q_nope.device
-        for b in range(meta.num_seqs):
-            s0, s1 = qs[b], qs[b + 1]
-            if s1 == s0:
-                continue
-            n = kl[b]
-            nb = (n + bs - 1) // bs
-            ent = k_cache[meta.block_table[b, :nb].long(), 0].reshape(nb * bs, dc + dr)
-            kvb = self.kv_b(ent[:, :dc].contiguous()).view(nb * bs, nh, dn + dv)
-            k = torch.cat([kvb[:, :, :dn], ent[:, dc:].view(nb * bs, 1, dr).expand(nb * bs, nh, dr)], dim=-1)
-            kc = k.view(nb, bs, nh, dn + dr).permute(0, 2, 1, 3).contiguous()
-            vc = kvb[:, :, dn:].reshape(nb, bs, nh, dv).permute(0, 2, 1, 3).contiguous()
-            q = torch.cat([q_nope[s0:s1], q_rope[s0:s1].to(q_nope.dtype)], dim=-1).contiguous()
-            ql = s1 - s0
-            m1 = AttnMetadata(num_seqs=1, q_start=torch.tensor([0, ql], dtype=torch.int32, device=d),
-                              kv_len=torch.tensor([n], dtype=torch.int32, device=d),
-                              block_table=torch.arange(nb, dtype=torch.int32, device=d).view(1, nb),
-                              slot_mapping=meta.slot_mapping[s0:s1], positions=meta.positions[s0:s1], max_q_len=ql,
-                              max_kv_len=n, is_decode=False, q_start_host=[0, ql], kv_len_host=[n])
-            out[s0:s1] = paged_attention(q, kc, vc, m1, self.scale)
-        return out
+        nbs = [(n + bs - 1) // bs for n in kl]
+        tot = sum(nbs)
+        if tot == 0:
+            return torch.zeros(q_nope.shape[0], nh, dv, dtype=torch.bfloat16, device=d)
+        mx = max(nbs)
+        # each sequence's first nb_b block ids, in order, and its run in the expanded cache
+        sel = torch.zeros(meta.num_seqs, mx, dtype=torch.bool)
+        new_bt = torch.zeros(meta.num_seqs, mx, dtype=torch.int32)
+        off = 0
+        for b, nb in enumerate(nbs):
+            sel[b, :nb] = True
+            new_bt[b, :nb] = torch.arange(off, off + nb, dtype=torch.int32)
+            off += nb
+        blocks = meta.block_table[:, :mx][sel.to(d)].long()                  # [tot]
+        ent = k_cache[blocks, 0].reshape(tot * bs, dc + dr)
+        kvb = self.kv_b(ent[:, :dc].contiguous()).view(tot * bs, nh, dn + dv)
+        k = torch.cat([kvb[:, :, :dn], ent[:, dc:].view(tot * bs, 1, dr).expand(tot * bs, nh, dr)], dim=-1)
+        kc = k.view(tot, bs, nh, dn + dr).permute(0, 2, 1, 3).contiguous()
+        vc = kvb[:, :, dn:].reshape(tot, bs, nh, dv).permute(0, 2, 1, 3).contiguous()
+        q = torch.cat([q_nope, q_rope.to(q_nope.dtype)], dim=-1).contiguous()
+        m2 = AttnMetadata(num_seqs=meta.num_seqs, q_start=meta.q_start, kv_len=meta.kv_len,
+                          block_table=new_bt.to(d, non_blocking=True), slot_mapping=meta.slot_mapping,
+                          positions=meta.positions, max_q_len=meta.max_q_len, max_kv_len=meta.max_kv_len,
+                          is_decode=False, q_start_host=meta.q_start_host, kv_len_host=meta.kv_len_host)
+        return paged_attention(q, kc, vc, m2, self.scale)
 
     def _prefill_ref(self, q_nope, q_rope, meta, k_cache):
         """Expand latent -> per-head K/V for every context token, causal attention."""
