@@ -1,6 +1,7 @@
 // Small-M (decode) GEMV / grouped-GEMV kernels for sm_100a, weight-streaming bound.
 //
-//   y[m, n] = sum_k x[m, k] * W[n, k]     (m < M <= 16, W bf16 or e4m3 + 128x128 fp32 scales)
+//   y[m, n] = sum_k x[m, k] * W[n, k]     (m < M <= 32 dense, <= 16 per expert grouped;
+//                                          W bf16 or e4m3 + 128x128 fp32 scales)
 //
 // At decode the GEMMs see 1..16 rows, so the job is to stream the weights at HBM
 // bandwidth.  A CTA owns one 32-row weight tile and streams it through a ring of
@@ -85,6 +86,7 @@ constexpr int GV_THREADS = 32 * (1 + GV_CWARPS);
 constexpr int GV_ROW_BYTES = 256;            // bytes of one weight row per stage (2 x 128-B boxes)
 constexpr int GV_W_BYTES = 32 * GV_ROW_BYTES;   // weight part of a stage: 32 rows
 constexpr int GV_MAX_KBLK = 128;             // block scales staged per tile (K <= 16384)
+constexpr int GV_MAX_ROWS = 32;              // activation rows of a dense GEMV call (NT <= 4)
 
 // A stage = the tile's 32 weight rows x 256 bytes, followed by the activations of the same
 // k range (bf16, 8 * NT token rows per 128-byte box), both loaded by TMA.
@@ -95,7 +97,7 @@ struct GvCfg {
   static constexpr int XBOXES = KSTAGE / 64;                     // 64 bf16 per 128-byte box
   static constexpr int X_BYTES = XBOXES * XROWS * 128;
   static constexpr int STAGE_BYTES = GV_W_BYTES + X_BYTES;       // multiple of 1024
-  static constexpr int STAGES = 4;
+  static constexpr int STAGES = NT >= 4 ? 3 : 4;                 // 32-row tiles: two CTAs per SM still fit
   static constexpr int RED_FLOATS = GV_CWARPS * 32 * 2 * NT * 4;
   static constexpr int BYTES = 1024 + STAGES * STAGE_BYTES + RED_FLOATS * 4 + 2 * GV_MAX_KBLK * 4 +
                                2 * STAGES * 8 + 64;
@@ -371,7 +373,7 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_dense_kernel(
         for (int i = 0; i < 4; ++i) {
           const int row = rows[t] + g4 + (i >> 1) * 8;
           const int tok = n * 8 + 2 * tq + (i & 1);
-          if (row < N && tok < M) ws[((size_t)split * 16 + tok) * N + row] = acc[t][n][i];
+          if (row < N && tok < M) ws[((size_t)split * GV_MAX_ROWS + tok) * N + row] = acc[t][n][i];
         }
     __threadfence();
     __syncwarp();
@@ -388,10 +390,11 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_dense_kernel(
         for (int i = 0; i < 4; ++i) acc[t][n][i] = 0.f;
     // four splits per round, all their loads issued before any add (one L2 latency per
     // round, not per split); the adds keep split order, so the sum is reproducible
-    for (int q0 = 0; q0 < splits; q0 += 4) {
-      float pv[4][2][NT][4];
+    constexpr int QB = NT >= 4 ? 1 : 4;      // splits per round (register budget of 32-row tiles)
+    for (int q0 = 0; q0 < splits; q0 += QB) {
+      float pv[QB][2][NT][4];
 #pragma unroll
-      for (int qq = 0; qq < 4; ++qq)
+      for (int qq = 0; qq < QB; ++qq)
 #pragma unroll
         for (int t = 0; t < 2; ++t)
 #pragma unroll
@@ -401,11 +404,11 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_dense_kernel(
               const int row = rows[t] + g4 + (i >> 1) * 8;
               const int tok = n * 8 + 2 * tq + (i & 1);
               const int q = q0 + qq;
-              pv[qq][t][n][i] = (q < splits && row < N && tok < M) ? __ldcg(ws + ((size_t)q * 16 + tok) * N + row)
+              pv[qq][t][n][i] = (q < splits && row < N && tok < M) ? __ldcg(ws + ((size_t)q * GV_MAX_ROWS + tok) * N + row)
                                                                    : 0.f;
             }
 #pragma unroll
-      for (int qq = 0; qq < 4; ++qq)
+      for (int qq = 0; qq < QB; ++qq)
 #pragma unroll
         for (int t = 0; t < 2; ++t)
 #pragma unroll
@@ -1002,7 +1005,7 @@ static int gv_splits(int tiles, int S, int N, int slots) {
   if (tiles >= slots) return 1;
   int splits = slots / tiles;
   if (splits > 16) splits = 16;
-  while (splits > 1 && (S / splits < 2 || (long long)splits * 16 * N > GV_WS_PART_FLOATS)) --splits;
+  while (splits > 1 && (S / splits < 2 || (long long)splits * GV_MAX_ROWS * N > GV_WS_PART_FLOATS)) --splits;
   return splits;
 }
 
@@ -1027,10 +1030,10 @@ int xtu_gemv(const void* W, const float* wscale, int fp8, int N, int K, const vo
   const int x_f16s = (fp8 >> 2) & 1;
   fp8 &= 1;
   if (M <= 0 || N <= 0) return 0;
-  if (M > 16 || K % 16 != 0 || ws == nullptr || counters == nullptr) return -2;
+  if (M > GV_MAX_ROWS || K % 16 != 0 || ws == nullptr || counters == nullptr) return -2;
   if (K > GV_MAX_KBLK * 128) return -3;
   if (fp8 && (long long)M * K > GV_WS_X_HALVES) return -4;
-  const int nt = M > 8 ? 2 : 1;
+  const int nt = M > 16 ? 4 : M > 8 ? 2 : 1;
   const int tiles = (N + 31) / 32;
   const int S = gv_stages_per_tile(K, fp8 != 0);
   int launches = 1;
@@ -1062,15 +1065,19 @@ int xtu_gemv(const void* W, const float* wscale, int fp8, int N, int K, const vo
   const bool w2d = ((long long)K * (fp8 ? 1 : 2)) % 128 != 0;
   if (fp8) {
     if (w2d) {
-      if (nt == 1) XTU_GEMV_LAUNCH(true, 1, 2); else XTU_GEMV_LAUNCH(true, 2, 2);
+      if (nt == 1) XTU_GEMV_LAUNCH(true, 1, 2); else if (nt == 2) XTU_GEMV_LAUNCH(true, 2, 2);
+      else XTU_GEMV_LAUNCH(true, 4, 2);
     } else {
-      if (nt == 1) XTU_GEMV_LAUNCH(true, 1, 0); else XTU_GEMV_LAUNCH(true, 2, 0);
+      if (nt == 1) XTU_GEMV_LAUNCH(true, 1, 0); else if (nt == 2) XTU_GEMV_LAUNCH(true, 2, 0);
+      else XTU_GEMV_LAUNCH(true, 4, 0);
     }
   } else {
     if (w2d) {
-      if (nt == 1) XTU_GEMV_LAUNCH(false, 1, 2); else XTU_GEMV_LAUNCH(false, 2, 2);
+      if (nt == 1) XTU_GEMV_LAUNCH(false, 1, 2); else if (nt == 2) XTU_GEMV_LAUNCH(false, 2, 2);
+      else XTU_GEMV_LAUNCH(false, 4, 2);
     } else {
-      if (nt == 1) XTU_GEMV_LAUNCH(false, 1, 0); else XTU_GEMV_LAUNCH(false, 2, 0);
+      if (nt == 1) XTU_GEMV_LAUNCH(false, 1, 0); else if (nt == 2) XTU_GEMV_LAUNCH(false, 2, 0);
+      else XTU_GEMV_LAUNCH(false, 4, 0);
     }
   }
 #undef XTU_GEMV_LAUNCH

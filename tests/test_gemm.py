@@ -191,7 +191,7 @@ def test_grouped_gemm_prefill_scale(fp8):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("fp8", [False, True])
-@pytest.mark.parametrize("M", [1, 3, 4, 8, 13, 16])
+@pytest.mark.parametrize("M", [1, 3, 4, 8, 13, 16, 17, 20, 32])
 @pytest.mark.parametrize("N_,K", [(14336, 4096), (4096, 10944), (4096, 12288), (300, 512)])
 def test_gemv_decode(fp8, M, N_, K):
     """Includes shapes with few 32-row slices, which split K across CTAs (run twice: the

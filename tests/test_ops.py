@@ -108,7 +108,9 @@ def test_router(E, K, scoring, ng, tg):
 @pytest.mark.gpu
 @pytest.mark.parametrize("fmt", ["bf16", "fp8"])
 @pytest.mark.parametrize("T,E,K,H,I", [(1, 8, 2, 256, 512), (200, 16, 4, 512, 256), (33, 64, 8, 1024, 384),
-                                       (4, 128, 8, 4096, 1408), (16, 128, 8, 1024, 256), (5, 16, 8, 512, 384)])
+                                       (4, 128, 8, 4096, 1408), (16, 128, 8, 1024, 256), (5, 16, 8, 512, 384),
+                                       # verification-size batches: the gathered grouped GEMV (17..64 rows)
+                                       (20, 128, 8, 4096, 1408), (40, 16, 8, 1024, 256), (64, 8, 8, 512, 384)])
 def test_fused_moe(fmt, T, E, K, H, I):
     torch.manual_seed(3)
     x = torch.randn(T, H, device="cuda", dtype=torch.bfloat16)

@@ -524,6 +524,9 @@ OPS = {
     "kda_prefill": lambda a: bench_kda(),
     "cpu_bridge": lambda a: bench_cpu_bridge(),
     "moe_vs_reference": lambda a: [bench_moe_vs_reference(t) for t in a.sizes],
+    # the small-M range that speculative verification produces (C x (k + 1) rows), GLM-4.5-Air shapes
+    "moe_fp8_smallm": lambda a: [bench_moe(t, "fp8") for t in (4, 8, 16, 17, 20, 24, 32, 40, 64)],
+    "linear_fp8_smallm": lambda a: [bench_gemv(14336, 4096, t, "fp8") for t in (4, 16, 17, 20, 32, 40, 64)],
     # Qwen3-Next-shaped packed-4-bit decode MoE (512 experts top-10, H 2048, I 512)
     "moe_decode_mxfp4": lambda a: [bench_moe(t, "mxfp4", E=512, H=2048, I=512, K=10) for t in (1, 4, 16)],
     "moe_decode_nvfp4": lambda a: [bench_moe(t, "nvfp4", E=512, H=2048, I=512, K=10) for t in (1, 4, 16)],

@@ -59,13 +59,15 @@ def gemm_fp8w(a: torch.Tensor, w8: torch.Tensor, w_scale: torch.Tensor, out: tor
     return out
 
 
-GEMV_MAX_M = 16
+GEMV_MAX_M = 16          # rows of the token-direct decode forms (MoE, fused TP, norms' f16 copies)
+GEMV_MAX_M_DENSE = 32    # rows a plain dense GEMV call takes (speculative verification batches)
+GEMV_MAX_M_MOE = 64      # rows the gathered grouped MoE GEMV takes (<= 16 per expert per pass)
 
 
 def gemv(x: torch.Tensor, weight: torch.Tensor, scale: torch.Tensor | None = None, bias: torch.Tensor | None = None,
          out_dtype: torch.dtype = torch.bfloat16, out: torch.Tensor | None = None,
          x16: torch.Tensor | None = None) -> torch.Tensor:
-    """Decode-size y[M<=16, N] = x W^T (+ bias) streaming W (bf16 or e4m3 + block scales).
+    """Decode-size y[M<=32, N] = x W^T (+ bias) streaming W (bf16 or e4m3 + block scales).
     ``x16``: the same rows already as f16 x 2^-8 (fp8 weights then skip their conversion)."""
     x = tma_rows(x)
     M, K = x.shape
@@ -132,7 +134,7 @@ def linear(x: torch.Tensor, weight: torch.Tensor, scale: torch.Tensor | None = N
     if not x2.is_contiguous():
         x2 = x2.contiguous()
     K = x2.shape[1]
-    if x2.is_cuda and x2.shape[0] <= GEMV_MAX_M and K % 64 == 0 and x2.dtype == torch.bfloat16:
+    if x2.is_cuda and x2.shape[0] <= GEMV_MAX_M_DENSE and K % 64 == 0 and x2.dtype == torch.bfloat16:
         y = gemv(x2, weight, scale, bias, out_dtype, x16=x16)
         return y.reshape(*shp[:-1], weight.shape[0])
     if scale is None:

@@ -166,9 +166,12 @@ def moe_experts_partial(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tenso
     I = experts.inter
     # decode: weight-streaming grouped GEMV (gate/up + SwiGLU, down + weight + scatter); with
     # fp8 experts it reads the gathered rows as f16 x 2^-8, which the permute writes
-    gemv_path = (T <= G.GEMV_MAX_M and experts.interleaved and experts.fmt not in G.FP4_FMTS
+    # up to GEMV_MAX_M_MOE rows (speculative verification batches) the grouped GEMV streams
+    # each active expert's weights once per 16 of its rows; up to 16 rows in all it reads the
+    # step's tokens directly (token-direct form), above that the permute gathers them
+    gemv_path = (T <= G.GEMV_MAX_M_MOE and experts.interleaved and experts.fmt not in G.FP4_FMTS
                  and H % 128 == 0 and I % 128 == 0)   # whole 128-byte chunks per weight row
-    if gemv_path and E <= 1024:
+    if gemv_path and T <= G.GEMV_MAX_M and E <= 1024:
         # one-CTA permute (no row gather): the gate/up GEMV reads the T tokens directly
         # and keeps each expert's own columns through ws.tokrow
         xt = G.tma_rows(x)
@@ -214,7 +217,8 @@ def moe_experts_partial(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tenso
         N.call("xtu_moe_gemv", experts.w13.data_ptr(), N.ptr(experts.s13 if fp8 else None),
                experts.w2.data_ptr(), N.ptr(experts.s2 if fp8 else None), int(fp8), E, H, I, ws.xp.data_ptr(), f16s,
                H, None, 0, ws.seg.data_ptr(), ws.perm_slot.data_ptr(), ws.perm_w.data_ptr(), ws.h.data_ptr(),
-               ws.slots.data_ptr(), T, min(E, T * K), n, ws.active.data_ptr(), 0, float(act_limit), float(act_alpha),
+               ws.slots.data_ptr(), min(T, G.GEMV_MAX_M), min(E, T * K), n, ws.active.data_ptr(), 0,
+               float(act_limit), float(act_alpha),
                float(act_beta), None, None, None, None, 0, _gv_ws(x.device), N.status_buffer(x.device).data_ptr(), s)
         return None
     # the segment table of this call has E + 1 entries (the workspace may serve more experts)
