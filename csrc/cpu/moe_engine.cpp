@@ -69,13 +69,13 @@ static float w_at(const DotArgs& a, const RowRef& r, int k) {
   }
 }
 
-void dot_rows_scalar(const DotArgs& a, const RowRef* rows, int R, const float* X, int ldx, int T, float* acc) {
+void dot_rows_scalar(const DotArgs& a, const RowRef* rows, int R, const float* const* X, int T, float* acc) {
   for (int r = 0; r < R; ++r)
     for (int t = 0; t < T; ++t) acc[r * T + t] = 0.f;
   for (int k = 0; k < a.K; ++k)
     for (int r = 0; r < R; ++r) {
       const float w = w_at(a, rows[r], k);
-      for (int t = 0; t < T; ++t) acc[r * T + t] += w * X[(size_t)t * ldx + k];
+      for (int t = 0; t < T; ++t) acc[r * T + t] += w * X[t][k];
     }
 }
 
@@ -97,7 +97,7 @@ void quant_row_s8_pow2(const float* x, int K, int8_t* q, int8_t* e) {
   }
 }
 
-void dot_rows_w4a8_scalar(const RowRef* rows, int R, int K, const int8_t* xq, const int8_t* xe, int ldq, int T,
+void dot_rows_w4a8_scalar(const RowRef* rows, int R, int K, const int8_t* const* xq, const int8_t* const* xe, int T,
                           float* acc) {
   static const int w4t[16] = {0, 1, 2, 3, 4, 6, 8, 12, 0, -1, -2, -3, -4, -6, -8, -12};
   for (int r = 0; r < R; ++r)
@@ -108,9 +108,9 @@ void dot_rows_w4a8_scalar(const RowRef* rows, int R, int K, const int8_t* xq, co
         for (int i = 0; i < 32; ++i) {
           const int k = b * 32 + i;
           const uint8_t byte = rows[r].w[k >> 1];
-          dot += w4t[(k & 1) ? (byte >> 4) : (byte & 0xF)] * xq[(size_t)t * ldq + k];
+          dot += w4t[(k & 1) ? (byte >> 4) : (byte & 0xF)] * xq[t][k];
         }
-        s += std::ldexp((float)dot, (int)xe[(size_t)t * (ldq / 32) + b] + (int)rows[r].s[b] - 128);
+        s += std::ldexp((float)dot, (int)xe[t][b] + (int)rows[r].s[b] - 128);
       }
       acc[r * T + t] = s;
     }
@@ -166,6 +166,9 @@ class Engine {
          const float* gs13, const float* gs2)
       : cfg_(c), pool_(c.threads, c.deadline_ms) {
     avx512_ = cpu_has_avx512_bf16_vnni() && std::getenv("XTU_CPU_SCALAR") == nullptr;
+    // bf16 activations with vdpbf16ps unless XIAOTU_MOE_BF16DOT=0 (then fp32 FMAs on decoded weights)
+    const char* bd = std::getenv("XIAOTU_MOE_BF16DOT");
+    bf16dot_ = avx512_ && !(bd && bd[0] == '0');
     const int nn = pool_.num_nodes();
     shards_.resize(nn);
     const int H = c.H, I = c.I, E = c.E;
@@ -285,25 +288,30 @@ class Engine {
     std::vector<int> active;
     for (int e = 0; e < E; ++e)
       if (seg[e + 1] > seg[e]) active.push_back(e);
-    // 2) gathered fp32 activations (and s8 + exponents for the INT8 path)
-    xf_.resize((size_t)P * H);
-    for (int q = 0; q < P; ++q) {
-      const uint16_t* src = x + (size_t)ptok[q] * H;
-      float* dst = xf_.data() + (size_t)q * H;
-      for (int k = 0; k < H; ++k) {
-        const uint32_t u = (uint32_t)src[k] << 16;
-        std::memcpy(dst + k, &u, 4);
-      }
-    }
+    // 2) activations once per token (not per pair), converted / quantised in parallel:
+    // bf16 rows are read as they are by the BF16 dot kernels; the fp32 path and the INT8
+    // path (MXFP4 x s8) convert each token row once
     const bool int8 = cfg_.fmt == FMT_MXFP4 && H % 64 == 0 &&
                       (cfg_.int8_mode == 1 || (cfg_.int8_mode == 2 && M >= cfg_.int8_min_tokens));
-    if (int8) {
-      xq_.resize((size_t)P * H);
-      xe_.resize((size_t)P * H / 32);
-      for (int q = 0; q < P; ++q)
-        quant_row_s8_pow2(xf_.data() + (size_t)q * H, H, xq_.data() + (size_t)q * H, xe_.data() + (size_t)q * H / 32);
+    const bool dp = bf16dot_ && !int8 && H % 32 == 0 && I % 32 == 0;
+    if (!dp) {
+      xf_.resize((size_t)M * H);
+      if (int8) {
+        xq_.resize((size_t)M * H);
+        xe_.resize((size_t)M * H / 32);
+      }
+      parallel_rows(M, [&](int t) {
+        const uint16_t* src = x + (size_t)t * H;
+        float* dst = xf_.data() + (size_t)t * H;
+        for (int k = 0; k < H; ++k) {
+          const uint32_t u = (uint32_t)src[k] << 16;
+          std::memcpy(dst + k, &u, 4);
+        }
+        if (int8) quant_row_s8_pow2(dst, H, xq_.data() + (size_t)t * H, xe_.data() + (size_t)t * H / 32);
+      });
     }
-    hbuf_.resize((size_t)P * I);
+    if (dp) hb16_.resize((size_t)P * I);
+    else hbuf_.resize((size_t)P * I);
     const int nn = pool_.num_nodes();
     // 3) phase A: per node, tasks of 16 gate/up columns over all active experts
     std::vector<int> countsA(nn), countsB(nn);
@@ -330,11 +338,23 @@ class Engine {
           for (int q = q0; q < q1; q += 6) {
             const int T = std::min(6, q1 - q);
             float acc[4 * 6];
-            if (int8)
-              (avx512_ ? dot_rows_w4a8_avx512 : dot_rows_w4a8_scalar)(rows, 2 * nj, H, xq_.data() + (size_t)q * H,
-                                                                      xe_.data() + (size_t)q * H / 32, H, T, acc);
-            else
-              (avx512_ ? dot_rows_avx512 : dot_rows_scalar)(da, rows, 2 * nj, xf_.data() + (size_t)q * H, H, T, acc);
+            if (int8) {
+              const int8_t* xq[6];
+              const int8_t* xe[6];
+              for (int t = 0; t < T; ++t) {
+                xq[t] = xq_.data() + (size_t)ptok[q + t] * H;
+                xe[t] = xe_.data() + (size_t)ptok[q + t] * H / 32;
+              }
+              (avx512_ ? dot_rows_w4a8_avx512 : dot_rows_w4a8_scalar)(rows, 2 * nj, H, xq, xe, T, acc);
+            } else if (dp) {
+              const uint16_t* xr[6];
+              for (int t = 0; t < T; ++t) xr[t] = x + (size_t)ptok[q + t] * H;
+              dot_rows_bf16_avx512(da, rows, 2 * nj, xr, T, acc);
+            } else {
+              const float* xr[6];
+              for (int t = 0; t < T; ++t) xr[t] = xf_.data() + (size_t)ptok[q + t] * H;
+              (avx512_ ? dot_rows_avx512 : dot_rows_scalar)(da, rows, 2 * nj, xr, T, acc);
+            }
             for (int u = 0; u < nj; ++u)
               for (int t = 0; t < T; ++t) {
                 float gv = acc[(2 * u) * T + t], uv = acc[(2 * u + 1) * T + t];
@@ -343,7 +363,8 @@ class Engine {
                   uv = std::fmax(std::fmin(uv, cfg_.limit), -cfg_.limit);
                 }
                 const float h = (gv / (1.f + std::exp(-cfg_.alpha * gv))) * (uv + cfg_.beta);
-                hbuf_[(size_t)(q + t) * I + s.j0 + j + u] = h;
+                if (dp) hb16_[(size_t)(q + t) * I + s.j0 + j + u] = f32_to_bf16_rne(h);
+                else hbuf_[(size_t)(q + t) * I + s.j0 + j + u] = h;
               }
           }
         }
@@ -368,7 +389,15 @@ class Engine {
           for (int q = q0; q < q1; q += 6) {
             const int T = std::min(6, q1 - q);
             float acc[4 * 6];
-            (avx512_ ? dot_rows_avx512 : dot_rows_scalar)(da, rows, nr, hbuf_.data() + (size_t)q * I, I, T, acc);
+            if (dp) {
+              const uint16_t* hr[6];
+              for (int t = 0; t < T; ++t) hr[t] = hb16_.data() + (size_t)(q + t) * I;
+              dot_rows_bf16_avx512(da, rows, nr, hr, T, acc);
+            } else {
+              const float* hr[6];
+              for (int t = 0; t < T; ++t) hr[t] = hbuf_.data() + (size_t)(q + t) * I;
+              (avx512_ ? dot_rows_avx512 : dot_rows_scalar)(da, rows, nr, hr, T, acc);
+            }
             for (int u = 0; u < nr; ++u)
               for (int t = 0; t < T; ++t)
                 out[(size_t)ptok[q + t] * H + s.h0 + h + u] += pw[q + t] * acc[u * T + t];
@@ -386,7 +415,29 @@ class Engine {
   std::vector<NodeShard> shards_;
   std::vector<float> gs13_, gs2_;
   std::vector<float> xf_, hbuf_;
+  std::vector<uint16_t> hb16_;
   std::vector<int8_t> xq_, xe_;
+  bool bf16dot_ = false;
+
+  static uint16_t f32_to_bf16_rne(float f) {
+    uint32_t u;
+    std::memcpy(&u, &f, 4);
+    u += 0x7FFFu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+  }
+
+  // fn(t) for every token row t in [0, M), chunks of 8 rows dealt over the NUMA nodes' workers
+  template <typename F>
+  void parallel_rows(int M, F fn) {
+    const int nn = pool_.num_nodes();
+    const int chunks = (M + 7) / 8;
+    std::vector<int> counts(nn, 0);
+    for (int c = 0; c < chunks; ++c) ++counts[c % nn];
+    pool_.parallel_for_nodes(counts, [&](int n, int i) {
+      const int c = i * nn + n;
+      for (int t = c * 8; t < std::min(M, c * 8 + 8); ++t) fn(t);
+    });
+  }
 };
 
 }  // namespace xtu_cpu

@@ -34,16 +34,20 @@ struct DotArgs {
 float e4m3_to_f32(uint8_t b);
 float e2m1_to_f32(uint8_t nib);
 
-// acc[r * T + t] = sum_k W_r[k] * X[t * ldx + k]
-void dot_rows_scalar(const DotArgs& a, const RowRef* rows, int R, const float* X, int ldx, int T, float* acc);
-void dot_rows_avx512(const DotArgs& a, const RowRef* rows, int R, const float* X, int ldx, int T, float* acc);
+// acc[r * T + t] = sum_k W_r[k] * X[t][k]  (X[t]: pointer to activation row t, fp32)
+void dot_rows_scalar(const DotArgs& a, const RowRef* rows, int R, const float* const* X, int T, float* acc);
+void dot_rows_avx512(const DotArgs& a, const RowRef* rows, int R, const float* const* X, int T, float* acc);
+// the same with bf16 activation rows and AVX512-BF16 dot products (vdpbf16ps): each weight is
+// decoded to fp32 and rounded to bf16 (the value a GPU bf16 MMA of the widened weight uses),
+// products summed in fp32.  K % 32 == 0.
+void dot_rows_bf16_avx512(const DotArgs& a, const RowRef* rows, int R, const uint16_t* const* X, int T, float* acc);
 
 // INT8-activation x MXFP4 (W4A8): xq[t] = per-32 s8 activations with exponents xe[t][k/32]
 // (a = a8 * 2^c), weights w = (2*fp4) * 2^(b - 128).  acc[r*T+t] = sum of exact per-block
 // integer dots scaled by 2^(c + b - 128), accumulated in fp32.
-void dot_rows_w4a8_scalar(const RowRef* rows, int R, int K, const int8_t* xq, const int8_t* xe, int ldq, int T,
+void dot_rows_w4a8_scalar(const RowRef* rows, int R, int K, const int8_t* const* xq, const int8_t* const* xe, int T,
                           float* acc);
-void dot_rows_w4a8_avx512(const RowRef* rows, int R, int K, const int8_t* xq, const int8_t* xe, int ldq, int T,
+void dot_rows_w4a8_avx512(const RowRef* rows, int R, int K, const int8_t* const* xq, const int8_t* const* xe, int T,
                           float* acc);
 
 // per-32 power-of-two s8 quantisation of one activation row: c = ceil(log2(max|a| / 127))

@@ -53,7 +53,7 @@ inline __m512 decode16(const DotArgs& a, const RowRef& r, int k) {
 }
 
 template <int R, int T>
-void dot_rt(const DotArgs& a, const RowRef* rows, const float* X, int ldx, float* acc) {
+void dot_rt(const DotArgs& a, const RowRef* rows, const float* const* X, float* acc) {
   __m512 c[R][T];
 #pragma GCC unroll 4
   for (int r = 0; r < R; ++r)
@@ -65,7 +65,7 @@ void dot_rt(const DotArgs& a, const RowRef* rows, const float* X, int ldx, float
     for (int r = 0; r < R; ++r) w[r] = decode16(a, rows[r], k);
 #pragma GCC unroll 6
     for (int t = 0; t < T; ++t) {
-      const __m512 xv = _mm512_loadu_ps(X + (size_t)t * ldx + k);
+      const __m512 xv = _mm512_loadu_ps(X[t] + k);
 #pragma GCC unroll 4
       for (int r = 0; r < R; ++r) c[r][t] = _mm512_fmadd_ps(w[r], xv, c[r][t]);
     }
@@ -75,14 +75,54 @@ void dot_rt(const DotArgs& a, const RowRef* rows, const float* X, int ldx, float
 }
 
 template <int R>
-void dot_r(const DotArgs& a, const RowRef* rows, const float* X, int ldx, int T, float* acc) {
+void dot_r(const DotArgs& a, const RowRef* rows, const float* const* X, int T, float* acc) {
   switch (T) {
-    case 1: dot_rt<R, 1>(a, rows, X, ldx, acc); break;
-    case 2: dot_rt<R, 2>(a, rows, X, ldx, acc); break;
-    case 3: dot_rt<R, 3>(a, rows, X, ldx, acc); break;
-    case 4: dot_rt<R, 4>(a, rows, X, ldx, acc); break;
-    case 5: dot_rt<R, 5>(a, rows, X, ldx, acc); break;
-    default: dot_rt<R, 6>(a, rows, X, ldx, acc); break;
+    case 1: dot_rt<R, 1>(a, rows, X, acc); break;
+    case 2: dot_rt<R, 2>(a, rows, X, acc); break;
+    case 3: dot_rt<R, 3>(a, rows, X, acc); break;
+    case 4: dot_rt<R, 4>(a, rows, X, acc); break;
+    case 5: dot_rt<R, 5>(a, rows, X, acc); break;
+    default: dot_rt<R, 6>(a, rows, X, acc); break;
+  }
+}
+
+// 32 weights of row r from k (k % 32 == 0), decoded and rounded to bf16 pairs in k order
+inline __m512bh decode32_bf16(const DotArgs& a, const RowRef& r, int k) {
+  if (a.fmt == FMT_BF16) return (__m512bh)_mm512_loadu_si512(r.w + 2 * (size_t)k);
+  return _mm512_cvtne2ps_pbh(decode16(a, r, k + 16), decode16(a, r, k));
+}
+
+template <int R, int T>
+void dotbf_rt(const DotArgs& a, const RowRef* rows, const uint16_t* const* X, float* acc) {
+  __m512 c[R][T];
+#pragma GCC unroll 4
+  for (int r = 0; r < R; ++r)
+#pragma GCC unroll 6
+    for (int t = 0; t < T; ++t) c[r][t] = _mm512_setzero_ps();
+  for (int k = 0; k < a.K; k += 32) {
+    __m512bh w[R];
+#pragma GCC unroll 4
+    for (int r = 0; r < R; ++r) w[r] = decode32_bf16(a, rows[r], k);
+#pragma GCC unroll 6
+    for (int t = 0; t < T; ++t) {
+      const __m512bh xv = (__m512bh)_mm512_loadu_si512(X[t] + k);
+#pragma GCC unroll 4
+      for (int r = 0; r < R; ++r) c[r][t] = _mm512_dpbf16_ps(c[r][t], w[r], xv);
+    }
+  }
+  for (int r = 0; r < R; ++r)
+    for (int t = 0; t < T; ++t) acc[r * T + t] = _mm512_reduce_add_ps(c[r][t]);
+}
+
+template <int R>
+void dotbf_r(const DotArgs& a, const RowRef* rows, const uint16_t* const* X, int T, float* acc) {
+  switch (T) {
+    case 1: dotbf_rt<R, 1>(a, rows, X, acc); break;
+    case 2: dotbf_rt<R, 2>(a, rows, X, acc); break;
+    case 3: dotbf_rt<R, 3>(a, rows, X, acc); break;
+    case 4: dotbf_rt<R, 4>(a, rows, X, acc); break;
+    case 5: dotbf_rt<R, 5>(a, rows, X, acc); break;
+    default: dotbf_rt<R, 6>(a, rows, X, acc); break;
   }
 }
 
@@ -101,16 +141,25 @@ inline __m512i w4_64(const uint8_t* p) {
 
 }  // namespace
 
-void dot_rows_avx512(const DotArgs& a, const RowRef* rows, int R, const float* X, int ldx, int T, float* acc) {
+void dot_rows_avx512(const DotArgs& a, const RowRef* rows, int R, const float* const* X, int T, float* acc) {
   switch (R) {
-    case 1: dot_r<1>(a, rows, X, ldx, T, acc); break;
-    case 2: dot_r<2>(a, rows, X, ldx, T, acc); break;
-    case 3: dot_r<3>(a, rows, X, ldx, T, acc); break;
-    default: dot_r<4>(a, rows, X, ldx, T, acc); break;
+    case 1: dot_r<1>(a, rows, X, T, acc); break;
+    case 2: dot_r<2>(a, rows, X, T, acc); break;
+    case 3: dot_r<3>(a, rows, X, T, acc); break;
+    default: dot_r<4>(a, rows, X, T, acc); break;
   }
 }
 
-void dot_rows_w4a8_avx512(const RowRef* rows, int R, int K, const int8_t* xq, const int8_t* xe, int ldq, int T,
+void dot_rows_bf16_avx512(const DotArgs& a, const RowRef* rows, int R, const uint16_t* const* X, int T, float* acc) {
+  switch (R) {
+    case 1: dotbf_r<1>(a, rows, X, T, acc); break;
+    case 2: dotbf_r<2>(a, rows, X, T, acc); break;
+    case 3: dotbf_r<3>(a, rows, X, T, acc); break;
+    default: dotbf_r<4>(a, rows, X, T, acc); break;
+  }
+}
+
+void dot_rows_w4a8_avx512(const RowRef* rows, int R, int K, const int8_t* const* xq, const int8_t* const* xe, int T,
                           float* acc) {
   const __m512i ones = _mm512_set1_epi8(1);
   const __m512i bias = _mm512_set1_epi8((char)0x80);
@@ -122,11 +171,11 @@ void dot_rows_w4a8_avx512(const RowRef* rows, int R, int K, const int8_t* xq, co
       const __m512i sw = _mm512_dpbusd_epi32(_mm512_setzero_si512(), ones, w4);   // sum of w4 per lane
       const int b0 = rows[r].s[k >> 5], b1 = rows[r].s[(k >> 5) + 1];
       for (int t = 0; t < T; ++t) {
-        const int8_t* q = xq + (size_t)t * ldq + k;
+        const int8_t* q = xq[t] + k;
         const __m512i au8 = _mm512_xor_si512(_mm512_loadu_si512(q), bias);
         const __m512i d = _mm512_dpbusd_epi32(_mm512_setzero_si512(), au8, w4);
         const __m512i sg = _mm512_sub_epi32(d, _mm512_slli_epi32(sw, 7));      // exact sum a8 * w4 per lane
-        const int e0 = xe[(size_t)t * (ldq / 32) + (k >> 5)], e1 = xe[(size_t)t * (ldq / 32) + (k >> 5) + 1];
+        const int e0 = xe[t][k >> 5], e1 = xe[t][(k >> 5) + 1];
         const __m512 s = _mm512_mask_mov_ps(_mm512_set1_ps(std::ldexp(1.f, e0 + b0 - 128)), (__mmask16)0xFF00,
                                             _mm512_set1_ps(std::ldexp(1.f, e1 + b1 - 128)));
         c[t] = _mm512_fmadd_ps(_mm512_cvtepi32_ps(sg), s, c[t]);

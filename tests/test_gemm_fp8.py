@@ -63,6 +63,8 @@ def test_dense_fp8_native_matches_reference(M_, N_, K, bias):
     if b is not None:
         ref = ref + b.float()
     assert _rel(y, ref) < 1e-4
+    if G.linear_takes_gemv(M_):      # decode sizes stay on the bf16-activation GEMV
+        return
     # through G.linear (the model's entry point) in W8A8 mode: quantizes internally, bf16 out
     G.FP8_MMA = True
     try:

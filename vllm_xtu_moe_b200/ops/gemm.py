@@ -201,6 +201,11 @@ def fp8_native_ok(M: int, N_out: int, K: int, swiglu: bool = False) -> bool:
     return FP8_MMA and M > GEMV_MAX_M and K % 128 == 0 and (N_out % 256 == 0 if swiglu else N_out % 16 == 0)
 
 
+def linear_takes_gemv(M: int) -> bool:
+    """Whether G.linear serves an M-row call with the weight-streaming GEMV."""
+    return M <= GEMV_MAX_M_DENSE
+
+
 def gemm_fp8_native(aq: torch.Tensor, a_scale: torch.Tensor, w8: torch.Tensor, w_scale: torch.Tensor, *,
                     seg: torch.Tensor | None = None, tiles=None, epilogue: int = 0,
                     out: torch.Tensor | None = None, out_scale: torch.Tensor | None = None,
