@@ -87,23 +87,34 @@ class GatedDeltaNet:
         a = bav[:, :, r:].reshape(T, nv)
         return q, k, v, z, b, a
 
+    def _f32(self, name: str, t: torch.Tensor, device) -> torch.Tensor:
+        """fp32 contiguous copy of a small parameter, made once per device."""
+        c = getattr(self, name, None)
+        if c is None or c.device != device:
+            c = t.float().contiguous().to(device)
+            setattr(self, name, c)
+        return c
+
     def __call__(self, x: torch.Tensor, meta: AttnMetadata, kv, rope) -> torch.Tensor:
         state: DeltaNetState = kv
         T = x.shape[0]
         qkvz = self.in_qkvz(x)
         ba = self.in_ba(x)
+        if x.is_cuda and N.has_symbol("xtu_deltanet_fwd") and self.dk == 128:
+            # gates, conv, recurrence and gated RMSNorm in the deltanet kernels
+            from ..ops.deltanet import deltanet_fwd
+            d = x.device
+            y = deltanet_fwd(qkvz.contiguous(), self._f32("_conv_w32", self.conv_w, d), None, None, meta, state,
+                             self.nk, self.nv, self.dk, self.dv, ba=ba.contiguous(),
+                             A_log32=self._f32("_A_log32", self.A_log, d),
+                             dt_bias32=self._f32("_dt_bias32", self.dt_bias, d),
+                             norm_w32=self._f32("_norm_w32", self.norm_w, d), eps=self.cfg.norm_eps)
+            return self.out(y)
         q, k, v, z, b, a = self._split(qkvz, ba)
         beta = torch.sigmoid(b.float())
         g = -torch.exp(self.A_log.float()) * F.softplus(a.float() + self.dt_bias.float())
-        if x.is_cuda and N.has_symbol("xtu_deltanet_fwd") and self.dk == 128:
-            from ..ops.deltanet import deltanet_fwd
-            if getattr(self, "_conv_w32", None) is None or self._conv_w32.device != x.device:
-                self._conv_w32 = self.conv_w.float().contiguous()
-            o = deltanet_fwd(qkvz.contiguous(), self._conv_w32, g, beta, meta, state, self.nk, self.nv, self.dk,
-                             self.dv)
-        else:
-            mixed = torch.cat([q, k, v], dim=-1)        # [T, channels]
-            o = self._core(mixed, g, beta, meta, state)  # [T, nv, dv] fp32
+        mixed = torch.cat([q, k, v], dim=-1)        # [T, channels]
+        o = self._core(mixed, g, beta, meta, state)  # [T, nv, dv] fp32
         o = self._gated_norm(o, z)
         return self.out(o.reshape(T, self.nv * self.dv))
 
@@ -139,6 +150,8 @@ class KimiDeltaAttention:
         self.nk, self.nv = cfg.linear_num_key_heads, cfg.linear_num_value_heads
         self.dk, self.dv = cfg.linear_key_head_dim, cfg.linear_value_head_dim
 
+    _f32 = GatedDeltaNet._f32
+
     def decay(self, x: torch.Tensor) -> torch.Tensor:
         """g [T, nv, dk] fp32."""
         T = x.shape[0]
@@ -154,11 +167,14 @@ class KimiDeltaAttention:
         g = self.decay(x)
         gate = self.g_b(self.g_a(x)).view(T, self.nv, self.dv)
         if x.is_cuda and N.has_symbol("xtu_deltanet_fwd") and self.dk == 128:
+            # conv, recurrence and the sigmoid-gated RMSNorm in the deltanet kernels
             from ..ops.deltanet import deltanet_fwd
-            if getattr(self, "_conv_w32", None) is None or self._conv_w32.device != x.device:
-                self._conv_w32 = self.conv_w.float().contiguous()
-            o = deltanet_fwd(qkv.contiguous(), self._conv_w32, g.contiguous(), beta, meta, state, self.nk, self.nv,
-                             self.dk, self.dv, blocked=True)
+            d = x.device
+            y = deltanet_fwd(qkv.contiguous(), self._f32("_conv_w32", self.conv_w, d), g.contiguous(), beta, meta,
+                             state, self.nk, self.nv, self.dk, self.dv, blocked=True,
+                             norm_w32=self._f32("_norm_w32", self.norm_w, d), eps=self.cfg.norm_eps,
+                             gate=gate.reshape(T, self.nv * self.dv).contiguous())
+            return self.out(y)
         else:
             if x.is_cuda and N.native_required() and self.dk == 128:
                 raise N.NativeLibraryMissing("xtu_deltanet_fwd missing from the CUDA library")

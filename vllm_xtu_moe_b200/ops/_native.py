@@ -55,7 +55,7 @@ _SIGS: dict[str, list] = {
                             c_float, c_float, c_float, P, c_int, P, P],
     "xtu_spec_chain_meta": [P, P, P, c_int, c_int, c_int, c_int, c_int, P, P, P, P],
     "xtu_deltanet_fwd": [P, c_int, c_int, c_int, P, P, P, c_int, c_int, c_int, c_int, c_int, P, P, P, P, P,
-                         P, P, P, P, c_int, c_int, P],
+                         P, P, P, P, c_int, c_int, c_int, P, P, c_int, P, P, P, c_int, c_int, P, c_float, P, P],
     "xtu_grouped_gemm_ex": [P, P, P, P, c_int, P, c_int, c_int, c_int, c_int, c_int, P, P, c_int, c_int, P, P,
                             c_float, c_float, c_float, P, c_int, P, P],
     "xtu_ipc_handle_size": [],
@@ -186,7 +186,8 @@ def status_buffer(device: torch.device | int | None = None) -> torch.Tensor:
                        (device if isinstance(device, int) else (device.index or 0)))
     t = _status.get(dev.index)
     if t is None:
-        t = torch.zeros(4, dtype=torch.int32, device=dev)
+        with torch.inference_mode(False):      # a process-lifetime buffer, not an inference tensor
+            t = torch.zeros(4, dtype=torch.int32, device=dev)
         _status[dev.index] = t
     return t
 
@@ -197,10 +198,13 @@ def check_status(device=None, reset: bool = True) -> None:
     vals = st.tolist()
     if vals[0] != 0:
         if reset:
-            st.zero_()
-            from . import attention, gemm   # a stopped launch may have left counters set
-            gemm.gemv_ws_reset(st.device)
-            attention.split_counters_reset(st.device)
+            # the buffers may have been made inside an inference-mode region (an engine
+            # step); in-place resets of both kinds of tensor are allowed in inference mode
+            with torch.inference_mode():
+                st.zero_()
+                from . import attention, gemm   # a stopped launch may have left counters set
+                gemm.gemv_ws_reset(st.device)
+                attention.split_counters_reset(st.device)
         raise RuntimeError(
             f"xtu kernel error: {ERROR_NAMES.get(vals[0], vals[0])} (site {vals[1]}, block {vals[2]}, extra {vals[3]})")
 
