@@ -63,6 +63,13 @@ def parse():
     ap.add_argument("--no-sweep", action="store_true", help="skip the C = 1/2/4 rounds after the timed steps")
     ap.add_argument("--layers", type=int, default=None, help="debug only: fewer layers (invalidates the number)")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--tiered", action="store_true",
+                    help="experts held once in host DRAM (CPU engine per rank), a hot-expert pool of "
+                         "--pool-experts per layer in HBM, prefill through the streamed expert ring, decode "
+                         "through the asynchronous CPU bridge with expert deferral (VLLM_EXPERTS_LOAD_DEVICE=cpu)")
+    ap.add_argument("--pool-experts", type=int, default=32, help="--tiered: hot-pool experts per MoE layer")
+    ap.add_argument("--zipf", type=float, default=1.1,
+                    help="--tiered: Zipf(s) expert-popularity bias of the router (0 = unbiased random router)")
     return ap.parse_args()
 
 
@@ -199,14 +206,35 @@ def main():
                       num_spec=k, num_blocks=max_c * per_seq_blocks)
     t0 = time.time()
     max_rows = max(args.max_batched_tokens, max_c * (1 + k))
+    tiering = order = None
+    if args.tiered:
+        import dataclasses
+        from vllm_xtu_moe_b200.config import get_engine_config
+        from vllm_xtu_moe_b200.tiering.executor import TieredExperts
+        from vllm_xtu_moe_b200.tiering.skew import zipf_order
+        moe_layers = [i for i in range(cfg.num_layers + cfg.num_mtp_layers) if cfg.is_moe_layer(i)]
+        order = zipf_order(cfg.num_experts, moe_layers, seed=1234) if args.zipf > 0 else None
+        # the hot pool seeded with each layer's most popular experts (a PIN table profiled on
+        # this traffic); it keeps adapting to the observed routes
+        pool = {l: order[l][: args.pool_experts] for l in moe_layers} if order else args.pool_experts
+        ec = dataclasses.replace(get_engine_config(), experts_load_device="cpu", moe_async=True, moe_defer=True)
+        threads = max(1, (os.cpu_count() or 1) // world)
+        tiering = TieredExperts(cfg, device=dev, engine_config=ec, resident_layers=set(), pool_experts=pool,
+                                ring=True, max_tokens=args.max_batched_tokens, bridge_tokens=max(64, max_rows),
+                                threads=threads)
     if world > 1:
         from vllm_xtu_moe_b200.parallel.tp import TPReducer, build_tp_model
         reducer = TPReducer(max_rows, cfg.hidden_size, device=dev, mode="fused")
-        model = build_tp_model(cfg, rank, world, dev, seed=1234, reducer=reducer, num_layers=args.layers)
+        model = build_tp_model(cfg, rank, world, dev, seed=1234, reducer=reducer, num_layers=args.layers,
+                               tiering=tiering)
     else:
         reducer = None
-        model = build_model(cfg, device=dev, seed=1234, num_layers=args.layers)
-    llm = LLM(model, device=str(dev), runner_config=rc)
+        model = build_model(cfg, device=dev, seed=1234, num_layers=args.layers,
+                            expert_sink=tiering.expert_sink if tiering is not None else None)
+    if order is not None:
+        from vllm_xtu_moe_b200.tiering.skew import apply_zipf_router_bias
+        apply_zipf_router_bias(model, order, s=args.zipf)
+    llm = LLM(model, device=str(dev), runner_config=rc, tiering=tiering)
     torch.cuda.synchronize()
     init_s = time.time() - t0
     # the same prompts on every rank: one model instance serves them (tensor parallel)
@@ -339,6 +367,12 @@ def main():
                "h2d_bytes_per_step": round((r.h2d_bytes - b_in0) / n_st),
                "d2h_bytes_per_step": round((r.d2h_bytes - b_out0) / n_st)}
 
+    tier_stats = None
+    if tiering is not None:
+        tier_stats = tiering.stats(hit_rate=True)
+        if tiering.ring is not None:
+            tier_stats["ring_gib_streamed"] = round(tiering.ring.copied_bytes / 2**30, 1)
+
     # ---- aggregate over ranks: every rank serves the same C requests; take the slowest
     mean_pre = sum(pre_ms) / len(pre_ms)
     mean_dec = sum(dec_ms) / len(dec_ms)
@@ -373,12 +407,19 @@ def main():
                                        "RMSNorm reduction, one-/two-shot all-reduce); NCCL for set-up only"
                                        if world > 1 else "none"),
                        "weights": f"experts {cfg.expert_fmt}, dense {cfg.dense_fmt}, block 128x128",
-                       "experts_placement": "GPU-resident (all experts fit in HBM)",
+                       "experts_placement": (
+                           f"host DRAM once per rank (CPU engine, {tiering.threads} threads), hot pool "
+                           f"{args.pool_experts}/{cfg.num_experts} experts per layer in HBM, prefill through the "
+                           f"streamed expert ring, decode via the async CPU bridge with deferral; router "
+                           f"Zipf({args.zipf}) popularity bias" if tiering is not None
+                           else "GPU-resident (all experts fit in HBM)"),
                        "mtp_draft_tokens": k, "max_batched_tokens": args.max_batched_tokens,
                        "l2": "inputs larger than L2 (weights + KV cache read every step); no flush",
                        "layers": args.layers or cfg.num_layers},
             "clocks": clocks, "e2e": e2e, "gpu_launches": launches, "init_s": round(init_s, 1),
         }
+        if tiering is not None:
+            line["tiering"] = tier_stats
         if args.layers:
             line["invalid"] = "debug run with fewer layers"
         print(json.dumps(line), flush=True)

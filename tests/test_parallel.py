@@ -222,6 +222,34 @@ def test_tensor_parallel_matches_single_rank_cpu(name):
     mp.spawn(_tp_cpu_worker, args=(2, _port(), name), nprocs=2)
 
 
+def _tp_tiered_cpu_worker(rank, world, port):
+    from vllm_xtu_moe_b200.models.model import build_model
+    from vllm_xtu_moe_b200.parallel.tp import TPReducer, build_tp_model
+    from vllm_xtu_moe_b200.tiering.executor import TieredExperts
+    _init(rank, world, port, "gloo")
+    cfg = _tp_cfg("glm-4.5-air").replace(expert_fmt="fp8")
+    ref = build_model(cfg, device="cpu", seed=4)
+    ref.act_dtype = torch.float32
+    red = TPReducer(256, cfg.hidden_size, mode="nccl")
+    tier = TieredExperts(cfg, device="cpu", resident_layers=set(), threads=2)
+    m = build_tp_model(cfg, rank, world, "cpu", seed=4, reducer=red, tiering=tier)
+    m.act_dtype = torch.float32
+    ex = [l.mlp.executor for l in m.layers if getattr(l.mlp, "executor", None) is not None]
+    assert ex and all(e.lo == rank * cfg.num_experts // world and e.engine.E == cfg.num_experts // world for e in ex)
+    a, b = _tp_logits(ref, "cpu"), _tp_logits(m, "cpu")
+    assert sum(e.calls["cpu"] for e in ex) == 0       # host tensors take the engine directly
+    err = (a - b).abs().max().item() / a.abs().max().item()
+    assert err < 3e-2, err
+    tier.shutdown()
+    dist.destroy_process_group()
+
+
+def test_tensor_parallel_with_cpu_tier_matches_single_rank():
+    """Each of 2 ranks keeps its half of the routed experts in its own CPU engine (expert
+    parallel tiers under tensor-parallel attention); the reduced logits match one resident rank."""
+    mp.spawn(_tp_tiered_cpu_worker, args=(2, _port()), nprocs=2)
+
+
 def _tp_gpu_worker(rank, world, port, mode="p2p"):
     from vllm_xtu_moe_b200.engine import LLM, SamplingParams
     from vllm_xtu_moe_b200.engine.runner import RunnerConfig

@@ -600,3 +600,71 @@ def test_pool_hit_share():
     assert pool_hits({0: 5, 3: 2, 7: 3}, [3, 7]) == (5, 10)
     assert pool_hits([1, 0, 4, 0], [2]) == (4, 5)
     assert pool_hits({}, [1]) == (0, 0)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("path", ["hybrid", "cpu", "async", "ring"])
+def test_expert_parallel_share_on_tiers(path):
+    """One expert-parallel rank's share (global experts 16..31 of 32) on the tiers: pairs
+    routed to other ranks' experts are skipped by every path (pool split, CPU engine through
+    either bridge, streamed ring), and the rank's partial equals the GPU-resident share's."""
+    from vllm_xtu_moe_b200.config import EngineConfig
+    from vllm_xtu_moe_b200.tiering.executor import TieredExperts
+    fmt, E, H, I, K, lo = "fp8", 32, 512, 256, 4, 16
+    cfg = _mini(fmt).replace(num_experts=E, top_k=K, hidden_size=H, moe_intermediate=I)
+    raw = _raw_gpu(fmt, E, H, I, 5)
+    share = {k: (v[lo:].contiguous() if isinstance(v, torch.Tensor) else v) for k, v in raw.items()}
+    ec = EngineConfig(stage_tile_e=6, stage_nslots=2, moe_async=path == "async")
+    pool = {1: [3, 17, 20, 29]} if path in ("hybrid", "async") else {}
+    tier = TieredExperts(cfg, device="cuda", engine_config=ec, resident_layers=set(), pool_experts=pool,
+                         ring=path == "ring", gpu_prefill_min_tokens=32, max_tokens=1024)
+    _live.append(tier)
+    assert tier.expert_sink(1, share, lo=lo) is None
+    cu = lambda k: share[k].cuda() if k in share else None
+    res = M.prepare_experts(fmt, cu("w13"), cu("w2"), cu("s13"), cu("s2"))
+
+    class Blk:
+        experts = None
+        executor = None
+        expert_lo = lo
+
+    Blk.cfg = cfg
+    blk = Blk()
+
+    class Mdl:
+        layers = [type("L", (), {"mlp": blk})()]
+        mtp = []
+
+    tier.attach(Mdl)
+    T = 48 if path == "ring" else 6
+    ids, w = _routes(T, E, K, 9)
+    x = (torch.randn(T, H, generator=torch.Generator().manual_seed(4)) * 0.5).to(torch.bfloat16).cuda()
+    ids, w = ids.cuda(), w.cuda()
+    ref = M.fused_moe(x, ids, w, res, lo=lo).float()
+    y = blk.executor(blk, x, ids, w, None)
+    torch.cuda.synchronize()
+    ok, err = _close(y, ref)
+    assert ok, err
+    if path == "hybrid":
+        assert blk.executor.pool.nslots == 3          # global 17, 20, 29 -> local 1, 4, 13
+    assert tier.stats()[path] >= 1
+
+
+def test_zipf_router_bias_skews_selection():
+    """The benchmark's Zipf(1.1) router bias: seeded per-layer popularity order, the hottest
+    quarter of the experts takes most routed pairs, selection weights stay the router's."""
+    from vllm_xtu_moe_b200.models.model import build_model
+    from vllm_xtu_moe_b200.tiering.skew import apply_zipf_router_bias, zipf_order
+    cfg = _mini("bf16").replace(num_experts=32, top_k=4)
+    m = build_model(cfg, device="cpu", seed=2)
+    blk = m.layers[1].mlp
+    x = torch.randn(512, cfg.hidden_size).to(torch.bfloat16)
+    ids0, _ = blk.route(x)
+    order = zipf_order(32, [1], seed=5)
+    assert order == zipf_order(32, [1], seed=5) and sorted(order[1]) == list(range(32))
+    apply_zipf_router_bias(m, order, s=1.1)
+    ids1, w1 = blk.route(x)
+    hot = torch.tensor(order[1][:8])
+    share = lambda ids: torch.isin(ids, hot).float().mean().item()
+    assert share(ids0) < 0.45 and share(ids1) > 0.6, (share(ids0), share(ids1))
+    assert torch.allclose(w1.sum(1), torch.ones(512), atol=1e-4) or not cfg.norm_topk_prob

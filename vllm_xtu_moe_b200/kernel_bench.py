@@ -339,11 +339,79 @@ def bench_deltanet(T=15000, nk=16, nv=32, dk=128, dv=128, kw=4, iters=3) -> dict
                         positions=torch.zeros(T, dtype=torch.int32, device=d), max_q_len=T, max_kv_len=T,
                         is_decode=False, seq_slots=torch.zeros(1, dtype=torch.int32, device=d),
                         seq_fresh=torch.ones(1, dtype=torch.int32, device=d))
-    fn = lambda: deltanet_fwd(qkvz, conv_w, g, beta, meta, st, nk, nv, dk, dv)
+    fn = lambda: deltanet_fwd(qkvz, conv_w, g, beta, meta, st, nk, nv, dk, dv, chunked=True)
     ms = time_fn(fn, iters)
+    serial = lambda: deltanet_fwd(qkvz, conv_w, g, beta, meta, st, nk, nv, dk, dv, chunked=False)
+    ms_serial = time_fn(serial, iters)
     flops = T * nv * dk * dv * 2 * 4
     nbytes = qkvz.numel() * 2 + T * nv * dv * 4
-    return _report("deltanet_prefill", dict(T=T, nk=nk, nv=nv, dk=dk, dv=dv), ms, nbytes, flops)
+    r = _report("deltanet_prefill", dict(T=T, nk=nk, nv=nv, dk=dk, dv=dv), ms, nbytes, flops)
+    r.update({"token_serial_ms": round(ms_serial, 3), "speedup_vs_token_serial": round(ms_serial / ms, 2)})
+    return r
+
+
+def bench_ring(T=16384, E=128, H=4096, I=1408, K=8, tile_e=16, nslots=2, iters=3) -> dict:
+    """Streamed prefill ring on one GLM-4.5-Air-shaped fp8 MoE layer held by the CPU engine:
+    the ring's host-link rate against a pinned ``cudaMemcpyAsync`` of the same bytes in this
+    run, and its copy / compute overlap.  ``ring_ms``: one layer through the ring (device
+    time on the compute stream); ``copy_ms``: the same expert copies alone on the ring's
+    copy stream; ``compute_ms``: the layer with every expert GPU-resident;
+    ``overlap`` = (copy_ms + compute_ms - ring_ms) / min(copy_ms, compute_ms) (1 = the
+    shorter of the two fully hidden)."""
+    from .ops.quant import quant_fp8_block
+    from .tiering.cpu_engine import CpuExpertEngine
+    from .tiering.host import HostExperts
+    from .tiering.ring import ExpertRing
+    g = torch.Generator(device="cuda").manual_seed(0)
+    q13, s13, q2, s2 = [], [], [], []
+    for e0 in range(0, E, 16):          # quantize on the GPU in slices, keep the host copy
+        n = min(16, E - e0)
+        a, sa = quant_fp8_block(torch.randn(n, 2 * I, H, device="cuda", generator=g) * 0.02)
+        b, sb = quant_fp8_block(torch.randn(n, H, I, device="cuda", generator=g) * 0.02)
+        q13.append(a.cpu()); s13.append(sa.cpu()); q2.append(b.cpu()); s2.append(sb.cpu())
+    q13, s13, q2, s2 = torch.cat(q13), torch.cat(s13), torch.cat(q2), torch.cat(s2)
+    eng = CpuExpertEngine("fp8", q13, q2, s13, s2)
+    host = HostExperts(eng, HostExperts.gpu_scales_from_checkpoint("fp8", s13, s2))
+    res = M.prepare_experts("fp8", q13.cuda(), q2.cuda(), s13.cuda(), s2.cuda())
+    del q13, q2
+    ring = ExpertRing("fp8", H, I, tile_e, nslots, "cuda")
+    x = (torch.randn(T, H, device="cuda", generator=g) * 0.5).to(torch.bfloat16)
+    logits = torch.randn(T, E, device="cuda", generator=g)
+    ids, w = router_topk(logits, K)
+    ws = M.MoEWorkspace(T, K, E, H, I, "cuda")
+    nbytes = E * host.expert_bytes()
+    # pinned host -> device peak of this box: one copy of the layer's bytes
+    src = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    dst = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    peak_ms = time_fn(lambda: dst.copy_(src, non_blocking=True), iters, flush=False)
+    del src, dst
+    slots = ring.slots[0]
+
+    def copies():
+        st = ring.copy_stream
+        st.wait_stream(torch.cuda.current_stream())
+        for e in range(E):
+            host.copy_slot(e, slots, e % tile_e, st)
+        torch.cuda.current_stream().wait_stream(st)
+
+    copy_ms = time_fn(copies, iters, flush=False)
+    compute_ms = time_fn(lambda: M.fused_moe(x, ids, w, res, ws), iters)
+    ring_ms = time_fn(lambda: ring.run_layer(host, x, ids, w, ws), iters)
+    out_ring = ring.run_layer(host, x, ids, w, ws).float()
+    out_res = M.fused_moe(x, ids, w, res, ws).float()
+    rel = float((out_ring - out_res).norm() / out_res.norm())
+    host.close()
+    eng.close()
+    gb = nbytes / 1e9
+    r = {"op": "ring_prefill_fp8", "shape": dict(T=T, E=E, H=H, I=I, K=K, tile_e=tile_e, nslots=nslots),
+         "layer_gb": round(gb, 3), "pinned_copy_gbs": round(gb / (peak_ms * 1e-3), 1),
+         "copy_ms": round(copy_ms, 3), "copy_gbs": round(gb / (copy_ms * 1e-3), 1),
+         "copy_frac_of_pinned": round(peak_ms / copy_ms, 3), "compute_ms": round(compute_ms, 3),
+         "ring_ms": round(ring_ms, 3), "ring_gbs": round(gb / (ring_ms * 1e-3), 1),
+         "ring_frac_of_pinned": round(peak_ms / ring_ms, 3),
+         "overlap": round((copy_ms + compute_ms - ring_ms) / min(copy_ms, compute_ms), 3),
+         "prefill_tok_s_per_layer": round(T / (ring_ms * 1e-3), 1), "rel_diff_vs_resident": round(rel, 5)}
+    return r
 
 
 def bench_kda(T=15000, nh=32, dk=128, dv=128, kw=4, iters=3) -> dict:
@@ -507,21 +575,22 @@ def bench_cpu_bridge(layers=46, T=1, E=8, H=4096, I=256, K=2, reps=20) -> dict:
 
 
 OPS = {
-    "moe_prefill_fp8": lambda a: bench_moe(a.tokens, "fp8"),
-    "moe_prefill_bf16": lambda a: bench_moe(a.tokens, "bf16"),
+    "moe_prefill_fp8": lambda a: bench_moe(a.tokens or 8192, "fp8"),
+    "moe_prefill_bf16": lambda a: bench_moe(a.tokens or 8192, "bf16"),
     "moe_decode_fp8": lambda a: bench_moe(4, "fp8"),
     "gemv_fp8": lambda a: bench_gemv(14336, 4096, 4, "fp8"),
     "gemv_fp8_oproj": lambda a: bench_gemv(4096, 12288, 4, "fp8"),
-    "gemm_fp8": lambda a: bench_gemm(a.tokens, 14336, 4096, "fp8"),
-    "gemm_bf16": lambda a: bench_gemm(a.tokens, 14336, 4096, "bf16"),
+    "gemm_fp8": lambda a: bench_gemm(a.tokens or 8192, 14336, 4096, "fp8"),
+    "gemm_bf16": lambda a: bench_gemm(a.tokens or 8192, 14336, 4096, "bf16"),
     "attention_decode": lambda a: bench_attn_decode(),
     "mla_decode": lambda a: bench_mla_decode(),
-    "attention_prefill": lambda a: bench_attn_prefill(min(a.tokens, 16384)),
+    "attention_prefill": lambda a: bench_attn_prefill(min(a.tokens or 8192, 16384)),
     "rmsnorm": lambda a: bench_rmsnorm(),
     "tp_fused": lambda a: bench_tp_fused(),
     "ep_fused": lambda a: bench_ep_fused(),
-    "deltanet_prefill": lambda a: bench_deltanet(),
-    "kda_prefill": lambda a: bench_kda(),
+    "deltanet_prefill": lambda a: bench_deltanet(T=a.tokens or 15000),
+    "kda_prefill": lambda a: bench_kda(T=a.tokens or 15000),
+    "ring_prefill": lambda a: [bench_ring(T=t) for t in ((a.tokens,) if a.tokens else (4096, 16384))],
     "cpu_bridge": lambda a: bench_cpu_bridge(),
     "moe_vs_reference": lambda a: [bench_moe_vs_reference(t) for t in a.sizes],
     # the small-M range that speculative verification produces (C x (k + 1) rows), GLM-4.5-Air shapes
@@ -537,7 +606,7 @@ OPS = {
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--op", default="all", choices=["all"] + list(OPS))
-    ap.add_argument("--tokens", type=int, default=8192)
+    ap.add_argument("--tokens", type=int, default=None, help="token count of the prefill ops (op default)")
     ap.add_argument("--sizes", default="1,4,16,512,2048,8192",
                     help="token counts of the moe_vs_reference sweep")
     a = ap.parse_args(argv)

@@ -373,8 +373,14 @@ class TPRowLinear:
 
 
 def build_tp_model(cfg: ModelConfig, rank: int, tp: int, device, seed: int = 0, source=None,
-                   reducer: TPReducer | None = None, num_layers: int | None = None):
-    """This rank's shard of the model (random init or ``source``) with the reducer installed."""
+                   reducer: TPReducer | None = None, num_layers: int | None = None, tiering=None):
+    """This rank's shard of the model (random init or ``source``) with the reducer installed.
+
+    ``tiering`` (a :class:`~vllm_xtu_moe_b200.tiering.executor.TieredExperts` of this rank):
+    the rank's E / tp routed experts of every MoE layer go to its tiers (CPU engine, hot
+    pool, ring) instead of HBM; each layer's executor serves only the pairs routed to the
+    rank's experts, and the layer's partial joins the attention / shared-expert partials in
+    the same reduction, as the GPU-resident experts do."""
     base = source if source is not None else WeightFactory(seed, device)
     f = TPWeightFactory(base, cfg, rank, tp)
     lcfg = local_config(cfg, tp)
@@ -382,6 +388,8 @@ def build_tp_model(cfg: ModelConfig, rank: int, tp: int, device, seed: int = 0, 
 
     def sink(layer, raw):
         lo_by_layer.setdefault(layer, []).append(f.expert_lo)
+        if tiering is not None:
+            return tiering.expert_sink(layer, raw, lo=f.expert_lo)
         from ..ops import moe as M
         return M.prepare_experts(raw["fmt"], raw["w13"], raw["w2"], raw.get("s13"), raw.get("s2"),
                                  raw.get("gs13"), raw.get("gs2"))
@@ -394,5 +402,7 @@ def build_tp_model(cfg: ModelConfig, rank: int, tp: int, device, seed: int = 0, 
             l.attn.o = TPRowLinear(l.attn.o, reducer)   # GQA / MLA output projection
         if isinstance(l.mlp, MoEBlock):
             l.mlp.expert_lo = rank * El
+    if tiering is not None:
+        tiering.attach(m)
     m.tp = (rank, tp)
     return m

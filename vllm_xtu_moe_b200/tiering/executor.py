@@ -45,9 +45,12 @@ GPU_FMTS = ("bf16", "fp8", "mxfp4", "nvfp4")
 
 class LayerExecutor:
     def __init__(self, owner: "TieredExperts", layer: int, engine: CpuExpertEngine, host: HostExperts | None,
-                 pool: LayerPool | None):
+                 pool: LayerPool | None, lo: int = 0):
         self.owner, self.layer = owner, layer
         self.engine, self.host, self.pool = engine, host, pool
+        # global id of this tier's first expert: under expert parallelism a rank holds the
+        # experts [lo, lo + E) and leaves every other pair to the rank that owns it
+        self.lo = lo
         self.bridge: CpuBridge | None = None
         self.calls = {"ring": 0, "hybrid": 0, "cpu": 0, "async": 0, "deferred": 0}
         self.is_mtp = False
@@ -63,7 +66,7 @@ class LayerExecutor:
         act = block.cfg.swiglu_limit
         T, H = x.shape
         if not x.is_cuda:
-            y = self._cpu_deferred(self.engine.forward(x, ids, w), T)
+            y = self._cpu_deferred(self.engine.forward(x, ids, w, lo=self.lo), T)
             if sh is not None:
                 y = y + sh.float()
             return y.to(x.dtype)
@@ -74,7 +77,7 @@ class LayerExecutor:
         if (o.ring is not None and self.host is not None and not capturing and T >= o.gpu_prefill_min_tokens):
             self.calls["ring"] += 1
             return o.ring.run_layer(self.host, x, ids, w, o.workspace(T, ids.shape[1], x.device), shared=sh,
-                                    act_limit=act)
+                                    act_limit=act, lo=self.lo)
         if o.use_async and T <= o.bridge_tokens:
             return self._async(x, ids, w, sh, act)
         extra = torch.empty(T, H, dtype=torch.float32, device=x.device)
@@ -83,7 +86,7 @@ class LayerExecutor:
             self.calls["hybrid"] += 1
             gpu_ids = torch.empty_like(ids)
             cpu_ids = torch.empty_like(ids)
-            M.route_split(ids, self.pool.slotmap, 0, gpu_ids, cpu_ids, self.pool.hits)
+            M.route_split(ids, self.pool.slotmap, self.lo, gpu_ids, cpu_ids, self.pool.hits)
             self._cpu(x, cpu_ids, w, extra, main, T)
             ws = o.pool_workspace(T, ids.shape[1], self.pool.nslots, x.device)
             M.moe_experts_partial(x, gpu_ids, w, self.pool.slots, ws, lo=0, act_limit=act)
@@ -126,14 +129,14 @@ class LayerExecutor:
         pool = self.pool if self.pool is not None and self.pool.nslots > 0 else None
         if pool is not None:
             gpu_ids, cpu_ids = torch.empty_like(ids), torch.empty_like(ids)
-            M.route_split(ids, pool.slotmap, 0, gpu_ids, cpu_ids, pool.hits)
+            M.route_split(ids, pool.slotmap, self.lo, gpu_ids, cpu_ids, pool.hits)
         else:
             gpu_ids, cpu_ids = ids, ids
         prev = o.defer_pending
         if prev is not None and prev != T:               # left by an aborted forward: drop it
             br.wait(torch.empty(prev, H, dtype=torch.float32, device=x.device))
             prev = None
-        br.post(x, cpu_ids, w, engine=self.engine_index)
+        br.post(x, cpu_ids, w, engine=self.engine_index, lo=self.lo, hi=self.lo + self.engine.E)
         if pool is not None:
             ws = o.pool_workspace(T, K, pool.nslots, x.device)
             M.moe_experts_partial(x, gpu_ids, w, pool.slots, ws, lo=0, act_limit=act)
@@ -160,12 +163,12 @@ class LayerExecutor:
         o = self.owner
         o.side.wait_stream(main)
         if T <= o.bridge_tokens:
-            self._bridge(ids.shape[1]).enqueue(x, ids, w, extra, 0, self.engine.E, stream=o.side)
+            self._bridge(ids.shape[1]).enqueue(x, ids, w, extra, self.lo, self.lo + self.engine.E, stream=o.side)
         else:
             if torch.cuda.is_current_stream_capturing():
                 raise RuntimeError("CPU expert call above the bridge's token limit inside graph capture")
             with torch.cuda.stream(o.side):
-                y = self.engine.forward(x.cpu(), ids.cpu(), w.cpu())
+                y = self.engine.forward(x.cpu(), ids.cpu(), w.cpu(), lo=self.lo)
                 extra.copy_(y, non_blocking=False)
 
 
@@ -208,7 +211,7 @@ class TieredExperts:
         self.gpu_prefill_min_tokens = (ec.gpu_prefill_min_tokens if gpu_prefill_min_tokens is None
                                        else gpu_prefill_min_tokens)
         self.threads = ec.moe_threads if threads is None else threads
-        self._pending: list[tuple[int, CpuExpertEngine, HostExperts | None, LayerPool | None]] = []
+        self._pending: list[tuple[int, CpuExpertEngine, HostExperts | None, LayerPool | None, int]] = []
         self.executors: list[LayerExecutor] = []
         self.ring: ExpertRing | None = None
         self._ws: dict = {}
@@ -222,13 +225,17 @@ class TieredExperts:
         self._last_main: LayerExecutor | None = None
 
     # ---------------------------------------------------------------- build
-    def _pool_list(self, layer: int) -> list[int]:
+    def _pool_list(self, layer: int, lo: int, E: int) -> list[int]:
+        """This tier's pool experts of `layer` as local indices (the PIN table names global ids;
+        an int asks for the first N experts of the tier)."""
         p = self.pool_experts
         if isinstance(p, int):
-            return list(range(min(p, self.cfg.num_experts)))
-        return list(p.get(layer, []))
+            return list(range(min(p, E)))
+        return [e - lo for e in p.get(layer, []) if lo <= e < lo + E]
 
-    def expert_sink(self, layer: int, raw: dict):
+    def expert_sink(self, layer: int, raw: dict, lo: int = 0):
+        """Routed experts of one layer (checkpoint layout).  ``lo``: global id of the first
+        expert in ``raw`` (a tensor / expert parallel rank's share starts at rank * E / world)."""
         fmt = raw["fmt"]
         if layer in self.resident:
             e = M.prepare_experts(fmt, raw["w13"], raw["w2"], raw.get("s13"), raw.get("s2"), raw.get("gs13"),
@@ -245,15 +252,15 @@ class TieredExperts:
             scales = HostExperts.gpu_scales_from_checkpoint(fmt, _cpu(raw.get("s13")), _cpu(raw.get("s2")),
                                                             _cpu(raw.get("gs13")), _cpu(raw.get("gs2")))
             host = HostExperts(eng, scales)
-            experts = self._pool_list(layer)
+            experts = self._pool_list(layer, lo, int(raw["w13"].shape[0]))
             if experts:
                 pool = LayerPool(host, experts, self.device, window=self.ec.pin_window if not self.ec.pin_static
                                  else 0, hyst=self.ec.pin_hyst, maxswap=self.ec.pin_maxswap)
             if self.want_ring and self.ring is None:
-                te = max(1, min(self.ec.stage_tile_e, c.num_experts))
+                te = max(1, min(self.ec.stage_tile_e, int(raw["w13"].shape[0])))
                 self.ring = ExpertRing(fmt, c.hidden_size, c.moe_intermediate, te, max(2, self.ec.stage_nslots),
                                        self.device)
-        self._pending.append((layer, eng, host, pool))
+        self._pending.append((layer, eng, host, pool, lo))
         return None
 
     def attach(self, model) -> None:
@@ -261,9 +268,9 @@ class TieredExperts:
         n_main = len(model.layers)
         it = iter(self._pending)
         for i, b in enumerate(blocks):
-            if getattr(b, "experts", "dense") is None:
-                layer, eng, host, pool = next(it)
-                ex = LayerExecutor(self, layer, eng, host, pool)
+            if getattr(b, "experts", "dense") is None and getattr(b, "executor", None) is None:
+                layer, eng, host, pool, lo = next(it)
+                ex = LayerExecutor(self, layer, eng, host, pool, lo)
                 ex.is_mtp = i >= n_main
                 b.executor = ex
                 self.executors.append(ex)

@@ -35,8 +35,10 @@ class ExpertRing:
         self.copied_bytes = 0
 
     def run_layer(self, host: HostExperts, x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor,
-                  ws: M.MoEWorkspace, *, shared=None, act_limit=0.0, out=None) -> torch.Tensor:
-        """All routed experts of one layer through the ring; returns the combined output."""
+                  ws: M.MoEWorkspace, *, shared=None, act_limit=0.0, out=None, lo: int = 0) -> torch.Tensor:
+        """All routed experts of one layer through the ring; returns the combined output.
+        ``lo``: global id of the host tier's first expert (pairs outside [lo, lo + E) are
+        another rank's)."""
         E = host.E
         main = torch.cuda.current_stream()
         ntiles = (E + self.tile_e - 1) // self.tile_e
@@ -56,6 +58,6 @@ class ExpertRing:
             cut = lambda t: None if t is None else t[:n]
             view = slot if n == self.tile_e else M.ExpertWeights(
                 slot.fmt, slot.w13[:n], slot.w2[:n], cut(slot.s13), cut(slot.s2), True, cut(slot.gs13), cut(slot.gs2))
-            M.moe_experts_partial(x, ids, weights, view, ws, lo=e0, act_limit=act_limit)
+            M.moe_experts_partial(x, ids, weights, view, ws, lo=lo + e0, act_limit=act_limit)
             self.free[s].record(main)
-        return M.moe_combine(ws, ids, 0, E, shared=shared, out=out)
+        return M.moe_combine(ws, ids, lo, lo + E, shared=shared, out=out)
