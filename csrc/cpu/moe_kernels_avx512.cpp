@@ -86,9 +86,43 @@ void dot_r(const DotArgs& a, const RowRef* rows, const float* const* X, int T, f
   }
 }
 
-// 32 weights of row r from k (k % 32 == 0), decoded and rounded to bf16 pairs in k order
+// e2m1 codes as bf16 bit patterns, twice (entries 0..15 and 16..31 of a vpermw table)
+const uint16_t kE2M1Bf16[32] = {0x0000, 0x3F00, 0x3F80, 0x3FC0, 0x4000, 0x4040, 0x4080, 0x40C0,
+                                0x8000, 0xBF00, 0xBF80, 0xBFC0, 0xC000, 0xC040, 0xC080, 0xC0C0,
+                                0x0000, 0x3F00, 0x3F80, 0x3FC0, 0x4000, 0x4040, 0x4080, 0x40C0,
+                                0x8000, 0xBF00, 0xBF80, 0xBFC0, 0xC000, 0xC040, 0xC080, 0xC0C0};
+
+// 16 bytes of packed e2m1 -> 32 word indices in k order (low nibble = even k)
+inline __m512i nibble_words32(const uint8_t* p) {
+  const __m512i b = _mm512_cvtepu8_epi32(_mm_loadu_si128(reinterpret_cast<const __m128i*>(p)));
+  return _mm512_or_si512(_mm512_and_si512(b, _mm512_set1_epi32(0x0F)),
+                         _mm512_slli_epi32(_mm512_and_si512(b, _mm512_set1_epi32(0xF0)), 12));
+}
+
+// 32 weights of row r from k (k % 32 == 0), decoded and rounded to bf16 pairs in k order.
+// Packed 4-bit rows decode through a 32-entry bf16 table (vpermw) that already holds the
+// block scale: MXFP4 adds the power-of-two scale to the exponent field of the nonzero
+// codes (exact); NVFP4 scales the 16 codes of each of its two 16-element blocks in fp32
+// and rounds them to bf16 once per block.
 inline __m512bh decode32_bf16(const DotArgs& a, const RowRef& r, int k) {
   if (a.fmt == FMT_BF16) return (__m512bh)_mm512_loadu_si512(r.w + 2 * (size_t)k);
+  if (a.fmt == FMT_MXFP4) {
+    const int e = (int)r.s[k >> 5] - 127;
+    if (e >= -120 && e <= 120) {
+      const __m512i base = _mm512_loadu_si512(kE2M1Bf16);
+      const __m512i lut = _mm512_mask_add_epi16(base, (__mmask32)0xFEFEFEFEu, base, _mm512_set1_epi16((short)(e << 7)));
+      return (__m512bh)_mm512_permutexvar_epi16(nibble_words32(r.w + (k >> 1)), lut);
+    }
+  } else if (a.fmt == FMT_NVFP4) {
+    const __m512 codes = _mm512_loadu_ps(kE2M1);
+    const float s0 = e4m3_to_f32(r.s[k >> 4]) * a.gscale, s1 = e4m3_to_f32(r.s[(k >> 4) + 1]) * a.gscale;
+    const __m512i lut = (__m512i)_mm512_cvtne2ps_pbh(_mm512_mul_ps(codes, _mm512_set1_ps(s1)),
+                                                     _mm512_mul_ps(codes, _mm512_set1_ps(s0)));
+    // weights k+16 .. k+31 (words 16..31) read the second block's half of the table
+    const __m512i idx = _mm512_mask_add_epi16(nibble_words32(r.w + (k >> 1)), (__mmask32)0xFFFF0000u,
+                                              nibble_words32(r.w + (k >> 1)), _mm512_set1_epi16(16));
+    return (__m512bh)_mm512_permutexvar_epi16(idx, lut);
+  }
   return _mm512_cvtne2ps_pbh(decode16(a, r, k + 16), decode16(a, r, k));
 }
 

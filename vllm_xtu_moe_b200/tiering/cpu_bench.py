@@ -38,19 +38,19 @@ def _ref_module():
     return xiaotu_moe, xiaotu_moe.load()
 
 
-def _weights(fmt: str, E: int, H: int, I: int, seed: int = 0):
+def _weights(fmt: str, E: int, H: int, I: int, seed: int = 0, slice_e: int = 8):
+    """Random experts quantized to `fmt`, a few experts at a time (the quantizers' fp32
+    temporaries of a whole layer would not fit a small host)."""
+    from ..ops.quant import quant_fp8_block, quant_mxfp4
+    quant = quant_fp8_block if fmt == "fp8" else quant_mxfp4
     g = torch.Generator().manual_seed(seed)
-    w13 = torch.randn(E, 2 * I, H, generator=g) * 0.02
-    w2 = torch.randn(E, H, I, generator=g) * 0.02
-    if fmt == "fp8":
-        from ..ops.quant import quant_fp8_block
-        q13, s13 = quant_fp8_block(w13)
-        q2, s2 = quant_fp8_block(w2)
-        return q13, q2, s13, s2
-    from ..ops.quant import quant_mxfp4
-    p13, s13 = quant_mxfp4(w13)
-    p2, s2 = quant_mxfp4(w2)
-    return p13, p2, s13, s2
+    parts = []
+    for e0 in range(0, E, slice_e):
+        n = min(slice_e, E - e0)
+        p13, s13 = quant(torch.randn(n, 2 * I, H, generator=g) * 0.02)
+        p2, s2 = quant(torch.randn(n, H, I, generator=g) * 0.02)
+        parts.append((p13, p2, s13, s2))
+    return tuple(torch.cat([p[i] for p in parts]) for i in range(4))
 
 
 def _time(fn, reps: int) -> float:
