@@ -68,6 +68,8 @@ def parse():
                          "--pool-experts per layer in HBM, prefill through the streamed expert ring, decode "
                          "through the asynchronous CPU bridge with expert deferral (VLLM_EXPERTS_LOAD_DEVICE=cpu)")
     ap.add_argument("--pool-experts", type=int, default=32, help="--tiered: hot-pool experts per MoE layer")
+    ap.add_argument("--kv-cache-dtype", default="bf16", choices=["bf16", "fp8"],
+                    help="KV cache storage: bf16, or e4m3 with per-layer scales (decode reads half the bytes)")
     ap.add_argument("--zipf", type=float, default=1.1,
                     help="--tiered: Zipf(s) expert-popularity bias of the router (0 = unbiased random router)")
     return ap.parse_args()
@@ -203,7 +205,7 @@ def main():
     rc = RunnerConfig(block_size=bs, max_seqs=max_c, max_batched_tokens=args.max_batched_tokens,
                       max_model_len=P + O + 64, use_cuda_graph=True,
                       graph_batch_sizes=tuple(b for b in (1, 2, 4, 8, 16, 32, 64) if b <= max_c) or (1,),
-                      num_spec=k, num_blocks=max_c * per_seq_blocks)
+                      num_spec=k, num_blocks=max_c * per_seq_blocks, kv_cache_dtype=args.kv_cache_dtype)
     t0 = time.time()
     max_rows = max(args.max_batched_tokens, max_c * (1 + k))
     tiering = order = None
@@ -414,6 +416,7 @@ def main():
                            f"Zipf({args.zipf}) popularity bias" if tiering is not None
                            else "GPU-resident (all experts fit in HBM)"),
                        "mtp_draft_tokens": k, "max_batched_tokens": args.max_batched_tokens,
+                       "kv_cache_dtype": args.kv_cache_dtype,
                        "l2": "inputs larger than L2 (weights + KV cache read every step); no flush",
                        "layers": args.layers or cfg.num_layers},
             "clocks": clocks, "e2e": e2e, "gpu_launches": launches, "init_s": round(init_s, 1),

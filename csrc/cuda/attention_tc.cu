@@ -605,7 +605,7 @@ int attn_decode_gqa(const CUtensorMap& tk, const CUtensorMap& tv, const void* q,
                     int o_stride, const int* q_start, const int* kv_len, const int* block_table, int bt_stride,
                     int B, int max_q_len, int T, int Hq, int Hkv, int D, float scale, int splits, float* ws_o,
                     float* ws_lse, int* counters, int num_blocks, int window, const float* sinks, void* status,
-                    cudaStream_t s);
+                    cudaStream_t s, int kv_fp8 = 0, float k_scale = 1.f, float v_scale = 1.f);
 }  // namespace xtu
 
 using namespace xtu;

@@ -13,6 +13,7 @@
 //   * greedy argmax and embedding gather
 // All kernels vectorise to 16-byte accesses where the row length allows.
 #include <cuda_bf16.h>
+#include <cuda_fp8.h>
 #include <cuda_runtime.h>
 #include <cstdint>
 #include <cfloat>
@@ -205,6 +206,8 @@ __global__ void __launch_bounds__(NT) tp_sum_rmsnorm_kernel(
 // q [T, Hq, D] (row stride q_stride), k [T, Hk, D], v [T, Hk, Dv] (strides given)
 // cos_sin [max_pos, rot] fp32: first rot/2 = cos, next rot/2 = sin.
 // Cache layout: [num_blocks, Hk, block_size, D] bf16; slot = block*block_size + offset.
+// kv_fp8: e4m3 caches (saturating), K [num_blocks, Hk, block_size, D] times k_inv and V
+// stored transposed per block, [num_blocks, Hk, Dv, block_size], times v_inv.
 // One warp per (token, head); heads [0,Hq) are q, [Hq, Hq+Hk) are k (+v copy).
 // ---------------------------------------------------------------------------
 __global__ void rope_kv_kernel(__nv_bfloat16* __restrict__ q, __nv_bfloat16* __restrict__ k,
@@ -213,8 +216,9 @@ __global__ void rope_kv_kernel(__nv_bfloat16* __restrict__ q, __nv_bfloat16* __r
                                int neox, int q_stride, int k_stride, int v_stride,
                                const __nv_bfloat16* __restrict__ q_norm_w, const __nv_bfloat16* __restrict__ k_norm_w,
                                float norm_eps, int norm_add_one, const int* __restrict__ slot_mapping,
-                               __nv_bfloat16* __restrict__ k_cache, __nv_bfloat16* __restrict__ v_cache,
-                               int block_size, long long num_slots, XtuStatus* st) {
+                               void* __restrict__ k_cache, void* __restrict__ v_cache,
+                               int block_size, long long num_slots, XtuStatus* st, int kv_fp8, float k_inv,
+                               float v_inv) {
   griddep_wait();   // launched with PDL: nothing upstream is touched before this
   griddep_launch_dependents();
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -265,11 +269,20 @@ __global__ void rope_kv_kernel(__nv_bfloat16* __restrict__ q, __nv_bfloat16* __r
     if (slot >= 0 && XTU_IN_BOUNDS(slot < num_slots, st, 220, slot) && slot < num_slots) {
       const int hk = h - Hq;
       const int blk = slot / block_size, off = slot - blk * block_size;
-      __nv_bfloat16* kc = k_cache + (((size_t)blk * Hk + hk) * block_size + off) * D;
-      for (int j = lane; j < D; j += 32) kc[j] = ptr[j];
       const __nv_bfloat16* vr = v + (size_t)t * v_stride + (size_t)hk * Dv;
-      __nv_bfloat16* vc = v_cache + (((size_t)blk * Hk + hk) * block_size + off) * Dv;
-      for (int j = lane; j < Dv; j += 32) vc[j] = vr[j];
+      if (kv_fp8) {
+        uint8_t* kc = static_cast<uint8_t*>(k_cache) + (((size_t)blk * Hk + hk) * block_size + off) * D;
+        for (int j = lane; j < D; j += 32)
+          kc[j] = __nv_cvt_float_to_fp8(__bfloat162float(ptr[j]) * k_inv, __NV_SATFINITE, __NV_E4M3);
+        uint8_t* vc = static_cast<uint8_t*>(v_cache) + ((size_t)blk * Hk + hk) * Dv * block_size + off;
+        for (int j = lane; j < Dv; j += 32)
+          vc[(size_t)j * block_size] = __nv_cvt_float_to_fp8(__bfloat162float(vr[j]) * v_inv, __NV_SATFINITE, __NV_E4M3);
+      } else {
+        __nv_bfloat16* kc = static_cast<__nv_bfloat16*>(k_cache) + (((size_t)blk * Hk + hk) * block_size + off) * D;
+        for (int j = lane; j < D; j += 32) kc[j] = ptr[j];
+        __nv_bfloat16* vc = static_cast<__nv_bfloat16*>(v_cache) + (((size_t)blk * Hk + hk) * block_size + off) * Dv;
+        for (int j = lane; j < Dv; j += 32) vc[j] = vr[j];
+      }
     }
   }
 }
@@ -901,7 +914,8 @@ int xtu_tp_sum_rmsnorm(const void* recv, long long slot, int world, int T, int H
 int xtu_rope_kv(void* q, void* k, const void* v, const int* positions, const float* cos_sin, int T, int Hq, int Hk,
                 int D, int Dv, int rot, int neox, int q_stride, int k_stride, int v_stride, const void* q_norm_w,
                 const void* k_norm_w, float norm_eps, int norm_add_one, const int* slot_mapping, void* k_cache,
-                void* v_cache, int block_size, long long num_slots, void* status, cudaStream_t s) {
+                void* v_cache, int block_size, long long num_slots, void* status, int kv_fp8, float k_inv,
+                float v_inv, cudaStream_t s) {
   if (T <= 0) return 0;
   if (D % 32 != 0 || D > 512 || rot > D) return -2;
   const int warps = T * (Hq + Hk);
@@ -910,8 +924,7 @@ int xtu_rope_kv(void* q, void* k, const void* v, const int* positions, const flo
   launch_pdl(rope_kv_kernel, dim3(blocks), dim3(threads), 0, s, (__nv_bfloat16*)q, (__nv_bfloat16*)k,
              (const __nv_bfloat16*)v, positions, cos_sin, T, Hq, Hk, D, Dv, rot, neox, q_stride, k_stride, v_stride,
              (const __nv_bfloat16*)q_norm_w, (const __nv_bfloat16*)k_norm_w, norm_eps, norm_add_one, slot_mapping,
-             (__nv_bfloat16*)k_cache, (__nv_bfloat16*)v_cache, block_size, num_slots,
-             reinterpret_cast<XtuStatus*>(status));
+             k_cache, v_cache, block_size, num_slots, reinterpret_cast<XtuStatus*>(status), kv_fp8, k_inv, v_inv);
   return rc_last();
 }
 

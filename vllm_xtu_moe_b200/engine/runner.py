@@ -47,6 +47,8 @@ class RunnerConfig:
     # reuse the KV blocks of a cached prompt prefix (models without linear-attention
     # state or a sliding-window pool, whose per-request state a shared prefix cannot carry)
     prefix_caching: bool = False
+    # "bf16" or "fp8" (e4m3, per-layer K / V scales; GQA layers -- MLA latents stay bf16)
+    kv_cache_dtype: str = "bf16"
 
 
 class ModelRunner:
@@ -68,12 +70,14 @@ class ModelRunner:
                          if has_swa and rc.swa_bounded else 0)
         if rc.num_blocks <= 0:
             rc.num_blocks = self._auto_blocks()
-        self.caches = model.allocate_caches(rc.num_blocks, rc.block_size, rc.max_seqs, swa_blocks=rc.swa_blocks)
+        self.caches = model.allocate_caches(rc.num_blocks, rc.block_size, rc.max_seqs, swa_blocks=rc.swa_blocks,
+                                            kv_dtype=rc.kv_cache_dtype)
         if rc.swa_blocks:
             for l in model.layers:
                 if getattr(l.attn, "window", 0) > 0:
                     l.attn.bounded = True
-        self.mtp_caches = model.allocate_mtp_caches(rc.num_blocks, rc.block_size, rc.max_seqs) if model.mtp else []
+        self.mtp_caches = (model.allocate_mtp_caches(rc.num_blocks, rc.block_size, rc.max_seqs,
+                                                     kv_dtype=rc.kv_cache_dtype) if model.mtp else [])
         max_rows = max(rc.max_batched_tokens, rc.max_seqs * (1 + rc.num_spec))
         model.prepare_workspaces(max_rows)
         self.graphs: dict[int, tuple] = {}
@@ -85,11 +89,13 @@ class ModelRunner:
 
     # ------------------------------------------------------------------
     def _auto_blocks(self) -> int:
-        per_tok = max(1, self.model.kv_bytes_per_token(skip_swa=self.rc.swa_blocks > 0))
+        per_tok = max(1, self.model.kv_bytes_per_token(skip_swa=self.rc.swa_blocks > 0,
+                                                       kv_dtype=self.rc.kv_cache_dtype))
         if self.model.mtp:
             c = self.model.cfg
             last = c.num_layers - 1     # MTP layers: the last decoder layer's attention type
-            per_tok += len(self.model.mtp) * ((c.kv_heads(last) * (c.head_dim + c.gqa_v_dim) * 2) if not c.is_mla
+            gb = 1 if self.rc.kv_cache_dtype == "fp8" else 2
+            per_tok += len(self.model.mtp) * ((c.kv_heads(last) * (c.head_dim + c.gqa_v_dim) * gb) if not c.is_mla
                                               else (c.kv_lora_rank + c.qk_rope_head_dim) * 2)
         need = self.rc.max_seqs * self.max_blocks_per_seq
         if not self.cuda:

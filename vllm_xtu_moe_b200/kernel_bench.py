@@ -259,24 +259,31 @@ def _cache(Bn, kv, Hkv, D, bs=64):
     return kc, vc, bt
 
 
-def bench_attn_decode(Bn=4, kv=15000, Hq=96, Hkv=8, D=128, iters=20) -> dict:
+def bench_attn_decode(Bn=4, kv=15000, Hq=96, Hkv=8, D=128, ql=1, kv_dtype="bf16", iters=20) -> dict:
+    """GQA decode attention over the paged cache: ``ql`` query positions per sequence (5 =
+    an MTP k=4 verification step), bf16 or fp8 (e4m3) cache."""
     kc, vc, bt = _cache(Bn, kv, Hkv, D)
-    q = (torch.randn(Bn, Hq, D, device="cuda") * 0.5).to(torch.bfloat16)
+    if kv_dtype == "fp8":
+        from .ops.basic import to_e4m3
+        kc = to_e4m3(kc, 1.0)
+        vc = to_e4m3(vc.transpose(2, 3).contiguous(), 1.0)
+    T = Bn * ql
+    q = (torch.randn(T, Hq, D, device="cuda") * 0.5).to(torch.bfloat16)
     d = "cuda"
-    meta = AttnMetadata(num_seqs=Bn, q_start=torch.arange(Bn + 1, dtype=torch.int32, device=d),
+    meta = AttnMetadata(num_seqs=Bn, q_start=torch.arange(0, T + 1, ql, dtype=torch.int32, device=d),
                         kv_len=torch.full((Bn,), kv, dtype=torch.int32, device=d), block_table=bt,
-                        slot_mapping=torch.zeros(Bn, dtype=torch.int32, device=d),
-                        positions=torch.full((Bn,), kv - 1, dtype=torch.int32, device=d), max_q_len=1,
+                        slot_mapping=torch.zeros(T, dtype=torch.int32, device=d),
+                        positions=torch.full((T,), kv - 1, dtype=torch.int32, device=d), max_q_len=ql,
                         max_kv_len=kv, is_decode=True)
     meta.num_splits = A.choose_splits(Bn, Hkv, kv, ctas_per_sm=2 if D in (64, 128) else 1)
-    ws = torch.empty(A.num_split_workspace(Bn, Hq, D, meta.num_splits), dtype=torch.float32, device=d)
-    out = torch.empty(Bn, Hq, D, dtype=torch.bfloat16, device=d)
+    ws = torch.empty(A.num_split_workspace(T, Hq, D, meta.num_splits), dtype=torch.float32, device=d)
+    out = torch.empty(T, Hq, D, dtype=torch.bfloat16, device=d)
     fn = lambda: A.paged_attention(q, kc, vc, meta, out=out, workspace=ws)
     ms = time_fn(fn, iters)
-    nbytes = 2 * Bn * kv * Hkv * D * 2
-    flops = 4 * Bn * kv * Hq * D
-    return _report("attention_decode", dict(B=Bn, kv=kv, Hq=Hq, Hkv=Hkv, D=D, splits=meta.num_splits), ms,
-                   nbytes, flops)
+    nbytes = 2 * Bn * kv * Hkv * D * (1 if kv_dtype == "fp8" else 2)
+    flops = 4 * T * kv * Hq * D
+    return _report("attention_decode", dict(B=Bn, kv=kv, Hq=Hq, Hkv=Hkv, D=D, q_len=ql, kv_dtype=kv_dtype,
+                                            splits=meta.num_splits), ms, nbytes, flops)
 
 
 def bench_mla_decode(Bn=4, kv=15000, Hq=128, iters=20) -> dict:
@@ -582,7 +589,7 @@ OPS = {
     "gemv_fp8_oproj": lambda a: bench_gemv(4096, 12288, 4, "fp8"),
     "gemm_fp8": lambda a: bench_gemm(a.tokens or 8192, 14336, 4096, "fp8"),
     "gemm_bf16": lambda a: bench_gemm(a.tokens or 8192, 14336, 4096, "bf16"),
-    "attention_decode": lambda a: bench_attn_decode(),
+    "attention_decode": lambda a: [bench_attn_decode(ql=ql, kv_dtype=kd) for kd in ("bf16", "fp8") for ql in (1, 5)],
     "mla_decode": lambda a: bench_mla_decode(),
     "attention_prefill": lambda a: bench_attn_prefill(min(a.tokens or 8192, 16384)),
     "rmsnorm": lambda a: bench_rmsnorm(),

@@ -81,6 +81,9 @@ class GQAAttention:
         self.bounded = False        # set by the runner when this window layer has its own bounded pool
         self.sinks = sinks.float().contiguous() if sinks is not None else None
         self.scale = 1.0 / math.sqrt(self.hd)
+        # dequantisation scales of an fp8 KV cache (checkpoint k_scale / v_scale; 1 by default)
+        self.k_scale = 1.0
+        self.v_scale = 1.0
 
     def __call__(self, x: torch.Tensor, meta: AttnMetadata, kv: tuple, rope: torch.Tensor) -> torch.Tensor:
         T = x.shape[0]
@@ -105,8 +108,10 @@ class GQAAttention:
             meta = dataclasses.replace(meta, block_table=meta.swa_block_table, slot_mapping=meta.swa_slot_mapping)
         B.rope_and_cache(q, k, v, meta.positions, rope, self.cfg.rot_dim, self.cfg.rope_neox,
                          slot_mapping=meta.slot_mapping, k_cache=k_cache, v_cache=v_cache, q_norm_w=self.q_norm,
-                         k_norm_w=self.k_norm, norm_eps=self.cfg.norm_eps, norm_add_one=self.cfg.norm_add_one)
-        o = paged_attention(q, k_cache, v_cache, meta, self.scale, window=self.window, sinks=self.sinks)
+                         k_norm_w=self.k_norm, norm_eps=self.cfg.norm_eps, norm_add_one=self.cfg.norm_add_one,
+                         k_scale=self.k_scale, v_scale=self.v_scale)
+        o = paged_attention(q, k_cache, v_cache, meta, self.scale, window=self.window, sinks=self.sinks,
+                            k_scale=self.k_scale, v_scale=self.v_scale)
         if gate is not None:
             o = (o.float() * torch.sigmoid(gate.float())).to(o.dtype)
         return self.o(o.reshape(T, nh * vd))

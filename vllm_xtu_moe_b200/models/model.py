@@ -201,32 +201,41 @@ class MoETransformer:
         return sum(t.numel() * t.element_size() for t in self.tensors() if (t.is_cuda or not device_only))
 
     # KV cache / state allocation ---------------------------------------
-    def kv_bytes_per_token(self, layers: range | None = None, skip_swa: bool = False) -> int:
+    def kv_bytes_per_token(self, layers: range | None = None, skip_swa: bool = False, kv_dtype: str = "bf16") -> int:
         """KV bytes per token of context (skip_swa: leave out sliding-window layers, whose
-        bounded pool does not grow with the context)."""
+        bounded pool does not grow with the context; kv_dtype "fp8": one byte per GQA value)."""
         c = self.cfg
         n = 0
+        gqa_b = 1 if kv_dtype == "fp8" else 2
         for i in layers if layers is not None else range(c.num_layers):
             if c.layer_type(i) == "linear" or (skip_swa and c.layer_type(i) == "swa"):
                 continue
             if c.is_mla:
                 n += (c.kv_lora_rank + c.qk_rope_head_dim) * 2
             else:
-                n += c.kv_heads(i) * (c.head_dim + c.gqa_v_dim) * 2
+                n += c.kv_heads(i) * (c.head_dim + c.gqa_v_dim) * gqa_b
         return n
 
-    def _attn_cache(self, i: int, num_blocks: int, block_size: int, dtype, device):
-        """Paged KV cache of attention layer i: (K, V), or (latent, None) for MLA."""
+    def _attn_cache(self, i: int, num_blocks: int, block_size: int, dtype, device, kv_dtype: str = "bf16"):
+        """Paged KV cache of attention layer i: (K, V), or (latent, None) for MLA.  kv_dtype
+        "fp8": e4m3 K [blocks, Hkv, bs, D] and V transposed per block [blocks, Hkv, Dv, bs]
+        (GQA layers; MLA latents stay bf16)."""
         c = self.cfg
         if c.is_mla:
             return (torch.zeros(num_blocks, 1, block_size, c.kv_lora_rank + c.qk_rope_head_dim,
                                 dtype=torch.bfloat16, device=device), None)
         nkv = c.kv_heads(i)
+        if kv_dtype == "fp8":
+            f8 = torch.float8_e4m3fn
+            return (torch.zeros(num_blocks, nkv, block_size, c.head_dim, dtype=f8, device=device),
+                    torch.zeros(num_blocks, nkv, c.gqa_v_dim, block_size, dtype=f8, device=device))
+        if kv_dtype not in ("bf16", "auto"):
+            raise ValueError(f"kv_cache_dtype {kv_dtype!r}: expected 'bf16' or 'fp8'")
         return (torch.zeros(num_blocks, nkv, block_size, c.head_dim, dtype=dtype, device=device),
                 torch.zeros(num_blocks, nkv, block_size, c.gqa_v_dim, dtype=dtype, device=device))
 
     def allocate_caches(self, num_blocks: int, block_size: int, max_seqs: int, device=None,
-                        layers: range | None = None, swa_blocks: int = 0) -> list:
+                        layers: range | None = None, swa_blocks: int = 0, kv_dtype: str = "bf16") -> list:
         """Per layer: recurrent state, or a paged KV cache of num_blocks blocks
         (sliding-window layers: swa_blocks blocks when a bounded pool is used)."""
         c = self.cfg
@@ -237,13 +246,14 @@ class MoETransformer:
                 caches.append(DeltaNetState(c, max_seqs, device))
             else:
                 nb = swa_blocks if (swa_blocks > 0 and c.layer_type(i) == "swa") else num_blocks
-                caches.append(self._attn_cache(i, nb, block_size, self.act_dtype, device))
+                caches.append(self._attn_cache(i, nb, block_size, self.act_dtype, device, kv_dtype))
         return caches
 
-    def allocate_mtp_caches(self, num_blocks: int, block_size: int, max_seqs: int, device=None) -> list:
+    def allocate_mtp_caches(self, num_blocks: int, block_size: int, max_seqs: int, device=None,
+                            kv_dtype: str = "bf16") -> list:
         device = device or self.device
         last = self.cfg.num_layers - 1      # an MTP layer has the last decoder layer's attention type
-        return [self._attn_cache(last, num_blocks, block_size, torch.bfloat16, device) for _ in self.mtp]
+        return [self._attn_cache(last, num_blocks, block_size, torch.bfloat16, device, kv_dtype) for _ in self.mtp]
 
     def prepare_workspaces(self, max_tokens: int):
         """Allocate one MoE workspace shared by every MoE layer (they run one at a time)."""

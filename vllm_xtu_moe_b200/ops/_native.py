@@ -40,7 +40,11 @@ _SIGS: dict[str, list] = {
                          c_float, c_float, c_float, P, P],
     "xtu_rmsnorm": [P, P, P, P, P, c_int, c_int, c_float, c_int, c_int, c_int, P, P],
     "xtu_rope_kv": [P, P, P, P, P, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, P, P,
-                    c_float, c_int, P, P, P, c_int, ctypes.c_longlong, P, P],
+                    c_float, c_int, P, P, P, c_int, ctypes.c_longlong, P, c_int, c_float, c_float, P],
+    "xtu_paged_attention_fp8": [P, c_int, P, P, P, c_int, P, P, P, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
+                                c_int, c_float, c_float, c_float, c_int, P, P, c_int, P, P, P],
+    "xtu_kv_dequant_gather": [P, P, P, c_int, P, P, c_int, c_int, c_int, c_int, c_int, c_float, c_float, P, P, P,
+                              c_int, c_int, P, P],
     "xtu_kv_write": [P, P, c_int, c_int, c_int, c_int, c_int, c_int, P, P, P, c_int, ctypes.c_longlong, P, P],
     "xtu_router_topk": [P, P, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_float, P, P, c_int, P],
     "xtu_moe_permute": [P, P, c_int, c_int, c_int, c_int, P, P, P, P, P, P, c_int, c_int, P, c_int, P],

@@ -13,9 +13,16 @@ On a GPU, ``paged_attention`` runs the tcgen05 flash-attention kernel in
 ``csrc/cuda/attention_tc.cu`` (query rows of a GQA group packed into one
 128-row MMA tile, split-KV for decode); ``paged_attention_ref`` is the
 PyTorch restatement used on CPU and as the test oracle.
+
+An fp8 KV cache (GQA, ``float8_e4m3fn``): ``k_cache [num_blocks, Hkv, block_size, D]``
+holds k / k_scale and ``v_cache [num_blocks, Hkv, Dv, block_size]`` holds v / v_scale,
+transposed per block (the decode kernel reads 4 consecutive keys of one value column per
+fragment).  Decode-shaped steps read it directly (``csrc/cuda/attention_decode.cu``);
+other steps dequantise the step's blocks into bf16 scratch blocks first.
 """
 from __future__ import annotations
 
+import dataclasses
 import math
 from dataclasses import dataclass
 
@@ -58,10 +65,20 @@ def _gather_kv(cache: torch.Tensor, block_table_row: torch.Tensor, n: int) -> to
     return blocks.permute(0, 2, 1, 3).reshape(nb * bs, cache.shape[1], cache.shape[3])[:n]
 
 
+def dequant_fp8_cache(k_cache: torch.Tensor, v_cache: torch.Tensor, k_scale: float = 1.0, v_scale: float = 1.0):
+    """fp8 GQA cache -> bf16 caches in the plain layout (K and V [blocks, Hkv, bs, D])."""
+    k = (k_cache.float() * k_scale).to(torch.bfloat16)
+    v = (v_cache.float() * v_scale).transpose(2, 3).contiguous().to(torch.bfloat16)
+    return k, v
+
+
 def paged_attention_ref(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor | None, meta: AttnMetadata,
                         scale: float, v_dim: int | None = None, out: torch.Tensor | None = None, window: int = 0,
-                        sinks: torch.Tensor | None = None) -> torch.Tensor:
+                        sinks: torch.Tensor | None = None, k_scale: float = 1.0,
+                        v_scale: float = 1.0) -> torch.Tensor:
     """q [T, Hq, Dqk] -> o [T, Hq, Dv] (fp32 math)."""
+    if k_cache.dtype == torch.float8_e4m3fn:
+        k_cache, v_cache = dequant_fp8_cache(k_cache, v_cache, k_scale, v_scale)
     T, Hq, D = q.shape
     qs = meta.q_start_host if meta.q_start_host is not None else meta.q_start.tolist()
     kl = meta.kv_len_host if meta.kv_len_host is not None else meta.kv_len.tolist()
@@ -124,14 +141,16 @@ def split_counters_reset(device) -> None:
 def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor | None, meta: AttnMetadata,
                     scale: float | None = None, v_dim: int | None = None, out: torch.Tensor | None = None,
                     workspace: torch.Tensor | None = None, window: int = 0,
-                    sinks: torch.Tensor | None = None) -> torch.Tensor:
+                    sinks: torch.Tensor | None = None, k_scale: float = 1.0, v_scale: float = 1.0) -> torch.Tensor:
     T, Hq, D = q.shape
     if scale is None:
         scale = 1.0 / math.sqrt(D)
     if not q.is_cuda or not N.has_symbol("xtu_paged_attention"):
         if q.is_cuda and N.native_required():
             raise N.NativeLibraryMissing("xtu_paged_attention missing from the CUDA library")
-        return paged_attention_ref(q, k_cache, v_cache, meta, scale, v_dim, out, window, sinks)
+        return paged_attention_ref(q, k_cache, v_cache, meta, scale, v_dim, out, window, sinks, k_scale, v_scale)
+    if k_cache.dtype == torch.float8_e4m3fn:
+        return _paged_attention_fp8(q, k_cache, v_cache, meta, scale, out, workspace, window, sinks, k_scale, v_scale)
     Hk = k_cache.shape[1]
     if sinks is not None:
         assert sinks.dtype == torch.float32 and sinks.is_contiguous() and sinks.numel() == Hq
@@ -156,6 +175,51 @@ def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
            N.ptr(sinks), N.status_buffer(q.device).data_ptr(),
            N.stream_ptr(q.device))
     return o
+
+
+def _paged_attention_fp8(q, k_cache, v_cache, meta: AttnMetadata, scale, out, workspace, window, sinks, k_scale,
+                         v_scale) -> torch.Tensor:
+    T, Hq, D = q.shape
+    nb, Hk, bs, _ = k_cache.shape
+    Dv = v_cache.shape[2]
+    assert v_cache.shape == (nb, Hk, Dv, bs) and bs == KV_BLOCK, "fp8 V cache is [blocks, Hkv, Dv, 64]"
+    o = out if out is not None else torch.empty(T, Hq, Dv, dtype=q.dtype, device=q.device)
+    assert q.stride(2) == 1 and q.stride(1) == D and o.is_contiguous()
+    if D == Dv and meta.max_q_len * (Hq // Hk) <= 64 and D in (64, 128):
+        splits = meta.num_splits
+        ws = workspace
+        need = num_split_workspace(T, Hq, Dv, splits) if splits > 1 else 0
+        if need and (ws is None or ws.numel() < need):
+            ws = torch.empty(need, dtype=torch.float32, device=q.device)
+        cnt = _split_counters(q.device) if splits > 1 and meta.num_seqs * Hk <= _MAX_SPLIT_GROUPS else None
+        if splits == 1 or cnt is not None:
+            r = N.call("xtu_paged_attention_fp8", q.data_ptr(), q.stride(0), k_cache.data_ptr(), v_cache.data_ptr(),
+                       o.data_ptr(), o.stride(0), meta.q_start.data_ptr(), meta.kv_len.data_ptr(),
+                       meta.block_table.data_ptr(), meta.block_table.stride(0), meta.num_seqs, meta.max_q_len, T, Hq,
+                       Hk, D, nb, float(scale), float(k_scale), float(v_scale), splits,
+                       N.ptr(ws) if splits > 1 else None, N.ptr(cnt), int(window), N.ptr(sinks),
+                       N.status_buffer(q.device).data_ptr(), N.stream_ptr(q.device))
+            if r == 1:
+                return o
+    # other shapes (prefill chunks, long verification steps): the step's blocks as bf16
+    if torch.cuda.is_current_stream_capturing():
+        raise RuntimeError("fp8 KV: this attention shape needs a dequantised copy, which cannot be captured")
+    kl = meta.kv_len_host if meta.kv_len_host is not None else meta.kv_len.tolist()
+    nblk = [(int(n) + bs - 1) // bs for n in kl]
+    start = [0]
+    for n in nblk:
+        start.append(start[-1] + n)
+    total, mx = start[-1], max(nblk) if nblk else 0
+    kb = torch.empty(max(1, total), Hk, bs, D, dtype=torch.bfloat16, device=q.device)
+    vb = torch.empty(max(1, total), Hk, bs, Dv, dtype=torch.bfloat16, device=q.device)
+    bt = torch.zeros(meta.num_seqs, max(1, mx), dtype=torch.int32, device=q.device)
+    st = torch.tensor(start, dtype=torch.int32).to(q.device, non_blocking=True)
+    N.call("xtu_kv_dequant_gather", k_cache.data_ptr(), v_cache.data_ptr(), meta.block_table.data_ptr(),
+           meta.block_table.stride(0), st.data_ptr(), meta.kv_len.data_ptr(), meta.num_seqs, mx, Hk, D, Dv,
+           float(k_scale), float(v_scale), kb.data_ptr(), vb.data_ptr(), bt.data_ptr(), bt.stride(0), nb,
+           N.status_buffer(q.device).data_ptr(), N.stream_ptr(q.device))
+    m2 = dataclasses.replace(meta, block_table=bt)
+    return paged_attention(q, kb, vb, m2, scale, Dv, o, workspace, window, sinks)
 
 
 def num_split_workspace(T: int, Hq: int, Dv: int, splits: int) -> int:

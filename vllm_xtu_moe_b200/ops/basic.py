@@ -118,12 +118,15 @@ def rope_and_cache(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, positions:
                    cos_sin: torch.Tensor, rot: int, neox: bool = True, *, slot_mapping: torch.Tensor | None = None,
                    k_cache: torch.Tensor | None = None, v_cache: torch.Tensor | None = None,
                    q_norm_w: torch.Tensor | None = None, k_norm_w: torch.Tensor | None = None,
-                   norm_eps: float = 1e-6, norm_add_one: bool = False):
+                   norm_eps: float = 1e-6, norm_add_one: bool = False, k_scale: float = 1.0,
+                   v_scale: float = 1.0):
     """In place: optional per-head RMSNorm of q/k, RoPE on the first `rot` dims,
     then write k, v into the paged cache ([blocks, Hk, block_size, D]).
 
     q [T, Hq, D], k [T, Hk, D], v [T, Hk, Dv] may be strided views of a fused QKV
-    projection output (the head dimension must be contiguous).
+    projection output (the head dimension must be contiguous).  An e4m3 cache (k_cache
+    dtype float8_e4m3fn) stores k / k_scale and v / v_scale, saturated, with V transposed
+    per block ([blocks, Hk, Dv, block_size]).
     """
     T, Hq, D = q.shape
     Hk = k.shape[1]
@@ -137,7 +140,7 @@ def rope_and_cache(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, positions:
             q.copy_(apply_rope_ref(q, positions, cos_sin, rot, neox))
             k.copy_(apply_rope_ref(k, positions, cos_sin, rot, neox))
         if k_cache is not None:
-            write_kv_ref(k, v, slot_mapping, k_cache, v_cache)
+            write_kv_ref(k, v, slot_mapping, k_cache, v_cache, k_scale, v_scale)
         return q, k
     assert q.stride(2) == 1 and k.stride(2) == 1 and v.stride(2) == 1
     assert q.stride(1) == D and k.stride(1) == D and v.stride(1) == Dv
@@ -146,18 +149,35 @@ def rope_and_cache(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, positions:
            Hq, Hk, D, Dv, rot, int(neox), q.stride(0), k.stride(0), v.stride(0), N.ptr(q_norm_w), N.ptr(k_norm_w),
            float(norm_eps), int(norm_add_one), N.ptr(slot_mapping), N.ptr(k_cache), N.ptr(v_cache), bs,
            k_cache.shape[0] * bs if k_cache is not None else 0, N.status_buffer(q.device).data_ptr(),
-           N.stream_ptr(q.device))
+           int(is_fp8_cache(k_cache)), 1.0 / k_scale, 1.0 / v_scale, N.stream_ptr(q.device))
     return q, k
 
 
-def write_kv_ref(k, v, slot_mapping, k_cache, v_cache):
+FP8_MAX = 448.0
+
+
+def is_fp8_cache(cache: torch.Tensor | None) -> bool:
+    return cache is not None and cache.dtype == torch.float8_e4m3fn
+
+
+def to_e4m3(x: torch.Tensor, inv_scale: float) -> torch.Tensor:
+    """x / scale -> e4m3, saturating at +-448 (as the cache-write kernel does)."""
+    return (x.float() * inv_scale).clamp(-FP8_MAX, FP8_MAX).to(torch.float8_e4m3fn)
+
+
+def write_kv_ref(k, v, slot_mapping, k_cache, v_cache, k_scale: float = 1.0, v_scale: float = 1.0):
     bs = k_cache.shape[2]
+    fp8 = is_fp8_cache(k_cache)
     for t in range(k.shape[0]):
         s = int(slot_mapping[t])
         if s < 0:
             continue
-        k_cache[s // bs, :, s % bs] = k[t]
-        v_cache[s // bs, :, s % bs] = v[t]
+        if fp8:
+            k_cache[s // bs, :, s % bs] = to_e4m3(k[t], 1.0 / k_scale)
+            v_cache[s // bs, :, :, s % bs] = to_e4m3(v[t], 1.0 / v_scale)
+        else:
+            k_cache[s // bs, :, s % bs] = k[t]
+            v_cache[s // bs, :, s % bs] = v[t]
 
 
 def write_kv(k, v, slot_mapping, k_cache, v_cache):

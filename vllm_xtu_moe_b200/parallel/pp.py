@@ -66,13 +66,13 @@ class PipelineStage(MoETransformer):
         return torch.stack([x, residual]).contiguous()
 
     # ------------------------------------------------------------------ engine contract
-    def kv_bytes_per_token(self, layers: range | None = None, skip_swa: bool = False) -> int:
-        return super().kv_bytes_per_token(range(self.lo, self.hi) if layers is None else layers, skip_swa)
+    def kv_bytes_per_token(self, layers: range | None = None, skip_swa: bool = False, kv_dtype: str = "bf16") -> int:
+        return super().kv_bytes_per_token(range(self.lo, self.hi) if layers is None else layers, skip_swa, kv_dtype)
 
     def allocate_caches(self, num_blocks: int, block_size: int, max_seqs: int, device=None,
-                        layers: range | None = None, swa_blocks: int = 0) -> list:
+                        layers: range | None = None, swa_blocks: int = 0, kv_dtype: str = "bf16") -> list:
         return super().allocate_caches(num_blocks, block_size, max_seqs, device,
-                                       range(self.lo, self.hi) if layers is None else layers, swa_blocks)
+                                       range(self.lo, self.hi) if layers is None else layers, swa_blocks, kv_dtype)
 
     def _run_layers(self, x, residual, meta, caches):
         for layer, kv in zip(self.layers, caches):
