@@ -171,3 +171,56 @@ def test_set_speculation_switches_between_requests_cpu():
     with pytest.raises(ValueError):
         llm.set_speculation(4)
     llm.shutdown()
+
+
+def test_rejection_sampling_emits_the_target_distribution():
+    """verify_sampled with a point-mass draft: the first emitted token is distributed as the
+    target's filtered distribution whatever the draft (here a likely one and an unlikely
+    one), and a fully accepted chain ends with a draw from the last row."""
+    from vllm_xtu_moe_b200.engine.spec_decode import verify_sampled
+    from vllm_xtu_moe_b200.engine.sampling import filtered_probs
+    torch.manual_seed(0)
+    V = 12
+    logits = torch.randn(3, V) * 1.5
+    sp = SamplingParams(temperature=0.8, top_k=8, max_tokens=1)
+    p0 = filtered_probs(logits[0], 0.8, 8)
+    for draft0 in (int(p0.argmax()), int(p0.argmin())):
+        g = torch.Generator().manual_seed(1)
+        N = 6000
+        counts = torch.zeros(V)
+        lens = []
+        for _ in range(N):
+            toks = verify_sampled(logits, [draft0, 3], sp, g)
+            counts[toks[0]] += 1
+            lens.append(len(toks))
+        emp = counts / N
+        assert (emp - p0).abs().max().item() < 0.025, (draft0, emp, p0)
+        assert min(lens) >= 1 and max(lens) <= 3
+    # drafts of probability 1 are always kept
+    sharp = torch.full((3, V), -30.0)
+    sharp[0, 4] = sharp[1, 5] = sharp[2, 6] = 30.0
+    toks = verify_sampled(sharp, [4, 5], SamplingParams(temperature=1.0, max_tokens=1), torch.Generator())
+    assert toks == [4, 5, 6]
+
+
+def test_sampled_requests_with_mtp_cpu():
+    """Sampled requests run with MTP drafts (rejection sampling); a seeded request repeats
+    its tokens, and greedy requests in the same batch still equal plain greedy decoding."""
+    m = build_model(_cfg(), device="cpu", seed=1)
+    m.act_dtype = torch.float32
+    prompts = [list(range(3, 40)), list(range(50, 61))]
+    base, _ = _run(m, 0, prompts, 10)
+    rc = RunnerConfig(block_size=64, max_seqs=4, max_model_len=512, max_batched_tokens=128, use_cuda_graph=False,
+                      num_spec=3)
+    outs = []
+    for _ in range(2):
+        llm = LLM(m, device="cpu", runner_config=rc)
+        ra = llm.add_request(prompts[0], SamplingParams(max_tokens=10))
+        rb = llm.add_request(prompts[1], SamplingParams(max_tokens=10, temperature=0.9, seed=7))
+        while llm.scheduler.has_work():
+            llm.step()
+        outs.append((list(ra.output), list(rb.output), rb.proposed))
+        llm.shutdown()
+    assert outs[0][0] == base[0].token_ids            # the greedy request is unchanged
+    assert outs[0][1] == outs[1][1] and len(outs[0][1]) == 10
+    assert outs[0][2] > 0                              # the sampled request was drafted for

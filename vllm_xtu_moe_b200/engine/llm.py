@@ -116,9 +116,8 @@ class LLM:
         """Raise ValueError for a request this engine cannot serve (called by add_request;
         the server calls it before queueing, so a bad request gets an HTTP 400 and never
         reaches the engine thread)."""
-        if (params.temperature > 0.0 or params.logprobs is not None) and self.spec is not None:
-            raise ValueError("speculative decoding verifies greedy drafts; sampled requests and logprobs "
-                             "need num_spec=0")
+        if params.logprobs is not None and self.spec is not None:
+            raise ValueError("token log-probabilities with speculative decoding are not supported: use num_spec=0")
         if not prompt:
             raise ValueError("empty prompt")
         if params.max_tokens < 1:

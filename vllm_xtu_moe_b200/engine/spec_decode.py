@@ -19,6 +19,14 @@ layers).  Here the drafter is the model's own ``MTPLayer`` and the loop is:
   prefix leave stale KV entries at positions that the next step overwrites before
   any row can attend to them.
 
+Sampled requests (temperature > 0) verify by rejection sampling against the point-mass
+draft distribution of the greedy drafter (Leviathan et al. 2023, Chen et al. 2023):
+draft d_j is kept with probability p_j(d_j) (p_j the request's filtered sampling
+distribution at that row), the first rejected position emits a draw from p_j with d_j
+removed and renormalised, and a fully accepted chain adds a draw from the last row's p;
+every emitted token is then an exact sample of the request's distribution.  Those steps
+run eagerly (the sampling draws are made with the request's own generator).
+
 Linear-attention (DeltaNet) models are not drafted: their recurrent state would
 need a rollback for rejected drafts.
 
@@ -58,6 +66,31 @@ def verify_greedy(target: torch.Tensor, ids: torch.Tensor, q_start: torch.Tensor
         acc[b] = a
         row[b] = qs[b] + a
     return acc, row
+
+
+def verify_sampled(logits: torch.Tensor, drafts: list[int], params, generator: torch.Generator) -> list[int]:
+    """Rejection-sampling verification of one request's greedy drafts.
+
+    logits [len(drafts) + 1, V]: row j is the target's distribution for the position that
+    draft j (0-based) fills; row len(drafts) the one after the last draft.  Returns the
+    emitted tokens: the accepted drafts, then one drawn token (2 host reads)."""
+    from .sampling import filtered_probs
+    n = len(drafts)
+    probs = torch.stack([filtered_probs(logits[j], params.temperature, params.top_k, params.top_p)
+                         for j in range(n + 1)])
+    d = torch.tensor(drafts, dtype=torch.long, device=logits.device)
+    u = torch.rand(n, generator=generator, device=logits.device)
+    keep = (u < probs[torch.arange(n, device=logits.device), d]).tolist() if n else []
+    a = 0
+    while a < n and keep[a]:
+        a += 1
+    p = probs[a].clone()
+    if a < n:                                 # residual of the point-mass draft: p without d_a
+        p[d[a]] = 0.0
+        tot = p.sum()
+        p = p / tot if float(tot) > 0 else probs[a]
+    x = int(torch.multinomial(p, 1, generator=generator)[0])
+    return drafts[:a] + [x]
 
 
 class SpecDecoder:
@@ -272,6 +305,8 @@ class SpecDecoder:
 
     @torch.inference_mode()
     def decode_step(self, plan, scheduler) -> list:
+        if any(ch.req.params.temperature > 0.0 for ch in plan.chunks):
+            return self._decode_step_eager(plan, scheduler)
         b = self._graph_bucket(plan)
         if b is not None:
             # the chain writes draft KV up to total_len + 2k - 1: hold those blocks first
@@ -316,13 +351,38 @@ class SpecDecoder:
         rn = self.runner
         ids, meta = rn.build_meta(plan)
         n_rows = ids.shape[0]
-        tgt, h, _, _ = rn.forward(ids, meta, torch.arange(n_rows, device=rn.device))
+        tgt, h, _, logits = rn.forward(ids, meta, torch.arange(n_rows, device=rn.device))
         k = max(len(ch.req.draft) for ch in plan.chunks)
-        acc, last = verify_greedy(tgt, ids, meta.q_start, meta.num_seqs, k)
-        out = self._mtp(tgt.to(torch.int32), h, meta)
+        emit = tgt.to(torch.int32)
+        if any(ch.req.params.temperature > 0.0 for ch in plan.chunks):
+            # sampled requests: rejection sampling; their emitted tokens feed the MTP pass
+            from .sampling import _generator
+            acc_l, last_l = [], []
+            emit_h = emit.tolist()
+            greedy_acc, _ = verify_greedy(tgt, ids, meta.q_start, meta.num_seqs, k)
+            greedy_acc = greedy_acc.tolist()
+            for i, ch in enumerate(plan.chunks):
+                r = ch.req
+                q0, q1 = meta.q_start_host[i], meta.q_start_host[i + 1]
+                if r.params.temperature > 0.0:
+                    nd = min(len(r.draft), q1 - q0 - 1)
+                    toks = verify_sampled(logits[q0:q0 + nd + 1], [int(t) for t in r.draft[:nd]], r.params,
+                                          _generator(r, logits.device))
+                    emit_h[q0:q0 + len(toks)] = toks
+                    a = len(toks) - 1
+                else:
+                    a = greedy_acc[i]
+                acc_l.append(a)
+                last_l.append(q0 + a)
+            emit = torch.tensor(emit_h, dtype=torch.int32, device=rn.device)
+            acc = torch.tensor(acc_l, dtype=torch.int32)
+            last = torch.tensor(last_l, dtype=torch.long, device=rn.device)
+        else:
+            acc, last = verify_greedy(tgt, ids, meta.q_start, meta.num_seqs, k)
+        out = self._mtp(emit, h, meta)
         hid = out.index_select(0, last.long())
         first = B.argmax(self.model.logits(hid))
-        tgt_h = tgt.tolist()
+        tgt_h = emit.tolist()
         acc_h = acc.tolist()
         now = time.perf_counter()
         done = []
