@@ -62,6 +62,11 @@ static float w_at(const DotArgs& a, const RowRef& r, int k) {
       const uint8_t byte = r.w[k >> 1];
       return e2m1_to_f32((k & 1) ? (byte >> 4) : (byte & 0xF)) * std::ldexp(1.f, (int)r.s[k >> 5] - 127);
     }
+    case FMT_INT4: {
+      const uint8_t byte = r.w[k >> 1];
+      const float* sz = reinterpret_cast<const float*>(r.s) + 2 * (k >> 7);
+      return ((float)((k & 1) ? (byte >> 4) : (byte & 0xF)) - sz[1]) * sz[0];
+    }
     default: {
       const uint8_t byte = r.w[k >> 1];
       return e2m1_to_f32((k & 1) ? (byte >> 4) : (byte & 0xF)) * e4m3_to_f32(r.s[k >> 4]) * a.gscale;
@@ -147,6 +152,7 @@ static size_t scale_bytes(int fmt, int K) {
     case FMT_BF16: return 0;
     case FMT_FP8: return 4 * (size_t)((K + 127) / 128);
     case FMT_MXFP4: return (size_t)K / 32;
+    case FMT_INT4: return 8 * (size_t)(K / 128);
     default: return (size_t)K / 16;
   }
 }
@@ -245,6 +251,9 @@ class Engine {
       }
       case FMT_MXFP4:
         std::memcpy(dst, src + ((size_t)e * rows + row) * (K / 32), K / 32);
+        return;
+      case FMT_INT4:     // checkpoint [E][rows][K/128][2] fp32 (scale, zero)
+        std::memcpy(dst, src + ((size_t)e * rows + row) * (K / 128) * 8, (size_t)(K / 128) * 8);
         return;
       default:
         std::memcpy(dst, src + ((size_t)e * rows + row) * (K / 16), K / 16);

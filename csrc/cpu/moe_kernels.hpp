@@ -17,7 +17,9 @@
 
 namespace xtu_cpu {
 
-enum Fmt : int { FMT_BF16 = 0, FMT_FP8 = 1, FMT_MXFP4 = 2, FMT_NVFP4 = 3 };
+// FMT_INT4: GPTQ-style 4-bit integers (low nibble = even k) with, per row and 128-wide
+// group, an fp32 (scale, zero point) pair: w = (q - zero) * scale
+enum Fmt : int { FMT_BF16 = 0, FMT_FP8 = 1, FMT_MXFP4 = 2, FMT_NVFP4 = 3, FMT_INT4 = 4 };
 
 struct RowRef {
   const uint8_t* w;     // row weights

@@ -25,6 +25,17 @@ inline __m512 nibbles16(const uint8_t* p) {
   return _mm512_permutexvar_ps(nib, _mm512_loadu_ps(kE2M1));
 }
 
+// 8 bytes -> 16 unsigned nibbles as fp32 in k order
+inline __m512 int4x16(const uint8_t* p) {
+  uint64_t v8;
+  std::memcpy(&v8, p, 8);
+  const __m512i bytes = _mm512_cvtepu8_epi32(_mm_cvtsi64_si128((long long)v8));
+  const __m512i idx = _mm512_set_epi32(7, 7, 6, 6, 5, 5, 4, 4, 3, 3, 2, 2, 1, 1, 0, 0);
+  const __m512i sh = _mm512_set_epi32(4, 0, 4, 0, 4, 0, 4, 0, 4, 0, 4, 0, 4, 0, 4, 0);
+  return _mm512_cvtepi32_ps(_mm512_and_si512(_mm512_srlv_epi32(_mm512_permutexvar_epi32(idx, bytes), sh),
+                                             _mm512_set1_epi32(0xF)));
+}
+
 // 16 weights of row r starting at k (k % 16 == 0), decoded to fp32
 inline __m512 decode16(const DotArgs& a, const RowRef& r, int k) {
   switch (a.fmt) {
@@ -44,6 +55,10 @@ inline __m512 decode16(const DotArgs& a, const RowRef& r, int k) {
     case FMT_MXFP4: {
       const float sc = std::ldexp(1.f, (int)r.s[k >> 5] - 127);
       return _mm512_mul_ps(nibbles16(r.w + (k >> 1)), _mm512_set1_ps(sc));
+    }
+    case FMT_INT4: {
+      const float* sz = reinterpret_cast<const float*>(r.s) + 2 * (k >> 7);
+      return _mm512_mul_ps(_mm512_sub_ps(int4x16(r.w + (k >> 1)), _mm512_set1_ps(sz[1])), _mm512_set1_ps(sz[0]));
     }
     default: {  // FMT_NVFP4
       const float sc = e4m3_to_f32(r.s[k >> 4]) * a.gscale;
@@ -113,6 +128,13 @@ inline __m512bh decode32_bf16(const DotArgs& a, const RowRef& r, int k) {
       const __m512i lut = _mm512_mask_add_epi16(base, (__mmask32)0xFEFEFEFEu, base, _mm512_set1_epi16((short)(e << 7)));
       return (__m512bh)_mm512_permutexvar_epi16(nibble_words32(r.w + (k >> 1)), lut);
     }
+  } else if (a.fmt == FMT_INT4) {
+    // one 128-wide group covers the 32 weights: table (i - zero) * scale, i = 0..15, twice
+    const float* sz = reinterpret_cast<const float*>(r.s) + 2 * (k >> 7);
+    const __m512 q = _mm512_set_ps(15, 14, 13, 12, 11, 10, 9, 8, 7, 6, 5, 4, 3, 2, 1, 0);
+    const __m512 v = _mm512_mul_ps(_mm512_sub_ps(q, _mm512_set1_ps(sz[1])), _mm512_set1_ps(sz[0]));
+    const __m512i lut = (__m512i)_mm512_cvtne2ps_pbh(v, v);
+    return (__m512bh)_mm512_permutexvar_epi16(nibble_words32(r.w + (k >> 1)), lut);
   } else if (a.fmt == FMT_NVFP4) {
     const __m512 codes = _mm512_loadu_ps(kE2M1);
     const float s0 = e4m3_to_f32(r.s[k >> 4]) * a.gscale, s1 = e4m3_to_f32(r.s[(k >> 4) + 1]) * a.gscale;

@@ -25,6 +25,17 @@ def _raw(fmt, E, H, I, seed=0):
         p13, s13 = quant_mxfp4(w13)
         p2, s2 = quant_mxfp4(w2)
         return dict(w13=p13, w2=p2, s13=s13, s2=s2)
+    if fmt == "int4":          # asymmetric 4-bit rows, 128-wide groups: w = (q - zero) * scale
+        def q4(w):
+            wg = w.view(*w.shape[:-1], -1, 128)
+            lo, hi = wg.amin(-1), wg.amax(-1)
+            sc = ((hi - lo) / 15).clamp(min=1e-6)
+            z = torch.round(-lo / sc).clamp(0, 15)
+            q = (torch.round(wg / sc[..., None]) + z[..., None]).clamp(0, 15).to(torch.uint8).flatten(-2)
+            return (q[..., 0::2] | (q[..., 1::2] << 4)).contiguous(), torch.stack([sc, z], -1).contiguous()
+        p13, s13 = q4(w13)
+        p2, s2 = q4(w2)
+        return dict(w13=p13, w2=p2, s13=s13, s2=s2)
     p13, s13, g13 = zip(*[quant_nvfp4(w13[e]) for e in range(E)])
     p2, s2, g2 = zip(*[quant_nvfp4(w2[e]) for e in range(E)])
     return dict(w13=torch.stack(p13), w2=torch.stack(p2), s13=torch.stack(s13).view(torch.uint8),
@@ -32,6 +43,11 @@ def _raw(fmt, E, H, I, seed=0):
 
 
 def _ref(fmt, raw, x, ids, w, lo, hi, limit=0.0):
+    if fmt == "int4":
+        from vllm_xtu_moe_b200.ops.quant import dequant_int4_rows
+        ex = M.ExpertWeights("bf16", dequant_int4_rows(raw["w13"], raw["s13"]).to(torch.bfloat16),
+                             dequant_int4_rows(raw["w2"], raw["s2"]).to(torch.bfloat16), None, None, False)
+        return M.moe_ref(x, ids, w, ex, lo, hi, act_limit=limit)
     ex = M.ExpertWeights(fmt, raw["w13"], raw["w2"], raw.get("s13"), raw.get("s2"), False, raw.get("gs13"),
                          raw.get("gs2"))
     if fmt == "nvfp4":
@@ -54,10 +70,10 @@ def test_e4m3_decoder_all_codes():
             assert v == r, (c, v, r)
 
 
-@pytest.mark.parametrize("fmt", ["bf16", "fp8", "mxfp4", "nvfp4"])
+@pytest.mark.parametrize("fmt", ["bf16", "fp8", "mxfp4", "nvfp4", "int4"])
 @pytest.mark.parametrize("T", [1, 5, 37])
 def test_engine_matches_reference(fmt, T):
-    E, H, I, K = 8, 256, 384 if fmt in ("bf16", "mxfp4", "nvfp4") else 256, 2
+    E, H, I, K = 8, 256, 384 if fmt in ("bf16", "mxfp4", "nvfp4", "int4") else 256, 2
     raw = _raw(fmt, E, H, I)
     eng = CpuExpertEngine(fmt, raw["w13"], raw["w2"], raw.get("s13"), raw.get("s2"), raw.get("gs13"),
                           raw.get("gs2"), threads=4, act_limit=7.0, int8_mode=0)

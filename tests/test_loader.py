@@ -184,3 +184,54 @@ def test_gptq_v2_zero_points_and_unsupported_formats(tmp_path):
                 CheckpointSource._gptq_format(d)
         else:
             assert CheckpointSource._gptq_format(d) == ok
+
+
+def test_gptq_int4_rows_match_dequant():
+    """4-bit, 128-grouped GPTQ weights repacked as INT4 rows (kept at 4 bits) stand for the
+    same weight as the dequantized checkpoint; other group sizes are left to dequantization."""
+    from vllm_xtu_moe_b200.ops.quant import dequant_gptq, dequant_int4_rows, gptq_to_int4_rows
+    torch.manual_seed(2)
+    t, deq = _gptq_pack(torch.randn(96, 256) * 0.05, group=128)
+    packed, sz = gptq_to_int4_rows(t["qweight"], t["scales"], t["qzeros"])
+    assert packed.shape == (96, 128) and packed.dtype == torch.uint8 and sz.shape == (96, 2, 2)
+    assert torch.equal(dequant_int4_rows(packed, sz), dequant_gptq(t["qweight"], t["scales"], t["qzeros"]))
+    t32, _ = _gptq_pack(torch.randn(96, 256) * 0.05, group=32)
+    assert gptq_to_int4_rows(t32["qweight"], t32["scales"], t32["qzeros"]) is None
+
+
+def test_gptq_int4_experts_stay_4bit_on_the_cpu_tier(tmp_path):
+    """A GPTQ expert checkpoint (4-bit, group 128) served with the experts on the CPU tier:
+    the engine holds INT4 rows (a quarter of bf16's bytes) and the logits match the model
+    loaded from the dequantized weights."""
+    from vllm_xtu_moe_b200.tiering.executor import TieredExperts
+    from vllm_xtu_moe_b200.utils.safetensors import SafetensorsFile, save_file
+    cfg = _cfg("tiny-mixtral")
+    m = build_model(cfg, device="cpu", seed=6)
+    export_hf(m, cfg, tmp_path / "model.safetensors")
+    f = SafetensorsFile(tmp_path / "model.safetensors")
+    tensors = {k: f.get(k).clone() for k in f.keys()}
+    f.close()
+    gptq, plain = dict(tensors), dict(tensors)
+    for k in list(tensors):
+        if k.endswith(".weight") and ".experts." in k:
+            pre = k[:-len(".weight")]
+            packed, deq = _gptq_pack(tensors[k].float(), group=128)
+            del gptq[k]
+            gptq.update({f"{pre}.{s}": v for s, v in packed.items()})
+            plain[k] = deq.to(torch.bfloat16)
+    for d, ts in (("g", gptq), ("p", plain)):
+        (tmp_path / d).mkdir()
+        save_file(ts, tmp_path / d / "model.safetensors", {"format": "pt"})
+    tier = TieredExperts(cfg, device="cpu", resident_layers=set(), threads=2)
+    mg, sg = load_model(tmp_path / "g", device="cpu", cfg=cfg, expert_sink=tier.expert_sink)
+    tier.attach(mg)
+    mp_, sp_ = load_model(tmp_path / "p", device="cpu", cfg=cfg)
+    engines = [ex.engine for ex in tier.executors]
+    assert engines and all(e.fmt == "int4" for e in engines)
+    E, I, H = cfg.num_experts, cfg.moe_intermediate, cfg.hidden_size
+    assert engines[0].info()["bytes"] <= E * 3 * I * H // 2 * 1.2          # ~4 bits per weight
+    a, b = _logits(mp_), _logits(mg)
+    assert (a - b).abs().max().item() <= 3e-2 * a.abs().max().item(), (a - b).abs().max().item()
+    tier.shutdown()
+    sg.close()
+    sp_.close()

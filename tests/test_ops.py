@@ -396,3 +396,26 @@ def test_route_decode_matches_separate_router(T, E, K, scoring, ng, tg):
             act = ws.active.cpu()
             assert act[0].item() == int((cnt > 0).sum()) and torch.equal(act[1:1 + act[0]],
                                                                           torch.nonzero(cnt).flatten().int())
+
+
+@pytest.mark.gpu
+def test_sigmoid_gate_kernels():
+    """gate_mul_ (strided gated-GQA output gate) and shared_gate_ (per-token sigmoid of a
+    dot product) against fp32 torch."""
+    from vllm_xtu_moe_b200.ops.basic import gate_mul_, shared_gate_
+    torch.manual_seed(9)
+    T, nh, hd = 37, 8, 256
+    qg = torch.randn(T, nh, 2 * hd, device="cuda").to(torch.bfloat16)
+    o = torch.randn(T, nh, hd, device="cuda").to(torch.bfloat16)
+    ref = (o.float() * torch.sigmoid(qg[:, :, hd:].float()))
+    gate_mul_(o, qg[:, :, hd:])
+    torch.cuda.synchronize()
+    assert (o.float() - ref).abs().max().item() < 2e-2
+    H = 2048
+    x = torch.randn(T, H, device="cuda").to(torch.bfloat16)
+    w = (torch.randn(1, H, device="cuda") * 0.02).to(torch.bfloat16)
+    y = torch.randn(T, H, device="cuda").to(torch.bfloat16)
+    ref = y.float() * torch.sigmoid(x.float() @ w.float().t())
+    shared_gate_(y, x, w)
+    torch.cuda.synchronize()
+    assert (y.float() - ref).abs().max().item() < 2e-2

@@ -113,7 +113,7 @@ class GQAAttention:
         o = paged_attention(q, k_cache, v_cache, meta, self.scale, window=self.window, sinks=self.sinks,
                             k_scale=self.k_scale, v_scale=self.v_scale)
         if gate is not None:
-            o = (o.float() * torch.sigmoid(gate.float())).to(o.dtype)
+            B.gate_mul_(o, gate)
         return self.o(o.reshape(T, nh * vd))
 
     def tensors(self):
@@ -220,8 +220,7 @@ class MoEBlock:
         if self.shared is not None:
             sh = self.shared(x)
             if self.shared_gate is not None:
-                g = torch.sigmoid(G.linear(x, self.shared_gate, out_dtype=torch.float32))
-                sh = (sh.float() * g).to(x.dtype)
+                sh = B.shared_gate_(sh, x, self.shared_gate)
         if self.executor is not None:
             return self.executor(self, x, ids, w, sh)
         return M.fused_moe(x, ids, w, self.experts, self.workspace(x), lo=self.expert_lo, shared=sh,
@@ -249,7 +248,7 @@ class MoEBlock:
             return routed
         sh = self.shared(x)
         if self.shared_gate is not None:
-            sh = (sh.float() * torch.sigmoid(G.linear(x, self.shared_gate, out_dtype=torch.float32))).to(x.dtype)
+            sh = B.shared_gate_(sh, x, self.shared_gate)
         return (routed.float() + sh.float()).to(x.dtype)
 
     def workspace(self, x: torch.Tensor) -> M.MoEWorkspace | None:

@@ -26,7 +26,7 @@ import re
 import torch
 
 from ..ops import gemm as G
-from ..ops.quant import dequant_fp8_block, dequant_gptq, quant_fp8_block
+from ..ops.quant import dequant_fp8_block, dequant_gptq, gptq_to_int4_rows, quant_fp8_block
 from ..utils.safetensors import CheckpointDir
 from .config import ModelConfig, from_hf_config
 from .layers import Linear
@@ -167,6 +167,26 @@ class CheckpointSource:
         t = self._get(self._hf(name)[0])       # any shape with n elements (KDA keeps A_log [1, 1, nv, 1])
         return t.to(device=self.device, dtype=ref.dtype, copy=True).reshape(ref.shape)
 
+    def _gptq_int4_experts(self, base: str, E: int) -> dict | None:
+        """The layer's GPTQ experts as INT4 rows (None when any projection is not in that form)."""
+        f = self.fam
+        opt = lambda p, n: self._get(p + n) if (p + n) in self.ckpt else None
+
+        def rows(prefix):
+            return gptq_to_int4_rows(self._get(prefix + ".qweight"), self._get(prefix + ".scales"),
+                                     opt(prefix, ".qzeros"), opt(prefix, ".g_idx"), self.gptq_zero_offset)
+        w13, s13, w2, s2 = [], [], [], []
+        for e in range(E):
+            g, u, d = (rows(f"{base}.{e}.{f[k]}") for k in ("gate", "up", "down"))
+            if g is None or u is None or d is None:
+                return None
+            w13.append(torch.cat([g[0], u[0]], 0))
+            s13.append(torch.cat([g[1], u[1]], 0))
+            w2.append(d[0])
+            s2.append(d[1])
+        return {"fmt": "int4", "w13": torch.stack(w13), "w2": torch.stack(w2), "s13": torch.stack(s13),
+                "s2": torch.stack(s2)}
+
     def _gptq(self, prefix: str) -> torch.Tensor:
         """A GPTQ-quantized projection, dequantized to fp32 [out, in]."""
         opt = lambda k: self._get(prefix + k) if (prefix + k) in self.ckpt else None
@@ -221,8 +241,12 @@ class CheckpointSource:
         f = self.fam
         base = f"{pre}.{f['experts']}"
         if f"{base}.0.{f['gate']}.qweight" in self.ckpt:
-            # GPTQ INT4 experts (the reference repacks them for its CPU engine): dequantized,
-            # then held as fp8-128 when the model's expert format asks for it, else bf16
+            # GPTQ INT4 experts: kept at 4 bits ("int4": the CPU tier's format; GPU-resident
+            # experts dequantize it when prepared) when the layer is 4-bit, 128-grouped, in
+            # input order; else dequantized, then held as fp8-128 or bf16 per the model's format
+            rows = self._gptq_int4_experts(base, E) if self.gptq_bits == 4 else None
+            if rows is not None:
+                return rows
             w13 = torch.stack([torch.cat([self._gptq(f"{base}.{e}.{f['gate']}"),
                                           self._gptq(f"{base}.{e}.{f['up']}")], 0) for e in range(E)])
             w2 = torch.stack([self._gptq(f"{base}.{e}.{f['down']}") for e in range(E)])

@@ -43,6 +43,8 @@ _SIGS: dict[str, list] = {
                     c_float, c_int, P, P, P, c_int, ctypes.c_longlong, P, c_int, c_float, c_float, P],
     "xtu_paged_attention_fp8": [P, c_int, P, P, P, c_int, P, P, P, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
                                 c_int, c_float, c_float, c_float, c_int, P, P, c_int, P, P, P],
+    "xtu_gate_mul": [P, c_int, c_int, P, c_int, c_int, c_int, c_int, c_int, P],
+    "xtu_shared_gate": [P, c_int, P, c_int, P, c_int, c_int, P],
     "xtu_kv_dequant_gather": [P, P, P, c_int, P, P, c_int, c_int, c_int, c_int, c_int, c_float, c_float, P, P, P,
                               c_int, c_int, P, P],
     "xtu_kv_write": [P, P, c_int, c_int, c_int, c_int, c_int, c_int, P, P, P, c_int, ctypes.c_longlong, P, P],

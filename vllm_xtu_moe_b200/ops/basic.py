@@ -253,3 +253,34 @@ def silu_mul(x: torch.Tensor, limit: float = 0.0, alpha: float = 1.0, beta: floa
     N.call("xtu_silu_mul", x.data_ptr(), T, I, float(limit), float(alpha), float(beta), y.data_ptr(),
            N.stream_ptr(x.device))
     return y
+
+
+# ---------------------------------------------------------------------------
+# sigmoid gates
+# ---------------------------------------------------------------------------
+def gate_mul_(y: torch.Tensor, g: torch.Tensor) -> torch.Tensor:
+    """In place: y [T, nh, D] *= sigmoid(g [T, nh, D]) (bf16; either may be a strided view
+    with a contiguous last dim) -- the gated-GQA output gate."""
+    if not y.is_cuda or y.dtype != torch.bfloat16 or g.dtype != torch.bfloat16:
+        y.copy_((y.float() * torch.sigmoid(g.float())).to(y.dtype))
+        return y
+    T, nh, D = y.shape
+    assert y.stride(2) == 1 and g.stride(2) == 1 and g.shape == y.shape
+    N.call("xtu_gate_mul", y.data_ptr(), y.stride(0), y.stride(1), g.data_ptr(), g.stride(0), g.stride(1), T, nh, D,
+           N.stream_ptr(y.device))
+    return y
+
+
+def shared_gate_(y: torch.Tensor, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """In place: y [T, H] *= sigmoid(x [T, H] . w) per token, w [1, H] or [H] (bf16) -- the
+    shared-expert gate."""
+    wv = w.reshape(-1)
+    if not y.is_cuda or y.dtype != torch.bfloat16 or x.dtype != torch.bfloat16 or wv.dtype != torch.bfloat16:
+        g = torch.sigmoid(x.float() @ wv.float())
+        y.copy_((y.float() * g[:, None]).to(y.dtype))
+        return y
+    T, H = y.shape
+    assert y.stride(1) == 1 and x.stride(1) == 1 and wv.is_contiguous() and x.shape == y.shape
+    N.call("xtu_shared_gate", y.data_ptr(), y.stride(0), x.data_ptr(), x.stride(0), wv.data_ptr(), T, H,
+           N.stream_ptr(y.device))
+    return y

@@ -408,8 +408,13 @@ def prepare_experts(fmt: str, w13: torch.Tensor, w2: torch.Tensor, s13=None, s2=
                     gs2=None) -> ExpertWeights:
     """Checkpoint layout (w13 [E, 2I, H] gate-then-up) -> kernel layout.
 
-    Interleaves gate/up rows in 128-row blocks when I % 128 == 0 (fused SwiGLU).
+    Interleaves gate/up rows in 128-row blocks when I % 128 == 0 (fused SwiGLU).  "int4"
+    (GPTQ rows kept at 4 bits for the CPU tier) is dequantized to bf16 for the GPU kernels.
     """
+    if fmt == "int4":
+        from .quant import dequant_int4_rows
+        dq = lambda w, sz: torch.stack([dequant_int4_rows(w[e], sz[e]) for e in range(w.shape[0])]).to(torch.bfloat16)
+        return prepare_experts("bf16", dq(w13, s13), dq(w2, s2))
     I = w13.shape[1] // 2
     inter = I % 128 == 0
     if inter:

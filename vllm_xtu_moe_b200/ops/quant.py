@@ -167,3 +167,41 @@ def dequant_gptq(qweight: torch.Tensor, scales: torch.Tensor, qzeros: torch.Tens
         z = torch.full((G, N), 1 << (bits - 1), dtype=torch.int64)
     w = (q - z[grp]).float() * scales.float()[grp]
     return w.t().contiguous()
+
+
+def gptq_to_int4_rows(qweight: torch.Tensor, scales: torch.Tensor, qzeros: torch.Tensor | None = None,
+                      g_idx: torch.Tensor | None = None, zero_offset: int = 1, group: int = 128):
+    """A 4-bit GPTQ linear weight kept at 4 bits, in the row layout of the CPU engine's INT4
+    format: (packed uint8 [out, in / 2], low nibble = even input index; scale / zero fp32
+    [out, in / group, 2]) with w[n, k] = (q - zero) * scale.  Returns None when the weight
+    is not in that form (group size other than ``group``, or act-order: g_idx not in input
+    order) -- the caller then dequantizes."""
+    K = qweight.shape[0] * 8
+    N = qweight.shape[1]
+    G = scales.shape[0]
+    if K % group or K // group != G:
+        return None
+    if g_idx is not None and not torch.equal(g_idx.to(torch.int64), torch.arange(K) // group):
+        return None
+    qw = qweight.to(torch.int64) & 0xFFFFFFFF
+    shifts = torch.arange(8, dtype=torch.int64) * 4
+    q = ((qw[:, None, :] >> shifts[None, :, None]) & 0xF).reshape(K, N).t().contiguous()   # [out, in]
+    packed = (q[:, 0::2] | (q[:, 1::2] << 4)).to(torch.uint8)
+    if qzeros is not None:
+        qz = qzeros.to(torch.int64) & 0xFFFFFFFF
+        z = ((qz[:, :, None] >> shifts[None, None, :]) & 0xF).reshape(G, -1)[:, :N] + zero_offset
+    else:
+        z = torch.full((G, N), 8, dtype=torch.int64)
+    sz = torch.stack([scales.float().t(), z.float().t()], dim=-1).contiguous()          # [out, G, 2]
+    return packed, sz
+
+
+def dequant_int4_rows(packed: torch.Tensor, sz: torch.Tensor) -> torch.Tensor:
+    """INT4 rows (``gptq_to_int4_rows``; leading dims allowed) -> fp32 [..., out, in]."""
+    lo = (packed & 0xF).to(torch.float32)
+    hi = (packed >> 4).to(torch.float32)
+    q = torch.stack([lo, hi], dim=-1).flatten(-2)                                   # [..., out, in]
+    group = q.shape[-1] // sz.shape[-2]
+    s = sz[..., 0].repeat_interleave(group, dim=-1)
+    z = sz[..., 1].repeat_interleave(group, dim=-1)
+    return (q - z) * s

@@ -24,7 +24,7 @@ _LIB = Path(__file__).resolve().parent.parent / "_lib" / "libxtu_cpu.so"
 _lock = threading.Lock()
 _lib = None
 
-FMT = {"bf16": 0, "fp8": 1, "mxfp4": 2, "nvfp4": 3}
+FMT = {"bf16": 0, "fp8": 1, "mxfp4": 2, "nvfp4": 3, "int4": 4}
 P, I_, F = ctypes.c_void_p, ctypes.c_int, ctypes.c_float
 
 
@@ -95,8 +95,10 @@ class CpuExpertEngine:
         self.H = w2.shape[1]
         ts = [t.detach().contiguous().cpu() if t is not None else None for t in (w13, w2, s13, s2, gs13, gs2)]
         w13c, w2c, s13c, s2c, gs13c, gs2c = ts
-        if fmt == "fp8":
-            s13c, s2c = s13c.float(), s2c.float()
+        if fmt in ("fp8", "int4"):
+            s13c, s2c = s13c.float().contiguous(), s2c.float().contiguous()
+        if fmt == "int4" and (self.H % 128 or self.I % 128):
+            raise ValueError("INT4 experts need H and I in multiples of the 128-wide quantization group")
         if gs13c is not None:
             gs13c = gs13c.float().reshape(-1)
             gs2c = gs2c.float().reshape(-1)

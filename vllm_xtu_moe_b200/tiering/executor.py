@@ -248,6 +248,7 @@ class TieredExperts:
                               act_limit=c.swiglu_limit, int8_mode=mode, int8_min_tokens=self.ec.moe_int8_min_tokens,
                               deadline_ms=self.ec.pool_deadline_ms)
         host = pool = None
+        # "int4" (GPTQ kept at 4 bits) has no GPU slot format: its pairs all run on the CPU tier
         if self.device.type == "cuda" and fmt in GPU_FMTS:
             scales = HostExperts.gpu_scales_from_checkpoint(fmt, _cpu(raw.get("s13")), _cpu(raw.get("s2")),
                                                             _cpu(raw.get("gs13")), _cpu(raw.get("gs2")))
