@@ -246,10 +246,13 @@ __global__ void __launch_bounds__(256) gdn_gated_norm_kernel(const float* __rest
   }
 }
 
-// grid: (B, ceil(ch / 256)); the new state of each channel = its last kw-1 inputs
+// grid: (B, ceil(ch / 256)); the new state of each channel = its last kw-1 inputs.
+// spec_conv (speculative verification steps of at most spec_n tokens per sequence): also
+// the state after each token j of the step, spec_conv [slots, spec_n, ch, kw-1].
 __global__ void gdn_conv_state_kernel(const __nv_bfloat16* __restrict__ qkvz, GdnShape s,
                                       __nv_bfloat16* __restrict__ conv_state, const int* __restrict__ q_start,
-                                      const int* __restrict__ slots, const int* __restrict__ fresh) {
+                                      const int* __restrict__ slots, const int* __restrict__ fresh,
+                                      __nv_bfloat16* __restrict__ spec_conv, int spec_n) {
   const int b = blockIdx.x;
   const int nq = s.nk * s.dk;
   const int ch = 2 * nq + s.nv * s.dv;
@@ -263,24 +266,55 @@ __global__ void gdn_conv_state_kernel(const __nv_bfloat16* __restrict__ qkvz, Gd
   const bool is_fresh = fresh != nullptr && fresh[b] != 0;
   const int col = qkvz_col(s, c);
   __nv_bfloat16* st = conv_state + ((size_t)slot * ch + c) * (s.kw - 1);
-  __nv_bfloat16 nw[8];
-  for (int j = 0; j < s.kw - 1; ++j) {
-    const int pos = L - (s.kw - 1) + j;    // index in [old state ++ chunk] relative to chunk start
-    if (pos >= 0) nw[j] = qkvz[(size_t)(t0 + pos) * s.qkvz_stride + col];
-    else nw[j] = is_fresh ? __float2bfloat16(0.f) : st[(s.kw - 1) + pos];
+  // input at position pos of [old state ++ step] (pos < 0: the old state)
+  auto input = [&](int pos) -> __nv_bfloat16 {
+    if (pos >= 0) return qkvz[(size_t)(t0 + pos) * s.qkvz_stride + col];
+    return is_fresh ? __float2bfloat16(0.f) : st[(s.kw - 1) + pos];
+  };
+  if (spec_conv != nullptr) {
+    for (int j = 0; j < L && j < spec_n; ++j) {
+      __nv_bfloat16* dst = spec_conv + (((size_t)slot * spec_n + j) * ch + c) * (s.kw - 1);
+      for (int i = 0; i < s.kw - 1; ++i) dst[i] = input(j - (s.kw - 2) + i);
+    }
   }
+  __nv_bfloat16 nw[8];
+  for (int j = 0; j < s.kw - 1; ++j) nw[j] = input(L - (s.kw - 1) + j);
   for (int j = 0; j < s.kw - 1; ++j) st[j] = nw[j];
+}
+
+// Speculative verification: per sequence b, the states after its accepted position
+// acc[b] (of the step's spec_n) become the slot's states.  grid (B, 64); block 256.
+__global__ void gdn_spec_commit_kernel(const int* __restrict__ acc, const int* __restrict__ slots, int spec_n,
+                                       const float4* __restrict__ spec_ssm, float4* __restrict__ ssm,
+                                       long long ssm_vec, const __nv_bfloat16* __restrict__ spec_conv,
+                                       __nv_bfloat16* __restrict__ conv, long long conv_elems) {
+  const int b = blockIdx.x;
+  const int slot = slots[b];
+  if (slot < 0) return;
+  const int a = min(max(acc[b], 0), spec_n - 1);
+  const float4* src = spec_ssm + ((size_t)slot * spec_n + a) * ssm_vec;
+  float4* dst = ssm + (size_t)slot * ssm_vec;
+  for (long long i = (long long)blockIdx.y * blockDim.x + threadIdx.x; i < ssm_vec; i += (long long)gridDim.y * blockDim.x)
+    dst[i] = src[i];
+  const __nv_bfloat16* cs = spec_conv + ((size_t)slot * spec_n + a) * conv_elems;
+  __nv_bfloat16* cd = conv + (size_t)slot * conv_elems;
+  for (long long i = (long long)blockIdx.y * blockDim.x + threadIdx.x; i < conv_elems;
+       i += (long long)gridDim.y * blockDim.x)
+    cd[i] = cs[i];
 }
 
 constexpr int GDN_COLS = 32;       // state columns per CTA
 constexpr int GDN_TB = 16;         // tokens staged in shared memory at a time
 
 // grid: (B, nv, dv / 32); block 128: lane = col8 * 4 + rq (8 columns x 4 row quarters per warp)
+// spec_ssm (speculative verification): also the state after each token j of the step,
+// spec_ssm [slots, spec_n, nv, DK, dv].
 template <int DK, bool CH>
 __global__ void __launch_bounds__(128) gdn_recurrent_kernel(
     const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v, const float* __restrict__ g,
     const float* __restrict__ beta, const int* __restrict__ q_start, const int* __restrict__ slots,
-    const int* __restrict__ fresh, float* __restrict__ ssm, float* __restrict__ out, int nk, int nv, int dv) {
+    const int* __restrict__ fresh, float* __restrict__ ssm, float* __restrict__ out, int nk, int nv, int dv,
+    float* __restrict__ spec_ssm, int spec_n) {
   constexpr int RPT = DK / 4;                 // state rows per thread
   __shared__ float sq[GDN_TB][DK], sk[GDN_TB][DK];
   __shared__ float sv[GDN_TB][GDN_COLS], sg[GDN_TB], sb[GDN_TB];
@@ -358,6 +392,11 @@ __global__ void __launch_bounds__(128) gdn_recurrent_kernel(
 #pragma unroll
         for (int i = 0; i < RPT; ++i) S[i] *= c;
         c = 1.f;
+      }
+      if (spec_ssm != nullptr && S_g != nullptr && tb + tt - t0 < spec_n) {
+        float* sp = spec_ssm + ((((size_t)slot * spec_n + (tb + tt - t0)) * nv + h) * DK) * dv;
+#pragma unroll
+        for (int i = 0; i < RPT; ++i) sp[(size_t)(4 * i + rq) * dv + col] = S[i] * c;
       }
     }
   }
@@ -871,13 +910,18 @@ extern "C" {
 // y != nullptr: y bf16 [T, nv*dv] <- gated RMSNorm of out with weight norm_w fp32 [dv]; the
 // gate is silu(z) of the qkvz rows (gate_mode 0; gate = qkvz) or sigmoid of a bf16
 // [T, gate_stride] tensor (gate_mode 1).
+// spec_ssm / spec_conv (speculative verification, at most spec_n tokens per sequence): the
+// recurrent and conv states after every token of the step, [slots, spec_n, ...] each (the
+// final states are written to ssm / conv_state as usual); xtu_deltanet_spec_commit then
+// installs the ones of each sequence's accepted position.
 // Returns kernels launched or a negative error.
 int xtu_deltanet_fwd(const void* qkvz, int qkvz_stride, int T, int B, const int* q_start, const int* slots,
                      const int* fresh, int nk, int nv, int dk, int dv, int kw, const float* conv_w, void* conv_state,
                      float* ssm, float* g, float* beta, float* qs, float* ks, float* vs, float* out,
                      int blocked, int g_channels, int chunked, float* chunk_ws, const void* ba, int ba_stride,
                      const float* A_log, const float* dt_bias, const void* gate, int gate_stride, int gate_mode,
-                     const float* norm_w, float eps, void* y, cudaStream_t stream) {
+                     const float* norm_w, float eps, void* y, float* spec_ssm, void* spec_conv, int spec_n,
+                     cudaStream_t stream) {
   if (T <= 0 || B <= 0) return 0;
   if (dk != 128 || dv % GDN_COLS != 0 || dv > 256 || kw < 2 || kw > 9 || nv % nk != 0) return -2;
   if (ba != nullptr && (g_channels || blocked || A_log == nullptr || dt_bias == nullptr)) return -2;
@@ -886,7 +930,8 @@ int xtu_deltanet_fwd(const void* qkvz, int qkvz_stride, int T, int B, const int*
   const int ch = 2 * nk * dk + nv * dv;
   GdnGates gt{(const __nv_bfloat16*)ba, ba_stride, A_log, dt_bias, g, beta};
   int launched = 2;
-  const bool use_chunks = chunked && chunk_ws != nullptr && !g_channels && dv == GD;
+  // speculative verification steps keep per-token states: token-serial kernel only
+  const bool use_chunks = chunked && chunk_ws != nullptr && !g_channels && dv == GD && spec_ssm == nullptr;
   const int tok_per_cta = GDN_CONV_WARPS * GDN_CONV_TPW;
   const dim3 cgrid((T + tok_per_cta - 1) / tok_per_cta, 2 * nk + nv);
 #define XTU_GDN_CONV(KWV)                                                                                        \
@@ -909,9 +954,9 @@ int xtu_deltanet_fwd(const void* qkvz, int qkvz_stride, int T, int B, const int*
     default: XTU_GDN_CONV(9); break;
   }
 #undef XTU_GDN_CONV
-  gdn_conv_state_kernel<<<dim3(B, (ch + 255) / 256), 256, 0, stream>>>((const __nv_bfloat16*)qkvz, s,
-                                                                        (__nv_bfloat16*)conv_state, q_start, slots,
-                                                                        fresh);
+  gdn_conv_state_kernel<<<dim3(B, (ch + 255) / 256), 256, 0, stream>>>(
+      (const __nv_bfloat16*)qkvz, s, (__nv_bfloat16*)conv_state, q_start, slots, fresh,
+      (__nv_bfloat16*)spec_conv, spec_n);
   if (use_chunks) {
     cudaError_t ea = cudaFuncSetAttribute(gdn_chunk_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           GDN_PREP_SMEM);
@@ -927,12 +972,12 @@ int xtu_deltanet_fwd(const void* qkvz, int qkvz_stride, int T, int B, const int*
         qs, ks, vs, ws_w, ws_p, ws_g, q_start, slots, fresh, ssm, out, nk, nv);
     launched += 2;
   } else if (g_channels) {
-    gdn_recurrent_kernel<128, true><<<dim3(B, nv, dv / GDN_COLS), 128, 0, stream>>>(qs, ks, vs, g, beta, q_start,
-                                                                                  slots, fresh, ssm, out, nk, nv, dv);
+    gdn_recurrent_kernel<128, true><<<dim3(B, nv, dv / GDN_COLS), 128, 0, stream>>>(
+        qs, ks, vs, g, beta, q_start, slots, fresh, ssm, out, nk, nv, dv, spec_ssm, spec_n);
     launched += 1;
   } else {
-    gdn_recurrent_kernel<128, false><<<dim3(B, nv, dv / GDN_COLS), 128, 0, stream>>>(qs, ks, vs, g, beta, q_start,
-                                                                                   slots, fresh, ssm, out, nk, nv, dv);
+    gdn_recurrent_kernel<128, false><<<dim3(B, nv, dv / GDN_COLS), 128, 0, stream>>>(
+        qs, ks, vs, g, beta, q_start, slots, fresh, ssm, out, nk, nv, dv, spec_ssm, spec_n);
     launched += 1;
   }
   if (y != nullptr) {
@@ -942,6 +987,20 @@ int xtu_deltanet_fwd(const void* qkvz, int qkvz_stride, int T, int B, const int*
   }
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? launched : -(int)e;
+}
+
+// acc [B]: the accepted position of each sequence (0 .. spec_n - 1); slots [B] (< 0 skipped);
+// ssm fp32 [slots, ssm_elems], conv bf16 [slots, conv_elems] <- their spec_n-way copies.
+int xtu_deltanet_spec_commit(const int* acc, const int* slots, int B, int spec_n, const float* spec_ssm, float* ssm,
+                             long long ssm_elems, const void* spec_conv, void* conv, long long conv_elems,
+                             cudaStream_t stream) {
+  if (B <= 0) return 0;
+  if (ssm_elems % 4 != 0) return -2;
+  gdn_spec_commit_kernel<<<dim3(B, 64), 256, 0, stream>>>(acc, slots, spec_n, (const float4*)spec_ssm, (float4*)ssm,
+                                                          ssm_elems / 4, (const __nv_bfloat16*)spec_conv,
+                                                          (__nv_bfloat16*)conv, conv_elems);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 1 : -(int)e;
 }
 
 }  // extern "C"

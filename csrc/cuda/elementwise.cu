@@ -877,6 +877,41 @@ static inline int rc_last(int launched = 1) {
   return e == cudaSuccess ? launched : -(int)e;
 }
 
+// ---------------------------------------------------------------------------
+// sigmoid gates
+//   gate_mul:    y[t, h, d] *= sigmoid(g[t, h, d])   (gated-GQA output gate; y and g strided)
+//   shared_gate: y[t, :]    *= sigmoid(x[t, :] . w)  (Qwen3-Next shared-expert gate, w [H])
+// ---------------------------------------------------------------------------
+__global__ void gate_mul_kernel(__nv_bfloat16* __restrict__ y, int y_tok, int y_head,
+                                const __nv_bfloat16* __restrict__ g, int g_tok, int g_head, int nh, int D) {
+  const int t = blockIdx.x / nh, h = blockIdx.x - (blockIdx.x / nh) * nh;
+  __nv_bfloat16* yr = y + (size_t)t * y_tok + (size_t)h * y_head;
+  const __nv_bfloat16* gr = g + (size_t)t * g_tok + (size_t)h * g_head;
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    const float gv = __bfloat162float(gr[d]);
+    yr[d] = __float2bfloat16(__bfloat162float(yr[d]) / (1.f + __expf(-gv)));
+  }
+}
+
+// one warp per token
+__global__ void shared_gate_kernel(__nv_bfloat16* __restrict__ y, int y_stride, const __nv_bfloat16* __restrict__ x,
+                                   int x_stride, const __nv_bfloat16* __restrict__ w, int T, int H) {
+  const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (t >= T) return;
+  const __nv_bfloat16* xr = x + (size_t)t * x_stride;
+  float acc = 0.f;
+  for (int i = lane * 2; i < H; i += 64) {
+    const __nv_bfloat162 xv = *reinterpret_cast<const __nv_bfloat162*>(xr + i);
+    const __nv_bfloat162 wv = *reinterpret_cast<const __nv_bfloat162*>(w + i);
+    acc = fmaf(__low2float(xv), __low2float(wv), acc);
+    acc = fmaf(__high2float(xv), __high2float(wv), acc);
+  }
+  acc = warp_sum(acc);
+  const float s = 1.f / (1.f + __expf(-acc));
+  __nv_bfloat16* yr = y + (size_t)t * y_stride;
+  for (int i = lane; i < H; i += 32) yr[i] = __float2bfloat16(__bfloat162float(yr[i]) * s);
+}
+
 extern "C" {
 
 // y16 (nullable): also write y as f16 x 2^-8 rows [T, H] (the fp8-weight GEMVs' input form)
@@ -1080,6 +1115,22 @@ int xtu_embed_host(const int* ids, const void* host_table, int T, int H, int voc
   }
   embed_kernel<<<T, 256, 0, s>>>(ids, (const __nv_bfloat16*)dtab, T, H, vocab, (__nv_bfloat16*)out,
                                  reinterpret_cast<XtuStatus*>(status));
+  return rc_last();
+}
+
+int xtu_gate_mul(void* y, int y_tok, int y_head, const void* g, int g_tok, int g_head, int T, int nh, int D,
+                 cudaStream_t s) {
+  if (T <= 0) return 0;
+  gate_mul_kernel<<<T * nh, D >= 128 ? 128 : 64, 0, s>>>((__nv_bfloat16*)y, y_tok, y_head, (const __nv_bfloat16*)g,
+                                                         g_tok, g_head, nh, D);
+  return rc_last();
+}
+
+int xtu_shared_gate(void* y, int y_stride, const void* x, int x_stride, const void* w, int T, int H, cudaStream_t s) {
+  if (T <= 0) return 0;
+  if (H % 2 != 0) return -2;
+  shared_gate_kernel<<<(T * 32 + 255) / 256, 256, 0, s>>>((__nv_bfloat16*)y, y_stride, (const __nv_bfloat16*)x,
+                                                          x_stride, (const __nv_bfloat16*)w, T, H);
   return rc_last();
 }
 

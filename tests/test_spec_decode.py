@@ -67,15 +67,33 @@ def test_oracle_drafts_are_all_accepted():
     assert steps < steps0
 
 
-def test_spec_decoder_rejects_linear_attention_models():
-    cfg = scaled_down(get_preset("qwen3-next-80b-a3b"), layers=4, hidden=256, experts=16).replace(
+def _qwen_cfg():
+    return scaled_down(get_preset("qwen3-next-80b-a3b"), layers=4, hidden=256, experts=16).replace(
         num_heads=4, num_kv_heads=2, head_dim=64, moe_intermediate=256, shared_intermediate=256,
         linear_num_key_heads=2, linear_num_value_heads=4, linear_key_head_dim=32, linear_value_head_dim=32,
         rotary_dim=32, num_mtp_layers=1)
-    m = build_model(cfg, device="cpu", seed=0)
-    with pytest.raises(NotImplementedError):
-        LLM(m, device="cpu", runner_config=RunnerConfig(block_size=16, max_seqs=2, max_model_len=128,
-                                                        max_batched_tokens=64, use_cuda_graph=False, num_spec=2))
+
+
+@pytest.mark.parametrize("oracle", [False, True])
+def test_spec_decode_linear_attention_rolls_back_state_cpu(oracle):
+    """Qwen3-Next-style hybrid (DeltaNet + gated GQA) with its MTP layer: the recurrent
+    state after a verification step is the one after the last accepted token, so tokens
+    equal plain greedy decoding, with MTP drafts (mostly rejected) and with oracle drafts
+    (all accepted but a wrong tail appended every step, so every step rolls back)."""
+    m = build_model(_qwen_cfg(), device="cpu", seed=0)
+    m.act_dtype = torch.float32
+    prompts = [list(range(3, 30)), list(range(50, 58))]
+    base, steps0 = _run(m, 0, prompts, 12)
+    if not oracle:
+        spec, _ = _run(m, 3, prompts, 12)
+    else:
+        ref = {tuple(p): o.token_ids for p, o in zip(prompts, base)}
+        half = {tuple(p): (o.token_ids[:2] + [1, 2, 3] * 8) for p, o in zip(prompts, base)}
+        spec, steps = _run(m, 3, prompts, 12, oracle=ref)
+        assert steps < steps0
+        spec2, _ = _run(m, 3, prompts, 12, oracle=half)     # right, then wrong drafts
+        assert [o.token_ids for o in spec2] == [o.token_ids for o in base]
+    assert [o.token_ids for o in spec] == [o.token_ids for o in base]
 
 
 @pytest.mark.gpu
@@ -224,3 +242,32 @@ def test_sampled_requests_with_mtp_cpu():
     assert outs[0][0] == base[0].token_ids            # the greedy request is unchanged
     assert outs[0][1] == outs[1][1] and len(outs[0][1]) == 10
     assert outs[0][2] > 0                              # the sampled request was drafted for
+
+
+@pytest.mark.gpu
+def test_spec_decode_linear_attention_gpu():
+    """Hybrid DeltaNet + gated-GQA model with MTP on the GPU: per-token recurrent / conv
+    states of the verification step and their commit (eager and inside the replayed graph)
+    give the tokens of plain greedy decoding (up to split-KV rounding)."""
+    cfg = _qwen_cfg().replace(linear_key_head_dim=128, linear_value_head_dim=128, linear_num_key_heads=1,
+                              linear_num_value_heads=2)
+    m = build_model(cfg, device="cuda", seed=2)
+    prompts = [list(range(3, 40)), list(range(50, 61)), list(range(100, 170))]
+
+    def run(k_, graph):
+        rc = RunnerConfig(block_size=64, max_seqs=4, max_model_len=512, max_batched_tokens=128,
+                          use_cuda_graph=graph, num_spec=k_)
+        llm = LLM(m, device="cuda", runner_config=rc)
+        outs = llm.generate(prompts, SamplingParams(max_tokens=20))
+        gsteps = llm.spec.graph_steps if llm.spec is not None else 0
+        llm.shutdown()
+        return outs, gsteps
+
+    plain, _ = run(0, True)
+    eager, _ = run(3, False)
+    graph, g1 = run(3, True)
+    assert g1 > 0
+    total = sum(len(o.token_ids) for o in plain)
+    for other in (eager, graph):
+        same = sum(a == b for x, y in zip(plain, other) for a, b in zip(x.token_ids, y.token_ids))
+        assert same >= 0.9 * total, (plain, other)

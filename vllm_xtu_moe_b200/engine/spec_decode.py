@@ -27,8 +27,11 @@ removed and renormalised, and a fully accepted chain adds a draw from the last r
 every emitted token is then an exact sample of the request's distribution.  Those steps
 run eagerly (the sampling draws are made with the request's own generator).
 
-Linear-attention (DeltaNet) models are not drafted: their recurrent state would
-need a rollback for rejected drafts.
+Linear-attention (DeltaNet / KDA) layers carry a recurrent state that rejected drafts
+must not advance: a verification step keeps the state after each of its rows
+(``DeltaNetState.spec_ssm`` / ``spec_conv``, written by the recurrent and conv-state
+kernels), and once the acceptance is known a kernel installs, per sequence, the states
+after its last accepted row (``xtu_deltanet_spec_commit``; inside the replayed graph).
 
 On a GPU a decode step whose requests all carry k drafts replays one CUDA graph per batch
 bucket: the verification forward, the acceptance kernel, the MTP pass over the verified
@@ -101,8 +104,11 @@ class SpecDecoder:
         self.k = k
         if not self.model.mtp:
             raise ValueError("speculative decoding needs a model with an MTP layer")
-        if any(self.model.cfg.layer_type(i) == "linear" for i in range(self.model.cfg.num_layers)):
-            raise NotImplementedError("MTP drafting with linear-attention layers (no state rollback)")
+        from ..models.deltanet import DeltaNetState
+        # recurrent layers: k + 1 state copies per slot for the rollback of rejected drafts
+        self.states = [c for c in runner.caches if isinstance(c, DeltaNetState)]
+        for st in self.states:
+            st.enable_spec(max(k, runner.rc.num_spec))
         self.mtp = self.model.mtp[0]
         self.caches = runner.mtp_caches[0]
         rc = runner.rc
@@ -154,6 +160,10 @@ class SpecDecoder:
         return torch.stack(drafts, dim=1).tolist()
 
     # ------------------------------------------------------------------ engine hooks
+    def _commit(self, accepted: torch.Tensor, slots: torch.Tensor) -> None:
+        for st in self.states:
+            st.commit_spec(accepted, slots)
+
     def after_prefill(self, r, extra) -> None:
         r.draft = []
 
@@ -228,13 +238,15 @@ class SpecDecoder:
         meta = AttnMetadata(num_seqs=b, q_start=st["q_start"][:b + 1], kv_len=st["kv_len"][:b],
                             block_table=st["bt"][:b], slot_mapping=st["slots"][:R], positions=st["pos"][:R],
                             max_q_len=k + 1, max_kv_len=rn.rc.max_model_len, is_decode=True,
-                            seq_slots=st["seq_slots"][:b], seq_fresh=st["fresh"][:b], num_splits=splits)
+                            seq_slots=st["seq_slots"][:b], seq_fresh=st["fresh"][:b], num_splits=splits,
+                            spec_rows=k + 1)
         out = st["out"][b]
         tgt_o, acc_o, drf_o = out[:R], out[R:R + b], out[R + b:].view(b, k)
         tgt, h, _, _ = rn.forward(st["ids"][:R], meta, st["rows"][:R])
         last = torch.empty(b, dtype=torch.int32, device=rn.device)
         N.call("xtu_spec_verify", tgt.data_ptr(), st["ids"].data_ptr(), meta.q_start.data_ptr(), b, k,
                acc_o.data_ptr(), last.data_ptr(), N.stream_ptr(rn.device))
+        self._commit(acc_o, st["seq_slots"][:b])
         hid = self._mtp(tgt, h, meta).index_select(0, last.long())
         tok = B.argmax(m.logits(hid))
         drf_o[:, 0].copy_(tok)
@@ -278,6 +290,8 @@ class SpecDecoder:
         w = meta.block_table.shape[1]
         st["bt"][:n, :w].copy_(meta.block_table)
         st["seq_slots"][:b].fill_(-1)
+        if meta.seq_slots is not None:        # recurrent-state slots (linear-attention layers)
+            st["seq_slots"][:n].copy_(meta.seq_slots)
         st["fresh"][:b].zero_()
         base = torch.tensor([ch.req.total_len for ch in plan.chunks] + [0] * (b - n), dtype=torch.int32)
         rn.h2d_bytes += base.numel() * 4
@@ -350,6 +364,7 @@ class SpecDecoder:
         self.eager_steps += 1
         rn = self.runner
         ids, meta = rn.build_meta(plan)
+        meta.spec_rows = meta.max_q_len
         n_rows = ids.shape[0]
         tgt, h, _, logits = rn.forward(ids, meta, torch.arange(n_rows, device=rn.device))
         k = max(len(ch.req.draft) for ch in plan.chunks)
@@ -379,6 +394,8 @@ class SpecDecoder:
             last = torch.tensor(last_l, dtype=torch.long, device=rn.device)
         else:
             acc, last = verify_greedy(tgt, ids, meta.q_start, meta.num_seqs, k)
+        if self.states and meta.seq_slots is not None:
+            self._commit(acc.to(device=rn.device, dtype=torch.int32), meta.seq_slots)
         out = self._mtp(emit, h, meta)
         hid = out.index_select(0, last.long())
         first = B.argmax(self.model.logits(hid))

@@ -191,7 +191,7 @@ def qwen3_next_80b() -> ModelConfig:
                        linear_value_head_dim=128, linear_conv_kernel=4, num_experts=512, top_k=10,
                        moe_intermediate=512, num_shared_experts=1, shared_intermediate=512, shared_expert_gate=True,
                        scoring="softmax", norm_topk_prob=True, expert_fmt="mxfp4", dense_fmt="bf16",
-                       norm_add_one=True, norm_eps=1e-6, max_position=262144)
+                       norm_add_one=True, norm_eps=1e-6, max_position=262144, num_mtp_layers=1)
 
 
 def glm45_air() -> ModelConfig:
@@ -348,7 +348,9 @@ def from_hf_config(path_or_dict) -> ModelConfig:
                            top_k=hf["num_experts_per_tok"], moe_intermediate=hf["moe_intermediate_size"],
                            num_shared_experts=1, shared_intermediate=hf["shared_expert_intermediate_size"],
                            shared_expert_gate=True, scoring="softmax", norm_topk_prob=hf.get("norm_topk_prob", True),
-                           expert_fmt=fmt, norm_add_one=True, **base)
+                           expert_fmt=fmt, norm_add_one=True,
+                           num_mtp_layers=min(1, hf.get("mtp_num_hidden_layers", hf.get("num_nextn_predict_layers", 0))),
+                           **base)
     if archs.startswith("MiMoV2"):
         # keys read: hybrid_layer_pattern (per layer, 1 = sliding window), sliding_window,
         # swa_num_key_value_heads, v_head_dim, partial_rotary_factor,

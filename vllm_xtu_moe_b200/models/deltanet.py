@@ -36,21 +36,55 @@ from .layers import Linear
 
 
 class DeltaNetState:
-    """Recurrent state [slots, nv, dk, dv] fp32 and conv state [slots, channels, kernel-1]."""
+    """Recurrent state [slots, nv, dk, dv] fp32 and conv state [slots, channels, kernel-1].
+
+    With speculative decoding (``enable_spec(k)``) each slot also has k + 1 copies of both,
+    ``spec_ssm`` / ``spec_conv``: a verification step writes the states after each of its
+    (at most k + 1) tokens there, and ``commit_spec`` installs, per sequence, the ones after
+    its last accepted token -- the rollback of rejected drafts."""
 
     def __init__(self, cfg: ModelConfig, max_slots: int, device):
         nv, dk, dv = cfg.linear_num_value_heads, cfg.linear_key_head_dim, cfg.linear_value_head_dim
         ch = 2 * cfg.linear_num_key_heads * dk + nv * dv
         self.ssm = torch.zeros(max_slots, nv, dk, dv, dtype=torch.float32, device=device)
         self.conv = torch.zeros(max_slots, ch, cfg.linear_conv_kernel - 1, dtype=torch.bfloat16, device=device)
+        self.spec_ssm: torch.Tensor | None = None
+        self.spec_conv: torch.Tensor | None = None
+
+    def enable_spec(self, k: int) -> None:
+        n = k + 1
+        if self.spec_ssm is not None and self.spec_ssm.shape[1] >= n:
+            return
+        self.spec_ssm = torch.zeros(self.ssm.shape[0], n, *self.ssm.shape[1:], dtype=torch.float32,
+                                    device=self.ssm.device)
+        self.spec_conv = torch.zeros(self.conv.shape[0], n, *self.conv.shape[1:], dtype=torch.bfloat16,
+                                     device=self.conv.device)
+
+    def commit_spec(self, accepted: torch.Tensor, slots: torch.Tensor) -> None:
+        """Per sequence b with slot >= 0: states <- the copies after position accepted[b]."""
+        n = self.spec_ssm.shape[1]
+        if self.ssm.is_cuda:
+            from ..ops import _native as N
+            N.call("xtu_deltanet_spec_commit", accepted.data_ptr(), slots.data_ptr(), slots.numel(), n,
+                   self.spec_ssm.data_ptr(), self.ssm.data_ptr(), self.ssm[0].numel(), self.spec_conv.data_ptr(),
+                   self.conv.data_ptr(), self.conv[0].numel(), N.stream_ptr(self.ssm.device))
+            return
+        for a, sl in zip(accepted.tolist(), slots.tolist()):
+            if sl >= 0:
+                a = min(max(int(a), 0), n - 1)
+                self.ssm[sl].copy_(self.spec_ssm[sl, a])
+                self.conv[sl].copy_(self.spec_conv[sl, a])
 
     def nbytes(self) -> int:
-        return self.ssm.numel() * 4 + self.conv.numel() * 2
+        n = self.ssm.numel() * 4 + self.conv.numel() * 2
+        if self.spec_ssm is not None:
+            n += self.spec_ssm.numel() * 4 + self.spec_conv.numel() * 2
+        return n
 
 
-def _delta_rule_ref(q, k, v, g, beta, state):
+def _delta_rule_ref(q, k, v, g, beta, state, per_token: torch.Tensor | None = None):
     """q,k [T, H, dk], v [T, H, dv], g [T, H] (or [T, H, dk]: a decay per key dim), beta [T, H];
-    state [H, dk, dv] (updated in place)."""
+    state [H, dk, dv] (updated in place); per_token [>= T, H, dk, dv]: the state after each token."""
     T = q.shape[0]
     out = torch.empty(T, v.shape[1], v.shape[2], dtype=torch.float32, device=q.device)
     S = state
@@ -60,6 +94,8 @@ def _delta_rule_ref(q, k, v, g, beta, state):
         delta = (v[t] - kv_mem) * beta[t][:, None]
         S.add_(torch.einsum("hk,hv->hkv", k[t], delta))
         out[t] = torch.einsum("hkv,hk->hv", S, q[t])
+        if per_token is not None and t < per_token.shape[0]:
+            per_token[t].copy_(S)
     return out
 
 
@@ -221,6 +257,10 @@ def deltanet_ref(mixed, conv_w, g, beta, meta, state: DeltaNetState, nk, nv, dk,
         for j in range(kw):
             conv += full[j:j + L] * w[:, j]
         conv = F.silu(conv)
+        spec = getattr(meta, "spec_rows", 0) > 0 and state.spec_ssm is not None and slot >= 0
+        if spec:       # the conv state after each token j: inputs j+1 .. j+kw-1 of [history ++ step]
+            for j in range(min(L, state.spec_conv.shape[1])):
+                state.spec_conv[slot, j].copy_(full[j + 1:j + kw].t().to(state.conv.dtype))
         conv_st.copy_(full[-(kw - 1):].t().to(state.conv.dtype))
         q = conv[:, : nk * dk].view(L, nk, dk)
         k = conv[:, nk * dk: 2 * nk * dk].view(L, nk, dk)
@@ -229,5 +269,6 @@ def deltanet_ref(mixed, conv_w, g, beta, meta, state: DeltaNetState, nk, nv, dk,
         k = F.normalize(k, dim=-1)
         q = q.repeat_interleave(r, dim=1)
         k = k.repeat_interleave(r, dim=1)
-        out[s0:s1] = _delta_rule_ref(q, k, v, g[s0:s1], beta[s0:s1], ssm_st)
+        out[s0:s1] = _delta_rule_ref(q, k, v, g[s0:s1], beta[s0:s1], ssm_st,
+                                     state.spec_ssm[slot] if spec else None)
     return out

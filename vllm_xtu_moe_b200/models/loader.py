@@ -81,12 +81,17 @@ class CheckpointSource:
         m = re.match(r"model\.layers\.(\d+)\.(.+)$", name)
         if m:
             return f"model.layers.{m.group(1)}", m.group(2)
+        # MTP layers: GLM / DeepSeek number them after the decoder layers; Qwen3-Next keeps
+        # them under "mtp.layers.{j}"
+        qn = self.cfg.arch == "qwen3_next"
         m = re.match(r"model\.mtp(\d+)\.(\d+)\.(.+)$", name)
         if m:
-            return f"model.layers.{self.cfg.num_layers + int(m.group(1))}", m.group(3)
+            j = int(m.group(1))
+            return (f"mtp.layers.{j}" if qn else f"model.layers.{self.cfg.num_layers + j}"), m.group(3)
         m = re.match(r"model\.mtp(\d+)\.(.+)$", name)
         if m:
-            return f"model.layers.{self.cfg.num_layers + int(m.group(1))}", m.group(2)
+            j = int(m.group(1))
+            return (f"mtp.layers.{j}" if qn else f"model.layers.{self.cfg.num_layers + j}"), m.group(2)
         raise KeyError(name)
 
     def _hf(self, name: str) -> list[str]:
@@ -98,7 +103,12 @@ class CheckpointSource:
             return fixed[name]
         m = re.match(r"mtp(\d+)\.eh$", name)
         if m:
-            return [f"model.layers.{c.num_layers + int(m.group(1))}.eh_proj"]
+            return ["mtp.fc"] if c.arch == "qwen3_next" else [f"model.layers.{c.num_layers + int(m.group(1))}.eh_proj"]
+        if c.arch == "qwen3_next":      # the MTP module's own norms (one MTP layer)
+            m = re.match(r"model\.mtp\d+\.(enorm|hnorm|head_norm)$", name)
+            if m:
+                return [{"enorm": "mtp.pre_fc_norm_embedding.weight", "hnorm": "mtp.pre_fc_norm_hidden.weight",
+                         "head_norm": "mtp.norm.weight"}[m.group(1)]]
         pre, rest = self._layer_prefix(name)
         sa = "self_attn"
         table = {

@@ -61,7 +61,9 @@ _SIGS: dict[str, list] = {
                             c_float, c_float, c_float, P, c_int, P, P],
     "xtu_spec_chain_meta": [P, P, P, c_int, c_int, c_int, c_int, c_int, P, P, P, P],
     "xtu_deltanet_fwd": [P, c_int, c_int, c_int, P, P, P, c_int, c_int, c_int, c_int, c_int, P, P, P, P, P,
-                         P, P, P, P, c_int, c_int, c_int, P, P, c_int, P, P, P, c_int, c_int, P, c_float, P, P],
+                         P, P, P, P, c_int, c_int, c_int, P, P, c_int, P, P, P, c_int, c_int, P, c_float, P, P, P,
+                         c_int, P],
+    "xtu_deltanet_spec_commit": [P, P, c_int, c_int, P, P, ctypes.c_longlong, P, P, ctypes.c_longlong, P],
     "xtu_grouped_gemm_ex": [P, P, P, P, c_int, P, c_int, c_int, c_int, c_int, c_int, P, P, c_int, c_int, P, P,
                             c_float, c_float, c_float, P, c_int, P, P],
     "xtu_ipc_handle_size": [],

@@ -51,6 +51,9 @@ class AttnMetadata:
     # sliding-window layers with a bounded pool: their own block table and KV-write slots
     swa_block_table: torch.Tensor | None = None
     swa_slot_mapping: torch.Tensor | None = None
+    # > 0: a speculative verification step (rows per sequence); recurrent layers keep the
+    # state after every row for the rollback of rejected drafts
+    spec_rows: int = 0
 
     @property
     def num_tokens(self) -> int:

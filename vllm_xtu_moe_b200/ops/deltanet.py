@@ -44,6 +44,12 @@ def deltanet_fwd(qkvz: torch.Tensor, conv_w32: torch.Tensor, g: torch.Tensor | N
     else:
         g = g.float().contiguous()
         beta = beta.float().contiguous()
+    # speculative verification: the states after every token are kept for the rollback
+    spec_n = meta.max_q_len if getattr(meta, "spec_rows", 0) > 0 and state.spec_ssm is not None else 0
+    if spec_n and spec_n > state.spec_ssm.shape[1]:
+        raise ValueError(f"verification step of {spec_n} tokens per sequence > {state.spec_ssm.shape[1]} spec states")
+    spec_ssm = state.spec_ssm if spec_n else None
+    spec_conv = state.spec_conv if spec_n else None
     if chunked is None:
         chunked = not meta.is_decode and meta.max_q_len >= CHUNK_MIN_TOKENS
     chunked = bool(chunked) and g.dim() == 2 and dk == 128 and dv == 128
@@ -64,5 +70,6 @@ def deltanet_fwd(qkvz: torch.Tensor, conv_w32: torch.Tensor, g: torch.Tensor | N
            qs.data_ptr(), ks.data_ptr(), vs.data_ptr(), out.data_ptr(), int(blocked), int(g.dim() == 3),
            int(chunked), N.ptr(ws), N.ptr(ba), ba.stride(0) if ba is not None else 0, N.ptr(A_log32),
            N.ptr(dt_bias32), N.ptr(gate_t) if y is not None else None, gate_t.stride(0) if y is not None else 0,
-           gate_mode if y is not None else 0, N.ptr(norm_w32), float(eps), N.ptr(y), N.stream_ptr(d))
+           gate_mode if y is not None else 0, N.ptr(norm_w32), float(eps), N.ptr(y),
+           N.ptr(spec_ssm), N.ptr(spec_conv), spec_n, N.stream_ptr(d))
     return out if y is None else y
