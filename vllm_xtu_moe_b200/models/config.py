@@ -56,6 +56,11 @@ class ModelConfig:
     linear_conv_kernel: int = 4
     linear_kind: str = "gdn"       # "gdn" (Qwen3-Next gated DeltaNet) | "kda" (Kimi Delta Attention)
     mla_rope: bool = True          # False: MLA without rotary embedding (Kimi-Linear's NoPE MLA)
+    # DeepSeek sparse attention (DeepSeek-V3.2-style MLA): a lightning indexer scores every
+    # context token per query and attention runs over the index_topk best (0 = dense MLA)
+    index_topk: int = 0
+    index_n_heads: int = 64
+    index_head_dim: int = 128
     # MLP / MoE
     num_dense_layers: int = 0      # leading dense-MLP layers
     dense_intermediate: int = 0
@@ -220,6 +225,14 @@ def deepseek_v3() -> ModelConfig:
                        num_mtp_layers=1, max_position=163840)
 
 
+def deepseek_v32() -> ModelConfig:
+    """DeepSeek-V3.2-style sparse attention on the DeepSeek-V3 shape: the same MLA plus a
+    lightning indexer (64 heads x 128, ReLU-gated, weighted over heads) that keeps the 2048
+    best-scored context tokens of every query."""
+    return deepseek_v3().replace(name="deepseek-v3.2", index_topk=2048, index_n_heads=64,
+                                 index_head_dim=128)
+
+
 def mimo_v2_flash() -> ModelConfig:
     """MiMo-V2-style hybrid-attention MoE (the shape the reference's MiMo guide lists): 48
     layers (1 dense + 47 MoE), hidden 4096, 9 global-attention layers (64 q / 4 kv heads) and
@@ -260,6 +273,7 @@ PRESETS = {
     "qwen3-next-80b-a3b": qwen3_next_80b,
     "glm-4.5-air": glm45_air,
     "deepseek-v3": deepseek_v3,
+    "deepseek-v3.2": deepseek_v32,
     "mimo-v2-flash": mimo_v2_flash,
     "kimi-linear-48b-a3b": kimi_linear_48b,
 }
@@ -416,5 +430,8 @@ def from_hf_config(path_or_dict) -> ModelConfig:
                            n_group=hf.get("n_group", 8), topk_group=hf.get("topk_group", 4),
                            routed_scale=hf.get("routed_scaling_factor", 2.5),
                            norm_topk_prob=hf.get("norm_topk_prob", True), expert_fmt=fmt, dense_fmt=fmt,
-                           num_mtp_layers=hf.get("num_nextn_predict_layers", 0), **base)
+                           num_mtp_layers=hf.get("num_nextn_predict_layers", 0),
+                           # DeepseekV32: the lightning indexer's width and how many tokens it keeps
+                           index_topk=hf.get("index_topk", 0) or 0, index_n_heads=hf.get("index_n_heads", 64),
+                           index_head_dim=hf.get("index_head_dim", 128), **base)
     raise ValueError(f"unsupported architecture {archs}")

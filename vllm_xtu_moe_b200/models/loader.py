@@ -141,6 +141,10 @@ class CheckpointSource:
                          f"{pre}.{sa}.v_conv1d.weight"],
                 "A_log": [f"{pre}.{sa}.A_log"], "dt_bias": [f"{pre}.{sa}.dt_bias"],
                 "gdn_norm": [f"{pre}.{sa}.o_norm.weight"], "out": [f"{pre}.{sa}.o_proj"]})
+        if c.index_topk:         # DSA lightning indexer (DeepSeek-V3.2 names)
+            ix = f"{pre}.{sa}.indexer"
+            table.update({"idx_wq_b": [f"{ix}.wq_b"], "idx_wk": [f"{ix}.wk"], "idx_w": [f"{ix}.weights_proj"],
+                          "idx_k_norm_w": [f"{ix}.k_norm.weight"], "idx_k_norm_b": [f"{ix}.k_norm.bias"]})
         if f.get("shared"):
             table["shared.gate_up"] = [f"{pre}.{f['shared']}.gate_proj", f"{pre}.{f['shared']}.up_proj"]
             table["shared.down"] = [f"{pre}.{f['shared']}.down_proj"]
@@ -387,6 +391,13 @@ def export_hf(model, cfg: ModelConfig, path) -> None:
             put(name + ".kv_a_norm", a.kv_a_norm)
             put_linear(name + ".kv_b", a.kv_b)
             put_linear(name + ".o", a.o)
+            if a.indexer is not None:
+                ix = a.indexer
+                put_linear(name + ".idx_wq_b", ix.wq_b)
+                put_linear(name + ".idx_wk", ix.wk)
+                put_linear(name + ".idx_w", ix.weights_proj)
+                put(name + ".idx_k_norm_w", ix.k_norm_w)
+                put(name + ".idx_k_norm_b", ix.k_norm_b)
         elif isinstance(a, KimiDeltaAttention):
             kd, vd = a.nk * a.dk, a.nv * a.dv
             put_linear(name + ".kda_qkv", a.in_qkv, [kd, kd, vd])

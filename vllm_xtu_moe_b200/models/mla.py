@@ -20,10 +20,72 @@ from .config import ModelConfig
 from .layers import Linear
 
 
+class DSAIndexer:
+    """DeepSeek-V3.2 lightning indexer of one MLA layer: index queries from the q latent
+    (wq_b: q_lora -> n_heads x 128), one index key per token (wk: hidden -> 128, LayerNorm
+    with bias), per-head weights (weights_proj: hidden -> n_heads, times n_heads^-1/2 and the
+    softmax scale 128^-1/2); RoPE (non-interleaved) on the first qk_rope_head_dim dims of both.
+    Its keys live in a paged cache of their own ([blocks, 1, 64, 128], the latent cache's
+    block tables).  Scores and selection: :mod:`..ops.dsa`."""
+
+    def __init__(self, cfg: ModelConfig, wq_b: Linear, wk: Linear, k_norm_w: torch.Tensor, k_norm_b: torch.Tensor,
+                 weights_proj: Linear):
+        self.cfg = cfg
+        self.wq_b, self.wk, self.weights_proj = wq_b, wk, weights_proj
+        self.k_norm_w, self.k_norm_b = k_norm_w, k_norm_b
+        self.nh, self.d = cfg.index_n_heads, cfg.index_head_dim
+        self.topk = cfg.index_topk
+        self.w_scale = self.nh ** -0.5 * self.d ** -0.5
+        self._ws = {}
+
+    def keys_and_queries(self, x: torch.Tensor, qa: torch.Tensor, meta: AttnMetadata, idx_cache: torch.Tensor,
+                         rope: torch.Tensor):
+        """Writes the step's index keys into the cache; returns (q [T, nh, d] bf16, w [T, nh] fp32)."""
+        import torch.nn.functional as F
+        T = x.shape[0]
+        c = self.cfg
+        q = self.wq_b(qa).view(T, self.nh, self.d)
+        k = F.layer_norm(self.wk(x).float(), (self.d,), self.k_norm_w.float(), self.k_norm_b.float(),
+                         1e-6).to(torch.bfloat16).view(T, 1, self.d)
+        rot = c.qk_rope_head_dim if c.mla_rope else 0
+        if rot:
+            if x.is_cuda:
+                B.rope_and_cache(q, k, k, meta.positions, rope, rot, True)
+            else:
+                q = B.apply_rope_ref(q, meta.positions, rope, rot, True)
+                k = B.apply_rope_ref(k, meta.positions, rope, rot, True)
+        B.write_cache_rows(k.contiguous(), meta.slot_mapping, idx_cache)
+        w = (self.weights_proj(x).float() * self.w_scale).contiguous()
+        return q.contiguous(), w
+
+    def select(self, q: torch.Tensor, w: torch.Tensor, meta: AttnMetadata, idx_cache: torch.Tensor,
+               max_len: int):
+        """-> (rows [T, topk] flat latent-cache rows, lens [T]) of every query row."""
+        from ..ops import dsa as D
+        T = q.shape[0]
+        ld = (max_len + 63) // 64 * 64
+        key = (T, ld, q.device)
+        ws = self._ws.get(key)
+        if ws is None:
+            ws = dict(scores=torch.empty(T, ld, dtype=torch.float32, device=q.device),
+                      rows=torch.empty(T, self.topk, dtype=torch.int32, device=q.device),
+                      lens=torch.empty(T, dtype=torch.int32, device=q.device))
+            if q.is_cuda:
+                self._ws[key] = ws
+        seq = D.seq_of_rows(meta.q_start, T)
+        scores = D.index_scores(q, w, idx_cache, meta, seq, ld, out=ws["scores"])
+        return D.topk_rows(scores, meta, seq, self.topk, ws["rows"], ws["lens"])
+
+    def tensors(self):
+        return (self.wq_b.tensors() + self.wk.tensors() + self.weights_proj.tensors() +
+                [self.k_norm_w, self.k_norm_b])
+
+
 class MLAAttention:
     def __init__(self, cfg: ModelConfig, q_a: Linear | None, q_a_norm: torch.Tensor | None, q_b: Linear,
-                 kv_a: Linear, kv_a_norm: torch.Tensor, kv_b: Linear, o: Linear):
+                 kv_a: Linear, kv_a_norm: torch.Tensor, kv_b: Linear, o: Linear, indexer: DSAIndexer | None = None):
         self.cfg = cfg
+        self.indexer = indexer
         self.q_a, self.q_a_norm, self.q_b = q_a, q_a_norm, q_b
         self.kv_a, self.kv_a_norm, self.kv_b, self.o = kv_a, kv_a_norm, kv_b, o
         self.nh = cfg.num_heads
@@ -114,6 +176,14 @@ class MLAAttention:
         k_cache = kv[0]
         self._write_latent(entry, meta, k_cache)
         q_nope = q[:, :, :dn]
+        if self.indexer is not None:
+            # DSA: the indexer sees every token; attention is sparse once a context can hold
+            # more than index_topk tokens (before that the selection is the whole context)
+            qi, wi = self.indexer.keys_and_queries(x, qa, meta, kv[1], rope)
+            if meta.max_kv_len > self.indexer.topk:
+                rows, lens = self.indexer.select(qi, wi, meta, kv[1], meta.max_kv_len)
+                o = self._sparse(q_nope, q_rope, k_cache, rows, lens)
+                return self.o(o.reshape(T, nh * dv))
         if meta.is_decode:
             w_uk, w_uv = self._absorbed()
             if x.is_cuda and dc % 128 == 0 and dn % 64 == 0 and dv % 16 == 0:
@@ -128,6 +198,38 @@ class MLAAttention:
         else:
             o = self._prefill(q_nope, q_rope, meta, k_cache)
         return self.o(o.reshape(T, nh * dv))
+
+    def _sparse(self, q_nope, q_rope, k_cache, rows, lens):
+        """Absorbed attention of every query row over its selected latent rows (DSA), in
+        chunks of query rows (each chunk's gathered rows are index_topk x 576 per row)."""
+        from ..ops import dsa as D
+        T = q_nope.shape[0]
+        nh, dn, dv, dc = self.nh, self.dn, self.dv, self.dc
+        w_uk, w_uv = self._absorbed()
+        native = q_nope.is_cuda and dc % 128 == 0 and dn % 64 == 0 and dv % 16 == 0
+        ch = T if T <= 64 else 256
+        outs = []
+        for s0 in range(0, T, ch):
+            s1 = min(T, s0 + ch)
+            qn, qr = q_nope[s0:s1], q_rope[s0:s1]
+            if native:
+                qfull = self._absorb_q(qn, qr)
+            else:
+                qfull = torch.cat([torch.einsum("thd,hdc->thc", qn.float(), w_uk.float()).to(torch.bfloat16),
+                                   qr.to(torch.bfloat16)], dim=-1).contiguous()
+            plan = None
+            if q_nope.is_cuda:
+                key = ("sparse", s1 - s0, q_nope.device)
+                plan = self._dec.get(key)
+                if plan is None:
+                    plan = D.SparsePlan(s1 - s0, rows.shape[1], dc + self.dr, q_nope.device)
+                    self._dec[key] = plan
+            o_lat = D.sparse_mla(qfull, k_cache, rows[s0:s1], lens[s0:s1], self.scale, dc, plan)
+            if native:
+                outs.append(self._absorb_o(o_lat))
+            else:
+                outs.append(torch.einsum("thc,hvc->thv", o_lat.float(), w_uv.float()).to(torch.bfloat16))
+        return outs[0] if len(outs) == 1 else torch.cat(outs)
 
     def _write_latent(self, entry, meta, k_cache):
         B.write_cache_rows(entry.to(k_cache.dtype).contiguous(), meta.slot_mapping, k_cache)
@@ -203,4 +305,6 @@ class MLAAttention:
         ts = self.q_b.tensors() + self.kv_a.tensors() + self.kv_b.tensors() + self.o.tensors() + [self.kv_a_norm]
         if self.q_a is not None:
             ts += self.q_a.tensors() + [self.q_a_norm]
+        if self.indexer is not None:
+            ts += self.indexer.tensors()
         return ts

@@ -211,7 +211,7 @@ class MoETransformer:
             if c.layer_type(i) == "linear" or (skip_swa and c.layer_type(i) == "swa"):
                 continue
             if c.is_mla:
-                n += (c.kv_lora_rank + c.qk_rope_head_dim) * 2
+                n += (c.kv_lora_rank + c.qk_rope_head_dim + (c.index_head_dim if c.index_topk else 0)) * 2
             else:
                 n += c.kv_heads(i) * (c.head_dim + c.gqa_v_dim) * gqa_b
         return n
@@ -222,8 +222,11 @@ class MoETransformer:
         (GQA layers; MLA latents stay bf16)."""
         c = self.cfg
         if c.is_mla:
+            # DSA layers: the indexer's key cache rides in the second slot
+            idx = (torch.zeros(num_blocks, 1, block_size, c.index_head_dim, dtype=torch.bfloat16, device=device)
+                   if c.index_topk else None)
             return (torch.zeros(num_blocks, 1, block_size, c.kv_lora_rank + c.qk_rope_head_dim,
-                                dtype=torch.bfloat16, device=device), None)
+                                dtype=torch.bfloat16, device=device), idx)
         nkv = c.kv_heads(i)
         if kv_dtype == "fp8":
             f8 = torch.float8_e4m3fn
@@ -378,6 +381,19 @@ def _dense_mlp(f: WeightFactory, name, H, I, fmt, limit=0.0) -> DenseMLP:
     return DenseMLP(gu, f.linear(name + ".down", H, I, fmt), inter, limit)
 
 
+def _dsa_indexer(f, cfg: ModelConfig, name: str, H: int, dfmt: str):
+    """The lightning indexer of a DSA (DeepSeek-V3.2-style) MLA layer, or None."""
+    if not cfg.index_topk:
+        return None
+    if not cfg.q_lora_rank:
+        raise ValueError("DSA needs the q latent (q_lora_rank > 0) for its index queries")
+    from .mla import DSAIndexer
+    ni, di = cfg.index_n_heads, cfg.index_head_dim
+    return DSAIndexer(cfg, f.linear(name + ".idx_wq_b", ni * di, cfg.q_lora_rank, dfmt),
+                      f.linear(name + ".idx_wk", di, H, dfmt), f.ones((di,), name=name + ".idx_k_norm_w"),
+                      f.zeros((di,), name=name + ".idx_k_norm_b"), f.linear(name + ".idx_w", ni, H, "bf16"))
+
+
 def build_layer(f: WeightFactory, cfg: ModelConfig, i: int, expert_sink=None, name_prefix="model.layers") -> DecoderLayer:
     H = cfg.hidden_size
     name = f"{name_prefix}.{i}"
@@ -414,7 +430,7 @@ def build_layer(f: WeightFactory, cfg: ModelConfig, i: int, expert_sink=None, na
                             f.ones((cfg.kv_lora_rank,), name=name + ".kv_a_norm"),
                             f.linear(name + ".kv_b", nh * (cfg.qk_nope_head_dim + cfg.v_head_dim), cfg.kv_lora_rank,
                                      dfmt),
-                            f.linear(name + ".o", H, nh * cfg.v_head_dim, dfmt))
+                            f.linear(name + ".o", H, nh * cfg.v_head_dim, dfmt), _dsa_indexer(f, cfg, name, H, dfmt))
     else:
         li = min(i, cfg.num_layers - 1)
         nh, nkv, hd, vd = cfg.num_heads, cfg.kv_heads(li), cfg.head_dim, cfg.gqa_v_dim

@@ -43,6 +43,10 @@ _SIGS: dict[str, list] = {
                     c_float, c_int, P, P, P, c_int, ctypes.c_longlong, P, c_int, c_float, c_float, P],
     "xtu_paged_attention_fp8": [P, c_int, P, P, P, c_int, P, P, P, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
                                 c_int, c_float, c_float, c_float, c_int, P, P, c_int, P, P, P],
+    "xtu_dsa_index_scores": [P, c_int, c_int, P, P, P, c_int, P, P, c_int, c_int, c_int, P, ctypes.c_longlong, P,
+                             P],
+    "xtu_dsa_topk": [P, ctypes.c_longlong, P, P, P, c_int, c_int, c_int, P, P, P],
+    "xtu_dsa_gather": [P, c_int, ctypes.c_longlong, P, P, c_int, c_int, c_int, P, P, P],
     "xtu_gate_mul": [P, c_int, c_int, P, c_int, c_int, c_int, c_int, c_int, P],
     "xtu_shared_gate": [P, c_int, P, c_int, P, c_int, c_int, P],
     "xtu_kv_dequant_gather": [P, P, P, c_int, P, P, c_int, c_int, c_int, c_int, c_int, c_float, c_float, P, P, P,
