@@ -217,3 +217,56 @@ def test_kda_sigmoid_gated_norm():
     torch.cuda.synchronize()
     err = (y.float().view(T, nv, dv) - ref.float()).abs().max().item() / ref.float().abs().max().item()
     assert err < 2e-2, err
+
+
+@pytest.mark.gpu
+def test_spec_verification_states_and_commit():
+    """A speculative verification step (4 rows per sequence, decode metadata): the kernels
+    keep the recurrent and conv states after every row, equal to the recurrence's; the
+    commit installs the ones of each sequence's accepted row (1 and 3 here)."""
+    from vllm_xtu_moe_b200.ops.deltanet import deltanet_fwd
+    torch.manual_seed(11)
+    cfg = scaled_down(get_preset("qwen3-next-80b-a3b"), layers=4, hidden=256, experts=8).replace(
+        linear_num_key_heads=1, linear_num_value_heads=2, linear_key_head_dim=128, linear_value_head_dim=128)
+    nk, nv, dk, dv, kw = 1, 2, 128, 128, cfg.linear_conv_kernel
+    r = nv // nk
+    W = 2 * dk + 2 * r * dv
+    ch = 2 * nk * dk + nv * dv
+    conv_w = (torch.randn(ch, kw) * 0.3).cuda()
+    st_g = DeltaNetState(cfg, 3, "cuda")
+    st_r = DeltaNetState(cfg, 3, "cuda")
+    st_g.enable_spec(3)
+    st_r.enable_spec(3)
+    slots = [2, 0]
+
+    def step(lens, starts, spec):
+        T = sum(lens)
+        qkvz = (torch.randn(T, nk * W) * 0.5).to(torch.bfloat16).cuda()
+        g = -torch.rand(T, nv).cuda() * 0.5
+        beta = torch.rand(T, nv).cuda()
+        meta = _meta(lens, starts, slots, "cuda")
+        if spec:
+            meta.is_decode = True
+            meta.spec_rows = max(lens)
+        deltanet_fwd(qkvz, conv_w, g, beta, meta, st_g, nk, nv, dk, dv, chunked=False)
+        x = qkvz.view(T, nk, W)
+        mixed = torch.cat([x[:, :, :dk].reshape(T, nk * dk), x[:, :, dk:2 * dk].reshape(T, nk * dk),
+                           x[:, :, 2 * dk:2 * dk + r * dv].reshape(T, nv * dv)], -1)
+        deltanet_ref(mixed, conv_w, g, beta, meta, st_r, nk, nv, dk, dv)
+
+    step([9, 30], [0, 0], False)                 # prompts
+    step([4, 4], [9, 30], True)                  # verification: last token + 3 drafts each
+    torch.cuda.synchronize()
+    for s in slots:
+        for j in range(4):
+            a, b = st_g.spec_ssm[s, j], st_r.spec_ssm[s, j]
+            assert (a - b).abs().max().item() <= 2e-3 * b.abs().max().item(), (s, j)
+            assert torch.equal(st_g.spec_conv[s, j], st_r.spec_conv[s, j]), (s, j)
+    acc = torch.tensor([1, 3], dtype=torch.int32, device="cuda")
+    sl = torch.tensor(slots, dtype=torch.int32, device="cuda")
+    st_g.commit_spec(acc, sl)
+    torch.cuda.synchronize()
+    for s, a in zip(slots, (1, 3)):
+        assert torch.equal(st_g.ssm[s], st_g.spec_ssm[s, a])
+        assert torch.equal(st_g.conv[s], st_g.spec_conv[s, a])
+        assert (st_g.ssm[s] - st_r.spec_ssm[s, a]).abs().max().item() <= 2e-3 * st_r.spec_ssm[s, a].abs().max().item()
