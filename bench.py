@@ -48,6 +48,13 @@ BASELINE_PREFILL = {1: 1477.0, 2: 1441.0, 4: 1394.0}
 ROOT = os.path.dirname(os.path.abspath(__file__))
 
 
+WEIGHTS_DTYPE = {("fp8", "fp8"): "fp8 e4m3, 128x128 fp32 block scales (experts and dense)",
+                 ("mxfp4", "bf16"): "experts MXFP4 (e2m1, e8m0 scales per 32), dense bf16"}
+MODEL_LABEL = {"glm-4.5-air": " (GLM-4.5-Air-style, BASELINE config 4)",
+               "qwen3-next-80b-a3b": " (Qwen3-Next-style hybrid, BASELINE config 3)",
+               "deepseek-v3": " (DeepSeek-V3 shape, BASELINE config 5)"}
+
+
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -68,6 +75,10 @@ def parse():
                          "--pool-experts per layer in HBM, prefill through the streamed expert ring, decode "
                          "through the asynchronous CPU bridge with expert deferral (VLLM_EXPERTS_LOAD_DEVICE=cpu)")
     ap.add_argument("--pool-experts", type=int, default=32, help="--tiered: hot-pool experts per MoE layer")
+    ap.add_argument("--resident-layers", type=int, default=0,
+                    help="--tiered: the first N MoE layers keep their experts GPU-resident (BASELINE config 3: 12)")
+    ap.add_argument("--cpu-int8", default="auto", choices=["auto", "on", "off"],
+                    help="--tiered: INT8 activations in the CPU engine (XIAOTU_MOE_INT8; MXFP4 experts)")
     ap.add_argument("--kv-cache-dtype", default="bf16", choices=["bf16", "fp8"],
                     help="KV cache storage: bf16, or e4m3 with per-layer scales (decode reads half the bytes)")
     ap.add_argument("--zipf", type=float, default=1.1,
@@ -219,9 +230,13 @@ def main():
         # the hot pool seeded with each layer's most popular experts (a PIN table profiled on
         # this traffic); it keeps adapting to the observed routes
         pool = {l: order[l][: args.pool_experts] for l in moe_layers} if order else args.pool_experts
-        ec = dataclasses.replace(get_engine_config(), experts_load_device="cpu", moe_async=True, moe_defer=True)
+        ec = dataclasses.replace(get_engine_config(), experts_load_device="cpu", moe_async=True, moe_defer=True,
+                                 moe_int8=args.cpu_int8)
         threads = max(1, (os.cpu_count() or 1) // world)
-        tiering = TieredExperts(cfg, device=dev, engine_config=ec, resident_layers=set(), pool_experts=pool,
+        resident = set(moe_layers[: args.resident_layers])
+        if isinstance(pool, dict):
+            pool = {l: v for l, v in pool.items() if l not in resident}
+        tiering = TieredExperts(cfg, device=dev, engine_config=ec, resident_layers=resident, pool_experts=pool,
                                 ring=True, max_tokens=args.max_batched_tokens, bridge_tokens=max(64, max_rows),
                                 threads=threads)
     if world > 1:
@@ -392,7 +407,8 @@ def main():
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 2),
             "higher_is_better": True, "scaling": "weak",
             "vs_baseline": round(decode_tok_s / base, 3) if base else None,
-            "dtype": "bf16", "weights_dtype": "fp8 e4m3, 128x128 fp32 block scales (experts and dense)",
+            "dtype": "bf16", "weights_dtype": WEIGHTS_DTYPE.get((cfg.expert_fmt, cfg.dense_fmt),
+                                                                f"experts {cfg.expert_fmt}, dense {cfg.dense_fmt}"),
             "data": "synthetic (uniform random token ids, random-init weights)",
             "prefill_tok_s": round(prefill_tok_s, 1),
             "prefill_vs_baseline": round(prefill_tok_s / BASELINE_PREFILL[C], 3) if C in BASELINE_PREFILL else None,
@@ -402,7 +418,7 @@ def main():
             "tokens_per_decode_step": round(C * (O - 1) / max(1.0, avg_dsteps), 3),
             "by_concurrency": sweep,
             "mtp_off": mtp_off,
-            "config": {"model": cfg.name + " (GLM-4.5-Air-style, BASELINE config 4)", "global_batch": C,
+            "config": {"model": cfg.name + MODEL_LABEL.get(args.model, ""), "global_batch": C,
                        "concurrency": C, "concurrency_per_gpu": C / world, "seq_len": P, "output_len": O,
                        "parallelism": (f"tp{world}+ep{world}" if world > 1 else "single GPU (tp1, ep1)"),
                        "collectives": ("library peer-memory kernels over NVLink (fused decode o_proj -> "
@@ -410,7 +426,9 @@ def main():
                                        if world > 1 else "none"),
                        "weights": f"experts {cfg.expert_fmt}, dense {cfg.dense_fmt}, block 128x128",
                        "experts_placement": (
-                           f"host DRAM once per rank (CPU engine, {tiering.threads} threads), hot pool "
+                           f"{args.resident_layers} MoE layers GPU-resident, the others in "
+                           f"host DRAM once per rank (CPU engine, {tiering.threads} threads, INT8 activations "
+                           f"{args.cpu_int8}), hot pool "
                            f"{args.pool_experts}/{cfg.num_experts} experts per layer in HBM, prefill through the "
                            f"streamed expert ring, decode via the async CPU bridge with deferral; router "
                            f"Zipf({args.zipf}) popularity bias" if tiering is not None

@@ -353,10 +353,13 @@ __device__ __forceinline__ void router_topk_warp(const float* __restrict__ lg, c
       sc[j] = sqrtf(sp);
     }
   }
+  // selection keys: experts past E and experts already taken are -inf; experts of groups
+  // that were not kept are -FLT_MAX (below every real score, above the taken ones), so that
+  // a K larger than the kept groups' experts still yields K distinct experts (index order)
   #pragma unroll
   for (int j = 0; j < PER; ++j) {
     const int e = lane + 32 * j;
-    sel[j] = e < E ? sc[j] + (bias ? bias[e] : 0.f) : -FLT_MAX;
+    sel[j] = e < E ? sc[j] + (bias ? bias[e] : 0.f) : -INFINITY;
   }
   if (n_group > 1 && topk_group < n_group) {
     // group g covers experts [g*gs, (g+1)*gs); experts of lane l, slot j: e = l + 32 j
@@ -416,7 +419,7 @@ __device__ __forceinline__ void router_topk_warp(const float* __restrict__ lg, c
     float w = 0.f;
     if ((bi & 31) == lane) {
       const int j = bi >> 5;
-      for (int jj = 0; jj < PER; ++jj) if (jj == j) { w = sc[jj]; sel[jj] = -FLT_MAX; }
+      for (int jj = 0; jj < PER; ++jj) if (jj == j) { w = sc[jj]; sel[jj] = -INFINITY; }
     }
     w = __shfl_sync(0xffffffffu, w, bi & 31);
     wsum += w;
@@ -521,6 +524,33 @@ __global__ void moe_scatter_gather_kernel(const int* __restrict__ ids, const flo
   }
 }
 
+// Row gather after the decode permute, for steps of more tokens than the token-direct
+// GEMV takes (speculative verification): warp w < n copies the token of permuted row w
+// (perm_slot[w] / K) into xp row w if w < seg_end[0] (the local pairs); warps n .. n + sh_rows
+// copy token w - n into xp row w (the rows a shared expert fused into the grouped GEMV reads).
+// xp_f16s: f16 x 2^-8 rows (the fp8-weight GEMV's input form) instead of bf16.
+__global__ void moe_gather_rows_kernel(const __nv_bfloat16* __restrict__ x, int x_stride, int K, int H,
+                                       const int* __restrict__ perm_slot, const int* __restrict__ seg_end, int n,
+                                       int sh_rows, __nv_bfloat16* __restrict__ xp, int xp_f16s) {
+  griddep_wait();   // launched with PDL: nothing upstream is touched before this
+  griddep_launch_dependents();
+  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (w >= n + sh_rows) return;
+  int t;
+  if (w < n) {
+    if (w >= __ldg(seg_end)) return;
+    t = __ldg(perm_slot + w) / K;
+  } else {
+    t = w - n;
+  }
+  const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)t * x_stride);
+  uint4* dst = reinterpret_cast<uint4*>(xp + (size_t)w * H);
+  if (xp_f16s)
+    for (int i = lane; i < H / 8; i += 32) dst[i] = bf16x8_f16x8_s8(src[i]);
+  else
+    for (int i = lane; i < H / 8; i += 32) dst[i] = src[i];
+}
+
 // Decode-size permute (one CTA, E <= 1024 local experts): per-expert counts, seg, the
 // (row -> pair) permutation, the list of experts that have rows, and for the token-direct
 // gate/up GEMV the map tokrow[a * 16 + t] = row of token t's pair with active expert a
@@ -616,11 +646,11 @@ __global__ void __launch_bounds__(512) moe_permute_decode_kernel(const int* __re
   permute_decode_block(ids, weights, n, K, lo, hi, seg, perm_slot, perm_w, active, tokrow);
 }
 
-// Decode router in one launch (T <= 16 tokens, E <= 1024 experts): every CTA computes the
-// fp32 logits of some experts for all tokens (one warp per expert row, bf16 gate weights
-// [E, H]), the CTA that finishes last (counter, re-zeroed) then runs the top-k of every
-// token and the decode permute.
-template <int PER>
+// Decode router in one launch (T <= TT tokens, TT = 16 or 32; E <= 1024 experts): every CTA
+// computes the fp32 logits of some experts for all tokens (one warp per expert row, bf16
+// gate weights [E, H]), the CTA that finishes last (counter, re-zeroed) then runs the top-k
+// of every token and the decode permute.
+template <int PER, int TT>
 __global__ void __launch_bounds__(512) moe_route_decode_kernel(
     const __nv_bfloat16* __restrict__ x, int x_stride, int T, const __nv_bfloat16* __restrict__ gate, int E, int H,
     const float* __restrict__ bias, int K, int scoring, int n_group, int topk_group, int renorm, float scale,
@@ -632,11 +662,11 @@ __global__ void __launch_bounds__(512) moe_route_decode_kernel(
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   // four experts per CTA, four warps per expert row (a quarter of H each), so that many
   // SMs stream the gate weights and every warp has few dependent loads
-  __shared__ float part[16][16];
+  __shared__ float part[16][TT];
   const int gw = blockIdx.x * 4 + (warp >> 2), q = warp & 3;
-  float acc[16];
+  float acc[TT];
 #pragma unroll
-  for (int t = 0; t < 16; ++t) acc[t] = 0.f;
+  for (int t = 0; t < TT; ++t) acc[t] = 0.f;
   if (gw < E) {
     const int kq = ((H / 8 + 3) / 4) * 8;           // this quarter's [k0, k1)
     const int k0 = q * kq, k1 = min(H, k0 + kq);
@@ -646,7 +676,7 @@ __global__ void __launch_bounds__(512) moe_route_decode_kernel(
       const uint4 gv = *reinterpret_cast<const uint4*>(g + k);
       const uint32_t gs[4] = {gv.x, gv.y, gv.z, gv.w};
 #pragma unroll
-      for (int t = 0; t < 16; ++t) {
+      for (int t = 0; t < TT; ++t) {
         if (t >= T) break;
         const uint4 xv = __ldg(reinterpret_cast<const uint4*>(x + (size_t)t * x_stride + k));
         const uint32_t xs[4] = {xv.x, xv.y, xv.z, xv.w};
@@ -656,13 +686,13 @@ __global__ void __launch_bounds__(512) moe_route_decode_kernel(
     }
   }
 #pragma unroll
-  for (int t = 0; t < 16; ++t) {
+  for (int t = 0; t < TT; ++t) {
     const float v = warp_sum(acc[t]);
     if (lane == 0) part[warp][t] = v;
   }
   __syncthreads();
-  if (threadIdx.x < 64) {   // (expert of the CTA, token): the four quarters in order
-    const int ee = threadIdx.x >> 4, t = threadIdx.x & 15, e = blockIdx.x * 4 + ee;
+  if (threadIdx.x < 4 * TT) {   // (expert of the CTA, token): the four quarters in order
+    const int ee = threadIdx.x / TT, t = threadIdx.x % TT, e = blockIdx.x * 4 + ee;
     if (e < E && t < T)
       logits[(size_t)t * E + e] = ((part[4 * ee][t] + part[4 * ee + 1][t]) + part[4 * ee + 2][t]) + part[4 * ee + 3][t];
   }
@@ -1028,21 +1058,42 @@ int xtu_moe_permute_decode(const int* ids, const float* weights, int T, int K, i
   return rc_last();
 }
 
-// decode router + permute in one launch (see moe_route_decode_kernel).  x [T <= 16, H] bf16
+// rows of the decode permute gathered into xp (see moe_gather_rows_kernel): n permuted
+// rows (seg_end: device int, the local pair count), then sh_rows token rows; x rows and H
+// 16-byte aligned.
+int xtu_moe_gather_rows(const void* x, int x_stride, int K, int H, const int* perm_slot, const int* seg_end, int n,
+                        int sh_rows, void* xp, int xp_f16s, cudaStream_t s) {
+  if (n + sh_rows <= 0) return 0;
+  if (H % 8 != 0 || x_stride % 8 != 0 || K <= 0) return -2;
+  const int warps = n + sh_rows;
+  launch_pdl(moe_gather_rows_kernel, dim3((warps * 32 + 255) / 256), dim3(256), 0, s, (const __nv_bfloat16*)x,
+             x_stride, K, H, perm_slot, seg_end, n, sh_rows, (__nv_bfloat16*)xp, xp_f16s);
+  return rc_last();
+}
+
+// decode router + permute in one launch (see moe_route_decode_kernel).  x [T <= 32, H] bf16
 // (rows 16-byte aligned), gate [E, H] bf16; logits: T * E fp32 scratch; counter: one zeroed
-// int (left zeroed).  Outputs as xtu_router_topk + xtu_moe_permute_decode.
+// int (left zeroed).  Outputs as xtu_router_topk + xtu_moe_permute_decode (tokrow, the
+// token-direct map, only for T <= 16; null otherwise).
 int xtu_moe_route_decode(const void* x, int x_stride, int T, const void* gate, int E, int H, const float* bias, int K,
                          int scoring, int n_group, int topk_group, int renorm, float scale, float* logits,
                          int* counter, int* out_ids, float* out_w, int lo, int hi, int* seg, int* perm_slot,
                          float* perm_w, int* active, int* tokrow, cudaStream_t s) {
   if (T <= 0) return 0;
-  if (T > 16 || E > 1024 || K > 32 || n_group > 64 || H % 8 != 0 || hi - lo <= 0 || hi - lo > 1024) return -2;
+  if (T > 32 || (tokrow && T > 16) || E > 1024 || K > 32 || n_group > 64 || H % 8 != 0 || hi - lo <= 0 ||
+      hi - lo > 1024)
+    return -2;
   const int per = (E + 31) / 32;
   const dim3 grid((E + 3) / 4);
-#define XTU_ROUTE(P)                                                                                         \
-  launch_pdl(moe_route_decode_kernel<P>, grid, dim3(512), 0, s, (const __nv_bfloat16*)x, x_stride, T,        \
+#define XTU_ROUTE_T(P, TTV)                                                                                  \
+  launch_pdl(moe_route_decode_kernel<P, TTV>, grid, dim3(512), 0, s, (const __nv_bfloat16*)x, x_stride, T,   \
              (const __nv_bfloat16*)gate, E, H, bias, K, scoring, n_group, topk_group, renorm, scale, logits,   \
              counter, out_ids, out_w, lo, hi, seg, perm_slot, perm_w, active, tokrow)
+#define XTU_ROUTE(P)                      \
+  do {                                    \
+    if (T <= 16) XTU_ROUTE_T(P, 16);      \
+    else XTU_ROUTE_T(P, 32);              \
+  } while (0)
   if (per <= 1) XTU_ROUTE(1);
   else if (per <= 2) XTU_ROUTE(2);
   else if (per <= 4) XTU_ROUTE(4);
@@ -1050,6 +1101,7 @@ int xtu_moe_route_decode(const void* x, int x_stride, int T, const void* gate, i
   else if (per <= 16) XTU_ROUTE(16);
   else XTU_ROUTE(32);
 #undef XTU_ROUTE
+#undef XTU_ROUTE_T
   return rc_last();
 }
 

@@ -81,6 +81,13 @@ __device__ __forceinline__ uint32_t u4w(const uint4& v, int i) {
   return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
 }
 
+// MMA row i (< 8) of a 16-row half holds weight row gv_prow(i) (and i + 8 row gv_prow(i) + 8):
+// the eight lanes of one shared-memory phase (MMA rows 2p, 2p + 1) then read weight rows p and
+// p + 4, whose 16-byte chunks of a 64-byte k slice fall in opposite halves of the 128-byte
+// swizzle atom, so the weight fragment loads are free of bank conflicts.  The epilogues map
+// accumulator rows back through the same function.
+__device__ __forceinline__ int gv_prow(int i) { return (i >> 1) | ((i & 1) << 2); }
+
 constexpr int GV_CWARPS = 4;                 // consumer warps (warp 0 is the producer)
 constexpr int GV_THREADS = 32 * (1 + GV_CWARPS);
 constexpr int GV_ROW_BYTES = 256;            // bytes of one weight row per stage (2 x 128-B boxes)
@@ -194,7 +201,7 @@ __device__ __forceinline__ bool gv_stream_tile(const CUtensorMap* tmap, const CU
       for (int t = 0; t < 2; ++t)
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          const int r = t * 16 + g4 + h * 8;
+          const int r = t * 16 + gv_prow(g4) + h * 8;
           w[t][h] = *reinterpret_cast<const uint4*>(box + r * 128 + ((c16 ^ (r & 7)) << 4));
         }
       // activations of token n*8+g4 for this lane's k slice (rows past mcount are zeroed)
@@ -371,7 +378,7 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_dense_kernel(
       for (int n = 0; n < NT; ++n)
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const int row = rows[t] + g4 + (i >> 1) * 8;
+          const int row = rows[t] + gv_prow(g4) + (i >> 1) * 8;
           const int tok = n * 8 + 2 * tq + (i & 1);
           if (row < N && tok < M) ws[((size_t)split * GV_MAX_ROWS + tok) * N + row] = acc[t][n][i];
         }
@@ -401,7 +408,7 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_dense_kernel(
           for (int n = 0; n < NT; ++n)
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-              const int row = rows[t] + g4 + (i >> 1) * 8;
+              const int row = rows[t] + gv_prow(g4) + (i >> 1) * 8;
               const int tok = n * 8 + 2 * tq + (i & 1);
               const int q = q0 + qq;
               pv[qq][t][n][i] = (q < splits && row < N && tok < M) ? __ldcg(ws + ((size_t)q * GV_MAX_ROWS + tok) * N + row)
@@ -433,7 +440,7 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_dense_kernel(
     for (int n = 0; n < NT; ++n)
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const int row = rows[t] + g4 + (i >> 1) * 8;
+        const int row = rows[t] + gv_prow(g4) + (i >> 1) * 8;
         const int tok = n * 8 + 2 * tq + (i & 1);
         if (row < N && tok < M) {
           float v = acc[t][n][i];
@@ -519,7 +526,7 @@ __global__ void __launch_bounds__(GV_THREADS) moe_gemv_gate_up_kernel(
     for (int n = 0; n < NT; ++n)
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const int j = j0 + g4 + (i >> 1) * 8;
+        const int j = j0 + gv_prow(g4) + (i >> 1) * 8;
         const int tok = n * 8 + 2 * tq + (i & 1);
         const int hr = tok >= mc ? -1 : trow ? trow[mb + tok] : s0 + mb + tok;
         if (hr >= 0) {
@@ -583,7 +590,7 @@ __global__ void __launch_bounds__(GV_THREADS) moe_gemv_down_kernel(
       for (int n = 0; n < NT; ++n)
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const int row = r0 + t * 16 + g4 + (i >> 1) * 8;
+          const int row = r0 + t * 16 + gv_prow(g4) + (i >> 1) * 8;
           const int tok = n * 8 + 2 * tq + (i & 1);
           if (row < H && tok < mc) {
             const int pr = s0 + mb + tok;
@@ -616,7 +623,7 @@ __global__ void moe_active_kernel(const int* __restrict__ seg, int E, int* __res
 // tensor cores).  A stage is still 32 weight rows x 256 bytes, now 512 k of packed e2m1
 // (low nibble = even k), with the activations of the same k range in bf16.  Consumer warp
 // cw owns bytes [64 cw, 64 cw + 64) of each row; lane (g4, tq) decodes its 16-byte chunk
-// (32 k = one MXFP4 scale group, two NVFP4 groups) of rows g4 and g4 + 8 through a
+// (32 k = one MXFP4 scale group, two NVFP4 groups) of rows gv_prow(g4) and + 8 through a
 // byte -> bf16-pair table in shared memory, multiplies by the row's group scale (exact in
 // bf16: a power of two, or an e4m3 value times an e2m1 value), and feeds bf16 m16n8k16
 // MMAs with k = 32 tq + 4 g + {0,1 | 2,3} for MMA g (the activations use the same order).
@@ -730,14 +737,14 @@ __device__ __forceinline__ bool gv4_stream_tile(const CUtensorMap* tmap, const C
     for (int i = 0; i < nst; ++i) {
       const uint32_t it = phase_base + i;
       const int slot = it % C::STAGES;
-      // this lane's group scales for rows g4 / g4 + 8 of both 16-row halves (fetched before the wait)
+      // this lane's group scales for rows gv_prow(g4) / + 8 of both 16-row halves (fetched before the wait)
       const int k0 = i * C::KSTAGE + cw * 128 + tq * 32;
       uint32_t s2[2][2][2];                   // [half t][row h][group of the 32 k]
 #pragma unroll
       for (int t = 0; t < 2; ++t)
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          const uint8_t* sr = sc8 + (size_t)(row0[t] + g4 + 8 * h) * ng;
+          const uint8_t* sr = sc8 + (size_t)(row0[t] + gv_prow(g4) + 8 * h) * ng;
           const int gi = min(k0 / G, ng - 1);
           s2[t][h][0] = gv4_scale2<NV>(__ldg(sr + gi));
           s2[t][h][1] = NV ? gv4_scale2<NV>(__ldg(sr + min(gi + 1, ng - 1))) : s2[t][h][0];
@@ -750,7 +757,7 @@ __device__ __forceinline__ bool gv4_stream_tile(const CUtensorMap* tmap, const C
       for (int t = 0; t < 2; ++t)
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          const int r = t * 16 + g4 + h * 8;
+          const int r = t * 16 + gv_prow(g4) + h * 8;
           w[t][h] = *reinterpret_cast<const uint4*>(box + r * 128 + ((c16 ^ (r & 7)) << 4));
         }
       uint4 xr[NT][4];
@@ -831,7 +838,7 @@ __global__ void __launch_bounds__(GV_THREADS) moe_gemv4_gate_up_kernel(
     for (int n = 0; n < NT; ++n)
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const int j = j0 + g4 + (i >> 1) * 8;
+        const int j = j0 + gv_prow(g4) + (i >> 1) * 8;
         const int tok = n * 8 + 2 * tq + (i & 1);
         const int hr = tok >= mc ? -1 : trow ? trow[mb + tok] : s0 + mb + tok;
         if (hr >= 0) {
@@ -882,7 +889,7 @@ __global__ void __launch_bounds__(GV_THREADS) moe_gemv4_down_kernel(
       for (int n = 0; n < NT; ++n)
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const int row = r0 + t * 16 + g4 + (i >> 1) * 8;
+          const int row = r0 + t * 16 + gv_prow(g4) + (i >> 1) * 8;
           const int tok = n * 8 + 2 * tq + (i & 1);
           if (row < H && tok < mc) {
             const int pr = s0 + mb + tok;
@@ -1168,7 +1175,13 @@ int xtu_moe_gemv(const void* W13, const float* s13, const void* W2, const float*
   const int nt = mmax > 8 ? 2 : 1;
   int launches = 3;
   if (tokrow && (ntok <= 0 || ntok > 16 || ntok > mmax)) return -2;
-  const int x_rows = tokrow ? ntok : n_rows;
+  // shared expert: one more grid row in both launches over the step's ntok tokens, its h
+  // rows after the pairs' (n_rows + token), its output rows sh_out0 + token of slots.  Its
+  // activations: the step's tokens (token-direct form) or xp rows n_rows .. n_rows + ntok
+  // (gathered form: xtu_moe_gather_rows writes them after the permuted rows)
+  const int has_sh = (W13s != nullptr && W2s != nullptr) ? 1 : 0;
+  if (has_sh && ntok <= 0) return -2;
+  const int x_rows = tokrow ? ntok : n_rows + (has_sh ? ntok : 0);
   if (x_stride <= 0) x_stride = H;
   if (fp8 && !xp_f16s) {
     if (ws == nullptr || (long long)x_rows * H > GV_WS_X_HALVES) return -4;
@@ -1183,9 +1196,6 @@ int xtu_moe_gemv(const void* W13, const float* s13, const void* W2, const float*
   if (rc) return rc;
   rc = gv_xmap(&xm, xp, (uint64_t)x_rows, H, x_stride, 8 * nt, fp8 != 0);
   if (rc) return rc;
-  // shared expert (token-direct form only): one more grid row in both launches, its h rows
-  // after the pairs' (n_rows + token), its output rows sh_out0 + token of slots
-  const int has_sh = (W13s != nullptr && W2s != nullptr && tokrow != nullptr) ? 1 : 0;
   CUtensorMap t13s = t13, t2s = t2;
   if (has_sh) {
     rc = gv_wmap(&t13s, W13s, (uint64_t)2 * I, H, fp8 != 0, true);

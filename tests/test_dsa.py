@@ -5,11 +5,11 @@ import math
 
 import pytest
 import torch
-import torch.nn.functional as F
 
 from vllm_xtu_moe_b200.models.config import get_preset, scaled_down
 from vllm_xtu_moe_b200.models.model import build_model
 from vllm_xtu_moe_b200.ops import basic as B
+from vllm_xtu_moe_b200.ops import _native as N
 from vllm_xtu_moe_b200.ops import dsa as D
 from vllm_xtu_moe_b200.ops.attention import AttnMetadata
 
@@ -33,43 +33,76 @@ def _meta(T, device="cpu", bs=64, nblocks=None):
                         is_decode=False, q_start_host=[0, T], kv_len_host=[T]), (nblocks or nb + 3)
 
 
-def test_dsa_layer_matches_masked_dense_reference_cpu():
-    """A 90-token prompt with index_topk 16: every query past position 15 attends to its 16
-    best-scored tokens.  The oracle expands K / V with kv_b and masks dense attention."""
+def _layer_vs_oracle(device, cfg, T, seed=3, decode=False):
+    """Run layer 0 of a DSA model on a T-token prompt and the fp32 oracle (expanded K / V,
+    dense attention masked to each query's top-k selection); returns the relative error.
+    decode: the prompt's first T - 1 tokens as a prefill step, then token T - 1 alone as a
+    decode step (the oracle's last row)."""
     torch.manual_seed(0)
-    cfg = _cfg(16)
-    m = build_model(cfg, device="cpu", seed=3)
-    m.act_dtype = torch.float32
+    m = build_model(cfg, device=device, seed=seed)
+    if device == "cpu":
+        m.act_dtype = torch.float32
     layer = m.layers[0].attn
-    T = 90
     meta, nbl = _meta(T)
-    x = (torch.randn(T, cfg.hidden_size) * 0.5).to(torch.bfloat16)
-    kv = m._attn_cache(0, nbl, 64, torch.bfloat16, "cpu")
-    out = layer(x, meta, kv, m.rope).float()
-    # --- oracle
+    to = lambda mt: AttnMetadata(**{k: (v.to(device) if isinstance(v, torch.Tensor) else v)
+                                    for k, v in mt.__dict__.items()})
+    x = (torch.randn(T, cfg.hidden_size) * 0.5).to(torch.bfloat16).to(device)
+    kv = m._attn_cache(0, nbl, 64, torch.bfloat16, device)
+    if decode:
+        bt = meta.block_table
+        pre = AttnMetadata(num_seqs=1, q_start=torch.tensor([0, T - 1], dtype=torch.int32),
+                           kv_len=torch.tensor([T - 1], dtype=torch.int32), block_table=bt,
+                           slot_mapping=meta.slot_mapping[:T - 1], positions=meta.positions[:T - 1],
+                           max_q_len=T - 1, max_kv_len=T - 1, is_decode=False, q_start_host=[0, T - 1],
+                           kv_len_host=[T - 1])
+        dec = AttnMetadata(num_seqs=1, q_start=torch.tensor([0, 1], dtype=torch.int32),
+                           kv_len=torch.tensor([T], dtype=torch.int32), block_table=bt,
+                           slot_mapping=meta.slot_mapping[T - 1:], positions=meta.positions[T - 1:], max_q_len=1,
+                           max_kv_len=T, is_decode=True, q_start_host=[0, 1], kv_len_host=[T])
+        layer(x[:T - 1], to(pre) if device != "cpu" else pre, kv, m.rope)
+        last = layer(x[T - 1:], to(dec) if device != "cpu" else dec, kv, m.rope).float()
+    if device != "cpu":
+        meta = to(meta)
+    kv_o = m._attn_cache(0, nbl, 64, torch.bfloat16, device)
+    out = layer(x, meta, kv_o, m.rope).float()
+    if decode:
+        out = torch.cat([out[:T - 1], last])
     c, ix = cfg, layer.indexer
     nh, dn, dr, dv, dc = layer.nh, layer.dn, layer.dr, layer.dv, layer.dc
+    K_ = ix.topk
     qa = B.rmsnorm(layer.q_a(x), layer.q_a_norm, c.norm_eps)
-    qi, wi = ix.keys_and_queries(x, qa, meta, torch.zeros_like(kv[1]), m.rope)
-    ki = kv[1][meta.block_table[0].long()].reshape(-1, 128)[:T].float()
+    qi, wi = ix.keys_and_queries(x, qa, meta, torch.zeros_like(kv_o[1]), m.rope)
+    ki = kv_o[1][meta.block_table[0].long()].reshape(-1, 128)[:T].float()
     I = torch.einsum("th,thj->tj", wi.float(), torch.relu(torch.einsum("thd,jd->thj", qi.float(), ki)))
     q = layer.q_b(qa).view(T, nh, dn + dr).float()
     ckv = layer.kv_a(x).float()
     lat = B.rmsnorm(ckv[:, :dc].to(torch.bfloat16), layer.kv_a_norm, c.norm_eps).float()
-    kr = B.apply_rope_ref(ckv[:, dc:].view(T, 1, dr), meta.positions, m.rope, dr, c.rope_neox)
-    qr = B.apply_rope_ref(q[:, :, dn:], meta.positions, m.rope, dr, c.rope_neox)
+    pos_c = meta.positions.cpu()
+    rope_c = m.rope.cpu()
+    kr = B.apply_rope_ref(ckv[:, dc:].view(T, 1, dr).cpu(), pos_c, rope_c, dr, c.rope_neox).to(x.device)
+    qr = B.apply_rope_ref(q[:, :, dn:].cpu(), pos_c, rope_c, dr, c.rope_neox).to(x.device)
     kvb = (lat @ layer.kv_b.dense_weight().float().t()).view(T, nh, dn + dv)
-    K = torch.cat([kvb[:, :, :dn], kr.float().expand(T, nh, dr)], -1)
-    Q = torch.cat([q[:, :, :dn], qr.float()], -1)
-    s = torch.einsum("thd,jhd->htj", Q, K) * layer.scale
-    allow = torch.zeros(T, T, dtype=torch.bool)
+    Kf = torch.cat([kvb[:, :, :dn], kr.float().expand(T, nh, dr)], -1)
+    Qf = torch.cat([q[:, :, :dn], qr.float()], -1)
+    s = torch.einsum("thd,jhd->htj", Qf, Kf) * layer.scale
+    allow = torch.zeros(T, T, dtype=torch.bool, device=x.device)
     for t in range(T):
-        sel = torch.arange(t + 1) if t < 16 else torch.topk(I[t, :t + 1], 16).indices
+        sel = torch.arange(t + 1, device=x.device) if t < K_ else torch.topk(I[t, :t + 1], K_).indices
         allow[t, sel] = True
     p = torch.softmax(s.masked_fill(~allow[None], float("-inf")), -1)
     o = torch.einsum("htj,jhv->thv", p, kvb[:, :, dn:]).to(torch.bfloat16)
     ref = layer.o(o.reshape(T, nh * dv)).float()
-    err = (out - ref).abs().max().item() / ref.abs().max().item()
+    if decode:
+        out, ref = out[T - 1:], ref[T - 1:]
+    return (out - ref).abs().max().item() / ref.abs().max().item()
+
+
+def test_dsa_layer_matches_masked_dense_reference_cpu():
+    """A 90-token prompt with index_topk 16: every query past position 15 attends to its 16
+    best-scored tokens.  The oracle expands K / V with kv_b and masks dense attention."""
+    err = _layer_vs_oracle("cpu", _cfg(16), 90)
+    assert err < 3e-2, err
+    err = _layer_vs_oracle("cpu", _cfg(16), 90, decode=True)
     assert err < 3e-2, err
 
 
@@ -159,25 +192,37 @@ def test_sparse_mla_gather_attention():
     assert err < 2e-2, err
 
 
+def _gpu_cfg():
+    """DeepSeek-V3 head geometry (latent 512 + rope 64, 16 heads) at a small width."""
+    return _cfg(64).replace(num_heads=16, qk_nope_head_dim=128, qk_rope_head_dim=64, v_head_dim=128,
+                            kv_lora_rank=512, q_lora_rank=128, head_dim=192, rotary_dim=64, num_mtp_layers=0)
+
+
 @pytest.mark.gpu
-@pytest.mark.parametrize("graph", [False, True])
-def test_dsa_model_generation_gpu_matches_cpu(graph):
-    """A tiny DSA model (index_topk 64, prompts up to 150 tokens) generates on the GPU
-    (eager and CUDA-graph decode) the tokens of the fp32 CPU path."""
+def test_dsa_layer_matches_masked_dense_reference_gpu():
+    """The GPU path (indexer kernels, top-k kernel, gathered latent attention with the
+    absorbed projections) against the fp32 oracle on a 150-token prompt, index_topk 64."""
+    err = _layer_vs_oracle("cuda", _gpu_cfg(), 150)
+    assert err < 3e-2, err
+    err = _layer_vs_oracle("cuda", _gpu_cfg(), 150, decode=True)
+    assert err < 3e-2, err
+
+
+@pytest.mark.gpu
+def test_dsa_model_generation_eager_and_graph_gpu():
+    """A tiny DSA model generates past index_topk (prompts up to 150 tokens, sparse decode)
+    eagerly and from captured decode graphs with the same tokens."""
     from vllm_xtu_moe_b200.engine import LLM, SamplingParams
     from vllm_xtu_moe_b200.engine.runner import RunnerConfig
-    cfg = _cfg(64).replace(num_heads=16, qk_nope_head_dim=128, qk_rope_head_dim=64, v_head_dim=128,
-                           kv_lora_rank=512, q_lora_rank=128, head_dim=192, rotary_dim=64, num_mtp_layers=0)
+    m = build_model(_gpu_cfg(), device="cuda", seed=5)
     prompts = [list(range(3, 153)), list(range(200, 260))]
     outs = {}
-    for dev in ("cpu", "cuda"):
-        m = build_model(cfg, device=dev, seed=5)
-        if dev == "cpu":
-            m.act_dtype = torch.float32
-        rc = RunnerConfig(block_size=64, max_seqs=2, max_model_len=512, max_batched_tokens=256,
-                          use_cuda_graph=graph and dev == "cuda")
-        llm = LLM(m, device=dev, runner_config=rc)
-        outs[dev] = [o.token_ids for o in llm.generate(prompts, SamplingParams(max_tokens=8))]
+    for graph in (False, True):
+        rc = RunnerConfig(block_size=64, max_seqs=2, max_model_len=512, max_batched_tokens=256, use_cuda_graph=graph)
+        llm = LLM(m, device="cuda", runner_config=rc)
+        outs[graph] = [o.token_ids for o in llm.generate(prompts, SamplingParams(max_tokens=12))]
         llm.shutdown()
-    same = sum(a == b for x, y in zip(outs["cpu"], outs["cuda"]) for a, b in zip(x, y))
-    assert same >= 0.75 * sum(len(x) for x in outs["cpu"]), outs
+    torch.cuda.synchronize()
+    N.check_status()
+    assert all(len(o) == 12 for o in outs[True])
+    assert outs[False] == outs[True]

@@ -30,6 +30,20 @@ def test_router_ref_group_limited():
         assert len(set((ids[t] // 8).tolist())) <= 4
 
 
+def test_router_ref_top_k_beyond_kept_groups():
+    """top_k larger than the kept groups' experts (8 experts, 4 groups of 2, 2 kept, top 8):
+    the kept experts by score, then the others in index order, never an expert twice."""
+    torch.manual_seed(1)
+    logits = torch.randn(6, 8)
+    ids, w = router_topk_ref(logits, 8, "sigmoid", None, n_group=4, topk_group=2, renorm=True)
+    for t in range(6):
+        assert sorted(ids[t].tolist()) == list(range(8))
+        kept = ids[t, :4].tolist()
+        assert len(set(e // 2 for e in kept)) == 2
+        rest = ids[t, 4:].tolist()
+        assert rest == sorted(rest) and not set(rest) & set(kept)
+
+
 def test_zipf_bias_is_seeded_and_skewed():
     a, b = zipf_bias(256, 1.1, seed=3), zipf_bias(256, 1.1, seed=3)
     assert torch.equal(a, b)
@@ -91,7 +105,8 @@ def test_rope_and_cache(D, rot, neox, qknorm):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("E,K,scoring,ng,tg", [(8, 2, "softmax", 1, 1), (128, 8, "sigmoid", 1, 1),
-                                               (256, 8, "sigmoid", 8, 4), (512, 10, "softmax", 1, 1)])
+                                               (256, 8, "sigmoid", 8, 4), (512, 10, "softmax", 1, 1),
+                                               (8, 8, "sigmoid", 4, 2)])   # top_k beyond the kept groups
 def test_router(E, K, scoring, ng, tg):
     torch.manual_seed(2)
     logits = torch.randn(300, E, device="cuda") + zipf_bias(E).cuda()
@@ -359,7 +374,7 @@ def test_dense_mlp_paths(T):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("T", [1, 4, 16])
+@pytest.mark.parametrize("T", [1, 4, 16, 20, 32])
 @pytest.mark.parametrize("E,K,scoring,ng,tg", [(128, 8, "sigmoid", 1, 1), (256, 8, "sigmoid", 8, 4),
                                                (64, 4, "softmax", 1, 1)])
 def test_route_decode_matches_separate_router(T, E, K, scoring, ng, tg):
@@ -373,7 +388,7 @@ def test_route_decode_matches_separate_router(T, E, K, scoring, ng, tg):
     ex = M.prepare_experts("bf16", torch.zeros(E, 2 * I, H, device="cuda", dtype=torch.bfloat16),
                            torch.zeros(E, H, I, device="cuda", dtype=torch.bfloat16))
     assert M.decode_route_ok(x, gate, ex, K, ng)
-    ws = M.MoEWorkspace(16, K, E, H, I, x.device)
+    ws = M.MoEWorkspace(32, K, E, H, I, x.device)
     for lo, n_local in [(0, E), (E // 4, E // 2)]:
         for _ in range(2):   # the launch counter must be left zeroed
             ids, w = M.route_decode(x, gate, bias, K, scoring, ng, tg, True, 2.5, ws, lo, n_local)
@@ -396,6 +411,52 @@ def test_route_decode_matches_separate_router(T, E, K, scoring, ng, tg):
             act = ws.active.cpu()
             assert act[0].item() == int((cnt > 0).sum()) and torch.equal(act[1:1 + act[0]],
                                                                           torch.nonzero(cnt).flatten().int())
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("fmt", ["fp8", "bf16"])
+@pytest.mark.parametrize("T", [17, 20, 32])
+def test_verification_moe_fused_router_gather_shared(fmt, T):
+    """A verification-size MoE step (16 < T <= 32 rows): router + permute in one launch, the
+    row gather (with the shared expert's token rows appended) and the grouped GEMV with the
+    shared expert as one more grid row, against the fp32 reference of routed + shared; also
+    the expert-parallel slice (local experts [E/4, 3E/4))."""
+    from vllm_xtu_moe_b200.models.layers import DenseMLP, Linear
+    torch.manual_seed(12)
+    E, K, H, I = 64, 8, 1024, 256
+    x = torch.randn(T, H, device="cuda", dtype=torch.bfloat16)
+    gate = (torch.randn(E, H, device="cuda") * 0.2).to(torch.bfloat16)
+    w13 = torch.randn(E, 2 * I, H, device="cuda") / H ** 0.5
+    w2 = torch.randn(E, H, I, device="cuda") / I ** 0.5
+    if fmt == "fp8":
+        q13, s13 = quant_fp8_block(w13)
+        q2, s2 = quant_fp8_block(w2)
+        ex = M.prepare_experts("fp8", q13, q2, s13, s2)
+    else:
+        ex = M.prepare_experts("bf16", w13.to(torch.bfloat16), w2.to(torch.bfloat16))
+    mlp = DenseMLP(Linear(ex.w13[0], ex.s13[0] if fmt == "fp8" else None),
+                   Linear(ex.w2[0], ex.s2[0] if fmt == "fp8" else None), interleaved=True, limit=7.0)
+    assert M.shared_fusable(mlp, ex, 7.0) and M.decode_route_ok(x, gate, ex, K, 1)
+    sh_ref = M.moe_ref(x, torch.zeros(T, 1, dtype=torch.int32, device="cuda"),
+                       torch.ones(T, 1, device="cuda"), ex, act_limit=7.0)
+    ws = M.MoEWorkspace(32, K, E, H, I, x.device)
+    for _ in range(2):   # repeated calls reuse the workspace (rows, counters, shared rows)
+        ids, w = M.route_decode(x, gate, None, K, "softmax", 1, 1, True, 1.0, ws, 0, E)
+        y = M.fused_moe(x, ids, w, ex, ws, act_limit=7.0, shared_mlp=mlp, permuted=True)
+        torch.cuda.synchronize()
+        N.check_status()
+        assert rel_err(y, M.moe_ref(x, ids, w, ex, act_limit=7.0) + sh_ref) < 2e-2
+    # the DenseMLP on its own at this size (one-expert gathered GEMV, two 16-row passes)
+    assert rel_err(mlp(x), sh_ref) < 2e-2
+    # expert-parallel slice: only pairs of experts [lo, lo + E/2) computed here
+    lo, nl = E // 4, E // 2
+    half = M.prepare_experts(ex.fmt, *(_slice_raw(ex, fmt, lo, lo + nl)))
+    ws2 = M.MoEWorkspace(32, K, nl, H, I, x.device)
+    ids, w = M.route_decode(x, gate, None, K, "softmax", 1, 1, True, 1.0, ws2, lo, nl)
+    y2 = M.fused_moe(x, ids, w, half, ws2, lo=lo, act_limit=7.0, permuted=True)
+    torch.cuda.synchronize()
+    N.check_status()
+    assert rel_err(y2, M.moe_ref(x, ids, w, half, lo=lo, hi=lo + nl, act_limit=7.0)) < 2e-2
 
 
 @pytest.mark.gpu

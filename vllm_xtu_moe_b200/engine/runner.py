@@ -174,7 +174,7 @@ class ModelRunner:
             meta.swa_slot_mapping = T(swa_slots)
         if plan.is_decode and self.cuda:
             meta.num_splits = choose_splits(Bn, max(1, self.model.cfg.num_kv_heads), meta.max_kv_len,
-                                            ctas_per_sm=decode_ctas_per_sm(self.model.cfg))
+                                            ctas_per_sm=decode_ctas_per_sm(self.model.cfg, meta.max_q_len))
         return T(ids), meta
 
     # ------------------------------------------------------------------

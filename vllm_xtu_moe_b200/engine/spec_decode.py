@@ -234,7 +234,7 @@ class SpecDecoder:
         R = b * (k + 1)
         cfg = m.cfg
         splits = choose_splits(b, max(1, cfg.num_kv_heads), rn.rc.max_model_len,
-                               ctas_per_sm=decode_ctas_per_sm(cfg))
+                               ctas_per_sm=decode_ctas_per_sm(cfg, k + 1))
         meta = AttnMetadata(num_seqs=b, q_start=st["q_start"][:b + 1], kv_len=st["kv_len"][:b],
                             block_table=st["bt"][:b], slot_mapping=st["slots"][:R], positions=st["pos"][:R],
                             max_q_len=k + 1, max_kv_len=rn.rc.max_model_len, is_decode=True,

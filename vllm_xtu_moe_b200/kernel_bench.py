@@ -259,9 +259,11 @@ def _cache(Bn, kv, Hkv, D, bs=64):
     return kc, vc, bt
 
 
-def bench_attn_decode(Bn=4, kv=15000, Hq=96, Hkv=8, D=128, ql=1, kv_dtype="bf16", iters=20) -> dict:
+def bench_attn_decode(Bn=4, kv=15000, Hq=96, Hkv=8, D=128, ql=1, kv_dtype="bf16", iters=20,
+                      splits: int | None = None) -> dict:
     """GQA decode attention over the paged cache: ``ql`` query positions per sequence (5 =
-    an MTP k=4 verification step), bf16 or fp8 (e4m3) cache."""
+    an MTP k=4 verification step), bf16 or fp8 (e4m3) cache; ``splits`` overrides the
+    split-KV factor."""
     kc, vc, bt = _cache(Bn, kv, Hkv, D)
     if kv_dtype == "fp8":
         from .ops.basic import to_e4m3
@@ -275,7 +277,8 @@ def bench_attn_decode(Bn=4, kv=15000, Hq=96, Hkv=8, D=128, ql=1, kv_dtype="bf16"
                         slot_mapping=torch.zeros(T, dtype=torch.int32, device=d),
                         positions=torch.full((T,), kv - 1, dtype=torch.int32, device=d), max_q_len=ql,
                         max_kv_len=kv, is_decode=True)
-    meta.num_splits = A.choose_splits(Bn, Hkv, kv, ctas_per_sm=2 if D in (64, 128) else 1)
+    per_sm = (2 if ql * (Hq // Hkv) <= 32 else 1) if D in (64, 128) else 1
+    meta.num_splits = splits or A.choose_splits(Bn, Hkv, kv, ctas_per_sm=per_sm)
     ws = torch.empty(A.num_split_workspace(T, Hq, D, meta.num_splits), dtype=torch.float32, device=d)
     out = torch.empty(T, Hq, D, dtype=torch.bfloat16, device=d)
     fn = lambda: A.paged_attention(q, kc, vc, meta, out=out, workspace=ws)
@@ -584,12 +587,14 @@ def bench_cpu_bridge(layers=46, T=1, E=8, H=4096, I=256, K=2, reps=20) -> dict:
 OPS = {
     "moe_prefill_fp8": lambda a: bench_moe(a.tokens or 8192, "fp8"),
     "moe_prefill_bf16": lambda a: bench_moe(a.tokens or 8192, "bf16"),
-    "moe_decode_fp8": lambda a: bench_moe(4, "fp8"),
-    "gemv_fp8": lambda a: bench_gemv(14336, 4096, 4, "fp8"),
-    "gemv_fp8_oproj": lambda a: bench_gemv(4096, 12288, 4, "fp8"),
+    "moe_decode_fp8": lambda a: bench_moe(a.tokens or 4, "fp8"),
+    "gemv_fp8": lambda a: bench_gemv(14336, 4096, a.tokens or 4, "fp8"),
+    "gemv_fp8_oproj": lambda a: bench_gemv(4096, 12288, a.tokens or 4, "fp8"),
     "gemm_fp8": lambda a: bench_gemm(a.tokens or 8192, 14336, 4096, "fp8"),
     "gemm_bf16": lambda a: bench_gemm(a.tokens or 8192, 14336, 4096, "bf16"),
     "attention_decode": lambda a: [bench_attn_decode(ql=ql, kv_dtype=kd) for kd in ("bf16", "fp8") for ql in (1, 5)],
+    # MTP k=4 verification shape (5 rows per sequence) at several split-KV factors
+    "attention_verify": lambda a: [bench_attn_decode(ql=5, splits=sp) for sp in (4, 8, 9, 16, 18)],
     "mla_decode": lambda a: bench_mla_decode(),
     "attention_prefill": lambda a: bench_attn_prefill(min(a.tokens or 8192, 16384)),
     "rmsnorm": lambda a: bench_rmsnorm(),

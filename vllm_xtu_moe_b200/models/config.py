@@ -297,6 +297,9 @@ def scaled_down(cfg: ModelConfig, layers: int = 2, hidden: int | None = None, ex
         if cfg.n_group > 1:
             kw["n_group"] = min(cfg.n_group, experts // 2)
             kw["topk_group"] = max(1, min(cfg.topk_group, kw["n_group"] // 2))
+            # the kept groups must hold at least top_k experts
+            per_group = experts // kw["n_group"]
+            kw["topk_group"] = min(kw["n_group"], max(kw["topk_group"], -(-kw["top_k"] // per_group)))
     if cfg.layer_types is not None:
         pat = cfg.layer_types[:4]
         kw["layer_types"] = (pat * ((layers + 3) // 4))[:layers]

@@ -55,7 +55,7 @@ class RMSNorm:
         self.emit_f16s = False
 
     def __call__(self, x, residual=None):
-        f16s = self.emit_f16s and x.is_cuda and x.dim() == 2 and x.shape[0] <= G.GEMV_MAX_M
+        f16s = self.emit_f16s and x.is_cuda and x.dim() == 2 and x.shape[0] <= G.DECODE_MAX_M
         return B.rmsnorm(x, self.weight, self.eps, residual=residual, add_one=self.add_one, f16s=f16s)
 
     def tensors(self):
@@ -131,7 +131,7 @@ class DenseMLP:
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         T = x.shape[0]
-        if (x.is_cuda and self.interleaved and T <= G.GEMV_MAX_M and x.shape[1] % 128 == 0
+        if (x.is_cuda and self.interleaved and T <= G.DECODE_MAX_M and x.shape[1] % 128 == 0
                 and self.down.weight.shape[1] % 128 == 0):
             return M.dense_swiglu_gemv(x.contiguous(), self.gate_up.weight, self.gate_up.scale, self.down.weight,
                                        self.down.scale, self.limit, self._seg)
@@ -212,7 +212,7 @@ class MoEBlock:
             self.tracer.routing.record(self.trace_idx, ids)
         sh = None
         if (self.shared is not None and self.shared_gate is None and self.executor is None and x.is_cuda
-                and x.shape[0] <= G.GEMV_MAX_M
+                and (x.shape[0] <= G.GEMV_MAX_M or permuted) and x.shape[0] <= G.DECODE_MAX_M
                 and M.shared_fusable(self.shared, self.experts, self.cfg.swiglu_limit)):
             # decode: the shared expert runs inside the routed experts' GEMV launches
             return M.fused_moe(x, ids, w, self.experts, self.workspace(x), lo=self.expert_lo,

@@ -90,6 +90,7 @@ _SIGS: dict[str, list] = {
     "xtu_tp_sum_rmsnorm": [P, ctypes.c_longlong, c_int, c_int, c_int, P, P, P, P, P, P, P, P, c_float, c_int, P,
                            ctypes.c_longlong, P],
     "xtu_moe_permute_decode": [P, P, c_int, c_int, c_int, c_int, P, P, P, P, P, P],
+    "xtu_moe_gather_rows": [P, c_int, c_int, c_int, P, P, c_int, c_int, P, c_int, P],
     "xtu_moe_route_decode": [P, c_int, c_int, P, c_int, c_int, P, c_int, c_int, c_int, c_int, c_int, c_float, P, P,
                              P, P, c_int, c_int, P, P, P, P, P, P],
     "xtu_bridge_post": [P, c_int, P, P, c_int, c_int, c_int, c_int, c_int, c_int, P, P, P, P, c_int, c_int, P, P, P],

@@ -244,8 +244,15 @@ def choose_splits(num_seqs: int, num_kv_heads: int, max_kv_len: int, rows_per_ti
     return int(max(1, min(max_split, slots // ctas, 64)))
 
 
-def decode_ctas_per_sm(cfg) -> int:
-    """CTAs per SM of the decode attention kernel that serves `cfg`: the warp-level GQA
-    decode kernel (head_dim 64 or 128, 96 KB ring) runs two per SM; the tcgen05 kernel
-    (MLA, other head sizes) one."""
-    return 2 if (not cfg.is_mla and cfg.head_dim in (64, 128)) else 1
+def decode_ctas_per_sm(cfg, q_len: int = 1) -> int:
+    """CTAs per SM the split count of a decode step of ``q_len`` query positions per
+    sequence is sized for: the warp-level GQA decode kernel (head_dim 64 or 128, 96 KB ring)
+    runs two per SM up to 32 query rows per KV head; with more rows (MTP verification steps
+    of a large GQA group: four m-tiles per CTA) one CTA keeps an SM's tensor pipe busy and
+    a second one only slows both (measured: 4 x 15K-token sequences, 60 rows per KV head,
+    94 us at 4 splits against 121 us at 9).  The tcgen05 kernel (MLA, other head sizes)
+    runs one per SM."""
+    if cfg.is_mla or cfg.head_dim not in (64, 128):
+        return 1
+    G = cfg.num_heads // max(1, cfg.num_kv_heads)
+    return 2 if q_len * G <= 32 else 1

@@ -76,12 +76,15 @@ def topk_rows(scores: torch.Tensor, meta: AttnMetadata, seq: torch.Tensor, k: in
 
 class SparsePlan:
     """Static buffers of the sparse attention of T query rows (graph-capturable): the gather
-    target and the pseudo-sequence metadata (query t owns blocks t * kb .. t * kb + kb - 1)."""
+    target and the pseudo-sequence metadata (query t owns blocks t * kb .. t * kb + kb - 1).
+    The gather target starts zeroed: the attention kernel reads whole 64-row blocks and
+    multiplies the rows past a query's selection by a zero probability, which must not meet
+    a NaN bit pattern (later calls leave finite latent rows there)."""
 
     def __init__(self, T: int, k: int, width: int, device):
         self.kb = (k + BLOCK - 1) // BLOCK
         self.T = T
-        self.scratch = torch.empty(T * self.kb, 1, BLOCK, width, dtype=torch.bfloat16, device=device)
+        self.scratch = torch.zeros(T * self.kb, 1, BLOCK, width, dtype=torch.bfloat16, device=device)
         self.q_start = torch.arange(T + 1, dtype=torch.int32, device=device)
         self.bt = torch.arange(T * self.kb, dtype=torch.int32, device=device).view(T, self.kb)
         self.zeros = torch.zeros(T, dtype=torch.int32, device=device)

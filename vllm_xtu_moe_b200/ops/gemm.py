@@ -62,6 +62,8 @@ def gemm_fp8w(a: torch.Tensor, w8: torch.Tensor, w_scale: torch.Tensor, out: tor
 GEMV_MAX_M = 16          # rows of the token-direct decode forms (MoE, fused TP, norms' f16 copies)
 GEMV_MAX_M_DENSE = 32    # rows a plain dense GEMV call takes (speculative verification batches)
 GEMV_MAX_M_MOE = 64      # rows the gathered grouped MoE GEMV takes (<= 16 per expert per pass)
+DECODE_MAX_M = 32        # rows of a decode / verification step the decode forms serve (RMSNorm f16
+                         # copies, fused router + permute, shared expert inside the routed GEMVs)
 
 
 def gemv(x: torch.Tensor, weight: torch.Tensor, scale: torch.Tensor | None = None, bias: torch.Tensor | None = None,

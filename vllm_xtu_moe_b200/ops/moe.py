@@ -95,7 +95,8 @@ class MoEWorkspace:
         self.cursor = torch.zeros(E, dtype=torch.int32, device=d)
         self.perm_slot = torch.zeros(n, dtype=torch.int32, device=d)
         self.perm_w = torch.zeros(n, dtype=torch.float32, device=d)
-        self.xp = torch.empty(n, H, dtype=torch.bfloat16, device=d)
+        # pair rows, then (decode verification steps) the token rows of a fused shared expert
+        self.xp = torch.empty(n + self.max_tokens, H, dtype=torch.bfloat16, device=d)
         # pair rows, then one row per token for a shared expert fused into the decode GEMV
         self.h = torch.empty(n + self.max_tokens, I, dtype=torch.bfloat16, device=d)
         self.h13 = None  # unfused gate/up output, allocated on demand
@@ -205,7 +206,23 @@ def moe_experts_partial(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tenso
                N.status_buffer(x.device).data_ptr(), s)
         return None
     if permuted:
-        raise ValueError("a decode-permuted workspace needs the decode GEMV path")
+        # a verification step of more tokens than the token-direct form takes: route_decode
+        # has built the permutation; gather its rows (and the token rows of a fused shared
+        # expert) and run the grouped GEMV on them
+        if not gemv_path or T > G.DECODE_MAX_M:
+            raise ValueError("a decode-permuted workspace needs the decode GEMV path")
+        f16s = int(fp8)
+        nsh = T if shared_mlp is not None else 0
+        xt = G.tma_rows(x)
+        N.call("xtu_moe_gather_rows", xt.data_ptr(), xt.stride(0), K, H, ws.perm_slot.data_ptr(),
+               ws.seg[E:].data_ptr(), n, nsh, ws.xp.data_ptr(), f16s, s)
+        N.call("xtu_moe_gemv", experts.w13.data_ptr(), N.ptr(experts.s13 if fp8 else None),
+               experts.w2.data_ptr(), N.ptr(experts.s2 if fp8 else None), int(fp8), E, H, I, ws.xp.data_ptr(), f16s,
+               H, None, T, ws.seg.data_ptr(), ws.perm_slot.data_ptr(), ws.perm_w.data_ptr(), ws.h.data_ptr(),
+               ws.slots.data_ptr(), min(T, G.GEMV_MAX_M), min(E, n), n, ws.active.data_ptr(), 1,
+               float(act_limit), float(act_alpha), float(act_beta), *_shared_ptrs(shared_mlp), n,
+               _gv_ws(x.device), N.status_buffer(x.device).data_ptr(), s)
+        return ws.slots[n:n + T] if shared_mlp is not None else None
     f16s = int(gemv_path and fp8)
     N.call("xtu_moe_permute", ids.data_ptr(), weights.data_ptr(), T, K, lo, lo + E, ws.counts.data_ptr(),
            ws.seg.data_ptr(), ws.cursor.data_ptr(), ws.perm_slot.data_ptr(), ws.perm_w.data_ptr(), x.data_ptr(), H,
@@ -317,7 +334,7 @@ def route_split(ids: torch.Tensor, slotmap: torch.Tensor, lo: int, gpu_ids: torc
 def decode_route_ok(x: torch.Tensor, gate: torch.Tensor, experts: ExpertWeights | None, top_k: int,
                     n_group: int) -> bool:
     """Whether :func:`route_decode` (router + permute in one launch) serves this step."""
-    if experts is None or not x.is_cuda or x.shape[0] > G.GEMV_MAX_M or x.dtype != torch.bfloat16:
+    if experts is None or not x.is_cuda or x.shape[0] > G.DECODE_MAX_M or x.dtype != torch.bfloat16:
         return False
     H = x.shape[1]
     return (gate.dtype == torch.bfloat16 and gate.is_contiguous() and gate.shape[0] <= 1024 and H % 128 == 0
@@ -335,15 +352,15 @@ def route_decode(x: torch.Tensor, gate: torch.Tensor, bias: torch.Tensor | None,
     T, H = x.shape
     E = gate.shape[0]
     xt = G.tma_rows(x)
-    if ws.route_logits is None or ws.route_logits.numel() < 16 * E:
-        ws.route_logits = torch.empty(16 * E, dtype=torch.float32, device=x.device)
+    if ws.route_logits is None or ws.route_logits.numel() < G.DECODE_MAX_M * E:
+        ws.route_logits = torch.empty(G.DECODE_MAX_M * E, dtype=torch.float32, device=x.device)
     ids = torch.empty(T, top_k, dtype=torch.int32, device=x.device)
     w = torch.empty(T, top_k, dtype=torch.float32, device=x.device)
     N.call("xtu_moe_route_decode", xt.data_ptr(), xt.stride(0), T, gate.data_ptr(), E, H, N.ptr(bias), top_k,
            SCORING[scoring], n_group, topk_group, int(renorm), float(scale), ws.route_logits.data_ptr(),
            ws.route_counter.data_ptr(), ids.data_ptr(), w.data_ptr(), lo, lo + num_local, ws.seg.data_ptr(),
-           ws.perm_slot.data_ptr(), ws.perm_w.data_ptr(), ws.active.data_ptr(), ws.tokrow.data_ptr(),
-           N.stream_ptr(x.device))
+           ws.perm_slot.data_ptr(), ws.perm_w.data_ptr(), ws.active.data_ptr(),
+           ws.tokrow.data_ptr() if T <= G.GEMV_MAX_M else None, N.stream_ptr(x.device))
     return ids, w
 
 
@@ -398,7 +415,8 @@ def dense_swiglu_gemv(x: torch.Tensor, w13: torch.Tensor, s13, w2: torch.Tensor,
     N.call("xtu_moe_gemv", w13.data_ptr(), N.ptr(s13), w2.data_ptr(), N.ptr(s2), int(s13 is not None), 1, H, I,
            x16.data_ptr() if use16 else x.data_ptr(), int(use16), H if use16 else x.stride(0), None, 0,
            st["seg"].data_ptr(), st["slot"].data_ptr(), st["w"].data_ptr(), st["h"].data_ptr(),
-           y.data_ptr(), T, 1, T, st["active"].data_ptr(), 1, float(limit), 1.0, 0.0, None, None, None, None, 0,
+           y.data_ptr(), min(T, G.GEMV_MAX_M), 1, T, st["active"].data_ptr(), 1, float(limit), 1.0, 0.0, None, None,
+           None, None, 0,
            _gv_ws(x.device),
            N.status_buffer(x.device).data_ptr(), N.stream_ptr(x.device))
     return y

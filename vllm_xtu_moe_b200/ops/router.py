@@ -37,8 +37,10 @@ def router_topk_ref(logits, top_k, scoring="softmax", bias=None, n_group=1, topk
         keep = gscore.topk(topk_group, dim=-1).indices
         mask = torch.zeros(T, n_group, dtype=torch.bool, device=sel.device)
         mask.scatter_(1, keep, True)
-        sel = sel.masked_fill(~mask.repeat_interleave(E // n_group, dim=1), float("-inf"))
-    ids = sel.topk(top_k, dim=-1).indices
+        # experts of dropped groups rank below every kept one but stay selectable (index
+        # order), so a top_k above the kept groups' experts still gives distinct experts
+        sel = sel.masked_fill(~mask.repeat_interleave(E // n_group, dim=1), torch.finfo(torch.float32).min)
+    ids = torch.sort(sel, dim=-1, descending=True, stable=True).indices[:, :top_k]
     w = sc.gather(1, ids)
     if renorm:
         w = w / w.sum(-1, keepdim=True).clamp(min=1e-20)

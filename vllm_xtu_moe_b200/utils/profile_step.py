@@ -3,7 +3,10 @@ tokens, warms up, then runs ``--steps`` decode steps between cudaProfilerStart/S
 an external profiler started with ``--profile-from-start off`` sees only those steps.
 
     python -m vllm_xtu_moe_b200.utils.profile_step --model glm-4.5-air --prompt-len 14500 \\
-        --concurrency 4 --steps 2 [--layers N] [--graph]
+        --concurrency 4 --steps 2 [--layers N] [--graph] [--num-spec K] [--kv-cache-dtype fp8]
+
+``--num-spec K``: the steps are MTP verification steps (K drafts per request; the
+drafts of a random model are rejected, so every step verifies K + 1 rows per request).
 """
 from __future__ import annotations
 
@@ -24,10 +27,14 @@ def main(argv=None):
     ap.add_argument("--steps", type=int, default=2)
     ap.add_argument("--layers", type=int, default=None)
     ap.add_argument("--graph", action="store_true")
+    ap.add_argument("--num-spec", type=int, default=0)
+    ap.add_argument("--kv-cache-dtype", default="bf16")
     a = ap.parse_args(argv)
     cfg = get_preset(a.model)
     rc = RunnerConfig(block_size=64, max_seqs=a.concurrency, max_batched_tokens=16384,
-                      max_model_len=a.prompt_len + 64, use_cuda_graph=a.graph)
+                      max_model_len=a.prompt_len + 64 + 4 * a.num_spec, use_cuda_graph=a.graph,
+                      num_spec=a.num_spec, kv_cache_dtype=a.kv_cache_dtype,
+                      graph_batch_sizes=tuple(b for b in (1, 2, 4, 8, 16) if b <= a.concurrency) or (1,))
     llm = LLM(cfg, device="cuda:0", seed=1, runner_config=rc, num_layers=a.layers)
     g = torch.Generator().manual_seed(0)
     for _ in range(a.concurrency):
@@ -47,7 +54,7 @@ def main(argv=None):
     torch.cuda.synchronize()
     torch.cuda.profiler.stop()
     print(f"decode {s.elapsed_time(e) / a.steps:.2f} ms/step ({cfg.num_layers if a.layers is None else a.layers} "
-          f"layers, graph={a.graph})", flush=True)
+          f"layers, graph={a.graph}, num_spec={a.num_spec}, kv={a.kv_cache_dtype})", flush=True)
 
 
 if __name__ == "__main__":
