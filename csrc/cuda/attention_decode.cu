@@ -6,8 +6,9 @@
 //   warp 0     producer: the split's page ids (read 32 at a time by the whole warp),
 //              then one elected thread streams each 64-key page of K and V through a
 //              3-deep shared-memory ring with TMA (128-byte swizzled 64 x 64 boxes).
-//   warps 1-4  consumers: warp w takes m-tile (w % MT) of 16 query rows and key
-//              subset (w / MT) of every page (16 keys when MT = 1, 32 when MT = 2):
+//   warps 1-CW consumers (CW = 4; 8 when MT = 4): warp w takes m-tile (w % MT) of 16
+//              query rows and key subset (w / MT) of every page (16 keys when MT = 1,
+//              32 when MT = 2 or 4):
 //                S = Q K^T      mma.sync m16n8k16 bf16, Q in registers, K by ldmatrix
 //                online softmax in the exp2 domain (quad shuffles for the row max),
 //                O += P V       P re-used from the S registers as the A fragment,
@@ -25,8 +26,10 @@
 // loaded in the same order) and the keys of each 16-key group in P V (S's n-positions
 // are mapped onto the permuted keys when K rows are read and when keys are masked).
 // The per-layer K scale is folded into the softmax scale and the V scale into the output.
-// MT = 4 (up to 64 query rows: MTP verification steps of a GQA group of 12) gives every
-// consumer warp one m-tile and all 64 keys of a page.
+// MT = 4 (up to 64 query rows: MTP verification steps of a GQA group of 12) runs eight
+// consumer warps, one CTA per SM with a 192 KB ring: with four warps each carried one
+// m-tile through all 64 keys of a page, and one warp per scheduler left every dependent
+// MMA and exp exposed (measured 94 us for 4 x 15K-token sequences, 60 rows per KV head).
 // Why not tcgen05 here: its smallest tile is 64 rows, so 12 real rows would carry 5x
 // padded softmax work, and softmax (not the tensor pipe) is what limits a decode CTA;
 // the warp-level MMA shape matches the GQA group.  The split count is chosen so that
@@ -48,19 +51,20 @@
 namespace xtu {
 namespace {
 
-constexpr int AD_CWARPS = 4;
-constexpr int AD_THREADS = 32 * (1 + AD_CWARPS);
 constexpr int AD_KEYS = 64;   // keys per paged-cache block
 
-template <int D, bool F8 = false>
+// CW consumer warps: 4 (two CTAs per SM, 96 KB ring) or 8 (MT = 4: one CTA per SM, twice
+// the ring, each m-tile's keys split between two warps so every scheduler runs two of them)
+template <int D, bool F8 = false, int CW = 4>
 struct AdCfg {
   static constexpr int BOXES = D / 64;                        // 64-wide (128-byte) column boxes (bf16)
   static constexpr int KV_BYTES = AD_KEYS * D * (F8 ? 1 : 2); // K (or V) of one page
   static constexpr int STAGE_BYTES = 2 * KV_BYTES;
-  static constexpr int STAGES = (D <= 64 ? 6 : 3) * (F8 ? 2 : 1);
+  static constexpr int STAGES = (D <= 64 ? 6 : 3) * (F8 ? 2 : 1) * (CW == 8 ? 2 : 1);
+  static constexpr int THREADS = 32 * (1 + CW);
   static constexpr int BYTES = 1024 + STAGES * STAGE_BYTES + 2 * STAGES * 8 + 64;
-  // the end-of-CTA merge reuses the ring: O, m, l of the 4 consumer warps
-  static_assert(AD_CWARPS * 16 * (D + 2) * 4 <= STAGES * STAGE_BYTES, "merge buffer");
+  // the end-of-CTA merge reuses the ring: O, m, l of the consumer warps
+  static_assert(CW * 16 * (D + 2) * 4 <= STAGES * STAGE_BYTES, "merge buffer");
 };
 
 struct AdParams {
@@ -161,14 +165,15 @@ __device__ __forceinline__ uint32_t ad_chunk(uint32_t base, int r, int ch) {
 }
 
 
-template <int D, int MT, bool F8>
-__global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(const __grid_constant__ CUtensorMap tk,
-                                                                 const __grid_constant__ CUtensorMap tv,
-                                                                 const __grid_constant__ AdParams p) {
+template <int D, int MT, bool F8, int CW>
+__global__ void __launch_bounds__(32 * (1 + CW)) attn_decode_kernel(const __grid_constant__ CUtensorMap tk,
+                                                                    const __grid_constant__ CUtensorMap tv,
+                                                                    const __grid_constant__ AdParams p) {
   griddep_wait();   // launched with PDL: nothing upstream is touched before this
   griddep_launch_dependents();
-  using C = AdCfg<D, F8>;
+  using C = AdCfg<D, F8, CW>;
   constexpr int STAGES = C::STAGES;
+  constexpr int AD_CWARPS = CW;
   constexpr int NS = AD_CWARPS / MT;   // key subsets per page
   constexpr int KW = AD_KEYS / NS;     // keys per consumer warp per page
   constexpr int NKT = KW / 8;          // 8-key n-tiles of S per warp
@@ -408,9 +413,9 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(const __grid_co
     l[h2] += __shfl_xor_sync(0xffffffffu, l[h2], 2);
   }
   asm volatile("bar.sync 1, %0;" ::"n"(32 * AD_CWARPS) : "memory");   // all warps done with the ring
-  float* co = reinterpret_cast<float*>(stages);                       // [4 warps][16 rows][D]
-  float* cm = co + AD_CWARPS * 16 * D;                                 // [4][16]
-  float* cl = cm + AD_CWARPS * 16;                                     // [4][16]
+  float* co = reinterpret_cast<float*>(stages);                       // [CW warps][16 rows][D]
+  float* cm = co + AD_CWARPS * 16 * D;                                 // [CW][16]
+  float* cl = cm + AD_CWARPS * 16;                                     // [CW][16]
   {
     float* mine = co + cw * 16 * D;
 #pragma unroll
@@ -534,17 +539,17 @@ __global__ void __launch_bounds__(AD_THREADS) attn_decode_kernel(const __grid_co
 
 }  // namespace
 
-template <int D, int MT, bool F8>
+template <int D, int MT, bool F8, int CW = 4>
 static int ad_launch(const CUtensorMap& tk, const CUtensorMap& tv, const AdParams& p, int B, cudaStream_t s) {
-  using C = AdCfg<D, F8>;
+  using C = AdCfg<D, F8, CW>;
   static bool init = false;
   if (!init) {
-    cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel<D, MT, F8>,
+    cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel<D, MT, F8, CW>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, C::BYTES);
     if (e != cudaSuccess) return -(int)e;
     init = true;
   }
-  launch_pdl(attn_decode_kernel<D, MT, F8>, dim3(p.splits, p.Hkv, B), dim3(AD_THREADS), C::BYTES, s, tk, tv, p);
+  launch_pdl(attn_decode_kernel<D, MT, F8, CW>, dim3(p.splits, p.Hkv, B), dim3(C::THREADS), C::BYTES, s, tk, tv, p);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 1 : -(int)e;
 }
@@ -599,7 +604,7 @@ int attn_decode_gqa(const CUtensorMap& tk, const CUtensorMap& tv, const void* q,
   p.status = reinterpret_cast<XtuStatus*>(status);
 #define XTU_AD(DD, F)                                                                                    \
   return rows <= 16 ? ad_launch<DD, 1, F>(tk, tv, p, B, s)                                               \
-                    : rows <= 32 ? ad_launch<DD, 2, F>(tk, tv, p, B, s) : ad_launch<DD, 4, F>(tk, tv, p, B, s)
+                    : rows <= 32 ? ad_launch<DD, 2, F>(tk, tv, p, B, s) : ad_launch<DD, 4, F, 8>(tk, tv, p, B, s)
   if (kv_fp8) {
     if (D == 128) XTU_AD(128, true);
     XTU_AD(64, true);

@@ -671,6 +671,16 @@ static int attn_softmax_parts() {
   return v;
 }
 
+// K/V ring depth of the verification-shaped configuration: XTU_ATTN_VERIFY_STAGES = 4 or 5
+static int attn_verify_stages() {
+  static int v = 0;
+  if (v == 0) {
+    const char* e = getenv("XTU_ATTN_VERIFY_STAGES");
+    v = (e && e[0] == '5') ? 5 : 4;
+  }
+  return v;
+}
+
 extern "C" {
 
 // q [T, Hq, D] (token stride q_stride), caches [blocks, Hkv, 64, D|DV]; v_is_k: V = first DV dims of K (MLA).
@@ -730,13 +740,23 @@ int xtu_paged_attention(const void* q, int q_stride, const void* k_cache, const 
   const int rows_used = max_q_len * G;
   // replica merge buffers live in the K ring: only the decode configurations (D <= 128) use it
   p.rf = (!decode_shape || D > 128) ? 1 : rows_used <= 32 ? 4 : rows_used <= 64 ? 2 : 1;
+  // verification-shaped steps (33..64 rows of a 128-wide head: MTP drafts of a large GQA
+  // group): 64-key tiles in a 4-deep ring, so the producer runs several pages ahead of the
+  // S -> softmax -> PV chain (a 2-deep ring of 128-key tiles left one page loading at a time)
+  const bool verify_shape = decode_shape && D == 128 && DV == 128 && rows_used > 32;
   // every replica scores a multiple of 16 keys per tile (the softmax reads S in 16-column chunks)
-  const int bn = (decode_shape && D == 64) ? 64 : 128;
+  const int bn = (decode_shape && D == 64) || verify_shape ? 64 : 128;
   while (p.rf > 1 && (bn / p.rf) % 16 != 0) p.rf >>= 1;
   // window / sinks: the EXT instantiations (GQA shapes only; MLA has neither)
   const bool ext = window > 0 || sinks != nullptr;
   if (mla && ext) return -7;
   if (mla) r = launch_attn<576, 256, 16, 2, 1024, 1>(tk, tv, p, grid_x, B, s);
+  else if (verify_shape && attn_verify_stages() == 5)
+    r = ext ? launch_attn<128, 128, 64, 5, 256, 0, 1>(tk, tv, p, grid_x, B, s)
+            : launch_attn<128, 128, 64, 5, 256>(tk, tv, p, grid_x, B, s);
+  else if (verify_shape)
+    r = ext ? launch_attn<128, 128, 64, 4, 256, 0, 1>(tk, tv, p, grid_x, B, s)
+            : launch_attn<128, 128, 64, 4, 256>(tk, tv, p, grid_x, B, s);
   else if (decode_shape && D == 128 && DV == 128)
     r = ext ? launch_attn<128, 128, 128, 2, 256, 0, 1>(tk, tv, p, grid_x, B, s)
             : launch_attn<128, 128, 128, 2, 256>(tk, tv, p, grid_x, B, s);

@@ -46,6 +46,7 @@
 #include <cuda_fp8.h>
 #include <cuda_runtime.h>
 #include <cstdint>
+#include <cstdlib>
 #include "ptx.cuh"
 #include "launch.cuh"
 #include "../comm/peer.cuh"
@@ -110,6 +111,108 @@ struct GvCfg {
                                2 * STAGES * 8 + 64;
 };
 
+// Producer: issue the TMA loads of one stage into dst (completing on bar): the 32 weight
+// rows x 256 bytes of k-stage s_abs (two 128-byte column chunks; WMODE 1: two 16-row halves
+// 128 rows apart; WMODE 2: rows whose byte length is not a multiple of 128, four 2-D boxes)
+// and the activations of the same k range (rows x_row0 ..).  The caller has armed bar.
+template <bool FP8, int NT, int WMODE>
+__device__ __forceinline__ void gv_issue_stage(const CUtensorMap* tmap, const CUtensorMap* xmap, uint8_t* dst,
+                                               uint64_t* bar, const int (&row0)[2], int s_abs, int x_row0) {
+  using C = GvCfg<FP8, NT>;
+  if (WMODE == 0) {
+    tma_load_3d(dst, tmap, bar, 0, row0[0], 2 * s_abs);
+  } else if (WMODE == 1) {
+    tma_load_4d(dst, tmap, bar, 0, row0[0], 0, 2 * s_abs);
+  } else {
+#pragma unroll
+    for (int b = 0; b < 2; ++b)
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+        tma_load_2d(dst + b * 4096 + h * 2048, tmap, bar, s_abs * C::KSTAGE + b * (C::KSTAGE / 2), row0[h]);
+  }
+  tma_load_3d(dst + GV_W_BYTES, xmap, bar, 0, x_row0, s_abs * C::XBOXES);
+}
+
+// Consumer warp cw (0..3): multiply its k slice of the landed stage at sbase into acc
+// (acc[t] += sc[t] * (W x) per 16-row half t), releasing the stage (empty) as soon as its
+// fragments are in registers.  Activation rows >= mcount count as zero.
+template <bool FP8, int NT>
+__device__ __forceinline__ void gv_mma_stage(const uint8_t* sbase, uint64_t* empty, int cw, int lane, int mcount,
+                                             const float (&sc)[2], float (&acc)[2][NT][4]) {
+  using C = GvCfg<FP8, NT>;
+  constexpr int LK = FP8 ? 16 : 8;           // k per lane per stage
+  const int g4 = lane >> 2, tq = lane & 3;
+  const int c16 = (cw & 1) * 4 + tq;         // 16-byte chunk of the 128-byte row within box (cw >> 1)
+  const uint8_t* box = sbase + (cw >> 1) * 4096;
+  uint4 w[2][2];
+#pragma unroll
+  for (int t = 0; t < 2; ++t)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int r = t * 16 + gv_prow(g4) + h * 8;
+      w[t][h] = *reinterpret_cast<const uint4*>(box + r * 128 + ((c16 ^ (r & 7)) << 4));
+    }
+  // activations of token n*8+g4 for this lane's k slice (rows past mcount are zeroed)
+  uint4 xr[NT][LK / 8];
+#pragma unroll
+  for (int n = 0; n < NT; ++n) {
+    const int tok = n * 8 + g4;
+    const uint8_t* xrow = sbase + GV_W_BYTES + (FP8 ? cw : (cw >> 1)) * (C::XROWS * 128) + tok * 128;
+#pragma unroll
+    for (int q = 0; q < LK / 8; ++q) {
+      const int ch = FP8 ? (2 * tq + q) : c16;
+      const uint4 v = *reinterpret_cast<const uint4*>(xrow + ((ch ^ (tok & 7)) << 4));
+      xr[n][q] = tok < mcount ? v : make_uint4(0, 0, 0, 0);
+    }
+  }
+  // these generic-proxy reads must be ordered before the TMA (async proxy) that
+  // refills the slot once it is released
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) mbar_arrive(empty);
+  uint32_t b[NT][LK / 2];
+#pragma unroll
+  for (int n = 0; n < NT; ++n)
+#pragma unroll
+    for (int q = 0; q < LK / 8; ++q)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) b[n][4 * q + j] = u4w(xr[n][q], j);   // f16 x 2^-8 (fp8) or bf16
+  float d[2][NT][4];
+#pragma unroll
+  for (int t = 0; t < 2; ++t)
+#pragma unroll
+    for (int n = 0; n < NT; ++n)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) d[t][n][j] = 0.f;
+#pragma unroll
+  for (int g = 0; g < LK / 4; ++g) {
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      uint32_t a0, a1, a2, a3;
+      if (FP8) {
+        e4m3x4_f16x4(u4w(w[t][0], g), a0, a2);
+        e4m3x4_f16x4(u4w(w[t][1], g), a1, a3);
+      } else {
+        a0 = u4w(w[t][0], 2 * g);
+        a1 = u4w(w[t][1], 2 * g);
+        a2 = u4w(w[t][0], 2 * g + 1);
+        a3 = u4w(w[t][1], 2 * g + 1);
+      }
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+        if (FP8) mma_f16_16816(d[t][n], a0, a1, a2, a3, b[n][2 * g], b[n][2 * g + 1]);
+        else mma_bf16_16816(d[t][n], a0, a1, a2, a3, b[n][2 * g], b[n][2 * g + 1]);
+      }
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < 2; ++t)
+#pragma unroll
+    for (int n = 0; n < NT; ++n)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[t][n][j] = fmaf(d[t][n][j], sc[t], acc[t][n][j]);
+}
+
 // Stream one 32-row tile (rows row0[0]..+15 and row0[1]..+15 of the tensor map) over
 // stages [s_begin, s_end) and multiply by activations x (rows x_row0 .. x_row0 + mcount).
 // Producer: warp 0.  Consumers: warps 1..4, each with acc[tile][nt][4] for its k slices.
@@ -123,7 +226,6 @@ __device__ __forceinline__ bool gv_stream_tile(const CUtensorMap* tmap, const CU
                                                XtuStatus* st) {
   using C = GvCfg<FP8, NT>;
   constexpr int CK = FP8 ? 64 : 32;          // k per warp per stage
-  constexpr int LK = FP8 ? 16 : 8;           // k per lane per stage
   constexpr int KSTAGE = C::KSTAGE;
   constexpr int GV_STAGES = C::STAGES;
   constexpr int GV_STAGE_BYTES = C::STAGE_BYTES;
@@ -145,22 +247,8 @@ __device__ __forceinline__ bool gv_stream_tile(const CUtensorMap* tmap, const CU
         if (it >= GV_STAGES && !mbar_wait(&empty[slot], ((it / GV_STAGES) - 1) & 1, st, 60)) { ok = false; break; }
         ++issued;
         mbar_arrive_expect_tx(&full[slot], GV_STAGE_BYTES);
-        uint8_t* dst = stages + slot * GV_STAGE_BYTES;
-        // one box for the stage's 32 weight rows x 256 bytes (two 128-byte column chunks;
-        // WMODE 1: two 16-row halves 128 rows apart) and one for its activations
-        const int s_abs = s_begin + i;
-        if (WMODE == 0) {
-          tma_load_3d(dst, tmap, &full[slot], 0, row0[0], 2 * s_abs);
-        } else if (WMODE == 1) {
-          tma_load_4d(dst, tmap, &full[slot], 0, row0[0], 0, 2 * s_abs);
-        } else {   // rows whose byte length is not a multiple of 128: four 2-D boxes
-#pragma unroll
-          for (int b = 0; b < 2; ++b)
-#pragma unroll
-            for (int h = 0; h < 2; ++h)
-              tma_load_2d(dst + b * 4096 + h * 2048, tmap, &full[slot], s_abs * KSTAGE + b * (KSTAGE / 2), row0[h]);
-        }
-        tma_load_3d(dst + GV_W_BYTES, xmap, &full[slot], 0, x_row0, s_abs * C::XBOXES);
+        gv_issue_stage<FP8, NT, WMODE>(tmap, xmap, stages + slot * GV_STAGE_BYTES, &full[slot], row0, s_begin + i,
+                                       x_row0);
       }
       if (!ok) {   // give the copies already issued (bounded) time to land before the CTA exits
         for (int j = issued > GV_STAGES ? issued - GV_STAGES : 0; j < issued; ++j) {
@@ -172,8 +260,6 @@ __device__ __forceinline__ bool gv_stream_tile(const CUtensorMap* tmap, const CU
     __syncwarp();
   } else {
     const int cw = warp - 1;
-    const int g4 = lane >> 2, tq = lane & 3;
-    const int c16 = (cw & 1) * 4 + tq;     // 16-byte chunk of the 128-byte row within box (cw >> 1)
     // this tile's block scales (x 2^8, the activation pre-scale) for its stage range
     const int kblk0 = (s_begin * KSTAGE) >> 7;
     const int nkblk = min(sk, ((s_end * KSTAGE + 127) >> 7)) - kblk0;
@@ -194,75 +280,7 @@ __device__ __forceinline__ bool gv_stream_tile(const CUtensorMap* tmap, const CU
         sc[1] = sc_sm[GV_MAX_KBLK + kb];
       }
       if (!mbar_wait(&full[slot], (it / GV_STAGES) & 1, st, 61)) { ok = false; break; }
-      const uint8_t* sbase = stages + slot * GV_STAGE_BYTES;
-      const uint8_t* box = sbase + (cw >> 1) * 4096;
-      uint4 w[2][2];
-#pragma unroll
-      for (int t = 0; t < 2; ++t)
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int r = t * 16 + gv_prow(g4) + h * 8;
-          w[t][h] = *reinterpret_cast<const uint4*>(box + r * 128 + ((c16 ^ (r & 7)) << 4));
-        }
-      // activations of token n*8+g4 for this lane's k slice (rows past mcount are zeroed)
-      uint4 xr[NT][LK / 8];
-#pragma unroll
-      for (int n = 0; n < NT; ++n) {
-        const int tok = n * 8 + g4;
-        const uint8_t* xrow = sbase + GV_W_BYTES + (FP8 ? cw : (cw >> 1)) * (C::XROWS * 128) + tok * 128;
-#pragma unroll
-        for (int q = 0; q < LK / 8; ++q) {
-          const int ch = FP8 ? (2 * tq + q) : c16;
-          const uint4 v = *reinterpret_cast<const uint4*>(xrow + ((ch ^ (tok & 7)) << 4));
-          xr[n][q] = tok < mcount ? v : make_uint4(0, 0, 0, 0);
-        }
-      }
-      // these generic-proxy reads must be ordered before the TMA (async proxy) that
-      // refills the slot once it is released
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[slot]);
-      uint32_t b[NT][LK / 2];
-#pragma unroll
-      for (int n = 0; n < NT; ++n)
-#pragma unroll
-        for (int q = 0; q < LK / 8; ++q)
-#pragma unroll
-          for (int j = 0; j < 4; ++j) b[n][4 * q + j] = u4w(xr[n][q], j);   // f16 x 2^-8 (fp8) or bf16
-      float d[2][NT][4];
-#pragma unroll
-      for (int t = 0; t < 2; ++t)
-#pragma unroll
-        for (int n = 0; n < NT; ++n)
-#pragma unroll
-          for (int j = 0; j < 4; ++j) d[t][n][j] = 0.f;
-#pragma unroll
-      for (int g = 0; g < LK / 4; ++g) {
-#pragma unroll
-        for (int t = 0; t < 2; ++t) {
-          uint32_t a0, a1, a2, a3;
-          if (FP8) {
-            e4m3x4_f16x4(u4w(w[t][0], g), a0, a2);
-            e4m3x4_f16x4(u4w(w[t][1], g), a1, a3);
-          } else {
-            a0 = u4w(w[t][0], 2 * g);
-            a1 = u4w(w[t][1], 2 * g);
-            a2 = u4w(w[t][0], 2 * g + 1);
-            a3 = u4w(w[t][1], 2 * g + 1);
-          }
-#pragma unroll
-          for (int n = 0; n < NT; ++n) {
-            if (FP8) mma_f16_16816(d[t][n], a0, a1, a2, a3, b[n][2 * g], b[n][2 * g + 1]);
-            else mma_bf16_16816(d[t][n], a0, a1, a2, a3, b[n][2 * g], b[n][2 * g + 1]);
-          }
-        }
-      }
-#pragma unroll
-      for (int t = 0; t < 2; ++t)
-#pragma unroll
-        for (int n = 0; n < NT; ++n)
-#pragma unroll
-          for (int j = 0; j < 4; ++j) acc[t][n][j] = fmaf(d[t][n][j], sc[t], acc[t][n][j]);
+      gv_mma_stage<FP8, NT>(stages + slot * GV_STAGE_BYTES, &empty[slot], cw, lane, mcount, sc, acc);
     }
   }
   phase_base += nst;
@@ -470,6 +488,225 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_dense_kernel(
       for (int p = 0; p < pr.world; ++p) st_release_sys(pr.flags[p] + pr.rank, e);
       *pr.ep_p = e;
     }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// dense fp8 decode GEMM on the 5th-generation tensor cores, for 17..32 activation rows
+// (speculative verification steps), where the warp-level MMAs of the kernels above bound
+// the call, not HBM (four 8-token column tiles per 16 weight rows).  The weight rows are
+// the MMA's M and the tokens its N:
+//   CTA = one 128-row weight tile (one block-scale row) x one K split; stages of 128 k.
+//   warp 0     TMA: the stage's e4m3 weights (128 rows x 128 B, 128-byte swizzle) and
+//              its activations (f16 x 2^-8, 32 rows x 128 k as two 64-k swizzled chunks)
+//              into a GT_RING-deep ring
+//   warp 1     TMEM (32 columns) + MMA issue: D[128, 32] += Wf16 x X^T, kind::f16,
+//              eight K = 16 steps per stage
+//   warps 2-9  widen the stage's weights: half a row per thread (warps 2-5 the first 64 k,
+//              6-9 the second), e4m3 -> f16 times the stage's block scale x 2^8 (the
+//              activations carry 2^-8), into a double-buffered K-major swizzled f16 tile
+//              (the widening, not HBM, paces the kernel: four warps left it at 2.2 TB/s);
+//              then warps 2-5 run the epilogue (row = TMEM lane, 32 token columns): y, or
+//              the split's fp32 partial, which the last split CTA of the tile sums in split
+//              order.
+// |W| x 2^8 must stay inside the f16 range (|W| < 255), which fp8 checkpoints meet by
+// construction of their block scales.
+// ---------------------------------------------------------------------------
+constexpr int GT_RING = 6;                        // weight + activation stages in flight
+constexpr int GT_W8 = 128 * 128;                  // e4m3 weights of one stage (bytes)
+constexpr int GT_X = 2 * 32 * 128;                // activations of one stage (bytes)
+constexpr int GT_STAGE = GT_W8 + GT_X;            // 24 KB
+constexpr int GT_WF16 = 2 * 128 * 128;            // widened weights: two 64-k chunks x 128 rows x 128 B
+constexpr int GT_SMEM = 1024 + GT_RING * GT_STAGE + 2 * GT_WF16 + 256 + GV_MAX_KBLK * 4;
+constexpr int GT_THREADS = 320;
+
+__host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
+  // kind::f16 with A = B = f16 (format code 0), fp32 D, both operands K-major
+  return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__global__ void __launch_bounds__(GT_THREADS, 1) gemv_tc_kernel(
+    const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
+    const float* __restrict__ wscale, int N, int K, int M, const __nv_bfloat16* __restrict__ bias, void* __restrict__ y,
+    int y_stride, int y_f32, float* __restrict__ ws, int* __restrict__ counters, XtuStatus* st) {
+  griddep_wait();   // launched with PDL: nothing upstream is touched before this
+  griddep_launch_dependents();
+  extern __shared__ uint8_t gt_smem_raw[];
+  const uint32_t raw = smem_u32(gt_smem_raw);
+  uint8_t* ring = gt_smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  uint8_t* wf16 = ring + GT_RING * GT_STAGE;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(wf16 + 2 * GT_WF16);
+  uint64_t* full = bars;                    // [GT_RING] TMA landed
+  uint64_t* empty = bars + GT_RING;         // [GT_RING] MMA done with the stage
+  uint64_t* cfull = empty + GT_RING;        // [2] widened tile ready
+  uint64_t* cempty = cfull + 2;             // [2] MMA done with the widened tile
+  uint64_t* dfull = cempty + 2;             // accumulator complete
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(dfull + 1);
+  float* scs = reinterpret_cast<float*>(bars + 32);   // the CTA's block scales x 2^8, [ns]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile = blockIdx.x, split = blockIdx.y, splits = gridDim.y;
+  const int S = K / 128, sk = (K + 127) >> 7;
+  const int per = (S + splits - 1) / splits;
+  const int s0 = min(S, split * per), s1 = min(S, s0 + per), ns = s1 - s0;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < GT_RING; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&cfull[i], 8);
+      mbar_init(&cempty[i], 1);
+    }
+    mbar_init(dfull, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(tslot, 32);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  bool ok = true;
+  if (warp == 0) {
+    // ---------------- producer
+    if (elect_one()) {
+      prefetch_tmap(&wmap);
+      prefetch_tmap(&xmap);
+      int issued = 0;
+      for (int i = 0; i < ns; ++i) {
+        const int slot = i % GT_RING;
+        if (i >= GT_RING && !mbar_wait(&empty[slot], ((i / GT_RING) - 1) & 1, st, 70)) { ok = false; break; }
+        ++issued;
+        mbar_arrive_expect_tx(&full[slot], GT_STAGE);
+        uint8_t* dst = ring + slot * GT_STAGE;
+        tma_load_3d(dst, &wmap, &full[slot], 0, tile * 128, s0 + i);
+        tma_load_3d(dst + GT_W8, &xmap, &full[slot], 0, 0, 2 * (s0 + i));
+      }
+      if (!ok) {   // give the copies already issued (bounded) time to land before the CTA exits
+        for (int j = issued > GT_RING ? issued - GT_RING : 0; j < issued; ++j)
+          mbar_wait(&full[j % GT_RING], (j / GT_RING) & 1, nullptr, 0, 50000000ull);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issue
+    if (elect_one()) {
+      constexpr uint32_t idesc = idesc_f16_f32(128, 32);
+      const uint32_t wf = smem_u32(wf16), rg = smem_u32(ring);
+      for (int i = 0; i < ns; ++i) {
+        const int slot = i % GT_RING, c = i & 1;
+        // the activations come straight from the TMA stage: observe its barrier here too
+        if (!mbar_wait(&full[slot], (i / GT_RING) & 1, st, 75) || !mbar_wait(&cfull[c], (i >> 1) & 1, st, 71)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a0 = wf + c * GT_WF16, b0 = rg + slot * GT_STAGE + GT_W8;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint32_t koff = (j >> 2) * (128 * 128) + (j & 3) * 32;
+          const uint32_t xoff = (j >> 2) * (32 * 128) + (j & 3) * 32;
+          mma_f16_ss(tmem, sdesc_kmajor_sw128(a0 + koff), sdesc_kmajor_sw128(b0 + xoff), idesc,
+                     (i > 0 || j > 0) ? 1u : 0u);
+        }
+        mma_commit(&empty[slot]);
+        mma_commit(&cempty[c]);
+      }
+      mma_commit(dfull);   // also on the error path: the epilogue waits on it (bounded)
+    }
+  } else {
+    // ---------------- widen (warps 2-9): thread = half of weight row r (= TMEM lane r)
+    const int q = warp & 3, r = q * 32 + lane, half = (warp - 2) >> 2;
+    const int rb = min(tile * 128, N - 1) >> 7;   // the tile's block-scale row
+    // the split's block scales, staged once (a global load per stage sat on every stage's path)
+    for (int j = threadIdx.x - 64; j < ns; j += 256) scs[j] = 256.f * __ldg(wscale + (size_t)rb * sk + s0 + j);
+    asm volatile("bar.sync 1, 256;" ::: "memory");
+    for (int i = 0; i < ns; ++i) {
+      const int slot = i % GT_RING, c = i & 1;
+      const float sc = scs[i];
+      if (!mbar_wait(&full[slot], (i / GT_RING) & 1, st, 72)) { ok = false; break; }
+      if (i >= 2 && !mbar_wait(&cempty[c], ((i >> 1) - 1) & 1, st, 73)) { ok = false; break; }
+      const uint8_t* src = ring + slot * GT_STAGE + r * 128;
+      uint8_t* dstrow = wf16 + c * GT_WF16 + r * 128;
+      const __half2 s2 = __floats2half2_rn(sc, sc);
+#pragma unroll
+      for (int ch = 4 * half; ch < 4 * half + 4; ++ch) {   // 16 e4m3 (k = 16 ch ..) -> two f16 pieces
+        const uint4 v = *reinterpret_cast<const uint4*>(src + ((ch ^ (r & 7)) << 4));
+        const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+        uint32_t h[8];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          uint32_t lo, hi;
+          e4m3x4_f16x4(wv[e], lo, hi);
+          __half2 l2 = __hmul2(*reinterpret_cast<__half2*>(&lo), s2);
+          __half2 h2 = __hmul2(*reinterpret_cast<__half2*>(&hi), s2);
+          h[2 * e] = *reinterpret_cast<uint32_t*>(&l2);
+          h[2 * e + 1] = *reinterpret_cast<uint32_t*>(&h2);
+        }
+        const int kc = ch >> 2, p0 = (ch & 3) * 2;   // 64-k chunk, first 16-byte piece
+        uint8_t* d = dstrow + kc * (128 * 128);
+        *reinterpret_cast<uint4*>(d + ((p0 ^ (r & 7)) << 4)) = make_uint4(h[0], h[1], h[2], h[3]);
+        *reinterpret_cast<uint4*>(d + (((p0 + 1) ^ (r & 7)) << 4)) = make_uint4(h[4], h[5], h[6], h[7]);
+      }
+      fence_proxy_async_smem();   // generic-proxy writes -> the tensor core's reads
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&cfull[c]);
+    }
+    // ---------------- epilogue (warps 2-5): row r, token columns 0..31
+    if (half == 0) {
+      const bool have = mbar_wait(dfull, 0, st, 74) && ok;
+      tc_fence_after();
+      uint32_t v[32];
+      tmem_ld32(tmem + ((uint32_t)(q * 32) << 16), v);
+      tmem_wait_ld();
+      const int row = tile * 128 + r;
+      if (have && ns > 0) {
+        float acc[32];
+#pragma unroll
+        for (int t = 0; t < 32; ++t) acc[t] = __uint_as_float(v[t]);
+        bool emit = splits == 1;
+        if (!emit) {
+          // each warp settles its own 32 rows (counter per tile quarter), so no barrier
+          // couples the four warps
+          if (row < N) {
+#pragma unroll
+            for (int t = 0; t < 32; ++t)
+              if (t < M) __stcg(ws + ((size_t)split * GV_MAX_ROWS + t) * N + row, acc[t]);
+          }
+          __threadfence();
+          __syncwarp();
+          int last = 0;
+          if (lane == 0) last = atomicAdd(counters + tile * 4 + q, 1) == splits - 1;
+          last = __shfl_sync(0xffffffffu, last, 0);
+          if (last) {
+            __threadfence();
+            if (row < N) {
+#pragma unroll
+              for (int t = 0; t < 32; ++t) acc[t] = 0.f;
+              for (int sp = 0; sp < splits; ++sp)   // split order: the bits do not depend on who came last
+#pragma unroll
+                for (int t = 0; t < 32; ++t)
+                  if (t < M) acc[t] += __ldcg(ws + ((size_t)sp * GV_MAX_ROWS + t) * N + row);
+            }
+            if (lane == 0) counters[tile * 4 + q] = 0;
+            emit = true;
+          }
+        }
+        if (emit && row < N) {
+          const float b = bias ? __bfloat162float(bias[row]) : 0.f;
+#pragma unroll
+          for (int t = 0; t < 32; ++t) {
+            if (t >= M) break;
+            if (y_f32) reinterpret_cast<float*>(y)[(size_t)t * y_stride + row] = acc[t] + b;
+            else reinterpret_cast<__nv_bfloat16*>(y)[(size_t)t * y_stride + row] = __float2bfloat16(acc[t] + b);
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 32);
   }
 }
 
@@ -1016,6 +1253,15 @@ static int gv_splits(int tiles, int S, int N, int slots) {
   return splits;
 }
 
+// the tcgen05 form of 17..32-row fp8 calls; XTU_GEMV_TC=0 keeps them on the warp-level kernel
+static bool gv_tc_enabled() {
+  static const int on = [] {
+    const char* e = getenv("XTU_GEMV_TC");
+    return e ? atoi(e) : 1;
+  }();
+  return on != 0;
+}
+
 // bf16 rows -> f16 x 2^-8 rows in the workspace's activation scratch
 static const void* gv_convert_x(const void* x, int rows, int K, int stride, float* ws, cudaStream_t s) {
   uint4* x16 = reinterpret_cast<uint4*>(ws + GV_WS_PART_FLOATS);
@@ -1049,12 +1295,39 @@ int xtu_gemv(const void* W, const float* wscale, int fp8, int N, int K, const vo
     x_stride = K;
     ++launches;
   }
+  XtuStatus* st = reinterpret_cast<XtuStatus*>(status);
   CUtensorMap tm, xm;
-  int rc = gv_wmap(&tm, W, (uint64_t)N, K, fp8 != 0, false);
+  int rc;
+  if (fp8 && M > 16 && K % 128 == 0 && gv_tc_enabled()) {
+    // 17..32 rows: the tcgen05 form (see gemv_tc_kernel)
+    const int tiles_tc = (N + 127) / 128, S_tc = K / 128;
+    int splits = tiles_tc >= gemv_num_sms() ? 1 : gemv_num_sms() / tiles_tc;
+    if (splits > S_tc) splits = S_tc;
+    while (splits > 1 && ((splits - 1) * ((S_tc + splits - 1) / splits) >= S_tc ||
+                          (long long)splits * GV_MAX_ROWS * N > GV_WS_PART_FLOATS || tiles_tc * 4 > 1024))
+      --splits;
+    const cuuint64_t wdims[3] = {128, (cuuint64_t)N, (cuuint64_t)K / 128};
+    const cuuint64_t wstr[2] = {(cuuint64_t)K, 128};
+    const cuuint32_t wbox[3] = {128, 128, 1};
+    rc = gv_tmap_nd(&tm, W, true, 3, wdims, wstr, wbox);
+    if (rc) return rc;
+    rc = gv_xmap(&xm, x, (uint64_t)M, K, x_stride, 32, false);
+    if (rc) return rc;
+    static bool init = false;
+    if (!init) {
+      rc = gv_smem_attr(gemv_tc_kernel, GT_SMEM);
+      if (rc) return rc;
+      init = true;
+    }
+    launch_pdl(gemv_tc_kernel, dim3(tiles_tc, splits), dim3(GT_THREADS), GT_SMEM, s, tm, xm, wscale, N, K, M,
+               (const __nv_bfloat16*)bias, y, y_stride, y_f32, ws, counters, st);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? launches : -(int)e;
+  }
+  rc = gv_wmap(&tm, W, (uint64_t)N, K, fp8 != 0, false);
   if (rc) return rc;
   rc = gv_xmap(&xm, x, (uint64_t)M, K, x_stride, 8 * nt, fp8 != 0);
   if (rc) return rc;
-  XtuStatus* st = reinterpret_cast<XtuStatus*>(status);
 #define XTU_GEMV_LAUNCH(F, NTV, WMV)                                                                         \
   do {                                                                                                       \
     static int occ = 0;                                                                                      \

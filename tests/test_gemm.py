@@ -192,10 +192,12 @@ def test_grouped_gemm_prefill_scale(fp8):
 @pytest.mark.gpu
 @pytest.mark.parametrize("fp8", [False, True])
 @pytest.mark.parametrize("M", [1, 3, 4, 8, 13, 16, 17, 20, 32])
-@pytest.mark.parametrize("N_,K", [(14336, 4096), (4096, 10944), (4096, 12288), (300, 512)])
+@pytest.mark.parametrize("N_,K", [(14336, 4096), (4096, 10944), (4096, 12288), (300, 512), (40000, 1024)])
 def test_gemv_decode(fp8, M, N_, K):
-    """Includes shapes with few 32-row slices, which split K across CTAs (run twice: the
-    split counters must be left zeroed for the next call)."""
+    """Shapes with few 32-row slices, which split K across CTAs, and a many-wave shape; M
+    above 16 with fp8 weights runs the tcgen05 form (weights widened to f16 on chip, 128-row
+    tiles, tokens as the MMA's N).  Run twice: the split counters must be left zeroed for
+    the next call."""
     torch.manual_seed(9)
     w = torch.randn(N_, K, device="cuda") / K ** 0.5
     bias = torch.randn(N_, device="cuda", dtype=torch.bfloat16)

@@ -237,12 +237,12 @@ def _make_paged(seqs, Hkv, D, Dv, bs=64, device="cuda"):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("Hq,Hkv,D", [(96, 8, 128), (4, 2, 64), (16, 2, 256), (8, 8, 128), (12, 1, 128)])
-@pytest.mark.parametrize("mode", ["prefill", "decode", "decode_split", "spec", "spec2"])
+@pytest.mark.parametrize("mode", ["prefill", "decode", "decode_split", "spec", "spec_split", "spec2"])
 def test_paged_attention(Hq, Hkv, D, mode):
     torch.manual_seed(5)
     if mode == "prefill":
         seqs = [(300, 300), (77, 590), (1, 1), (130, 130)]
-    elif mode == "spec":
+    elif mode in ("spec", "spec_split"):
         seqs = [(5, 700), (5, 129), (5, 64)]
     elif mode == "spec2":          # 2 query positions: up to 32 rows per KV head (two 16-row tiles)
         seqs = [(2, 700), (2, 129), (2, 64), (2, 2)]
@@ -251,6 +251,8 @@ def test_paged_attention(Hq, Hkv, D, mode):
     kc, vc, meta, T = _make_paged(seqs, Hkv, D, D)
     if mode == "decode_split":
         meta.num_splits = 8
+    elif mode == "spec_split":
+        meta.num_splits = 4
     q = torch.randn(T, Hq, D, device="cuda", dtype=torch.bfloat16)
     scale = 1.0 / math.sqrt(D)
     o = paged_attention(q, kc, vc, meta, scale)
@@ -274,6 +276,8 @@ def test_paged_attention_window_and_sinks(Hq, Hkv, D, Dv, mode, window, sinks):
     kc, vc, meta, T = _make_paged(seqs, Hkv, D, Dv)
     if mode == "decode_split":
         meta.num_splits = 8
+    elif mode == "spec_split":
+        meta.num_splits = 4
     q = torch.randn(T, Hq, D, device="cuda", dtype=torch.bfloat16)
     sk = (torch.randn(Hq, device="cuda") * 2.0).float() if sinks else None
     scale = 1.0 / math.sqrt(D)
