@@ -675,10 +675,13 @@ __global__ void __launch_bounds__(512) moe_route_decode_kernel(
     for (int k = k0 + lane * 8; k < k1; k += 256) {
       const uint4 gv = *reinterpret_cast<const uint4*>(g + k);
       const uint32_t gs[4] = {gv.x, gv.y, gv.z, gv.w};
+      // every token's load is issued unconditionally (rows past T re-read row T - 1 and are
+      // never stored), so the loads of one k step are independent and overlap: a break at
+      // T made each wait for the previous token's multiply-add (one L2 latency per token)
 #pragma unroll
       for (int t = 0; t < TT; ++t) {
-        if (t >= T) break;
-        const uint4 xv = __ldg(reinterpret_cast<const uint4*>(x + (size_t)t * x_stride + k));
+        const int tr = t < T ? t : T - 1;
+        const uint4 xv = __ldg(reinterpret_cast<const uint4*>(x + (size_t)tr * x_stride + k));
         const uint32_t xs[4] = {xv.x, xv.y, xv.z, xv.w};
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[t] += bf16_lo(gs[j]) * bf16_lo(xs[j]) + bf16_hi(gs[j]) * bf16_hi(xs[j]);

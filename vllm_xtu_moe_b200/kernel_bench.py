@@ -452,6 +452,18 @@ def bench_kda(T=15000, nh=32, dk=128, dv=128, kw=4, iters=3) -> dict:
     return _report("kda_prefill", dict(T=T, nh=nh, dk=dk, dv=dv), ms, nbytes, flops)
 
 
+def bench_router_decode(T: int, E=128, H=4096, K=8, iters=20) -> dict:
+    """Decode router + permute in one launch (GLM-4.5-Air: 128 experts, sigmoid + bias,
+    top-8) for T tokens; bytes = the bf16 gate weights and the tokens."""
+    x = torch.randn(T, H, device="cuda").to(torch.bfloat16)
+    gate = (torch.randn(E, H, device="cuda") * 0.02).to(torch.bfloat16)
+    bias = torch.randn(E, device="cuda") * 0.01
+    ws = M.MoEWorkspace(max(T, 16), K, E, H, 1408, x.device)
+    fn = lambda: M.route_decode(x, gate, bias, K, "sigmoid", 1, 1, True, 1.0, ws, 0, E)
+    ms = time_fn(fn, iters)
+    return _report("router_decode", dict(T=T, E=E, H=H, K=K), ms, E * H * 2 + T * H * 2, 2 * T * E * H)
+
+
 def bench_rmsnorm(T=16384, H=4096, iters=20) -> dict:
     x = torch.randn(T, H, device="cuda").to(torch.bfloat16)
     r = torch.randn(T, H, device="cuda").to(torch.bfloat16)
@@ -598,6 +610,7 @@ OPS = {
     "mla_decode": lambda a: bench_mla_decode(),
     "attention_prefill": lambda a: bench_attn_prefill(min(a.tokens or 8192, 16384)),
     "rmsnorm": lambda a: bench_rmsnorm(),
+    "router_decode": lambda a: [bench_router_decode(t) for t in ((a.tokens,) if a.tokens else (4, 20, 32))],
     "tp_fused": lambda a: bench_tp_fused(),
     "ep_fused": lambda a: bench_ep_fused(),
     "deltanet_prefill": lambda a: bench_deltanet(T=a.tokens or 15000),
