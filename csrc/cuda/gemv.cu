@@ -95,6 +95,9 @@ constexpr int GV_ROW_BYTES = 256;            // bytes of one weight row per stag
 constexpr int GV_W_BYTES = 32 * GV_ROW_BYTES;   // weight part of a stage: 32 rows
 constexpr int GV_MAX_KBLK = 128;             // block scales staged per tile (K <= 16384)
 constexpr int GV_MAX_ROWS = 32;              // activation rows of a dense GEMV call (NT <= 4)
+#ifndef GV_STAGES_NT1
+#define GV_STAGES_NT1 4                      // ring depth of the one-column-tile forms
+#endif
 
 // A stage = the tile's 32 weight rows x 256 bytes, followed by the activations of the same
 // k range (bf16, 8 * NT token rows per 128-byte box), both loaded by TMA.
@@ -105,7 +108,8 @@ struct GvCfg {
   static constexpr int XBOXES = KSTAGE / 64;                     // 64 bf16 per 128-byte box
   static constexpr int X_BYTES = XBOXES * XROWS * 128;
   static constexpr int STAGE_BYTES = GV_W_BYTES + X_BYTES;       // multiple of 1024
-  static constexpr int STAGES = NT >= 4 ? 3 : 4;                 // 32-row tiles: two CTAs per SM still fit
+  // 32-row tiles: two CTAs per SM still fit (NT = 4), three (NT = 1, 2)
+  static constexpr int STAGES = NT >= 4 ? 3 : NT == 1 ? GV_STAGES_NT1 : 4;
   static constexpr int RED_FLOATS = GV_CWARPS * 32 * 2 * NT * 4;
   static constexpr int BYTES = 1024 + STAGES * STAGE_BYTES + RED_FLOATS * 4 + 2 * GV_MAX_KBLK * 4 +
                                2 * STAGES * 8 + 64;

@@ -146,6 +146,18 @@ def moe_ref(x, ids, weights, experts: ExpertWeights, lo=0, hi=None, act_limit=0.
     return out
 
 
+# rows per pass of the gathered grouped GEMV on verification steps (8 or 16): an expert
+# rarely holds more than a few of a 20-row step's pairs, and 8-row activation boxes leave
+# more of each CTA's ring to weights (GLM-4.5-Air, C = 4, MTP k = 4: decode step 21.31 ->
+# 19.52 ms against 16-row passes); XTU_MOE_VERIFY_ROWS overrides
+import os as _os
+_VERIFY_PASS_ROWS = int(_os.environ.get("XTU_MOE_VERIFY_ROWS", "8"))
+# steps of at most this many tokens take the token-direct form (every active expert
+# multiplies all of the step's tokens); larger ones gather each expert's rows (C = 2,
+# MTP k = 4, 10 rows: decode step 14.31 -> 13.33 ms against the token-direct form)
+_DIRECT_MAX_ROWS = int(_os.environ.get("XTU_MOE_DIRECT_ROWS", "8"))
+
+
 def moe_experts_partial(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, experts: ExpertWeights,
                         ws: MoEWorkspace, *, lo: int = 0, act_limit: float = 0.0, act_alpha: float = 1.0,
                         act_beta: float = 0.0, shared_mlp=None, permuted: bool = False) -> torch.Tensor | None:
@@ -172,7 +184,7 @@ def moe_experts_partial(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tenso
     # step's tokens directly (token-direct form), above that the permute gathers them
     gemv_path = (T <= G.GEMV_MAX_M_MOE and experts.interleaved and experts.fmt not in G.FP4_FMTS
                  and H % 128 == 0 and I % 128 == 0)   # whole 128-byte chunks per weight row
-    if gemv_path and T <= G.GEMV_MAX_M and E <= 1024:
+    if gemv_path and T <= min(G.GEMV_MAX_M, _DIRECT_MAX_ROWS) and E <= 1024:
         # one-CTA permute (no row gather): the gate/up GEMV reads the T tokens directly
         # and keeps each expert's own columns through ws.tokrow
         xt = G.tma_rows(x)
@@ -219,7 +231,7 @@ def moe_experts_partial(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tenso
         N.call("xtu_moe_gemv", experts.w13.data_ptr(), N.ptr(experts.s13 if fp8 else None),
                experts.w2.data_ptr(), N.ptr(experts.s2 if fp8 else None), int(fp8), E, H, I, ws.xp.data_ptr(), f16s,
                H, None, T, ws.seg.data_ptr(), ws.perm_slot.data_ptr(), ws.perm_w.data_ptr(), ws.h.data_ptr(),
-               ws.slots.data_ptr(), min(T, G.GEMV_MAX_M), min(E, n), n, ws.active.data_ptr(), 1,
+               ws.slots.data_ptr(), min(T, _VERIFY_PASS_ROWS), min(E, n), n, ws.active.data_ptr(), 1,
                float(act_limit), float(act_alpha), float(act_beta), *_shared_ptrs(shared_mlp), n,
                _gv_ws(x.device), N.status_buffer(x.device).data_ptr(), s)
         return ws.slots[n:n + T] if shared_mlp is not None else None
