@@ -160,3 +160,107 @@ def test_generation_with_fp8_cache_gpu(graph):
         llm.shutdown()
     same = sum(x == y for a, b in zip(out["bf16"], out["fp8"]) for x, y in zip(a, b))
     assert same >= 0.6 * sum(len(a) for a in out["bf16"]), out
+
+
+# ----------------------------------------------------------------------------- MLA latent
+def _tiny_dsv3():
+    from vllm_xtu_moe_b200.models.config import get_preset, scaled_down
+    return scaled_down(get_preset("deepseek-v3"), layers=2, hidden=512, experts=16).replace(
+        num_heads=8, q_lora_rank=256, moe_intermediate=256, shared_intermediate=256, dense_intermediate=1024,
+        expert_fmt="bf16", dense_fmt="bf16", num_mtp_layers=0)
+
+
+def test_mla_fp8_latent_cache_write_and_dequant_cpu():
+    """The fp8 latent write rounds latent / scale to e4m3 at each slot; the dequantising
+    gather lays the step's blocks out in sequence order (b * maxb + j) times the scale."""
+    from vllm_xtu_moe_b200.models.mla import dequant_latent_cache, write_latent_fp8
+    torch.manual_seed(0)
+    D, bs, nb = 96, 64, 6
+    cache = torch.zeros(nb, 1, bs, D, dtype=torch.float8_e4m3fn)
+    T = 70
+    x = (torch.randn(T, 1, D) * 3).to(torch.bfloat16)
+    bt = torch.tensor([[4, 1]], dtype=torch.int32)
+    slots = torch.tensor([int(bt[0, t // bs]) * bs + t % bs for t in range(T)], dtype=torch.int32)
+    write_latent_fp8(x, slots, cache, 0.5)
+    meta = AttnMetadata(num_seqs=1, q_start=torch.tensor([0, T]), kv_len=torch.tensor([T]), block_table=bt,
+                        slot_mapping=slots, positions=torch.arange(T), max_q_len=T, max_kv_len=T, is_decode=False,
+                        q_start_host=[0, T], kv_len_host=[T])
+    out, m2 = dequant_latent_cache(cache, meta, 0.5)
+    assert torch.equal(m2.block_table, torch.tensor([[0, 1]], dtype=torch.int32))
+    flat = out.view(-1, D)[:T].float()
+    want = (to_e4m3(x[:, 0].float(), 2.0).float() * 0.5).to(torch.bfloat16).float()
+    assert torch.equal(flat, want)
+
+
+def test_mla_model_with_fp8_latent_cache_close_to_bf16_cpu():
+    from vllm_xtu_moe_b200.engine import LLM, SamplingParams
+    from vllm_xtu_moe_b200.engine.runner import RunnerConfig
+    from vllm_xtu_moe_b200.models.model import build_model
+    m = build_model(_tiny_dsv3(), device="cpu", seed=2)
+    prompts = [list(range(3, 90)), list(range(7, 30))]
+    out = {}
+    for kv in ("bf16", "fp8"):
+        rc = RunnerConfig(block_size=64, max_seqs=2, max_model_len=256, max_batched_tokens=128,
+                          use_cuda_graph=False, kv_cache_dtype=kv)
+        out[kv] = [r.token_ids for r in LLM(m, device="cpu", runner_config=rc).generate(
+            prompts, SamplingParams(max_tokens=6))]
+    same = sum(x == y for a, b in zip(out["bf16"], out["fp8"]) for x, y in zip(a, b))
+    assert same >= 0.6 * 12, out
+
+
+@pytest.mark.gpu
+def test_mla_fp8_latent_kernels_match_reference():
+    """xtu_mla_latent_write_fp8 / xtu_mla_latent_dequant_gather against the CPU path, bit
+    for bit (e4m3 rounding with saturation, then e4m3 x scale rounded to bf16)."""
+    from vllm_xtu_moe_b200.models.mla import dequant_latent_cache, write_latent_fp8
+    torch.manual_seed(1)
+    D, bs, nb = 576, 64, 12
+    T = [150, 40]
+    x = (torch.randn(sum(T), 1, D) * 40).to(torch.bfloat16)   # some values past 448 x scale saturate
+    bt = torch.tensor([[7, 2, 9], [5, 0, 0]], dtype=torch.int32)
+    slots, q_start, pos = [], [0], []
+    for b, n in enumerate(T):
+        slots += [int(bt[b, t // bs]) * bs + t % bs for t in range(n)]
+        q_start.append(q_start[-1] + n)
+        pos += list(range(n))
+    slots = torch.tensor(slots, dtype=torch.int32)
+    meta = AttnMetadata(num_seqs=2, q_start=torch.tensor(q_start, dtype=torch.int32),
+                        kv_len=torch.tensor(T, dtype=torch.int32), block_table=bt, slot_mapping=slots,
+                        positions=torch.tensor(pos, dtype=torch.int32), max_q_len=150, max_kv_len=150,
+                        is_decode=False, q_start_host=q_start, kv_len_host=T)
+    ref_cache = torch.zeros(nb, 1, bs, D, dtype=torch.float8_e4m3fn)
+    write_latent_fp8(x, slots, ref_cache, 0.25)
+    ref, _ = dequant_latent_cache(ref_cache, meta, 0.25)
+    gmeta = AttnMetadata(**{k: (v.cuda() if isinstance(v, torch.Tensor) else v) for k, v in meta.__dict__.items()})
+    cache = torch.zeros(nb, 1, bs, D, dtype=torch.float8_e4m3fn, device="cuda")
+    write_latent_fp8(x.cuda(), gmeta.slot_mapping, cache, 0.25)
+    got, _ = dequant_latent_cache(cache, gmeta, 0.25)
+    torch.cuda.synchronize()
+    N.check_status()
+    assert torch.equal(cache.cpu().view(torch.uint8), ref_cache.view(torch.uint8))
+    for b, n in enumerate(T):   # blocks past a sequence's length are not written
+        nbk = (n + bs - 1) // bs
+        assert torch.equal(got.view(2, 3, bs, D)[b, :nbk].cpu(), ref.view(2, 3, bs, D)[b, :nbk])
+
+
+@pytest.mark.gpu
+def test_mla_generation_with_fp8_latent_cache_gpu():
+    """DeepSeek-V3-shaped MLA with an fp8 latent cache: CUDA-graph decode equals eager decode
+    token for token, and both stay close to the bf16 cache's tokens."""
+    from vllm_xtu_moe_b200.engine import LLM, SamplingParams
+    from vllm_xtu_moe_b200.engine.runner import RunnerConfig
+    from vllm_xtu_moe_b200.models.model import build_model
+    m = build_model(_tiny_dsv3(), device="cuda", seed=4)
+    prompts = [list(range(1, 150)), list(range(9, 70))]
+    out = {}
+    for kv, graph in (("bf16", False), ("fp8", False), ("fp8", True)):
+        rc = RunnerConfig(block_size=64, max_seqs=2, max_model_len=512, max_batched_tokens=256,
+                          use_cuda_graph=graph, kv_cache_dtype=kv)
+        llm = LLM(m, device="cuda", runner_config=rc)
+        out[(kv, graph)] = [r.token_ids for r in llm.generate(prompts, SamplingParams(max_tokens=10))]
+        torch.cuda.synchronize()
+        N.check_status()
+        llm.shutdown()
+    assert out[("fp8", False)] == out[("fp8", True)]
+    same = sum(x == y for a, b in zip(out[("bf16", False)], out[("fp8", False)]) for x, y in zip(a, b))
+    assert same >= 0.6 * 20, out

@@ -6,18 +6,71 @@ expands the latent into per-head K/V (qk dim = nope + rope, v dim = v_head_dim)
 and runs causal attention; decode absorbs W_UK into the query and W_UV into the
 output so attention runs directly over the 576-wide latent (MQA-like: all 128
 heads share one KV "head"), which is what makes MLA decode bandwidth-cheap.
+
+An fp8 latent cache (``kv_cache_dtype="fp8"``) stores e4m3 rows (latent / latent_scale,
+one scale per layer): half the bytes per cached token, so twice the context fits.  Each
+step dequantises its sequences' blocks into a bf16 scratch cache that the latent kernels
+read (``csrc/cuda/mla_fp8.cu``); the trade is capacity, not bandwidth.
 """
 from __future__ import annotations
 
+import dataclasses
 import math
 
 import torch
 
+from ..ops import _native as N
 from ..ops import basic as B
 from ..ops import gemm as G
 from ..ops.attention import AttnMetadata, paged_attention
 from .config import ModelConfig
 from .layers import Linear
+
+
+_LATENT_SCRATCH: dict = {}
+
+
+def write_latent_fp8(entry: torch.Tensor, slot_mapping: torch.Tensor, cache: torch.Tensor, scale: float) -> None:
+    """entry [T, 1, D] bf16 -> e4m3 rows entry / scale (saturated at +-448) of the paged
+    latent cache [blocks, 1, bs, D] at each token's slot (slot < 0: skipped)."""
+    T, _, D = entry.shape
+    bs = cache.shape[2]
+    if not entry.is_cuda:
+        sm = slot_mapping.long()
+        valid = sm >= 0
+        cache[(sm // bs)[valid], 0, (sm % bs)[valid]] = B.to_e4m3(entry[valid, 0], 1.0 / scale)
+        return
+    x = entry.reshape(T, D).to(torch.bfloat16).contiguous()
+    N.call("xtu_mla_latent_write_fp8", x.data_ptr(), x.stride(0), T, D, slot_mapping.data_ptr(),
+           cache.shape[0] * bs, cache.data_ptr(), float(1.0 / scale), N.status_buffer(x.device).data_ptr(),
+           N.stream_ptr(x.device))
+
+
+def dequant_latent_cache(cache: torch.Tensor, meta: AttnMetadata, scale: float):
+    """The blocks of the step's sequences of an e4m3 latent cache -> (bf16 cache [B * maxb,
+    1, bs, D] with block j of sequence b at b * maxb + j, metadata with that block table).
+    The scratch cache and block table are shared by all layers (one layer runs at a time)
+    and keep their addresses, so a captured decode graph replays them."""
+    nb, _, bs, D = cache.shape
+    Bn, maxb = meta.block_table.shape
+    dev = cache.device
+    key = (dev, Bn * maxb, bs, D)
+    sc = _LATENT_SCRATCH.get(key)
+    if sc is None:
+        sc = (torch.zeros(Bn * maxb, 1, bs, D, dtype=torch.bfloat16, device=dev),
+              torch.arange(Bn * maxb, dtype=torch.int32, device=dev).view(Bn, maxb))
+        _LATENT_SCRATCH[key] = sc
+    out, bt = sc
+    if cache.is_cuda:
+        N.call("xtu_mla_latent_dequant_gather", cache.data_ptr(), D, meta.block_table.data_ptr(),
+               meta.block_table.stride(0), meta.kv_len.data_ptr(), Bn, maxb, nb, float(scale), out.data_ptr(),
+               N.status_buffer(dev).data_ptr(), N.stream_ptr(dev))
+    else:
+        kl = meta.kv_len_host if meta.kv_len_host is not None else meta.kv_len.tolist()
+        for b in range(Bn):
+            for j in range((int(kl[b]) + bs - 1) // bs):
+                out[b * maxb + j] = (cache[int(meta.block_table[b, j])].float() * scale).to(torch.bfloat16)
+    return out, dataclasses.replace(meta, block_table=bt)
 
 
 class DSAIndexer:
@@ -97,6 +150,7 @@ class MLAAttention:
             m = 0.1 * float(rs["mscale_all_dim"]) * math.log(f) + 1.0 if f > 1 else 1.0
             mscale = m * m
         self.scale = mscale / math.sqrt(self.dn + self.dr)
+        self.latent_scale = 1.0    # fp8 latent cache: stored value = latent / latent_scale
         self._w_uk = None
         self._w_uv = None
         self._w_ukT = None
@@ -175,6 +229,10 @@ class MLAAttention:
         entry = torch.cat([latent, k_rope.view(T, dr)], dim=-1).view(T, 1, dc + dr)
         k_cache = kv[0]
         self._write_latent(entry, meta, k_cache)
+        if k_cache.dtype == torch.float8_e4m3fn:
+            # fp8 latent cache: the step's sequences' blocks, dequantised into a bf16 scratch
+            # cache that the latent attention kernels read (block table remapped)
+            k_cache, meta = dequant_latent_cache(k_cache, meta, self.latent_scale)
         q_nope = q[:, :, :dn]
         if self.indexer is not None:
             # DSA: the indexer sees every token; attention is sparse once a context can hold
@@ -232,6 +290,9 @@ class MLAAttention:
         return outs[0] if len(outs) == 1 else torch.cat(outs)
 
     def _write_latent(self, entry, meta, k_cache):
+        if k_cache.dtype == torch.float8_e4m3fn:
+            write_latent_fp8(entry, meta.slot_mapping, k_cache, self.latent_scale)
+            return
         B.write_cache_rows(entry.to(k_cache.dtype).contiguous(), meta.slot_mapping, k_cache)
 
     def _prefill(self, q_nope, q_rope, meta, k_cache):

@@ -211,7 +211,7 @@ class MoETransformer:
             if c.layer_type(i) == "linear" or (skip_swa and c.layer_type(i) == "swa"):
                 continue
             if c.is_mla:
-                n += (c.kv_lora_rank + c.qk_rope_head_dim + (c.index_head_dim if c.index_topk else 0)) * 2
+                n += (c.kv_lora_rank + c.qk_rope_head_dim) * gqa_b + (c.index_head_dim * 2 if c.index_topk else 0)
             else:
                 n += c.kv_heads(i) * (c.head_dim + c.gqa_v_dim) * gqa_b
         return n
@@ -219,14 +219,20 @@ class MoETransformer:
     def _attn_cache(self, i: int, num_blocks: int, block_size: int, dtype, device, kv_dtype: str = "bf16"):
         """Paged KV cache of attention layer i: (K, V), or (latent, None) for MLA.  kv_dtype
         "fp8": e4m3 K [blocks, Hkv, bs, D] and V transposed per block [blocks, Hkv, Dv, bs]
-        (GQA layers; MLA latents stay bf16)."""
+        (GQA layers), e4m3 latent rows [blocks, 1, bs, kv_lora + rope] (MLA layers without
+        sparse attention)."""
         c = self.cfg
+        if kv_dtype not in ("bf16", "auto", "fp8"):
+            raise ValueError(f"kv_cache_dtype {kv_dtype!r}: expected 'bf16' or 'fp8'")
         if c.is_mla:
+            if kv_dtype == "fp8" and c.index_topk:
+                raise NotImplementedError("fp8 latent cache with DeepSeek sparse attention")
             # DSA layers: the indexer's key cache rides in the second slot
             idx = (torch.zeros(num_blocks, 1, block_size, c.index_head_dim, dtype=torch.bfloat16, device=device)
                    if c.index_topk else None)
+            ldt = torch.float8_e4m3fn if kv_dtype == "fp8" else torch.bfloat16
             return (torch.zeros(num_blocks, 1, block_size, c.kv_lora_rank + c.qk_rope_head_dim,
-                                dtype=torch.bfloat16, device=device), idx)
+                                dtype=ldt, device=device), idx)
         nkv = c.kv_heads(i)
         if kv_dtype == "fp8":
             f8 = torch.float8_e4m3fn

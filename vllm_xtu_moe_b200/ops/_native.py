@@ -91,6 +91,8 @@ _SIGS: dict[str, list] = {
                            ctypes.c_longlong, P],
     "xtu_moe_permute_decode": [P, P, c_int, c_int, c_int, c_int, P, P, P, P, P, P],
     "xtu_moe_gather_rows": [P, c_int, c_int, c_int, P, P, c_int, c_int, P, c_int, P],
+    "xtu_mla_latent_write_fp8": [P, c_int, c_int, c_int, P, ctypes.c_longlong, P, c_float, P, P],
+    "xtu_mla_latent_dequant_gather": [P, c_int, P, c_int, P, c_int, c_int, c_int, c_float, P, P, P],
     "xtu_moe_route_decode": [P, c_int, c_int, P, c_int, c_int, P, c_int, c_int, c_int, c_int, c_int, c_float, P, P,
                              P, P, c_int, c_int, P, P, P, P, P, P],
     "xtu_bridge_post": [P, c_int, P, P, c_int, c_int, c_int, c_int, c_int, c_int, P, P, P, P, c_int, c_int, P, P, P],
