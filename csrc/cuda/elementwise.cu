@@ -646,10 +646,10 @@ __global__ void __launch_bounds__(512) moe_permute_decode_kernel(const int* __re
   permute_decode_block(ids, weights, n, K, lo, hi, seg, perm_slot, perm_w, active, tokrow);
 }
 
-// Decode router in one launch (T <= TT tokens, TT = 16 or 32; E <= 1024 experts): every CTA
-// computes the fp32 logits of some experts for all tokens (one warp per expert row, bf16
-// gate weights [E, H]), the CTA that finishes last (counter, re-zeroed) then runs the top-k
-// of every token and the decode permute.
+// Decode router in one launch (T <= TT tokens, TT = 16 or 32; E <= 1024 experts): CTA e
+// computes the fp32 logits of expert e for all tokens (bf16 gate weights [E, H]), the CTA
+// that finishes last (counter, re-zeroed) then runs the top-k of every token and the
+// decode permute.
 template <int PER, int TT>
 __global__ void __launch_bounds__(512) moe_route_decode_kernel(
     const __nv_bfloat16* __restrict__ x, int x_stride, int T, const __nv_bfloat16* __restrict__ gate, int E, int H,
@@ -660,18 +660,19 @@ __global__ void __launch_bounds__(512) moe_route_decode_kernel(
   griddep_wait();   // launched with PDL: nothing upstream is touched before this
   griddep_launch_dependents();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  // four experts per CTA, four warps per expert row (a quarter of H each), so that many
-  // SMs stream the gate weights and every warp has few dependent loads
+  // one expert row per CTA, its 16 warps each a sixteenth of H, so that E CTAs share the
+  // multiply-adds (four experts per CTA left 32 SMs issuing every token's products for a
+  // quarter of H: 20 us of a 40 us call at 20 tokens)
   __shared__ float part[16][TT];
-  const int gw = blockIdx.x * 4 + (warp >> 2), q = warp & 3;
+  const int gw = blockIdx.x;
   float acc[TT];
 #pragma unroll
   for (int t = 0; t < TT; ++t) acc[t] = 0.f;
-  if (gw < E) {
-    const int kq = ((H / 8 + 3) / 4) * 8;           // this quarter's [k0, k1)
-    const int k0 = q * kq, k1 = min(H, k0 + kq);
+  {
+    const int kq = ((H / 8 + 15) / 16) * 8;          // this warp's [k0, k1)
+    const int k0 = warp * kq, k1 = min(H, k0 + kq);
     const __nv_bfloat16* g = gate + (size_t)gw * H;
-#pragma unroll 4
+#pragma unroll 2
     for (int k = k0 + lane * 8; k < k1; k += 256) {
       const uint4 gv = *reinterpret_cast<const uint4*>(g + k);
       const uint32_t gs[4] = {gv.x, gv.y, gv.z, gv.w};
@@ -694,10 +695,12 @@ __global__ void __launch_bounds__(512) moe_route_decode_kernel(
     if (lane == 0) part[warp][t] = v;
   }
   __syncthreads();
-  if (threadIdx.x < 4 * TT) {   // (expert of the CTA, token): the four quarters in order
-    const int ee = threadIdx.x / TT, t = threadIdx.x % TT, e = blockIdx.x * 4 + ee;
-    if (e < E && t < T)
-      logits[(size_t)t * E + e] = ((part[4 * ee][t] + part[4 * ee + 1][t]) + part[4 * ee + 2][t]) + part[4 * ee + 3][t];
+  if (threadIdx.x < TT && threadIdx.x < T) {   // token t of this expert: the 16 slices in order
+    const int t = threadIdx.x;
+    float v = 0.f;
+#pragma unroll
+    for (int w = 0; w < 16; ++w) v += part[w][t];
+    logits[(size_t)t * E + gw] = v;
   }
   __shared__ int s_last;
   __threadfence();
@@ -1087,7 +1090,7 @@ int xtu_moe_route_decode(const void* x, int x_stride, int T, const void* gate, i
       hi - lo > 1024)
     return -2;
   const int per = (E + 31) / 32;
-  const dim3 grid((E + 3) / 4);
+  const dim3 grid(E);
 #define XTU_ROUTE_T(P, TTV)                                                                                  \
   launch_pdl(moe_route_decode_kernel<P, TTV>, grid, dim3(512), 0, s, (const __nv_bfloat16*)x, x_stride, T,   \
              (const __nv_bfloat16*)gate, E, H, bias, K, scoring, n_group, topk_group, renorm, scale, logits,   \
