@@ -516,12 +516,21 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_dense_kernel(
 // |W| x 2^8 must stay inside the f16 range (|W| < 255), which fp8 checkpoints meet by
 // construction of their block scales.
 // ---------------------------------------------------------------------------
-constexpr int GT_RING = 6;                        // weight + activation stages in flight
+#ifndef GT_RING_DEPTH
+#define GT_RING_DEPTH 6
+#endif
+#ifndef GT_CBUF_DEPTH
+#define GT_CBUF_DEPTH 2
+#endif
+constexpr int GT_RING = GT_RING_DEPTH;            // weight + activation stages in flight
+constexpr int GT_CBUF = GT_CBUF_DEPTH;            // widened tiles in flight (widening runs ahead of the MMA)
+// (qkv 14336 x 4096, 20 rows: 6 / 2 -> 25.6 us per call, 4 / 3 -> 27.9 us: the weight bytes
+// in flight count for more than the widening running further ahead)
 constexpr int GT_W8 = 128 * 128;                  // e4m3 weights of one stage (bytes)
 constexpr int GT_X = 2 * 32 * 128;                // activations of one stage (bytes)
 constexpr int GT_STAGE = GT_W8 + GT_X;            // 24 KB
 constexpr int GT_WF16 = 2 * 128 * 128;            // widened weights: two 64-k chunks x 128 rows x 128 B
-constexpr int GT_SMEM = 1024 + GT_RING * GT_STAGE + 2 * GT_WF16 + 256 + GV_MAX_KBLK * 4;
+constexpr int GT_SMEM = 1024 + GT_RING * GT_STAGE + GT_CBUF * GT_WF16 + 256 + GV_MAX_KBLK * 4;
 constexpr int GT_THREADS = 320;
 
 __host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
@@ -539,12 +548,12 @@ __global__ void __launch_bounds__(GT_THREADS, 1) gemv_tc_kernel(
   const uint32_t raw = smem_u32(gt_smem_raw);
   uint8_t* ring = gt_smem_raw + (((raw + 1023u) & ~1023u) - raw);
   uint8_t* wf16 = ring + GT_RING * GT_STAGE;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(wf16 + 2 * GT_WF16);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(wf16 + GT_CBUF * GT_WF16);
   uint64_t* full = bars;                    // [GT_RING] TMA landed
   uint64_t* empty = bars + GT_RING;         // [GT_RING] MMA done with the stage
-  uint64_t* cfull = empty + GT_RING;        // [2] widened tile ready
-  uint64_t* cempty = cfull + 2;             // [2] MMA done with the widened tile
-  uint64_t* dfull = cempty + 2;             // accumulator complete
+  uint64_t* cfull = empty + GT_RING;        // [GT_CBUF] widened tile ready
+  uint64_t* cempty = cfull + GT_CBUF;       // [GT_CBUF] MMA done with the widened tile
+  uint64_t* dfull = cempty + GT_CBUF;       // accumulator complete
   uint32_t* tslot = reinterpret_cast<uint32_t*>(dfull + 1);
   float* scs = reinterpret_cast<float*>(bars + 32);   // the CTA's block scales x 2^8, [ns]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -557,7 +566,7 @@ __global__ void __launch_bounds__(GT_THREADS, 1) gemv_tc_kernel(
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < GT_CBUF; ++i) {
       mbar_init(&cfull[i], 8);
       mbar_init(&cempty[i], 1);
     }
@@ -596,9 +605,10 @@ __global__ void __launch_bounds__(GT_THREADS, 1) gemv_tc_kernel(
       constexpr uint32_t idesc = idesc_f16_f32(128, 32);
       const uint32_t wf = smem_u32(wf16), rg = smem_u32(ring);
       for (int i = 0; i < ns; ++i) {
-        const int slot = i % GT_RING, c = i & 1;
+        const int slot = i % GT_RING, c = i % GT_CBUF;
         // the activations come straight from the TMA stage: observe its barrier here too
-        if (!mbar_wait(&full[slot], (i / GT_RING) & 1, st, 75) || !mbar_wait(&cfull[c], (i >> 1) & 1, st, 71)) {
+        if (!mbar_wait(&full[slot], (i / GT_RING) & 1, st, 75) ||
+            !mbar_wait(&cfull[c], (i / GT_CBUF) & 1, st, 71)) {
           ok = false;
           break;
         }
@@ -624,10 +634,10 @@ __global__ void __launch_bounds__(GT_THREADS, 1) gemv_tc_kernel(
     for (int j = threadIdx.x - 64; j < ns; j += 256) scs[j] = 256.f * __ldg(wscale + (size_t)rb * sk + s0 + j);
     asm volatile("bar.sync 1, 256;" ::: "memory");
     for (int i = 0; i < ns; ++i) {
-      const int slot = i % GT_RING, c = i & 1;
+      const int slot = i % GT_RING, c = i % GT_CBUF;
       const float sc = scs[i];
       if (!mbar_wait(&full[slot], (i / GT_RING) & 1, st, 72)) { ok = false; break; }
-      if (i >= 2 && !mbar_wait(&cempty[c], ((i >> 1) - 1) & 1, st, 73)) { ok = false; break; }
+      if (i >= GT_CBUF && !mbar_wait(&cempty[c], ((i / GT_CBUF) - 1) & 1, st, 73)) { ok = false; break; }
       const uint8_t* src = ring + slot * GT_STAGE + r * 128;
       uint8_t* dstrow = wf16 + c * GT_WF16 + r * 128;
       const __half2 s2 = __floats2half2_rn(sc, sc);
