@@ -496,7 +496,7 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_dense_kernel(
 }
 
 // ---------------------------------------------------------------------------
-// dense fp8 decode GEMM on the 5th-generation tensor cores, for 17..32 activation rows
+// dense decode GEMM on the 5th-generation tensor cores, for 17..32 activation rows
 // (speculative verification steps), where the warp-level MMAs of the kernels above bound
 // the call, not HBM (four 8-token column tiles per 16 weight rows).  The weight rows are
 // the MMA's M and the tokens its N:
@@ -515,6 +515,9 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_dense_kernel(
 //              order.
 // |W| x 2^8 must stay inside the f16 range (|W| < 255), which fp8 checkpoints meet by
 // construction of their block scales.
+// bf16 weights (FP8 = false: e.g. the LM head of a verification step) need no widening: the
+// MMA reads each stage's weights as TMA lands them (two 64-k swizzled chunks) with the bf16
+// activations, through a 5-deep ring of 40 KB stages.
 // ---------------------------------------------------------------------------
 #ifndef GT_RING_DEPTH
 #define GT_RING_DEPTH 6
@@ -532,12 +535,17 @@ constexpr int GT_STAGE = GT_W8 + GT_X;            // 24 KB
 constexpr int GT_WF16 = 2 * 128 * 128;            // widened weights: two 64-k chunks x 128 rows x 128 B
 constexpr int GT_SMEM = 1024 + GT_RING * GT_STAGE + GT_CBUF * GT_WF16 + 256 + GV_MAX_KBLK * 4;
 constexpr int GT_THREADS = 320;
+// the bf16-weight form: 32 KB of weights + the activations per stage, no widened tiles
+constexpr int GT_RING_BF = 5;
+constexpr int GT_STAGE_BF = 2 * GT_W8 + GT_X;
+constexpr int GT_SMEM_BF = 1024 + GT_RING_BF * GT_STAGE_BF + 256 + GV_MAX_KBLK * 4;
 
 __host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
   // kind::f16 with A = B = f16 (format code 0), fp32 D, both operands K-major
   return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
+template <bool FP8>
 __global__ void __launch_bounds__(GT_THREADS, 1) gemv_tc_kernel(
     const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
     const float* __restrict__ wscale, int N, int K, int M, const __nv_bfloat16* __restrict__ bias, void* __restrict__ y,
@@ -546,12 +554,15 @@ __global__ void __launch_bounds__(GT_THREADS, 1) gemv_tc_kernel(
   griddep_launch_dependents();
   extern __shared__ uint8_t gt_smem_raw[];
   const uint32_t raw = smem_u32(gt_smem_raw);
+  constexpr int RING = FP8 ? GT_RING : GT_RING_BF;
+  constexpr int STAGE = FP8 ? GT_STAGE : GT_STAGE_BF;
+  constexpr int WB = FP8 ? GT_W8 : 2 * GT_W8;           // weight bytes of a stage
   uint8_t* ring = gt_smem_raw + (((raw + 1023u) & ~1023u) - raw);
-  uint8_t* wf16 = ring + GT_RING * GT_STAGE;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(wf16 + GT_CBUF * GT_WF16);
-  uint64_t* full = bars;                    // [GT_RING] TMA landed
-  uint64_t* empty = bars + GT_RING;         // [GT_RING] MMA done with the stage
-  uint64_t* cfull = empty + GT_RING;        // [GT_CBUF] widened tile ready
+  uint8_t* wf16 = ring + RING * STAGE;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(wf16 + (FP8 ? GT_CBUF * GT_WF16 : 0));
+  uint64_t* full = bars;                    // [RING] TMA landed
+  uint64_t* empty = bars + RING;            // [RING] MMA done with the stage
+  uint64_t* cfull = empty + RING;           // [GT_CBUF] widened tile ready
   uint64_t* cempty = cfull + GT_CBUF;       // [GT_CBUF] MMA done with the widened tile
   uint64_t* dfull = cempty + GT_CBUF;       // accumulator complete
   uint32_t* tslot = reinterpret_cast<uint32_t*>(dfull + 1);
@@ -562,7 +573,7 @@ __global__ void __launch_bounds__(GT_THREADS, 1) gemv_tc_kernel(
   const int per = (S + splits - 1) / splits;
   const int s0 = min(S, split * per), s1 = min(S, s0 + per), ns = s1 - s0;
   if (threadIdx.x == 0) {
-    for (int i = 0; i < GT_RING; ++i) {
+    for (int i = 0; i < RING; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1);
     }
@@ -586,34 +597,35 @@ __global__ void __launch_bounds__(GT_THREADS, 1) gemv_tc_kernel(
       prefetch_tmap(&xmap);
       int issued = 0;
       for (int i = 0; i < ns; ++i) {
-        const int slot = i % GT_RING;
-        if (i >= GT_RING && !mbar_wait(&empty[slot], ((i / GT_RING) - 1) & 1, st, 70)) { ok = false; break; }
+        const int slot = i % RING;
+        if (i >= RING && !mbar_wait(&empty[slot], ((i / RING) - 1) & 1, st, 70)) { ok = false; break; }
         ++issued;
-        mbar_arrive_expect_tx(&full[slot], GT_STAGE);
-        uint8_t* dst = ring + slot * GT_STAGE;
-        tma_load_3d(dst, &wmap, &full[slot], 0, tile * 128, s0 + i);
-        tma_load_3d(dst + GT_W8, &xmap, &full[slot], 0, 0, 2 * (s0 + i));
+        mbar_arrive_expect_tx(&full[slot], STAGE);
+        uint8_t* dst = ring + slot * STAGE;
+        // fp8: one 128-byte chunk x 128 rows; bf16: two 64-element chunks x 128 rows
+        tma_load_3d(dst, &wmap, &full[slot], 0, tile * 128, (FP8 ? 1 : 2) * (s0 + i));
+        tma_load_3d(dst + WB, &xmap, &full[slot], 0, 0, 2 * (s0 + i));
       }
       if (!ok) {   // give the copies already issued (bounded) time to land before the CTA exits
-        for (int j = issued > GT_RING ? issued - GT_RING : 0; j < issued; ++j)
-          mbar_wait(&full[j % GT_RING], (j / GT_RING) & 1, nullptr, 0, 50000000ull);
+        for (int j = issued > RING ? issued - RING : 0; j < issued; ++j)
+          mbar_wait(&full[j % RING], (j / RING) & 1, nullptr, 0, 50000000ull);
       }
     }
   } else if (warp == 1) {
     // ---------------- MMA issue
     if (elect_one()) {
-      constexpr uint32_t idesc = idesc_f16_f32(128, 32);
+      constexpr uint32_t idesc = FP8 ? idesc_f16_f32(128, 32) : idesc_bf16_f32(128, 32);
       const uint32_t wf = smem_u32(wf16), rg = smem_u32(ring);
       for (int i = 0; i < ns; ++i) {
-        const int slot = i % GT_RING, c = i % GT_CBUF;
+        const int slot = i % RING, c = i % GT_CBUF;
         // the activations come straight from the TMA stage: observe its barrier here too
-        if (!mbar_wait(&full[slot], (i / GT_RING) & 1, st, 75) ||
-            !mbar_wait(&cfull[c], (i / GT_CBUF) & 1, st, 71)) {
+        if (!mbar_wait(&full[slot], (i / RING) & 1, st, 75) ||
+            (FP8 && !mbar_wait(&cfull[c], (i / GT_CBUF) & 1, st, 71))) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t a0 = wf + c * GT_WF16, b0 = rg + slot * GT_STAGE + GT_W8;
+        const uint32_t a0 = FP8 ? wf + c * GT_WF16 : rg + slot * STAGE, b0 = rg + slot * STAGE + WB;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const uint32_t koff = (j >> 2) * (128 * 128) + (j & 3) * 32;
@@ -622,7 +634,7 @@ __global__ void __launch_bounds__(GT_THREADS, 1) gemv_tc_kernel(
                      (i > 0 || j > 0) ? 1u : 0u);
         }
         mma_commit(&empty[slot]);
-        mma_commit(&cempty[c]);
+        if (FP8) mma_commit(&cempty[c]);
       }
       mma_commit(dfull);   // also on the error path: the epilogue waits on it (bounded)
     }
@@ -631,14 +643,15 @@ __global__ void __launch_bounds__(GT_THREADS, 1) gemv_tc_kernel(
     const int q = warp & 3, r = q * 32 + lane, half = (warp - 2) >> 2;
     const int rb = min(tile * 128, N - 1) >> 7;   // the tile's block-scale row
     // the split's block scales, staged once (a global load per stage sat on every stage's path)
-    for (int j = threadIdx.x - 64; j < ns; j += 256) scs[j] = 256.f * __ldg(wscale + (size_t)rb * sk + s0 + j);
+    if (FP8)
+      for (int j = threadIdx.x - 64; j < ns; j += 256) scs[j] = 256.f * __ldg(wscale + (size_t)rb * sk + s0 + j);
     asm volatile("bar.sync 1, 256;" ::: "memory");
-    for (int i = 0; i < ns; ++i) {
-      const int slot = i % GT_RING, c = i % GT_CBUF;
+    for (int i = 0; i < (FP8 ? ns : 0); ++i) {
+      const int slot = i % RING, c = i % GT_CBUF;
       const float sc = scs[i];
-      if (!mbar_wait(&full[slot], (i / GT_RING) & 1, st, 72)) { ok = false; break; }
+      if (!mbar_wait(&full[slot], (i / RING) & 1, st, 72)) { ok = false; break; }
       if (i >= GT_CBUF && !mbar_wait(&cempty[c], ((i / GT_CBUF) - 1) & 1, st, 73)) { ok = false; break; }
-      const uint8_t* src = ring + slot * GT_STAGE + r * 128;
+      const uint8_t* src = ring + slot * STAGE + r * 128;
       uint8_t* dstrow = wf16 + c * GT_WF16 + r * 128;
       const __half2 s2 = __floats2half2_rn(sc, sc);
 #pragma unroll
@@ -1267,7 +1280,7 @@ static int gv_splits(int tiles, int S, int N, int slots) {
   return splits;
 }
 
-// the tcgen05 form of 17..32-row fp8 calls; XTU_GEMV_TC=0 keeps them on the warp-level kernel
+// the tcgen05 form of 17..32-row calls; XTU_GEMV_TC=0 keeps them on the warp-level kernel
 static bool gv_tc_enabled() {
   static const int on = [] {
     const char* e = getenv("XTU_GEMV_TC");
@@ -1312,7 +1325,7 @@ int xtu_gemv(const void* W, const float* wscale, int fp8, int N, int K, const vo
   XtuStatus* st = reinterpret_cast<XtuStatus*>(status);
   CUtensorMap tm, xm;
   int rc;
-  if (fp8 && M > 16 && K % 128 == 0 && gv_tc_enabled()) {
+  if (M > 16 && K % 128 == 0 && gv_tc_enabled()) {
     // 17..32 rows: the tcgen05 form (see gemv_tc_kernel)
     const int tiles_tc = (N + 127) / 128, S_tc = K / 128;
     int splits = tiles_tc >= gemv_num_sms() ? 1 : gemv_num_sms() / tiles_tc;
@@ -1320,21 +1333,37 @@ int xtu_gemv(const void* W, const float* wscale, int fp8, int N, int K, const vo
     while (splits > 1 && ((splits - 1) * ((S_tc + splits - 1) / splits) >= S_tc ||
                           (long long)splits * GV_MAX_ROWS * N > GV_WS_PART_FLOATS || tiles_tc * 4 > 1024))
       --splits;
-    const cuuint64_t wdims[3] = {128, (cuuint64_t)N, (cuuint64_t)K / 128};
-    const cuuint64_t wstr[2] = {(cuuint64_t)K, 128};
-    const cuuint32_t wbox[3] = {128, 128, 1};
-    rc = gv_tmap_nd(&tm, W, true, 3, wdims, wstr, wbox);
+    if (fp8) {   // e4m3 [N, K] as (128-byte chunk, row, chunk): one chunk x 128 rows per stage
+      const cuuint64_t wdims[3] = {128, (cuuint64_t)N, (cuuint64_t)K / 128};
+      const cuuint64_t wstr[2] = {(cuuint64_t)K, 128};
+      const cuuint32_t wbox[3] = {128, 128, 1};
+      rc = gv_tmap_nd(&tm, W, true, 3, wdims, wstr, wbox);
+    } else {     // bf16 [N, K] as (64-element chunk, row, chunk): two chunks x 128 rows per stage
+      const cuuint64_t wdims[3] = {64, (cuuint64_t)N, (cuuint64_t)K / 64};
+      const cuuint64_t wstr[2] = {(cuuint64_t)K * 2, 128};
+      const cuuint32_t wbox[3] = {64, 128, 2};
+      rc = gv_tmap_nd(&tm, W, false, 3, wdims, wstr, wbox);
+    }
     if (rc) return rc;
     rc = gv_xmap(&xm, x, (uint64_t)M, K, x_stride, 32, false);
     if (rc) return rc;
-    static bool init = false;
-    if (!init) {
-      rc = gv_smem_attr(gemv_tc_kernel, GT_SMEM);
+    static bool init8 = false, init16 = false;
+    if (fp8 && !init8) {
+      rc = gv_smem_attr(gemv_tc_kernel<true>, GT_SMEM);
       if (rc) return rc;
-      init = true;
+      init8 = true;
     }
-    launch_pdl(gemv_tc_kernel, dim3(tiles_tc, splits), dim3(GT_THREADS), GT_SMEM, s, tm, xm, wscale, N, K, M,
-               (const __nv_bfloat16*)bias, y, y_stride, y_f32, ws, counters, st);
+    if (!fp8 && !init16) {
+      rc = gv_smem_attr(gemv_tc_kernel<false>, GT_SMEM_BF);
+      if (rc) return rc;
+      init16 = true;
+    }
+    if (fp8)
+      launch_pdl(gemv_tc_kernel<true>, dim3(tiles_tc, splits), dim3(GT_THREADS), GT_SMEM, s, tm, xm, wscale, N, K,
+                 M, (const __nv_bfloat16*)bias, y, y_stride, y_f32, ws, counters, st);
+    else
+      launch_pdl(gemv_tc_kernel<false>, dim3(tiles_tc, splits), dim3(GT_THREADS), GT_SMEM_BF, s, tm, xm, wscale, N,
+                 K, M, (const __nv_bfloat16*)bias, y, y_stride, y_f32, ws, counters, st);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? launches : -(int)e;
   }

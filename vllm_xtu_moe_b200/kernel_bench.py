@@ -602,6 +602,7 @@ OPS = {
     "moe_decode_fp8": lambda a: bench_moe(a.tokens or 4, "fp8"),
     "gemv_fp8": lambda a: bench_gemv(14336, 4096, a.tokens or 4, "fp8"),
     "gemv_fp8_oproj": lambda a: bench_gemv(4096, 12288, a.tokens or 4, "fp8"),
+    "lm_head_bf16": lambda a: bench_gemv(151552, 4096, a.tokens or 20, "bf16", iters=10),
     "gemm_fp8": lambda a: bench_gemm(a.tokens or 8192, 14336, 4096, "fp8"),
     "gemm_bf16": lambda a: bench_gemm(a.tokens or 8192, 14336, 4096, "bf16"),
     "attention_decode": lambda a: [bench_attn_decode(ql=ql, kv_dtype=kd) for kd in ("bf16", "fp8") for ql in (1, 5)],
