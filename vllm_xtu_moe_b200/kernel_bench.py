@@ -452,6 +452,34 @@ def bench_kda(T=15000, nh=32, dk=128, dv=128, kw=4, iters=3) -> dict:
     return _report("kda_prefill", dict(T=T, nh=nh, dk=dk, dv=dv), ms, nbytes, flops)
 
 
+def bench_moe_verify(T: int, E=128, H=4096, I=1408, K=8, iters=10) -> dict:
+    """A verification-size MoE layer as the model runs it (GLM-4.5-Air shapes, fp8 experts
+    and shared expert): router + permute in one launch, the row gather, the grouped GEMVs
+    with the shared expert as one more grid row, the combine.  Bytes = the active experts'
+    and the shared expert's weights."""
+    from .models.layers import DenseMLP, Linear
+    ex = _experts(E, H, I, "fp8")
+    w13 = torch.randn(1, 2 * I, H, device="cuda") * 0.02
+    w2 = torch.randn(1, H, I, device="cuda") * 0.02
+    q13, s13 = quant_fp8_block(w13)
+    q2, s2 = quant_fp8_block(w2)
+    sh = M.prepare_experts("fp8", q13, q2, s13, s2)
+    mlp = DenseMLP(Linear(sh.w13[0], sh.s13[0]), Linear(sh.w2[0], sh.s2[0]), interleaved=True)
+    x = (torch.randn(T, H, device="cuda") * 0.5).to(torch.bfloat16)
+    gate = (torch.randn(E, H, device="cuda") * 0.02).to(torch.bfloat16)
+    ws = M.MoEWorkspace(T, K, E, H, I, x.device)
+
+    def fn():
+        ids, w = M.route_decode(x, gate, None, K, "sigmoid", 1, 1, True, 1.0, ws, 0, E)
+        return M.fused_moe(x, ids, w, ex, ws, shared_mlp=mlp, permuted=True), ids
+
+    ms = time_fn(lambda: fn(), iters)
+    active = torch.unique(fn()[1]).numel()
+    nbytes = 3 * H * I * (active + 1)
+    return _report("moe_verify_fp8", dict(T=T, E=E, H=H, I=I, K=K, active_experts=active), ms, nbytes,
+                   2 * T * (K + 1) * 3 * H * I)
+
+
 def bench_router_decode(T: int, E=128, H=4096, K=8, iters=20) -> dict:
     """Decode router + permute in one launch (GLM-4.5-Air: 128 experts, sigmoid + bias,
     top-8) for T tokens; bytes = the bf16 gate weights and the tokens."""
@@ -611,6 +639,7 @@ OPS = {
     "mla_decode": lambda a: bench_mla_decode(),
     "attention_prefill": lambda a: bench_attn_prefill(min(a.tokens or 8192, 16384)),
     "rmsnorm": lambda a: bench_rmsnorm(),
+    "moe_verify_fp8": lambda a: [bench_moe_verify(t) for t in ((a.tokens,) if a.tokens else (10, 20))],
     "router_decode": lambda a: [bench_router_decode(t) for t in ((a.tokens,) if a.tokens else (4, 20, 32))],
     "tp_fused": lambda a: bench_tp_fused(),
     "ep_fused": lambda a: bench_ep_fused(),
