@@ -347,6 +347,7 @@ def main():
     mtp_off = None
     if k > 0 and not args.no_sweep:
         llm.set_speculation(0)
+        one_round(C)                     # warm-up: captures the plain decode graphs
         a, b, s, _, _ = one_round(C)
         v = torch.tensor([a, b, float(s)], dtype=torch.float64, device=dev)
         if world > 1:
