@@ -61,6 +61,39 @@ def time_fn(fn, iters: int = 10, warmup: int = 3, flush: bool = True) -> float:
     return ts[len(ts) // 2]
 
 
+def time_graph(fns, reps: int = 7) -> float:
+    """Median device milliseconds per call of `fns` (callables) replayed back to back from one
+    CUDA graph, as the decode step runs them: launch gaps and programmatic-dependent-launch
+    overlap included, host launch cost excluded.  Callers pass enough distinct weight copies
+    that one pass over them exceeds L2."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for f in fns:
+            f()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for f in fns:
+            f()
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(reps):
+        torch.cuda._sleep(200_000)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        g.replay()
+        b.record()
+        b.synchronize()
+        ts.append(a.elapsed_time(b) / len(fns))
+    ts.sort()
+    del g
+    return ts[len(ts) // 2]
+
+
 def _report(op: str, shape: dict, ms: float, nbytes: float, flops: float) -> dict:
     pk = peaks()
     tbs = nbytes / (ms * 1e-3) / 1e12
@@ -224,17 +257,26 @@ def bench_moe_w8a8(T: int, E=128, H=4096, I=1408, K=8, iters=10) -> dict:
     return r
 
 
-def bench_gemv(N: int, Kd: int, M_: int, fmt: str, iters=20) -> dict:
+def bench_gemv(N: int, Kd: int, M_: int, fmt: str, iters=20, graph: bool = False) -> dict:
+    """Decode GEMV y[M, N] = x W^T.  graph: the per-call time of calls replayed from one CUDA
+    graph over distinct weight copies (more than 2x L2 in all); else single calls with an L2
+    flush before each."""
     w = torch.randn(N, Kd, device="cuda") * 0.02
     if fmt == "fp8":
         w, s = quant_fp8_block(w)
     else:
         w, s = w.to(torch.bfloat16), None
     x = torch.randn(M_, Kd, device="cuda").to(torch.bfloat16)
-    fn = lambda: G.linear(x, w, s)
-    ms = time_fn(fn, iters)
-    nbytes = w.numel() * w.element_size() + M_ * (Kd + N) * 2
-    return _report(f"gemv_{fmt}", dict(N=N, K=Kd, M=M_), ms, nbytes, 2 * M_ * N * Kd)
+    wbytes = w.numel() * w.element_size()
+    if graph:
+        copies = [w] + [w.clone() for _ in range(max(1, (260 << 20) // wbytes))]
+        y = torch.empty(M_, N, device="cuda", dtype=torch.bfloat16)
+        ms = time_graph([lambda c=c: G.gemv(x, c, s, out=y) for c in copies] * 2)
+    else:
+        ms = time_fn(lambda: G.linear(x, w, s), iters)
+    nbytes = wbytes + M_ * (Kd + N) * 2
+    return _report(f"gemv_{fmt}" + ("_graph" if graph else ""), dict(N=N, K=Kd, M=M_), ms, nbytes,
+                   2 * M_ * N * Kd)
 
 
 def bench_gemm(Mr: int, N: int, Kd: int, fmt: str, iters=10) -> dict:
@@ -630,6 +672,8 @@ OPS = {
     "moe_decode_fp8": lambda a: bench_moe(a.tokens or 4, "fp8"),
     "gemv_fp8": lambda a: bench_gemv(14336, 4096, a.tokens or 4, "fp8"),
     "gemv_fp8_oproj": lambda a: bench_gemv(4096, 12288, a.tokens or 4, "fp8"),
+    "gemv_fp8_graph": lambda a: [bench_gemv(n, k, a.tokens or 20, "fp8", graph=True)
+                                 for n, k in ((14336, 4096), (4096, 12288))],
     "lm_head_bf16": lambda a: bench_gemv(151552, 4096, a.tokens or 20, "bf16", iters=10),
     "gemm_fp8": lambda a: bench_gemm(a.tokens or 8192, 14336, 4096, "fp8"),
     "gemm_bf16": lambda a: bench_gemm(a.tokens or 8192, 14336, 4096, "bf16"),
