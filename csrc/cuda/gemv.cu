@@ -96,7 +96,11 @@ constexpr int GV_W_BYTES = 32 * GV_ROW_BYTES;   // weight part of a stage: 32 ro
 constexpr int GV_MAX_KBLK = 128;             // block scales staged per tile (K <= 16384)
 constexpr int GV_MAX_ROWS = 32;              // activation rows of a dense GEMV call (NT <= 4)
 #ifndef GV_STAGES_NT1
-#define GV_STAGES_NT1 4                      // ring depth of the one-column-tile forms
+// ring depth of the one-column-tile forms: 3 stages (42 KB a CTA, five CTAs per SM) beat 4
+// (four per SM) on the short MoE tiles -- a verification step's MoE layer 335.8 -> 324.4 us
+// at 20 rows, decode step 20.3 -> 18.5 ms at 4 requests -- where more CTAs in flight hide
+// each CTA's start-up reads better than a deeper ring; 2 and 6 measured slower
+#define GV_STAGES_NT1 3
 #endif
 
 // A stage = the tile's 32 weight rows x 256 bytes, followed by the activations of the same
@@ -108,7 +112,7 @@ struct GvCfg {
   static constexpr int XBOXES = KSTAGE / 64;                     // 64 bf16 per 128-byte box
   static constexpr int X_BYTES = XBOXES * XROWS * 128;
   static constexpr int STAGE_BYTES = GV_W_BYTES + X_BYTES;       // multiple of 1024
-  // 32-row tiles: two CTAs per SM still fit (NT = 4), three (NT = 1, 2)
+  // 32-row tiles: two CTAs per SM still fit (NT = 4), three (NT = 2), five (NT = 1)
   static constexpr int STAGES = NT >= 4 ? 3 : NT == 1 ? GV_STAGES_NT1 : 4;
   static constexpr int RED_FLOATS = GV_CWARPS * 32 * 2 * NT * 4;
   static constexpr int BYTES = 1024 + STAGES * STAGE_BYTES + RED_FLOATS * 4 + 2 * GV_MAX_KBLK * 4 +
