@@ -102,6 +102,12 @@ constexpr int GV_MAX_ROWS = 32;              // activation rows of a dense GEMV 
 // each CTA's start-up reads better than a deeper ring; 2 and 6 measured slower
 #define GV_STAGES_NT1 3
 #endif
+#ifndef GV_STAGES_NT2
+// ring depth of the two-column-tile forms (9..16 rows): here 4 stages (three CTAs per SM)
+// measured best -- qkv / o_proj at 10 rows 17.8 / 15.4 us per graph-replayed call against
+// 19.0 / 15.7 (3 stages) and 21.9 / 16.9 (2 stages, five CTAs per SM)
+#define GV_STAGES_NT2 4
+#endif
 
 // A stage = the tile's 32 weight rows x 256 bytes, followed by the activations of the same
 // k range (bf16, 8 * NT token rows per 128-byte box), both loaded by TMA.
@@ -113,7 +119,7 @@ struct GvCfg {
   static constexpr int X_BYTES = XBOXES * XROWS * 128;
   static constexpr int STAGE_BYTES = GV_W_BYTES + X_BYTES;       // multiple of 1024
   // 32-row tiles: two CTAs per SM still fit (NT = 4), three (NT = 2), five (NT = 1)
-  static constexpr int STAGES = NT >= 4 ? 3 : NT == 1 ? GV_STAGES_NT1 : 4;
+  static constexpr int STAGES = NT >= 4 ? 3 : NT == 1 ? GV_STAGES_NT1 : GV_STAGES_NT2;
   static constexpr int RED_FLOATS = GV_CWARPS * 32 * 2 * NT * 4;
   static constexpr int BYTES = 1024 + STAGES * STAGE_BYTES + RED_FLOATS * 4 + 2 * GV_MAX_KBLK * 4 +
                                2 * STAGES * 8 + 64;
